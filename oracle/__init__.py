@@ -1,0 +1,210 @@
+"""TEST INFRASTRUCTURE ONLY -- the oracle.
+
+Python bindings (ctypes) for the two CPU checkers that oracle/Makefile builds:
+
+* ``liboracle.so`` -- this repository's plain-C restatement of the Clutor MoE feed-forward block (moe_oracle.c);
+* ``_ref/libclref.so`` -- the reference engine's own C sources (c/src/{quant,kernel,iq,cache,xs,route,gguf,meta}.c and,
+  through ref_harness.c, c/src/forward.c), compiled unmodified.
+
+Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline leg of bench.py import this package, and only as the
+checker: the product (clutor_b200) never calls into it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libclref.so")
+REF_DIR_DEFAULT = "/root/reference/c/src"
+
+T_F32, T_F16, T_Q8_0, T_Q4_K, T_Q6_K = 0, 1, 8, 12, 14
+
+
+class Layer(C.Structure):
+    """Mirror of ``orc_layer`` / ``ref_layer`` (both laid out like the fields the reference binds, c/src/forward.h:18-29)."""
+    _fields_ = [
+        ("ffn_norm", C.c_void_p), ("router", C.c_void_p),
+        ("gate_type", C.c_uint32), ("up_type", C.c_uint32), ("down_type", C.c_uint32),
+        ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+        ("gate_slab", C.c_uint64), ("up_slab", C.c_uint64), ("down_slab", C.c_uint64),
+        ("E", C.c_int), ("FF", C.c_int), ("NE", C.c_int), ("K", C.c_int), ("norm_topk", C.c_int),
+        ("resid_scale", C.c_float), ("rms_eps", C.c_float),
+    ]
+
+
+def build(ref_dir: str | None = None, quiet: bool = True) -> None:
+    """Compiles liboracle.so, and _ref/libclref.so when the reference sources are present."""
+    ref_dir = ref_dir or os.environ.get("CLUTOR_REF_DIR", REF_DIR_DEFAULT)
+    out = subprocess.DEVNULL if quiet else None
+    subprocess.run(["make", "-C", HERE, "liboracle.so"], check=True, stdout=out)
+    if os.path.isdir(ref_dir):
+        subprocess.run(["make", "-C", HERE, "ref", f"REF_DIR={ref_dir}"], check=True, stdout=out)
+
+
+_libs: dict[str, C.CDLL] = {}
+
+
+def _load(path: str) -> C.CDLL:
+    if path not in _libs:
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is not built (run `make -C oracle`)")
+        _libs[path] = C.CDLL(path)
+    return _libs[path]
+
+
+def oracle_lib() -> C.CDLL:
+    lib = _load(ORACLE_SO)
+    lib.orc_f16_to_f32.restype = C.c_float
+    lib.orc_f16_to_f32.argtypes = [C.c_uint16]
+    lib.orc_dot_row.restype = C.c_float
+    lib.orc_dotf.restype = C.c_float
+    lib.orc_row_bytes.restype = C.c_uint64
+    return lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref_lib() -> C.CDLL:
+    lib = _load(REF_SO)
+    lib.cl_f16_to_f32_soft.restype = C.c_float
+    lib.cl_f16_to_f32_soft.argtypes = [C.c_uint16]
+    lib.ref_dotf.restype = C.c_float
+    lib.cl_quant_path.restype = C.c_char_p
+    lib.cl_cache_new.restype = C.c_void_p
+    lib.cl_cache_new.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.c_uint32]
+    lib.cl_cache_access.argtypes = [C.c_void_p, C.c_uint32, C.POINTER(C.c_int)]
+    lib.cl_cache_stage.argtypes = [C.c_void_p, C.c_uint32]
+    lib.cl_cache_unpin.argtypes = [C.c_void_p, C.c_int]
+    lib.cl_cache_pin.argtypes = [C.c_void_p, C.c_int]
+    lib.cl_cache_find.argtypes = [C.c_void_p, C.c_uint32]
+    lib.cl_cache_free.argtypes = [C.c_void_p]
+    lib.cl_cache_freq.argtypes = [C.c_void_p, C.c_uint32]
+    lib.cl_cache_freq.restype = C.c_uint32
+    lib.cl_cache_count.argtypes = [C.c_void_p]
+    lib.cl_cache_count.restype = C.c_uint32
+    return lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def make_struct(layer) -> Layer:
+    """A Layer struct pointing into the numpy arrays of a clutor_b200.synth.HostLayer (kept alive by the caller)."""
+    s = Layer()
+    s.ffn_norm, s.router = _ptr(layer.ffn_norm), _ptr(layer.router)
+    s.gate_type, s.up_type, s.down_type = layer.gate_type, layer.up_type, layer.down_type
+    s.gate, s.up, s.down = _ptr(layer.gate), _ptr(layer.up), _ptr(layer.down)
+    s.gate_slab, s.up_slab, s.down_slab = layer.gate_slab, layer.up_slab, layer.down_slab
+    s.E, s.FF, s.NE, s.K, s.norm_topk = layer.E, layer.FF, layer.NE, layer.K, layer.norm_topk
+    s.resid_scale, s.rms_eps = layer.resid_scale, layer.rms_eps
+    return s
+
+
+def moe_ffn(layer, x: np.ndarray, which: str = "oracle"):
+    """Runs one MoE layer on the CPU. ``which`` is "oracle" (the restatement) or "ref" (the reference engine).
+
+    Returns (x_out [T, E] float32, sel [T, K] int32, wt [T, K] float32); x is not modified."""
+    x = np.ascontiguousarray(x, dtype=np.float32).copy()
+    T = x.shape[0]
+    sel = np.zeros((T, layer.K), np.int32)
+    wt = np.zeros((T, layer.K), np.float32)
+    s = make_struct(layer)
+    if which == "oracle":
+        rc = oracle_lib().orc_moe_ffn(C.byref(s), C.c_void_p(_ptr(x)), T, C.c_void_p(_ptr(sel)), C.c_void_p(_ptr(wt)))
+    else:
+        rc = ref_lib().ref_moe_ffn(C.byref(s), C.c_void_p(_ptr(x)), T, C.c_void_p(_ptr(sel)), C.c_void_p(_ptr(wt)))
+    if rc:
+        raise RuntimeError(f"{which} moe_ffn failed")
+    return x, sel, wt
+
+
+def set_ref_threads(n: int) -> None:
+    ref_lib().cl_set_threads(int(n))
+
+
+def dequant_row(type_: int, row: np.ndarray, n: int, which: str = "oracle") -> np.ndarray:
+    out = np.zeros(n, np.float32)
+    row = np.ascontiguousarray(row, dtype=np.uint8)
+    if which == "oracle":
+        oracle_lib().orc_dequant_row(C.c_uint32(type_), C.c_void_p(_ptr(row)), C.c_void_p(_ptr(out)), n)
+    else:
+        ref_lib().cl_dequant_row(C.c_uint32(type_), C.c_void_p(_ptr(row)), C.c_void_p(_ptr(out)), n)
+    return out
+
+
+Q8K_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", 256), ("bsums", "<i2", 16)])   # cl_q8k (c/src/quant.h:22), 292 bytes
+assert Q8K_DTYPE.itemsize == 292
+
+
+def q8k_quantize(x: np.ndarray, which: str = "oracle") -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.size
+    out = np.zeros(n // 256, Q8K_DTYPE)
+    if which == "oracle":
+        oracle_lib().orc_q8k_quantize(C.c_void_p(_ptr(x)), n, C.c_void_p(out.ctypes.data))
+    else:
+        class XQ(C.Structure):
+            _fields_ = [("b", C.c_void_p), ("n", C.c_int)]
+        xq = XQ(out.ctypes.data, n)
+        ref_lib().cl_xq_quantize(C.byref(xq), C.c_void_p(_ptr(x)))
+    return out
+
+
+def dot_row(type_: int, row: np.ndarray, cols: int, xq: np.ndarray | None, xf: np.ndarray | None) -> float:
+    row = np.ascontiguousarray(row, dtype=np.uint8)
+    xq_p = C.c_void_p(xq.ctypes.data) if xq is not None else C.c_void_p(0)
+    xf_p = C.c_void_p(_ptr(np.ascontiguousarray(xf, dtype=np.float32))) if xf is not None else C.c_void_p(0)
+    return oracle_lib().orc_dot_row(C.c_uint32(type_), C.c_void_p(_ptr(row)), cols, xq_p, xf_p)
+
+
+def ref_matvec(type_: int, w: np.ndarray, rows: int, cols: int, xf: np.ndarray, xq: np.ndarray | None) -> np.ndarray:
+    """The reference's cl_matvec_batch on one job (c/src/quant.c:995-1004)."""
+    class XQ(C.Structure):
+        _fields_ = [("b", C.c_void_p), ("n", C.c_int)]
+
+    class MV(C.Structure):
+        _fields_ = [("type", C.c_uint32), ("w", C.c_void_p), ("rows", C.c_int), ("cols", C.c_int), ("xf", C.c_void_p),
+                    ("xq", C.c_void_p), ("out", C.c_void_p), ("nb", C.c_int), ("xf_stride", C.c_size_t),
+                    ("out_stride", C.c_size_t)]
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    xf = np.ascontiguousarray(xf, dtype=np.float32)
+    out = np.zeros(rows, np.float32)
+    xqs = XQ(xq.ctypes.data, cols) if xq is not None else None
+    job = MV(type_, _ptr(w), rows, cols, _ptr(xf), C.addressof(xqs) if xqs is not None else 0, _ptr(out), 1, 0, 0)
+    ref_lib().cl_matvec_batch(C.byref(job), 1)
+    return out
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, which: str = "oracle") -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = np.zeros_like(x)
+    fn = oracle_lib().orc_rmsnorm if which == "oracle" else ref_lib().ref_rmsnorm
+    fn(C.c_void_p(_ptr(out)), C.c_void_p(_ptr(x)), C.c_void_p(_ptr(w)), x.size, C.c_float(eps))
+    return out
+
+
+def dotf(a: np.ndarray, b: np.ndarray, which: str = "oracle") -> float:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    fn = oracle_lib().orc_dotf if which == "oracle" else ref_lib().ref_dotf
+    fn.restype = C.c_float
+    return fn(C.c_void_p(_ptr(a)), C.c_void_p(_ptr(b)), a.size)
+
+
+def route(logits: np.ndarray, K: int, norm_topk: int = 1, which: str = "oracle"):
+    rl = np.ascontiguousarray(logits, dtype=np.float32).copy()
+    sel = np.zeros(K, np.int32)
+    wt = np.zeros(K, np.float32)
+    fn = oracle_lib().orc_route if which == "oracle" else ref_lib().ref_route
+    fn(C.c_void_p(_ptr(rl)), rl.size, K, norm_topk, C.c_void_p(_ptr(sel)), C.c_void_p(_ptr(wt)))
+    return sel, wt

@@ -1,0 +1,124 @@
+/*
+ * TEST INFRASTRUCTURE ONLY: a harness around the reference engine compiled from its own sources (oracle/Makefile builds it with
+ * them into oracle/_ref/libclref.so). It includes the reference's c/src/forward.c, as the reference's c/test/test_attention.c:4
+ * does, to reach its static rmsnorm and dotf, and drives the reference's MoE arithmetic in the order of the forward pass:
+ *   one token   c/src/forward.c:949-1033 (rank-order combine),
+ *   a batch     c/src/forward.c:1132-1210 (experts in order of first appearance, each over its tokens in ascending order).
+ * The glue below (loops, buffers) is this repository's own; every number it produces comes from the reference's functions:
+ * rmsnorm, dotf, expf, cl_xq_quantize and cl_matvec_batch (the CPU backend with its thread pool).
+ */
+#include "forward.c"
+
+typedef struct {
+  const float *ffn_norm;
+  const float *router;
+  uint32_t gate_type, up_type, down_type;
+  const uint8_t *gate, *up, *down;
+  uint64_t gate_slab, up_slab, down_slab;
+  int E, FF, NE, K, norm_topk;
+  float resid_scale, rms_eps;
+} ref_layer;
+
+void ref_rmsnorm(float *out, const float *x, const float *w, int n, float eps) { rmsnorm(out, x, w, n, eps); }
+float ref_dotf(const float *a, const float *b, int n) { return dotf(a, b, n); }
+
+/* softmax, top-k by repeated arg-max (ties to the lower id), renormalisation: the statements of c/src/forward.c:954-984 */
+static void route_one(float *rl, int NE, int K, int norm_topk, int *sel, float *wt) {
+  float mx = rl[0];
+  for (int e = 1; e < NE; e++) if (rl[e] > mx) mx = rl[e];
+  double sum = 0;
+  for (int e = 0; e < NE; e++) { rl[e] = expf(rl[e] - mx); sum += rl[e]; }
+  for (int e = 0; e < NE; e++) rl[e] = (float)(rl[e] / sum);
+  char used[4096] = {0};
+  for (int k = 0; k < K; k++) {
+    int best = -1;
+    for (int e = 0; e < NE; e++) if (!used[e] && (best < 0 || rl[e] > rl[best])) best = e;
+    used[best] = 1; sel[k] = best; wt[k] = rl[best];
+  }
+  if (norm_topk) { float z = 0; for (int k = 0; k < K; k++) z += wt[k]; if (z > 0) for (int k = 0; k < K; k++) wt[k] /= z; }
+}
+
+void ref_route(float *rl, int NE, int K, int norm_topk, int *sel, float *wt) { route_one(rl, NE, K, norm_topk, sel, wt); }
+
+static int decode_one(const ref_layer *L, float *x, int *sel, float *wt) {
+  const int E = L->E, FF = L->FF, K = L->K;
+  float *xn = malloc((size_t)E * 4), *rl = malloc((size_t)L->NE * 4), *moe = calloc((size_t)E, 4);
+  float *hg = malloc((size_t)K * FF * 4), *hu = malloc((size_t)K * FF * 4), *hd = malloc((size_t)K * E * 4);
+  cl_xq xq = {0}, *xqf = calloc((size_t)K, sizeof(cl_xq));
+  int ok = xn && rl && moe && hg && hu && hd && xqf && cl_xq_init(&xq, E);
+  for (int k = 0; ok && k < K; k++) ok = cl_xq_init(&xqf[k], FF);
+  if (ok) {
+    rmsnorm(xn, x, L->ffn_norm, E, L->rms_eps);
+    for (int e = 0; e < L->NE; e++) rl[e] = dotf(L->router + (size_t)e * E, xn, E);
+    route_one(rl, L->NE, K, L->norm_topk, sel, wt);
+    cl_xq_quantize(&xq, xn);
+    cl_mv j[64];
+    for (int k = 0; k < K; k++) {
+      j[2 * k] = (cl_mv){L->gate_type, L->gate + (size_t)sel[k] * L->gate_slab, FF, E, xn, &xq, hg + (size_t)k * FF, 1, 0, 0};
+      j[2 * k + 1] = (cl_mv){L->up_type, L->up + (size_t)sel[k] * L->up_slab, FF, E, xn, &xq, hu + (size_t)k * FF, 1, 0, 0};
+    }
+    cl_matvec_batch(j, 2 * K);
+    for (int k = 0; k < K; k++) {
+      float *g = hg + (size_t)k * FF, *u = hu + (size_t)k * FF;
+      for (int i = 0; i < FF; i++) g[i] = g[i] / (1.0f + expf(-g[i])) * u[i];
+      cl_xq_quantize(&xqf[k], g);
+      j[k] = (cl_mv){L->down_type, L->down + (size_t)sel[k] * L->down_slab, E, FF, g, &xqf[k], hd + (size_t)k * E, 1, 0, 0};
+    }
+    cl_matvec_batch(j, K);
+    for (int k = 0; k < K; k++) for (int i = 0; i < E; i++) moe[i] += wt[k] * hd[(size_t)k * E + i];
+    for (int i = 0; i < E; i++) x[i] += L->resid_scale * moe[i];
+  }
+  for (int k = 0; xqf && k < K; k++) cl_xq_free(&xqf[k]);
+  cl_xq_free(&xq); free(xqf); free(xn); free(rl); free(moe); free(hg); free(hu); free(hd);
+  return ok ? 0 : 1;
+}
+
+static int batch(const ref_layer *L, float *X, int nb, int *sel, float *wt) {
+  const int E = L->E, FF = L->FF, NE = L->NE, NU = L->K;
+  float *XN = malloc((size_t)nb * E * 4), *XG = malloc((size_t)nb * E * 4), *MOE = calloc((size_t)nb * E, 4), *rl = malloc((size_t)NE * 4);
+  float *HG = malloc((size_t)nb * FF * 4), *HU = malloc((size_t)nb * FF * 4), *HDE = malloc((size_t)nb * E * 4);
+  cl_xq *xqe = calloc((size_t)nb, sizeof(cl_xq)), *xqf = calloc((size_t)nb, sizeof(cl_xq)), *sub = calloc((size_t)nb, sizeof(cl_xq));
+  int *who = malloc((size_t)nb * sizeof(int)), *todo = malloc((size_t)NE * sizeof(int));
+  float *wgt = malloc((size_t)nb * 4);
+  char *seen = calloc((size_t)NE, 1);
+  int ok = XN && XG && MOE && rl && HG && HU && HDE && xqe && xqf && sub && who && todo && wgt && seen;
+  for (int b = 0; ok && b < nb; b++) ok = cl_xq_init(&xqe[b], E) && cl_xq_init(&xqf[b], FF);
+  if (ok) {
+    for (int b = 0; b < nb; b++) {   /* route_task (c/src/forward.c:1065-1072), then the per-token softmax/top-k (:1135-1157) */
+      float *xn = XN + (size_t)b * E;
+      rmsnorm(xn, X + (size_t)b * E, L->ffn_norm, E, L->rms_eps);
+      cl_xq_quantize(&xqe[b], xn);
+      for (int e = 0; e < NE; e++) rl[e] = dotf(L->router + (size_t)e * E, xn, E);
+      route_one(rl, NE, NU, L->norm_topk, sel + (size_t)b * NU, wt + (size_t)b * NU);
+    }
+    int n_todo = 0;
+    for (int b = 0; b < nb; b++) for (int k = 0; k < NU; k++) { const int e = sel[(size_t)b * NU + k]; if (!seen[e]) { seen[e] = 1; todo[n_todo++] = e; } }
+    for (int i = 0; i < n_todo; i++) {
+      const int e = todo[i];
+      int ni = 0;
+      for (int b = 0; b < nb; b++) for (int k = 0; k < NU; k++) if (sel[(size_t)b * NU + k] == e) { who[ni] = b; wgt[ni] = wt[(size_t)b * NU + k]; ni++; break; }
+      for (int t = 0; t < ni; t++) { sub[t] = xqe[who[t]]; memcpy(XG + (size_t)t * E, XN + (size_t)who[t] * E, (size_t)E * 4); }
+      cl_mv j[2] = {{L->gate_type, L->gate + (size_t)e * L->gate_slab, FF, E, XG, sub, HG, ni, (size_t)E, (size_t)FF},
+                    {L->up_type, L->up + (size_t)e * L->up_slab, FF, E, XG, sub, HU, ni, (size_t)E, (size_t)FF}};
+      cl_matvec_batch(j, 2);
+      for (int t = 0; t < ni; t++) {
+        float *hg = HG + (size_t)t * FF, *hu = HU + (size_t)t * FF;
+        for (int q = 0; q < FF; q++) hg[q] = hg[q] / (1.0f + expf(-hg[q])) * hu[q];
+        cl_xq_quantize(&xqf[t], hg);
+      }
+      cl_mv d = {L->down_type, L->down + (size_t)e * L->down_slab, E, FF, HG, xqf, HDE, ni, (size_t)FF, (size_t)E};
+      cl_matvec_batch(&d, 1);
+      for (int t = 0; t < ni; t++) { float *m = MOE + (size_t)who[t] * E; const float *h = HDE + (size_t)t * E; for (int q = 0; q < E; q++) m[q] += wgt[t] * h[q]; }
+    }
+    for (size_t i = 0; i < (size_t)nb * E; i++) X[i] += L->resid_scale * MOE[i];
+  }
+  for (int b = 0; b < nb; b++) { if (xqe) cl_xq_free(&xqe[b]); if (xqf) cl_xq_free(&xqf[b]); }
+  free(XN); free(XG); free(MOE); free(rl); free(HG); free(HU); free(HDE); free(xqe); free(xqf); free(sub); free(who); free(todo); free(wgt); free(seen);
+  return ok ? 0 : 1;
+}
+
+/* T tokens through one MoE layer (x [T x E] in place); sel/wt [T x K]. At most CL_PS_B tokens per batch, like the reference. */
+int ref_moe_ffn(const ref_layer *L, float *x, int T, int *sel, float *wt) {
+  if (T < 1 || T > CL_PS_B || L->K > 64 || L->NE > 4096) return 1;
+  return T == 1 ? decode_one(L, x, sel, wt) : batch(L, x, T, sel, wt);
+}
