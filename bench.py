@@ -1,0 +1,301 @@
+"""Benchmark of the MoE feed-forward hot path on B200.
+
+Default workload (N=1 per GPU): the Qwen3-30B-A3B MoE layer at decode, one token (hidden 2048, 128 experts, top-8,
+intermediate 768, Q4_K experts, fp32 router). A step is one token through a pool of `--layers` distinct layers (48, about
+16 GB of expert weights, far larger than the 126 MB L2), chained: each layer's output is the next one's input, replayed
+from a CUDA graph. The metric is MoE-layer tokens per second (layer-token = one token through one layer).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill64] [--impl ours|reference]
+
+Under torchrun with N > 1 every rank runs the same workload on its own GPU (the decode layer does not shard: replicas),
+value = all ranks' layer-tokens / the slowest rank's time. --impl reference times the reference engine's own CPU code
+(oracle/_ref, built from its sources) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+METRIC = "MoE-layer tokens/s (decode, Qwen3-30B-A3B layer, Q4_K)"
+
+WORKLOADS = {
+    # name: (T, gate type, down type, E, FF, NE, K, layers)
+    "decode": dict(T=1, gate="q4_k", down="q4_k", E=2048, FF=768, NE=128, K=8, layers=48,
+                   desc="Qwen3-30B-A3B MoE layer, decode T=1, Q4_K experts"),
+    "prefill64": dict(T=64, gate="q8_0", down="q8_0", E=2048, FF=768, NE=128, K=8, layers=8,
+                      desc="Qwen3-30B-A3B MoE layer, T=64, Q8_0 experts"),
+}
+
+
+def peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p)), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def layer_bytes(wl: dict, distinct: float) -> float:
+    """Algorithmic bytes of one call: the distinct experts' gate/up/down slabs, the fp32 router, the norm weights, and x in
+    and out."""
+    from clutor_b200 import synth
+    g = synth.TYPE_NAMES[wl["gate"]]
+    d = synth.TYPE_NAMES[wl["down"]]
+    E, FF, NE, T = wl["E"], wl["FF"], wl["NE"], wl["T"]
+    expert = 2 * FF * synth.row_bytes(g, E) + E * synth.row_bytes(d, FF)
+    return distinct * expert + NE * E * 4 + E * 4 + 2 * T * E * 4
+
+
+class Clocks:
+    """Samples nvidia-smi every 200 ms during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows: list[list[str]] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["not sampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def read_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary (profiles/), if there is one."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_reference(wl: dict, seconds: float, threads: int | None = None) -> dict:
+    """The reference engine's CPU path (oracle/_ref) on a bounded sample of the workload: one layer, fresh activations per
+    call, all host threads (the reference caps its pool at 16)."""
+    import numpy as np
+
+    import oracle
+    from clutor_b200 import synth
+    if not oracle.ref_available():
+        oracle.build()
+    nthreads = threads or min(os.cpu_count() or 1, 16)
+    oracle.set_ref_threads(nthreads)
+    L = synth.host_layer(E=wl["E"], FF=wl["FF"], NE=wl["NE"], K=wl["K"], gate_type=synth.TYPE_NAMES[wl["gate"]],
+                         down_type=synth.TYPE_NAMES[wl["down"]], seed=1, router_scale=0.05 if wl["T"] > 1 else 0.02)
+    xs = [synth.activations(wl["T"], wl["E"], seed=1000 + i) for i in range(8)]
+    for i in range(2):
+        oracle.moe_ffn(L, xs[i], "ref")
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        oracle.moe_ffn(L, xs[n % len(xs)], "ref")
+        n += 1
+    dt = time.perf_counter() - t0
+    path = oracle.ref_lib().cl_quant_path().decode()
+    return {"value": n * wl["T"] / dt, "unit": "layer-tokens/s", "cores": nthreads, "kind": "reference",
+            "sample": f"{n} calls of one layer ({wl['T']} token(s) each) in {dt:.1f} s on {nthreads} threads, ISA path {path}; "
+                      f"reference built from its sources (oracle/_ref)", "ms_per_call": 1000 * dt / n}
+
+
+def run_reference_arm(a, wl, rank: int) -> None:
+    if rank != 0:
+        return
+    secs = max(5.0, min(60.0, 2.0 * a.steps))
+    cb = cpu_reference(wl, secs)
+    line = {"impl": "reference", "metric": METRIC if a.workload == "decode" else METRIC.replace("decode", "T=64").replace("Q4_K", "Q8_0"),
+            "value": round(cb["value"], 3), "unit": "layer-tokens/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": round(cb["ms_per_call"], 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate" if wl["gate"] != "q8_0" else "f32",
+            "data": "synthetic (seeded)", "config": {"workload": wl["desc"], "tokens_per_call": wl["T"]},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(cb["value"], 3), "unit": "layer-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--layers", type=int, default=None, help="distinct layers in the pool (default: the workload's)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    a = ap.parse_args()
+    wl = dict(WORKLOADS[a.workload])
+    if a.layers:
+        wl["layers"] = a.layers
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference_arm(a, wl, rank)
+        return
+
+    import numpy as np
+    import torch
+
+    import clutor_b200 as cb
+    from clutor_b200 import synth
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    T, NL, K = wl["T"], wl["layers"], wl["K"]
+    ctx = cb.Context(local)
+    layers = [synth.device_layer(E=wl["E"], FF=wl["FF"], NE=wl["NE"], K=K, gate_type=synth.TYPE_NAMES[wl["gate"]],
+                                 down_type=synth.TYPE_NAMES[wl["down"]], seed=1000 * rank + i + 1,
+                                 router_scale=0.05 if T > 1 else 0.02) for i in range(NL)]
+    handles = [ctx.bind(L) for L in layers]
+    x0 = torch.from_numpy(synth.activations(T, wl["E"], seed=11 + rank)).cuda()
+    x = x0.clone()
+    sel = torch.zeros((NL, T, K), dtype=torch.int32, device="cuda")
+    wt = torch.zeros((NL, T, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def step():
+        for i, h in enumerate(handles):
+            ctx.moe_ffn_dev(h, x, sel[i], wt[i], stream=stream)
+
+    # warm up eagerly once (sizes the scratch), then capture one step into a graph
+    with torch.cuda.stream(stream):
+        step()
+    ctx.status()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(a.warmup):
+        x.copy_(x0)
+        graph.replay()
+    torch.cuda.synchronize()
+    ctx.status()
+    launches_per_step = NL * (1 if T == 1 else 7)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(a.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    ctx.status()
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    units = NL * T * a.steps * world
+    value = units / (ms / 1000.0)
+    ms_per_step = ms / a.steps
+    # roofline of the dominant kernel (the whole step is its launches)
+    distinct = float(np.mean([len(np.unique(sel[i].cpu().numpy())) for i in range(NL)]))
+    bytes_per_launch = layer_bytes(wl, distinct)
+    launch_us = 1000.0 * ms_per_step / NL
+    pk, pk_kind = peaks()
+    achieved = bytes_per_launch / (launch_us * 1e-6) / 1e9
+    kernel = "moe_decode_kernel" if T == 1 else "moe_batched"
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": read_traffic(f"{kernel}_{a.workload}"),
+            "peak_kind": pk_kind, "kernel": kernel, "bytes_per_launch": int(bytes_per_launch), "launch_us": round(launch_us, 3)}
+
+    # end to end through the host-pointer entry point (clb200_moe_ffn): x from pinned host memory in, x/sel/wt back out
+    e2e = None
+    if not a.no_e2e:
+        ne = min(NL, 16)
+        host_layers = [synth.to_host(L) for L in layers[:ne]]
+        structs = [cb.layer_struct(L) for L in host_layers]
+        xh = torch.from_numpy(synth.activations(T, wl["E"], seed=21 + rank)).pin_memory()
+        selh = torch.zeros((T, K), dtype=torch.int32).pin_memory()
+        wth = torch.zeros((T, K), dtype=torch.float32).pin_memory()
+        xn, sn, wn = xh.numpy(), selh.numpy(), wth.numpy()
+        for s in structs:                # the first call of each layer uploads its weights
+            ctx.moe_ffn_inplace(s, xn, sn, wn)
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            for s in structs:
+                ctx.moe_ffn_inplace(s, xn, sn, wn)
+        dt = time.perf_counter() - t0
+        if dist:
+            tt = torch.tensor([dt], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            dt = float(tt.item())
+        e2e = {"value": round(ne * T * a.steps * world / dt, 3), "unit": "layer-tokens/s",
+               "h2d_bytes_per_step": ne * T * wl["E"] * 4, "d2h_bytes_per_step": ne * T * (wl["E"] * 4 + 2 * K * 4),
+               "calls_per_step": ne, "api": "clb200_moe_ffn (host pointers, synchronous)"}
+    cpu = None
+    if rank == 0 and not a.no_cpu_baseline:
+        cpu = cpu_reference(wl, a.cpu_seconds)
+        cpu.pop("ms_per_call", None)
+    if rank == 0:
+        line = {"metric": METRIC if a.workload == "decode" else METRIC.replace("decode", "T=64").replace("Q4_K", "Q8_0"),
+                "value": round(value, 3), "unit": "layer-tokens/s", "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate" if wl["gate"] != "q8_0" else "f32",
+                "data": "synthetic (seeded random GGUF blocks)",
+                "config": {"workload": wl["desc"], "tokens_per_call": T, "layers_per_step": NL, "hidden": wl["E"],
+                           "experts": wl["NE"], "top_k": K, "ff": wl["FF"], "parallelism": f"replicas x{world}",
+                           "l2": f"inputs larger than L2: {NL} distinct layers, {NL * layers[0].NE * layers[0].expert_bytes / 1e9:.1f} GB of experts"},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * a.steps,
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    del graph
+    ctx.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

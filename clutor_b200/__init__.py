@@ -1,0 +1,208 @@
+"""clutor-b200: the Clutor engine's MoE feed-forward block on B200 (sm_100a), through the C ABI of include/clb200.h.
+
+This module is the Python view of that ABI (ctypes), used by the tests and bench.py; C host code (the reference engine)
+calls the same entry points directly. There is no CPU path: importing works anywhere, but every entry point needs the
+built library (python -m clutor_b200.build) and a CUDA device, and fails loudly without them.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+
+from . import synth
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libclutor_b200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "clb200.h")
+
+T_F32, T_F16, T_Q8_0, T_Q4_K, T_Q6_K = 0, 1, 8, 12, 14
+
+
+class CLW(C.Structure):
+    """clb200_w == the reference's cl_w (c/src/forward.h:18)."""
+    _fields_ = [("p", C.c_void_p), ("type", C.c_uint32), ("rows", C.c_int), ("cols", C.c_int)]
+
+
+class MoELayer(C.Structure):
+    """clb200_moe_layer (include/clb200.h)."""
+    _fields_ = [("ffn_norm_f", C.c_void_p), ("router_f", C.c_void_p), ("gate", CLW), ("up", CLW), ("down", CLW),
+                ("gate_slab", C.c_uint64), ("up_slab", C.c_uint64), ("down_slab", C.c_uint64),
+                ("n_embd", C.c_int), ("n_ff_exp", C.c_int), ("n_expert", C.c_int), ("n_used", C.c_int),
+                ("norm_topk", C.c_int), ("resid_scale", C.c_float), ("rms_eps", C.c_float)]
+
+
+class Q8K(C.Structure):
+    _fields_ = [("d", C.c_float), ("qs", C.c_int8 * 256), ("bsums", C.c_int16 * 16)]
+
+
+class XQ(C.Structure):
+    _fields_ = [("b", C.c_void_p), ("n", C.c_int)]
+
+
+class MV(C.Structure):
+    """clb200_mv == the reference's cl_mv (c/src/quant.h:31-34)."""
+    _fields_ = [("type", C.c_uint32), ("w", C.c_void_p), ("rows", C.c_int), ("cols", C.c_int), ("xf", C.c_void_p),
+                ("xq", C.c_void_p), ("out", C.c_void_p), ("nb", C.c_int), ("xf_stride", C.c_size_t),
+                ("out_stride", C.c_size_t)]
+
+
+SUPPORTS = C.CFUNCTYPE(C.c_int, C.c_uint32)
+MATVEC = C.CFUNCTYPE(None, C.POINTER(MV), C.c_int)
+
+
+class Backend(C.Structure):
+    """clb200_backend_t == the reference's cl_backend (c/src/backend.h:9-13)."""
+    _fields_ = [("name", C.c_char_p), ("supports", SUPPORTS), ("matvec_batch", MATVEC)]
+
+
+_lib: C.CDLL | None = None
+
+
+def header_functions() -> list[str]:
+    """Names of the functions include/clb200.h declares."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(clb200_\w+)\s*\(", text, re.M)))
+
+
+def lib() -> C.CDLL:
+    """The CUDA library; raises if it is not built (there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built: run `python -m clutor_b200.build` (no CPU fallback exists)")
+        L = C.CDLL(LIB_PATH)
+        L.clb200_open.restype = C.c_void_p
+        L.clb200_open.argtypes = [C.c_int, C.c_char_p, C.c_size_t]
+        L.clb200_close.argtypes = [C.c_void_p]
+        L.clb200_moe_ffn.argtypes = [C.c_void_p, C.POINTER(MoELayer), C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_layer_bind.argtypes = [C.c_void_p, C.POINTER(MoELayer), C.c_int, C.c_char_p, C.c_size_t]
+        L.clb200_moe_ffn_dev.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_status.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_device_bytes.restype = C.c_uint64
+        L.clb200_device_bytes.argtypes = [C.c_void_p]
+        L.clb200_backend.restype = C.POINTER(Backend)
+        _lib = L
+    return _lib
+
+
+class ClutorError(RuntimeError):
+    pass
+
+
+def _ptr(a) -> int:
+    if a is None:
+        return 0
+    if isinstance(a, np.ndarray):
+        assert a.flags["C_CONTIGUOUS"]
+        return a.ctypes.data
+    return a.data_ptr()   # torch tensor
+
+
+def layer_struct(layer) -> MoELayer:
+    """A clb200_moe_layer over a synth.HostLayer (numpy, host pointers) or synth.DeviceLayer (torch, device pointers)."""
+    s = MoELayer()
+    s.ffn_norm_f, s.router_f = _ptr(layer.ffn_norm), _ptr(layer.router)
+    E, FF = layer.E, layer.FF
+    s.gate = CLW(_ptr(layer.gate), layer.gate_type, FF, E)
+    s.up = CLW(_ptr(layer.up), layer.up_type, FF, E)
+    s.down = CLW(_ptr(layer.down), layer.down_type, E, FF)
+    s.gate_slab, s.up_slab, s.down_slab = layer.gate_slab, layer.up_slab, layer.down_slab
+    s.n_embd, s.n_ff_exp, s.n_expert, s.n_used = E, FF, layer.NE, layer.K
+    s.norm_topk, s.resid_scale, s.rms_eps = layer.norm_topk, layer.resid_scale, layer.rms_eps
+    return s
+
+
+class Context:
+    """A clb200 context on one CUDA device (clb200_open)."""
+
+    def __init__(self, device: int = 0):
+        self._err = C.create_string_buffer(512)
+        self.handle = lib().clb200_open(device, self._err, 512)
+        if not self.handle:
+            raise ClutorError(self._err.value.decode())
+        self.device = device
+        self._keep: list = []
+
+    def close(self) -> None:
+        if self.handle:
+            lib().clb200_close(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int) -> None:
+        if rc:
+            raise ClutorError(self._err.value.decode())
+
+    def moe_ffn(self, layer: "synth.HostLayer", x: np.ndarray):
+        """The host-pointer entry point (clb200_moe_ffn): returns (x_out, sel, wt); x is not modified."""
+        x = np.ascontiguousarray(x, dtype=np.float32).copy()
+        T = x.shape[0]
+        sel = np.zeros((T, layer.K), np.int32)
+        wt = np.zeros((T, layer.K), np.float32)
+        s = layer_struct(layer)
+        self._check(lib().clb200_moe_ffn(self.handle, C.byref(s), _ptr(x), T, _ptr(sel), _ptr(wt), self._err, 512))
+        return x, sel, wt
+
+    def moe_ffn_inplace(self, s: MoELayer, x: np.ndarray, sel: np.ndarray, wt: np.ndarray) -> None:
+        """clb200_moe_ffn on caller buffers (x updated in place), with a prebuilt layer struct: no copies on the Python side
+        (for timing the host entry point from pinned memory)."""
+        self._check(lib().clb200_moe_ffn(self.handle, C.byref(s), _ptr(x), x.shape[0], _ptr(sel), _ptr(wt), self._err, 512))
+
+    def bind(self, layer, on_device: bool | None = None) -> int:
+        """Registers a layer (clb200_layer_bind); device tensors are used in place, host arrays are uploaded."""
+        if on_device is None:
+            on_device = not isinstance(layer.gate, np.ndarray)
+        s = layer_struct(layer)
+        h = lib().clb200_layer_bind(self.handle, C.byref(s), 1 if on_device else 0, self._err, 512)
+        if h < 0:
+            raise ClutorError(self._err.value.decode())
+        self._keep.append(layer)
+        return h
+
+    def moe_ffn_dev(self, handle: int, x, sel=None, wt=None, stream=None) -> None:
+        """The device entry point (clb200_moe_ffn_dev) on torch CUDA tensors; asynchronous on `stream` (a torch stream)."""
+        T = x.shape[0]
+        st = 0 if stream is None else stream.cuda_stream
+        self._check(lib().clb200_moe_ffn_dev(self.handle, handle, _ptr(x), T, _ptr(sel), _ptr(wt), C.c_void_p(st), self._err, 512))
+
+    def status(self) -> None:
+        self._check(lib().clb200_status(self.handle, self._err, 512))
+
+    def device_bytes(self) -> int:
+        return int(lib().clb200_device_bytes(self.handle))
+
+
+def backend() -> Backend:
+    """The "b200" cl_backend struct (clb200_backend)."""
+    return lib().clb200_backend().contents
+
+
+def matvec(type_: int, w: np.ndarray, rows: int, cols: int, xf: np.ndarray | None = None, xq: np.ndarray | None = None):
+    """One cl_mv job through the backend's matvec_batch (host pointers, like the reference's seam). xf [nb, cols] float32;
+    xq: numpy array of Q8K structured dtype [nb, cols/256]. Returns out [nb, rows]."""
+    nb = (xf.shape[0] if xf is not None and xf.ndim == 2 else (xq.shape[0] if xq is not None and xq.ndim == 2 else 1))
+    out = np.zeros((nb, rows), np.float32)
+    xqs = None
+    if xq is not None:
+        xq = np.ascontiguousarray(xq.reshape(nb, -1))
+        xqs = (XQ * nb)(*[XQ(xq[b].ctypes.data, cols) for b in range(nb)])
+    xf_c = None if xf is None else np.ascontiguousarray(xf.reshape(nb, cols), dtype=np.float32)
+    job = MV(type_, _ptr(np.ascontiguousarray(w)), rows, cols, _ptr(xf_c), C.addressof(xqs) if xqs is not None else 0,
+             _ptr(out), nb, cols, rows)
+    be = backend()
+    be.matvec_batch(C.byref(job), 1)
+    return out

@@ -1,0 +1,429 @@
+// The C ABI of include/clb200.h: contexts, layer registration and upload, scratch, the per-layer MoE entry points and the
+// "b200" cl_backend.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/clb200.h"
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace clb {
+
+static void errf(char *err, size_t errlen, const char *fmt, ...) {
+  if (!err || !errlen) return;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(err, errlen, fmt, ap);
+  va_end(ap);
+}
+
+static uint64_t row_bytes(uint32_t t, uint64_t n) {
+  switch (t) {
+    case T_Q4_K: return n / 256 * 144;
+    case T_Q6_K: return n / 256 * 210;
+    case T_Q8_0: return n / 32 * 34;
+    case T_F32: return n * 4;
+    case T_F16: return n * 2;
+    default: return 0;
+  }
+}
+static bool expert_type(uint32_t t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; }
+static const char *type_name(uint32_t t) {
+  switch (t) {
+    case T_Q4_K: return "Q4_K";
+    case T_Q6_K: return "Q6_K";
+    case T_Q8_0: return "Q8_0";
+    case T_F32: return "F32";
+    case T_F16: return "F16";
+    default: return "an unsupported type";
+  }
+}
+static size_t al(size_t v, size_t a = 256) { return (v + a - 1) / a * a; }
+
+#define CUDA_OR(call, msg)                                                                                            \
+  do {                                                                                                                \
+    cudaError_t e_ = (call);                                                                                          \
+    if (e_ != cudaSuccess) { errf(err, errlen, "%s: %s", msg, cudaGetErrorString(e_)); return 1; }                    \
+  } while (0)
+
+struct DevLayer {
+  clb200_moe_layer d{};              // device pointers
+  const void *hkey[5] = {};          // host pointers of router, norm, gate, up, down (0 when bound on the device)
+  void *block = nullptr;             // the owned device copy (upload), else null
+  size_t bytes = 0;
+};
+
+}  // namespace clb
+
+using namespace clb;
+
+struct clb200_ctx {
+  int device = 0, sms = 0, max_smem = 0;
+  cudaStream_t stream = nullptr;
+  std::vector<DevLayer> layers;
+  std::unordered_map<const void *, int> by_gate;   // host gate pointer -> layer index
+  int *small = nullptr;                            // [0] device error word, [64..] counters of the one-token kernel
+  uint8_t *scratch = nullptr;
+  size_t scratch_cap = 0;
+  float *hx = nullptr;                             // host-call staging of x / sel / wt on the device (in scratch)
+  uint64_t bytes = 0;
+  bool attrs_set = false;
+};
+
+namespace clb {
+
+struct Scratch {
+  size_t off_logits, off_hg, off_x, off_sel, off_wt, total;
+  // batched
+  size_t off_xn, off_xq_qs, off_xq_d, off_xq_bs, off_bsel, off_bwt, off_counts, off_offsets, off_first, off_pos_token,
+      off_pos_wt, off_slot_pos, off_bhg, off_hq_qs, off_hq_d, off_hq_bs, off_hd;
+};
+
+static Scratch plan_scratch(int T, int E, int FF, int NE, int K) {
+  Scratch s{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) { const size_t at = o; o = al(o + bytes); return at; };
+  const size_t TK = static_cast<size_t>(T) * K;
+  s.off_x = take(static_cast<size_t>(T) * E * 4);
+  s.off_sel = take(TK * 4);
+  s.off_wt = take(TK * 4);
+  s.off_logits = take(static_cast<size_t>(T) * NE * 4);
+  s.off_hg = take(static_cast<size_t>(K) * FF * 4);
+  if (T > 1) {
+    s.off_xn = take(static_cast<size_t>(T) * E * 4);
+    s.off_xq_qs = take(static_cast<size_t>(T) * E);
+    s.off_xq_d = take(static_cast<size_t>(T) * (E / 256) * 4);
+    s.off_xq_bs = take(static_cast<size_t>(T) * (E / 16) * 2);
+    s.off_bsel = take(TK * 4);
+    s.off_bwt = take(TK * 4);
+    s.off_counts = take(static_cast<size_t>(NE) * 4);
+    s.off_offsets = take(static_cast<size_t>(NE + 1) * 4);
+    s.off_first = take(static_cast<size_t>(NE) * 4);
+    s.off_pos_token = take(TK * 4);
+    s.off_pos_wt = take(TK * 4);
+    s.off_slot_pos = take(TK * 4);
+    s.off_bhg = take(TK * FF * 4);
+    s.off_hq_qs = take(TK * FF);
+    s.off_hq_d = take(TK * (FF / 256) * 4);
+    s.off_hq_bs = take(TK * (FF / 16) * 2);
+    s.off_hd = take(TK * E * 4);
+  }
+  s.total = o;
+  return s;
+}
+
+static int ensure_scratch(clb200_ctx *c, size_t need, char *err, size_t errlen) {
+  if (need <= c->scratch_cap) return 0;
+  CUDA_OR(cudaStreamSynchronize(c->stream), "waiting for the device before growing scratch");
+  if (c->scratch) { cudaFree(c->scratch); c->bytes -= c->scratch_cap; }
+  c->scratch = nullptr;
+  c->scratch_cap = 0;
+  const size_t cap = al(need, 1 << 20);
+  CUDA_OR(cudaMalloc(&c->scratch, cap), "allocating scratch");
+  c->scratch_cap = cap;
+  c->bytes += cap;
+  return 0;
+}
+
+// Shared-memory plan of the one-token kernel for a layer; 0 when it fits.
+static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArgs &a, char *err, size_t errlen) {
+  const int G = c->sms, E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+  a.rgu_max = (FF + G - 1) / G;
+  a.rd_max = (E + G - 1) / G;
+  a.grb = static_cast<uint32_t>(row_bytes(L.gate.type, E));
+  a.drb = static_cast<uint32_t>(row_bytes(L.down.type, FF));
+  a.gseg = static_cast<uint32_t>(al(static_cast<size_t>(a.rgu_max) * a.grb + 32, 16));
+  a.dseg = static_cast<uint32_t>(al(static_cast<size_t>(a.rd_max) * a.drb + 32, 16));
+  a.slot_bytes = 2 * a.gseg + a.dseg;
+  const int nre = (NE + G - 1) / G;
+  constexpr int NW = DECODE_THREADS / 32;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { const size_t at = o; o = al(o + bytes, 16); return static_cast<uint32_t>(at); };
+  a.off_bars = take(8 * (K + 1));
+  a.off_xn = take(static_cast<size_t>(E) * 4);
+  a.off_xq = take(static_cast<size_t>(E) + 4 * (E / 256) + 2 * (E / 16));
+  a.off_router = take(static_cast<size_t>(nre) * E * 4);
+  a.off_misc = take(NE * 4 + 32 * 4 + 32 * 4 + NW * 8 + 16);
+  a.off_hq = take(static_cast<size_t>(FF) * 5 + 4 * (FF / 256) + 2 * (FF / 16));
+  a.off_gres = take(2 * static_cast<size_t>(a.rgu_max) * 4);
+  a.off_moe = take(2 * static_cast<size_t>(a.rd_max) * 4);
+  a.off_slots = static_cast<uint32_t>(al(o, 128));
+  const size_t fixed = a.off_slots + 16;
+  const size_t avail = static_cast<size_t>(c->max_smem) > fixed ? c->max_smem - fixed : 0;
+  int nslot = static_cast<int>(avail / a.slot_bytes);
+  if (nslot > K) nslot = K;
+  if (nslot < (K < 2 ? K : 2)) {
+    errf(err, errlen, "the one-token kernel cannot hold two experts' rows per CTA (%u bytes each, %zu free) for this shape", a.slot_bytes, avail);
+    return 1;
+  }
+  a.nslot = nslot;
+  a.smem_bytes = static_cast<uint32_t>(fixed + static_cast<size_t>(nslot) * a.slot_bytes);
+  return 0;
+}
+
+static int validate(const clb200_moe_layer *L, char *err, size_t errlen) {
+  if (!L) { errf(err, errlen, "no layer"); return 1; }
+  const int E = L->n_embd, FF = L->n_ff_exp;
+  if (E < 256 || E % 256 || E > 4096 || FF < 256 || FF % 256 || FF > 4096) {
+    errf(err, errlen, "embedding width %d and expert width %d must be multiples of 256 between 256 and 4096", E, FF);
+    return 1;
+  }
+  if (L->n_expert < 1 || L->n_expert > DECODE_MAX_NE || L->n_used < 1 || L->n_used > DECODE_MAX_K || L->n_used > L->n_expert) {
+    errf(err, errlen, "unsupported expert counts (%d experts, %d used; at most %d and %d)", L->n_expert, L->n_used, DECODE_MAX_NE, DECODE_MAX_K);
+    return 1;
+  }
+  if (!expert_type(L->gate.type) || !expert_type(L->up.type) || !expert_type(L->down.type)) {
+    errf(err, errlen, "expert tensors are %s / %s / %s; this backend computes Q4_K, Q6_K and Q8_0", type_name(L->gate.type),
+         type_name(L->up.type), type_name(L->down.type));
+    return 1;
+  }
+  if (L->gate.type != L->up.type) { errf(err, errlen, "gate (%s) and up (%s) experts must share a type", type_name(L->gate.type), type_name(L->up.type)); return 1; }
+  if (L->gate.rows != FF || L->gate.cols != E || L->up.rows != FF || L->up.cols != E || L->down.rows != E || L->down.cols != FF) {
+    errf(err, errlen, "expert tensor shapes do not match the widths (%d, %d)", E, FF);
+    return 1;
+  }
+  if (L->gate_slab != FF * row_bytes(L->gate.type, E) || L->up_slab != FF * row_bytes(L->up.type, E) ||
+      L->down_slab != E * row_bytes(L->down.type, FF)) {
+    errf(err, errlen, "expert slab sizes do not match rows x row bytes");
+    return 1;
+  }
+  if (!L->gate.p || !L->up.p || !L->down.p || !L->router_f || !L->ffn_norm_f) { errf(err, errlen, "a layer tensor is missing"); return 1; }
+  return 0;
+}
+
+static const char *device_error_text(int code) {
+  switch (code) {
+    case ERR_WAIT_ROUTER: return "timed out waiting for the router logits of other CTAs (are all CTAs resident?)";
+    case ERR_WAIT_EXPERT: return "timed out waiting for an expert's gate/up rows from other CTAs";
+    case ERR_WAIT_COPY: return "timed out waiting for a bulk copy into shared memory";
+    case ERR_BAD_EXPERT: return "an expert id out of range reached the dispatch";
+    default: return "unknown device error";
+  }
+}
+
+}  // namespace clb
+
+extern "C" {
+
+clb200_ctx *clb200_open(int device, char *err, size_t errlen) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) { errf(err, errlen, "no CUDA device: %s", e != cudaSuccess ? cudaGetErrorString(e) : "none found"); return nullptr; }
+  if (device < 0) cudaGetDevice(&device);
+  if (device >= n) { errf(err, errlen, "CUDA device %d does not exist (%d found)", device, n); return nullptr; }
+  if (cudaSetDevice(device) != cudaSuccess) { errf(err, errlen, "cannot use CUDA device %d", device); return nullptr; }
+  cudaDeviceProp p{};
+  cudaGetDeviceProperties(&p, device);
+  if (p.major < 10) { errf(err, errlen, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, p.major, p.minor); return nullptr; }
+  auto *c = new clb200_ctx();
+  c->device = device;
+  c->sms = p.multiProcessorCount;
+  c->max_smem = static_cast<int>(p.sharedMemPerBlockOptin);
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&c->small, 4096) != cudaSuccess || cudaMemset(c->small, 0, 4096) != cudaSuccess) {
+    errf(err, errlen, "cannot set up a stream and 4 KB on device %d", device);
+    clb200_close(c);
+    return nullptr;
+  }
+  c->bytes = 4096;
+  return c;
+}
+
+void clb200_close(clb200_ctx *c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  for (auto &l : c->layers) if (l.block) cudaFree(l.block);
+  if (c->scratch) cudaFree(c->scratch);
+  if (c->small) cudaFree(c->small);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+uint64_t clb200_device_bytes(const clb200_ctx *c) { return c ? c->bytes : 0; }
+
+int clb200_layer_bind(clb200_ctx *c, const clb200_moe_layer *L, int on_device, char *err, size_t errlen) {
+  if (!c) { errf(err, errlen, "no context"); return -1; }
+  if (validate(L, err, errlen)) return -1;
+  cudaSetDevice(c->device);
+  DevLayer dl;
+  dl.d = *L;
+  const size_t E = L->n_embd, NE = L->n_expert;
+  if (!on_device) {
+    const size_t sz[5] = {E * 4, NE * E * 4, NE * L->gate_slab, NE * L->up_slab, NE * L->down_slab};
+    size_t off[5], tot = 0;
+    for (int i = 0; i < 5; ++i) { off[i] = tot; tot = al(tot + sz[i] + 64); }
+    if (cudaMalloc(&dl.block, tot) != cudaSuccess) { errf(err, errlen, "cannot allocate %zu bytes for the layer", tot); return -1; }
+    uint8_t *b = static_cast<uint8_t *>(dl.block);
+    const void *src[5] = {L->ffn_norm_f, L->router_f, L->gate.p, L->up.p, L->down.p};
+    for (int i = 0; i < 5; ++i)
+      if (cudaMemcpy(b + off[i], src[i], sz[i], cudaMemcpyHostToDevice) != cudaSuccess) {
+        errf(err, errlen, "uploading the layer failed");
+        cudaFree(dl.block);
+        return -1;
+      }
+    dl.d.ffn_norm_f = reinterpret_cast<const float *>(b + off[0]);
+    dl.d.router_f = reinterpret_cast<const float *>(b + off[1]);
+    dl.d.gate.p = b + off[2];
+    dl.d.up.p = b + off[3];
+    dl.d.down.p = b + off[4];
+    dl.bytes = tot;
+    for (int i = 0; i < 5; ++i) dl.hkey[i] = src[i];
+    c->bytes += tot;
+  } else {
+    const void *ptrs[5] = {L->ffn_norm_f, L->router_f, L->gate.p, L->up.p, L->down.p};
+    for (int i = 0; i < 5; ++i) {
+      cudaPointerAttributes at{};
+      if (cudaPointerGetAttributes(&at, ptrs[i]) != cudaSuccess || at.type != cudaMemoryTypeDevice || at.device != c->device) {
+        cudaGetLastError();
+        errf(err, errlen, "layer tensor %d is not memory of device %d", i, c->device);
+        return -1;
+      }
+    }
+  }
+  c->layers.push_back(dl);
+  const int h = static_cast<int>(c->layers.size()) - 1;
+  if (!on_device) c->by_gate[L->gate.p] = h;
+  return h;
+}
+
+// Launches the MoE block for T tokens on device data.
+static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,
+                     size_t errlen) {
+  const clb200_moe_layer &L = dl.d;
+  const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+  const Scratch s = plan_scratch(T, E, FF, NE, K);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  uint8_t *sc = c->scratch;
+  if (T == 1) {
+    DecodeArgs a{};
+    if (plan_decode(c, L, a, err, errlen)) return 1;
+    a.x_in = x; a.x_out = x;
+    a.norm = L.ffn_norm_f; a.router = L.router_f;
+    a.gate = L.gate.p; a.up = L.up.p; a.down = L.down.p;
+    a.gate_slab = L.gate_slab; a.up_slab = L.up_slab; a.down_slab = L.down_slab;
+    a.gate_type = L.gate.type; a.up_type = L.up.type; a.down_type = L.down.type;
+    a.E = E; a.FF = FF; a.NE = NE; a.K = K; a.norm_topk = L.norm_topk;
+    a.resid_scale = L.resid_scale; a.eps = L.rms_eps;
+    a.logits = reinterpret_cast<float *>(sc + s.off_logits);
+    a.hg = reinterpret_cast<float *>(sc + s.off_hg);
+    a.sel_out = sel; a.wt_out = wt;
+    a.sync = reinterpret_cast<uint32_t *>(c->small + 64);
+    a.err = c->small;
+    if (!c->attrs_set) {
+      CUDA_OR(cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "kernel attribute");
+      c->attrs_set = true;
+    }
+    int occ = 0;
+    CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_decode_kernel, DECODE_THREADS, a.smem_bytes), "occupancy");
+    if (occ < 1) { errf(err, errlen, "the one-token kernel does not fit on an SM (%u bytes of shared memory)", a.smem_bytes); return 1; }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(c->sms);
+    cfg.blockDim = dim3(DECODE_THREADS);
+    cfg.dynamicSmemBytes = a.smem_bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_OR(cudaLaunchKernelEx(&cfg, moe_decode_kernel, a), "launching the one-token kernel");
+    return 0;
+  }
+  BatchArgs b{};
+  b.x_in = x; b.x_out = x;
+  b.norm = L.ffn_norm_f; b.router = L.router_f;
+  b.gate = L.gate.p; b.up = L.up.p; b.down = L.down.p;
+  b.gate_slab = L.gate_slab; b.up_slab = L.up_slab; b.down_slab = L.down_slab;
+  b.gate_type = L.gate.type; b.up_type = L.up.type; b.down_type = L.down.type;
+  b.T = T; b.E = E; b.FF = FF; b.NE = NE; b.K = K; b.norm_topk = L.norm_topk;
+  b.resid_scale = L.resid_scale; b.eps = L.rms_eps;
+  b.grb = static_cast<uint32_t>(row_bytes(L.gate.type, E));
+  b.drb = static_cast<uint32_t>(row_bytes(L.down.type, FF));
+  b.xn = reinterpret_cast<float *>(sc + s.off_xn);
+  b.xq_qs = reinterpret_cast<int8_t *>(sc + s.off_xq_qs);
+  b.xq_d = reinterpret_cast<float *>(sc + s.off_xq_d);
+  b.xq_bs = reinterpret_cast<int16_t *>(sc + s.off_xq_bs);
+  b.logits = reinterpret_cast<float *>(sc + s.off_logits);
+  b.sel = reinterpret_cast<int *>(sc + s.off_bsel);
+  b.wt = reinterpret_cast<float *>(sc + s.off_bwt);
+  b.counts = reinterpret_cast<int *>(sc + s.off_counts);
+  b.offsets = reinterpret_cast<int *>(sc + s.off_offsets);
+  b.first = reinterpret_cast<int *>(sc + s.off_first);
+  b.pos_token = reinterpret_cast<int *>(sc + s.off_pos_token);
+  b.pos_wt = reinterpret_cast<float *>(sc + s.off_pos_wt);
+  b.slot_pos = reinterpret_cast<int *>(sc + s.off_slot_pos);
+  b.hg = reinterpret_cast<float *>(sc + s.off_bhg);
+  b.hq_qs = reinterpret_cast<int8_t *>(sc + s.off_hq_qs);
+  b.hq_d = reinterpret_cast<float *>(sc + s.off_hq_d);
+  b.hq_bs = reinterpret_cast<int16_t *>(sc + s.off_hq_bs);
+  b.hd = reinterpret_cast<float *>(sc + s.off_hd);
+  b.sel_out = sel; b.wt_out = wt;
+  b.err = c->small;
+  const int rc = launch_batched(b, st);
+  if (rc) { errf(err, errlen, "launching the batched kernels: %s", cudaGetErrorString(static_cast<cudaError_t>(rc))); return 1; }
+  return 0;
+}
+
+int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, float *wt, void *stream, char *err, size_t errlen) {
+  if (!c) { errf(err, errlen, "no context"); return 1; }
+  if (layer < 0 || layer >= static_cast<int>(c->layers.size())) { errf(err, errlen, "no layer %d", layer); return 1; }
+  if (T < 1 || T > 512) { errf(err, errlen, "%d tokens: a call takes 1 to 512", T); return 1; }
+  if (!x) { errf(err, errlen, "no activations"); return 1; }
+  cudaSetDevice(c->device);
+  return run_block(c, c->layers[layer], x, T, sel, wt, stream ? static_cast<cudaStream_t>(stream) : c->stream, err, errlen);
+}
+
+int clb200_status(clb200_ctx *c, char *err, size_t errlen) {
+  if (!c) { errf(err, errlen, "no context"); return 1; }
+  cudaSetDevice(c->device);
+  CUDA_OR(cudaDeviceSynchronize(), "device");
+  int code = 0;
+  CUDA_OR(cudaMemcpy(&code, c->small, 4, cudaMemcpyDeviceToHost), "reading the device error word");
+  if (code) {
+    errf(err, errlen, "device error %d: %s", code, device_error_text(code));
+    cudaMemset(c->small, 0, 4096);   // clear the error and the counters a failed kernel may have left behind
+    return 1;
+  }
+  return 0;
+}
+
+int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, int *sel_out, float *wt_out, char *err,
+                   size_t errlen) {
+  if (!c) { errf(err, errlen, "no context"); return 1; }
+  if (T < 1 || T > 512) { errf(err, errlen, "%d tokens: a call takes 1 to 512", T); return 1; }
+  if (!x || !L) { errf(err, errlen, "no activations or no layer"); return 1; }
+  cudaSetDevice(c->device);
+  int h = -1;
+  auto it = c->by_gate.find(L->gate.p);
+  if (it != c->by_gate.end()) {
+    const DevLayer &dl = c->layers[it->second];
+    if (dl.hkey[0] == L->ffn_norm_f && dl.hkey[1] == L->router_f && dl.hkey[3] == L->up.p && dl.hkey[4] == L->down.p) h = it->second;
+  }
+  if (h < 0) {
+    h = clb200_layer_bind(c, L, 0, err, errlen);
+    if (h < 0) return 1;
+  }
+  const DevLayer &dl = c->layers[h];
+  const int E = L->n_embd, K = L->n_used;
+  const Scratch s = plan_scratch(T, E, L->n_ff_exp, L->n_expert, K);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  float *dx = reinterpret_cast<float *>(c->scratch + s.off_x);
+  int *dsel = reinterpret_cast<int *>(c->scratch + s.off_sel);
+  float *dwt = reinterpret_cast<float *>(c->scratch + s.off_wt);
+  const size_t xb = static_cast<size_t>(T) * E * 4, kb = static_cast<size_t>(T) * K * 4;
+  CUDA_OR(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, c->stream), "copying x to the device");
+  if (run_block(c, dl, dx, T, dsel, dwt, c->stream, err, errlen)) return 1;
+  CUDA_OR(cudaMemcpyAsync(x, dx, xb, cudaMemcpyDeviceToHost, c->stream), "copying x back");
+  if (sel_out) CUDA_OR(cudaMemcpyAsync(sel_out, dsel, kb, cudaMemcpyDeviceToHost, c->stream), "copying the routing back");
+  if (wt_out) CUDA_OR(cudaMemcpyAsync(wt_out, dwt, kb, cudaMemcpyDeviceToHost, c->stream), "copying the weights back");
+  CUDA_OR(cudaStreamSynchronize(c->stream), "running the MoE block");
+  return clb200_status(c, err, errlen);
+}
+
+}  // extern "C"

@@ -1,0 +1,354 @@
+// The batched MoE block (T > 1 tokens): the reference's c/src/forward.c:1132-1210.
+//
+//   route_kernel     per (token, 32 experts): rmsnorm (double sum of squares), Q8_K of xn, the reference's dotf logits
+//   topk_kernel      per token: softmax (double sum), top-k by repeated arg-max with ties to the lower id, renormalisation
+//   dispatch_kernel  counting sort of the T*K (token, expert) slots by expert; each expert's tokens in ascending token order
+//                    (the reference's who[] list, c/src/forward.c:1189-1190), plus each expert's first appearance
+//   gateup_kernel    per (expert, 16 rows): gate and up row dots for every token of that expert (weights read once, staged
+//                    in shared memory by a bulk copy), SwiGLU -> hg by dispatch position
+//   hq_kernel        Q8_K of each hg row (K-quant down weights)
+//   down_kernel      per (expert, 16 rows): down row dots for every token of that expert -> hd by dispatch position
+//   combine_kernel   per token: moe = sum over its experts in order of first appearance of wt*hd (the reference's todo
+//                    order, c/src/forward.c:1163-1164), x += resid_scale * moe
+#include <cstdio>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "rowdot.cuh"
+
+namespace clb {
+
+constexpr int BT = 256;          // threads of the batched kernels
+constexpr int BNW = BT / 32;
+constexpr int ROUTE_EXPERTS = BT / 8;
+constexpr int ROWS_PER_CTA = 16; // weight rows per CTA in the expert kernels
+
+__global__ void __launch_bounds__(BT) route_kernel(const BatchArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  float *xn = reinterpret_cast<float *>(sm);
+  double *red = reinterpret_cast<double *>(xn + a.E);
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, E = a.E;
+  const float *x = a.x_in + static_cast<size_t>(t) * E;
+  double ss = 0.0;
+  for (int i = tid; i < E; i += BT) { const float v = x[i]; xn[i] = v; ss += static_cast<double>(v) * v; }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  double tot = 0.0;
+  for (int w = 0; w < BNW; ++w) tot += red[w];
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / static_cast<double>(E)), a.eps)));
+  for (int i = tid; i < E; i += BT) xn[i] = __fmul_rn(__fmul_rn(xn[i], scale), a.norm[i]);
+  __syncthreads();
+  if (blockIdx.y == 0) {
+    for (int i = tid; i < E; i += BT) a.xn[static_cast<size_t>(t) * E + i] = xn[i];
+    q8k_quantize_block(xn, E, a.xq_qs + static_cast<size_t>(t) * E, a.xq_d + static_cast<size_t>(t) * (E / 256),
+                       a.xq_bs + static_cast<size_t>(t) * (E / 16), warp, BNW, lane);
+  }
+  const int grp = tid >> 3, l8 = tid & 7;
+  const int e = blockIdx.y * ROUTE_EXPERTS + grp;
+  float s = 0.f;
+  if (e < a.NE) {
+    const float *w = a.router + static_cast<size_t>(e) * E;
+    for (int i = l8; i < E; i += 8) s = __fadd_rn(s, __fmul_rn(__ldg(w + i), xn[i]));
+  }
+  float p[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) p[l] = __shfl_sync(FULL, s, (lane & ~7) + l);
+  if (e < a.NE && l8 == 0)
+    a.logits[static_cast<size_t>(t) * a.NE + e] =
+        __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])), __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+}
+
+__global__ void __launch_bounds__(32) topk_kernel(const BatchArgs a) {
+  const int t = blockIdx.x, lane = threadIdx.x, NE = a.NE, K = a.K;
+  const float *lg = a.logits + static_cast<size_t>(t) * NE;
+  float v[DECODE_MAX_NE / 32];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < DECODE_MAX_NE / 32; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < NE ? lg[e] : -INFINITY;
+    mx = fmaxf(mx, v[j]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  double sum = 0.0;
+#pragma unroll
+  for (int j = 0; j < DECODE_MAX_NE / 32; ++j)
+    if (lane + 32 * j < NE) { v[j] = expf_cr(__fsub_rn(v[j], mx)); sum += static_cast<double>(v[j]); }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(FULL, sum, o);
+  uint32_t used = 0;
+#pragma unroll
+  for (int j = 0; j < DECODE_MAX_NE / 32; ++j) {
+    if (lane + 32 * j < NE) v[j] = __double2float_rn(__ddiv_rn(static_cast<double>(v[j]), sum));
+    else used |= 1u << j;
+  }
+  __shared__ int s_sel[DECODE_MAX_K];
+  __shared__ float s_wt[DECODE_MAX_K];
+  for (int k = 0; k < K; ++k) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < DECODE_MAX_NE / 32; ++j)
+      if (!((used >> j) & 1u) && (v[j] > bv || be == 0x7fffffff)) { bv = v[j]; be = lane + 32 * j; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(FULL, bv, o);
+      const int oe = __shfl_xor_sync(FULL, be, o);
+      if (oe != 0x7fffffff && (be == 0x7fffffff || ov > bv || (ov == bv && oe < be))) { bv = ov; be = oe; }
+    }
+    if ((be & 31) == lane) used |= 1u << (be >> 5);
+    if (lane == 0) { s_sel[k] = be; s_wt[k] = bv; }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    if (a.norm_topk) {
+      float z = 0.f;
+      for (int k = 0; k < K; ++k) z = __fadd_rn(z, s_wt[k]);
+      if (z > 0.f) for (int k = 0; k < K; ++k) s_wt[k] = __fdiv_rn(s_wt[k], z);
+    }
+  }
+  __syncwarp();
+  for (int k = lane; k < K; k += 32) {
+    const size_t i = static_cast<size_t>(t) * K + k;
+    a.sel[i] = s_sel[k];
+    a.wt[i] = s_wt[k];
+    if (a.sel_out) a.sel_out[i] = s_sel[k];
+    if (a.wt_out) a.wt_out[i] = s_wt[k];
+  }
+}
+
+// One CTA. The (expert, token) pairs form a bit matrix (expert rows, token bits); an expert's tokens are its set bits in
+// ascending order, so its dispatch positions come from population counts.
+__global__ void __launch_bounds__(1024) dispatch_kernel(const BatchArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int NE = a.NE, K = a.K, T = a.T, nw = (T + 31) / 32;
+  uint32_t *bits = reinterpret_cast<uint32_t *>(sm);            // [NE][nw]
+  int *cnt = reinterpret_cast<int *>(bits + NE * nw);           // [NE]
+  int *off = cnt + NE;                                          // [NE + 1]
+  int *first = off + NE + 1;                                    // [NE]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  for (int i = tid; i < NE * nw; i += blockDim.x) bits[i] = 0;
+  for (int e = tid; e < NE; e += blockDim.x) first[e] = 0x7fffffff;
+  __syncthreads();
+  for (int s = tid; s < T * K; s += blockDim.x) {
+    const int t = s / K, e = a.sel[s];
+    if (e < 0 || e >= NE) { set_error(a.err, ERR_BAD_EXPERT); continue; }
+    atomicOr(&bits[e * nw + t / 32], 1u << (t & 31));
+    atomicMin(&first[e], s);
+  }
+  __syncthreads();
+  for (int e = warp; e < NE; e += nwarps) {
+    int c = 0;
+    for (int w = lane; w < nw; w += 32) c += __popc(bits[e * nw + w]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(FULL, c, o);
+    if (lane == 0) cnt[e] = c;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < NE; ++e) { off[e] = acc; acc += cnt[e]; }
+    off[NE] = acc;
+  }
+  __syncthreads();
+  for (int e = tid; e < NE; e += blockDim.x) { a.counts[e] = cnt[e]; a.offsets[e] = off[e]; a.first[e] = first[e]; }
+  if (tid == 0) a.offsets[NE] = off[NE];
+  for (int e = warp; e < NE; e += nwarps) {
+    int base = off[e];
+    for (int w0 = 0; w0 < nw; w0 += 32) {
+      const int w = w0 + lane;
+      const uint32_t word = w < nw ? bits[e * nw + w] : 0u;
+      int c = __popc(word), incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) { const int v = __shfl_up_sync(FULL, incl, o); if (lane >= o) incl += v; }
+      int pos = base + incl - c;
+      uint32_t m = word;
+      while (m) {
+        const int b = __ffs(m) - 1;
+        m &= m - 1;
+        const int t = 32 * w + b;
+        int k = 0;
+        while (k < K && a.sel[static_cast<size_t>(t) * K + k] != e) ++k;
+        a.pos_token[pos] = t;
+        a.pos_wt[pos] = a.wt[static_cast<size_t>(t) * K + k];
+        a.slot_pos[static_cast<size_t>(t) * K + k] = pos;
+        ++pos;
+      }
+      base += __shfl_sync(FULL, incl, 31);
+    }
+  }
+}
+
+// gate and up rows [r0, r0+R) of expert e for each of its tokens.
+__global__ void __launch_bounds__(BT) gateup_kernel(const BatchArgs a) {
+  const int e = blockIdx.x, n = a.counts[e];
+  if (n == 0) return;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, E = a.E, FF = a.FF;
+  const int r0 = blockIdx.y * ROWS_PER_CTA, R = min(ROWS_PER_CTA, FF - r0);
+  const uint32_t grb = a.grb;
+  const uint32_t seg = (R * grb + 32 + 15) & ~15u;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(sm);
+  float *xf = reinterpret_cast<float *>(sm + 16);                          // [E] (Q8_0: the token's xn)
+  float *res = xf + E;                                                     // [2 * ROWS_PER_CTA]
+  uint8_t *wbuf = reinterpret_cast<uint8_t *>(res + 2 * ROWS_PER_CTA);
+  const uint8_t *sg = a.gate + static_cast<size_t>(e) * a.gate_slab + static_cast<size_t>(r0) * grb;
+  const uint8_t *su = a.up + static_cast<size_t>(e) * a.up_slab + static_cast<size_t>(r0) * grb;
+  const uint32_t lg = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(sg) & 15u), lu = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(su) & 15u);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+    const uint32_t ng = (lg + R * grb + 15u) & ~15u, nu = (lu + R * grb + 15u) & ~15u;
+    mbar_arrive_expect_tx(bar, ng + nu);
+    bulk_copy_g2s(wbuf, sg - lg, ng, bar);
+    bulk_copy_g2s(wbuf + seg, su - lu, nu, bar);
+  }
+  __syncthreads();
+  const uint8_t *g = wbuf + lg, *u = wbuf + seg + lu;
+  const bool q80 = a.gate_type == T_Q8_0;
+  const int nb = q80 ? E / 32 : E / 256;
+  const RowShape rs = row_shape(q80 ? nb : 4 * nb);
+  const int sub = lane / rs.LG, lig = lane % rs.LG;
+  if (!mbar_wait_bounded(bar, 0)) { set_error(a.err, ERR_WAIT_COPY); return; }
+  const int p0 = a.offsets[e];
+  for (int i = 0; i < n; ++i) {
+    const int pos = p0 + i, t = a.pos_token[pos];
+    KQAct act;
+    if (q80) {
+      __syncthreads();
+      for (int j = tid; j < E; j += BT) xf[j] = a.xn[static_cast<size_t>(t) * E + j];
+      __syncthreads();
+    } else {
+      load_kq_act(a.gate_type, a.xq_qs + static_cast<size_t>(t) * E, a.xq_d + static_cast<size_t>(t) * (E / 256),
+                  a.xq_bs + static_cast<size_t>(t) * (E / 16), nb, rs, lig, act);
+    }
+    for (int base = warp * rs.RPW; base < 2 * R; base += BNW * rs.RPW) {
+      const int task = base + sub;
+      const bool active = sub < rs.RPW && task < 2 * R;
+      const int r = task < R ? task : task - R;
+      const uint8_t *row = (task < R ? g : u) + static_cast<size_t>(active ? r : 0) * grb;
+      const float v = q80 ? q80_row(row, nb, rs, lig, sub * rs.LG, xf, active) : kq_row(a.gate_type, row, nb, rs, lig, sub * rs.LG, act, active);
+      if (active && lig == 0) res[task] = v;
+    }
+    __syncthreads();
+    for (int r = tid; r < R; r += BT) a.hg[static_cast<size_t>(pos) * FF + r0 + r] = silu_mul(res[r], res[R + r]);
+    __syncthreads();
+  }
+}
+
+__global__ void hq_kernel(const BatchArgs a, int npos) {
+  const int pos = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, FF = a.FF;
+  if (pos >= npos) return;
+  q8k_quantize_block(a.hg + static_cast<size_t>(pos) * FF, FF, a.hq_qs + static_cast<size_t>(pos) * FF,
+                     a.hq_d + static_cast<size_t>(pos) * (FF / 256), a.hq_bs + static_cast<size_t>(pos) * (FF / 16), warp,
+                     blockDim.x >> 5, lane);
+}
+
+// down rows [r0, r0+R) of expert e for each of its tokens.
+__global__ void __launch_bounds__(BT) down_kernel(const BatchArgs a) {
+  const int e = blockIdx.x, n = a.counts[e];
+  if (n == 0) return;
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, E = a.E, FF = a.FF;
+  const int r0 = blockIdx.y * ROWS_PER_CTA, R = min(ROWS_PER_CTA, E - r0);
+  const uint32_t drb = a.drb;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(sm);
+  float *xf = reinterpret_cast<float *>(sm + 16);   // [FF] (Q8_0: the token's hg)
+  uint8_t *wbuf = reinterpret_cast<uint8_t *>(xf + FF);
+  const uint8_t *src = a.down + static_cast<size_t>(e) * a.down_slab + static_cast<size_t>(r0) * drb;
+  const uint32_t lo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(src) & 15u);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+    const uint32_t n16 = (lo + R * drb + 15u) & ~15u;
+    mbar_arrive_expect_tx(bar, n16);
+    bulk_copy_g2s(wbuf, src - lo, n16, bar);
+  }
+  __syncthreads();
+  const uint8_t *rows = wbuf + lo;
+  const bool q80 = a.down_type == T_Q8_0;
+  const int nb = q80 ? FF / 32 : FF / 256;
+  const RowShape rs = row_shape(q80 ? nb : 4 * nb);
+  const int sub = lane / rs.LG, lig = lane % rs.LG;
+  if (!mbar_wait_bounded(bar, 0)) { set_error(a.err, ERR_WAIT_COPY); return; }
+  const int p0 = a.offsets[e];
+  for (int i = 0; i < n; ++i) {
+    const int pos = p0 + i;
+    KQAct act;
+    if (q80) {
+      __syncthreads();
+      for (int j = tid; j < FF; j += BT) xf[j] = a.hg[static_cast<size_t>(pos) * FF + j];
+      __syncthreads();
+    } else {
+      load_kq_act(a.down_type, a.hq_qs + static_cast<size_t>(pos) * FF, a.hq_d + static_cast<size_t>(pos) * (FF / 256),
+                  a.hq_bs + static_cast<size_t>(pos) * (FF / 16), nb, rs, lig, act);
+    }
+    for (int base = warp * rs.RPW; base < R; base += BNW * rs.RPW) {
+      const int r = base + sub;
+      const bool active = sub < rs.RPW && r < R;
+      const uint8_t *row = rows + static_cast<size_t>(active ? r : 0) * drb;
+      const float v = q80 ? q80_row(row, nb, rs, lig, sub * rs.LG, xf, active) : kq_row(a.down_type, row, nb, rs, lig, sub * rs.LG, act, active);
+      if (active && lig == 0) a.hd[static_cast<size_t>(pos) * E + r0 + r] = v;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(BT) combine_kernel(const BatchArgs a) {
+  const int t = blockIdx.x, K = a.K, E = a.E;
+  __shared__ int s_pos[DECODE_MAX_K];
+  __shared__ float s_w[DECODE_MAX_K];
+  if (threadIdx.x == 0) {
+    int order[DECODE_MAX_K], key[DECODE_MAX_K];
+    for (int k = 0; k < K; ++k) {   // insertion sort of the token's slots by their expert's first appearance
+      const int kk = a.first[a.sel[static_cast<size_t>(t) * K + k]];
+      int j = k;
+      while (j > 0 && key[j - 1] > kk) { key[j] = key[j - 1]; order[j] = order[j - 1]; --j; }
+      key[j] = kk; order[j] = k;
+    }
+    for (int j = 0; j < K; ++j) {
+      s_pos[j] = a.slot_pos[static_cast<size_t>(t) * K + order[j]];
+      s_w[j] = a.wt[static_cast<size_t>(t) * K + order[j]];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += BT) {
+    float m = 0.f;
+    for (int j = 0; j < K; ++j) m = __fadd_rn(m, __fmul_rn(s_w[j], a.hd[static_cast<size_t>(s_pos[j]) * E + i]));
+    const size_t xi = static_cast<size_t>(t) * E + i;
+    a.x_out[xi] = __fadd_rn(a.x_in[xi], __fmul_rn(a.resid_scale, m));
+  }
+}
+
+static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+
+int launch_batched(const BatchArgs &a, void *stream_) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  const int T = a.T, E = a.E, FF = a.FF, NE = a.NE, K = a.K;
+  const size_t route_smem = E * 4 + BNW * 8;
+  route_kernel<<<dim3(T, (NE + ROUTE_EXPERTS - 1) / ROUTE_EXPERTS), BT, route_smem, st>>>(a);
+  topk_kernel<<<T, 32, 0, st>>>(a);
+  const int nw = (T + 31) / 32;
+  const size_t disp_smem = static_cast<size_t>(NE) * nw * 4 + (3 * NE + 1) * 4;
+  dispatch_kernel<<<1, 1024, disp_smem, st>>>(a);
+  const size_t gu_smem = 16 + E * 4 + 2 * ROWS_PER_CTA * 4 + 2 * align16(ROWS_PER_CTA * a.grb + 32) + 16;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attrs[64] = {};
+  if (dev < 64 && !attrs[dev]) {   // per device: the attribute belongs to the current device's context
+    cudaFuncSetAttribute(gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attrs[dev] = true;
+  }
+  gateup_kernel<<<dim3(NE, (FF + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, gu_smem, st>>>(a);
+  if (a.down_type != T_Q8_0) hq_kernel<<<T * K, 32 * (FF / 256), 0, st>>>(a, T * K);
+  const size_t dn_smem = 16 + FF * 4 + align16(ROWS_PER_CTA * a.drb + 32) + 16;
+  down_kernel<<<dim3(NE, (E + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, dn_smem, st>>>(a);
+  combine_kernel<<<T, BT, 0, st>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace clb

@@ -1,0 +1,117 @@
+// Shared device code: PTX wrappers (mbarriers, bulk copies, programmatic dependent launch), bounded waits, and the
+// exactly-rounded scalar steps of the reference's arithmetic.
+//
+// Parity rule for this whole library: the reference is built without FMA contraction (c/Makefile:3-9, -std=c11), so
+// every float operation that must match it is written with an explicit round-to-nearest intrinsic (__fmul_rn, __fadd_rn,
+// __fsub_rn, __fdiv_rn, __fsqrt_rn) and the library is compiled with --fmad=false.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define CLB_DEV __device__ __forceinline__
+
+namespace clb {
+
+// ggml type ids (the reference's CL_T_*, c/src/quant.h:7)
+constexpr uint32_t T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14;
+
+// Device error codes written to the context's error word (first error wins).
+enum : int { ERR_NONE = 0, ERR_WAIT_ROUTER = 1, ERR_WAIT_EXPERT = 2, ERR_WAIT_COPY = 3, ERR_BAD_EXPERT = 4, ERR_WAIT_GRID = 5 };
+
+// A spin on a flag written by another CTA gives up after this many polls (each with a short sleep): about a second.
+constexpr uint32_t SPIN_LIMIT = 1u << 22;
+
+CLB_DEV uint32_t smem_addr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// ---- mbarrier + bulk copy (global -> shared, no multicast) -------------------------------------------------------------
+CLB_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+CLB_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+CLB_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+CLB_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Untiled bulk copy: dst (shared) and src (global) 16-byte aligned, bytes a multiple of 16.
+CLB_DEV void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+CLB_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for an mbarrier phase; false when the limit ran out.
+CLB_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(32);
+  }
+  return false;
+}
+
+// ---- programmatic dependent launch ---------------------------------------------------------------------------------------
+CLB_DEV void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+CLB_DEV void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- inter-CTA flags -------------------------------------------------------------------------------------------------------
+CLB_DEV uint32_t ld_acquire(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+CLB_DEV void red_release_add(uint32_t *p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Waits until *p >= target (bounded). Call from one thread.
+CLB_DEV bool wait_counter(const uint32_t *p, uint32_t target) {
+  for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
+    if (ld_acquire(p) >= target) return true;
+    if (i > 32) __nanosleep(64);
+  }
+  return false;
+}
+CLB_DEV void set_error(int *err, int code) { atomicCAS(err, 0, code); }
+
+// ---- the reference's scalar steps, exactly rounded ---------------------------------------------------------------------------
+// fp16 bits to float: exact (every half is a float).
+CLB_DEV float f16_bits_to_f32(uint16_t h) {
+  float f;
+  asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"(h));
+  return f;
+}
+// expf, correctly rounded except in vanishingly rare double-rounding cases: exp in double precision, rounded once to float.
+// (The reference calls glibc's expf, which is within about half an ulp, so the two agree to an ulp.)
+CLB_DEV float expf_cr(float x) { return __double2float_rn(exp(static_cast<double>(x))); }
+// silu(g) * u as the reference writes it: g / (1 + expf(-g)) * u (c/src/forward.c:1018)
+CLB_DEV float silu_mul(float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g))), u); }
+
+// Unaligned little-endian 32-bit load from shared memory (reads the aligned word after p too: keep 4 bytes of slack).
+CLB_DEV uint32_t lds_u32_unaligned(const uint8_t *p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t *q = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+  return __funnelshift_r(q[0], q[1], static_cast<uint32_t>(a & 3) * 8u);
+}
+CLB_DEV uint16_t lds_u16(const uint8_t *p) { return static_cast<uint16_t>(p[0] | (p[1] << 8)); }
+
+// 6-bit scale and min of sub-block j (0..7) of a Q4_K block from its 12 packed bytes (ggml layout; c/src/quant.c:36-40).
+CLB_DEV void q4k_scale_min(const uint8_t *s12, int j, int &sc, int &mn) {
+  if (j < 4) {
+    sc = s12[j] & 63;
+    mn = s12[j + 4] & 63;
+  } else {
+    sc = (s12[j + 4] & 15) | ((s12[j - 4] >> 6) << 4);
+    mn = (s12[j + 4] >> 4) | ((s12[j] >> 6) << 4);
+  }
+}
+
+CLB_DEV uint32_t block_elems(uint32_t t) { return t == T_Q8_0 ? 32u : 256u; }
+CLB_DEV uint32_t block_bytes(uint32_t t) { return t == T_Q8_0 ? 34u : t == T_Q4_K ? 144u : 210u; }
+
+}  // namespace clb

@@ -1,0 +1,72 @@
+// Arguments and limits of the one-token MoE kernel (decode.cu) and the batched kernels (batched.cu).
+#pragma once
+#include <cstdint>
+
+namespace clb {
+
+constexpr int DECODE_THREADS = 256;
+constexpr int DECODE_MAX_NE = 256;   // experts per layer the one-token kernel ranks in one warp
+constexpr int DECODE_MAX_K = 32;     // experts used per token
+
+struct DecodeArgs {
+  const float *x_in;
+  float *x_out;                  // may equal x_in
+  const float *norm, *router;
+  const uint8_t *gate, *up, *down;
+  uint64_t gate_slab, up_slab, down_slab;
+  uint32_t gate_type, up_type, down_type;
+  int E, FF, NE, K, norm_topk;
+  float resid_scale, eps;
+  float *logits;                 // [NE] scratch
+  float *hg;                     // [K * FF] scratch
+  int *sel_out;                  // [K] or null
+  float *wt_out;                 // [K] or null
+  uint32_t *sync;                // [0] logits done, [1..K] experts whose hg is complete, [K+1] CTAs finished; zero on entry
+  int *err;                      // first device error
+  // shared-memory plan (host-computed)
+  int nslot, rgu_max, rd_max;
+  uint32_t grb, drb, gseg, dseg, slot_bytes;
+  uint32_t off_bars, off_xn, off_xq, off_router, off_misc, off_hq, off_gres, off_moe, off_slots, smem_bytes;
+};
+
+__global__ void moe_decode_kernel(const DecodeArgs a);
+
+// ---- batched path ------------------------------------------------------------------------------------------------------
+struct BatchArgs {
+  const float *x_in;
+  float *x_out;
+  const float *norm, *router;
+  const uint8_t *gate, *up, *down;
+  uint64_t gate_slab, up_slab, down_slab;
+  uint32_t gate_type, up_type, down_type;
+  int T, E, FF, NE, K, norm_topk;
+  float resid_scale, eps;
+  uint32_t grb, drb;
+  // scratch
+  float *xn;            // [T * E]
+  int8_t *xq_qs;        // [T * E]
+  float *xq_d;          // [T * E / 256]
+  int16_t *xq_bs;       // [T * E / 16]
+  float *logits;        // [T * NE]
+  int *sel;             // [T * K]
+  float *wt;            // [T * K]
+  int *counts;          // [NE]
+  int *offsets;         // [NE + 1]
+  int *first;           // [NE] first appearance (slot index t*K+k) of each expert
+  int *pos_token;       // [T * K] dispatch position -> token
+  float *pos_wt;        // [T * K] dispatch position -> routing weight
+  int *slot_pos;        // [T * K] (t, k) -> dispatch position
+  float *hg;            // [T * K * FF] by dispatch position
+  int8_t *hq_qs;        // [T * K * FF]
+  float *hq_d;          // [T * K * FF / 256]
+  int16_t *hq_bs;       // [T * K * FF / 16]
+  float *hd;            // [T * K * E] by dispatch position
+  int *sel_out;         // [T * K] or null
+  float *wt_out;        // [T * K] or null
+  int *err;
+};
+
+// Launches the batched path on `stream`; returns a CUDA error code.
+int launch_batched(const BatchArgs &a, void *stream);
+
+}  // namespace clb

@@ -1,0 +1,108 @@
+/*
+ * clutor-b200: the Clutor engine's mixture-of-experts feed-forward block on NVIDIA B200 (sm_100a), behind a plain C ABI.
+ *
+ * Two ways in, both drop-ins for the reference engine's C host code:
+ *
+ *  1. clb200_moe_ffn(): the whole per-layer MoE block in one call. It replaces the inline block of the reference's forward
+ *     pass, c/src/forward.c:949-1033 (one token: rmsnorm, router, softmax/top-k/renorm, Q8_K quantization, gate/up products,
+ *     SwiGLU, down products, weighted combine, residual) and c/src/forward.c:1132-1210 (a batch of tokens: the same per token,
+ *     with each chosen expert's weights read once for all the tokens that chose it). The layer description mirrors the
+ *     fields the reference binds in cl_fwd_open (c/src/forward.h:18-29, c/src/forward.c:204-240).
+ *
+ *  2. clb200_backend(): a cl_backend (c/src/backend.h:9-13) named "b200" for the reference's plugin seam, cl_matvec_batch
+ *     (c/src/quant.c:995-1004). Register it with cl_backend_register() and select it with CLUTOR_BACKEND=b200; it runs the
+ *     Q4_K, Q6_K and Q8_0 products on the GPU and leaves every other type to the CPU, as the seam prescribes.
+ *
+ * Conventions follow the reference: functions that can fail return 0 on success and 1 on failure with a message written to
+ * err (snprintf into errlen bytes), as cl_fwd_open / cl_fwd_step do (c/src/forward.c:24-27). No entry point falls back to
+ * the CPU: without a usable CUDA device, clb200_open fails.
+ *
+ * Weights stay in their GGUF block layout on the device: the device format is the file format.
+ */
+#ifndef CLB200_H
+#define CLB200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CLB200_ABI_VERSION 1
+
+/* ggml tensor type ids, the values of the reference's CL_T_* (c/src/quant.h:7). Expert weights may be Q4_K, Q6_K or Q8_0. */
+enum { CLB200_T_F32 = 0, CLB200_T_F16 = 1, CLB200_T_Q8_0 = 8, CLB200_T_Q4_K = 12, CLB200_T_Q6_K = 14 };
+
+/* rows x cols weights of `type`, row-major, cols is the input width: the reference's cl_w (c/src/forward.h:18), same layout. */
+typedef struct { const uint8_t *p; uint32_t type; int rows, cols; } clb200_w;
+
+/* One MoE layer: what the reference's MoE block reads from cl_fwd_layer and cl_fwd (c/src/forward.h:20-29, 35-51).
+ * gate/up/down are the fused expert tensors ffn_gate_exps / ffn_up_exps / ffn_down_exps: rows x cols is ONE expert
+ * (gate/up: n_ff_exp x n_embd, down: n_embd x n_ff_exp) and n_expert slabs of gate_slab / up_slab / down_slab bytes follow
+ * one another. ffn_norm_f and router_f are the fp32 copies the reference makes at load time (c/src/forward.c:234-239). */
+typedef struct {
+  const float *ffn_norm_f;   /* [n_embd] */
+  const float *router_f;     /* [n_expert * n_embd], row e scores expert e */
+  clb200_w gate, up, down;
+  uint64_t gate_slab, up_slab, down_slab;
+  int n_embd, n_ff_exp, n_expert, n_used;
+  int norm_topk;             /* 1: renormalise the chosen weights to sum to 1 (qwen3moe, granitemoe); 0: raw probabilities (olmoe) */
+  float resid_scale;         /* x += resid_scale * moe (1 except granitemoe) */
+  float rms_eps;
+} clb200_moe_layer;
+
+typedef struct clb200_ctx clb200_ctx;
+
+/* Opens a context on CUDA device `device` (-1: the current device). One stream per context; a context is used by one host
+ * thread at a time, like the reference's single forward thread. */
+clb200_ctx *clb200_open(int device, char *err, size_t errlen);
+void clb200_close(clb200_ctx *c);
+
+/* The MoE block for T tokens (1 <= T <= 512, the reference's CL_PS_B) with HOST pointers: x [T x n_embd] is read and updated
+ * in place (x += resid_scale * moe); sel_out / wt_out [T x n_used] (may be NULL) receive each token's chosen experts, best
+ * first, and their weights, as cl_fwd_route does (c/src/forward.h:94). Synchronous. The layer's weights are uploaded to the
+ * device on first use and kept, keyed by the host pointers (they must stay valid and unchanged, as the reference's mapped
+ * model does). Replaces c/src/forward.c:949-1033 (T = 1) and :1132-1210 (T > 1). */
+int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, int *sel_out, float *wt_out, char *err,
+                   size_t errlen);
+
+/* Device-resident use (no host copies): registers a layer and returns a handle >= 0 (or -1 with err set). With on_device = 1
+ * every pointer in L is a device pointer and is used in place (the caller keeps the memory alive); with on_device = 0 the
+ * tensors are copied to the device now. */
+int clb200_layer_bind(clb200_ctx *c, const clb200_moe_layer *L, int on_device, char *err, size_t errlen);
+/* Same block as clb200_moe_ffn on a bound layer with DEVICE pointers x [T x n_embd] (updated in place), sel [T x n_used] and
+ * wt [T x n_used] (either may be NULL). Asynchronous on `stream` (a cudaStream_t; NULL: the context's stream). Argument errors
+ * are reported at once; device-side errors (a timed-out wait) by clb200_status. Safe to capture in a CUDA graph once the
+ * context's scratch has been sized by an earlier call with the same or larger T. */
+int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, float *wt, void *stream, char *err,
+                       size_t errlen);
+/* Waits for the context's work and reports a device-side error recorded since the last call (0: none). */
+int clb200_status(clb200_ctx *c, char *err, size_t errlen);
+/* Bytes of device memory the context holds for layers and scratch. */
+uint64_t clb200_device_bytes(const clb200_ctx *c);
+
+/* ---- the plugin seam: a cl_backend for cl_matvec_batch ------------------------------------------------------------------- */
+/* Layout-compatible copies of the reference's cl_q8k, cl_xq and cl_mv (c/src/quant.h:22-34) and cl_backend (backend.h:9-13). */
+typedef struct { float d; int8_t qs[256]; int16_t bsums[16]; } clb200_q8k;
+typedef struct { clb200_q8k *b; int n; } clb200_xq;
+typedef struct {
+  uint32_t type; const void *w; int rows, cols; const float *xf; const clb200_xq *xq; float *out;
+  int nb; size_t xf_stride, out_stride;
+} clb200_mv;
+typedef struct {
+  const char *name;
+  int (*supports)(uint32_t type);
+  void (*matvec_batch)(const clb200_mv *jobs, int n);
+} clb200_backend_t;
+
+/* The "b200" backend. supports() is 1 for Q4_K, Q6_K and Q8_0. matvec_batch() runs the jobs on the GPU (device from
+ * CLUTOR_B200_DEVICE, default 0) and returns when the results are in the jobs' out arrays: K-quant jobs use the caller's
+ * Q8_K activations and give the CPU's numbers bit for bit; Q8_0 jobs use the float activations in the CPU's summation order.
+ * Weights are uploaded on first use, keyed by host pointer. The seam has no error channel: on a device error the backend
+ * prints the error to stderr and aborts, rather than returning wrong numbers. */
+const clb200_backend_t *clb200_backend(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
