@@ -81,6 +81,7 @@ def lib() -> C.CDLL:
         L.clb200_layer_bind.argtypes = [C.c_void_p, C.POINTER(MoELayer), C.c_int, C.c_char_p, C.c_size_t]
         L.clb200_moe_ffn_dev.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
         L.clb200_status.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_layer_release.argtypes = [C.c_void_p, C.c_int]
         L.clb200_device_bytes.restype = C.c_uint64
         L.clb200_device_bytes.argtypes = [C.c_void_p]
         L.clb200_backend.restype = C.POINTER(Backend)
@@ -172,6 +173,11 @@ class Context:
             raise ClutorError(self._err.value.decode())
         self._keep.append(layer)
         return h
+
+    def release(self, handle: int) -> None:
+        """Frees a bound layer's device copy (clb200_layer_release)."""
+        if lib().clb200_layer_release(self.handle, handle):
+            raise ClutorError(f"no layer {handle}")
 
     def moe_ffn_dev(self, handle: int, x, sel=None, wt=None, stream=None) -> None:
         """The device entry point (clb200_moe_ffn_dev) on torch CUDA tensors; asynchronous on `stream` (a torch stream)."""

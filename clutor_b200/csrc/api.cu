@@ -53,10 +53,34 @@ static size_t al(size_t v, size_t a = 256) { return (v + a - 1) / a * a; }
 
 struct DevLayer {
   clb200_moe_layer d{};              // device pointers
-  const void *hkey[5] = {};          // host pointers of router, norm, gate, up, down (0 when bound on the device)
+  const void *hkey[5] = {};          // host pointers of norm, router, gate, up, down (0 when bound on the device)
+  uint64_t fp = 0;                   // fingerprint of the host tensors' shapes and edge bytes (uploaded layers)
   void *block = nullptr;             // the owned device copy (upload), else null
   size_t bytes = 0;
+  bool live = false;
 };
+
+// FNV-1a over the layer's shape fields and the first and last 64 bytes of each host tensor: a cheap check that a host
+// pointer seen before still holds the weights that were uploaded from it (a freed and reused buffer usually does not).
+static uint64_t fingerprint(const clb200_moe_layer *L) {
+  uint64_t h = 1469598103934665603ull;
+  auto mix = [&](const void *p, size_t n) {
+    const uint8_t *b = static_cast<const uint8_t *>(p);
+    for (size_t i = 0; i < n; ++i) { h ^= b[i]; h *= 1099511628211ull; }
+  };
+  const int shape[9] = {L->n_embd, L->n_ff_exp, L->n_expert, L->n_used, L->norm_topk, static_cast<int>(L->gate.type),
+                        static_cast<int>(L->up.type), static_cast<int>(L->down.type), 0};
+  mix(shape, sizeof shape);
+  const size_t E = L->n_embd, NE = L->n_expert;
+  const void *ptr[5] = {L->ffn_norm_f, L->router_f, L->gate.p, L->up.p, L->down.p};
+  const size_t sz[5] = {E * 4, NE * E * 4, NE * L->gate_slab, NE * L->up_slab, NE * L->down_slab};
+  for (int i = 0; i < 5; ++i) {
+    const size_t n = sz[i] < 64 ? sz[i] : 64;
+    mix(ptr[i], n);
+    mix(static_cast<const uint8_t *>(ptr[i]) + sz[i] - n, n);
+  }
+  return h;
+}
 
 }  // namespace clb
 
@@ -274,6 +298,7 @@ int clb200_layer_bind(clb200_ctx *c, const clb200_moe_layer *L, int on_device, c
     dl.d.down.p = b + off[4];
     dl.bytes = tot;
     for (int i = 0; i < 5; ++i) dl.hkey[i] = src[i];
+    dl.fp = fingerprint(L);
     c->bytes += tot;
   } else {
     const void *ptrs[5] = {L->ffn_norm_f, L->router_f, L->gate.p, L->up.p, L->down.p};
@@ -286,10 +311,23 @@ int clb200_layer_bind(clb200_ctx *c, const clb200_moe_layer *L, int on_device, c
       }
     }
   }
+  dl.live = true;
   c->layers.push_back(dl);
   const int h = static_cast<int>(c->layers.size()) - 1;
   if (!on_device) c->by_gate[L->gate.p] = h;
   return h;
+}
+
+int clb200_layer_release(clb200_ctx *c, int layer) {
+  if (!c || layer < 0 || layer >= static_cast<int>(c->layers.size()) || !c->layers[layer].live) return 1;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  DevLayer &dl = c->layers[layer];
+  auto it = c->by_gate.find(dl.hkey[2]);
+  if (it != c->by_gate.end() && it->second == layer) c->by_gate.erase(it);
+  if (dl.block) { cudaFree(dl.block); c->bytes -= dl.bytes; }
+  dl = DevLayer();
+  return 0;
 }
 
 // Launches the MoE block for T tokens on device data.
@@ -372,7 +410,7 @@ static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *se
 
 int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, float *wt, void *stream, char *err, size_t errlen) {
   if (!c) { errf(err, errlen, "no context"); return 1; }
-  if (layer < 0 || layer >= static_cast<int>(c->layers.size())) { errf(err, errlen, "no layer %d", layer); return 1; }
+  if (layer < 0 || layer >= static_cast<int>(c->layers.size()) || !c->layers[layer].live) { errf(err, errlen, "no layer %d", layer); return 1; }
   if (T < 1 || T > 512) { errf(err, errlen, "%d tokens: a call takes 1 to 512", T); return 1; }
   if (!x) { errf(err, errlen, "no activations"); return 1; }
   cudaSetDevice(c->device);
@@ -403,7 +441,11 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
   auto it = c->by_gate.find(L->gate.p);
   if (it != c->by_gate.end()) {
     const DevLayer &dl = c->layers[it->second];
-    if (dl.hkey[0] == L->ffn_norm_f && dl.hkey[1] == L->router_f && dl.hkey[3] == L->up.p && dl.hkey[4] == L->down.p) h = it->second;
+    if (dl.hkey[0] == L->ffn_norm_f && dl.hkey[1] == L->router_f && dl.hkey[3] == L->up.p && dl.hkey[4] == L->down.p &&
+        validate(L, err, errlen) == 0 && dl.fp == fingerprint(L))
+      h = it->second;
+    else
+      clb200_layer_release(c, it->second);   // the host memory now holds something else: drop the stale upload
   }
   if (h < 0) {
     h = clb200_layer_bind(c, L, 0, err, errlen);

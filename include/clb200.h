@@ -70,6 +70,10 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
  * every pointer in L is a device pointer and is used in place (the caller keeps the memory alive); with on_device = 0 the
  * tensors are copied to the device now. */
 int clb200_layer_bind(clb200_ctx *c, const clb200_moe_layer *L, int on_device, char *err, size_t errlen);
+/* Frees a layer's device copy (when clb200 made one) and forgets it; its handle becomes invalid. 0 on success, 1 for an
+ * unknown handle. clb200_moe_ffn also drops an upload by itself when the host memory it came from no longer holds the same
+ * tensors (it compares shapes and the first and last bytes of each tensor on every call). */
+int clb200_layer_release(clb200_ctx *c, int layer);
 /* Same block as clb200_moe_ffn on a bound layer with DEVICE pointers x [T x n_embd] (updated in place), sel [T x n_used] and
  * wt [T x n_used] (either may be NULL). Asynchronous on `stream` (a cudaStream_t; NULL: the context's stream). Argument errors
  * are reported at once; device-side errors (a timed-out wait) by clb200_status. Safe to capture in a CUDA graph once the
