@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -108,7 +109,8 @@ struct Scratch {
       off_pos_wt, off_slot_pos, off_bhg, off_hq_qs, off_hq_d, off_hq_bs, off_hd;
 };
 
-static Scratch plan_scratch(int T, int E, int FF, int NE, int K) {
+// `batched`: the batched kernels will run (T > 1, or one token of a shape the one-token kernel does not take).
+static Scratch plan_scratch(int T, int E, int FF, int NE, int K, bool batched) {
   Scratch s{};
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = al(o + bytes); return at; };
@@ -118,7 +120,7 @@ static Scratch plan_scratch(int T, int E, int FF, int NE, int K) {
   s.off_wt = take(TK * 4);
   s.off_logits = take(static_cast<size_t>(T) * NE * 4);
   s.off_hg = take(static_cast<size_t>(K) * FF * 4);
-  if (T > 1) {
+  if (batched) {
     s.off_xn = take(static_cast<size_t>(T) * E * 4);
     s.off_xq_qs = take(static_cast<size_t>(T) * E);
     s.off_xq_d = take(static_cast<size_t>(T) * (E / 256) * 4);
@@ -154,9 +156,13 @@ static int ensure_scratch(clb200_ctx *c, size_t need, char *err, size_t errlen) 
   return 0;
 }
 
-// Shared-memory plan of the one-token kernel for a layer; 0 when it fits.
-static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArgs &a, char *err, size_t errlen) {
+// Shared-memory plan of the one-token kernel for a layer; 0 when it fits (else the batched kernels take T = 1 too).
+static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArgs &a) {
   const int G = c->sms, E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+  auto kq = [](uint32_t t) { return t == T_Q4_K || t == T_Q6_K; };
+  if (!kq(L.gate.type) || !kq(L.up.type) || !kq(L.down.type) || NE > DECODE_MAX_NE || K > DECODE_MAX_K) return 1;
+  const int nb = E / 256, nbd = FF / 256;
+  if (nbd * K > DECODE_THREADS || nb > DECODE_THREADS / 8) return 1;
   a.rgu_max = (FF + G - 1) / G;
   a.rd_max = (E + G - 1) / G;
   a.grb = static_cast<uint32_t>(row_bytes(L.gate.type, E));
@@ -164,29 +170,28 @@ static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArg
   a.gseg = static_cast<uint32_t>(al(static_cast<size_t>(a.rgu_max) * a.grb + 32, 16));
   a.dseg = static_cast<uint32_t>(al(static_cast<size_t>(a.rd_max) * a.drb + 32, 16));
   a.slot_bytes = 2 * a.gseg + a.dseg;
+  a.slot_bytes += (16 - a.slot_bytes % 128 + 128) % 128;   // slots 16 bytes off a 128-byte period: experts in different banks
   const int nre = (NE + G - 1) / G;
   constexpr int NW = DECODE_THREADS / 32;
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = al(o + bytes, 16); return static_cast<uint32_t>(at); };
   a.off_bars = take(8 * (K + 1));
   a.off_xn = take(static_cast<size_t>(E) * 4);
-  a.off_xq = take(static_cast<size_t>(E) + 4 * (E / 256) + 2 * (E / 16));
+  a.off_norm = take(static_cast<size_t>(E) * 4);
+  a.off_xq = take(static_cast<size_t>(E) + 2 * (E / 16) + 4 * (E / 256));
   a.off_router = take(static_cast<size_t>(nre) * E * 4);
-  a.off_misc = take(NE * 4 + 32 * 4 + 32 * 4 + NW * 8 + 16);
-  a.off_hq = take(static_cast<size_t>(FF) * 5 + 4 * (FF / 256) + 2 * (FF / 16));
-  a.off_gres = take(2 * static_cast<size_t>(a.rgu_max) * 4);
-  a.off_moe = take(2 * static_cast<size_t>(a.rd_max) * 4);
+  a.off_misc = take(NW * 8 + 16 + 32 * 4 + 32 * 4 + NW * 4 + ((NE + 3) & ~3) * 4);
+  const size_t nterm = std::max(static_cast<size_t>(2) * K * a.rgu_max * nb, static_cast<size_t>(a.rd_max) * K * nbd);
+  a.off_terms = take(nterm * 4);
+  a.off_gres = take(static_cast<size_t>(2) * K * a.rgu_max * 4);
+  a.off_rowoff = take(static_cast<size_t>(2) * K * a.rgu_max * 4);
+  a.off_hq = take(static_cast<size_t>(K) * FF + 2 * (static_cast<size_t>(K) * FF / 16) + 4 * (static_cast<size_t>(K) * FF / 256));
+  a.off_xr = take(static_cast<size_t>(a.rd_max) * 4);
+  a.off_hd = take(static_cast<size_t>(a.rd_max) * K * 4);
   a.off_slots = static_cast<uint32_t>(al(o, 128));
-  const size_t fixed = a.off_slots + 16;
-  const size_t avail = static_cast<size_t>(c->max_smem) > fixed ? c->max_smem - fixed : 0;
-  int nslot = static_cast<int>(avail / a.slot_bytes);
-  if (nslot > K) nslot = K;
-  if (nslot < (K < 2 ? K : 2)) {
-    errf(err, errlen, "the one-token kernel cannot hold two experts' rows per CTA (%u bytes each, %zu free) for this shape", a.slot_bytes, avail);
-    return 1;
-  }
-  a.nslot = nslot;
-  a.smem_bytes = static_cast<uint32_t>(fixed + static_cast<size_t>(nslot) * a.slot_bytes);
+  const size_t total = a.off_slots + static_cast<size_t>(K) * a.slot_bytes + 16;
+  if (total > static_cast<size_t>(c->max_smem)) return 1;
+  a.smem_bytes = static_cast<uint32_t>(total);
   return 0;
 }
 
@@ -335,12 +340,12 @@ static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *se
                      size_t errlen) {
   const clb200_moe_layer &L = dl.d;
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
-  const Scratch s = plan_scratch(T, E, FF, NE, K);
+  DecodeArgs a{};
+  const bool one = T == 1 && plan_decode(c, L, a) == 0;
+  const Scratch s = plan_scratch(T, E, FF, NE, K, !one);
   if (ensure_scratch(c, s.total, err, errlen)) return 1;
   uint8_t *sc = c->scratch;
-  if (T == 1) {
-    DecodeArgs a{};
-    if (plan_decode(c, L, a, err, errlen)) return 1;
+  if (one) {
     a.x_in = x; a.x_out = x;
     a.norm = L.ffn_norm_f; a.router = L.router_f;
     a.gate = L.gate.p; a.up = L.up.p; a.down = L.down.p;
@@ -453,7 +458,7 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
   }
   const DevLayer &dl = c->layers[h];
   const int E = L->n_embd, K = L->n_used;
-  const Scratch s = plan_scratch(T, E, L->n_ff_exp, L->n_expert, K);
+  const Scratch s = plan_scratch(T, E, L->n_ff_exp, L->n_expert, K, true);   // the staging buffers lead either plan
   if (ensure_scratch(c, s.total, err, errlen)) return 1;
   float *dx = reinterpret_cast<float *>(c->scratch + s.off_x);
   int *dsel = reinterpret_cast<int *>(c->scratch + s.off_sel);

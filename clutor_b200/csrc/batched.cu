@@ -208,14 +208,16 @@ __global__ void __launch_bounds__(BT) gateup_kernel(const BatchArgs a) {
   }
   __syncthreads();
   const uint8_t *g = wbuf + lg, *u = wbuf + seg + lu;
+  const int p0 = a.offsets[e];
+  if (p0 < 0 || n < 0 || p0 + n > a.T * a.K) { set_error(a.err, ERR_BAD_EXPERT); mbar_wait_bounded(bar, 0); return; }
   const bool q80 = a.gate_type == T_Q8_0;
   const int nb = q80 ? E / 32 : E / 256;
   const RowShape rs = row_shape(q80 ? nb : 4 * nb);
   const int sub = lane / rs.LG, lig = lane % rs.LG;
   if (!mbar_wait_bounded(bar, 0)) { set_error(a.err, ERR_WAIT_COPY); return; }
-  const int p0 = a.offsets[e];
   for (int i = 0; i < n; ++i) {
     const int pos = p0 + i, t = a.pos_token[pos];
+    if (t < 0 || t >= a.T) { set_error(a.err, ERR_BAD_EXPERT); return; }
     KQAct act;
     if (q80) {
       __syncthreads();
@@ -275,6 +277,7 @@ __global__ void __launch_bounds__(BT) down_kernel(const BatchArgs a) {
   const int sub = lane / rs.LG, lig = lane % rs.LG;
   if (!mbar_wait_bounded(bar, 0)) { set_error(a.err, ERR_WAIT_COPY); return; }
   const int p0 = a.offsets[e];
+  if (p0 < 0 || n < 0 || p0 + n > a.T * a.K) { set_error(a.err, ERR_BAD_EXPERT); return; }
   for (int i = 0; i < n; ++i) {
     const int pos = p0 + i;
     KQAct act;
@@ -314,6 +317,8 @@ __global__ void __launch_bounds__(BT) combine_kernel(const BatchArgs a) {
     }
   }
   __syncthreads();
+  for (int j = 0; j < K; ++j)
+    if (s_pos[j] < 0 || s_pos[j] >= a.T * K) { if (threadIdx.x == 0) set_error(a.err, ERR_BAD_EXPERT); return; }
   for (int i = threadIdx.x; i < E; i += BT) {
     float m = 0.f;
     for (int j = 0; j < K; ++j) m = __fadd_rn(m, __fmul_rn(s_w[j], a.hd[static_cast<size_t>(s_pos[j]) * E + i]));

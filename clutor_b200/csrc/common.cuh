@@ -73,7 +73,7 @@ CLB_DEV void red_release_add(uint32_t *p, uint32_t v) {
 CLB_DEV bool wait_counter(const uint32_t *p, uint32_t target) {
   for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
     if (ld_acquire(p) >= target) return true;
-    if (i > 32) __nanosleep(64);
+    if (i > 4096) __nanosleep(64);   // poll flat out for the first few microseconds: these waits are on the critical path
   }
   return false;
 }

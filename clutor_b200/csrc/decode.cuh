@@ -4,8 +4,8 @@
 
 namespace clb {
 
-constexpr int DECODE_THREADS = 256;
-constexpr int DECODE_MAX_NE = 256;   // experts per layer the one-token kernel ranks in one warp
+constexpr int DECODE_THREADS = 512;
+constexpr int DECODE_MAX_NE = 256;   // experts per layer the one-token kernel ranks
 constexpr int DECODE_MAX_K = 32;     // experts used per token
 
 struct DecodeArgs {
@@ -21,12 +21,13 @@ struct DecodeArgs {
   float *hg;                     // [K * FF] scratch
   int *sel_out;                  // [K] or null
   float *wt_out;                 // [K] or null
-  uint32_t *sync;                // [0] logits done, [1..K] experts whose hg is complete, [K+1] CTAs finished; zero on entry
+  uint32_t *sync;                // [0] logits written, [1] CTAs whose hg rows are written, [2] CTAs finished; zero on entry
   int *err;                      // first device error
-  // shared-memory plan (host-computed)
-  int nslot, rgu_max, rd_max;
+  // shared-memory plan (host-computed): one slot per chosen expert holds this CTA's gate, up and down rows of it
+  int rgu_max, rd_max;
   uint32_t grb, drb, gseg, dseg, slot_bytes;
-  uint32_t off_bars, off_xn, off_xq, off_router, off_misc, off_hq, off_gres, off_moe, off_slots, smem_bytes;
+  uint32_t off_bars, off_xn, off_norm, off_xq, off_router, off_misc, off_terms, off_gres, off_rowoff, off_hq, off_xr, off_hd,
+      off_slots, smem_bytes;
 };
 
 __global__ void moe_decode_kernel(const DecodeArgs a);

@@ -19,6 +19,10 @@ constexpr unsigned FULL = 0xffffffffu;
 constexpr int KQ_MAXI = 2;     // units per lane: rows up to 8 * 32 / 4 * 2 = 4096 wide
 constexpr int Q80_MAXI = 4;    // Q8_0 blocks per lane: rows up to 4096 wide
 
+// Byte offset of 16-byte chunk j of 256-block b in a swizzled Q8_K value array: chunk j sits at position j ^ (b & 7), so
+// that eight lanes reading chunk j of eight consecutive blocks hit eight different groups of banks.
+CLB_DEV int q8k_chunk_off(int b, int j, bool swz) { return 256 * b + 16 * (swz ? (j ^ (b & 7)) : j); }
+
 // How a warp splits rows of `units` units into row groups.
 struct RowShape {
   int LG;   // lanes per row group
@@ -205,7 +209,7 @@ CLB_DEV float q80_row(const uint8_t *row, int nb32, RowShape rs, int lane_in_grp
 // Q8_K quantization of n floats (shared memory) into qs/d/bsums (shared memory), one 256-block per warp at a time
 // (c/src/quant.c:195-206): d = amax/127, q = roundf(x * (1/d)), bsums = sums of 16. Call from all threads of the block.
 CLB_DEV void q8k_quantize_block(const float *x, int n, int8_t *qs, float *dd, int16_t *bsums, int warp, int nwarps,
-                                int lane) {
+                                int lane, bool swz = false) {
   for (int b = warp; b < n / 256; b += nwarps) {
     const float *v = x + 256 * b + 8 * lane;
     float vals[8];
@@ -224,10 +228,153 @@ CLB_DEV void q8k_quantize_block(const float *x, int n, int8_t *qs, float *dd, in
       s += q;
       packed[j >> 2] |= (static_cast<uint32_t>(q) & 0xffu) << (8 * (j & 3));
     }
-    reinterpret_cast<uint2 *>(qs + 256 * b + 8 * lane)[0] = make_uint2(packed[0], packed[1]);
+    reinterpret_cast<uint2 *>(qs + q8k_chunk_off(b, lane >> 1, swz) + 8 * (lane & 1))[0] = make_uint2(packed[0], packed[1]);
     s += __shfl_xor_sync(FULL, s, 1);
     if ((lane & 1) == 0) bsums[16 * b + lane / 2] = static_cast<int16_t>(s);
     if (lane == 0) dd[b] = d;
+  }
+}
+
+// ---- one lane per 256-element block ---------------------------------------------------------------------------------------
+// Activation registers for one whole block: 256 int8 values (64 words), the 16 group sums, the scale.
+struct BlockAct {
+  int32_t q[64];
+  int32_t bs[16];
+  float d;
+};
+// Loads 256-block blk of a swizzled Q8_K value array (q8k_chunk_off) with its group sums and scale.
+CLB_DEV void load_block_act(const int8_t *qs, const float *dd, const int16_t *bsums, int blk, BlockAct &a) {
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const int4 v = *reinterpret_cast<const int4 *>(qs + q8k_chunk_off(blk, t, true));
+    a.q[4 * t] = v.x; a.q[4 * t + 1] = v.y; a.q[4 * t + 2] = v.z; a.q[4 * t + 3] = v.w;
+  }
+  const int4 *b = reinterpret_cast<const int4 *>(bsums + 16 * blk);   // 16 int16 = two int4
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int4 v = b[t];
+    const uint32_t w[4] = {static_cast<uint32_t>(v.x), static_cast<uint32_t>(v.y), static_cast<uint32_t>(v.z), static_cast<uint32_t>(v.w)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a.bs[8 * t + 2 * j] = static_cast<int16_t>(w[j] & 0xffffu);
+      a.bs[8 * t + 2 * j + 1] = static_cast<int16_t>(w[j] >> 16);
+    }
+  }
+  a.d = dd[blk];
+}
+
+CLB_DEV uint32_t lds_u32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+CLB_DEV int byte_of(uint32_t w, int i) { return static_cast<int>((w >> (8 * i)) & 0xffu); }
+
+// One Q4_K block (144 bytes at bp, 4-byte aligned) times a register block: the reference's term
+// yd * (d * sumi - dmin * summs) with exact integer sums (c/src/quant.c:255-287, 832-846). The 12 packed scale bytes are
+// unpacked with word operations: scales 0-3 / mins 0-3 are the low 6 bits of bytes 0-3 / 4-7; scales 4-7 / mins 4-7 are the
+// low / high nibbles of bytes 8-11 with the top two bits of bytes 0-3 / 4-7 above them (ggml's layout, c/src/quant.c:36-52).
+CLB_DEV float q4k_block(const uint8_t *bp, const BlockAct &a) {
+  const uint32_t dm = lds_u32(bp), w0 = lds_u32(bp + 4), w1 = lds_u32(bp + 8), w2 = lds_u32(bp + 12);
+  const uint32_t scA = w0 & 0x3f3f3f3fu, mnA = w1 & 0x3f3f3f3fu;
+  const uint32_t scB = (w2 & 0x0f0f0f0fu) | (((w0 >> 6) & 0x03030303u) << 4);
+  const uint32_t mnB = ((w2 >> 4) & 0x0f0f0f0fu) | (((w1 >> 6) & 0x03030303u) << 4);
+  int sumi = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint4 x0 = reinterpret_cast<const uint4 *>(bp + 16 + 32 * g)[0];
+    const uint4 x1 = reinterpret_cast<const uint4 *>(bp + 16 + 32 * g)[1];
+    const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    int lo = 0, hi = 0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      lo = __dp4a(static_cast<int>(w[t] & 0x0f0f0f0fu), a.q[16 * g + t], lo);
+      hi = __dp4a(static_cast<int>((w[t] >> 4) & 0x0f0f0f0fu), a.q[16 * g + 8 + t], hi);
+    }
+    const uint32_t sw = g < 2 ? scA : scB;
+    sumi += byte_of(sw, 2 * (g & 1)) * lo + byte_of(sw, 2 * (g & 1) + 1) * hi;
+  }
+  int summs = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) summs += byte_of(j < 4 ? mnA : mnB, j & 3) * (a.bs[2 * j] + a.bs[2 * j + 1]);
+  const float d = f16_bits_to_f32(static_cast<uint16_t>(dm & 0xffffu)), dmin = f16_bits_to_f32(static_cast<uint16_t>(dm >> 16));
+  return __fmul_rn(a.d, __fsub_rn(__fmul_rn(d, static_cast<float>(sumi)), __fmul_rn(dmin, static_cast<float>(summs))));
+}
+
+// One Q6_K block (210 bytes at bp, any alignment) times a register block: the reference's term (d * yd) * sumi
+// (c/src/quant.c:329-360). Element 128h + 32c + l takes a nibble of ql[64h + 32(c%2) + l] (low for c < 2) and bits 2c..2c+1
+// of qh[32h + l]; the 6-bit value minus 32 is the weight. Each 16-group's dot is taken on the unsigned 6-bit values and
+// corrected by 32 * (sum of the group's activations), which is the same integer.
+CLB_DEV float q6k_block(const uint8_t *bp, const BlockAct &a) {
+  int dot[16];
+#pragma unroll
+  for (int g = 0; g < 16; ++g) dot[g] = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const uint32_t L0 = lds_u32_unaligned(bp + 64 * h + 4 * t), L1 = lds_u32_unaligned(bp + 64 * h + 32 + 4 * t);
+      const uint32_t H = lds_u32_unaligned(bp + 128 + 32 * h + 4 * t);
+      const int v0 = static_cast<int>((L0 & 0x0f0f0f0fu) | ((H & 0x03030303u) << 4));
+      const int v1 = static_cast<int>((L1 & 0x0f0f0f0fu) | (((H >> 2) & 0x03030303u) << 4));
+      const int v2 = static_cast<int>(((L0 >> 4) & 0x0f0f0f0fu) | (((H >> 4) & 0x03030303u) << 4));
+      const int v3 = static_cast<int>(((L1 >> 4) & 0x0f0f0f0fu) | (((H >> 6) & 0x03030303u) << 4));
+      const int gq = t / 4;   // 16-group within each 32-element run
+      dot[8 * h + gq] = __dp4a(v0, a.q[32 * h + t], dot[8 * h + gq]);
+      dot[8 * h + 2 + gq] = __dp4a(v1, a.q[32 * h + 8 + t], dot[8 * h + 2 + gq]);
+      dot[8 * h + 4 + gq] = __dp4a(v2, a.q[32 * h + 16 + t], dot[8 * h + 4 + gq]);
+      dot[8 * h + 6 + gq] = __dp4a(v3, a.q[32 * h + 24 + t], dot[8 * h + 6 + gq]);
+    }
+  }
+  const int8_t *sc = reinterpret_cast<const int8_t *>(bp + 192);
+  int sumi = 0;
+#pragma unroll
+  for (int g = 0; g < 16; ++g) sumi += static_cast<int>(sc[g]) * (dot[g] - 32 * a.bs[g]);
+  const float d = f16_bits_to_f32(lds_u16(bp + 208));
+  return __fmul_rn(__fmul_rn(d, a.d), static_cast<float>(sumi));
+}
+
+CLB_DEV float kq_block(uint32_t type, const uint8_t *row, int blk, const BlockAct &a) {
+  return type == T_Q4_K ? q4k_block(row + 144 * blk, a) : q6k_block(row + 210 * blk, a);
+}
+
+// Q8_K quantization of nblocks 256-blocks of floats in global memory (written by other CTAs; read through L2) into shared
+// qs/d/bsums. Each warp takes blocks warp, warp + nwarps, ...; a lane issues the loads of up to four blocks before the first
+// reduction, so their round trips overlap.
+CLB_DEV void q8k_quantize_global(const float *src, int nblocks, int8_t *qs, float *dd, int16_t *bsums, int warp, int nwarps,
+                                 int lane, bool swz = false) {
+  for (int b0 = warp; b0 < nblocks; b0 += 4 * nwarps) {
+    float4 v[4][2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = b0 + j * nwarps;
+      if (b < nblocks) {
+        const float4 *p = reinterpret_cast<const float4 *>(src + 256 * b + 8 * lane);
+        v[j][0] = __ldcg(p);
+        v[j][1] = __ldcg(p + 1);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = b0 + j * nwarps;
+      if (b >= nblocks) break;
+      const float vals[8] = {v[j][0].x, v[j][0].y, v[j][0].z, v[j][0].w, v[j][1].x, v[j][1].y, v[j][1].z, v[j][1].w};
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(vals[i]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
+      const float d = __fdiv_rn(amax, 127.0f);
+      const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+      int s = 0;
+      uint32_t packed[2] = {0, 0};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = static_cast<int>(roundf(__fmul_rn(vals[i], id)));
+        s += q;
+        packed[i >> 2] |= (static_cast<uint32_t>(q) & 0xffu) << (8 * (i & 3));
+      }
+      reinterpret_cast<uint2 *>(qs + q8k_chunk_off(b, lane >> 1, swz) + 8 * (lane & 1))[0] = make_uint2(packed[0], packed[1]);
+      s += __shfl_xor_sync(FULL, s, 1);
+      if ((lane & 1) == 0) bsums[16 * b + lane / 2] = static_cast<int16_t>(s);
+      if (lane == 0) dd[b] = d;
+    }
   }
 }
 
