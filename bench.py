@@ -56,44 +56,52 @@ def layer_bytes(wl: dict, distinct: float) -> float:
 
 
 class Clocks:
-    """Samples nvidia-smi every 200 ms during the timed region."""
+    """Samples the SM clock and the clock-event (throttle) reasons every millisecond through NVML during the timed region
+    (nvidia-smi cannot sample a region this short)."""
 
-    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, gpu: int):
         self.gpu = gpu
-        self.rows: list[list[str]] = []
-        self.proc = None
+        self.rows: list[tuple[int, int, int]] = []
+        self.stop = threading.Event()
+        self.t = None
+        self.error = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        self.rows.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), self.max_mhz,
+                                          pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception as e:  # keep the timing run alive; report what failed
+                        self.error = str(e)
+                        return
+                    time.sleep(0.001)
+            self.t = threading.Thread(target=poll, daemon=True)
             self.t.start()
-        except FileNotFoundError:
-            self.proc = None
+        except Exception as e:
+            self.error = f"NVML unavailable: {e}"
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
-
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            self.proc.wait()
+        self.stop.set()
+        if self.t:
+            self.t.join()
 
     def summary(self) -> dict:
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["not sampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error or "not sampled"]}
+        reasons = sorted({name for _, _, r in self.rows for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.rows[0][1], "reasons": reasons,
+                "samples": len(self.rows), "source": "NVML, 1 ms polling"}
 
 
 def read_traffic(kernel: str) -> float | None:

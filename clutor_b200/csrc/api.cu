@@ -160,9 +160,10 @@ static int ensure_scratch(clb200_ctx *c, size_t need, char *err, size_t errlen) 
 static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArgs &a) {
   const int G = c->sms, E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
   auto kq = [](uint32_t t) { return t == T_Q4_K || t == T_Q6_K; };
-  if (!kq(L.gate.type) || !kq(L.up.type) || !kq(L.down.type) || NE > DECODE_MAX_NE || K > DECODE_MAX_K) return 1;
+  // four threads rank each expert, one warp issues each expert's copies
+  if (!kq(L.gate.type) || !kq(L.up.type) || !kq(L.down.type) || NE > DECODE_THREADS / 4 || K > DECODE_MAX_K) return 1;
   const int nb = E / 256, nbd = FF / 256;
-  if (nbd * K > DECODE_THREADS || nb > DECODE_THREADS / 8) return 1;
+  if (nbd * K > DECODE_THREADS || nb > DECODE_THREADS / 8 || K > DECODE_THREADS / 32) return 1;   // one warp issues each expert's copies
   a.rgu_max = (FF + G - 1) / G;
   a.rd_max = (E + G - 1) / G;
   a.grb = static_cast<uint32_t>(row_bytes(L.gate.type, E));

@@ -95,9 +95,9 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     __syncthreads();
     for (int i = tid; i < E; i += DECODE_THREADS) xn[i] = __fmul_rn(__fmul_rn(xn[i], scale), wn[i]);
     __syncthreads();
-    // products of the router rows (in place) by every thread; Q8_K of xn by the first warps meanwhile
-    for (int i = tid; i < nre * E; i += DECODE_THREADS) rrows[i] = __fmul_rn(rrows[i], xn[i % E]);
-    q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
+    // products of the router rows (in place) by every thread; the Q8_K blocks of xn wait until the copies are out
+    for (int m = 0; m < nre; ++m)
+      for (int i = tid; i < E; i += DECODE_THREADS) rrows[m * E + i] = __fmul_rn(rrows[m * E + i], xn[i]);
     __syncthreads();
   }
 
@@ -152,17 +152,20 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     const float p = __double2float_rn(__ddiv_rn(static_cast<double>(ev), tot));
     if (tid < ((NE + 3) & ~3)) probs[tid] = tid < NE ? p : -1.0f;
     __syncthreads();
-    if (tid < NE) {   // rank = experts ahead of this one in the reference's arg-max order
+    {   // rank = experts ahead of this one in the reference's arg-max order; four threads per expert, a quarter each
+      const int e = tid >> 2, part = tid & 3, n4 = (NE + 3) / 4, per = (n4 + 3) / 4;
+      const float pe = e < NE ? probs[e] : 0.f;
       int rank = 0;
       const float4 *p4 = reinterpret_cast<const float4 *>(probs);
-#pragma unroll 8
-      for (int j = 0; j < (NE + 3) / 4; ++j) {
+      for (int j = part * per; j < min(n4, (part + 1) * per); ++j) {
         const float4 q = p4[j];
-        const int e = 4 * j;
-        rank += (q.x > p || (q.x == p && e < tid)) + (q.y > p || (q.y == p && e + 1 < tid)) +
-                (q.z > p || (q.z == p && e + 2 < tid)) + (q.w > p || (q.w == p && e + 3 < tid));
+        const int f = 4 * j;
+        rank += (q.x > pe || (q.x == pe && f < e)) + (q.y > pe || (q.y == pe && f + 1 < e)) +
+                (q.z > pe || (q.z == pe && f + 2 < e)) + (q.w > pe || (q.w == pe && f + 3 < e));
       }
-      if (rank < K) { s_sel[rank] = tid; s_wt[rank] = p; }
+      rank += __shfl_xor_sync(FULL, rank, 1);
+      rank += __shfl_xor_sync(FULL, rank, 2);
+      if (e < NE && part == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = pe; }
     }
     __syncthreads();
     if (tid < K) {   // renormalise: each of K threads forms the same sum in rank order
@@ -194,8 +197,8 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
            static_cast<uint32_t>(reinterpret_cast<uintptr_t>(seg_src(k, q)) & 15u);
   };
   const bool go = !s_flag[0];
-  if (go && warp == 0 && lane < K) {
-    const int k = lane;
+  if (go && lane == 0 && warp < K) {   // one warp per expert: their copy requests go out in parallel
+    const int k = warp;
     uint8_t *slot = slots + static_cast<size_t>(k) * a.slot_bytes;
     const uint32_t len[3] = {static_cast<uint32_t>(ngu) * grb, static_cast<uint32_t>(ngu) * grb, static_cast<uint32_t>(nd) * drb};
     uint8_t *dst[3] = {slot, slot + gseg, slot + 2 * gseg};
@@ -210,9 +213,10 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     mbar_arrive_expect_tx(&bars[k], total);
     for (int q = 0; q < 3; ++q)
       if (n16[q]) bulk_copy_g2s(dst[q], src[q] - lo[q], n16[q], &bars[k]);
-    if (lane == 0) s_flag[1] = 1;
+    if (k == 0) s_flag[1] = 1;
   }
-  // offsets of the gate/up rows, in task order (expert, gate then up, row)
+  // while the copies fly: the Q8_K blocks of xn, and the offsets of the gate/up rows in task order (expert, gate/up, row)
+  if (go) q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
   const int per_k = 2 * ngu, tasks = K * per_k;
   if (go)
     for (int t = tid; t < tasks; t += DECODE_THREADS) {
@@ -287,10 +291,9 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   // ---- exit: copies in flight land first; the last CTA out resets the counters ----------------------------------------------
   __syncthreads();
   if (tid == 0) {
-    if (s_flag[1])
+    if (s_flag[1] && s_flag[0])   // an error path may leave copies unwaited; the normal path waited in phase 6
       for (int k = 0; k < K; ++k)
         if (!mbar_wait_bounded(&bars[k], 0)) set_error(a.err, ERR_WAIT_COPY);
-    __threadfence();
     const uint32_t prev = atomicAdd(&a.sync[2], 1u);
     if (prev == static_cast<uint32_t>(G) - 1) {
       atomicExch(&a.sync[0], 0u);
