@@ -82,6 +82,8 @@ def lib() -> C.CDLL:
         L.clb200_moe_ffn_dev.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
         L.clb200_status.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
         L.clb200_layer_release.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_moe_ffn_decode_noalloc.argtypes = [C.POINTER(MoELayer), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                    C.c_char_p, C.c_size_t]
         L.clb200_device_bytes.restype = C.c_uint64
         L.clb200_device_bytes.argtypes = [C.c_void_p]
         L.clb200_backend.restype = C.POINTER(Backend)

@@ -156,9 +156,10 @@ static int ensure_scratch(clb200_ctx *c, size_t need, char *err, size_t errlen) 
   return 0;
 }
 
-// Shared-memory plan of the one-token kernel for a layer; 0 when it fits (else the batched kernels take T = 1 too).
-static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArgs &a) {
-  const int G = c->sms, E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+// Shared-memory plan of the one-token kernel for a layer on a device with `sms` SMs and `max_smem` bytes of opt-in shared
+// memory per block; 0 when it fits.
+int plan_decode_shape(int sms, int max_smem, const clb200_moe_layer &L, DecodeArgs &a) {
+  const int G = sms, E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
   auto kq = [](uint32_t t) { return t == T_Q4_K || t == T_Q6_K; };
   // four threads rank each expert, one warp issues each expert's copies
   if (!kq(L.gate.type) || !kq(L.up.type) || !kq(L.down.type) || NE > DECODE_THREADS / 4 || K > DECODE_MAX_K) return 1;
@@ -191,9 +192,14 @@ static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArg
   a.off_hd = take(static_cast<size_t>(a.rd_max) * K * 4);
   a.off_slots = static_cast<uint32_t>(al(o, 128));
   const size_t total = a.off_slots + static_cast<size_t>(K) * a.slot_bytes + 16;
-  if (total > static_cast<size_t>(c->max_smem)) return 1;
+  if (total > static_cast<size_t>(max_smem)) return 1;
   a.smem_bytes = static_cast<uint32_t>(total);
   return 0;
+}
+
+// The plan for a context's device; 0 when it fits (else the batched kernels take T = 1 too).
+static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArgs &a) {
+  return plan_decode_shape(c->sms, c->max_smem, L, a);
 }
 
 static int validate(const clb200_moe_layer *L, char *err, size_t errlen) {

@@ -1,0 +1,127 @@
+// The one-token MoE block for callers that cannot allocate device memory.
+//
+// Some hosts must not call cudaMalloc once they are running: an engine whose device memory is all carved out up front by
+// another allocator (a framework's caching pool owns the GPU, and a raw cudaMalloc beside it fails or fragments), or one
+// that decodes under a latency budget (cudaMalloc can synchronise the device and take milliseconds). Such a host owns its
+// inputs and outputs and cannot give this library a context with scratch. clb200_moe_ffn_decode_noalloc runs the same
+// one-token kernel as clb200_moe_ffn_dev with its scratch -- the router logits, the experts' hg rows, three grid counters
+// and the error word -- in a fixed array of this file that every device holds from the moment it loads the library.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/clb200.h"
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace clb {
+
+int plan_decode_shape(int sms, int max_smem, const clb200_moe_layer &L, DecodeArgs &a);   // api.cu
+
+namespace {
+
+// Scratch layout: [0, 4) device error word; [256, 268) the kernel's three counters; [512, 1024) router logits of up to
+// 128 experts; [1024, 1024 + 4 * NOALLOC_MAX_HG) hg rows, n_used x n_ff_exp floats.
+constexpr size_t NOALLOC_MAX_HG = 16384;
+constexpr size_t NOALLOC_BYTES = 1024 + 4 * NOALLOC_MAX_HG;   // 66,560 bytes
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_BYTES];
+
+struct DeviceSetup {
+  bool ready = false;
+  uint8_t *scratch = nullptr;   // device address of g_noalloc_scratch on this device
+  int sms = 0, max_smem = 0;
+};
+std::mutex g_setup_mu;
+DeviceSetup g_setup[64];
+
+void errf(char *err, size_t errlen, const char *fmt, ...) {
+  if (!err || !errlen) return;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(err, errlen, fmt, ap);
+  va_end(ap);
+}
+
+}  // namespace
+}  // namespace clb
+
+using namespace clb;
+
+extern "C" int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x, int *sel_out, float *wt_out, void *stream,
+                                              char *err, size_t errlen) {
+  if (!L || !x) { errf(err, errlen, "no layer or no activations"); return 1; }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { errf(err, errlen, "no usable current CUDA device"); return 1; }
+  DeviceSetup su;
+  {
+    // once per device, with that device current: the array's device address (the host-side name is only a stand-in)
+    std::lock_guard<std::mutex> lock(g_setup_mu);
+    DeviceSetup &s = g_setup[dev];
+    if (!s.ready) {
+      void *ptr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess) { errf(err, errlen, "cannot locate the scratch array on device %d: %s", dev, cudaGetErrorString(e)); return 1; }
+      if (cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&s.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+          cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, s.max_smem) != cudaSuccess) {
+        errf(err, errlen, "cannot set up device %d", dev);
+        return 1;
+      }
+      s.scratch = static_cast<uint8_t *>(ptr);
+      s.ready = true;
+    }
+    su = s;
+  }
+  const int E = L->n_embd, FF = L->n_ff_exp, NE = L->n_expert, K = L->n_used;
+  if (E < 256 || E % 256 || FF < 256 || FF % 256 || L->gate.rows != FF || L->gate.cols != E || L->up.rows != FF ||
+      L->up.cols != E || L->down.rows != E || L->down.cols != FF || !L->gate.p || !L->up.p || !L->down.p || !L->router_f ||
+      !L->ffn_norm_f) {
+    errf(err, errlen, "layer shapes or tensors are inconsistent");
+    return 1;
+  }
+  if (NE < 1 || NE > 128 || K < 1 || K > NE || static_cast<size_t>(K) * FF > NOALLOC_MAX_HG) {
+    errf(err, errlen, "%d experts, %d used, expert width %d: the allocation-free entry point takes at most 128 experts and "
+         "n_used * n_ff_exp <= %zu (its fixed scratch is %zu bytes)", NE, K, FF, NOALLOC_MAX_HG, NOALLOC_BYTES);
+    return 1;
+  }
+  DecodeArgs a{};
+  if (plan_decode_shape(su.sms, su.max_smem, *L, a)) {
+    errf(err, errlen, "this layer shape or weight type is not one the one-token kernel takes (K-quant experts, at most 16 used)");
+    return 1;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  a.x_in = x; a.x_out = x;
+  a.norm = L->ffn_norm_f; a.router = L->router_f;
+  a.gate = L->gate.p; a.up = L->up.p; a.down = L->down.p;
+  a.gate_slab = L->gate_slab; a.up_slab = L->up_slab; a.down_slab = L->down_slab;
+  a.gate_type = L->gate.type; a.up_type = L->up.type; a.down_type = L->down.type;
+  a.E = E; a.FF = FF; a.NE = NE; a.K = K; a.norm_topk = L->norm_topk;
+  a.resid_scale = L->resid_scale; a.eps = L->rms_eps;
+  a.err = reinterpret_cast<int *>(su.scratch);
+  a.sync = reinterpret_cast<uint32_t *>(su.scratch + 256);
+  a.logits = reinterpret_cast<float *>(su.scratch + 512);
+  a.hg = reinterpret_cast<float *>(su.scratch + 1024);
+  a.sel_out = sel_out; a.wt_out = wt_out;
+  // the array keeps the last call's contents: the error word and the counters must start at zero
+  cudaError_t e = cudaMemsetAsync(su.scratch, 0, 512, st);
+  if (e != cudaSuccess) { errf(err, errlen, "clearing the scratch counters: %s", cudaGetErrorString(e)); return 1; }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(su.sms);
+  cfg.blockDim = dim3(DECODE_THREADS);
+  cfg.dynamicSmemBytes = a.smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, moe_decode_kernel, a);
+  if (e != cudaSuccess) { errf(err, errlen, "launching the one-token kernel: %s", cudaGetErrorString(e)); return 1; }
+  e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) { errf(err, errlen, "running the one-token kernel: %s", cudaGetErrorString(e)); return 1; }
+  int code = 0;
+  e = cudaMemcpy(&code, su.scratch, sizeof code, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) { errf(err, errlen, "reading the device error word: %s", cudaGetErrorString(e)); return 1; }
+  if (code) { errf(err, errlen, "device error %d (a bounded wait ran out)", code); return 1; }
+  return 0;
+}

@@ -80,6 +80,18 @@ int clb200_layer_release(clb200_ctx *c, int layer);
  * context's scratch has been sized by an earlier call with the same or larger T. */
 int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, float *wt, void *stream, char *err,
                        size_t errlen);
+/* No counterpart in the reference: an entry point for hosts that cannot allocate device memory once they run (their
+ * device memory is carved out up front by another allocator, or cudaMalloc's device-wide synchronisation would break a
+ * decode latency budget). The one-token block of clb200_moe_ffn_dev on DEVICE pointers (layer tensors, x [n_embd]
+ * updated in place, sel / wt [n_used] or NULL) on `stream` (NULL: the default stream), with no context: its scratch is a
+ * fixed 66,560-byte array that every device holds from the time the library is loaded, and it calls no cudaMalloc,
+ * cudaFree or allocating routine. Limits: K-quant expert weights, at most 128 experts, at most 16 used, and
+ * n_used * n_ff_exp <= 16384; larger layers are refused with a message. The first call on a device locates the array and
+ * sets the kernel's shared-memory limit on that device (make it before any stream capture). Synchronous: it returns after
+ * the kernel, with the device's error word read. Every call shares the one array, so calls that overlap on the GPU (from
+ * several host threads or streams) race; serialise them. 0 on success, 1 with err set otherwise. */
+int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x, int *sel_out, float *wt_out, void *stream, char *err,
+                                  size_t errlen);
 /* Waits for the context's work and reports a device-side error recorded since the last call (0: none). */
 int clb200_status(clb200_ctx *c, char *err, size_t errlen);
 /* Bytes of device memory the context holds for layers and scratch. */
