@@ -106,7 +106,7 @@ struct Scratch {
   size_t off_logits, off_hg, off_x, off_sel, off_wt, total;
   // batched
   size_t off_xn, off_xq_qs, off_xq_d, off_xq_bs, off_bsel, off_bwt, off_counts, off_offsets, off_first, off_pos_token,
-      off_pos_wt, off_slot_pos, off_bhg, off_hq_qs, off_hq_d, off_hq_bs, off_hd;
+      off_pos_wt, off_slot_pos, off_bhg, off_hq_qs, off_hq_d, off_hq_bs, off_hd, off_xh, off_xl, off_hgh, off_hgl, off_xdh, off_xdl;
 };
 
 // `batched`: the batched kernels will run (T > 1, or one token of a shape the one-token kernel does not take).
@@ -138,6 +138,12 @@ static Scratch plan_scratch(int T, int E, int FF, int NE, int K, bool batched) {
     s.off_hq_d = take(TK * (FF / 256) * 4);
     s.off_hq_bs = take(TK * (FF / 16) * 2);
     s.off_hd = take(TK * E * 4);
+    s.off_xh = take(static_cast<size_t>(T) * E * 2);
+    s.off_xl = take(static_cast<size_t>(T) * E * 2);
+    s.off_hgh = take(TK * FF * 2);
+    s.off_hgl = take(TK * FF * 2);
+    s.off_xdh = take(TK * E * 2);
+    s.off_xdl = take(TK * E * 2);
   }
   s.total = o;
   return s;
@@ -415,6 +421,14 @@ static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *se
   b.hd = reinterpret_cast<float *>(sc + s.off_hd);
   b.sel_out = sel; b.wt_out = wt;
   b.err = c->small;
+  if (L.gate.type == T_Q8_0 && L.up.type == T_Q8_0 && L.down.type == T_Q8_0) {   // tensor-core expert products
+    b.xh = reinterpret_cast<__half *>(sc + s.off_xh);
+    b.xl = reinterpret_cast<__half *>(sc + s.off_xl);
+    b.hgh = reinterpret_cast<__half *>(sc + s.off_hgh);
+    b.hgl = reinterpret_cast<__half *>(sc + s.off_hgl);
+    b.xdh = reinterpret_cast<__half *>(sc + s.off_xdh);
+    b.xdl = reinterpret_cast<__half *>(sc + s.off_xdl);
+  }
   const int rc = launch_batched(b, st);
   if (rc) { errf(err, errlen, "launching the batched kernels: %s", cudaGetErrorString(static_cast<cudaError_t>(rc))); return 1; }
   return 0;

@@ -11,6 +11,7 @@
 //   combine_kernel   per token: moe = sum over its experts in order of first appearance of wt*hd (the reference's todo
 //                    order, c/src/forward.c:1163-1164), x += resid_scale * moe
 #include <cstdio>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "decode.cuh"
@@ -42,6 +43,12 @@ __global__ void __launch_bounds__(BT) route_kernel(const BatchArgs a) {
   __syncthreads();
   if (blockIdx.y == 0) {
     for (int i = tid; i < E; i += BT) a.xn[static_cast<size_t>(t) * E + i] = xn[i];
+    if (a.xh)   // fp16 hi/lo planes of xn for the tensor-core products: xn = hi + lo to about 2^-22
+      for (int i = tid; i < E; i += BT) {
+        const __half h = __float2half_rn(xn[i]);
+        a.xh[static_cast<size_t>(t) * E + i] = h;
+        a.xl[static_cast<size_t>(t) * E + i] = __float2half_rn(__fsub_rn(xn[i], __half2float(h)));
+      }
     q8k_quantize_block(xn, E, a.xq_qs + static_cast<size_t>(t) * E, a.xq_d + static_cast<size_t>(t) * (E / 256),
                        a.xq_bs + static_cast<size_t>(t) * (E / 16), warp, BNW, lane);
   }
@@ -348,10 +355,16 @@ int launch_batched(const BatchArgs &a, void *stream_) {
     cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attrs[dev] = true;
   }
-  gateup_kernel<<<dim3(NE, (FF + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, gu_smem, st>>>(a);
-  if (a.down_type != T_Q8_0) hq_kernel<<<T * K, 32 * (FF / 256), 0, st>>>(a, T * K);
-  const size_t dn_smem = 16 + FF * 4 + align16(ROWS_PER_CTA * a.drb + 32) + 16;
-  down_kernel<<<dim3(NE, (E + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, dn_smem, st>>>(a);
+  if (a.xh) {   // Q8_0 experts: grouped GEMMs on the tensor cores
+    int rc = launch_q80_tc(a, stream_, true);
+    if (rc == 0) rc = launch_q80_tc(a, stream_, false);
+    if (rc) return rc;
+  } else {
+    gateup_kernel<<<dim3(NE, (FF + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, gu_smem, st>>>(a);
+    if (a.down_type != T_Q8_0) hq_kernel<<<T * K, 32 * (FF / 256), 0, st>>>(a, T * K);
+    const size_t dn_smem = 16 + FF * 4 + align16(ROWS_PER_CTA * a.drb + 32) + 16;
+    down_kernel<<<dim3(NE, (E + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, dn_smem, st>>>(a);
+  }
   combine_kernel<<<T, BT, 0, st>>>(a);
   return static_cast<int>(cudaGetLastError());
 }

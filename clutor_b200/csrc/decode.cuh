@@ -1,6 +1,7 @@
 // Arguments and limits of the one-token MoE kernel (decode.cu) and the batched kernels (batched.cu).
 #pragma once
 #include <cstdint>
+#include <cuda_fp16.h>
 
 namespace clb {
 
@@ -62,6 +63,9 @@ struct BatchArgs {
   float *hq_d;          // [T * K * FF / 256]
   int16_t *hq_bs;       // [T * K * FF / 16]
   float *hd;            // [T * K * E] by dispatch position
+  __half *xh, *xl;      // [T * E] xn as fp16 hi and lo planes (tensor-core path; null otherwise)
+  __half *hgh, *hgl;    // [T * K * FF] hg as fp16 hi and lo planes, by dispatch position (tensor-core path)
+  __half *xdh, *xdl;    // [T * K * E] the xn planes gathered into dispatch order (tensor-core path)
   int *sel_out;         // [T * K] or null
   float *wt_out;        // [T * K] or null
   int *err;
@@ -69,5 +73,7 @@ struct BatchArgs {
 
 // Launches the batched path on `stream`; returns a CUDA error code.
 int launch_batched(const BatchArgs &a, void *stream);
+// The Q8_0 expert products on tcgen05 (grouped_tc.cu): gate/up (writes hgh/hgl) or down (writes hd).
+int launch_q80_tc(const BatchArgs &a, void *stream, bool gateup);
 
 }  // namespace clb

@@ -1,0 +1,66 @@
+// tcgen05 (5th-generation tensor core) and TMEM helpers for sm_100a, written from the PTX ISA.
+//
+// Operand tiles live in shared memory in the canonical K-major 128-byte-swizzled layout: a tile of R rows x 64 fp16 is
+// R/8 atoms of 1024 bytes; row r of an atom is 128 bytes at (r % 8) * 128, and its 16-byte chunk j sits at chunk position
+// j ^ (r % 8). The tile starts on a 1024-byte boundary. One MMA (K = 16 fp16 = 32 bytes) reads a 32-byte column slice of
+// every row; successive K steps advance the descriptor's start address by 32 bytes.
+#pragma once
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace clb {
+namespace tc {
+
+// Byte offset of 16-byte chunk j (elements 8j .. 8j+7) of row r in a K-major SW128 tile of 64 fp16 per row.
+CLB_DEV uint32_t sw128_chunk(int r, int j) {
+  return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// Shared-memory matrix descriptor: start address, LBO 16 bytes (unused by swizzled K-major layouts), SBO 1024 bytes
+// (between 8-row atoms), descriptor version 1, layout SWIZZLE_128B.
+CLB_DEV uint64_t sw128_desc(uint32_t smem_byte_addr) {
+  return (static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFFu)) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor of kind::f16 with fp16 A and B, fp32 accumulators, both operands K-major, M x N.
+constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+CLB_DEV void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+// The mbarrier gets one arrival when every tcgen05 operation this thread issued before has completed.
+CLB_DEV void commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// Called by a whole warp. The allocated TMEM address is written to *dst (shared memory).
+CLB_DEV void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+CLB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+CLB_DEV void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+CLB_DEV void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 8 consecutive fp32 columns of this thread's TMEM lane (the warp reads lanes 32*(warp%4) .. +31).
+CLB_DEV void ld_x8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace tc
+}  // namespace clb

@@ -61,29 +61,38 @@ def test_golden_fixtures(ctx, golden):
 @pytest.mark.parametrize("gt,dt", [(synth.T_Q4_K, synth.T_Q4_K), (synth.T_Q4_K, synth.T_Q6_K), (synth.T_Q8_0, synth.T_Q8_0),
                                    (synth.T_Q6_K, synth.T_Q4_K)])
 def test_decode_full_size_chain(ctx, gt, dt):
-    """Qwen3-30B-A3B layer shape, one token through 4 layers in a chain (device layers, device entry point), against the
-    oracle run on copies of the same bytes."""
+    """Qwen3-30B-A3B layer shape, one token through 4 layers (device layers, device entry point). Each layer is checked
+    from the oracle's own input to it (top-k exact, weights 1e-6, update 1e-3), and the chain run on the GPU end to end is
+    checked against the oracle's chain (top-k exact, final update 1e-3; Q8_0 layers take the tensor-core path, accurate to
+    ~1e-7 rather than bit-exact, so chained inputs drift by that much)."""
     import torch
     layers = [synth.device_layer(gate_type=gt, down_type=dt, seed=100 + i) for i in range(4)]
     handles = [ctx.bind(L) for L in layers]
+    host = [synth.to_host(L) for L in layers]
     x0 = synth.activations(1, 2048, seed=5)
-    x = torch.from_numpy(x0).cuda()
-    sel = torch.zeros((4, 8), dtype=torch.int32, device="cuda")
-    wt = torch.zeros((4, 8), dtype=torch.float32, device="cuda")
-    for i, h in enumerate(handles):
-        ctx.moe_ffn_dev(h, x, sel[i], wt[i])
-    ctx.status()
     xr = x0.copy()
-    for i, L in enumerate(layers):
-        HL = synth.to_host(L)
-        xin = xr.copy()
-        xr, s, w = oracle.moe_ffn(HL, xin, "oracle")
-        assert np.array_equal(sel[i].cpu().numpy(), s[0]), f"layer {i} top-k"
-        assert np.allclose(wt[i].cpu().numpy(), w[0], rtol=TOL_WT)
-    got = x.cpu().numpy()
-    e = rel_l2(got - x0, xr - x0)
+    worst = 0.0
+    for i, h in enumerate(handles):           # layer by layer, from the oracle's input
+        x = torch.from_numpy(xr).cuda()
+        sel = torch.zeros((1, 8), dtype=torch.int32, device="cuda")
+        wt = torch.zeros((1, 8), dtype=torch.float32, device="cuda")
+        ctx.moe_ffn_dev(h, x, sel, wt)
+        ctx.status()
+        want = oracle.moe_ffn(host[i], xr, "oracle")
+        worst = max(worst, check(xr, (x.cpu().numpy(), sel.cpu().numpy(), wt.cpu().numpy()), want, f"layer {i}"))
+        xr = want[0]
+    x = torch.from_numpy(x0).cuda()           # the chain on the GPU alone
+    sel = torch.zeros((4, 8), dtype=torch.int32, device="cuda")
+    for i, h in enumerate(handles):
+        ctx.moe_ffn_dev(h, x, sel[i])
+    ctx.status()
+    xc = x0.copy()
+    for i in range(4):
+        xc, s, _ = oracle.moe_ffn(host[i], xc, "oracle")
+        assert np.array_equal(sel[i].cpu().numpy(), s[0]), f"chained layer {i} top-k"
+    e = rel_l2(x.cpu().numpy() - x0, xc - x0)
     assert e <= TOL_REL_L2
-    print(f"chain of 4 layers {gt}/{dt}: relative L2 of the update {e:.3e}")
+    print(f"{gt}/{dt}: worst per-layer relative L2 {worst:.3e}, chain of 4 {e:.3e}")
 
 
 def test_repeated_calls_reset_their_counters(ctx):
