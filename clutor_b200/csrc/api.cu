@@ -421,7 +421,8 @@ static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *se
   b.hd = reinterpret_cast<float *>(sc + s.off_hd);
   b.sel_out = sel; b.wt_out = wt;
   b.err = c->small;
-  if (L.gate.type == T_Q8_0 && L.up.type == T_Q8_0 && L.down.type == T_Q8_0) {   // tensor-core expert products
+  if (L.gate.type == T_Q8_0 && L.up.type == T_Q8_0 && L.down.type == T_Q8_0 &&
+      q80_tc_supported(L.gate.p, L.up.p, L.down.p, E, FF)) {   // tensor-core expert products
     b.xh = reinterpret_cast<__half *>(sc + s.off_xh);
     b.xl = reinterpret_cast<__half *>(sc + s.off_xl);
     b.hgh = reinterpret_cast<__half *>(sc + s.off_hgh);

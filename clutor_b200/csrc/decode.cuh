@@ -75,5 +75,7 @@ struct BatchArgs {
 int launch_batched(const BatchArgs &a, void *stream);
 // The Q8_0 expert products on tcgen05 (grouped_tc.cu): gate/up (writes hgh/hgl) or down (writes hd).
 int launch_q80_tc(const BatchArgs &a, void *stream, bool gateup);
+// Whether the tensor-core Q8_0 path takes these experts (16-byte aligned weights, E and FF multiples of 256).
+bool q80_tc_supported(const void *gate, const void *up, const void *down, int E, int FF);
 
 }  // namespace clb
