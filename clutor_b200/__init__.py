@@ -58,6 +58,18 @@ class Backend(C.Structure):
     _fields_ = [("name", C.c_char_p), ("supports", SUPPORTS), ("matvec_batch", MATVEC)]
 
 
+class CacheStats(C.Structure):
+    """clb200_cache_stats == the reference's cl_cache_stats (c/src/cache.h:14-17)."""
+    _fields_ = [(n, C.c_uint64) for n in ("hits", "misses", "stage_hits", "inserts", "evictions", "admit_rejects",
+                                         "stage_inserts", "stage_wasted", "aging_resets")] + [("window_slots", C.c_uint32)]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+LRU, WTINYLFU, ADAPTIVE = 0, 1, 2
+
+
 _lib: C.CDLL | None = None
 
 
@@ -87,6 +99,25 @@ def lib() -> C.CDLL:
         L.clb200_device_bytes.restype = C.c_uint64
         L.clb200_device_bytes.argtypes = [C.c_void_p]
         L.clb200_backend.restype = C.POINTER(Backend)
+        L.clb200_cache_new.restype = C.c_void_p
+        L.clb200_cache_new.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.c_uint32]
+        L.clb200_cache_free.argtypes = [C.c_void_p]
+        L.clb200_cache_access.argtypes = [C.c_void_p, C.c_uint32, C.POINTER(C.c_int)]
+        L.clb200_cache_stage.argtypes = [C.c_void_p, C.c_uint32]
+        for f in ("pin", "unpin", "abandon"):
+            getattr(L, f"clb200_cache_{f}").argtypes = [C.c_void_p, C.c_int]
+        L.clb200_cache_find.argtypes = [C.c_void_p, C.c_uint32]
+        L.clb200_cache_freq.argtypes = [C.c_void_p, C.c_uint32]
+        L.clb200_cache_freq.restype = C.c_uint32
+        L.clb200_cache_count.argtypes = [C.c_void_p]
+        L.clb200_cache_count.restype = C.c_uint32
+        L.clb200_cache_total_slots.argtypes = [C.c_void_p]
+        L.clb200_cache_total_slots.restype = C.c_uint32
+        L.clb200_cache_segment.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_cache_slot_key.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_cache_slot_key.restype = C.c_uint32
+        L.clb200_cache_get_stats.argtypes = [C.c_void_p]
+        L.clb200_cache_get_stats.restype = CacheStats
         _lib = L
     return _lib
 
@@ -214,3 +245,56 @@ def matvec(type_: int, w: np.ndarray, rows: int, cols: int, xf: np.ndarray | Non
     be = backend()
     be.matvec_batch(C.byref(job), 1)
     return out
+
+
+class ExpertCache:
+    """The expert-cache policy (clb200_cache_*): which expert holds which HBM slot. Host code; needs no GPU."""
+
+    def __init__(self, cache_slots: int, stage_slots: int, universe: int, policy: int = WTINYLFU, window_pct: int = 0):
+        self.L = lib()
+        self.h = self.L.clb200_cache_new(cache_slots, stage_slots, universe, policy, window_pct)
+        if not self.h:
+            raise ValueError("clb200_cache_new refused the sizes")
+
+    def close(self) -> None:
+        if self.h:
+            self.L.clb200_cache_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def access(self, key: int) -> tuple[int, int]:
+        slot = C.c_int(-1)
+        r = self.L.clb200_cache_access(self.h, key, C.byref(slot))
+        return r, slot.value
+
+    def stage(self, key: int) -> int:
+        return self.L.clb200_cache_stage(self.h, key)
+
+    def pin(self, slot: int) -> None:
+        self.L.clb200_cache_pin(self.h, slot)
+
+    def unpin(self, slot: int) -> None:
+        self.L.clb200_cache_unpin(self.h, slot)
+
+    def abandon(self, slot: int) -> None:
+        self.L.clb200_cache_abandon(self.h, slot)
+
+    def find(self, key: int) -> int:
+        return self.L.clb200_cache_find(self.h, key)
+
+    def freq(self, key: int) -> int:
+        return self.L.clb200_cache_freq(self.h, key)
+
+    def count(self) -> int:
+        return self.L.clb200_cache_count(self.h)
+
+    def total_slots(self) -> int:
+        return self.L.clb200_cache_total_slots(self.h)
+
+    def segment(self, slot: int) -> int:
+        return self.L.clb200_cache_segment(self.h, slot)
+
+    def stats(self) -> dict:
+        return self.L.clb200_cache_get_stats(self.h).as_dict()

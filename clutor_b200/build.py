@@ -8,6 +8,7 @@ spell out the few fused multiply-adds they want.
 from __future__ import annotations
 
 import argparse
+import concurrent.futures
 import os
 import subprocess
 import sys
@@ -15,7 +16,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ["api.cu", "decode.cu", "batched.cu", "backend.cu", "noalloc.cu", "grouped_tc.cu"]
+SOURCES = ["api.cu", "decode.cu", "batched.cu", "backend.cu", "noalloc.cu", "grouped_tc.cu", "cache.cpp"]
 LIB = os.path.join(HERE, "libclutor_b200.so")
 
 
@@ -39,10 +40,10 @@ def build(verbose: bool = False, ptxas_v: bool = False, force: bool = False) -> 
     deps = srcs + [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith(".cuh")] + [os.path.join(ROOT, "include", "clb200.h")]
     if not force and os.path.exists(LIB) and all(os.path.getmtime(d) <= os.path.getmtime(LIB) for d in deps):
         return LIB
-    objs = []
     bdir = os.path.join(HERE, "_build")
     os.makedirs(bdir, exist_ok=True)
-    for s in srcs:
+
+    def compile_one(s: str) -> str:
         o = os.path.join(bdir, os.path.basename(s) + ".o")
         cmd = [nvcc(), *flags(ptxas_v), "-c", s, "-o", o]
         if verbose:
@@ -52,7 +53,10 @@ def build(verbose: bool = False, ptxas_v: bool = False, force: bool = False) -> 
             raise RuntimeError(f"nvcc failed on {s}:\n{r.stdout}\n{r.stderr}")
         if ptxas_v or verbose:
             sys.stdout.write(r.stdout + r.stderr)
-        objs.append(o)
+        return o
+
+    with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as pool:
+        objs = list(pool.map(compile_one, srcs))
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC", *objs, "-o", LIB, "-lcudart"]
     if verbose:
         print(" ".join(cmd), flush=True)

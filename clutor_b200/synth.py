@@ -207,3 +207,78 @@ def to_host(layer: DeviceLayer) -> HostLayer:
                      down_type=layer.down_type, ffn_norm=layer.ffn_norm.cpu().numpy(), router=layer.router.cpu().numpy(),
                      gate=layer.gate.cpu().numpy(), up=layer.up.cpu().numpy(), down=layer.down.cpu().numpy(),
                      norm_topk=layer.norm_topk, resid_scale=layer.resid_scale, rms_eps=layer.rms_eps)
+
+
+# ---- synthetic expert-selection stream for the cache stress workload -----------------------------------------------------
+# The reference's own stress harness draws router logits with this generator (c/src/stream.c:114-140): per layer a fixed
+# Zipf-like popularity (a seeded permutation of experts, logit -3 * locality * ln(rank + 1) / ln(E)), 8 "topics" that each
+# lift 12 experts per layer by 1.5 and change every 16 tokens, and unit Gaussian noise per (token, layer, expert); the
+# predictor's logits share the noise with correlation rho. Restated here (vectorised) so the cache workload sees the
+# reference's key stream; routing from these logits is the plain top-K (c/src/route.c:13-30).
+
+_M64 = np.uint64(0xFFFFFFFFFFFFFFFF)
+
+
+def _mix64(x: np.ndarray) -> np.ndarray:
+    x = np.asarray(x, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        x = x + np.uint64(0x9E3779B97F4A7C15)
+        x = (x ^ (x >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        x = (x ^ (x >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return x ^ (x >> np.uint64(31))
+
+
+def _unit(x: np.ndarray) -> np.ndarray:
+    return (_mix64(x) >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
+
+
+def _gauss(x: np.ndarray) -> np.ndarray:
+    with np.errstate(over="ignore"):
+        return (_unit(x) + _unit(x + np.uint64(1)) + _unit(x + np.uint64(2)) + _unit(x + np.uint64(3)) - 2.0) * 1.7320508
+
+
+class ExpertStream:
+    """Router logits of the reference's stress harness: logits(t, l) for token t and layer l, float32 [E]."""
+
+    TOPICS, TOPIC_LEN = 8, 16
+
+    def __init__(self, L: int, E: int, locality: float = 1.0, seed: int = 1, rho: float = 0.8):
+        self.L, self.E, self.seed, self.rho, self.sigma = L, E, seed, rho, 1.0
+        self.base = np.zeros((L, E), np.float32)
+        self.bonus = np.zeros((self.TOPICS, L, E), np.float32)
+        s = np.uint64(seed)
+        for l in range(L):
+            perm = list(range(E))
+            for i in range(E - 1, 0, -1):
+                j = int(_mix64(s ^ np.uint64(l << 20) ^ np.uint64(i)) % np.uint64(i + 1))
+                perm[i], perm[j] = perm[j], perm[i]
+            for rank in range(E):
+                self.base[l, perm[rank]] = np.float32(-3.0 * locality * np.log(rank + 1.0) / np.log(E))
+            for tp in range(self.TOPICS):
+                for k in range(min(12, E)):
+                    e = int(_mix64(s ^ np.uint64(0xABCDEF) ^ np.uint64(tp << 32) ^ np.uint64(l << 16) ^ np.uint64(k)) % np.uint64(E))
+                    self.bonus[tp, l, e] += np.float32(1.5)
+
+    def logits(self, t: np.ndarray | int, l: int, predicted: bool = False) -> np.ndarray:
+        """[len(t), E] float32 logits of layer l for tokens t (topics drift every 16 tokens)."""
+        t = np.atleast_1d(np.asarray(t, dtype=np.int64))
+        e = np.arange(self.E, dtype=np.uint64)
+        with np.errstate(over="ignore"):
+            k = (np.uint64(self.seed) ^ (t.astype(np.uint64)[:, None] << np.uint64(24)) ^ np.uint64(l << 12)
+                 ^ (e[None, :] * np.uint64(0x9E3779B1)))
+            n = _gauss(k * np.uint64(4) + np.uint64(1))
+            if predicted:
+                n = self.rho * n + np.sqrt(max(0.0, 1.0 - self.rho * self.rho)) * _gauss(k * np.uint64(4) + np.uint64(7777))
+        tp = (t // self.TOPIC_LEN) % self.TOPICS
+        out = (self.base[l][None, :] + self.bonus[tp, l]).astype(np.float64) + self.sigma * n   # float sum, then double
+        return out.astype(np.float32)
+
+
+def route_topk(logits: np.ndarray, K: int) -> tuple[np.ndarray, np.ndarray]:
+    """Plain top-K of each row of logits (c/src/route.c:17-23): softmax in double, best first, ties to the lower id.
+    Returns (sel int32 [n, K], p float32 [n, K] -- the chosen probabilities, not renormalised)."""
+    lg = np.atleast_2d(logits).astype(np.float64)
+    p = np.exp(lg - lg.max(axis=1, keepdims=True))
+    p /= p.sum(axis=1, keepdims=True)
+    order = np.lexsort((np.broadcast_to(np.arange(lg.shape[1]), lg.shape), -p), axis=1)[:, :K]
+    return order.astype(np.int32), np.take_along_axis(p, order, axis=1).astype(np.float32)

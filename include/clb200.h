@@ -97,6 +97,35 @@ int clb200_status(clb200_ctx *c, char *err, size_t errlen);
 /* Bytes of device memory the context holds for layers and scratch. */
 uint64_t clb200_device_bytes(const clb200_ctx *c);
 
+/* ---- the expert cache policy (host) -------------------------------------------------------------------------------------- */
+/* Which expert occupies which HBM slot: the reference's cl_cache (c/src/cache.h:11-47, c/src/cache.c), same decisions, same
+ * slot numbers for the same sequence of calls. It holds no data; the device store below owns the slots. */
+enum { CLB200_LRU = 0, CLB200_WTINYLFU = 1, CLB200_ADAPTIVE = 2 };                          /* cl_policy (cache.h:11) */
+enum { CLB200_SEG_FREE = 0, CLB200_SEG_WINDOW, CLB200_SEG_PROBATION, CLB200_SEG_PROTECTED, CLB200_SEG_STAGE }; /* cl_list */
+typedef struct {   /* cl_cache_stats (cache.h:14-17), same layout */
+  uint64_t hits, misses, stage_hits, inserts, evictions, admit_rejects, stage_inserts, stage_wasted, aging_resets;
+  uint32_t window_slots;
+} clb200_cache_stats;
+typedef struct clb200_cache clb200_cache;
+/* cl_cache_new (cache.c:86-112): cache_slots experts, stage_slots prefetch slots, keys 0..universe-1 (layer * n_expert +
+ * expert); window_pct 0 = the default window. NULL for zero slots or keys. */
+clb200_cache *clb200_cache_new(uint32_t cache_slots, uint32_t stage_slots, uint32_t universe, int policy, uint32_t window_pct);
+void clb200_cache_free(clb200_cache *c);                                   /* cl_cache_free */
+uint32_t clb200_cache_total_slots(const clb200_cache *c);                  /* cl_cache_total_slots: cache + stage + 1 */
+int clb200_cache_find(const clb200_cache *c, uint32_t key);                /* cl_cache_find: slot or -1 */
+int clb200_cache_segment(const clb200_cache *c, int slot);                 /* cl_cache_list */
+uint32_t clb200_cache_slot_key(const clb200_cache *c, int slot);           /* cl_cache_slot_key */
+/* cl_cache_access (cache.c:190-216): 1 hit, 2 hit in staging (adopted), 0 miss (slot assigned and pinned: fill it),
+ * -1 miss with nothing evictable (bypass). The slot is pinned in every case but -1. */
+int clb200_cache_access(clb200_cache *c, uint32_t key, int *slot);
+int clb200_cache_stage(clb200_cache *c, uint32_t key);                     /* cl_cache_stage (cache.c:218-232) */
+void clb200_cache_pin(clb200_cache *c, int slot);                          /* cl_cache_pin */
+void clb200_cache_unpin(clb200_cache *c, int slot);                        /* cl_cache_unpin */
+void clb200_cache_abandon(clb200_cache *c, int slot);                      /* cl_cache_abandon */
+uint32_t clb200_cache_freq(const clb200_cache *c, uint32_t key);           /* cl_cache_freq: sketch estimate 0..15 */
+clb200_cache_stats clb200_cache_get_stats(const clb200_cache *c);          /* cl_cache_get_stats */
+uint32_t clb200_cache_count(const clb200_cache *c);                        /* cl_cache_count: experts cached (not staged) */
+
 /* ---- the plugin seam: a cl_backend for cl_matvec_batch ------------------------------------------------------------------- */
 /* Layout-compatible copies of the reference's cl_q8k, cl_xq and cl_mv (c/src/quant.h:22-34) and cl_backend (backend.h:9-13). */
 typedef struct { float d; int8_t qs[256]; int16_t bsums[16]; } clb200_q8k;

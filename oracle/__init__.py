@@ -89,7 +89,72 @@ def ref_lib() -> C.CDLL:
     lib.cl_cache_freq.restype = C.c_uint32
     lib.cl_cache_count.argtypes = [C.c_void_p]
     lib.cl_cache_count.restype = C.c_uint32
+    lib.cl_cache_abandon.argtypes = [C.c_void_p, C.c_int]
+    lib.cl_cache_total_slots.argtypes = [C.c_void_p]
+    lib.cl_cache_total_slots.restype = C.c_uint32
+    lib.cl_cache_list.argtypes = [C.c_void_p, C.c_int]
+    lib.cl_cache_get_stats.argtypes = [C.c_void_p]
+    lib.cl_cache_get_stats.restype = CacheStats
     return lib
+
+
+class CacheStats(C.Structure):
+    """cl_cache_stats (c/src/cache.h:14-17)."""
+    _fields_ = [(n, C.c_uint64) for n in ("hits", "misses", "stage_hits", "inserts", "evictions", "admit_rejects",
+                                         "stage_inserts", "stage_wasted", "aging_resets")] + [("window_slots", C.c_uint32)]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+class RefCache:
+    """The reference's own expert-cache policy (c/src/cache.c, compiled into _ref/libclref.so), driven call by call."""
+
+    def __init__(self, cache_slots: int, stage_slots: int, universe: int, policy: int, window_pct: int = 0):
+        self.L = ref_lib()
+        self.h = self.L.cl_cache_new(cache_slots, stage_slots, universe, policy, window_pct)
+        if not self.h:
+            raise ValueError("cl_cache_new refused the sizes")
+
+    def close(self) -> None:
+        if self.h:
+            self.L.cl_cache_free(self.h)
+            self.h = None
+
+    def access(self, key: int) -> tuple[int, int]:
+        slot = C.c_int(-1)
+        r = self.L.cl_cache_access(self.h, key, C.byref(slot))
+        return r, slot.value
+
+    def stage(self, key: int) -> int:
+        return self.L.cl_cache_stage(self.h, key)
+
+    def pin(self, slot: int) -> None:
+        self.L.cl_cache_pin(self.h, slot)
+
+    def unpin(self, slot: int) -> None:
+        self.L.cl_cache_unpin(self.h, slot)
+
+    def abandon(self, slot: int) -> None:
+        self.L.cl_cache_abandon(self.h, slot)
+
+    def find(self, key: int) -> int:
+        return self.L.cl_cache_find(self.h, key)
+
+    def freq(self, key: int) -> int:
+        return self.L.cl_cache_freq(self.h, key)
+
+    def count(self) -> int:
+        return self.L.cl_cache_count(self.h)
+
+    def total_slots(self) -> int:
+        return self.L.cl_cache_total_slots(self.h)
+
+    def segment(self, slot: int) -> int:
+        return self.L.cl_cache_list(self.h, slot)
+
+    def stats(self) -> dict:
+        return self.L.cl_cache_get_stats(self.h).as_dict()
 
 
 def _ptr(a: np.ndarray) -> int:
