@@ -70,6 +70,16 @@ class CacheStats(C.Structure):
 LRU, WTINYLFU, ADAPTIVE = 0, 1, 2
 
 
+class StoreStats(C.Structure):
+    """clb200_store_stats (the reference's cl_xs_stats, c/src/xs.h:14-17, with copy_ns for read_ns)."""
+    _fields_ = [(n, C.c_uint64) for n in ("accesses", "hits", "stage_hits", "misses", "bypass", "prefetch_issued",
+                                         "prefetch_late", "prefetch_wasted", "admit_rejects", "evictions", "demand_bytes",
+                                         "prefetch_bytes", "copy_ns", "wait_ns")]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
 _lib: C.CDLL | None = None
 
 
@@ -118,6 +128,31 @@ def lib() -> C.CDLL:
         L.clb200_cache_slot_key.restype = C.c_uint32
         L.clb200_cache_get_stats.argtypes = [C.c_void_p]
         L.clb200_cache_get_stats.restype = CacheStats
+        L.clb200_store_open.restype = C.c_void_p
+        L.clb200_store_open.argtypes = [C.c_void_p, C.POINTER(MoELayer), C.c_int, C.c_uint64, C.c_int, C.c_int, C.c_char_p, C.c_size_t]
+        L.clb200_store_close.argtypes = [C.c_void_p]
+        L.clb200_store_load_layer.argtypes = [C.c_void_p, C.c_int, C.POINTER(MoELayer), C.c_char_p, C.c_size_t]
+        L.clb200_store_cache_slots.argtypes = [C.c_void_p]
+        L.clb200_store_cache_slots.restype = C.c_uint32
+        L.clb200_store_slot_bytes.argtypes = [C.c_void_p]
+        L.clb200_store_slot_bytes.restype = C.c_uint64
+        L.clb200_store_get_stats.argtypes = [C.c_void_p]
+        L.clb200_store_get_stats.restype = StoreStats
+        L.clb200_store_reset_stats.argtypes = [C.c_void_p]
+        L.clb200_store_set_prefetch.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_store_log.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_store_read_log.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
+        L.clb200_store_read_log.restype = C.c_int64
+        L.clb200_store_request.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        L.clb200_store_wait.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_store_wait.restype = C.c_void_p
+        L.clb200_store_release.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        L.clb200_store_resident.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        L.clb200_store_prefetch.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        L.clb200_moe_ffn_stored.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                            C.c_char_p, C.c_size_t]
+        L.clb200_moe_experts_stored.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                C.c_void_p, C.c_char_p, C.c_size_t]
         _lib = L
     return _lib
 
@@ -298,3 +333,68 @@ class ExpertCache:
 
     def stats(self) -> dict:
         return self.L.clb200_cache_get_stats(self.h).as_dict()
+
+
+class Store:
+    """The HBM expert store (clb200_store_*): every layer's experts in pinned host memory, a cache budget of them in HBM."""
+
+    def __init__(self, ctx: "Context", shape, n_layer: int, cache_bytes: int, stage_slots: int, policy: int = WTINYLFU):
+        self.ctx, self.L = ctx, lib()
+        self._err = C.create_string_buffer(512)
+        self._shape = layer_struct(shape)
+        self.h = self.L.clb200_store_open(ctx.handle, C.byref(self._shape), n_layer, cache_bytes, stage_slots, policy, self._err, 512)
+        if not self.h:
+            raise ClutorError(self._err.value.decode())
+        self.K = shape.K
+
+    def close(self) -> None:
+        if self.h:
+            self.L.clb200_store_close(self.h)
+            self.h = None
+
+    def load_layer(self, i: int, layer) -> None:
+        s = layer_struct(layer)
+        if self.L.clb200_store_load_layer(self.h, i, C.byref(s), self._err, 512):
+            raise ClutorError(self._err.value.decode())
+
+    def cache_slots(self) -> int:
+        return self.L.clb200_store_cache_slots(self.h)
+
+    def slot_bytes(self) -> int:
+        return self.L.clb200_store_slot_bytes(self.h)
+
+    def stats(self) -> dict:
+        return self.L.clb200_store_get_stats(self.h).as_dict()
+
+    def reset_stats(self) -> None:
+        self.L.clb200_store_reset_stats(self.h)
+
+    def set_prefetch(self, on: bool) -> None:
+        self.L.clb200_store_set_prefetch(self.h, int(on))
+
+    def log(self, on: bool) -> None:
+        self.L.clb200_store_log(self.h, int(on))
+
+    def read_log(self) -> np.ndarray:
+        n = self.L.clb200_store_read_log(self.h, None, 0)
+        out = np.zeros(n, np.int64)
+        self.L.clb200_store_read_log(self.h, out.ctypes.data, n)
+        return out.reshape(-1, 3)
+
+    def moe_ffn(self, layer: int, x, stream=None):
+        """One token of `layer` through the store; x a device tensor [n_embd], updated in place. Returns (sel, wt)."""
+        sel = np.zeros(self.K, np.int32)
+        wt = np.zeros(self.K, np.float32)
+        if self.L.clb200_moe_ffn_stored(self.ctx.handle, self.h, layer, _ptr(x), sel.ctypes.data, wt.ctypes.data, stream,
+                                        self._err, 512):
+            raise ClutorError(self._err.value.decode())
+        return sel, wt
+
+    def experts(self, layer: int, x, sel: np.ndarray, wt: np.ndarray, next_pred: np.ndarray | None = None, stream=None):
+        """The experts of a given routing (host arrays) through the store; x a device tensor, updated in place."""
+        sel = np.ascontiguousarray(sel, np.int32)
+        wt = np.ascontiguousarray(wt, np.float32)
+        nxt = None if next_pred is None else np.ascontiguousarray(next_pred, np.int32)
+        if self.L.clb200_moe_experts_stored(self.ctx.handle, self.h, layer, _ptr(x), sel.ctypes.data, wt.ctypes.data,
+                                            None if nxt is None else nxt.ctypes.data, stream, self._err, 512):
+            raise ClutorError(self._err.value.decode())

@@ -9,96 +9,10 @@
 #include <unordered_map>
 #include <vector>
 
-#include "../../include/clb200.h"
-#include "common.cuh"
-#include "decode.cuh"
-
-namespace clb {
-
-static void errf(char *err, size_t errlen, const char *fmt, ...) {
-  if (!err || !errlen) return;
-  va_list ap;
-  va_start(ap, fmt);
-  vsnprintf(err, errlen, fmt, ap);
-  va_end(ap);
-}
-
-static uint64_t row_bytes(uint32_t t, uint64_t n) {
-  switch (t) {
-    case T_Q4_K: return n / 256 * 144;
-    case T_Q6_K: return n / 256 * 210;
-    case T_Q8_0: return n / 32 * 34;
-    case T_F32: return n * 4;
-    case T_F16: return n * 2;
-    default: return 0;
-  }
-}
-static bool expert_type(uint32_t t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; }
-static const char *type_name(uint32_t t) {
-  switch (t) {
-    case T_Q4_K: return "Q4_K";
-    case T_Q6_K: return "Q6_K";
-    case T_Q8_0: return "Q8_0";
-    case T_F32: return "F32";
-    case T_F16: return "F16";
-    default: return "an unsupported type";
-  }
-}
-static size_t al(size_t v, size_t a = 256) { return (v + a - 1) / a * a; }
-
-#define CUDA_OR(call, msg)                                                                                            \
-  do {                                                                                                                \
-    cudaError_t e_ = (call);                                                                                          \
-    if (e_ != cudaSuccess) { errf(err, errlen, "%s: %s", msg, cudaGetErrorString(e_)); return 1; }                    \
-  } while (0)
-
-struct DevLayer {
-  clb200_moe_layer d{};              // device pointers
-  const void *hkey[5] = {};          // host pointers of norm, router, gate, up, down (0 when bound on the device)
-  uint64_t fp = 0;                   // fingerprint of the host tensors' shapes and edge bytes (uploaded layers)
-  void *block = nullptr;             // the owned device copy (upload), else null
-  size_t bytes = 0;
-  bool live = false;
-};
-
-// FNV-1a over the layer's shape fields and the first and last 64 bytes of each host tensor: a cheap check that a host
-// pointer seen before still holds the weights that were uploaded from it (a freed and reused buffer usually does not).
-static uint64_t fingerprint(const clb200_moe_layer *L) {
-  uint64_t h = 1469598103934665603ull;
-  auto mix = [&](const void *p, size_t n) {
-    const uint8_t *b = static_cast<const uint8_t *>(p);
-    for (size_t i = 0; i < n; ++i) { h ^= b[i]; h *= 1099511628211ull; }
-  };
-  const int shape[9] = {L->n_embd, L->n_ff_exp, L->n_expert, L->n_used, L->norm_topk, static_cast<int>(L->gate.type),
-                        static_cast<int>(L->up.type), static_cast<int>(L->down.type), 0};
-  mix(shape, sizeof shape);
-  const size_t E = L->n_embd, NE = L->n_expert;
-  const void *ptr[5] = {L->ffn_norm_f, L->router_f, L->gate.p, L->up.p, L->down.p};
-  const size_t sz[5] = {E * 4, NE * E * 4, NE * L->gate_slab, NE * L->up_slab, NE * L->down_slab};
-  for (int i = 0; i < 5; ++i) {
-    const size_t n = sz[i] < 64 ? sz[i] : 64;
-    mix(ptr[i], n);
-    mix(static_cast<const uint8_t *>(ptr[i]) + sz[i] - n, n);
-  }
-  return h;
-}
-
-}  // namespace clb
+#include "ctx.cuh"
 
 using namespace clb;
 
-struct clb200_ctx {
-  int device = 0, sms = 0, max_smem = 0;
-  cudaStream_t stream = nullptr;
-  std::vector<DevLayer> layers;
-  std::unordered_map<const void *, int> by_gate;   // host gate pointer -> layer index
-  int *small = nullptr;                            // [0] device error word, [64..] counters of the one-token kernel
-  uint8_t *scratch = nullptr;
-  size_t scratch_cap = 0;
-  float *hx = nullptr;                             // host-call staging of x / sel / wt on the device (in scratch)
-  uint64_t bytes = 0;
-  bool attrs_set = false;
-};
 
 namespace clb {
 
@@ -208,7 +122,7 @@ static int plan_decode(const clb200_ctx *c, const clb200_moe_layer &L, DecodeArg
   return plan_decode_shape(c->sms, c->max_smem, L, a);
 }
 
-static int validate(const clb200_moe_layer *L, char *err, size_t errlen) {
+int validate(const clb200_moe_layer *L, char *err, size_t errlen) {
   if (!L) { errf(err, errlen, "no layer"); return 1; }
   const int E = L->n_embd, FF = L->n_ff_exp;
   if (E < 256 || E % 256 || E > 4096 || FF < 256 || FF % 256 || FF > 4096) {
@@ -246,6 +160,54 @@ static const char *device_error_text(int code) {
     case ERR_BAD_EXPERT: return "an expert id out of range reached the dispatch";
     default: return "unknown device error";
   }
+}
+
+int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
+               const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen) {
+  const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+  DecodeArgs a{};
+  if (plan_decode(c, L, a)) { errf(err, errlen, "the one-token kernel does not take this layer (K-quant experts only)"); return 1; }
+  const Scratch s = plan_scratch(1, E, FF, NE, K, false);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  uint8_t *sc = c->scratch;
+  a.x_in = x; a.x_out = x;
+  a.norm = L.ffn_norm_f; a.router = L.router_f;
+  a.gate = L.gate.p; a.up = L.up.p; a.down = L.down.p;
+  a.gate_slab = L.gate_slab; a.up_slab = L.up_slab; a.down_slab = L.down_slab;
+  a.gate_type = L.gate.type; a.up_type = L.up.type; a.down_type = L.down.type;
+  a.E = E; a.FF = FF; a.NE = NE; a.K = K; a.norm_topk = L.norm_topk;
+  a.resid_scale = L.resid_scale; a.eps = L.rms_eps;
+  a.logits = reinterpret_cast<float *>(sc + s.off_logits);
+  a.hg = reinterpret_cast<float *>(sc + s.off_hg);
+  a.sel_out = sel_out; a.wt_out = wt_out;
+  a.sync = reinterpret_cast<uint32_t *>(c->small + 64);
+  a.err = c->small;
+  a.mode = mode;
+  if (mode == 2)
+    for (int k = 0; k < K; ++k) {
+      a.sel_in[k] = sel_in[k];
+      a.wt_in[k] = wt_in[k];
+      a.slab[k] = slabs ? slabs[k] : nullptr;
+    }
+  if (!c->attrs_set) {
+    CUDA_OR(cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "kernel attribute");
+    c->attrs_set = true;
+  }
+  int occ = 0;
+  CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_decode_kernel, DECODE_THREADS, a.smem_bytes), "occupancy");
+  if (occ < 1) { errf(err, errlen, "the one-token kernel does not fit on an SM (%u bytes of shared memory)", a.smem_bytes); return 1; }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(c->sms);
+  cfg.blockDim = dim3(DECODE_THREADS);
+  cfg.dynamicSmemBytes = a.smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUDA_OR(cudaLaunchKernelEx(&cfg, moe_decode_kernel, a), "launching the one-token kernel");
+  return 0;
 }
 
 }  // namespace clb
@@ -348,49 +310,17 @@ int clb200_layer_release(clb200_ctx *c, int layer) {
   return 0;
 }
 
+
 // Launches the MoE block for T tokens on device data.
 static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,
                      size_t errlen) {
   const clb200_moe_layer &L = dl.d;
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
-  DecodeArgs a{};
-  const bool one = T == 1 && plan_decode(c, L, a) == 0;
-  const Scratch s = plan_scratch(T, E, FF, NE, K, !one);
+  DecodeArgs probe{};
+  if (T == 1 && plan_decode(c, L, probe) == 0) return launch_one(c, L, x, 0, nullptr, nullptr, nullptr, sel, wt, st, err, errlen);
+  const Scratch s = plan_scratch(T, E, FF, NE, K, true);
   if (ensure_scratch(c, s.total, err, errlen)) return 1;
   uint8_t *sc = c->scratch;
-  if (one) {
-    a.x_in = x; a.x_out = x;
-    a.norm = L.ffn_norm_f; a.router = L.router_f;
-    a.gate = L.gate.p; a.up = L.up.p; a.down = L.down.p;
-    a.gate_slab = L.gate_slab; a.up_slab = L.up_slab; a.down_slab = L.down_slab;
-    a.gate_type = L.gate.type; a.up_type = L.up.type; a.down_type = L.down.type;
-    a.E = E; a.FF = FF; a.NE = NE; a.K = K; a.norm_topk = L.norm_topk;
-    a.resid_scale = L.resid_scale; a.eps = L.rms_eps;
-    a.logits = reinterpret_cast<float *>(sc + s.off_logits);
-    a.hg = reinterpret_cast<float *>(sc + s.off_hg);
-    a.sel_out = sel; a.wt_out = wt;
-    a.sync = reinterpret_cast<uint32_t *>(c->small + 64);
-    a.err = c->small;
-    if (!c->attrs_set) {
-      CUDA_OR(cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "kernel attribute");
-      c->attrs_set = true;
-    }
-    int occ = 0;
-    CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_decode_kernel, DECODE_THREADS, a.smem_bytes), "occupancy");
-    if (occ < 1) { errf(err, errlen, "the one-token kernel does not fit on an SM (%u bytes of shared memory)", a.smem_bytes); return 1; }
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(c->sms);
-    cfg.blockDim = dim3(DECODE_THREADS);
-    cfg.dynamicSmemBytes = a.smem_bytes;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    CUDA_OR(cudaLaunchKernelEx(&cfg, moe_decode_kernel, a), "launching the one-token kernel");
-    return 0;
-  }
   BatchArgs b{};
   b.x_in = x; b.x_out = x;
   b.norm = L.ffn_norm_f; b.router = L.router_f;

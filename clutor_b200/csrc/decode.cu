@@ -1,5 +1,9 @@
 // The one-token MoE block as one persistent kernel: the reference's c/src/forward.c:949-1033 on one B200.
 //
+// Modes (DecodeArgs::mode): 0 runs every phase below; 1 stops after phase 3 (routing only, for a host that must see the
+// choice before it places the experts -- the expert store); 2 skips the router (phases 2-3) and takes the routing and the
+// experts' addresses from its arguments (the experts as the store placed them in HBM).
+//
 // One CTA per SM (G CTAs, all co-resident), 512 threads. Every CTA streams the same share of every chosen expert, and all
 // of a CTA's share of the chosen experts sits in shared memory at once. Data that crosses CTAs goes through global memory
 // behind two counters (bounded waits):
@@ -57,7 +61,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   const int j0 = static_cast<int>((static_cast<long long>(FF) * c) / G), j1 = static_cast<int>((static_cast<long long>(FF) * (c + 1)) / G);
   const int i0 = static_cast<int>((static_cast<long long>(E) * c) / G), i1 = static_cast<int>((static_cast<long long>(E) * (c + 1)) / G);
   const int ngu = j1 - j0, nd = i1 - i0;
-  const int nre = c < NE ? (NE - c + G - 1) / G : 0;   // experts this CTA scores: c, c+G, ...
+  const int nre = (a.mode != 2 && c < NE) ? (NE - c + G - 1) / G : 0;   // experts this CTA scores: c, c+G, ...
   const uint32_t grb = a.grb, drb = a.drb, gseg = a.gseg;
 
   // ---- 0: barriers, router rows and norm weights (weights only, so before the dependency wait) ------------------------------
@@ -128,9 +132,19 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   }
 
   // ---- 3: softmax, top-k, renormalisation (c/src/forward.c:954-984), in every CTA --------------------------------------------
-  if (tid == 0 && !wait_counter(&a.sync[0], static_cast<uint32_t>(NE))) { set_error(a.err, ERR_WAIT_ROUTER); s_flag[0] = 1; }
+  if (a.mode == 2) {   // the routing is given
+    if (tid < K) {
+      const int e = a.sel_in[tid];
+      if (e < 0 || e >= NE) { set_error(a.err, ERR_BAD_EXPERT); s_flag[0] = 1; }
+      s_sel[tid] = e;
+      s_wt[tid] = a.wt_in[tid];
+    }
+  } else if (tid == 0 && !wait_counter(&a.sync[0], static_cast<uint32_t>(NE))) {
+    set_error(a.err, ERR_WAIT_ROUTER);
+    s_flag[0] = 1;
+  }
   __syncthreads();
-  if (!s_flag[0]) {
+  if (a.mode != 2 && !s_flag[0]) {
     const float l = tid < NE ? __ldcg(a.logits + tid) : -INFINITY;
     float mx = l;
 #pragma unroll
@@ -187,6 +201,12 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
 
   // ---- 4: bulk copies of this CTA's share of each chosen expert, one lane per expert ------------------------------------------
   auto seg_src = [&](int k, int q) -> const uint8_t * {
+    if (a.mode == 2 && a.slab[k]) {   // the store's copy: gate, up and down slabs back to back
+      const uint8_t *b = a.slab[k];
+      return q == 0 ? b + static_cast<size_t>(j0) * grb
+           : q == 1 ? b + a.gate_slab + static_cast<size_t>(j0) * grb
+                    : b + a.gate_slab + a.up_slab + static_cast<size_t>(i0) * drb;
+    }
     const size_t e = static_cast<size_t>(s_sel[k]);
     return q == 0 ? a.gate + e * a.gate_slab + static_cast<size_t>(j0) * grb
          : q == 1 ? a.up + e * a.up_slab + static_cast<size_t>(j0) * grb
@@ -196,7 +216,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     return static_cast<uint32_t>(k) * a.slot_bytes + (q == 0 ? 0u : q == 1 ? gseg : 2 * gseg) +
            static_cast<uint32_t>(reinterpret_cast<uintptr_t>(seg_src(k, q)) & 15u);
   };
-  const bool go = !s_flag[0];
+  const bool go = !s_flag[0] && a.mode != 1;
   if (go && lane == 0 && warp < K) {   // one warp per expert: their copy requests go out in parallel
     const int k = warp;
     uint8_t *slot = slots + static_cast<size_t>(k) * a.slot_bytes;
@@ -260,7 +280,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   // ---- 6: every expert's hg, down rows, combine in rank order, residual ------------------------------------------------------
   if (go && tid == 0 && !wait_counter(&a.sync[1], static_cast<uint32_t>(G))) { set_error(a.err, ERR_WAIT_EXPERT); s_flag[0] = 1; }
   __syncthreads();
-  if (!s_flag[0]) {
+  if (go && !s_flag[0]) {
     q8k_quantize_global(a.hg, K * FF / 256, hq_qs, hq_d, hq_bs, warp, NW, lane, true);
     for (int k = 0; k < K; ++k)   // every copy has landed (a CTA with no gate/up rows has not waited yet)
       if (!mbar_wait_bounded(&bars[k], 0)) set_error(a.err, ERR_WAIT_COPY);

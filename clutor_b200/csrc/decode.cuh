@@ -24,6 +24,13 @@ struct DecodeArgs {
   float *wt_out;                 // [K] or null
   uint32_t *sync;                // [0] logits written, [1] CTAs whose hg rows are written, [2] CTAs finished; zero on entry
   int *err;                      // first device error
+  // 0: the whole block; 1: routing only (sel_out / wt_out; x unchanged); 2: the experts of a given routing (sel_in / wt_in,
+  // renormalised already), each expert's weights at slab[k] (gate, up and down slabs back to back) or, where slab[k] is
+  // null, in gate / up / down
+  int mode;
+  int sel_in[DECODE_MAX_K];
+  float wt_in[DECODE_MAX_K];
+  const uint8_t *slab[DECODE_MAX_K];
   // shared-memory plan (host-computed): one slot per chosen expert holds this CTA's gate, up and down rows of it
   int rgu_max, rd_max;
   uint32_t grb, drb, gseg, dseg, slot_bytes;

@@ -1,0 +1,380 @@
+// The HBM expert store: the reference's disk-backed expert store (c/src/xs.c, cl_xs_*) turned into a B200 memory
+// hierarchy. Every layer's experts live in pinned host memory (gate, up and down slabs of one expert back to back, the
+// layout of a reference slot); a budget of HBM slots holds the experts the cache policy (cache.cpp, the reference's
+// cache.c) keeps, plus staging slots for prefetches and a few bypass buffers. A miss or a prefetch is one cudaMemcpyAsync
+// on the store's own copy stream (a copy engine), ordered after the last kernel that read the slot's previous expert
+// (an event recorded at release), so copies overlap the compute stream. cl_xs_wait's blocking wait becomes a host wait
+// on the fill's event, timed, so the store reports how much of the copy time the prefetches hid.
+//
+// One decode step of a layer through the store (clb200_moe_ffn_stored) follows the reference's forward pass
+// (c/src/forward.c:888-1033 with an expert store): stage the next layer's experts as the previous token chose them, route
+// (the one-token kernel in routing mode; its choice comes back to the host), request the chosen experts resident ones first
+// (c/src/forward.c:992-997), wait, run the experts from their slots (the one-token kernel in given-routing mode), release.
+#include <chrono>
+#include <cstring>
+#include <vector>
+
+#include "ctx.cuh"
+
+using namespace clb;
+
+namespace {
+enum { S_EMPTY = 0, S_LOADING = 1, S_READY = 2 };
+uint64_t now_ns() {
+  return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now().time_since_epoch()).count());
+}
+}  // namespace
+
+struct clb200_store {
+  clb200_ctx *ctx = nullptr;
+  int n_layer = 0, NE = 0, K = 0;
+  clb200_moe_layer shape{};              // widths, types and slabs every layer shares
+  uint64_t expert_bytes = 0, stride = 0;
+  std::vector<clb200_moe_layer> layer;   // per layer: norm and router on the device; expert pointers unused
+  std::vector<uint8_t> loaded;
+  uint8_t *host = nullptr;               // pinned: [layer][expert] at `stride`
+  uint8_t *arena = nullptr;              // HBM: total + nbypass slots at `stride`
+  uint8_t *dense = nullptr;              // HBM: every layer's norm and router
+  clb200_cache *cache = nullptr;
+  uint32_t total = 0, nbypass = 0, bypass_next = 0;
+  std::vector<int> state;
+  std::vector<cudaEvent_t> started, filled, used;
+  std::vector<uint8_t> used_set, timed;
+  std::vector<int> staged;               // staging slots whose fill is in flight: unpinned when it lands
+  cudaStream_t copy = nullptr;
+  int *sel_host = nullptr;               // pinned, device-visible: the routing kernel's choice
+  float *wt_host = nullptr;
+  std::vector<int> prev_sel;             // [n_layer * K] the previous token's choice, -1 before the first
+  int prefetch = 1;
+  clb200_store_stats st{};
+  uint64_t dev_bytes = 0;                // device memory counted in the context's total
+  bool logging = false;
+  std::vector<int64_t> oplog;
+};
+
+namespace {
+
+void log_op(clb200_store *s, int op, int64_t a, int64_t r) {
+  if (s->logging) {
+    s->oplog.push_back(op);
+    s->oplog.push_back(a);
+    s->oplog.push_back(r);
+  }
+}
+
+void count_copy(clb200_store *s, int buf) {   // the fill of `buf` has completed: add its duration to copy_ns once
+  if (s->timed[buf]) return;
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, s->started[buf], s->filled[buf]) == cudaSuccess) s->st.copy_ns += static_cast<uint64_t>(ms * 1e6);
+  s->timed[buf] = 1;
+}
+
+// Staging fills that have landed: ready, and unpinned (the reference's I/O worker does this when a prefetch read ends).
+void poll(clb200_store *s) {
+  size_t keep = 0;
+  for (size_t i = 0; i < s->staged.size(); ++i) {
+    const int b = s->staged[i];
+    if (cudaEventQuery(s->filled[b]) == cudaSuccess) {
+      s->state[b] = S_READY;
+      count_copy(s, b);
+      clb200_cache_unpin(s->cache, b);
+      log_op(s, 3, b, 0);
+    } else {
+      s->staged[keep++] = b;
+    }
+  }
+  s->staged.resize(keep);
+  cudaGetLastError();   // a "not ready" answer is not an error
+}
+
+void fill(clb200_store *s, int buf, int layer, int expert, bool prefetch) {
+  if (s->used_set[buf]) cudaStreamWaitEvent(s->copy, s->used[buf], 0);   // the previous expert's readers are done
+  cudaEventRecord(s->started[buf], s->copy);
+  cudaMemcpyAsync(s->arena + static_cast<size_t>(buf) * s->stride,
+                  s->host + (static_cast<size_t>(layer) * s->NE + expert) * s->stride, s->expert_bytes, cudaMemcpyHostToDevice, s->copy);
+  cudaEventRecord(s->filled[buf], s->copy);
+  s->state[buf] = S_LOADING;
+  s->timed[buf] = 0;
+  (prefetch ? s->st.prefetch_bytes : s->st.demand_bytes) += s->expert_bytes;
+}
+
+bool valid_expert(const clb200_store *s, int layer, int expert) {
+  return s && layer >= 0 && layer < s->n_layer && expert >= 0 && expert < s->NE && s->loaded[layer];
+}
+
+}  // namespace
+
+extern "C" {
+
+clb200_store *clb200_store_open(clb200_ctx *c, const clb200_moe_layer *shape, int n_layer, uint64_t cache_bytes, int stage_slots,
+                                int policy, char *err, size_t errlen) {
+  if (!c || !shape || n_layer < 1) { errf(err, errlen, "no context, shape or layers"); return nullptr; }
+  if (validate(shape, err, errlen)) return nullptr;
+  DecodeArgs probe{};
+  if (plan_decode_shape(c->sms, c->max_smem, *shape, probe)) { errf(err, errlen, "the store serves the one-token kernel: K-quant experts only"); return nullptr; }
+  cudaSetDevice(c->device);
+  auto *s = new clb200_store();
+  s->ctx = c;
+  s->n_layer = n_layer;
+  s->NE = shape->n_expert;
+  s->K = shape->n_used;
+  s->shape = *shape;
+  s->expert_bytes = shape->gate_slab + shape->up_slab + shape->down_slab;
+  s->stride = al(s->expert_bytes, 256);
+  s->layer.assign(n_layer, *shape);
+  s->loaded.assign(n_layer, 0);
+  s->prev_sel.assign(static_cast<size_t>(n_layer) * s->K, -1);
+  uint32_t slots = static_cast<uint32_t>(cache_bytes / s->stride);
+  if (slots < static_cast<uint32_t>(s->K)) slots = static_cast<uint32_t>(s->K);   // a layer's experts must fit at once (xs.c:103)
+  s->cache = clb200_cache_new(slots, stage_slots < 0 ? 0u : static_cast<uint32_t>(stage_slots),
+                              static_cast<uint32_t>(n_layer) * static_cast<uint32_t>(s->NE), policy, 0);
+  if (!s->cache) { errf(err, errlen, "bad cache settings"); delete s; return nullptr; }
+  s->total = clb200_cache_total_slots(s->cache);
+  s->nbypass = static_cast<uint32_t>(s->K) + 2;
+  const uint32_t nbuf = s->total + s->nbypass;
+  const size_t host_bytes = static_cast<size_t>(n_layer) * s->NE * s->stride;
+  const size_t dense_per = al(static_cast<size_t>(shape->n_embd) * 4) + al(static_cast<size_t>(s->NE) * shape->n_embd * 4);
+  bool ok = cudaHostAlloc(reinterpret_cast<void **>(&s->host), host_bytes, cudaHostAllocDefault) == cudaSuccess &&
+            cudaMalloc(&s->arena, static_cast<size_t>(nbuf) * s->stride) == cudaSuccess &&
+            cudaMalloc(&s->dense, dense_per * n_layer) == cudaSuccess &&
+            cudaHostAlloc(reinterpret_cast<void **>(&s->sel_host), 64 * sizeof(int), cudaHostAllocMapped) == cudaSuccess &&
+            cudaHostAlloc(reinterpret_cast<void **>(&s->wt_host), 64 * sizeof(float), cudaHostAllocMapped) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&s->copy, cudaStreamNonBlocking) == cudaSuccess;
+  s->state.assign(nbuf, S_EMPTY);
+  s->used_set.assign(nbuf, 0);
+  s->timed.assign(nbuf, 1);
+  s->started.assign(nbuf, nullptr);
+  s->filled.assign(nbuf, nullptr);
+  s->used.assign(nbuf, nullptr);
+  for (uint32_t i = 0; ok && i < nbuf; ++i)
+    ok = cudaEventCreate(&s->started[i]) == cudaSuccess && cudaEventCreate(&s->filled[i]) == cudaSuccess &&
+         cudaEventCreateWithFlags(&s->used[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    errf(err, errlen, "cannot allocate the store: %zu bytes pinned host memory and %zu bytes on device %d", host_bytes,
+         static_cast<size_t>(nbuf) * s->stride + dense_per * n_layer, c->device);
+    clb200_store_close(s);
+    return nullptr;
+  }
+  for (int l = 0; l < n_layer; ++l) {
+    s->layer[l].ffn_norm_f = reinterpret_cast<const float *>(s->dense + dense_per * l);
+    s->layer[l].router_f = reinterpret_cast<const float *>(s->dense + dense_per * l + al(static_cast<size_t>(shape->n_embd) * 4));
+    s->layer[l].gate.p = s->layer[l].up.p = s->layer[l].down.p = nullptr;
+  }
+  s->dev_bytes = static_cast<uint64_t>(nbuf) * s->stride + dense_per * n_layer;
+  c->bytes += s->dev_bytes;
+  return s;
+}
+
+void clb200_store_close(clb200_store *s) {
+  if (!s) return;
+  cudaSetDevice(s->ctx->device);
+  if (s->copy) cudaStreamSynchronize(s->copy);
+  cudaStreamSynchronize(s->ctx->stream);
+  for (auto e : s->started) if (e) cudaEventDestroy(e);
+  for (auto e : s->filled) if (e) cudaEventDestroy(e);
+  for (auto e : s->used) if (e) cudaEventDestroy(e);
+  if (s->copy) cudaStreamDestroy(s->copy);
+  if (s->arena) cudaFree(s->arena);
+  s->ctx->bytes -= s->dev_bytes;
+  if (s->dense) cudaFree(s->dense);
+  if (s->host) cudaFreeHost(s->host);
+  if (s->sel_host) cudaFreeHost(s->sel_host);
+  if (s->wt_host) cudaFreeHost(s->wt_host);
+  if (s->cache) clb200_cache_free(s->cache);
+  delete s;
+}
+
+int clb200_store_load_layer(clb200_store *s, int layer, const clb200_moe_layer *L, char *err, size_t errlen) {
+  if (!s || layer < 0 || layer >= s->n_layer) { errf(err, errlen, "no layer %d in the store", layer); return 1; }
+  if (validate(L, err, errlen)) return 1;
+  const clb200_moe_layer &h = s->shape;
+  if (L->n_embd != h.n_embd || L->n_ff_exp != h.n_ff_exp || L->n_expert != h.n_expert || L->n_used != h.n_used ||
+      L->gate.type != h.gate.type || L->down.type != h.down.type) {
+    errf(err, errlen, "layer %d does not have the store's shape", layer);
+    return 1;
+  }
+  cudaSetDevice(s->ctx->device);
+  clb200_moe_layer &d = s->layer[layer];
+  const size_t E = h.n_embd, NE = h.n_expert;
+  d.norm_topk = L->norm_topk;
+  d.resid_scale = L->resid_scale;
+  d.rms_eps = L->rms_eps;
+  CUDA_OR(cudaMemcpy(const_cast<float *>(d.ffn_norm_f), L->ffn_norm_f, E * 4, cudaMemcpyDefault), "copying the norm weights");
+  CUDA_OR(cudaMemcpy(const_cast<float *>(d.router_f), L->router_f, NE * E * 4, cudaMemcpyDefault), "copying the router");
+  // expert e of the layer at host + (layer * NE + e) * stride: gate, up, down slabs back to back (the reference's slot layout)
+  uint8_t *dst = s->host + static_cast<size_t>(layer) * NE * s->stride;
+  CUDA_OR(cudaMemcpy2D(dst, s->stride, L->gate.p, h.gate_slab, h.gate_slab, NE, cudaMemcpyDefault), "copying gate experts");
+  CUDA_OR(cudaMemcpy2D(dst + h.gate_slab, s->stride, L->up.p, h.up_slab, h.up_slab, NE, cudaMemcpyDefault), "copying up experts");
+  CUDA_OR(cudaMemcpy2D(dst + h.gate_slab + h.up_slab, s->stride, L->down.p, h.down_slab, h.down_slab, NE, cudaMemcpyDefault),
+          "copying down experts");
+  s->loaded[layer] = 1;
+  return 0;
+}
+
+uint32_t clb200_store_cache_slots(const clb200_store *s) { return s ? s->total : 0; }
+uint64_t clb200_store_slot_bytes(const clb200_store *s) { return s ? s->stride : 0; }
+void clb200_store_set_prefetch(clb200_store *s, int on) { if (s) s->prefetch = on; }
+
+int clb200_store_request(clb200_store *s, int layer, int expert) {
+  if (!valid_expert(s, layer, expert)) return -1;
+  poll(s);
+  const uint32_t key = static_cast<uint32_t>(layer * s->NE + expert);
+  int slot = -1;
+  const int r = clb200_cache_access(s->cache, key, &slot);
+  log_op(s, 1, key, r >= 0 ? r * 65536 + slot : -1);
+  ++s->st.accesses;
+  if (r == 1) {
+    ++s->st.hits;
+  } else if (r == 2) {
+    ++s->st.stage_hits;
+    ++s->st.hits;
+    if (s->state[slot] != S_READY) ++s->st.prefetch_late;
+  } else {
+    ++s->st.misses;
+    if (r == -1) {   // nothing evictable: a bypass buffer outside the cache (xs.c:160-163)
+      slot = static_cast<int>(s->total + (s->bypass_next++ % s->nbypass));
+      ++s->st.bypass;
+    }
+    fill(s, slot, layer, expert, false);
+  }
+  return slot;
+}
+
+const void *clb200_store_wait(clb200_store *s, int h) {
+  if (!s || h < 0 || h >= static_cast<int>(s->total + s->nbypass)) return nullptr;
+  if (s->state[h] != S_READY) {
+    const uint64_t t0 = now_ns();
+    if (cudaEventSynchronize(s->filled[h]) != cudaSuccess) return nullptr;
+    s->st.wait_ns += now_ns() - t0;
+    s->state[h] = S_READY;
+  }
+  count_copy(s, h);
+  return s->arena + static_cast<size_t>(h) * s->stride;
+}
+
+void clb200_store_release(clb200_store *s, int h, void *stream) {
+  if (!s || h < 0 || h >= static_cast<int>(s->total + s->nbypass)) return;
+  cudaEventRecord(s->used[h], stream ? static_cast<cudaStream_t>(stream) : s->ctx->stream);   // the next fill waits for it
+  s->used_set[h] = 1;
+  if (static_cast<uint32_t>(h) < s->total) {
+    clb200_cache_unpin(s->cache, h);
+    log_op(s, 3, h, 0);
+  } else {
+    s->state[h] = S_EMPTY;
+  }
+}
+
+int clb200_store_resident(clb200_store *s, int layer, int expert) {
+  if (!valid_expert(s, layer, expert)) return 0;
+  poll(s);
+  const int slot = clb200_cache_find(s->cache, static_cast<uint32_t>(layer * s->NE + expert));
+  return slot >= 0 && s->state[slot] == S_READY;
+}
+
+void clb200_store_prefetch(clb200_store *s, int layer, int expert) {
+  if (!valid_expert(s, layer, expert)) return;
+  poll(s);
+  const uint32_t key = static_cast<uint32_t>(layer * s->NE + expert);
+  const int slot = clb200_cache_stage(s->cache, key);
+  log_op(s, 2, key, slot);
+  if (slot < 0) return;
+  fill(s, slot, layer, expert, true);
+  s->staged.push_back(slot);
+  ++s->st.prefetch_issued;
+}
+
+clb200_store_stats clb200_store_get_stats(const clb200_store *s) {
+  clb200_store_stats r{};
+  if (!s) return r;
+  r = s->st;
+  const clb200_cache_stats cs = clb200_cache_get_stats(s->cache);
+  r.evictions = cs.evictions;
+  r.admit_rejects = cs.admit_rejects;
+  r.prefetch_wasted = cs.stage_wasted;
+  return r;
+}
+
+void clb200_store_reset_stats(clb200_store *s) {
+  if (!s) return;
+  s->st = clb200_store_stats{};
+}
+
+void clb200_store_log(clb200_store *s, int on) {
+  if (!s) return;
+  s->logging = on != 0;
+  s->oplog.clear();
+}
+
+int64_t clb200_store_read_log(const clb200_store *s, int64_t *dst, int64_t cap) {
+  if (!s) return 0;
+  const int64_t n = static_cast<int64_t>(s->oplog.size());
+  if (dst) std::memcpy(dst, s->oplog.data(), static_cast<size_t>(n < cap ? n : cap) * sizeof(int64_t));
+  return n;
+}
+
+// Experts of `layer` for one token with the routing sel / wt [n_used] given (host arrays): requests (resident ones first),
+// stages next_pred [n_used] of layer + 1 when given, waits, runs the experts from their slots and releases them.
+static int experts_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, const int *sel, const float *wt, const int *next_pred,
+                          cudaStream_t st, char *err, size_t errlen) {
+  const int K = s->K;
+  int h[DECODE_MAX_K];
+  const uint8_t *ptr[DECODE_MAX_K];
+  for (int k = 0; k < K; ++k)
+    if (sel[k] < 0 || sel[k] >= s->NE) { errf(err, errlen, "expert %d out of range", sel[k]); return 1; }
+  // ask for what is already in HBM first, so a miss cannot evict an expert this layer is about to use
+  int here[DECODE_MAX_K];
+  for (int k = 0; k < K; ++k) here[k] = clb200_store_resident(s, layer, sel[k]);
+  for (int pass = 0; pass < 2; ++pass)
+    for (int k = 0; k < K; ++k)
+      if ((pass == 0) == (here[k] != 0)) h[k] = clb200_store_request(s, layer, sel[k]);
+  if (next_pred && layer + 1 < s->n_layer && s->loaded[layer + 1])
+    for (int k = 0; k < K; ++k) clb200_store_prefetch(s, layer + 1, next_pred[k]);
+  for (int k = 0; k < K; ++k) {
+    ptr[k] = static_cast<const uint8_t *>(clb200_store_wait(s, h[k]));
+    if (!ptr[k]) { errf(err, errlen, "filling an expert slot failed: %s", cudaGetErrorString(cudaGetLastError())); return 1; }
+  }
+  const int rc = launch_one(c, s->layer[layer], x, 2, sel, wt, ptr, nullptr, nullptr, st, err, errlen);
+  for (int k = 0; k < K; ++k) clb200_store_release(s, h[k], st);
+  return rc;
+}
+
+int clb200_moe_experts_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, const int *sel, const float *wt,
+                              const int *next_pred, void *stream, char *err, size_t errlen) {
+  if (!c || !s || s->ctx != c) { errf(err, errlen, "no context or store, or a store of another context"); return 1; }
+  if (layer < 0 || layer >= s->n_layer || !s->loaded[layer]) { errf(err, errlen, "layer %d is not loaded", layer); return 1; }
+  if (!x || !sel || !wt) { errf(err, errlen, "no activations or routing"); return 1; }
+  cudaSetDevice(c->device);
+  return experts_stored(c, s, layer, x, sel, wt, next_pred, stream ? static_cast<cudaStream_t>(stream) : c->stream, err, errlen);
+}
+
+int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, int *sel_out, float *wt_out, void *stream,
+                          char *err, size_t errlen) {
+  if (!c || !s || s->ctx != c) { errf(err, errlen, "no context or store, or a store of another context"); return 1; }
+  if (layer < 0 || layer >= s->n_layer || !s->loaded[layer]) { errf(err, errlen, "layer %d is not loaded", layer); return 1; }
+  if (!x) { errf(err, errlen, "no activations"); return 1; }
+  cudaSetDevice(c->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+  const int K = s->K;
+  // the next layer's experts as the previous token chose them, read while this layer routes and computes
+  if (s->prefetch && layer + 1 < s->n_layer && s->loaded[layer + 1])
+    for (int k = 0; k < K; ++k) {
+      const int e = s->prev_sel[static_cast<size_t>(layer + 1) * K + k];
+      if (e >= 0) clb200_store_prefetch(s, layer + 1, e);
+    }
+  if (launch_one(c, s->layer[layer], x, 1, nullptr, nullptr, nullptr, s->sel_host, s->wt_host, st, err, errlen)) return 1;
+  CUDA_OR(cudaStreamSynchronize(st), "routing");
+  int sel[DECODE_MAX_K];
+  float wt[DECODE_MAX_K];
+  for (int k = 0; k < K; ++k) {
+    sel[k] = s->sel_host[k];
+    wt[k] = s->wt_host[k];
+    s->prev_sel[static_cast<size_t>(layer) * K + k] = sel[k];
+  }
+  if (experts_stored(c, s, layer, x, sel, wt, nullptr, st, err, errlen)) return 1;
+  if (sel_out) std::memcpy(sel_out, sel, K * sizeof(int));
+  if (wt_out) std::memcpy(wt_out, wt, K * sizeof(float));
+  return 0;
+}
+
+}  // extern "C"

@@ -126,6 +126,52 @@ uint32_t clb200_cache_freq(const clb200_cache *c, uint32_t key);           /* cl
 clb200_cache_stats clb200_cache_get_stats(const clb200_cache *c);          /* cl_cache_get_stats */
 uint32_t clb200_cache_count(const clb200_cache *c);                        /* cl_cache_count: experts cached (not staged) */
 
+/* ---- the HBM expert store ------------------------------------------------------------------------------------------------- */
+/* The reference's expert store (c/src/xs.h:11-38, c/src/xs.c) with HBM slots in place of RAM slots and pinned host memory in
+ * place of the model file: every layer's experts are held in pinned host memory; the cache policy above keeps a budget of
+ * them in HBM slots (plus staging slots for prefetches); a miss or prefetch is one host-to-device copy on the store's copy
+ * stream, overlapping the compute stream. One-token (decode) use, K-quant experts. */
+typedef struct {   /* cl_xs_stats (xs.h:14-17); copy_ns = time the copy engine spent filling slots (cl_xs_stats.read_ns) */
+  uint64_t accesses, hits, stage_hits, misses, bypass, prefetch_issued, prefetch_late, prefetch_wasted, admit_rejects, evictions;
+  uint64_t demand_bytes, prefetch_bytes, copy_ns, wait_ns;
+} clb200_store_stats;
+typedef struct clb200_store clb200_store;
+/* cl_xs_open (xs.c:89-120): n_layer layers shaped like `shape`, HBM slots for cache_bytes (at least n_used slots), stage_slots
+ * prefetch slots, policy CLB200_LRU / WTINYLFU / ADAPTIVE. Allocates n_layer * n_expert expert slots of pinned host memory.
+ * NULL with err set on failure. */
+clb200_store *clb200_store_open(clb200_ctx *c, const clb200_moe_layer *shape, int n_layer, uint64_t cache_bytes, int stage_slots,
+                                int policy, char *err, size_t errlen);
+void clb200_store_close(clb200_store *s);                                         /* cl_xs_close */
+/* Copies layer `layer`'s tensors into the store (L's pointers may be host or device memory; L must have the store's shape):
+ * norm and router to HBM, the experts to pinned host memory. A layer is served once loaded. */
+int clb200_store_load_layer(clb200_store *s, int layer, const clb200_moe_layer *L, char *err, size_t errlen);
+uint32_t clb200_store_cache_slots(const clb200_store *s);                         /* cl_xs_cache_slots */
+uint64_t clb200_store_slot_bytes(const clb200_store *s);                          /* cl_xs_slot_bytes */
+int clb200_store_request(clb200_store *s, int layer, int expert);                 /* cl_xs_request: handle (>= 0) or -1 */
+const void *clb200_store_wait(clb200_store *s, int handle);                       /* cl_xs_wait: the expert's DEVICE address */
+void clb200_store_release(clb200_store *s, int handle, void *stream);             /* cl_xs_release, once `stream`'s work so far is done */
+int clb200_store_resident(clb200_store *s, int layer, int expert);                /* cl_xs_resident */
+void clb200_store_prefetch(clb200_store *s, int layer, int expert);               /* cl_xs_prefetch */
+clb200_store_stats clb200_store_get_stats(const clb200_store *s);                 /* cl_xs_get_stats */
+void clb200_store_reset_stats(clb200_store *s);                                   /* cl_xs_reset_stats */
+/* 1: clb200_moe_ffn_stored stages the next layer's experts as the previous token chose them (the reference's --prefetch, on
+ * by default); 0: no prefetch. */
+void clb200_store_set_prefetch(clb200_store *s, int on);
+/* Test hooks: record every cache operation the store makes (triples: 1 access key -> code*65536+slot or -1, 2 stage key ->
+ * slot, 3 unpin slot), and read the record (returns its length; copies at most cap values). */
+void clb200_store_log(clb200_store *s, int on);
+int64_t clb200_store_read_log(const clb200_store *s, int64_t *dst, int64_t cap);
+/* The one-token MoE block of `layer` with its experts served by the store (c/src/forward.c:888-1033 with an expert store):
+ * x [n_embd] DEVICE, updated in place; sel_out / wt_out HOST arrays [n_used] or NULL. Returns after the experts are
+ * enqueued on `stream` (NULL: the context's stream); the routing is read back to the host on the way. */
+int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, int *sel_out, float *wt_out, void *stream,
+                          char *err, size_t errlen);
+/* The experts of `layer` for a routing decided elsewhere (HOST sel / wt [n_used], wt renormalised), served by the store;
+ * next_pred [n_used] (or NULL) are staged for layer + 1 between the requests and the waits, as the reference's stress
+ * harness does with its predictor (c/src/stream.c:311-324). */
+int clb200_moe_experts_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, const int *sel, const float *wt,
+                              const int *next_pred, void *stream, char *err, size_t errlen);
+
 /* ---- the plugin seam: a cl_backend for cl_matvec_batch ------------------------------------------------------------------- */
 /* Layout-compatible copies of the reference's cl_q8k, cl_xq and cl_mv (c/src/quant.h:22-34) and cl_backend (backend.h:9-13). */
 typedef struct { float d; int8_t qs[256]; int16_t bsums[16]; } clb200_q8k;
