@@ -34,6 +34,9 @@ WORKLOADS = {
                    desc="Qwen3-30B-A3B MoE layer, decode T=1, Q4_K experts"),
     "prefill64": dict(T=64, gate="q8_0", down="q8_0", E=2048, FF=768, NE=128, K=8, layers=8,
                       desc="Qwen3-30B-A3B MoE layer, T=64, Q8_0 experts"),
+    "ep235b": dict(T=2048, gate="q4_k", down="q4_k", E=4096, FF=1536, NE=128, K=8, layers=2,
+                   desc="Qwen3-235B-A22B MoE layer, prefill 2048 tokens per GPU, Q4_K experts, expert-parallel over the GPUs "
+                        "(NCCL all-to-all dispatch and combine)"),
     "cache": dict(T=1, gate="q4_k", down="q4_k", E=2048, FF=768, NE=128, K=8, layers=48, budget=0.4, locality=1.78,
                   desc="expert-cache stress: 48 Qwen3-30B-A3B MoE layers (Q4_K), HBM cache of 40% of expert bytes, the rest "
                        "in pinned host memory, Zipf(1.1)-skewed routing with topics drifting every 16 tokens"),
@@ -287,6 +290,98 @@ def run_cache(a, wl: dict) -> None:
     ctx.close()
 
 
+def run_ep(a, wl: dict) -> None:
+    """Expert-parallel MoE layers of the Qwen3-235B-A22B shape: each of the N ranks (one per GPU) holds the router and
+    128/N experts of every layer and routes its own 2048 tokens; a step is those tokens through `layers` layers (one
+    all-to-all each way per layer). Weak scaling: value = all ranks' layer-tokens / the slowest rank's time."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import clutor_b200 as cb
+    from clutor_b200 import ep, synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    T, NL, K, E, FF, NE = wl["T"], wl["layers"], wl["K"], wl["E"], wl["FF"], wl["NE"]
+    n_local = NE // world
+    ctx = cb.Context(local)
+    comps, keep = [], []
+    for i in range(NL):
+        L = synth.device_layer(E=E, FF=FF, NE=NE, K=K, gate_type=synth.TYPE_NAMES[wl["gate"]],
+                               down_type=synth.TYPE_NAMES[wl["down"]], seed=i + 1, router_scale=0.02)
+        sh = ep.shard_layer(L, rank, world)
+        g, u, d = sh.gate.clone(), sh.up.clone(), sh.down.clone()
+        mk = lambda ne, router: synth.DeviceLayer(E=E, FF=FF, NE=ne, K=K, gate_type=L.gate_type, up_type=L.up_type,
+                                                  down_type=L.down_type, ffn_norm=L.ffn_norm, router=router, gate=g, up=u, down=d)
+        route_layer = mk(NE, L.router)              # norm + router; routing never reads the expert pointers
+        shard_layer = mk(n_local, sh.router.clone())
+        keep.append((route_layer, shard_layer))
+        comps.append(ep.GpuCompute(ctx, ctx.bind(route_layer), ctx.bind(shard_layer), E, K))
+        del L, sh
+        torch.cuda.empty_cache()
+    x0 = torch.from_numpy(synth.activations(T, E, seed=11 + rank)).cuda()
+    x = x0.clone()
+    phases: dict = {}
+
+    def step(timed=None):
+        x.copy_(x0)
+        for c in comps:
+            ep.moe_layer(x, c, n_local, 1.0, timings=timed)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx.status()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        ev0.record()
+        for _ in range(a.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    ctx.status()
+    step(phases)   # one more step with the phase events (not timed above)
+    torch.cuda.synchronize()
+    ph = {k: round(sum(ev[0].elapsed_time(ev[1]) for ev in v) / NL, 3) for k, v in phases.items() if k != "rows"}
+    rows = phases.get("rows", [0])
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = NL * T * a.steps * world / (ms / 1000.0)
+    flop = T * K * 3 * 2 * E * FF                      # per layer per rank (weak scaling: each rank's assignments)
+    achieved = flop * NL * a.steps / (ms / 1000.0) / 1e12
+    pk, pk_kind = peaks()
+    if rank == 0:
+        line = {"metric": "MoE-layer tokens/s (Qwen3-235B-A22B layer, prefill 2048 tokens/GPU, Q4_K, expert-parallel)",
+                "value": round(value, 3), "unit": "layer-tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8 dot (Q8_K x Q4_K), fp32 accumulate", "data": "synthetic (seeded random GGUF blocks)",
+                "config": {"workload": wl["desc"], "tokens_per_gpu": T, "layers_per_step": NL, "hidden": E, "experts": NE,
+                           "experts_per_gpu": n_local, "top_k": K, "ff": FF, "parallelism": f"ep{world}",
+                           "l2": f"inputs larger than L2: {NL} layers, {NE * E * FF * 3 * 144 / 256 / 1e9 * NL / world:.2f} GB of experts per GPU"},
+                "phases_ms_per_layer_rank0": ph, "rows_received_rank0": int(sum(rows) / max(len(rows), 1)),
+                "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk.get("bf16_tflops"), "unit": "TFLOP/s",
+                             "frac": round(achieved / pk.get("bf16_tflops", 1.0), 4), "traffic": None, "peak_kind": pk_kind,
+                             "note": "expert products on CUDA cores (int8 dot); bf16 tensor peak as the ridge"},
+                "cpu_baseline": None, "e2e": None, "gpu_launches": NL * a.steps * 9, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    del comps
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -310,6 +405,9 @@ def main() -> None:
         return
     if a.workload == "cache":
         run_cache(a, wl)
+        return
+    if a.workload == "ep235b":
+        run_ep(a, wl)
         return
 
     import numpy as np

@@ -170,6 +170,17 @@ def _ptr(a) -> int:
     return a.data_ptr()   # torch tensor
 
 
+def _stream(stream) -> int:
+    """The cudaStream_t for a call on torch tensors: the given torch stream, else torch's current stream (so the call is
+    ordered with the torch work that made its inputs and will read its outputs)."""
+    import torch
+    st = (stream if stream is not None else torch.cuda.current_stream()).cuda_stream
+    return st or CUDA_STREAM_LEGACY   # torch's default stream is the legacy stream; 0 would mean the context's own stream
+
+
+CUDA_STREAM_LEGACY = 1   # cudaStreamLegacy
+
+
 def layer_struct(layer) -> MoELayer:
     """A clb200_moe_layer over a synth.HostLayer (numpy, host pointers) or synth.DeviceLayer (torch, device pointers)."""
     s = MoELayer()
@@ -250,7 +261,7 @@ class Context:
     def moe_ffn_dev(self, handle: int, x, sel=None, wt=None, stream=None) -> None:
         """The device entry point (clb200_moe_ffn_dev) on torch CUDA tensors; asynchronous on `stream` (a torch stream)."""
         T = x.shape[0]
-        st = 0 if stream is None else stream.cuda_stream
+        st = _stream(stream)
         self._check(lib().clb200_moe_ffn_dev(self.handle, handle, _ptr(x), T, _ptr(sel), _ptr(wt), C.c_void_p(st), self._err, 512))
 
     def status(self) -> None:
@@ -385,8 +396,8 @@ class Store:
         """One token of `layer` through the store; x a device tensor [n_embd], updated in place. Returns (sel, wt)."""
         sel = np.zeros(self.K, np.int32)
         wt = np.zeros(self.K, np.float32)
-        if self.L.clb200_moe_ffn_stored(self.ctx.handle, self.h, layer, _ptr(x), sel.ctypes.data, wt.ctypes.data, stream,
-                                        self._err, 512):
+        if self.L.clb200_moe_ffn_stored(self.ctx.handle, self.h, layer, _ptr(x), sel.ctypes.data, wt.ctypes.data,
+                                        stream if isinstance(stream, int) else _stream(stream), self._err, 512):
             raise ClutorError(self._err.value.decode())
         return sel, wt
 
@@ -396,5 +407,6 @@ class Store:
         wt = np.ascontiguousarray(wt, np.float32)
         nxt = None if next_pred is None else np.ascontiguousarray(next_pred, np.int32)
         if self.L.clb200_moe_experts_stored(self.ctx.handle, self.h, layer, _ptr(x), sel.ctypes.data, wt.ctypes.data,
-                                            None if nxt is None else nxt.ctypes.data, stream, self._err, 512):
+                                            None if nxt is None else nxt.ctypes.data,
+                                            stream if isinstance(stream, int) else _stream(stream), self._err, 512):
             raise ClutorError(self._err.value.decode())

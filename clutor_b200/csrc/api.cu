@@ -311,15 +311,9 @@ int clb200_layer_release(clb200_ctx *c, int layer) {
 }
 
 
-// Launches the MoE block for T tokens on device data.
-static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,
-                     size_t errlen) {
-  const clb200_moe_layer &L = dl.d;
+// The batched kernels' arguments for layer L (device pointers), T tokens at x, the context's scratch laid out as s.
+static BatchArgs batch_args(clb200_ctx *c, const clb200_moe_layer &L, float *x, int T, const Scratch &s, int *sel, float *wt) {
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
-  DecodeArgs probe{};
-  if (T == 1 && plan_decode(c, L, probe) == 0) return launch_one(c, L, x, 0, nullptr, nullptr, nullptr, sel, wt, st, err, errlen);
-  const Scratch s = plan_scratch(T, E, FF, NE, K, true);
-  if (ensure_scratch(c, s.total, err, errlen)) return 1;
   uint8_t *sc = c->scratch;
   BatchArgs b{};
   b.x_in = x; b.x_out = x;
@@ -360,6 +354,19 @@ static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *se
     b.xdh = reinterpret_cast<__half *>(sc + s.off_xdh);
     b.xdl = reinterpret_cast<__half *>(sc + s.off_xdl);
   }
+  return b;
+}
+
+// Launches the MoE block for T tokens on device data.
+static int run_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,
+                     size_t errlen) {
+  const clb200_moe_layer &L = dl.d;
+  const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+  DecodeArgs probe{};
+  if (T == 1 && plan_decode(c, L, probe) == 0) return launch_one(c, L, x, 0, nullptr, nullptr, nullptr, sel, wt, st, err, errlen);
+  const Scratch s = plan_scratch(T, E, FF, NE, K, true);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  BatchArgs b = batch_args(c, L, x, T, s, sel, wt);
   const int rc = launch_batched(b, st);
   if (rc) { errf(err, errlen, "launching the batched kernels: %s", cudaGetErrorString(static_cast<cudaError_t>(rc))); return 1; }
   return 0;
@@ -372,6 +379,54 @@ int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, floa
   if (!x) { errf(err, errlen, "no activations"); return 1; }
   cudaSetDevice(c->device);
   return run_block(c, c->layers[layer], x, T, sel, wt, stream ? static_cast<cudaStream_t>(stream) : c->stream, err, errlen);
+}
+
+static const DevLayer *ep_layer(clb200_ctx *c, int layer, int T, char *err, size_t errlen) {
+  if (!c) { errf(err, errlen, "no context"); return nullptr; }
+  if (layer < 0 || layer >= static_cast<int>(c->layers.size()) || !c->layers[layer].live) { errf(err, errlen, "no layer %d", layer); return nullptr; }
+  if (T < 1 || T > 32768) { errf(err, errlen, "%d tokens: an expert-parallel call takes 1 to 32768", T); return nullptr; }
+  const clb200_moe_layer &L = c->layers[layer].d;
+  if (L.gate.type == T_Q8_0) { errf(err, errlen, "expert-parallel calls take K-quant gate/up experts (Q4_K, Q6_K)"); return nullptr; }
+  cudaSetDevice(c->device);
+  return &c->layers[layer];
+}
+
+int clb200_ep_route(clb200_ctx *c, int layer, float *x, int T, int *sel, float *wt, int8_t *xq_qs, float *xq_d, int16_t *xq_bs,
+                    void *stream, char *err, size_t errlen) {
+  const DevLayer *dl = ep_layer(c, layer, T, err, errlen);
+  if (!dl) return 1;
+  if (!x || !sel || !wt || !xq_qs || !xq_d || !xq_bs) { errf(err, errlen, "a buffer is missing"); return 1; }
+  const clb200_moe_layer &L = dl->d;
+  const Scratch s = plan_scratch(T, L.n_embd, L.n_ff_exp, L.n_expert, L.n_used, true);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  BatchArgs b = batch_args(c, L, x, T, s, nullptr, nullptr);
+  b.sel = sel; b.wt = wt;
+  b.xq_qs = xq_qs; b.xq_d = xq_d; b.xq_bs = xq_bs;
+  const int rc = launch_route(b, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+  if (rc) { errf(err, errlen, "launching the router: %s", cudaGetErrorString(static_cast<cudaError_t>(rc))); return 1; }
+  return 0;
+}
+
+int clb200_ep_experts(clb200_ctx *c, int layer, int T, const int8_t *xq_qs, const float *xq_d, const int16_t *xq_bs, const int *sel,
+                      const float *wt, float *partial, void *stream, char *err, size_t errlen) {
+  const DevLayer *dl = ep_layer(c, layer, T, err, errlen);
+  if (!dl) return 1;
+  if (!partial || !sel || !wt || !xq_qs || !xq_d || !xq_bs) { errf(err, errlen, "a buffer is missing"); return 1; }
+  const clb200_moe_layer &L = dl->d;
+  const Scratch s = plan_scratch(T, L.n_embd, L.n_ff_exp, L.n_expert, L.n_used, true);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  BatchArgs b = batch_args(c, L, partial, T, s, nullptr, nullptr);
+  b.x_in = nullptr;
+  b.x_out = partial;
+  b.ep = 1;
+  b.sel = const_cast<int *>(sel);
+  b.wt = const_cast<float *>(wt);
+  b.xq_qs = const_cast<int8_t *>(xq_qs);
+  b.xq_d = const_cast<float *>(xq_d);
+  b.xq_bs = const_cast<int16_t *>(xq_bs);
+  const int rc = launch_experts(b, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+  if (rc) { errf(err, errlen, "launching the expert kernels: %s", cudaGetErrorString(static_cast<cudaError_t>(rc))); return 1; }
+  return 0;
 }
 
 int clb200_status(clb200_ctx *c, char *err, size_t errlen) {

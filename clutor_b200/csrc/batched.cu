@@ -142,7 +142,10 @@ __global__ void __launch_bounds__(1024) dispatch_kernel(const BatchArgs a) {
   __syncthreads();
   for (int s = tid; s < T * K; s += blockDim.x) {
     const int t = s / K, e = a.sel[s];
-    if (e < 0 || e >= NE) { set_error(a.err, ERR_BAD_EXPERT); continue; }
+    if (e < 0 || e >= NE) {
+      if (!(a.ep && e < 0)) set_error(a.err, ERR_BAD_EXPERT);   // -1: held by another GPU (expert-parallel)
+      continue;
+    }
     atomicOr(&bits[e * nw + t / 32], 1u << (t & 31));
     atomicMin(&first[e], s);
   }
@@ -310,38 +313,54 @@ __global__ void __launch_bounds__(BT) combine_kernel(const BatchArgs a) {
   const int t = blockIdx.x, K = a.K, E = a.E;
   __shared__ int s_pos[DECODE_MAX_K];
   __shared__ float s_w[DECODE_MAX_K];
+  __shared__ int s_n;
   if (threadIdx.x == 0) {
-    int order[DECODE_MAX_K], key[DECODE_MAX_K];
+    int order[DECODE_MAX_K], key[DECODE_MAX_K], n = 0;
     for (int k = 0; k < K; ++k) {   // insertion sort of the token's slots by their expert's first appearance
-      const int kk = a.first[a.sel[static_cast<size_t>(t) * K + k]];
-      int j = k;
+      const int e = a.sel[static_cast<size_t>(t) * K + k];
+      if (e < 0 && a.ep) continue;  // held by another GPU
+      const int kk = (e >= 0 && e < a.NE) ? a.first[e] : 0x7fffffff;
+      int j = n;
       while (j > 0 && key[j - 1] > kk) { key[j] = key[j - 1]; order[j] = order[j - 1]; --j; }
       key[j] = kk; order[j] = k;
+      ++n;
     }
-    for (int j = 0; j < K; ++j) {
+    for (int j = 0; j < n; ++j) {
       s_pos[j] = a.slot_pos[static_cast<size_t>(t) * K + order[j]];
       s_w[j] = a.wt[static_cast<size_t>(t) * K + order[j]];
     }
+    s_n = n;
   }
   __syncthreads();
-  for (int j = 0; j < K; ++j)
+  const int n = s_n;
+  for (int j = 0; j < n; ++j)
     if (s_pos[j] < 0 || s_pos[j] >= a.T * K) { if (threadIdx.x == 0) set_error(a.err, ERR_BAD_EXPERT); return; }
   for (int i = threadIdx.x; i < E; i += BT) {
     float m = 0.f;
-    for (int j = 0; j < K; ++j) m = __fadd_rn(m, __fmul_rn(s_w[j], a.hd[static_cast<size_t>(s_pos[j]) * E + i]));
+    for (int j = 0; j < n; ++j) m = __fadd_rn(m, __fmul_rn(s_w[j], a.hd[static_cast<size_t>(s_pos[j]) * E + i]));
     const size_t xi = static_cast<size_t>(t) * E + i;
-    a.x_out[xi] = __fadd_rn(a.x_in[xi], __fmul_rn(a.resid_scale, m));
+    a.x_out[xi] = a.ep ? m : __fadd_rn(a.x_in[xi], __fmul_rn(a.resid_scale, m));
   }
 }
 
 static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
+int launch_route(const BatchArgs &a, void *stream_) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  const size_t route_smem = a.E * 4 + BNW * 8;
+  route_kernel<<<dim3(a.T, (a.NE + ROUTE_EXPERTS - 1) / ROUTE_EXPERTS), BT, route_smem, st>>>(a);
+  topk_kernel<<<a.T, 32, 0, st>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
 int launch_batched(const BatchArgs &a, void *stream_) {
+  const int rc = launch_route(a, stream_);
+  return rc ? rc : launch_experts(a, stream_);
+}
+
+int launch_experts(const BatchArgs &a, void *stream_) {
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
   const int T = a.T, E = a.E, FF = a.FF, NE = a.NE, K = a.K;
-  const size_t route_smem = E * 4 + BNW * 8;
-  route_kernel<<<dim3(T, (NE + ROUTE_EXPERTS - 1) / ROUTE_EXPERTS), BT, route_smem, st>>>(a);
-  topk_kernel<<<T, 32, 0, st>>>(a);
   const int nw = (T + 31) / 32;
   const size_t disp_smem = static_cast<size_t>(NE) * nw * 4 + (3 * NE + 1) * 4;
   dispatch_kernel<<<1, 1024, disp_smem, st>>>(a);

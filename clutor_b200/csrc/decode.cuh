@@ -76,10 +76,16 @@ struct BatchArgs {
   int *sel_out;         // [T * K] or null
   float *wt_out;        // [T * K] or null
   int *err;
+  // expert-parallel expert side: sel entries may be -1 (an expert another GPU holds); the dispatch leaves them out and
+  // the combine writes the weighted sum of the present experts alone (x_out = moe, no residual, x_in unused)
+  int ep;
 };
 
 // Launches the batched path on `stream`; returns a CUDA error code.
 int launch_batched(const BatchArgs &a, void *stream);
+// Its two halves: rmsnorm + Q8_K + router + top-k (sel / wt), and everything from the dispatch on (given sel / wt / xq).
+int launch_route(const BatchArgs &a, void *stream);
+int launch_experts(const BatchArgs &a, void *stream);
 // The Q8_0 expert products on tcgen05 (grouped_tc.cu): gate/up (writes hgh/hgl) or down (writes hd).
 int launch_q80_tc(const BatchArgs &a, void *stream, bool gateup);
 // Whether the tensor-core Q8_0 path takes these experts (16-byte aligned weights, E and FF multiples of 256).

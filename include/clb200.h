@@ -92,6 +92,21 @@ int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, floa
  * several host threads or streams) race; serialise them. 0 on success, 1 with err set otherwise. */
 int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x, int *sel_out, float *wt_out, void *stream, char *err,
                                   size_t errlen);
+/* ---- expert parallelism: the two halves of the batched block, around an exchange ------------------------------------------
+ * No single counterpart in the reference (it runs on one machine); together with an all-to-all they are its batched block
+ * (c/src/forward.c:1132-1210) with the experts spread over GPUs. Asynchronous on `stream`; K-quant gate/up experts; T up to
+ * 32768. */
+/* Source side of a bound layer: rmsnorm, Q8_K of xn (xq_qs [T x n_embd] int8, xq_d [T x n_embd/256] fp32, xq_bs
+ * [T x n_embd/16] int16: the reference's cl_q8k rows as planes, c/src/quant.h:22), router, softmax, top-k, renormalisation
+ * (sel / wt [T x n_used]) -- c/src/forward.c:1135-1155. All DEVICE pointers. */
+int clb200_ep_route(clb200_ctx *c, int layer, float *x, int T, int *sel, float *wt, int8_t *xq_qs, float *xq_d, int16_t *xq_bs,
+                    void *stream, char *err, size_t errlen);
+/* Expert side: `layer` is a bound layer holding only this GPU's experts (n_expert = the local count); for T received rows
+ * (Q8_K planes as above) with sel [T x n_used] local expert ids, -1 where the expert is another GPU's, and wt the routing
+ * weights, partial [T x n_embd] = sum over the present experts, in order of first appearance, of wt * expert(row)
+ * (c/src/forward.c:1160-1208 without the residual add). All DEVICE pointers. */
+int clb200_ep_experts(clb200_ctx *c, int layer, int T, const int8_t *xq_qs, const float *xq_d, const int16_t *xq_bs, const int *sel,
+                      const float *wt, float *partial, void *stream, char *err, size_t errlen);
 /* Waits for the context's work and reports a device-side error recorded since the last call (0: none). */
 int clb200_status(clb200_ctx *c, char *err, size_t errlen);
 /* Bytes of device memory the context holds for layers and scratch. */
