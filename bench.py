@@ -373,7 +373,7 @@ def run_ep(a, wl: dict) -> None:
                 "phases_ms_per_layer_rank0": ph, "rows_received_rank0": int(sum(rows) / max(len(rows), 1)),
                 "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk.get("bf16_tflops"), "unit": "TFLOP/s",
                              "frac": round(achieved / pk.get("bf16_tflops", 1.0), 4), "traffic": None, "peak_kind": pk_kind,
-                             "note": "expert products on CUDA cores (int8 dot); bf16 tensor peak as the ridge"},
+                             "note": "expert products as tcgen05 grouped GEMMs (fp16 hi/lo planes, 4 MMAs per algorithmic product); FLOPs counted algorithmically; bf16 dense peak"},
                 "cpu_baseline": None, "e2e": None, "gpu_launches": NL * a.steps * 9, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     del comps

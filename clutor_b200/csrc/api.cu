@@ -20,7 +20,7 @@ struct Scratch {
   size_t off_logits, off_hg, off_x, off_sel, off_wt, total;
   // batched
   size_t off_xn, off_xq_qs, off_xq_d, off_xq_bs, off_bsel, off_bwt, off_counts, off_offsets, off_first, off_pos_token,
-      off_pos_wt, off_slot_pos, off_bhg, off_hq_qs, off_hq_d, off_hq_bs, off_hd, off_xh, off_xl, off_hgh, off_hgl, off_xdh, off_xdl;
+      off_pos_wt, off_slot_pos, off_bhg, off_hq_qs, off_hq_d, off_hq_bs, off_hd, off_xh, off_xl, off_hgh, off_hgl, off_xdh, off_xdl, off_rs;
 };
 
 // `batched`: the batched kernels will run (T > 1, or one token of a shape the one-token kernel does not take).
@@ -58,6 +58,7 @@ static Scratch plan_scratch(int T, int E, int FF, int NE, int K, bool batched) {
     s.off_hgl = take(TK * FF * 2);
     s.off_xdh = take(TK * E * 2);
     s.off_xdl = take(TK * E * 2);
+    s.off_rs = take(TK * 4);
   }
   s.total = o;
   return s;
@@ -345,14 +346,23 @@ static BatchArgs batch_args(clb200_ctx *c, const clb200_moe_layer &L, float *x, 
   b.hd = reinterpret_cast<float *>(sc + s.off_hd);
   b.sel_out = sel; b.wt_out = wt;
   b.err = c->small;
-  if (L.gate.type == T_Q8_0 && L.up.type == T_Q8_0 && L.down.type == T_Q8_0 &&
-      q80_tc_supported(L.gate.p, L.up.p, L.down.p, E, FF)) {   // tensor-core expert products
-    b.xh = reinterpret_cast<__half *>(sc + s.off_xh);
-    b.xl = reinterpret_cast<__half *>(sc + s.off_xl);
-    b.hgh = reinterpret_cast<__half *>(sc + s.off_hgh);
-    b.hgl = reinterpret_cast<__half *>(sc + s.off_hgl);
+  // tensor-core expert products where the types allow (Q8_0 down needs the hg planes a tensor-core gate/up writes)
+  const bool tcg = L.gate.type == L.up.type && tc_type_supported(L.gate.type, L.gate.p, E, FF) && tc_type_supported(L.up.type, L.up.p, E, FF);
+  const bool tcd = tc_type_supported(L.down.type, L.down.p, E, FF) && (L.down.type != T_Q8_0 || (tcg && L.gate.type == T_Q8_0));
+  if (tcg || tcd) b.rs = reinterpret_cast<float *>(sc + s.off_rs);
+  if (tcg) {
+    b.tc_gu = 1;
+    if (L.gate.type == T_Q8_0) {   // xn's fp16 planes (the route kernel writes them)
+      b.xh = reinterpret_cast<__half *>(sc + s.off_xh);
+      b.xl = reinterpret_cast<__half *>(sc + s.off_xl);
+    }
     b.xdh = reinterpret_cast<__half *>(sc + s.off_xdh);
     b.xdl = reinterpret_cast<__half *>(sc + s.off_xdl);
+  }
+  if (tcd) {
+    b.tc_dn = 1;
+    b.hgh = reinterpret_cast<__half *>(sc + s.off_hgh);
+    b.hgl = reinterpret_cast<__half *>(sc + s.off_hgl);
   }
   return b;
 }

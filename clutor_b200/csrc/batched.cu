@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(BT) gateup_kernel(const BatchArgs a) {
 
 __global__ void hq_kernel(const BatchArgs a, int npos) {
   const int pos = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, FF = a.FF;
-  if (pos >= npos) return;
+  if (pos >= npos || pos >= a.offsets[a.NE]) return;   // only dispatched slots hold an hg row
   q8k_quantize_block(a.hg + static_cast<size_t>(pos) * FF, FF, a.hq_qs + static_cast<size_t>(pos) * FF,
                      a.hq_d + static_cast<size_t>(pos) * (FF / 256), a.hq_bs + static_cast<size_t>(pos) * (FF / 16), warp,
                      blockDim.x >> 5, lane);
@@ -374,13 +374,17 @@ int launch_experts(const BatchArgs &a, void *stream_) {
     cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attrs[dev] = true;
   }
-  if (a.xh) {   // Q8_0 experts: grouped GEMMs on the tensor cores
-    int rc = launch_q80_tc(a, stream_, true);
-    if (rc == 0) rc = launch_q80_tc(a, stream_, false);
+  if (a.tc_gu) {   // grouped GEMMs on the tensor cores
+    const int rc = launch_tc(a, stream_, true);
     if (rc) return rc;
   } else {
     gateup_kernel<<<dim3(NE, (FF + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, gu_smem, st>>>(a);
-    if (a.down_type != T_Q8_0) hq_kernel<<<T * K, 32 * (FF / 256), 0, st>>>(a, T * K);
+  }
+  if (a.down_type != T_Q8_0) hq_kernel<<<T * K, 32 * (FF / 256), 0, st>>>(a, T * K);   // Q8_K of hg (K-quant down)
+  if (a.tc_dn) {
+    const int rc = launch_tc(a, stream_, false);
+    if (rc) return rc;
+  } else {
     const size_t dn_smem = 16 + FF * 4 + align16(ROWS_PER_CTA * a.drb + 32) + 16;
     down_kernel<<<dim3(NE, (E + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, dn_smem, st>>>(a);
   }

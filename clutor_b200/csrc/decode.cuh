@@ -79,6 +79,11 @@ struct BatchArgs {
   // expert-parallel expert side: sel entries may be -1 (an expert another GPU holds); the dispatch leaves them out and
   // the combine writes the weighted sum of the present experts alone (x_out = moe, no residual, x_in unused)
   int ep;
+  // tensor-core expert products (grouped_tc.cu) for gate/up and for down
+  int tc_gu, tc_dn;
+  // [T * K] the power of two each dispatch row of the current K-quant activation planes was divided by (so that the fp16
+  // planes hold any Q8_K row without overflow); the tensor-core epilogue multiplies it back. Null: no scaling (Q8_0).
+  float *rs;
 };
 
 // Launches the batched path on `stream`; returns a CUDA error code.
@@ -86,9 +91,10 @@ int launch_batched(const BatchArgs &a, void *stream);
 // Its two halves: rmsnorm + Q8_K + router + top-k (sel / wt), and everything from the dispatch on (given sel / wt / xq).
 int launch_route(const BatchArgs &a, void *stream);
 int launch_experts(const BatchArgs &a, void *stream);
-// The Q8_0 expert products on tcgen05 (grouped_tc.cu): gate/up (writes hgh/hgl) or down (writes hd).
-int launch_q80_tc(const BatchArgs &a, void *stream, bool gateup);
-// Whether the tensor-core Q8_0 path takes these experts (16-byte aligned weights, E and FF multiples of 256).
-bool q80_tc_supported(const void *gate, const void *up, const void *down, int E, int FF);
+// The Q8_0 / Q4_K expert products on tcgen05 (grouped_tc.cu): gate/up (writes hg, and hgh/hgl for Q8_0 down) or down
+// (writes hd).
+int launch_tc(const BatchArgs &a, void *stream, bool gateup);
+// Whether the tensor-core path takes experts of this type at w (Q8_0 or Q4_K, 16-byte aligned, E and FF multiples of 256).
+bool tc_type_supported(uint32_t type, const void *w, int E, int FF);
 
 }  // namespace clb

@@ -1,25 +1,32 @@
-// Batched expert products on the 5th-generation tensor cores (tcgen05, accumulators in TMEM) for Q8_0 experts: the
-// gate/up and down products of the reference's batched block (c/src/forward.c:1197-1201) as grouped GEMMs.
+// Batched expert products on the 5th-generation tensor cores (tcgen05, accumulators in TMEM) as grouped GEMMs: the
+// gate/up and down products of the reference's batched block (c/src/forward.c:1197-1201) for Q8_0 and Q4_K experts.
 //
-// Work: a tile is one expert, 256 weight rows and up to 32 of the expert's tokens (dispatch order). For gate/up the 256
-// rows are gate rows [128m, 128m+128) (matrix 0) and the up rows of the same range (matrix 1); for down, down rows
-// [256m, 256m+128) and [256m+128, 256m+256). A persistent CTA per SM walks the tiles round-robin; its warps specialise:
-//   warp 8  (one lane) TMA-loads the raw Q8_0 weights, 128 rows x 256 elements (272 bytes a row) per box, into a ring
-//           of shared-memory stages, running ahead of the dequantization across tiles;
+// Work: a tile is one expert, 256 weight rows and up to NT of the expert's tokens (dispatch order; NT = 32 for Q8_0, 64
+// for Q4_K). For gate/up the 256 rows are gate rows [128m, 128m+128) (matrix 0) and the up rows of the same range
+// (matrix 1); for down, down rows [256m, 256m+128) and [256m+128, 256m+256). A persistent CTA per SM walks the tiles
+// round-robin; its warps specialise:
+//   warp 8  (one lane) TMA-loads the raw weights, 128 rows x one 256-element chunk (Q8_0: 272 bytes a row, eight blocks;
+//           Q4_K: 144 bytes, one block) per box, into a ring of shared-memory stages, running ahead across tiles;
 //   warps 0-7  one weight row per thread (warps 0-3 matrix 0, 4-7 matrix 1): per 64-element atom they read their row's
-//           bytes from the stage and write the dequantized weights into TMEM as two fp16 planes, hi = fp16(q*d) and
-//           lo = fp16(q*d - hi) (half2 arithmetic: exact products, one rounding each), as the A operand of the MMAs;
-//           at the end of a tile they read the accumulators (epilogue);
-//   warp 10 (one lane) TMA-loads the tokens' activations (fp16 hi/lo planes, 64 x 16 boxes, 128-byte swizzle) as one
-//           operand of 2N rows, [x hi | x lo];
+//           bytes from the stage and write the dequantized weights w into TMEM as two fp16 planes, hi = fp16(w) and
+//           lo = fp16(w - hi), the A operand of the MMAs. Q8_0: w = q*d (half2 arithmetic: exact products, one rounding
+//           each). Q4_K: w = d*sc*q - dmin*mn, the block's whole dequantized weight (c/src/quant.c:54-68) -- so the min
+//           term needs no second product -- formed in fp32 (d*sc*q is exact, one rounding for the difference); at the
+//           end of a tile they read the accumulators (epilogue);
+//   warp 10 (one lane) TMA-loads the tokens' activations as one operand of 2N rows, [x hi | x lo] (fp16, 64 x 16 boxes,
+//           128-byte swizzle): Q8_0 experts take xn itself (the reference's float path, c/src/quant.c:889-902); K-quant
+//           experts take the value of the reference's Q8_K activations, yd * q8 (c/src/quant.h:22), so the product is
+//           the reference's integer dot sum_b yd (d * sumi - dmin * summs) (c/src/quant.c:255-287) up to rounding;
 //   warps 9 and 11 (one lane each; matrix 0 and matrix 1) issue per 16-element K step two MMAs, A hi and A lo (from
-//           TMEM) times [x hi | x lo] (shared memory), into an fp32 TMEM accumulator of 128 rows x 2N, whose two halves the
-//           epilogue adds: (w hi + w lo) * (x hi + x lo) in two instructions. An M=128, K=16 MMA takes about 45 cycles
-//           whatever its N up to 64, so at a few tokens an expert the number of MMAs, not their width, bounds the loop.
-// Products accurate to about 2^-22, so the result stays within 1e-6 relative of the reference's fp32 float path
-// (c/src/quant.c:889-902) instead of the ~4e-4 that single fp16 operands give. Every hand-off is an mbarrier (TMA
-// completion, tcgen05.commit, or warp arrivals); every wait is bounded and a timeout sets the error flag.
-// Epilogue: gate/up -> SwiGLU -> hg as fp16 hi/lo planes (the down product's activations); down -> hd fp32.
+//           TMEM) times [x hi | x lo] (shared memory), into an fp32 TMEM accumulator of 128 rows x 2N, whose two halves
+//           the epilogue adds: (w hi + w lo) * (x hi + x lo) in two instructions. An M=128, K=16 MMA takes about 45
+//           cycles whatever its N up to 64, so at a few tokens an expert the number of MMAs, not their width, counts.
+// Products accurate to about 2^-22, so the result stays within about 1e-6 relative of the reference's. Every hand-off is
+// an mbarrier (TMA completion, tcgen05.commit, or warp arrivals); every wait is bounded and a timeout sets the error flag.
+// Epilogue: gate/up -> SwiGLU -> hg (fp32, and for Q8_0 down also as fp16 hi/lo planes, its activations); down -> hd.
+//
+// Dispatch positions at or past the number of dispatched slots (offsets[NE]; fewer than T * K on an expert-parallel
+// expert side, where other GPUs hold some of the experts) hold no data: no kernel here reads them for a result.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -36,22 +43,29 @@ namespace {
 constexpr int DQ_WARPS = 8;                         // dequantizing warps, one weight row per thread
 constexpr int W_RAW = DQ_WARPS, W_MMA0 = DQ_WARPS + 1, W_ACT = DQ_WARPS + 2, W_MMA1 = DQ_WARPS + 3;
 constexpr int TC_THREADS = 32 * (DQ_WARPS + 4);
-constexpr int TC_NT = 32;                           // tokens per accumulator tile
-constexpr int RAW_STAGES = 5;
-constexpr uint32_t CHUNK_BYTES = 272;               // 256 elements of Q8_0 (8 blocks of 34 bytes)
-constexpr uint32_t RAW_STAGE = 128 * CHUNK_BYTES;   // one matrix's 128 rows of one chunk
-constexpr int B_STAGES = 4;
-constexpr uint32_t B_TILE = TC_NT * 128;            // up to 32 tokens x 64 fp16, 128-byte swizzle
-constexpr uint32_t B_STAGE = 2 * B_TILE;            // hi rows [0, NT), lo rows [NT, 2 NT)
-constexpr int A_STAGES = 3;
-// TMEM columns: accumulators (2 NT columns: x hi products, then x lo products) of matrix 0 at [0, 64) and matrix 1 at
-// [64, 128); A stage j at 128 + 128 j as [matrix 0 hi: 32][matrix 0 lo: 32][matrix 1 hi: 32][matrix 1 lo: 32] (64 fp16
-// of K per row, two per column).
-constexpr uint32_t ACC_COLS = 4 * TC_NT, A_COLS = 128, TMEM_COLS = 512;
-static_assert(ACC_COLS + A_STAGES * A_COLS <= TMEM_COLS, "TMEM budget");
-constexpr int N_BARS = 2 * RAW_STAGES + 2 * B_STAGES + 2 * A_STAGES + 3;
-constexpr uint32_t SMEM_BYTES = RAW_STAGES * RAW_STAGE + B_STAGES * B_STAGE + 8 * N_BARS + 16 + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+constexpr int B_STAGES = 4;                         // activation stages, one 64-column atom each
+constexpr uint32_t A_COLS = 128, TMEM_COLS = 512;   // A stage: [m0 hi 32][m0 lo 32][m1 hi 32][m1 lo 32] TMEM columns
+
+// Per weight type: bytes of a row's 256-element chunk, tokens per tile, ring depths. TMEM columns: the accumulators
+// (2 NT each: x hi products, then x lo products) of matrix 0 at [0, 2NT) and matrix 1 at [2NT, 4NT); A stage j at
+// 4NT + 128 j (64 fp16 of K per row, two per column).
+template <uint32_t WT>
+struct TcShape {
+  static constexpr uint32_t CHUNK = WT == T_Q8_0 ? 272u : 144u;
+  static constexpr int NT = WT == T_Q8_0 ? 32 : 64;
+  static constexpr int RAW_STAGES = WT == T_Q8_0 ? 5 : 6;
+  static constexpr uint32_t RAW_STAGE = 128 * CHUNK;
+  static constexpr uint32_t B_TILE = NT * 128;      // NT tokens x 64 fp16, 128-byte swizzle
+  static constexpr uint32_t B_STAGE = 2 * B_TILE;   // hi rows [0, NT), lo rows [NT, 2 NT)
+  static constexpr uint32_t ACC_COLS = 4 * NT;
+  static constexpr int A_STAGES = static_cast<int>((TMEM_COLS - ACC_COLS) / A_COLS);
+  static constexpr int WORDS = CHUNK / 4;
+  static constexpr int N_BARS = 2 * RAW_STAGES + 2 * B_STAGES + 2 * A_STAGES + 3;
+  static constexpr uint32_t SMEM = RAW_STAGES * RAW_STAGE + B_STAGES * B_STAGE + 8 * N_BARS + 16 + 1024;
+  static_assert(A_STAGES >= 2, "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(CHUNK % 16 == 0, "TMA boxes are 16-byte multiples");
+};
 
 // 2-D tiled TMA load of one box into shared memory, completing on `bar`.
 CLB_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -60,8 +74,9 @@ CLB_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64
                : "memory");
 }
 
-// The 4 bytes at byte offset `off` of a 272-byte chunk held as 68 little-endian words (off is a constant once unrolled).
-CLB_DEV uint32_t word_at(const uint32_t (&w)[68], int off) {
+// The 4 bytes at byte offset `off` of a chunk held as little-endian words (off is a constant once unrolled).
+template <int NW>
+CLB_DEV uint32_t word_at(const uint32_t (&w)[NW], int off) {
   const int i = off >> 2, sh = off & 3;
   return sh == 0 ? w[i] : __byte_perm(w[i], w[i + 1], 0x3210 + 0x1111 * sh);
 }
@@ -92,34 +107,72 @@ CLB_DEV void dequant4(uint32_t qw, __half2 d2, uint32_t &hi01, uint32_t &hi23, u
 }
 
 // Q8_0 block b (0..7) of a 272-byte chunk as 16 columns of packed fp16 pairs, hi and lo planes.
-CLB_DEV void dequant_block(const uint32_t (&w)[68], int b, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+CLB_DEV void dequant_q80(const uint32_t (&w)[68], int b, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
   const uint32_t dw = w[(34 * b) >> 2];   // the block's fp16 scale at byte 34b (2-byte aligned)
   const __half2 d2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(((34 * b) & 3) == 0 ? (dw & 0xffffu) : (dw >> 16))));
 #pragma unroll
   for (int i = 0; i < 8; ++i) dequant4(word_at(w, 34 * b + 2 + 4 * i), d2, hi[2 * i], hi[2 * i + 1], lo[2 * i], lo[2 * i + 1]);
 }
 
+CLB_DEV float half_bits(uint32_t bits16) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16))); }
+CLB_DEV uint32_t pack_half2(float a, float b) { return as_u32(__floats2half2_rn(a, b)); }   // a in the low half
+
+// Sub-block j (0..7) of a Q4_K block (144 bytes as 36 words: d, dmin, 12 scale bytes, 128 quant bytes) as 16 columns of
+// packed fp16 pairs of w = d*sc*q - dmin*mn, hi and lo planes. Sub-block j's values are the low (j even) or high (j odd)
+// nibbles of quant bytes 32*(j/2) .. +31; scales and mins unpack as in c/src/quant.c:36-40.
+CLB_DEV void dequant_q4k(const uint32_t (&w)[36], int j, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+  const float d = half_bits(w[0] & 0xffffu), dmin = half_bits(w[0] >> 16);
+  auto sbyte = [&](int i) -> int { return static_cast<int>((w[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu); };   // scale byte i
+  int sc, mn;
+  if (j < 4) {
+    sc = sbyte(j) & 63;
+    mn = sbyte(j + 4) & 63;
+  } else {
+    sc = (sbyte(j + 4) & 15) | ((sbyte(j - 4) >> 6) << 4);
+    mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+  }
+  const float a1 = __fmul_rn(d, static_cast<float>(sc)), a0 = __fmul_rn(dmin, static_cast<float>(mn));   // both exact
+  const int shift = (j & 1) ? 4 : 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {   // quant bytes 4i .. 4i+3 of the group: elements 4i .. 4i+3
+    const uint32_t qw = w[4 + 8 * (j >> 1) + i] >> shift;
+    float v[4], h[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      v[k] = __fmaf_rn(a1, static_cast<float>((qw >> (8 * k)) & 15u), -a0);   // d*sc*q exact; one rounding
+      h[k] = __half2float(__float2half_rn(v[k]));
+    }
+    hi[2 * i] = pack_half2(h[0], h[1]);
+    hi[2 * i + 1] = pack_half2(h[2], h[3]);
+    lo[2 * i] = pack_half2(__fsub_rn(v[0], h[0]), __fsub_rn(v[1], h[1]));
+    lo[2 * i + 1] = pack_half2(__fsub_rn(v[2], h[2]), __fsub_rn(v[3], h[3]));
+  }
+}
+
 // Calls f(e, m, pos0, nt) for this CTA's tiles: expert e, row tile m, tokens at dispatch positions [pos0, pos0 + nt).
 // Every role of the CTA walks the same sequence. Stops (false) as soon as f fails.
-template <class F>
+template <int NT, class F>
 CLB_DEV bool for_each_tile(const BatchArgs &a, int MT, F &&f) {
   const int TK = a.T * a.K;
   for (int w = blockIdx.x; w < a.NE * MT; w += gridDim.x) {
     const int e = w / MT, m = w - e * MT;
     const int n_e = a.counts[e], p0 = a.offsets[e];
     if (n_e <= 0 || p0 < 0 || p0 + n_e > TK) continue;
-    for (int n0 = 0; n0 < n_e; n0 += TC_NT)
-      if (!f(e, m, p0 + n0, min(TC_NT, n_e - n0))) return false;
+    for (int n0 = 0; n0 < n_e; n0 += NT)
+      if (!f(e, m, p0 + n0, min(NT, n_e - n0))) return false;
   }
   return true;
 }
 
 }  // namespace
 
-template <bool GATEUP>
+template <bool GATEUP, uint32_t WT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    q80_group_tc_kernel(const BatchArgs a, const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
-                        const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl) {
+    group_tc_kernel(const BatchArgs a, const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                    const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl) {
+  using S = TcShape<WT>;
+  constexpr int NT = S::NT, RAW_STAGES = S::RAW_STAGES, A_STAGES = S::A_STAGES;
+  constexpr uint32_t RAW_STAGE = S::RAW_STAGE, B_STAGE = S::B_STAGE, ACC_COLS = S::ACC_COLS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *raw = smem, *bst = smem + RAW_STAGES * RAW_STAGE;
@@ -157,14 +210,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == W_RAW) {
     if (lane == 0) {
       uint32_t u = 0;   // half-stages issued: (chunk, matrix) in order
-      ok = for_each_tile(a, MT, [&](int e, int m, int, int) {
+      ok = for_each_tile<NT>(a, MT, [&](int e, int m, int, int) {
         for (int c = 0; c < nchunk; ++c) {
           for (int mA = 0; mA < 2; ++mA, ++u) {
             const uint32_t s = u % RAW_STAGES;
             if (u >= RAW_STAGES && !mbar_wait_bounded(&raw_free[s], (u / RAW_STAGES - 1) & 1)) return false;
             const int y = e * rows_e + (GATEUP ? 128 * m : 256 * m + 128 * mA);
             mbar_arrive_expect_tx(&raw_full[s], RAW_STAGE);
-            tma_load_2d(raw + s * RAW_STAGE, mA ? &tm_w1 : &tm_w0, 34 * c, y, &raw_full[s]);
+            tma_load_2d(raw + s * RAW_STAGE, mA ? &tm_w1 : &tm_w0, static_cast<int>(S::CHUNK / 8) * c, y, &raw_full[s]);
           }
         }
         return true;
@@ -176,17 +229,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == W_ACT) {
     if (lane == 0) {
       uint32_t t = 0;   // atoms issued
-      ok = for_each_tile(a, MT, [&](int, int, int pos0, int nt) {
-        const int NT = (nt + 15) & ~15;
+      ok = for_each_tile<NT>(a, MT, [&](int, int, int pos0, int nt) {
+        const int NTt = (nt + 15) & ~15;
         for (int c = 0; c < nchunk; ++c) {
           for (int at = 0; at < 4; ++at, ++t) {
             const uint32_t s = t % B_STAGES;
             if (t >= B_STAGES && !mbar_wait_bounded(&b_free[s], (t / B_STAGES - 1) & 1)) return false;
-            mbar_arrive_expect_tx(&b_full[s], static_cast<uint32_t>(NT) * 256u);
+            mbar_arrive_expect_tx(&b_full[s], static_cast<uint32_t>(NTt) * 256u);
             uint8_t *bs = bst + s * B_STAGE;
-            for (int j = 0; j < NT / 16; ++j) {
+            for (int j = 0; j < NTt / 16; ++j) {
               tma_load_2d(bs + 2048 * j, &tm_bh, 256 * c + 64 * at, pos0 + 16 * j, &b_full[s]);
-              tma_load_2d(bs + 128 * NT + 2048 * j, &tm_bl, 256 * c + 64 * at, pos0 + 16 * j, &b_full[s]);
+              tma_load_2d(bs + 128 * NTt + 2048 * j, &tm_bl, 256 * c + 64 * at, pos0 + 16 * j, &b_full[s]);
             }
           }
         }
@@ -198,9 +251,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == W_MMA0 || warp == W_MMA1) {
     if (lane == 0) {
       const int mA = warp == W_MMA0 ? 0 : 1;
-      const uint32_t acc = tmem + 2 * TC_NT * mA;
+      const uint32_t acc = tmem + 2 * NT * mA;
       uint32_t t = 0, it = 0;
-      ok = for_each_tile(a, MT, [&](int, int, int, int nt) {
+      ok = for_each_tile<NT>(a, MT, [&](int, int, int, int nt) {
         const uint32_t idesc = tc::idesc_f16_f32(128, 2 * ((nt + 15) & ~15));
         if (it > 0 && !mbar_wait_bounded(acc_free, (it - 1) & 1)) return false;
         tc::fence_after_sync();
@@ -232,14 +285,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int mA = warp >> 2, q = warp & 3, r = 32 * q + lane;
     const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
     uint32_t g = 0, t = 0, it = 0;   // chunks, atoms, tiles consumed
-    ok = for_each_tile(a, MT, [&](int, int m, int pos0, int nt) {
+    ok = for_each_tile<NT>(a, MT, [&](int, int m, int pos0, int nt) {
       for (int c = 0; c < nchunk; ++c, ++g) {
         const uint32_t u = 2 * g + mA, s = u % RAW_STAGES;
         if (!mbar_wait_bounded(&raw_full[s], (u / RAW_STAGES) & 1)) return false;
-        uint32_t w[68];
-        const uint4 *src = reinterpret_cast<const uint4 *>(raw + s * RAW_STAGE + r * CHUNK_BYTES);
+        uint32_t w[S::WORDS];
+        const uint4 *src = reinterpret_cast<const uint4 *>(raw + s * RAW_STAGE + r * S::CHUNK);
 #pragma unroll
-        for (int i = 0; i < 17; ++i) {
+        for (int i = 0; i < S::WORDS / 4; ++i) {
           const uint4 v = src[i];
           w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
         }
@@ -252,9 +305,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc::fence_after_sync();
           const uint32_t col = tmem + lane_base + ACC_COLS + A_COLS * sa + 64 * mA;
 #pragma unroll
-          for (int bb = 0; bb < 2; ++bb) {
+          for (int bb = 0; bb < 2; ++bb) {   // two 32-element pieces: Q8_0 blocks, Q4_K sub-blocks
             uint32_t hi[16], lo[16];
-            dequant_block(w, 2 * at + bb, hi, lo);
+            if constexpr (WT == T_Q8_0) dequant_q80(w, 2 * at + bb, hi, lo);
+            else dequant_q4k(w, 2 * at + bb, hi, lo);
             tc::st_x16(col + 16 * bb, hi);
             tc::st_x16(col + 32 + 16 * bb, lo);
           }
@@ -264,38 +318,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (lane == 0) mbar_arrive(&a_full[sa]);
         }
       }
-      // epilogue: warps of matrix 0 take tokens [0, 16), those of matrix 1 [16, 32); each reads both accumulators, whose
-      // column n holds the x hi products and column NT + n the x lo products of token n
+      // epilogue: warps of matrix 0 take tokens [0, NT/2), those of matrix 1 [NT/2, NT), 16 at a time; each reads both
+      // accumulators, whose column n holds the x hi products and column NTt + n the x lo products of token n
       if (!mbar_wait_bounded(acc_full, it & 1)) return false;
       tc::fence_after_sync();
-      const int c0 = 16 * mA, NT = (nt + 15) & ~15;
-      float v0[16], v1[16];
-      if (c0 < nt) {
-        float l0[16], l1[16];
-        tc::ld_x16(tmem + lane_base + c0, v0);
-        tc::ld_x16(tmem + lane_base + NT + c0, l0);
-        tc::ld_x16(tmem + lane_base + 2 * TC_NT + c0, v1);
-        tc::ld_x16(tmem + lane_base + 2 * TC_NT + NT + c0, l1);
+      const int NTt = (nt + 15) & ~15;
+#pragma unroll 1
+      for (int h = 0; h < NT / 32; ++h) {
+        const int c0 = (NT / 2) * mA + 16 * h;
+        if (c0 >= nt) break;   // warp-uniform
+        float v0[16], v1[16];
+        {
+          float l0[16], l1[16];
+          tc::ld_x16(tmem + lane_base + c0, v0);
+          tc::ld_x16(tmem + lane_base + NTt + c0, l0);
+          tc::ld_x16(tmem + lane_base + 2 * NT + c0, v1);
+          tc::ld_x16(tmem + lane_base + 2 * NT + NTt + c0, l1);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) { v0[j] = __fadd_rn(v0[j], l0[j]); v1[j] = __fadd_rn(v1[j], l1[j]); }
-      }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_free);
-      ++it;
-      if (c0 < nt) {
+          for (int j = 0; j < 16; ++j) { v0[j] = __fadd_rn(v0[j], l0[j]); v1[j] = __fadd_rn(v1[j], l1[j]); }
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = c0 + j;
           if (n >= nt) break;
           const size_t pos = static_cast<size_t>(pos0 + n);
+          if constexpr (WT != T_Q8_0) {   // undo the planes' power-of-two row scale (exact)
+            const float sc = a.rs[pos];
+            v0[j] = __fmul_rn(v0[j], sc);
+            v1[j] = __fmul_rn(v1[j], sc);
+          }
           if (GATEUP) {
-            const float h = silu_mul(v0[j], v1[j]);
-            const __half hh = __float2half_rn(h);
-            const __half hl = __float2half_rn(__fsub_rn(h, __half2float(hh)));
+            const float hv = silu_mul(v0[j], v1[j]);
             const size_t o = pos * a.FF + 128 * m + r;
-            a.hgh[o] = hh;
-            a.hgl[o] = hl;
+            a.hg[o] = hv;
+            if (a.tc_dn && a.down_type == T_Q8_0) {   // the Q8_0 down product's activations
+              const __half hh = __float2half_rn(hv);
+              a.hgh[o] = hh;
+              a.hgl[o] = __float2half_rn(__fsub_rn(hv, __half2float(hh)));
+            }
           } else {
             const size_t o = pos * a.E + 256 * m + r;
             a.hd[o] = v0[j];
@@ -303,6 +363,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_free);
+      ++it;
       return true;
     });
     if (warp == 0 && lane == 0) {   // experts whose dispatch range is out of bounds are skipped; report them
@@ -320,20 +384,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
 }
 
-template __global__ void q80_group_tc_kernel<true>(const BatchArgs, const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                                   const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap);
-template __global__ void q80_group_tc_kernel<false>(const BatchArgs, const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                                    const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap);
-
-// Gathers the fp16 hi/lo planes of xn into dispatch order (row p = the token at dispatch position p).
+// Gathers the fp16 hi/lo planes of xn into dispatch order (row p = the token at dispatch position p). Q8_0 experts.
 __global__ void gather_x_kernel(const BatchArgs a) {
-  const int p = blockIdx.x, t = a.pos_token[p];
+  const int p = blockIdx.x;
+  if (p >= a.offsets[a.NE]) return;   // not a dispatched slot
+  const int t = a.pos_token[p];
   if (t < 0 || t >= a.T) { if (threadIdx.x == 0) set_error(a.err, ERR_BAD_EXPERT); return; }
   const uint4 *sh = reinterpret_cast<const uint4 *>(a.xh + static_cast<size_t>(t) * a.E);
   const uint4 *sl = reinterpret_cast<const uint4 *>(a.xl + static_cast<size_t>(t) * a.E);
   uint4 *dh = reinterpret_cast<uint4 *>(a.xdh + static_cast<size_t>(p) * a.E);
   uint4 *dl = reinterpret_cast<uint4 *>(a.xdl + static_cast<size_t>(p) * a.E);
   for (int i = threadIdx.x; i < a.E / 8; i += blockDim.x) { dh[i] = sh[i]; dl[i] = sl[i]; }
+}
+
+// The value of a Q8_K row (yd * q8 per 256-element block) as fp16 hi/lo planes, row p of the output, for p below *count
+// (the dispatched slots). K-quant experts: gate/up read the token's Q8_K row of xn (row_of: the token at dispatch
+// position p), down reads the Q8_K row of hg at position p itself (row_of null). The row is divided by rs[p] = 2^k, k the
+// exponent of its largest block scale, so every value lies within +-254 whatever the row's range (hg rows can exceed
+// fp16's); division by a power of two is exact, and the tensor-core epilogue multiplies rs[p] back.
+__global__ void q8k_planes_kernel(const int8_t *qs, const float *d, int n, const int *row_of, int rows, const int *count, __half *outh,
+                                  __half *outl, float *rs, int *err) {
+  const int p = blockIdx.x;
+  if (p >= *count) return;
+  const int src = row_of ? row_of[p] : p;
+  if (src < 0 || src >= rows) { if (threadIdx.x == 0) set_error(err, ERR_BAD_EXPERT); return; }
+  const int8_t *q = qs + static_cast<size_t>(src) * n;
+  const float *dd = d + static_cast<size_t>(src) * (n / 256);
+  float mx = 0.f;
+  for (int b = 0; b < n / 256; ++b) mx = fmaxf(mx, dd[b]);
+  const float scale = mx > 0.f ? ldexpf(1.0f, ilogbf(mx)) : 1.0f;
+  const float inv = 1.0f / scale;   // a power of two: exact
+  if (threadIdx.x == 0) rs[p] = scale;
+  for (int i = 2 * threadIdx.x; i < n; i += 2 * blockDim.x) {
+    const float yd = __fmul_rn(dd[i / 256], inv);
+    const float v0 = __fmul_rn(yd, static_cast<float>(q[i])), v1 = __fmul_rn(yd, static_cast<float>(q[i + 1]));
+    const __half2 h = __floats2half2_rn(v0, v1);
+    const __half2 l = __floats2half2_rn(__fsub_rn(v0, __low2float(h)), __fsub_rn(v1, __high2float(h)));
+    reinterpret_cast<__half2 *>(outh + static_cast<size_t>(p) * n)[i / 2] = h;
+    reinterpret_cast<__half2 *>(outl + static_cast<size_t>(p) * n)[i / 2] = l;
+  }
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *, const cuuint64_t *,
@@ -361,51 +450,60 @@ static bool encode_plane(CUtensorMap *m, const void *base, int rows, int cols) {
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// A 2-D map over Q8_0 weight rows [rows x row_bytes] (all experts' rows one after another), in 8-byte units: boxes of
-// 272 bytes (one 256-element chunk) x 128 rows, no swizzle (rows land 272 bytes apart).
-static bool encode_raw(CUtensorMap *m, const void *base, int rows, uint32_t row_bytes) {
+// A 2-D map over weight rows [rows x row_bytes] (all experts' rows one after another), in 8-byte units: boxes of one
+// 256-element chunk (`chunk` bytes) x 128 rows, no swizzle (rows land `chunk` bytes apart).
+static bool encode_raw(CUtensorMap *m, const void *base, int rows, uint32_t row_bytes, uint32_t chunk) {
   const EncodeTiled fn = encoder();
-  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes % CHUNK_BYTES)) return false;
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes % chunk) || (row_bytes % 16)) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 8), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[2] = {CHUNK_BYTES / 8, 128}, estr[2] = {1, 1};
+  const cuuint32_t box[2] = {chunk / 8, 128}, estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool q80_tc_supported(const void *gate, const void *up, const void *down, int E, int FF) {
-  const uintptr_t any = reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(down);
-  return (any & 15) == 0 && E % 256 == 0 && FF % 256 == 0 && E >= 256 && FF >= 256;
+bool tc_type_supported(uint32_t type, const void *w, int E, int FF) {
+  return (type == T_Q8_0 || type == T_Q4_K) && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && E % 256 == 0 && FF % 256 == 0 &&
+         E >= 256 && FF >= 256;
 }
 
-int launch_q80_tc(const BatchArgs &a, void *stream_, bool gateup) {
-  cudaStream_t st = static_cast<cudaStream_t>(stream_);
-  const int TK = a.T * a.K;
-  CUtensorMap tw0, tw1, tbh, tbl;
-  bool ok;
-  if (gateup) {
-    gather_x_kernel<<<TK, 256, 0, st>>>(a);
-    ok = encode_raw(&tw0, a.gate, a.NE * a.FF, a.grb) && encode_raw(&tw1, a.up, a.NE * a.FF, a.grb) &&
-         encode_plane(&tbh, a.xdh, TK, a.E) && encode_plane(&tbl, a.xdl, TK, a.E);
-  } else {
-    ok = encode_raw(&tw0, a.down, a.NE * a.E, a.drb) && encode_raw(&tw1, a.down, a.NE * a.E, a.drb) &&
-         encode_plane(&tbh, a.hgh, TK, a.FF) && encode_plane(&tbl, a.hgl, TK, a.FF);
-  }
-  if (!ok) return static_cast<int>(cudaErrorInvalidValue);
+template <bool GATEUP, uint32_t WT>
+static int launch_kernel(const BatchArgs &a, cudaStream_t st, const CUtensorMap &tw0, const CUtensorMap &tw1, const CUtensorMap &tbh,
+                         const CUtensorMap &tbl) {
   int dev = 0;
   cudaGetDevice(&dev);
   static int sms[64] = {};
   if (dev < 0 || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
   if (!sms[dev]) {
-    cudaFuncSetAttribute(q80_group_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    cudaFuncSetAttribute(q80_group_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(group_tc_kernel<GATEUP, WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcShape<WT>::SMEM);
     cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   }
-  const int tiles = a.NE * (gateup ? a.FF / 128 : a.E / 256);
+  const int tiles = a.NE * (GATEUP ? a.FF / 128 : a.E / 256);
   const int grid = tiles < sms[dev] ? tiles : sms[dev];
-  if (gateup) q80_group_tc_kernel<true><<<grid, TC_THREADS, SMEM_BYTES, st>>>(a, tw0, tw1, tbh, tbl);
-  else q80_group_tc_kernel<false><<<grid, TC_THREADS, SMEM_BYTES, st>>>(a, tw0, tw1, tbh, tbl);
+  group_tc_kernel<GATEUP, WT><<<grid, TC_THREADS, TcShape<WT>::SMEM, st>>>(a, tw0, tw1, tbh, tbl);
   return static_cast<int>(cudaGetLastError());
+}
+
+int launch_tc(const BatchArgs &a, void *stream_, bool gateup) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  const int TK = a.T * a.K;
+  const uint32_t wt = gateup ? a.gate_type : a.down_type;
+  const uint32_t chunk = wt == T_Q8_0 ? TcShape<T_Q8_0>::CHUNK : TcShape<T_Q4_K>::CHUNK;
+  CUtensorMap tw0, tw1, tbh, tbl;
+  bool ok;
+  if (gateup) {
+    if (wt == T_Q8_0) gather_x_kernel<<<TK, 256, 0, st>>>(a);
+    else q8k_planes_kernel<<<TK, 256, 0, st>>>(a.xq_qs, a.xq_d, a.E, a.pos_token, a.T, a.offsets + a.NE, a.xdh, a.xdl, a.rs, a.err);
+    ok = encode_raw(&tw0, a.gate, a.NE * a.FF, a.grb, chunk) && encode_raw(&tw1, a.up, a.NE * a.FF, a.grb, chunk) &&
+         encode_plane(&tbh, a.xdh, TK, a.E) && encode_plane(&tbl, a.xdl, TK, a.E);
+  } else {
+    if (wt != T_Q8_0) q8k_planes_kernel<<<TK, 256, 0, st>>>(a.hq_qs, a.hq_d, a.FF, nullptr, TK, a.offsets + a.NE, a.hgh, a.hgl, a.rs, a.err);
+    ok = encode_raw(&tw0, a.down, a.NE * a.E, a.drb, chunk) && encode_raw(&tw1, a.down, a.NE * a.E, a.drb, chunk) &&
+         encode_plane(&tbh, a.hgh, TK, a.FF) && encode_plane(&tbl, a.hgl, TK, a.FF);
+  }
+  if (!ok) return static_cast<int>(cudaErrorInvalidValue);
+  if (gateup) return wt == T_Q8_0 ? launch_kernel<true, T_Q8_0>(a, st, tw0, tw1, tbh, tbl) : launch_kernel<true, T_Q4_K>(a, st, tw0, tw1, tbh, tbl);
+  return wt == T_Q8_0 ? launch_kernel<false, T_Q8_0>(a, st, tw0, tw1, tbh, tbl) : launch_kernel<false, T_Q4_K>(a, st, tw0, tw1, tbh, tbl);
 }
 
 }  // namespace clb

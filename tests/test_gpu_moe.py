@@ -136,3 +136,13 @@ def test_bad_arguments_are_errors(ctx):
     bad.K = 40
     with pytest.raises(cb.ClutorError, match="expert counts"):
         ctx.moe_ffn(bad, np.zeros((1, 512), np.float32))
+
+
+@pytest.mark.parametrize("T,dt", [(130, synth.T_Q4_K), (512, synth.T_Q4_K), (300, synth.T_Q6_K)])
+def test_batched_k_quant_tensor_core(ctx, T, dt):
+    """Q4_K gate/up (and Q4_K down) as tensor-core grouped GEMMs of the dequantized weights and the value of the Q8_K
+    activations, up to 128 tokens an expert (tiles of 64): top-k exact, update within 1e-3 of the oracle's integer dots."""
+    L = synth.host_layer(E=1024, FF=768, NE=16, K=4, seed=T + 7, gate_type=synth.T_Q4_K, down_type=dt, router_scale=0.05)
+    x = synth.activations(T, 1024, seed=T + 8)
+    e = check(x, ctx.moe_ffn(L, x), oracle.moe_ffn(L, x, "oracle"), f"T={T}")
+    print(f"T={T} down {dt}: relative L2 of the update {e:.2e}")
