@@ -23,7 +23,7 @@ constexpr uint32_t SPIN_LIMIT = 1u << 22;
 
 CLB_DEV uint32_t smem_addr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
-// ---- mbarrier + bulk copy (global -> shared, no multicast) -------------------------------------------------------------
+// ---- mbarrier + bulk copy (global -> shared, this CTA only) -------------------------------------------------------------
 CLB_DEV void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
