@@ -1,6 +1,7 @@
 // The batched MoE block (T > 1 tokens): the reference's c/src/forward.c:1132-1210.
 //
-//   route_kernel     per (token, 32 experts): rmsnorm (double sum of squares), Q8_K of xn, the reference's dotf logits
+//   norm_kernel      per token: rmsnorm (double sum of squares), xn, Q8_K of xn
+//   router_kernel    per (8 tokens, 32 experts): the reference's dotf logits, each router row read once for the 8 tokens
 //   topk_kernel      per token: softmax (double sum), top-k by repeated arg-max with ties to the lower id, renormalisation
 //   dispatch_kernel  counting sort of the T*K (token, expert) slots by expert; each expert's tokens in ascending token order
 //                    (the reference's who[] list, c/src/forward.c:1189-1190), plus each expert's first appearance
@@ -8,7 +9,7 @@
 //                    in shared memory by a bulk copy), SwiGLU -> hg by dispatch position
 //   hq_kernel        Q8_K of each hg row (K-quant down weights)
 //   down_kernel      per (expert, 16 rows): down row dots for every token of that expert -> hd by dispatch position
-//   combine_kernel   per token: moe = sum over its experts in order of first appearance of wt*hd (the reference's todo
+//   combine_kernel   per (token, 512 columns): moe = sum over its experts in order of first appearance of wt*hd (the reference's todo
 //                    order, c/src/forward.c:1163-1164), x += resid_scale * moe
 #include <cstdio>
 #include <cuda_fp16.h>
@@ -24,14 +25,32 @@ constexpr int BNW = BT / 32;
 constexpr int ROUTE_EXPERTS = BT / 8;
 constexpr int ROWS_PER_CTA = 16; // weight rows per CTA in the expert kernels
 
-__global__ void __launch_bounds__(BT) route_kernel(const BatchArgs a) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  float *xn = reinterpret_cast<float *>(sm);
-  double *red = reinterpret_cast<double *>(xn + a.E);
+// Per token: rmsnorm (double sum of squares, c/src/forward.c:412-417), xn to global memory (and its fp16 hi/lo planes for
+// Q8_0 tensor-core experts), the Q8_K blocks of xn.
+__global__ void __launch_bounds__(BT) norm_kernel(const BatchArgs a) {
+  __shared__ double red[BNW];
+  __shared__ __align__(16) float xs[4096];
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, E = a.E;
-  const float *x = a.x_in + static_cast<size_t>(t) * E;
+  const float4 *x4 = reinterpret_cast<const float4 *>(a.x_in + static_cast<size_t>(t) * E);
+  float *xn = a.xn + static_cast<size_t>(t) * E;
   double ss = 0.0;
-  for (int i = tid; i < E; i += BT) { const float v = x[i]; xn[i] = v; ss += static_cast<double>(v) * v; }
+  {   // the row (E <= 4096: at most four float4 a thread), all loads in flight, into shared memory
+    float4 r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int v = u * BT + tid;
+      r[u] = v < E / 4 ? x4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int v = u * BT + tid;
+      if (v < E / 4) {
+        reinterpret_cast<float4 *>(xs)[v] = r[u];
+        ss += static_cast<double>(r[u].x) * r[u].x + static_cast<double>(r[u].y) * r[u].y +
+              static_cast<double>(r[u].z) * r[u].z + static_cast<double>(r[u].w) * r[u].w;
+      }
+    }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
   if (lane == 0) red[warp] = ss;
@@ -39,32 +58,90 @@ __global__ void __launch_bounds__(BT) route_kernel(const BatchArgs a) {
   double tot = 0.0;
   for (int w = 0; w < BNW; ++w) tot += red[w];
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / static_cast<double>(E)), a.eps)));
-  for (int i = tid; i < E; i += BT) xn[i] = __fmul_rn(__fmul_rn(xn[i], scale), a.norm[i]);
-  __syncthreads();
-  if (blockIdx.y == 0) {
-    for (int i = tid; i < E; i += BT) a.xn[static_cast<size_t>(t) * E + i] = xn[i];
-    if (a.xh)   // fp16 hi/lo planes of xn for the tensor-core products: xn = hi + lo to about 2^-22
-      for (int i = tid; i < E; i += BT) {
-        const __half h = __float2half_rn(xn[i]);
-        a.xh[static_cast<size_t>(t) * E + i] = h;
-        a.xl[static_cast<size_t>(t) * E + i] = __float2half_rn(__fsub_rn(xn[i], __half2float(h)));
-      }
-    q8k_quantize_block(xn, E, a.xq_qs + static_cast<size_t>(t) * E, a.xq_d + static_cast<size_t>(t) * (E / 256),
-                       a.xq_bs + static_cast<size_t>(t) * (E / 16), warp, BNW, lane);
+  for (int i = tid; i < E; i += BT) {
+    const float v = __fmul_rn(__fmul_rn(xs[i], scale), a.norm[i]);
+    xs[i] = v;
+    xn[i] = v;
+    if (a.xh) {   // fp16 hi/lo planes of xn for the Q8_0 tensor-core products: xn = hi + lo to about 2^-22
+      const __half h = __float2half_rn(v);
+      a.xh[static_cast<size_t>(t) * E + i] = h;
+      a.xl[static_cast<size_t>(t) * E + i] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+    }
   }
-  const int grp = tid >> 3, l8 = tid & 7;
-  const int e = blockIdx.y * ROUTE_EXPERTS + grp;
-  float s = 0.f;
+  __syncthreads();
+  q8k_quantize_block(xs, E, a.xq_qs + static_cast<size_t>(t) * E, a.xq_d + static_cast<size_t>(t) * (E / 256),
+                     a.xq_bs + static_cast<size_t>(t) * (E / 16), warp, BNW, lane);
+}
+
+// Router logits of ROUTER_TOKENS tokens x 32 experts per CTA, the reference's dotf (c/src/forward.c:574-581): eight lanes per
+// expert, lane l summing w[i] * x[i] for i = l, l + 8, ... in element order, then ((0+1)+(2+3))+((4+5)+(6+7)). The tokens'
+// xn rows sit in shared memory transposed by chain -- element i of token t at [t][i % 8][i / 8], rows padded by 4 floats so
+// the eight chains fall in different banks -- so a lane reads its chain's next four elements with one 16-byte load, and a
+// router row is read once for all the tokens.
+// ROUTER_TOKENS: 8 tokens a CTA for large batches (fewer router reads), 2 for small ones (more CTAs).
+CLB_DEV int router_row(int E) { return E / 8 + 4; }   // floats per chain row
+template <int ROUTER_TOKENS>
+__global__ void __launch_bounds__(BT) router_kernel(const BatchArgs a) {
+  extern __shared__ __align__(16) float xs[];   // [ROUTER_TOKENS][8][E/8 + 4]
+  const int E = a.E, t0 = blockIdx.x * ROUTER_TOKENS, nt = min(ROUTER_TOKENS, a.T - t0), XR = router_row(E), XT = 8 * XR;
+  const int tid = threadIdx.x, lane = tid & 31;
+  {   // the tokens' rows: every load of a batch in flight before the transposing stores
+    const int nvec = ROUTER_TOKENS * E / 4;
+    const float4 *src = reinterpret_cast<const float4 *>(a.xn + static_cast<size_t>(t0) * E);
+    for (int v0 = 0; v0 < nvec; v0 += 16 * BT) {
+      float4 r[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int v = v0 + u * BT + tid;
+        r[u] = (v < nvec && (4 * v) / E < nt) ? src[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int v = v0 + u * BT + tid;
+        if (v < nvec) {
+          const int t = (4 * v) / E, k = 4 * v - t * E;   // k is a multiple of 4: chains k%8 .. k%8+3, step k/8
+          float *d = xs + t * XT + (k & 7) * XR + (k >> 3);
+          d[0] = r[u].x;
+          d[XR] = r[u].y;
+          d[2 * XR] = r[u].z;
+          d[3 * XR] = r[u].w;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int grp = tid >> 3, l8 = tid & 7, e = blockIdx.y * ROUTE_EXPERTS + grp;
+  float s[ROUTER_TOKENS];
+#pragma unroll
+  for (int t = 0; t < ROUTER_TOKENS; ++t) s[t] = 0.f;
   if (e < a.NE) {
     const float *w = a.router + static_cast<size_t>(e) * E;
-    for (int i = l8; i < E; i += 8) s = __fadd_rn(s, __fmul_rn(__ldg(w + i), xn[i]));
-  }
-  float p[8];
+    for (int k0 = 0; k0 < E / 8; k0 += 32) {   // chain steps k0 .. k0+31: 32 router loads in flight
+      float wv[32];
 #pragma unroll
-  for (int l = 0; l < 8; ++l) p[l] = __shfl_sync(FULL, s, (lane & ~7) + l);
-  if (e < a.NE && l8 == 0)
-    a.logits[static_cast<size_t>(t) * a.NE + e] =
-        __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])), __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+      for (int j = 0; j < 32; ++j) wv[j] = __ldg(w + l8 + 8 * (k0 + j));
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+#pragma unroll
+        for (int t = 0; t < ROUTER_TOKENS; ++t) {
+          const float4 xv = *reinterpret_cast<const float4 *>(xs + t * XT + l8 * XR + k0 + 4 * j4);
+          s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4], xv.x));
+          s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4 + 1], xv.y));
+          s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4 + 2], xv.z));
+          s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4 + 3], xv.w));
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < ROUTER_TOKENS; ++t) {
+    float p[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) p[l] = __shfl_sync(FULL, s[t], (lane & ~7) + l);
+    if (t < nt && e < a.NE && l8 == 0)
+      a.logits[static_cast<size_t>(t0 + t) * a.NE + e] =
+          __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])), __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+  }
 }
 
 __global__ void __launch_bounds__(32) topk_kernel(const BatchArgs a) {
@@ -128,12 +205,15 @@ __global__ void __launch_bounds__(32) topk_kernel(const BatchArgs a) {
 }
 
 // One CTA. The (expert, token) pairs form a bit matrix (expert rows, token bits); an expert's tokens are its set bits in
-// ascending order, so its dispatch positions come from population counts.
+// ascending order (the reference's who[] list, c/src/forward.c:1189-1190), so the dispatch position of slot (t, k) with
+// expert e is offset[e] + the set bits of row e before bit t -- from a per-word prefix of population counts, in parallel
+// over the slots.
 __global__ void __launch_bounds__(1024) dispatch_kernel(const BatchArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int NE = a.NE, K = a.K, T = a.T, nw = (T + 31) / 32;
   uint32_t *bits = reinterpret_cast<uint32_t *>(sm);            // [NE][nw]
-  int *cnt = reinterpret_cast<int *>(bits + NE * nw);           // [NE]
+  int *wpre = reinterpret_cast<int *>(bits + NE * nw);          // [NE][nw] set bits of the row before word w
+  int *cnt = wpre + NE * nw;                                    // [NE]
   int *off = cnt + NE;                                          // [NE + 1]
   int *first = off + NE + 1;                                    // [NE]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
@@ -150,45 +230,44 @@ __global__ void __launch_bounds__(1024) dispatch_kernel(const BatchArgs a) {
     atomicMin(&first[e], s);
   }
   __syncthreads();
-  for (int e = warp; e < NE; e += nwarps) {
-    int c = 0;
-    for (int w = lane; w < nw; w += 32) c += __popc(bits[e * nw + w]);
+  for (int e = warp; e < NE; e += nwarps) {   // per expert: exclusive prefix of the words' population counts
+    int base = 0;
+    for (int w0 = 0; w0 < nw; w0 += 32) {
+      const int w = w0 + lane;
+      const int c = w < nw ? __popc(bits[e * nw + w]) : 0;
+      int incl = c;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(FULL, c, o);
-    if (lane == 0) cnt[e] = c;
+      for (int o = 1; o < 32; o <<= 1) { const int v = __shfl_up_sync(FULL, incl, o); if (lane >= o) incl += v; }
+      if (w < nw) wpre[e * nw + w] = base + incl - c;
+      base += __shfl_sync(FULL, incl, 31);
+    }
+    if (lane == 0) cnt[e] = base;
   }
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int e = 0; e < NE; ++e) { off[e] = acc; acc += cnt[e]; }
-    off[NE] = acc;
+  if (warp == 0) {   // exclusive prefix over the experts
+    int base = 0;
+    for (int e0 = 0; e0 < NE; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < NE ? cnt[e] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) { const int v = __shfl_up_sync(FULL, incl, o); if (lane >= o) incl += v; }
+      if (e < NE) off[e] = base + incl - c;
+      base += __shfl_sync(FULL, incl, 31);
+    }
+    if (lane == 0) off[NE] = base;
   }
   __syncthreads();
   for (int e = tid; e < NE; e += blockDim.x) { a.counts[e] = cnt[e]; a.offsets[e] = off[e]; a.first[e] = first[e]; }
   if (tid == 0) a.offsets[NE] = off[NE];
-  for (int e = warp; e < NE; e += nwarps) {
-    int base = off[e];
-    for (int w0 = 0; w0 < nw; w0 += 32) {
-      const int w = w0 + lane;
-      const uint32_t word = w < nw ? bits[e * nw + w] : 0u;
-      int c = __popc(word), incl = c;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) { const int v = __shfl_up_sync(FULL, incl, o); if (lane >= o) incl += v; }
-      int pos = base + incl - c;
-      uint32_t m = word;
-      while (m) {
-        const int b = __ffs(m) - 1;
-        m &= m - 1;
-        const int t = 32 * w + b;
-        int k = 0;
-        while (k < K && a.sel[static_cast<size_t>(t) * K + k] != e) ++k;
-        a.pos_token[pos] = t;
-        a.pos_wt[pos] = a.wt[static_cast<size_t>(t) * K + k];
-        a.slot_pos[static_cast<size_t>(t) * K + k] = pos;
-        ++pos;
-      }
-      base += __shfl_sync(FULL, incl, 31);
-    }
+  for (int s = tid; s < T * K; s += blockDim.x) {
+    const int t = s / K, e = a.sel[s];
+    if (e < 0 || e >= NE) continue;
+    const int w = t / 32;
+    const int pos = off[e] + wpre[e * nw + w] + __popc(bits[e * nw + w] & ((1u << (t & 31)) - 1u));
+    a.pos_token[pos] = t;
+    a.pos_wt[pos] = a.wt[s];
+    a.slot_pos[s] = pos;
   }
 }
 
@@ -309,8 +388,9 @@ __global__ void __launch_bounds__(BT) down_kernel(const BatchArgs a) {
   }
 }
 
+// Per (token, 512 columns): the token's experts in order of first appearance, weighted, plus the residual.
 __global__ void __launch_bounds__(BT) combine_kernel(const BatchArgs a) {
-  const int t = blockIdx.x, K = a.K, E = a.E;
+  const int t = blockIdx.x, K = a.K, E = a.E, i0 = blockIdx.y * 2 * BT, i1 = min(E, i0 + 2 * BT);
   __shared__ int s_pos[DECODE_MAX_K];
   __shared__ float s_w[DECODE_MAX_K];
   __shared__ int s_n;
@@ -335,7 +415,7 @@ __global__ void __launch_bounds__(BT) combine_kernel(const BatchArgs a) {
   const int n = s_n;
   for (int j = 0; j < n; ++j)
     if (s_pos[j] < 0 || s_pos[j] >= a.T * K) { if (threadIdx.x == 0) set_error(a.err, ERR_BAD_EXPERT); return; }
-  for (int i = threadIdx.x; i < E; i += BT) {
+  for (int i = i0 + threadIdx.x; i < i1; i += BT) {
     float m = 0.f;
     for (int j = 0; j < n; ++j) m = __fadd_rn(m, __fmul_rn(s_w[j], a.hd[static_cast<size_t>(s_pos[j]) * E + i]));
     const size_t xi = static_cast<size_t>(t) * E + i;
@@ -347,8 +427,18 @@ static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
 int launch_route(const BatchArgs &a, void *stream_) {
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
-  const size_t route_smem = a.E * 4 + BNW * 8;
-  route_kernel<<<dim3(a.T, (a.NE + ROUTE_EXPERTS - 1) / ROUTE_EXPERTS), BT, route_smem, st>>>(a);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr[64] = {};
+  if (dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(router_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 8 * (4096 / 8 + 4) * 4);
+    cudaFuncSetAttribute(router_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8 * (4096 / 8 + 4) * 4);
+    attr[dev] = true;
+  }
+  norm_kernel<<<a.T, BT, 0, st>>>(a);
+  const dim3 rg8((a.T + 7) / 8, (a.NE + ROUTE_EXPERTS - 1) / ROUTE_EXPERTS), rg2((a.T + 1) / 2, rg8.y);
+  if (a.T > 512) router_kernel<8><<<rg8, BT, 8 * 8 * (a.E / 8 + 4) * 4, st>>>(a);
+  else router_kernel<2><<<rg2, BT, 2 * 8 * (a.E / 8 + 4) * 4, st>>>(a);
   topk_kernel<<<a.T, 32, 0, st>>>(a);
   return static_cast<int>(cudaGetLastError());
 }
@@ -362,7 +452,8 @@ int launch_experts(const BatchArgs &a, void *stream_) {
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
   const int T = a.T, E = a.E, FF = a.FF, NE = a.NE, K = a.K;
   const int nw = (T + 31) / 32;
-  const size_t disp_smem = static_cast<size_t>(NE) * nw * 4 + (3 * NE + 1) * 4;
+  const size_t disp_smem = static_cast<size_t>(NE) * nw * 8 + (3 * NE + 1) * 4;
+  if (disp_smem > 200 * 1024) return static_cast<int>(cudaErrorInvalidValue);   // tokens x experts beyond one CTA's bit matrix
   dispatch_kernel<<<1, 1024, disp_smem, st>>>(a);
   const size_t gu_smem = 16 + E * 4 + 2 * ROWS_PER_CTA * 4 + 2 * align16(ROWS_PER_CTA * a.grb + 32) + 16;
   int dev = 0;
@@ -388,7 +479,7 @@ int launch_experts(const BatchArgs &a, void *stream_) {
     const size_t dn_smem = 16 + FF * 4 + align16(ROWS_PER_CTA * a.drb + 32) + 16;
     down_kernel<<<dim3(NE, (E + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, dn_smem, st>>>(a);
   }
-  combine_kernel<<<T, BT, 0, st>>>(a);
+  combine_kernel<<<dim3(T, (E + 2 * BT - 1) / (2 * BT)), BT, 0, st>>>(a);
   return static_cast<int>(cudaGetLastError());
 }
 
