@@ -16,7 +16,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ["api.cu", "decode.cu", "batched.cu", "backend.cu", "noalloc.cu", "grouped_tc.cu", "cache.cpp", "store.cu"]
+SOURCES = ["api.cu", "decode.cu", "batched.cu", "backend.cu", "noalloc.cu", "grouped_tc.cu", "cache.cpp", "store.cu", "gguf.cpp",
+           "fwd.cu", "model.cu"]
 LIB = os.path.join(HERE, "libclutor_b200.so")
 
 
@@ -37,7 +38,7 @@ def flags(ptxas_v: bool = False) -> list[str]:
 
 def build(verbose: bool = False, ptxas_v: bool = False, force: bool = False) -> str:
     srcs = [os.path.join(CSRC, s) for s in SOURCES]
-    deps = srcs + [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith(".cuh")] + [os.path.join(ROOT, "include", "clb200.h")]
+    deps = srcs + [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith((".cuh", ".h"))] + [os.path.join(ROOT, "include", "clb200.h")]
     if not force and os.path.exists(LIB) and all(os.path.getmtime(d) <= os.path.getmtime(LIB) for d in deps):
         return LIB
     bdir = os.path.join(HERE, "_build")

@@ -103,14 +103,11 @@ int plan_decode_shape(int sms, int max_smem, const clb200_moe_layer &L, DecodeAr
   a.off_norm = take(static_cast<size_t>(E) * 4);
   a.off_xq = take(static_cast<size_t>(E) + 2 * (E / 16) + 4 * (E / 256));
   a.off_router = take(static_cast<size_t>(nre) * E * 4);
-  a.off_misc = take(NW * 8 + 16 + 32 * 4 + 32 * 4 + NW * 4 + ((NE + 3) & ~3) * 4);
-  const size_t nterm = std::max(static_cast<size_t>(2) * K * a.rgu_max * nb, static_cast<size_t>(a.rd_max) * K * nbd);
-  a.off_terms = take(nterm * 4);
-  a.off_gres = take(static_cast<size_t>(2) * K * a.rgu_max * 4);
-  a.off_rowoff = take(static_cast<size_t>(2) * K * a.rgu_max * 4);
+  a.off_rprod = take(static_cast<size_t>(nre) * 8 * (E / 8 + 4) * 4);   // products, one padded row per strided sum
+  a.off_misc = take(NW * 8 + 16 + 3 * 32 * 4 + (DECODE_THREADS / 4) * 4);   // probs: one per expert the kernel can rank
+  a.off_terms = take(static_cast<size_t>(a.rd_max) * K * nbd * 4);
   a.off_hq = take(static_cast<size_t>(K) * FF + 2 * (static_cast<size_t>(K) * FF / 16) + 4 * (static_cast<size_t>(K) * FF / 256));
   a.off_xr = take(static_cast<size_t>(a.rd_max) * 4);
-  a.off_hd = take(static_cast<size_t>(a.rd_max) * K * 4);
   a.off_slots = static_cast<uint32_t>(al(o, 128));
   const size_t total = a.off_slots + static_cast<size_t>(K) * a.slot_bytes + 16;
   if (total > static_cast<size_t>(max_smem)) return 1;
@@ -183,6 +180,7 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   a.sel_out = sel_out; a.wt_out = wt_out;
   a.sync = reinterpret_cast<uint32_t *>(c->small + 64);
   a.err = c->small;
+  a.trace = c->trace;
   a.mode = mode;
   if (mode == 2)
     for (int k = 0; k < K; ++k) {
@@ -191,11 +189,12 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
       a.slab[k] = slabs ? slabs[k] : nullptr;
     }
   if (!c->attrs_set) {
-    CUDA_OR(cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "kernel attribute");
+    CUDA_OR(decode_allow_smem(c->max_smem), "kernel attribute");
     c->attrs_set = true;
   }
+  const DecodeFn fn = decode_kernel_for(a.gate_type, a.down_type);
   int occ = 0;
-  CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, moe_decode_kernel, DECODE_THREADS, a.smem_bytes), "occupancy");
+  CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DECODE_THREADS, a.smem_bytes), "occupancy");
   if (occ < 1) { errf(err, errlen, "the one-token kernel does not fit on an SM (%u bytes of shared memory)", a.smem_bytes); return 1; }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->sms);
@@ -207,7 +206,7 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CUDA_OR(cudaLaunchKernelEx(&cfg, moe_decode_kernel, a), "launching the one-token kernel");
+  CUDA_OR(cudaLaunchKernelEx(&cfg, fn, a), "launching the one-token kernel");
   return 0;
 }
 
@@ -251,6 +250,10 @@ void clb200_close(clb200_ctx *c) {
 }
 
 uint64_t clb200_device_bytes(const clb200_ctx *c) { return c ? c->bytes : 0; }
+
+void clb200_set_trace(clb200_ctx *c, void *dev_buf) {
+  if (c) c->trace = static_cast<unsigned long long *>(dev_buf);
+}
 
 int clb200_layer_bind(clb200_ctx *c, const clb200_moe_layer *L, int on_device, char *err, size_t errlen) {
   if (!c) { errf(err, errlen, "no context"); return -1; }

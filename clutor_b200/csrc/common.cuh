@@ -82,6 +82,31 @@ CLB_DEV bool wait_counter(const uint32_t *p, uint32_t target) {
 }
 CLB_DEV void set_error(int *err, int code) { atomicCAS(err, 0, code); }
 
+// ---- phase trace -------------------------------------------------------------------------------------------------------------
+CLB_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t)::"memory");   // not moved across memory operations
+  return t;
+}
+// Thread 0 of the CTA stamps boundary i of its row (32 entries per CTA) when tracing is on; trace_stamp_here stamps from
+// whichever thread calls it. Boundaries hold the SM's cycle counter (exact within a CTA); entries 30 and 31 the global
+// nanosecond timer at entry and exit (comparable across CTAs and launches).
+constexpr int TRACE_ROW = 32;
+CLB_DEV unsigned long long sm_cycles() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %clock64;" : "=l"(t)::"memory");
+  return t;
+}
+CLB_DEV void trace_stamp_here(unsigned long long *trace, int i) {
+  if (trace) trace[TRACE_ROW * blockIdx.x + i] = sm_cycles();
+}
+CLB_DEV void trace_time(unsigned long long *trace, int i) {
+  if (trace && threadIdx.x == 0) trace[TRACE_ROW * blockIdx.x + i] = global_ns();
+}
+CLB_DEV void trace_stamp(unsigned long long *trace, int i) {
+  if (threadIdx.x == 0) trace_stamp_here(trace, i);
+}
+
 // ---- the reference's scalar steps, exactly rounded ---------------------------------------------------------------------------
 // fp16 bits to float: exact (every half is a float).
 CLB_DEV float f16_bits_to_f32(uint16_t h) {

@@ -101,6 +101,7 @@ struct clb200_ctx {
   float *hx = nullptr;                             // host-call staging of x / sel / wt on the device (in scratch)
   uint64_t bytes = 0;
   bool attrs_set = false;
+  unsigned long long *trace = nullptr;             // phase trace of the one-token kernel (device, 16 per CTA) or null
 };
 
 namespace clb {

@@ -2,6 +2,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 
 namespace clb {
 
@@ -34,11 +35,17 @@ struct DecodeArgs {
   // shared-memory plan (host-computed): one slot per chosen expert holds this CTA's gate, up and down rows of it
   int rgu_max, rd_max;
   uint32_t grb, drb, gseg, dseg, slot_bytes;
-  uint32_t off_bars, off_xn, off_norm, off_xq, off_router, off_misc, off_terms, off_gres, off_rowoff, off_hq, off_xr, off_hd,
-      off_slots, smem_bytes;
+  uint32_t off_bars, off_xn, off_norm, off_xq, off_router, off_rprod, off_misc, off_terms, off_hq, off_xr, off_slots, smem_bytes;
+  // phase trace (null: off): thread 0 of CTA c writes its SM's cycle counter at phase boundary i to trace[32 * c + i] and the global
+  // nanosecond timer at entry and exit to trace[32 * c + 30] and [31]
+  unsigned long long *trace;
 };
 
-__global__ void moe_decode_kernel(const DecodeArgs a);
+// The one-token kernel for experts of these types (gate/up share one type), or null when it has none.
+using DecodeFn = void (*)(DecodeArgs);
+DecodeFn decode_kernel_for(uint32_t gate_type, uint32_t down_type);
+// Lets every instantiation use `bytes` of dynamic shared memory (on the current device).
+cudaError_t decode_allow_smem(int bytes);
 
 // ---- batched path ------------------------------------------------------------------------------------------------------
 struct BatchArgs {

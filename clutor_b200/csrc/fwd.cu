@@ -1,0 +1,838 @@
+// The whole-model one-token step as ONE persistent kernel: the reference's cl_fwd_step (c/src/forward.c:878-1040) for the
+// mixture-of-experts transformers (olmoe, qwen3moe, granitemoe) on one B200.
+//
+// One CTA per SM (G CTAs, a cooperative launch, so all are resident), 512 threads. Work that crosses CTAs goes through
+// global memory behind one grid barrier counter (bounded waits; any CTA's error ends every CTA's wait). Per layer:
+//   A  attention input: x (global) -> rmsnorm -> Q8_K blocks (every CTA); this CTA's rows of the stacked [wq; wk; wv]
+//      (exact integer block sums, the reference's float block terms in block order: c/src/quant.c:832-846)   | barrier
+//   B  attention, one work item per (key/value head, chunk of 256 positions): QK-norm and rotary embedding of the item's
+//      query heads and key (c/src/forward.c:905-915), the new key/value into the half-precision cache (kv_put, :563-572),
+//      scores against the cached keys, softmax and the weighted values, in fp32 (the grouped form of :665-737);
+//      a context longer than one chunk merges the chunks' partials afterwards                               | barrier(s)
+//   C  attention output: Q8_K of the attention vector (every CTA); this CTA's rows of wo; x += resid * wo att | barrier
+//   D  mixture of experts, as the one-token MoE kernel (decode.cu) does it: rmsnorm, router (the reference's dotf),
+//      softmax, top-k, renormalisation, this CTA's share of every chosen expert's gate/up rows (bulk copies into shared
+//      memory), SwiGLU                                                                                       | barrier
+//      the Q8_K blocks of every expert's hg, this CTA's down rows, x += resid * sum_k wt_k hd_k in rank order  | barrier
+// then the output norm and this CTA's rows of the output matrix, streamed through shared memory, their logits and the
+// greedy arg-max (lowest id on ties, c/src/main.c:349-350). The last CTA out advances the sequence state.
+//
+// While a layer's experts stream, every CTA asks L2 for the rows of the next layer's dense matrices it will read, and the
+// next layer's router rows are copied into shared memory as soon as this layer's router products are formed.
+#include "common.cuh"
+#include "fwd.cuh"
+#include "rowdot.cuh"
+
+namespace clb {
+namespace {
+
+constexpr int NW = FWD_THREADS / 32;
+constexpr int RW = NW - 1;              // the router warp
+constexpr int HEAD_ROWS = 16;           // output-matrix rows per shared-memory stage
+constexpr int HEAD_STAGES = 4;
+
+CLB_DEV int ld_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
+
+CLB_DEV void prefetch_l2(const void *p, uint32_t bytes) {   // p and bytes 16-byte aligned
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// The block of one grid barrier: every CTA arrives, then waits for all G (bounded; returns early when any CTA has
+// recorded an error). Returns false on a timeout or a recorded error.
+struct Grid {
+  uint32_t *ctr;
+  int *err;
+  int *s_ok;      // shared: the barrier's verdict for the whole CTA
+  uint32_t G, gen;
+  CLB_DEV bool sync() {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      ++gen;
+      red_release_add(ctr, 1u);
+      const uint32_t target = gen * G;
+      bool ok = false;
+      for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
+        if (ld_acquire(ctr) >= target) { ok = true; break; }
+        if ((i & 127) == 127 && ld_volatile(err)) break;
+        if (i > 4096) __nanosleep(64);
+      }
+      if (!ok) set_error(err, ERR_WAIT_GRID);
+      *s_ok = ok && !ld_volatile(err);
+    }
+    __syncthreads();
+    return *s_ok != 0;
+  }
+};
+
+// rmsnorm (c/src/forward.c:412-417) of the n floats at x (global, written by other CTAs) with weights w: xn (shared) =
+// x * (1 / sqrtf(mean(x^2) + eps)) * w, the mean of squares in double. red: NW doubles of shared scratch.
+CLB_DEV void rmsnorm_to_smem(const float *x, const float *w, float *xn, int n, float eps, double *red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int XV = 4096 / 4 / FWD_THREADS;
+  float4 xv[XV];
+  double ss = 0.0;
+#pragma unroll
+  for (int u = 0; u < XV; ++u) {
+    const int i = (tid + u * FWD_THREADS) * 4;
+    if (i < n) {
+      const float4 v = __ldcg(reinterpret_cast<const float4 *>(x + i));
+      xv[u] = v;
+      ss += static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y + static_cast<double>(v.z) * v.z + static_cast<double>(v.w) * v.w;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  double tot = 0.0;
+#pragma unroll
+  for (int k = 0; k < NW; ++k) tot += red[k];
+  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tot / static_cast<double>(n)), eps)));
+#pragma unroll
+  for (int u = 0; u < XV; ++u) {
+    const int i = (tid + u * FWD_THREADS) * 4;
+    if (i < n) {
+      const float4 v = xv[u], g = __ldg(reinterpret_cast<const float4 *>(w + i));
+      reinterpret_cast<float4 *>(xn + i)[0] = make_float4(__fmul_rn(__fmul_rn(v.x, s), g.x), __fmul_rn(__fmul_rn(v.y, s), g.y),
+                                                          __fmul_rn(__fmul_rn(v.z, s), g.z), __fmul_rn(__fmul_rn(v.w, s), g.w));
+    }
+  }
+  __syncthreads();
+}
+
+CLB_DEV int lanes_for(int nb) { return nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : nb <= 8 ? 8 : 16; }
+
+// Rows [r0, r1) of a K-quant matrix (rows at m.p + r * m.rb, nb 256-blocks each, in global memory) times the Q8_K vector
+// in shared memory: a group of lanes per row, one lane per block, the block terms
+// added in block order at the group's first lane, which calls out(r, value). Call from all threads.
+template <class Out>
+CLB_DEV void gemv_rows(const FwdMat &m, int nb, int r0, int r1, const int8_t *qs, const float *dd, const int16_t *bs, Out out) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int GL = lanes_for(nb), lg = lane & (GL - 1), gpw = 32 / GL, ngroups = NW * gpw, gid = warp * gpw + lane / GL;
+  const int base = lane - lg;
+  const bool has = lg < nb;
+  const SmemAct act{qs, bs, dd};
+  for (int b0 = r0; b0 < r1; b0 += ngroups) {   // the same trip count in every warp
+    const int r = b0 + gid;
+    const bool valid = r < r1;
+    float t = 0.f;
+    if (valid && has) t = kq_block_s(m.type, m.p + static_cast<size_t>(r) * m.rb, lg, act, lg);
+    float s = 0.f;
+    for (int b = 0; b < nb; ++b) s = __fadd_rn(s, __shfl_sync(FULL, t, base + b));
+    if (valid && lg == 0) out(r, s);
+  }
+}
+
+// One row of the token embedding as floats, the reference's cl_dequant_row (c/src/quant.c:59-66, 87-105, 155-158).
+CLB_DEV void embed_row(const FwdMat &m, int token, int E, float *y) {
+  const uint8_t *row = m.p + static_cast<size_t>(token) * m.rb;
+  for (int i = threadIdx.x; i < E; i += FWD_THREADS) {
+    float v;
+    if (m.type == T_Q4_K) {
+      const uint8_t *b = row + 144 * (i / 256);
+      const int e = i % 256, j = e / 64, hi = (e / 32) & 1, l = e % 32;
+      int sc, mn;
+      q4k_scale_min(b + 4, 2 * j + hi, sc, mn);
+      const float d = f16_bits_to_f32(lds_u16(b)), dmin = f16_bits_to_f32(lds_u16(b + 2));
+      const int q = hi ? (b[16 + 32 * j + l] >> 4) : (b[16 + 32 * j + l] & 15);
+      v = __fsub_rn(__fmul_rn(__fmul_rn(d, static_cast<float>(sc)), static_cast<float>(q)), __fmul_rn(dmin, static_cast<float>(mn)));
+    } else if (m.type == T_Q6_K) {
+      const uint8_t *b = row + 210 * (i / 256);
+      const int e = i % 256, n = e / 128, r = e % 128, part = r / 32, l = r % 32;
+      const uint8_t *ql = b + 64 * n, *qh = b + 128 + 32 * n;
+      const int8_t *sc = reinterpret_cast<const int8_t *>(b + 192) + 8 * n;
+      const int lo = (part & 1) ? ql[l + 32] : ql[l];
+      const int q = ((part < 2 ? (lo & 15) : (lo >> 4)) | (((qh[l] >> (2 * part)) & 3) << 4)) - 32;
+      const float d = f16_bits_to_f32(lds_u16(b + 208));
+      v = __fmul_rn(__fmul_rn(d, static_cast<float>(sc[l / 16 + 2 * part])), static_cast<float>(q));
+    } else if (m.type == T_Q8_0) {
+      const uint8_t *b = row + 34 * (i / 32);
+      v = __fmul_rn(static_cast<float>(static_cast<int8_t>(b[2 + i % 32])), f16_bits_to_f32(lds_u16(b)));
+    } else {   // F32
+      v = reinterpret_cast<const float *>(row)[i];
+    }
+    y[i] = v;
+  }
+}
+
+// Rotary embedding of one head held by a warp, EPL = hd / 32 elements per lane at i = lane + 32 e. NEOX pairs (i, i + hd/2)
+// (c/src/forward.c:428-435) or adjacent pairs (2i, 2i + 1) (:420-426). theta_i = pos * base^(-2i/hd), each step rounded to
+// float as the reference's powf, cosf and sinf give it (correctly rounded here, via double).
+template <int EPL>
+CLB_DEV void rope_warp(float (&v)[EPL], int hd, int pos, float base, bool pairs) {
+  const int lane = threadIdx.x & 31;
+  auto angle = [&](int i, float &c, float &s) {
+    const float ex = __fdiv_rn(__fmul_rn(-2.0f, static_cast<float>(i)), static_cast<float>(hd));
+    const float p = __double2float_rn(pow(static_cast<double>(base), static_cast<double>(ex)));
+    const float th = __fmul_rn(static_cast<float>(pos), p);
+    c = __double2float_rn(cos(static_cast<double>(th)));
+    s = __double2float_rn(sin(static_cast<double>(th)));
+  };
+  if (!pairs) {
+#pragma unroll
+    for (int e = 0; e < EPL / 2; ++e) {
+      float c, s;
+      angle(lane + 32 * e, c, s);
+      const float a = v[e], b = v[e + EPL / 2];
+      v[e] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+      v[e + EPL / 2] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int i = lane + 32 * e;
+      float c, s;
+      angle(i / 2, c, s);
+      const float other = __shfl_xor_sync(FULL, v[e], 1);
+      const float a = (i & 1) ? other : v[e], b = (i & 1) ? v[e] : other;
+      v[e] = (i & 1) ? __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c)) : __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    }
+  }
+}
+
+// The arg-max key of a logit: larger value first, then the lower id.
+CLB_DEV unsigned long long argmax_key(float v, int id) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(ord) << 32) | (0xffffffffu - static_cast<uint32_t>(id));
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int E = a.E, FF = a.FF, NE = a.NE, K = a.K, hd = a.hd;
+  const int nb = E / 256, nbd = FF / 256;
+  FwdState *st = a.st;
+
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);   // [K] experts, [K] router rows, [K+1..] output stages
+  float *xn = reinterpret_cast<float *>(smem + a.off_xn);             // [E]
+  int8_t *xq_qs = reinterpret_cast<int8_t *>(smem + a.off_xq);        // Q8_K of the current vector (up to n_q wide)
+  const int XQW = a.n_q > E ? a.n_q : E;
+  int16_t *xq_bs = reinterpret_cast<int16_t *>(smem + a.off_xq + XQW);
+  float *xq_d = reinterpret_cast<float *>(smem + a.off_xq + XQW + 2 * (XQW / 16));
+  double *s_red = reinterpret_cast<double *>(smem + a.off_misc);      // [NW]
+  // [0] barrier verdict, [1] a router copy in flight, [2] the router logits arrived, [3] the parity of the router copy in
+  // flight, [4] the layer whose expert copies went out last (-1: none)
+  int *s_flag = reinterpret_cast<int *>(s_red + NW);
+  int *s_sel = s_flag + 8;                                             // [32]
+  float *s_wt = reinterpret_cast<float *>(s_sel + 32);                 // [32]
+  float *s_wn = s_wt + 32;                                             // [32]
+  float *probs = s_wn + 32;                                            // [FWD_MAX_NE]
+  unsigned long long *s_best = reinterpret_cast<unsigned long long *>(probs + FWD_MAX_NE);   // [NW]
+  float *rrows = reinterpret_cast<float *>(smem + a.off_router);      // [nre][E]
+  float *rprod = reinterpret_cast<float *>(smem + a.off_rprod);       // [nre][8][E/8 + 4]
+  float *terms = reinterpret_cast<float *>(smem + a.off_terms);
+  int8_t *hq_qs = reinterpret_cast<int8_t *>(smem + a.off_hq);
+  int16_t *hq_bs = reinterpret_cast<int16_t *>(smem + a.off_hq + K * FF);
+  float *hq_d = reinterpret_cast<float *>(smem + a.off_hq + K * FF + 2 * (K * FF / 16));
+  float *xr = reinterpret_cast<float *>(smem + a.off_xr);
+  uint8_t *slots = smem + a.off_slots;     // gate/up rows of the chosen experts; the output matrix's stages
+  uint8_t *dslots = smem + a.off_dslots;   // down rows of the chosen experts; the attention scratch
+  const int GRP = a.n_head / a.n_kv;
+  float *qs_h = reinterpret_cast<float *>(dslots);                     // attention: [GROUP][hd] queries, then value sums
+  float *sc = qs_h + GRP * a.hd;                                       // attention: scores / weights of an item
+
+  const uint32_t uG = static_cast<uint32_t>(G), uc = static_cast<uint32_t>(c);
+  const int j0 = static_cast<int>(FF * uc / uG), j1 = static_cast<int>(FF * (uc + 1) / uG);
+  const int i0 = static_cast<int>(E * uc / uG), i1 = static_cast<int>(E * (uc + 1) / uG);
+  const int ngu = j1 - j0, nd = i1 - i0;
+  const int nre = c < NE ? (NE - c + G - 1) / G : 0;
+  const int RS = E / 8 + 4;
+  const int QKVR = a.n_q + 2 * a.n_kvw;
+  const int qr0 = static_cast<int>(static_cast<uint32_t>(QKVR) * uc / uG), qr1 = static_cast<int>(static_cast<uint32_t>(QKVR) * (uc + 1) / uG);
+
+  Grid grid{&st->sync[0], &st->err, &s_flag[0], uG, 0};
+  const int pos = st->pos, token = st->token;
+  trace_time(a.trace, 30);
+
+  if (tid == 0) {
+    for (int s = 0; s < K + 1 + HEAD_STAGES; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    // layer 0's router rows
+    if (nre > 0) {
+      mbar_arrive_expect_tx(&bars[K], static_cast<uint32_t>(nre) * E * 4u);
+      for (int m = 0; m < nre; ++m)
+        bulk_copy_g2s(rrows + static_cast<size_t>(m) * E, a.layers[0].router + static_cast<size_t>(c + m * G) * E, E * 4u, &bars[K]);
+    }
+    s_flag[1] = nre > 0;
+    s_flag[3] = 0;
+    s_flag[4] = -1;
+  }
+  // the token's embedding: this CTA's rows of x
+  bool ok = true;
+  if (token < 0 || token >= a.vocab || pos < 0 || pos >= a.ctx) {
+    if (tid == 0) set_error(&st->err, ERR_BAD_EXPERT);
+    ok = false;
+  }
+  if (ok) {
+    embed_row(a.tok_embd, token, E, xn);
+    __syncthreads();
+    for (int i = i0 + tid; i < i1; i += FWD_THREADS) a.x[i] = a.embed_scale != 1.0f ? __fmul_rn(xn[i], a.embed_scale) : xn[i];
+  }
+  ok = grid.sync() && ok;
+  const int nchunk = (pos + 1 + FWD_ATT_CHUNK - 1) / FWD_ATT_CHUNK;
+
+  for (int l = 0; l < a.n_layer && ok; ++l) {
+    const FwdLayer &Ly = a.layers[l];
+    const uint32_t par = static_cast<uint32_t>(l & 1);
+    trace_stamp(a.trace, 0);
+    // ---- A: attention input; this CTA's rows of [wq; wk; wv] --------------------------------------------------------
+    rmsnorm_to_smem(a.x, Ly.attn_norm, xn, E, a.eps, s_red);
+    q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
+    __syncthreads();
+    {
+      const int nq = a.n_q, nk = a.n_kvw;
+      gemv_rows(Ly.wq, nb, max(qr0, 0), min(qr1, nq), xq_qs, xq_d, xq_bs, [&](int r, float v) { __stcg(a.qkv + r, v); });
+      gemv_rows(Ly.wk, nb, max(qr0 - nq, 0), min(qr1 - nq, nk), xq_qs, xq_d, xq_bs, [&](int r, float v) { __stcg(a.qkv + nq + r, v); });
+      gemv_rows(Ly.wv, nb, max(qr0 - nq - nk, 0), min(qr1 - nq - nk, nk), xq_qs, xq_d, xq_bs, [&](int r, float v) { __stcg(a.qkv + nq + nk + r, v); });
+    }
+    trace_stamp(a.trace, 1);
+    if (!(ok = grid.sync())) break;
+    trace_stamp(a.trace, 2);
+
+    // ---- B1: attention scores, one item per (key/value head, 32 positions), spread over all CTAs -------------------------
+    const bool grouped = GRP >= 2 && GRP <= FWD_MAX_GROUP && pos + 1 >= 64;   // the reference's choice (c/src/forward.c:740-744)
+    {
+      const size_t cache_l = static_cast<size_t>(l) * a.ctx * a.n_kvw;
+      const float *qg = a.qkv, *kg = a.qkv + a.n_q, *vg = a.qkv + a.n_q + a.n_kvw;
+      // QK-norm over the whole vector (olmoe): the scales of q and of k
+      float qscale = 1.f, kscale = 1.f;
+      if (a.qk_mode == 1) {
+        double sq = 0.0, sk = 0.0;
+        for (int i = tid; i < a.n_q; i += FWD_THREADS) { const double v = __ldcg(qg + i); sq += v * v; }
+        for (int i = tid; i < a.n_kvw; i += FWD_THREADS) { const double v = __ldcg(kg + i); sk += v * v; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) { sq += __shfl_xor_sync(FULL, sq, o); sk += __shfl_xor_sync(FULL, sk, o); }
+        __syncthreads();
+        if (lane == 0) { s_red[warp] = sq; reinterpret_cast<double *>(terms)[warp] = sk; }
+        __syncthreads();
+        double tq = 0.0, tk = 0.0;
+        for (int k = 0; k < NW; ++k) { tq += s_red[k]; tk += reinterpret_cast<double *>(terms)[k]; }
+        qscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tq / a.n_q), a.eps)));
+        kscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tk / a.n_kvw), a.eps)));
+      }
+      constexpr int SB = 32;
+      const int nsb = (pos + 1 + SB - 1) / SB;
+      for (int item = c; item < a.n_kv * nsb; item += G) {
+        const int g = item / nsb, t0 = (item - g * nsb) * SB, n = min(SB, pos + 1 - t0);
+        const bool has_pos = t0 + n == pos + 1;
+        __syncthreads();   // the scratch of the previous item
+        // the group's query heads (warps 0..GRP-1) and, in the block of the new position, the key head (warp GRP):
+        // QK-norm, rotary embedding (c/src/forward.c:905-915); the new key and value into the cache (kv_put, :563-572)
+        for (int h = warp; h < GRP + (has_pos ? 1 : 0); h += NW) {
+          const bool isk = h == GRP;
+          const float *src = isk ? kg + g * hd : qg + (g * GRP + h) * hd;
+          float v[EPL];
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) v[e] = __ldcg(src + lane + 32 * e);
+          if (a.qk_mode == 2) {   // per head, one shared weight
+            double ss = 0.0;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) ss += static_cast<double>(v[e]) * v[e];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
+            const float sc1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(ss / hd), a.eps)));
+            const float *w = isk ? Ly.kn : Ly.qn;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], sc1), __ldg(w + lane + 32 * e));
+          } else if (a.qk_mode == 1) {   // over the whole projected vector
+            const float sc1 = isk ? kscale : qscale;
+            const float *w = isk ? Ly.kn + g * hd : Ly.qn + (g * GRP + h) * hd;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], sc1), __ldg(w + lane + 32 * e));
+          }
+          rope_warp<EPL>(v, hd, pos, a.rope_base, a.rope_pairs != 0);
+          if (isk) {
+            __half *kd = a.kc + cache_l + static_cast<size_t>(pos) * a.n_kvw + g * hd;
+            __half *vd = a.vc + cache_l + static_cast<size_t>(pos) * a.n_kvw + g * hd;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+              kd[lane + 32 * e] = __float2half_rn(v[e]);
+              vd[lane + 32 * e] = __float2half_rn(__ldcg(vg + g * hd + lane + 32 * e));
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) qs_h[h * hd + lane + 32 * e] = v[e];
+          }
+        }
+        __syncthreads();
+        // scores: the reference's dotf_h (c/src/forward.c:492-510: eight running sums over the head, combined
+        // ((0+1)+(2+3))+((4+5)+(6+7))) times the attention scale; two threads per (head, position), sums 0-3 and 4-7
+        const __half *kb = a.kc + cache_l + g * hd;
+        const int half = tid & 1;
+        for (int p = tid >> 1; p < GRP * SB; p += FWD_THREADS / 2) {
+          const int j = p / SB, tt = p - j * SB;
+          const bool valid = tt < n;
+          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+          if (valid) {
+            const __half *kr = kb + static_cast<size_t>(t0 + tt) * a.n_kvw + 4 * half;
+            const float *q = qs_h + j * hd + 4 * half;
+            for (int i = 0; i < hd; i += 8) {
+              const uint2 kk = __ldcg(reinterpret_cast<const uint2 *>(kr + i));
+              const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.x));
+              const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.y));
+              const float4 qq = *reinterpret_cast<const float4 *>(q + i);
+              s4[0] = __fadd_rn(s4[0], __fmul_rn(qq.x, k01.x));
+              s4[1] = __fadd_rn(s4[1], __fmul_rn(qq.y, k01.y));
+              s4[2] = __fadd_rn(s4[2], __fmul_rn(qq.z, k23.x));
+              s4[3] = __fadd_rn(s4[3], __fmul_rn(qq.w, k23.y));
+            }
+          }
+          const float part = __fadd_rn(__fadd_rn(s4[0], s4[1]), __fadd_rn(s4[2], s4[3]));
+          const float other = __shfl_xor_sync(FULL, part, 1);
+          if (valid && half == 0) __stcg(a.scores + static_cast<size_t>(g * GRP + j) * a.ctx + t0 + tt, __fmul_rn(__fadd_rn(part, other), a.attn_scale));
+        }
+      }
+    }
+    trace_stamp(a.trace, 3);
+    if (!(ok = grid.sync())) break;
+
+    // ---- B2: softmax and weighted values in the reference's order --------------------------------------------------------
+    // grouped (c/src/forward.c:665-737): an item per (key/value head, chunk of 256 positions): per query head the chunk's
+    // maximum m, e_t = expf(s_t - m), the sum l in position order, o = sum_t e_t v_t in position order; one chunk gives
+    // o * (1 / l) directly, more are merged below. plain (c/src/forward.c:584-627): an item per query head over every
+    // position: the maximum, e_t, their sum in order, then o = sum_t (e_t / sum) v_t in order.
+    {
+      const size_t cache_l = static_cast<size_t>(l) * a.ctx * a.n_kvw;
+      const int items = grouped ? a.n_kv * nchunk : a.n_head;
+      float *hm = reinterpret_cast<float *>(probs);   // [16] maxima, [16] sums
+      float *ob = qs_h;                               // [NH][hd] value sums
+      for (int item = c; item < items; item += G) {
+        const int g = grouped ? item / nchunk : item / GRP;
+        const int ch = grouped ? item - g * nchunk : 0;
+        const int j0 = grouped ? 0 : item - g * GRP, NH = grouped ? GRP : 1;
+        const int t0 = ch * FWD_ATT_CHUNK, n = grouped ? min(FWD_ATT_CHUNK, pos + 1 - t0) : pos + 1;
+        __syncthreads();
+        for (int i = tid; i < NH * n; i += FWD_THREADS) {
+          const int jj = i / n, t = i - jj * n;
+          sc[i] = __ldcg(a.scores + static_cast<size_t>(g * GRP + j0 + jj) * a.ctx + t0 + t);
+        }
+        __syncthreads();
+        for (int jj = warp; jj < NH; jj += NW) {   // a warp per head: the maximum, then e_t
+          float mx = -INFINITY;
+          for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sc[jj * n + t]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+          for (int t = lane; t < n; t += 32) sc[jj * n + t] = expf_cr(__fsub_rn(sc[jj * n + t], mx));
+          if (lane == 0) hm[jj] = mx;
+        }
+        __syncthreads();
+        if (tid < NH) {   // the sums, in position order
+          float sum = 0.f;
+          for (int t = 0; t < n; ++t) sum = __fadd_rn(sum, sc[tid * n + t]);
+          hm[16 + tid] = sum;
+        }
+        if (!grouped) {
+          __syncthreads();
+          for (int t = tid; t < n; t += FWD_THREADS) sc[t] = __fdiv_rn(sc[t], hm[16]);   // p_t = e_t / sum
+          __syncthreads();
+        }
+        // o[jj][i] = sum over t in order of w_t * v_t[i] (w = e, grouped; w = p, plain)
+        const __half *vb = a.vc + cache_l + g * hd;
+        for (int oi = tid; oi < NH * hd; oi += FWD_THREADS) {
+          const int jj = oi / hd, i = oi - jj * hd;
+          const float *w = sc + jj * n;
+          const __half *vcol = vb + i;
+          float o = 0.f;
+          int t = 0;
+          for (; t + 4 <= n; t += 4) {
+            float vv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) vv[u] = __half2float(__ldcg(vcol + static_cast<size_t>(t0 + t + u) * a.n_kvw));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) o = __fadd_rn(o, __fmul_rn(w[t + u], vv[u]));
+          }
+          for (; t < n; ++t) o = __fadd_rn(o, __fmul_rn(w[t], __half2float(__ldcg(vcol + static_cast<size_t>(t0 + t) * a.n_kvw))));
+          ob[oi] = o;
+        }
+        __syncthreads();
+        for (int oi = tid; oi < NH * hd; oi += FWD_THREADS) {
+          const int jj = oi / hd, i = oi - jj * hd, h = g * GRP + j0 + jj;
+          if (!grouped) {
+            __stcg(a.att + h * hd + i, ob[oi]);
+          } else if (nchunk == 1) {   // the merge of one chunk: weight expf(0) = 1, so o * (1 / l)
+            __stcg(a.att + h * hd + i, __fmul_rn(ob[oi], __fdiv_rn(1.0f, hm[16 + jj])));
+          } else {
+            float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + jj) * (2 + hd);
+            if (i == 0) { __stcg(pp, hm[jj]); __stcg(pp + 1, hm[16 + jj]); }
+            __stcg(pp + 2 + i, ob[oi]);
+          }
+        }
+      }
+    }
+    if (!(ok = grid.sync())) break;
+    if (grouped && nchunk > 1) {   // merge the chunks of each query head (c/src/forward.c:719-737)
+      for (int h = c; h < a.n_head; h += G) {
+        const int g = h / GRP, j = h - g * GRP;
+        for (int d = tid; d < hd; d += FWD_THREADS) {
+          float M = -INFINITY;
+          for (int ch = 0; ch < nchunk; ++ch) M = fmaxf(M, __ldcg(a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + j) * (2 + hd)));
+          float L = 0.f, o = 0.f;
+          for (int ch = 0; ch < nchunk; ++ch) {
+            const float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + j) * (2 + hd);
+            const float w = expf_cr(__fsub_rn(__ldcg(pp), M));
+            L = __fadd_rn(L, __fmul_rn(w, __ldcg(pp + 1)));
+            o = __fadd_rn(o, __fmul_rn(w, __ldcg(pp + 2 + d)));
+          }
+          __stcg(a.att + h * hd + d, __fmul_rn(o, __fdiv_rn(1.0f, L)));
+        }
+      }
+      if (!(ok = grid.sync())) break;
+    }
+    trace_stamp(a.trace, 4);
+
+    // ---- C: attention output: x += resid * wo att, this CTA's rows ------------------------------------------------------
+    q8k_quantize_global(a.att, a.n_q / 256, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
+    __syncthreads();
+    gemv_rows(Ly.wo, a.n_q / 256, i0, i1, xq_qs, xq_d, xq_bs,
+              [&](int r, float v) { a.x[r] = __fadd_rn(__ldcg(a.x + r), __fmul_rn(a.resid_scale, v)); });
+    trace_stamp(a.trace, 5);
+    if (!(ok = grid.sync())) break;
+    trace_stamp(a.trace, 6);
+
+    // ---- D: mixture of experts -------------------------------------------------------------------------------------------
+    rmsnorm_to_smem(a.x, Ly.ffn_norm, xn, E, a.eps, s_red);
+    for (int i = i0 + tid; i < i1; i += FWD_THREADS) xr[i - i0] = __ldcg(a.x + i);
+    if (s_flag[1] && !mbar_wait_bounded(&bars[K], par)) { set_error(&st->err, ERR_WAIT_COPY); }
+    for (int m = 0; m < nre; ++m)   // the router products, laid out for the strided sums
+      for (int i = tid; i < E; i += FWD_THREADS) rprod[(m * 8 + (i & 7)) * RS + (i >> 3)] = __fmul_rn(rrows[m * E + i], xn[i]);
+    __syncthreads();
+    if (tid == 0) {   // the next layer's router rows, while this one's are consumed from the products
+      s_flag[1] = 0;
+      if (nre > 0 && l + 1 < a.n_layer) {
+        s_flag[3] = (l + 1) & 1;
+        fence_proxy_async();   // the generic reads of rrows before the bulk copy's writes
+        mbar_arrive_expect_tx(&bars[K], static_cast<uint32_t>(nre) * E * 4u);
+        for (int m = 0; m < nre; ++m)
+          bulk_copy_g2s(rrows + static_cast<size_t>(m) * E, a.layers[l + 1].router + static_cast<size_t>(c + m * G) * E, E * 4u, &bars[K]);
+        s_flag[1] = 1;
+      }
+    }
+    if (warp == RW) {
+      if (nre > 0) {
+        const int grp = lane >> 3, l8 = lane & 7;
+        for (int m0 = 0; m0 < nre; m0 += 4) {
+          const int m = m0 + grp;
+          float s = 0.f;
+          if (m < nre) {
+            const float4 *p4 = reinterpret_cast<const float4 *>(rprod + (m * 8 + l8) * RS);
+            for (int q = 0; q < E / 32; q += 4) {
+              float4 v[4];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) v[t] = p4[q + t];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[t].x), v[t].y), v[t].z), v[t].w);
+            }
+          }
+          float p8[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) p8[k] = __shfl_sync(FULL, s, (lane & ~7) + k);
+          if (m < nre && l8 == 0)
+            a.rlogits[c + m * G] = __fadd_rn(__fadd_rn(__fadd_rn(p8[0], p8[1]), __fadd_rn(p8[2], p8[3])),
+                                             __fadd_rn(__fadd_rn(p8[4], p8[5]), __fadd_rn(p8[6], p8[7])));
+        }
+        __syncwarp();
+        if (lane == 0) red_release_add(&st->sync[1], static_cast<uint32_t>(nre));
+      }
+    } else {
+      q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, RW, lane, true);
+    }
+    trace_stamp(a.trace, 7);
+    if (warp == 0) {   // softmax (c/src/forward.c:954-958)
+      if (lane == 0) {
+        const uint32_t target = static_cast<uint32_t>(NE) * static_cast<uint32_t>(l + 1);
+        bool got = false;
+        for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
+          if (ld_acquire(&st->sync[1]) >= target) { got = true; break; }
+          if ((i & 127) == 127 && ld_volatile(&st->err)) break;
+          if (i > 4096) __nanosleep(64);
+        }
+        if (!got) set_error(&st->err, ERR_WAIT_ROUTER);
+        s_flag[2] = got;
+      }
+      __syncwarp();
+      if (s_flag[2]) {
+        constexpr int PER = FWD_MAX_NE / 32;
+        float lg[PER], ev[PER];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+          const int e = lane + 32 * j;
+          lg[j] = e < NE ? __ldcg(a.rlogits + e) : -INFINITY;
+          mx = fmaxf(mx, lg[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+        double part[PER];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+          ev[j] = lane + 32 * j < NE ? expf_cr(__fsub_rn(lg[j], mx)) : 0.f;
+          part[j] = static_cast<double>(ev[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int j = 0; j < PER; ++j) part[j] += __shfl_xor_sync(FULL, part[j], o);
+        double tot = 0.0;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) tot += part[j];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+          const int e = lane + 32 * j;
+          if (e < ((NE + 3) & ~3)) probs[e] = e < NE ? __double2float_rn(__ddiv_rn(static_cast<double>(ev[j]), tot)) : -1.0f;
+        }
+      }
+    }
+    __syncthreads();
+    if (!s_flag[2]) { ok = false; break; }
+    {   // top-k by rank counting, ties to the lower id (c/src/forward.c:975-980)
+      const int e = tid >> 2, part = tid & 3, n4 = (NE + 3) / 4, per = (n4 + 3) / 4;
+      const float pe = e < NE ? probs[e] : 0.f;
+      int rank = 0;
+      const float4 *p4 = reinterpret_cast<const float4 *>(probs);
+      for (int j = part * per; j < min(n4, (part + 1) * per); ++j) {
+        const float4 q = p4[j];
+        const int f = 4 * j;
+        rank += (q.x > pe || (q.x == pe && f < e)) + (q.y > pe || (q.y == pe && f + 1 < e)) +
+                (q.z > pe || (q.z == pe && f + 2 < e)) + (q.w > pe || (q.w == pe && f + 3 < e));
+      }
+      rank += __shfl_xor_sync(FULL, rank, 1);
+      rank += __shfl_xor_sync(FULL, rank, 2);
+      if (e < NE && part == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = pe; }
+    }
+    __syncthreads();
+    if (tid < K) {   // renormalisation (c/src/forward.c:984)
+      float w = s_wt[tid];
+      if (a.norm_topk) {
+        float z = 0.f;
+        for (int k = 0; k < K; ++k) z = __fadd_rn(z, s_wt[k]);
+        if (z > 0.f) w = __fdiv_rn(w, z);
+      }
+      s_wn[tid] = w;
+      if (c == 0) {
+        a.route_sel[l * K + tid] = s_sel[tid];
+        a.route_wt[l * K + tid] = w;
+      }
+    }
+    trace_stamp(a.trace, 8);
+    // this CTA's share of every chosen expert: gate/up rows into slots, down rows into dslots
+    auto gu_src = [&](int k, int q) -> const uint8_t * {
+      const size_t e = static_cast<size_t>(s_sel[k]);
+      return q == 0 ? Ly.gate + e * Ly.gate_slab + static_cast<size_t>(j0) * a.grb : Ly.up + e * Ly.up_slab + static_cast<size_t>(j0) * a.grb;
+    };
+    auto dn_src = [&](int k) -> const uint8_t * { return Ly.down + static_cast<size_t>(s_sel[k]) * Ly.down_slab + static_cast<size_t>(i0) * a.drb; };
+    auto lo16 = [](const void *p) { return static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 15u); };
+    if (tid == 0) s_flag[4] = l;   // read at the exit only
+    if (lane == 0 && warp < K) {
+      const int k = warp;
+      uint8_t *gs = slots + static_cast<size_t>(k) * a.slot_bytes, *ds = dslots + static_cast<size_t>(k) * a.dslot_bytes;
+      const uint8_t *src[3] = {gu_src(k, 0), gu_src(k, 1), dn_src(k)};
+      uint8_t *dst[3] = {gs, gs + a.gseg, ds};
+      const uint32_t len[3] = {static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(nd) * a.drb};
+      uint32_t n16[3], total = 0;
+      for (int q = 0; q < 3; ++q) { n16[q] = len[q] ? (lo16(src[q]) + len[q] + 15u) & ~15u : 0u; total += n16[q]; }
+      fence_proxy_async();   // the generic accesses of these buffers (attention scratch, last layer's rows) come first
+      mbar_arrive_expect_tx(&bars[k], total);
+      for (int q = 0; q < 3; ++q)
+        if (n16[q]) bulk_copy_g2s(dst[q], src[q] - lo16(src[q]), n16[q], &bars[k]);
+    }
+    if (tid == 32 * K && l + 1 < a.n_layer) {   // the next layer's dense rows of this CTA into L2
+      const FwdLayer &Nx = a.layers[l + 1];
+      const FwdMat mats[3] = {Nx.wq, Nx.wk, Nx.wv};
+      const int lo[3] = {0, a.n_q, a.n_q + a.n_kvw}, cnt[3] = {a.n_q, a.n_kvw, a.n_kvw};
+      for (int q = 0; q < 3; ++q) {
+        const int r0 = max(qr0 - lo[q], 0), r1 = min(qr1 - lo[q], cnt[q]);
+        if (r1 > r0) {
+          const uintptr_t b = reinterpret_cast<uintptr_t>(mats[q].p + static_cast<size_t>(r0) * mats[q].rb) & ~uintptr_t(15);
+          const uintptr_t e = (reinterpret_cast<uintptr_t>(mats[q].p + static_cast<size_t>(r1) * mats[q].rb) + 15) & ~uintptr_t(15);
+          prefetch_l2(reinterpret_cast<const void *>(b), static_cast<uint32_t>(e - b));
+        }
+      }
+      if (nd > 0) {
+        const uintptr_t b = reinterpret_cast<uintptr_t>(Nx.wo.p + static_cast<size_t>(i0) * Nx.wo.rb) & ~uintptr_t(15);
+        const uintptr_t e = (reinterpret_cast<uintptr_t>(Nx.wo.p + static_cast<size_t>(i1) * Nx.wo.rb) + 15) & ~uintptr_t(15);
+        prefetch_l2(reinterpret_cast<const void *>(b), static_cast<uint32_t>(e - b));
+      }
+    }
+    // gate and up rows: a group of lanes per (expert, row), one lane per block
+    {
+      const int GL = lanes_for(nb);
+      const int lg = lane & (GL - 1), gpw = 32 / GL, ngroups = NW * gpw, gid = warp * gpw + lane / GL;
+      const int tasks = K * ngu, base = lane - lg;
+      const bool has_blk = lg < nb;
+      const SmemAct act{xq_qs, xq_bs, xq_d};
+      int waited = -1;
+      for (int t0 = 0; t0 < tasks; t0 += ngroups) {
+        const int t = t0 + gid;
+        const bool valid = t < tasks;
+        const int k = valid ? t / ngu : 0, j = valid ? t - k * ngu : 0;
+        float tg = 0.f, tu = 0.f;
+        if (valid) {
+          while (waited < k) {
+            ++waited;
+            if (!mbar_wait_bounded(&bars[waited], par)) set_error(&st->err, ERR_WAIT_COPY);
+          }
+          if (has_blk) {
+            const uint8_t *gs = slots + static_cast<size_t>(k) * a.slot_bytes;
+#pragma unroll 1
+            for (int m = 0; m < 2; ++m) {
+              const uint8_t *row = gs + m * a.gseg + lo16(gu_src(k, m)) + static_cast<uint32_t>(j) * a.grb;
+              const float v = kq_block_s(Ly.gate_type, row, lg, act, lg);
+              if (m == 0) tg = v; else tu = v;
+            }
+          }
+        }
+        float sg = 0.f, su = 0.f;
+        for (int b = 0; b < nb; ++b) {
+          sg = __fadd_rn(sg, __shfl_sync(FULL, tg, base + b));
+          su = __fadd_rn(su, __shfl_sync(FULL, tu, base + b));
+        }
+        if (valid && lg == 0) __stcg(a.hg + static_cast<size_t>(k) * FF + j0 + j, silu_mul(sg, su));
+      }
+    }
+    trace_stamp(a.trace, 9);
+    if (!(ok = grid.sync())) break;
+    trace_stamp(a.trace, 10);
+    // every expert's hg as Q8_K blocks; this CTA's down rows; the combine in rank order and the residual
+    q8k_quantize_global(a.hg, K * FF / 256, hq_qs, hq_d, hq_bs, warp, NW, lane, true);
+    for (int k = 0; k < K; ++k)
+      if (!mbar_wait_bounded(&bars[k], par)) set_error(&st->err, ERR_WAIT_COPY);
+    __syncthreads();
+    {
+      const int C = K * nbd, combo = tid % C, grp = tid / C, ngrp = FWD_THREADS / C;
+      if (grp < ngrp) {
+        const int blk = combo / K, k = combo - blk * K;
+        const SmemAct dact{hq_qs, hq_bs, hq_d};   // expert k's hg is blocks k * nbd ...
+        const uint8_t *drows = dslots + static_cast<size_t>(k) * a.dslot_bytes + lo16(dn_src(k));
+        for (int r = grp; r < nd; r += ngrp) terms[(r * K + k) * nbd + blk] = kq_block_s(Ly.down_type, drows + static_cast<size_t>(r) * a.drb, blk, dact, k * nbd + blk);
+      }
+    }
+    __syncthreads();
+    for (int r = tid; r < nd; r += FWD_THREADS) {
+      float moe = 0.f;
+      for (int k = 0; k < K; ++k) {
+        float h = 0.f;
+        for (int b = 0; b < nbd; ++b) h = __fadd_rn(h, terms[(r * K + k) * nbd + b]);
+        moe = __fadd_rn(moe, __fmul_rn(s_wn[k], h));
+      }
+      a.x[i0 + r] = __fadd_rn(xr[r], __fmul_rn(a.resid_scale, moe));
+    }
+    trace_stamp(a.trace, 11);
+    if (!(ok = grid.sync())) break;
+  }
+
+  // ---- output norm, this CTA's rows of the output matrix, arg-max ------------------------------------------------------------
+  if (ok) {
+    trace_stamp(a.trace, 12);
+    rmsnorm_to_smem(a.x, a.out_norm, xn, E, a.eps, s_red);
+    q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
+    __syncthreads();
+    const int v0 = static_cast<int>(static_cast<uint64_t>(a.vocab) * uc / uG), v1 = static_cast<int>(static_cast<uint64_t>(a.vocab) * (uc + 1) / uG);
+    const int nrows = v1 - v0, nst = (nrows + HEAD_ROWS - 1) / HEAD_ROWS;
+    // a stage holds HEAD_ROWS rows copied from the 16-byte boundary at or below their start (rows of a Q6_K matrix may
+    // start anywhere), so it is 32 bytes longer than the rows and they begin lo(s) bytes into it
+    const uint32_t rb = a.output.rb, stage_bytes = (HEAD_ROWS * rb + 32 + 15) & ~15u;
+    uint64_t *hb = bars + K + 1;
+    auto stage_lo = [&](int s) { return static_cast<uint32_t>(reinterpret_cast<uintptr_t>(a.output.p + static_cast<size_t>(v0 + s * HEAD_ROWS) * rb) & 15u); };
+    auto issue = [&](int s) {   // stage s of this CTA's rows into buffer s % HEAD_STAGES
+      const int r0 = v0 + s * HEAD_ROWS, cnt = min(HEAD_ROWS, v1 - r0);
+      const uint8_t *src = a.output.p + static_cast<size_t>(r0) * rb;
+      const uint32_t lo = stage_lo(s), n16 = (lo + static_cast<uint32_t>(cnt) * rb + 15u) & ~15u;
+      uint64_t *b = &hb[s % HEAD_STAGES];
+      fence_proxy_async();
+      mbar_arrive_expect_tx(b, n16);
+      bulk_copy_g2s(slots + static_cast<size_t>(s % HEAD_STAGES) * stage_bytes, src - lo, n16, b);
+    };
+    if (tid == 0)
+      for (int s = 0; s < min(nst, HEAD_STAGES); ++s) issue(s);
+    const int GL = lanes_for(nb), lg = lane & (GL - 1), gpw = 32 / GL, gid = warp * gpw + lane / GL, base = lane - lg;
+    const bool has_blk = lg < nb;
+    const SmemAct act{xq_qs, xq_bs, xq_d};
+    unsigned long long best = 0;
+    for (int s = 0; s < nst; ++s) {
+      const uint32_t hpar = static_cast<uint32_t>((s / HEAD_STAGES) & 1);
+      if (!mbar_wait_bounded(&hb[s % HEAD_STAGES], hpar)) set_error(&st->err, ERR_WAIT_COPY);
+      const int r0 = v0 + s * HEAD_ROWS, cnt = min(HEAD_ROWS, v1 - r0);
+      const uint8_t *buf = slots + static_cast<size_t>(s % HEAD_STAGES) * stage_bytes + stage_lo(s);
+      // HEAD_ROWS rows, a group of lanes each (NW * gpw >= HEAD_ROWS groups)
+      const bool valid = gid < cnt;
+      float t = 0.f;
+      if (valid && has_blk) t = kq_block_s(a.output.type, buf + static_cast<size_t>(gid) * rb, lg, act, lg);
+      float sum = 0.f;
+      for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, __shfl_sync(FULL, t, base + b));
+      if (valid && lg == 0) {
+        const float v = a.logit_scale != 1.0f ? __fdiv_rn(sum, a.logit_scale) : sum;
+        __stcg(a.logits + r0 + gid, v);
+        if (v == v) best = max(best, argmax_key(v, r0 + gid));
+      }
+      __syncthreads();   // the buffer is free again
+      if (tid == 0 && s + HEAD_STAGES < nst) issue(s + HEAD_STAGES);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(FULL, best, o));
+    if (lane == 0) s_best[warp] = best;
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < NW; ++w) best = max(best, s_best[w]);
+      best = max(best, s_best[0]);
+      atomicMax(&st->best, best);
+    }
+    trace_stamp(a.trace, 13);
+  }
+
+  // ---- exit: copies in flight land first; the last CTA out advances the sequence and resets the counters ----------------------
+  __syncthreads();
+  if (tid == 0) {
+    if (s_flag[1]) mbar_wait_bounded(&bars[K], static_cast<uint32_t>(s_flag[3]));   // an unconsumed router copy
+    if (s_flag[4] >= 0)   // the last layer's expert copies (waited already unless a wait gave up)
+      for (int k = 0; k < K; ++k) mbar_wait_bounded(&bars[k], static_cast<uint32_t>(s_flag[4] & 1));
+    __threadfence();
+    const uint32_t prev = atomicAdd(&st->sync[2], 1u);
+    if (prev == uG - 1) {
+      __threadfence();
+      if (!ld_volatile(&st->err)) {
+        const unsigned long long b = atomicAdd(&st->best, 0ull);
+        const int id = static_cast<int>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffull));
+        st->next = id;
+        a.gen_out[pos] = id;
+        if (a.feed) st->token = id;
+        st->pos = pos + 1;
+      }
+      st->best = 0;
+      atomicExch(&st->sync[0], 0u);
+      atomicExch(&st->sync[1], 0u);
+      atomicExch(&st->sync[2], 0u);
+      __threadfence();
+    }
+  }
+  trace_time(a.trace, 31);
+}
+
+}  // namespace
+
+cudaError_t fwd_allow_smem(int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(fwd_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(fwd_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(fwd_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e;
+}
+
+cudaError_t fwd_launch(const FwdArgs &a, int ctas, cudaStream_t stream) {
+  void (*fn)(FwdArgs) = a.hd == 64 ? fwd_kernel<2> : a.hd == 128 ? fwd_kernel<4> : a.hd == 256 ? fwd_kernel<8> : nullptr;
+  if (!fn) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(ctas);
+  cfg.blockDim = dim3(FWD_THREADS);
+  cfg.dynamicSmemBytes = a.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+}  // namespace clb

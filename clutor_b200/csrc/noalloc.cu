@@ -63,7 +63,7 @@ extern "C" int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x
       if (e != cudaSuccess) { errf(err, errlen, "cannot locate the scratch array on device %d: %s", dev, cudaGetErrorString(e)); return 1; }
       if (cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
           cudaDeviceGetAttribute(&s.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-          cudaFuncSetAttribute(moe_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, s.max_smem) != cudaSuccess) {
+          decode_allow_smem(s.max_smem) != cudaSuccess) {
         errf(err, errlen, "cannot set up device %d", dev);
         return 1;
       }
@@ -115,7 +115,7 @@ extern "C" int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, moe_decode_kernel, a);
+  e = cudaLaunchKernelEx(&cfg, decode_kernel_for(a.gate_type, a.down_type), a);
   if (e != cudaSuccess) { errf(err, errlen, "launching the one-token kernel: %s", cudaGetErrorString(e)); return 1; }
   e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) { errf(err, errlen, "running the one-token kernel: %s", cudaGetErrorString(e)); return 1; }

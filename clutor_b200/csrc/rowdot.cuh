@@ -334,6 +334,88 @@ CLB_DEV float kq_block(uint32_t type, const uint8_t *row, int blk, const BlockAc
   return type == T_Q4_K ? q4k_block(row + 144 * blk, a) : q6k_block(row + 210 * blk, a);
 }
 
+// The same two block terms with the activation block read from shared memory as it is needed (a swizzled Q8_K array:
+// q8k_chunk_off) instead of held in registers: for kernels that use a block for one or two rows only, where 81 registers
+// of activations would cost more than the shared-memory reads.
+struct SmemAct {
+  const int8_t *qs;      // swizzled values
+  const int16_t *bsums;
+  const float *dd;
+};
+CLB_DEV int4 act_chunk(const SmemAct &a, int blk, int j) {
+  return *reinterpret_cast<const int4 *>(a.qs + q8k_chunk_off(blk, j, true));
+}
+CLB_DEV float q4k_block_s(const uint8_t *bp, const SmemAct &a, int blk) {
+  const uint32_t dm = lds_u32(bp), w0 = lds_u32(bp + 4), w1 = lds_u32(bp + 8), w2 = lds_u32(bp + 12);
+  const uint32_t scA = w0 & 0x3f3f3f3fu, mnA = w1 & 0x3f3f3f3fu;
+  const uint32_t scB = (w2 & 0x0f0f0f0fu) | (((w0 >> 6) & 0x03030303u) << 4);
+  const uint32_t mnB = ((w2 >> 4) & 0x0f0f0f0fu) | (((w1 >> 6) & 0x03030303u) << 4);
+  int sumi = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint4 x0 = reinterpret_cast<const uint4 *>(bp + 16 + 32 * g)[0];
+    const uint4 x1 = reinterpret_cast<const uint4 *>(bp + 16 + 32 * g)[1];
+    const int4 c0 = act_chunk(a, blk, 4 * g), c1 = act_chunk(a, blk, 4 * g + 1), c2 = act_chunk(a, blk, 4 * g + 2),
+               c3 = act_chunk(a, blk, 4 * g + 3);
+    const int ql[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w}, qh[8] = {c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+    const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    int lo = 0, hi = 0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      lo = __dp4a(static_cast<int>(w[t] & 0x0f0f0f0fu), ql[t], lo);
+      hi = __dp4a(static_cast<int>((w[t] >> 4) & 0x0f0f0f0fu), qh[t], hi);
+    }
+    const uint32_t sw = g < 2 ? scA : scB;
+    sumi += byte_of(sw, 2 * (g & 1)) * lo + byte_of(sw, 2 * (g & 1) + 1) * hi;
+  }
+  const int16_t *b16 = a.bsums + 16 * blk;
+  int summs = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) summs += byte_of(j < 4 ? mnA : mnB, j & 3) * (b16[2 * j] + b16[2 * j + 1]);
+  const float d = f16_bits_to_f32(static_cast<uint16_t>(dm & 0xffffu)), dmin = f16_bits_to_f32(static_cast<uint16_t>(dm >> 16));
+  return __fmul_rn(a.dd[blk], __fsub_rn(__fmul_rn(d, static_cast<float>(sumi)), __fmul_rn(dmin, static_cast<float>(summs))));
+}
+CLB_DEV float q6k_block_s(const uint8_t *bp, const SmemAct &a, int blk) {
+  const int8_t *sc = reinterpret_cast<const int8_t *>(bp + 192);
+  const int16_t *b16 = a.bsums + 16 * blk;
+  int sumi = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    int dot[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) dot[g] = 0;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {   // t = 4 * half .. 4 * half + 3: one 16-group of each 32-element run
+      const int4 a0 = act_chunk(a, blk, 8 * h + half), a1 = act_chunk(a, blk, 8 * h + 2 + half),
+                 a2 = act_chunk(a, blk, 8 * h + 4 + half), a3 = act_chunk(a, blk, 8 * h + 6 + half);
+      const int q0[4] = {a0.x, a0.y, a0.z, a0.w}, q1[4] = {a1.x, a1.y, a1.z, a1.w}, q2[4] = {a2.x, a2.y, a2.z, a2.w},
+                q3[4] = {a3.x, a3.y, a3.z, a3.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = 4 * half + u;
+        const uint32_t L0 = lds_u32_unaligned(bp + 64 * h + 4 * t), L1 = lds_u32_unaligned(bp + 64 * h + 32 + 4 * t);
+        const uint32_t H = lds_u32_unaligned(bp + 128 + 32 * h + 4 * t);
+        const int v0 = static_cast<int>((L0 & 0x0f0f0f0fu) | ((H & 0x03030303u) << 4));
+        const int v1 = static_cast<int>((L1 & 0x0f0f0f0fu) | (((H >> 2) & 0x03030303u) << 4));
+        const int v2 = static_cast<int>(((L0 >> 4) & 0x0f0f0f0fu) | (((H >> 4) & 0x03030303u) << 4));
+        const int v3 = static_cast<int>(((L1 >> 4) & 0x0f0f0f0fu) | (((H >> 6) & 0x03030303u) << 4));
+        dot[half] = __dp4a(v0, q0[u], dot[half]);
+        dot[2 + half] = __dp4a(v1, q1[u], dot[2 + half]);
+        dot[4 + half] = __dp4a(v2, q2[u], dot[4 + half]);
+        dot[6 + half] = __dp4a(v3, q3[u], dot[6 + half]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < 8; ++g) sumi += static_cast<int>(sc[8 * h + g]) * (dot[g] - 32 * b16[8 * h + g]);
+  }
+  const float d = f16_bits_to_f32(lds_u16(bp + 208));
+  return __fmul_rn(__fmul_rn(d, a.dd[blk]), static_cast<float>(sumi));
+}
+// Weight block blk of `row` times activation block ablk (the swizzle key of the array: its index in the whole array).
+CLB_DEV float kq_block_s(uint32_t type, const uint8_t *row, int blk, const SmemAct &a, int ablk) {
+  return type == T_Q4_K ? q4k_block_s(row + 144 * blk, a, ablk) : q6k_block_s(row + 210 * blk, a, ablk);
+}
+
 // Q8_K quantization of nblocks 256-blocks of floats in global memory (written by other CTAs; read through L2) into shared
 // qs/d/bsums. Each warp takes blocks warp, warp + nwarps, ...; a lane issues the loads of up to four blocks before the first
 // reduction, so their round trips overlap.

@@ -111,6 +111,11 @@ int clb200_ep_experts(clb200_ctx *c, int layer, int T, const int8_t *xq_qs, cons
 int clb200_status(clb200_ctx *c, char *err, size_t errlen);
 /* Bytes of device memory the context holds for layers and scratch. */
 uint64_t clb200_device_bytes(const clb200_ctx *c);
+/* Phase trace of the one-token kernel, the device-side counterpart of the reference's CLUTOR_PROFILE phase clock
+ * (c/src/forward.c:360-376): with dev_buf set (device memory, 32 uint64 per SM), every later one-token launch has thread 0 of
+ * each CTA write the SM cycle counter at its phase boundaries (entries 0-29 of its row) and the global nanosecond timer at
+ * entry and exit (entries 30, 31). NULL turns it off. */
+void clb200_set_trace(clb200_ctx *c, void *dev_buf);
 
 /* ---- the expert cache policy (host) -------------------------------------------------------------------------------------- */
 /* Which expert occupies which HBM slot: the reference's cl_cache (c/src/cache.h:11-47, c/src/cache.c), same decisions, same
@@ -207,6 +212,38 @@ typedef struct {
  * Weights are uploaded on first use, keyed by host pointer. The seam has no error channel: on a device error the backend
  * prints the error to stderr and aborts, rather than returning wrong numbers. */
 const clb200_backend_t *clb200_backend(void);
+
+/* ---- whole models: the forward pass of c/src/forward.h ------------------------------------------------------------------- */
+/* A mixture-of-experts GGUF model (architectures olmoe, qwen3moe, qwen3vlmoe, granitemoe) uploaded to HBM in its own block
+ * format, with a half-precision key/value cache of n_ctx positions. One token step is one persistent kernel: attention
+ * (QK-norm, rotary embedding, the key/value cache), the MoE block of clb200_moe_ffn, the output matrix and the greedy
+ * arg-max. Attention matrices, experts and the output matrix must be Q4_K or Q6_K; the embedding Q4_K, Q6_K, Q8_0 or F32. */
+typedef struct clb200_model clb200_model;
+typedef struct {
+  char arch[16];
+  int n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff_exp, n_expert, n_used, n_vocab, n_ctx;
+  uint64_t device_bytes;   /* HBM the model holds: weights, cache, scratch */
+  uint32_t smem_bytes;     /* shared memory per CTA of the step */
+} clb200_model_info;
+/* cl_fwd_open (forward.h:114): from a file path, or a GGUF image in host memory. n_ctx <= 0: 512 (capped at the model's). */
+clb200_model *clb200_model_open(clb200_ctx *c, const char *path, int n_ctx, char *err, size_t errlen);
+clb200_model *clb200_model_open_image(clb200_ctx *c, const void *image, size_t bytes, int n_ctx, char *err, size_t errlen);
+void clb200_model_close(clb200_model *m);                          /* cl_fwd_close (forward.h:115) */
+void clb200_model_reset(clb200_model *m);                          /* cl_fwd_reset (forward.h:116): back to position 0 */
+int clb200_model_pos(const clb200_model *m);                       /* the reference's f->pos */
+int clb200_model_get_info(const clb200_model *m, clb200_model_info *out);
+/* cl_fwd_step (forward.h:117-118): runs `token` at the current position and advances it. logits (host, n_vocab floats),
+ * next_token (the arg-max, lowest id on ties), sel_out / wt_out (host, n_layer * n_used: each layer's experts in rank order
+ * and their weights, the reference's cl_fwd_route) may each be NULL. Returns 0, or 1 with err set. */
+int clb200_model_step(clb200_model *m, int token, float *logits, int *next_token, int *sel_out, float *wt_out, char *err,
+                      size_t errlen);
+/* Greedy generation on the device, the loop of the reference's generate command (c/src/main.c:342-360) without the host:
+ * feeds `token`, then each step's arg-max, n times; tokens_out (host, n) receives the n chosen tokens. */
+int clb200_model_generate(clb200_model *m, int token, int n, int *tokens_out, char *err, size_t errlen);
+/* The same n steps queued on `stream` (NULL: the model's own) without waiting, after one clb200_model_generate; read the
+ * tokens of positions [start, start + n) afterwards with clb200_model_tokens. */
+int clb200_model_generate_async(clb200_model *m, int token, int n, void *stream, char *err, size_t errlen);
+int clb200_model_tokens(clb200_model *m, int start, int n, int *tokens_out, char *err, size_t errlen);
 
 #ifdef __cplusplus
 }

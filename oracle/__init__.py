@@ -273,3 +273,50 @@ def route(logits: np.ndarray, K: int, norm_topk: int = 1, which: str = "oracle")
     fn = oracle_lib().orc_route if which == "oracle" else ref_lib().ref_route
     fn(C.c_void_p(_ptr(rl)), rl.size, K, norm_topk, C.c_void_p(_ptr(sel)), C.c_void_p(_ptr(wt)))
     return sel, wt
+
+
+class RefModel:
+    """The reference's whole forward pass (cl_fwd_open / cl_fwd_step, c/src/forward.h:114-118, compiled into
+    _ref/libclref.so) on a GGUF file: the checker for the device step."""
+
+    def __init__(self, path: str, n_ctx: int):
+        L = ref_lib()
+        L.ref_fwd_open.restype = C.c_void_p
+        L.ref_fwd_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]
+        L.ref_fwd_info.argtypes = [C.c_void_p, C.c_void_p]
+        L.ref_fwd_step.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.ref_fwd_close.argtypes = [C.c_void_p]
+        self.L = L
+        self.err = C.create_string_buffer(512)
+        self.h = L.ref_fwd_open(path.encode(), n_ctx, self.err, 512)
+        if not self.h:
+            raise RuntimeError(self.err.value.decode())
+        info = (C.c_int * 8)()
+        L.ref_fwd_info(self.h, info)
+        self.n_layer, self.n_embd, self.n_vocab, self.n_expert, self.n_used, self.n_ctx, _, self.head_dim = list(info)
+
+    def step(self, token: int):
+        """-> (logits [n_vocab] f32, sel [n_layer, n_used] int32, wt [n_layer, n_used] f32)"""
+        logits = np.zeros(self.n_vocab, np.float32)
+        sel = np.zeros((self.n_layer, self.n_used), np.int32)
+        wt = np.zeros((self.n_layer, self.n_used), np.float32)
+        if self.L.ref_fwd_step(self.h, token, logits.ctypes.data, sel.ctypes.data, wt.ctypes.data, self.err, 512):
+            raise RuntimeError(self.err.value.decode())
+        return logits, sel, wt
+
+    def greedy(self, first: int, n: int) -> list[int]:
+        """The reference's generate loop (c/src/main.c:342-360) on ids: feed `first`, then each arg-max, n tokens."""
+        out, cur = [], first
+        for _ in range(n):
+            logits, _, _ = self.step(cur)
+            cur = int(np.argmax(logits))   # first maximum: the reference's strict > scan
+            out.append(cur)
+        return out
+
+    def close(self) -> None:
+        if self.h:
+            self.L.ref_fwd_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()

@@ -122,3 +122,29 @@ int ref_moe_ffn(const ref_layer *L, float *x, int T, int *sel, float *wt) {
   if (T < 1 || T > CL_PS_B || L->K > 64 || L->NE > 4096) return 1;
   return T == 1 ? decode_one(L, x, sel, wt) : batch(L, x, T, sel, wt);
 }
+
+/* ---- the reference's whole forward pass (c/src/forward.h:114-118), for the device step's parity checks ------------------ */
+/* Opens a GGUF model with the reference's cl_fwd_open (mapped, no streaming); NULL with err set on failure. */
+void *ref_fwd_open(const char *path, int n_ctx, char *err, size_t errlen) {
+  cl_fwd *f = calloc(1, sizeof *f);
+  if (!f) return NULL;
+  if (cl_fwd_open(f, path, n_ctx, NULL, err, errlen)) { free(f); return NULL; }
+  return f;
+}
+/* info[0..7] = n_layer, n_embd, n_vocab, n_expert, n_used, n_ctx_max, pos, head_dim */
+void ref_fwd_info(void *h, int *info) {
+  const cl_fwd *f = h;
+  info[0] = f->n_layer; info[1] = f->n_embd; info[2] = f->n_vocab; info[3] = f->n_expert; info[4] = f->n_used;
+  info[5] = f->n_ctx_max; info[6] = f->pos; info[7] = f->head_dim;
+}
+/* cl_fwd_step: logits [n_vocab]; sel / wt [n_layer * n_used] (may be NULL). */
+int ref_fwd_step(void *h, int token, float *logits, int *sel, float *wt, char *err, size_t errlen) {
+  cl_fwd *f = h;
+  cl_fwd_route rt = {sel, wt, NULL, f->n_layer, f->n_used};
+  return cl_fwd_step(f, token, logits, sel && wt ? &rt : NULL, err, errlen);
+}
+void ref_fwd_close(void *h) {
+  if (!h) return;
+  cl_fwd_close(h);
+  free(h);
+}
