@@ -37,6 +37,10 @@ WORKLOADS = {
     "ep235b": dict(T=2048, gate="q4_k", down="q4_k", E=4096, FF=1536, NE=128, K=8, layers=2,
                    desc="Qwen3-235B-A22B MoE layer, prefill 2048 tokens per GPU, Q4_K experts, expert-parallel over the GPUs "
                         "(NCCL all-to-all dispatch and combine)"),
+    "model": dict(T=1, gate="q4_k", down="q6_k", E=2048, FF=768, NE=128, K=8, layers=48,
+                  desc="Qwen3-30B-A3B whole model, greedy decode at batch 1 from a 1-token prompt: 48 layers, GQA 32/4 heads "
+                       "x 128, QK-norm, NEOX rotary (base 1e6), fp16 key/value cache, Q4_K_M mix (Q4_K embedding, attn_q/k/o and "
+                       "gate/up experts; Q6_K attn_v, down experts and the 151,936-row output matrix)"),
     "cache": dict(T=1, gate="q4_k", down="q4_k", E=2048, FF=768, NE=128, K=8, layers=48, budget=0.4, locality=1.78,
                   desc="expert-cache stress: 48 Qwen3-30B-A3B MoE layers (Q4_K), HBM cache of 40% of expert bytes, the rest "
                        "in pinned host memory, Zipf(1.1)-skewed routing with topics drifting every 16 tokens"),
@@ -152,8 +156,59 @@ def cpu_reference(wl: dict, seconds: float, threads: int | None = None) -> dict:
                       f"reference built from its sources (oracle/_ref)", "ms_per_call": 1000 * dt / n}
 
 
+MODEL_METRIC = "full-model decode tokens/s (Qwen3-30B-A3B, Q4_K_M mix, batch 1)"
+SHM_MODEL = "/dev/shm/clutor_b200_qwen3_30b_a3b.gguf"
+
+
+def model_reference(image, n_ctx: int, seconds: float, threads: int | None = None) -> dict:
+    """The reference engine's own forward pass (cl_fwd_open / cl_fwd_step, oracle/_ref) on the same synthetic model, from a
+    GGUF file in shared memory (the reference opens models by path): greedy steps from a 1-token prompt for about
+    `seconds`, all host threads (the reference caps its pool at 16)."""
+    import numpy as np
+
+    import oracle
+    if not oracle.ref_available():
+        oracle.build()
+    nthreads = threads or min(os.cpu_count() or 1, 16)
+    oracle.set_ref_threads(nthreads)
+    image.tofile(SHM_MODEL)
+    try:
+        ref = oracle.RefModel(SHM_MODEL, n_ctx)
+        tok, n = 1, 0
+        logits, _, _ = ref.step(tok)        # the first step pages the weights in
+        tok = int(np.argmax(logits))
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < seconds and n < n_ctx - 2:
+            logits, _, _ = ref.step(tok)
+            tok = int(np.argmax(logits))
+            n += 1
+        dt = time.perf_counter() - t0
+        ref.close()
+    finally:
+        os.unlink(SHM_MODEL)
+    path = oracle.ref_lib().cl_quant_path().decode()
+    return {"value": n / dt, "unit": "tokens/s", "cores": nthreads, "kind": "reference",
+            "sample": f"{n} greedy decode steps (positions 1..{n}) of the whole model in {dt:.1f} s on {nthreads} threads, ISA "
+                      f"path {path}; the reference's cl_fwd_step built from its sources (oracle/_ref), model mapped from "
+                      f"/dev/shm", "ms_per_token": 1000 * dt / max(n, 1)}
+
+
 def run_reference_arm(a, wl, rank: int) -> None:
     if rank != 0:
+        return
+    if a.workload == "model":
+        from clutor_b200 import synth_model as sm
+        image = sm.image(sm.QWEN3_30B_A3B, seed=1)
+        secs = max(5.0, min(60.0, 2.0 * a.steps))
+        cb = model_reference(image, a.warmup + a.steps + 8, secs)
+        line = {"impl": "reference", "metric": MODEL_METRIC, "value": round(cb["value"], 4), "unit": "tokens/s",
+                "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(cb["ms_per_token"], 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate; fp32 attention", "data": "synthetic (seeded random GGUF)",
+                "config": {"workload": wl["desc"]},
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": round(cb["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     secs = max(5.0, min(60.0, 2.0 * a.steps))
     cb = cpu_reference(wl, secs)
@@ -382,6 +437,103 @@ def run_ep(a, wl: dict) -> None:
         dist.destroy_process_group()
 
 
+def run_model(a, wl: dict) -> None:
+    """The whole model, one token per step: the persistent one-step kernel (fwd.cu) replayed from a graph, each step
+    feeding the previous step's greedy choice. Every rank runs its own replica (the model does not shard)."""
+    import numpy as np
+    import torch
+
+    import clutor_b200 as cb
+    from clutor_b200 import synth_model as sm
+    from clutor_b200.model import Model
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    spec = sm.QWEN3_30B_A3B
+    t_img = time.perf_counter()
+    image = sm.image(spec, seed=1)
+    t_img = time.perf_counter() - t_img
+    ctx = cb.Context(local)
+    n_ctx = a.warmup + 2 * a.steps + 16
+    model = Model(ctx, image, n_ctx)
+    W, K = a.warmup, a.steps
+    first = 1
+    warm = model.generate(first, W)          # positions 0..W-1; captures the one-step graph
+    stream = torch.cuda.Stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            model.generate_async(warm[-1], K, stream.cuda_stream)   # positions W..W+K-1
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    toks = model.tokens(W, K)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = K * world / (ms / 1000.0)
+    ms_per_step = ms / K
+    mb = sm.model_bytes(spec)
+    avg_pos = W + (K - 1) / 2.0
+    kv_bytes = 2 * 2 * spec.n_kvw * spec.n_layer * (avg_pos + 1)      # keys and values read per token, half precision
+    bytes_per_token = mb["total"] + mb["embedding_row"] + kv_bytes
+    pk, pk_kind = peaks()
+    achieved = bytes_per_token / (ms_per_step * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": read_traffic("fwd_kernel_model"), "peak_kind": pk_kind,
+            "kernel": "fwd_kernel", "bytes_per_launch": int(bytes_per_token), "launch_us": round(1000 * ms_per_step, 2),
+            "note": "one launch per token: experts 1.175 GB + attention 0.523 GB + routers 50 MB + output 255 MB + "
+                    "key/value reads at the mean position"}
+    # end to end through the public API with host buffers: clb200_model_generate (state up, tokens down, synchronous)
+    e2e = None
+    if not a.no_e2e:
+        model.reset()
+        model.generate(first, W)
+        t0 = time.perf_counter()
+        out = model.generate(warm[-1], K)
+        dt = time.perf_counter() - t0
+        if dist:
+            tt = torch.tensor([dt], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            dt = float(tt.item())
+        same = out == toks
+        e2e = {"value": round(K * world / dt, 3), "unit": "tokens/s", "h2d_bytes_per_step": round(24 / K, 3),
+               "d2h_bytes_per_step": round(4 + 24 / K, 3), "api": "clb200_model_generate (host token buffer, synchronous)",
+               "same_tokens_as_timed_run": same}
+    cpu = None
+    if rank == 0 and not a.no_cpu_baseline:
+        cpu = model_reference(image, W + K + 8, a.cpu_seconds)
+        cpu.pop("ms_per_token", None)
+    if rank == 0:
+        line = {"metric": MODEL_METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate; fp32 attention, fp16 key/value cache",
+                "data": "synthetic (seeded random GGUF weights with the model's shapes and types)",
+                "config": {"workload": wl["desc"], "model_bytes": mb["total"], "positions": [W, W + K - 1],
+                           "parallelism": f"replicas x{world}", "l2": "inputs larger than L2: 2.0 GB of weights per token",
+                           "image_seconds": round(t_img, 1)},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": K, "clocks": clk.summary(),
+                "tokens": toks[:16]}
+        print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -408,6 +560,9 @@ def main() -> None:
         return
     if a.workload == "ep235b":
         run_ep(a, wl)
+        return
+    if a.workload == "model":
+        run_model(a, wl)
         return
 
     import numpy as np

@@ -41,6 +41,18 @@ CLB_DEV void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t 
                ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
                : "memory");
 }
+// The same copy with an L2 cache policy (createpolicy): for data read once, evict-first keeps it from displacing what
+// is read again (code, activations, caches).
+CLB_DEV uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+CLB_DEV void bulk_copy_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t policy) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+               : "memory");
+}
 CLB_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -52,6 +64,7 @@ CLB_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 // Bounded wait for an mbarrier phase; false when the limit ran out.
 CLB_DEV bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+#pragma unroll 1
   for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 64) __nanosleep(32);
@@ -74,6 +87,7 @@ CLB_DEV void red_release_add(uint32_t *p, uint32_t v) {
 }
 // Waits until *p >= target (bounded). Call from one thread.
 CLB_DEV bool wait_counter(const uint32_t *p, uint32_t target) {
+#pragma unroll 1
   for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
     if (ld_acquire(p) >= target) return true;
     if (i > 4096) __nanosleep(64);   // poll flat out for the first few microseconds: these waits are on the critical path

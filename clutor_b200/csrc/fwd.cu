@@ -4,21 +4,26 @@
 // One CTA per SM (G CTAs, a cooperative launch, so all are resident), 512 threads. Work that crosses CTAs goes through
 // global memory behind one grid barrier counter (bounded waits; any CTA's error ends every CTA's wait). Per layer:
 //   A  attention input: x (global) -> rmsnorm -> Q8_K blocks (every CTA); this CTA's rows of the stacked [wq; wk; wv]
-//      (exact integer block sums, the reference's float block terms in block order: c/src/quant.c:832-846)   | barrier
-//   B  attention, one work item per (key/value head, chunk of 256 positions): QK-norm and rotary embedding of the item's
-//      query heads and key (c/src/forward.c:905-915), the new key/value into the half-precision cache (kv_put, :563-572),
-//      scores against the cached keys, softmax and the weighted values, in fp32 (the grouped form of :665-737);
-//      a context longer than one chunk merges the chunks' partials afterwards                               | barrier(s)
+//      from shared memory (exact integer block sums, the reference's float block terms in block order)       | barrier
+//   B1 attention scores, one item per (key/value head, 32 positions) over all CTAs: QK-norm and rotary embedding of the
+//      item's query heads (c/src/forward.c:905-915), in the block of the new position also of its key, which goes into
+//      the half-precision cache with the value (kv_put, :563-572); the reference's dotf_h per (head, position)  | barrier
+//   B2 softmax and weighted values in the reference's order: per (key/value head, 256-position chunk) when a group has
+//      2..16 query heads and the context is 64 positions or more (c/src/forward.c:665-737), else per query head over
+//      every position (:584-627); several chunks are merged afterwards (:719-737)                           | barrier(s)
 //   C  attention output: Q8_K of the attention vector (every CTA); this CTA's rows of wo; x += resid * wo att | barrier
-//   D  mixture of experts, as the one-token MoE kernel (decode.cu) does it: rmsnorm, router (the reference's dotf),
+//   D  mixture of experts as the one-token MoE kernel (decode.cu) does it: rmsnorm, router (the reference's dotf),
 //      softmax, top-k, renormalisation, this CTA's share of every chosen expert's gate/up rows (bulk copies into shared
 //      memory), SwiGLU                                                                                       | barrier
 //      the Q8_K blocks of every expert's hg, this CTA's down rows, x += resid * sum_k wt_k hd_k in rank order  | barrier
 // then the output norm and this CTA's rows of the output matrix, streamed through shared memory, their logits and the
 // greedy arg-max (lowest id on ties, c/src/main.c:349-350). The last CTA out advances the sequence state.
 //
-// While a layer's experts stream, every CTA asks L2 for the rows of the next layer's dense matrices it will read, and the
-// next layer's router rows are copied into shared memory as soon as this layer's router products are formed.
+// Weights never wait on activations: a layer's dense rows (wq, wk, wv, wo) are copied into shared memory while the
+// previous layer's down rows compute, and its router rows as soon as the previous layer's router products are formed.
+// The code a layer runs is kept small (the block dot products, quantizers and transcendental steps are out-of-line
+// functions): a layer executes every phase once, so code that outgrows the SM's instruction caches is fetched again
+// for every layer.
 #include "common.cuh"
 #include "fwd.cuh"
 #include "rowdot.cuh"
@@ -27,15 +32,31 @@ namespace clb {
 namespace {
 
 constexpr int NW = FWD_THREADS / 32;
-constexpr int RW = NW - 1;              // the router warp
-constexpr int HEAD_ROWS = 16;           // output-matrix rows per shared-memory stage
-constexpr int HEAD_STAGES = 4;
+constexpr int RW = NW - 1;   // the router warp
+constexpr int SB = 32;       // positions per attention-score item
+constexpr int VB = 64;       // positions of values staged at a time
 
 CLB_DEV int ld_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
 
-CLB_DEV void prefetch_l2(const void *p, uint32_t bytes) {   // p and bytes 16-byte aligned
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// ---- out-of-line steps (one copy of their code for every call) and small inline ones --------------------------------------------------------------
+__device__ __noinline__ float blk_dot(uint32_t type, const uint8_t *row, int blk, const int8_t *qs, const int16_t *bs,
+                                      const float *dd, int ablk) {
+  return kq_block_s(type, row, blk, SmemAct{qs, bs, dd}, ablk);
 }
+__device__ __noinline__ float blk_dot_fast(uint32_t type, const uint8_t *row, int blk, const int8_t *qs, const int16_t *bs,
+                                           const float *dd, int ablk) {
+  return kq_block_s<false>(type, row, blk, SmemAct{qs, bs, dd}, ablk);
+}
+__device__ __noinline__ void quant_smem(const float *x, int n, int8_t *qs, float *dd, int16_t *bs, int warp, int nwarps, int lane) {
+  q8k_quantize_block(x, n, qs, dd, bs, warp, nwarps, lane, true);
+}
+__device__ __noinline__ void quant_global(const float *src, int nblocks, int8_t *qs, float *dd, int16_t *bs, int warp, int nwarps,
+                                          int lane) {
+  q8k_quantize_global<2>(src, nblocks, qs, dd, bs, warp, nwarps, lane, true);
+}
+CLB_DEV float exp_cr(float x) { return expf_cr(x); }
+CLB_DEV float swiglu(float g, float u) { return silu_mul(g, u); }
+CLB_DEV float div_d(float a, double b) { return __double2float_rn(__ddiv_rn(static_cast<double>(a), b)); }
 
 // The block of one grid barrier: every CTA arrives, then waits for all G (bounded; returns early when any CTA has
 // recorded an error). Returns false on a timeout or a recorded error.
@@ -51,6 +72,7 @@ struct Grid {
       red_release_add(ctr, 1u);
       const uint32_t target = gen * G;
       bool ok = false;
+#pragma unroll 1
       for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
         if (ld_acquire(ctr) >= target) { ok = true; break; }
         if ((i & 127) == 127 && ld_volatile(err)) break;
@@ -102,24 +124,27 @@ CLB_DEV void rmsnorm_to_smem(const float *x, const float *w, float *xn, int n, f
 
 CLB_DEV int lanes_for(int nb) { return nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : nb <= 8 ? 8 : 16; }
 
-// Rows [r0, r1) of a K-quant matrix (rows at m.p + r * m.rb, nb 256-blocks each, in global memory) times the Q8_K vector
-// in shared memory: a group of lanes per row, one lane per block, the block terms
-// added in block order at the group's first lane, which calls out(r, value). Call from all threads.
-template <class Out>
-CLB_DEV void gemv_rows(const FwdMat &m, int nb, int r0, int r1, const int8_t *qs, const float *dd, const int16_t *bs, Out out) {
+// n rows of a K-quant matrix (row i at rows + i * rb, nb 256-blocks each; shared or global memory) times the Q8_K
+// vector in shared memory: a group of lanes per row, one lane per block, the block terms added in block order at the
+// group's first lane. mode 0: dst[i] = value; mode 1: dst[i] = dst[i] + scale * value (the residual update). Call from
+// all threads.
+__device__ __noinline__ void gemv_rows(uint32_t type, const uint8_t *rows, uint32_t rb, int nb, int n, const int8_t *qs,
+                                       const float *dd, const int16_t *bs, float *dst, int mode, float scale) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int GL = lanes_for(nb), lg = lane & (GL - 1), gpw = 32 / GL, ngroups = NW * gpw, gid = warp * gpw + lane / GL;
   const int base = lane - lg;
   const bool has = lg < nb;
-  const SmemAct act{qs, bs, dd};
-  for (int b0 = r0; b0 < r1; b0 += ngroups) {   // the same trip count in every warp
+  for (int b0 = 0; b0 < n; b0 += ngroups) {   // the same trip count in every warp
     const int r = b0 + gid;
-    const bool valid = r < r1;
+    const bool valid = r < n;
     float t = 0.f;
-    if (valid && has) t = kq_block_s(m.type, m.p + static_cast<size_t>(r) * m.rb, lg, act, lg);
+    if (valid && has) t = blk_dot(type, rows + static_cast<size_t>(r) * rb, lg, qs, bs, dd, lg);
     float s = 0.f;
     for (int b = 0; b < nb; ++b) s = __fadd_rn(s, __shfl_sync(FULL, t, base + b));
-    if (valid && lg == 0) out(r, s);
+    if (valid && lg == 0) {
+      if (mode == 0) __stcg(dst + r, s);
+      else dst[r] = __fadd_rn(__ldcg(dst + r), __fmul_rn(scale, s));
+    }
   }
 }
 
@@ -156,23 +181,17 @@ CLB_DEV void embed_row(const FwdMat &m, int token, int E, float *y) {
 }
 
 // Rotary embedding of one head held by a warp, EPL = hd / 32 elements per lane at i = lane + 32 e. NEOX pairs (i, i + hd/2)
-// (c/src/forward.c:428-435) or adjacent pairs (2i, 2i + 1) (:420-426). theta_i = pos * base^(-2i/hd), each step rounded to
-// float as the reference's powf, cosf and sinf give it (correctly rounded here, via double).
+// (c/src/forward.c:428-435) or adjacent pairs (2i, 2i + 1) (:420-426). The angle's cosine and sine come from tables the
+// host filled with the reference's own expressions and C library (cosf / sinf of pos * powf(base, -2i / hd)): cs holds
+// [hd / 2] cosines then [hd / 2] sines for this position.
 template <int EPL>
-CLB_DEV void rope_warp(float (&v)[EPL], int hd, int pos, float base, bool pairs) {
+CLB_DEV void rope_warp(float (&v)[EPL], const float *cs, bool pairs) {
+  constexpr int H = 16 * EPL;   // hd / 2
   const int lane = threadIdx.x & 31;
-  auto angle = [&](int i, float &c, float &s) {
-    const float ex = __fdiv_rn(__fmul_rn(-2.0f, static_cast<float>(i)), static_cast<float>(hd));
-    const float p = __double2float_rn(pow(static_cast<double>(base), static_cast<double>(ex)));
-    const float th = __fmul_rn(static_cast<float>(pos), p);
-    c = __double2float_rn(cos(static_cast<double>(th)));
-    s = __double2float_rn(sin(static_cast<double>(th)));
-  };
   if (!pairs) {
 #pragma unroll
     for (int e = 0; e < EPL / 2; ++e) {
-      float c, s;
-      angle(lane + 32 * e, c, s);
+      const float c = __ldg(cs + lane + 32 * e), s = __ldg(cs + H + lane + 32 * e);
       const float a = v[e], b = v[e + EPL / 2];
       v[e] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
       v[e + EPL / 2] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
@@ -181,8 +200,7 @@ CLB_DEV void rope_warp(float (&v)[EPL], int hd, int pos, float base, bool pairs)
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
       const int i = lane + 32 * e;
-      float c, s;
-      angle(i / 2, c, s);
+      const float c = __ldg(cs + i / 2), s = __ldg(cs + H + i / 2);
       const float other = __shfl_xor_sync(FULL, v[e], 1);
       const float a = (i & 1) ? other : v[e], b = (i & 1) ? v[e] : other;
       v[e] = (i & 1) ? __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c)) : __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
@@ -197,24 +215,57 @@ CLB_DEV unsigned long long argmax_key(float v, int id) {
   return (static_cast<unsigned long long>(ord) << 32) | (0xffffffffu - static_cast<uint32_t>(id));
 }
 
+CLB_DEV uint32_t lo16(const void *p) { return static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 15u); }
+
+// Where this CTA's rows [r0[q], r1[q]) of a layer's wq, wk, wv, wo sit in the slots: one segment after another, each
+// 32 bytes longer than its rows (the copy starts at the 16-byte boundary at or below the first row).
+CLB_DEV uint32_t dense_offset(const FwdLayer &Ly, const int (&r0)[4], const int (&r1)[4], int q) {
+  const FwdMat mats[4] = {Ly.wq, Ly.wk, Ly.wv, Ly.wo};
+  uint32_t off = 0;
+  for (int i = 0; i < q; ++i) off += (static_cast<uint32_t>(r1[i] - r0[i]) * mats[i].rb + 32u + 15u) & ~15u;
+  return off;
+}
+
+// This CTA's rows of a layer's wq, wk, wv, wo, one bulk copy each into its segment of the slots. One thread.
+CLB_DEV void issue_dense(const FwdLayer &Ly, uint8_t *slots, uint64_t *bar, const int (&r0)[4], const int (&r1)[4]) {
+  const FwdMat mats[4] = {Ly.wq, Ly.wk, Ly.wv, Ly.wo};
+  uint32_t total = 0, n16[4];
+  const uint8_t *src[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int cnt = r1[q] - r0[q];
+    src[q] = mats[q].p + static_cast<size_t>(r0[q]) * mats[q].rb;
+    n16[q] = cnt > 0 ? (lo16(src[q]) + static_cast<uint32_t>(cnt) * mats[q].rb + 15u) & ~15u : 0u;
+    total += n16[q];
+  }
+  fence_proxy_async();
+  mbar_arrive_expect_tx(bar, total);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (n16[q]) bulk_copy_g2s_hint(slots + dense_offset(Ly, r0, r1, q), src[q] - lo16(src[q]), n16[q], bar, l2_evict_first());
+}
+
 template <int EPL>
 __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, c = blockIdx.x;
-  const int E = a.E, FF = a.FF, NE = a.NE, K = a.K, hd = a.hd;
+  const int E = a.E, FF = a.FF, NE = a.NE, K = a.K;
+  constexpr int hd = 32 * EPL;
   const int nb = E / 256, nbd = FF / 256;
   FwdState *st = a.st;
 
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);   // [K] experts, [K] router rows, [K+1..] output stages
+  // [0, K) experts, [K] router rows, [K+1] dense rows, [K+2, K+2+HEAD_STAGES) output stages
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);
+  uint64_t *rbar = bars + K, *dbar = bars + K + 1, *hb = bars + K + 2;
   float *xn = reinterpret_cast<float *>(smem + a.off_xn);             // [E]
   int8_t *xq_qs = reinterpret_cast<int8_t *>(smem + a.off_xq);        // Q8_K of the current vector (up to n_q wide)
   const int XQW = a.n_q > E ? a.n_q : E;
   int16_t *xq_bs = reinterpret_cast<int16_t *>(smem + a.off_xq + XQW);
   float *xq_d = reinterpret_cast<float *>(smem + a.off_xq + XQW + 2 * (XQW / 16));
   double *s_red = reinterpret_cast<double *>(smem + a.off_misc);      // [NW]
-  // [0] barrier verdict, [1] a router copy in flight, [2] the router logits arrived, [3] the parity of the router copy in
-  // flight, [4] the layer whose expert copies went out last (-1: none)
+  // [0] barrier verdict, [1] a router copy in flight, [2] the router logits arrived, [3] its parity, [4] the layer whose
+  // expert copies went out last (-1: none), [5] a dense copy in flight, [6] its parity
   int *s_flag = reinterpret_cast<int *>(s_red + NW);
   int *s_sel = s_flag + 8;                                             // [32]
   float *s_wt = reinterpret_cast<float *>(s_sel + 32);                 // [32]
@@ -228,11 +279,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   int16_t *hq_bs = reinterpret_cast<int16_t *>(smem + a.off_hq + K * FF);
   float *hq_d = reinterpret_cast<float *>(smem + a.off_hq + K * FF + 2 * (K * FF / 16));
   float *xr = reinterpret_cast<float *>(smem + a.off_xr);
-  uint8_t *slots = smem + a.off_slots;     // gate/up rows of the chosen experts; the output matrix's stages
+  uint8_t *slots = smem + a.off_slots;     // dense rows of the layer, then the chosen experts' gate/up rows; output stages
   uint8_t *dslots = smem + a.off_dslots;   // down rows of the chosen experts; the attention scratch
   const int GRP = a.n_head / a.n_kv;
-  float *qs_h = reinterpret_cast<float *>(dslots);                     // attention: [GROUP][hd] queries, then value sums
-  float *sc = qs_h + GRP * a.hd;                                       // attention: scores / weights of an item
+  float *qs_h = reinterpret_cast<float *>(dslots);                     // attention: [GROUP][hd] queries
+  float *sc = qs_h + GRP * hd;                                         // attention: scores / weights of an item
+  __half *kvs = reinterpret_cast<__half *>(dslots + a.off_kvstage);    // attention: staged key / value rows
 
   const uint32_t uG = static_cast<uint32_t>(G), uc = static_cast<uint32_t>(c);
   const int j0 = static_cast<int>(FF * uc / uG), j1 = static_cast<int>(FF * (uc + 1) / uG);
@@ -240,25 +292,30 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   const int ngu = j1 - j0, nd = i1 - i0;
   const int nre = c < NE ? (NE - c + G - 1) / G : 0;
   const int RS = E / 8 + 4;
-  const int QKVR = a.n_q + 2 * a.n_kvw;
+  const int nq = a.n_q, nk = a.n_kvw, QKVR = nq + 2 * nk;
   const int qr0 = static_cast<int>(static_cast<uint32_t>(QKVR) * uc / uG), qr1 = static_cast<int>(static_cast<uint32_t>(QKVR) * (uc + 1) / uG);
+  // this CTA's rows of wq, wk, wv, wo
+  const int dr0[4] = {min(max(qr0, 0), nq), min(max(qr0 - nq, 0), nk), min(max(qr0 - nq - nk, 0), nk), i0};
+  const int dr1[4] = {max(min(qr1, nq), dr0[0]), max(min(qr1 - nq, nk), dr0[1]), max(min(qr1 - nq - nk, nk), dr0[2]), i1};
 
   Grid grid{&st->sync[0], &st->err, &s_flag[0], uG, 0};
   const int pos = st->pos, token = st->token;
   trace_time(a.trace, 30);
 
   if (tid == 0) {
-    for (int s = 0; s < K + 1 + HEAD_STAGES; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < K + 2 + HEAD_STAGES; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
-    // layer 0's router rows
-    if (nre > 0) {
-      mbar_arrive_expect_tx(&bars[K], static_cast<uint32_t>(nre) * E * 4u);
+    if (nre > 0) {   // layer 0's router rows
+      mbar_arrive_expect_tx(rbar, static_cast<uint32_t>(nre) * E * 4u);
       for (int m = 0; m < nre; ++m)
-        bulk_copy_g2s(rrows + static_cast<size_t>(m) * E, a.layers[0].router + static_cast<size_t>(c + m * G) * E, E * 4u, &bars[K]);
+        bulk_copy_g2s_hint(rrows + static_cast<size_t>(m) * E, a.layers[0].router + static_cast<size_t>(c + m * G) * E, E * 4u, rbar, l2_evict_first());
     }
+    issue_dense(a.layers[0], slots, dbar, dr0, dr1);   // layer 0's dense rows
     s_flag[1] = nre > 0;
     s_flag[3] = 0;
     s_flag[4] = -1;
+    s_flag[5] = 1;
+    s_flag[6] = 0;
   }
   // the token's embedding: this CTA's rows of x
   bool ok = true;
@@ -273,36 +330,41 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   }
   ok = grid.sync() && ok;
   const int nchunk = (pos + 1 + FWD_ATT_CHUNK - 1) / FWD_ATT_CHUNK;
+  const bool grouped = GRP >= 2 && GRP <= FWD_MAX_GROUP && pos + 1 >= 64;   // the reference's choice (c/src/forward.c:740-744)
 
   for (int l = 0; l < a.n_layer && ok; ++l) {
     const FwdLayer &Ly = a.layers[l];
     const uint32_t par = static_cast<uint32_t>(l & 1);
+    const size_t cache_l = static_cast<size_t>(l) * a.ctx * a.n_kvw;
     trace_stamp(a.trace, 0);
     // ---- A: attention input; this CTA's rows of [wq; wk; wv] --------------------------------------------------------
     rmsnorm_to_smem(a.x, Ly.attn_norm, xn, E, a.eps, s_red);
-    q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
+    quant_smem(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane);
+    if (!mbar_wait_bounded(dbar, par)) set_error(&st->err, ERR_WAIT_COPY);
     __syncthreads();
+    if (tid == 0) s_flag[5] = 0;
+    trace_stamp(a.trace, 14);
     {
-      const int nq = a.n_q, nk = a.n_kvw;
-      gemv_rows(Ly.wq, nb, max(qr0, 0), min(qr1, nq), xq_qs, xq_d, xq_bs, [&](int r, float v) { __stcg(a.qkv + r, v); });
-      gemv_rows(Ly.wk, nb, max(qr0 - nq, 0), min(qr1 - nq, nk), xq_qs, xq_d, xq_bs, [&](int r, float v) { __stcg(a.qkv + nq + r, v); });
-      gemv_rows(Ly.wv, nb, max(qr0 - nq - nk, 0), min(qr1 - nq - nk, nk), xq_qs, xq_d, xq_bs, [&](int r, float v) { __stcg(a.qkv + nq + nk + r, v); });
+      const FwdMat mats[3] = {Ly.wq, Ly.wk, Ly.wv};
+      float *outs[3] = {a.qkv + dr0[0], a.qkv + nq + dr0[1], a.qkv + nq + nk + dr0[2]};
+#pragma unroll 1
+      for (int q = 0; q < 3; ++q) {
+        const uint8_t *rows = slots + dense_offset(Ly, dr0, dr1, q) + lo16(mats[q].p + static_cast<size_t>(dr0[q]) * mats[q].rb);
+        gemv_rows(mats[q].type, rows, mats[q].rb, nb, dr1[q] - dr0[q], xq_qs, xq_d, xq_bs, outs[q], 0, 0.f);
+      }
     }
     trace_stamp(a.trace, 1);
     if (!(ok = grid.sync())) break;
     trace_stamp(a.trace, 2);
 
-    // ---- B1: attention scores, one item per (key/value head, 32 positions), spread over all CTAs -------------------------
-    const bool grouped = GRP >= 2 && GRP <= FWD_MAX_GROUP && pos + 1 >= 64;   // the reference's choice (c/src/forward.c:740-744)
+    // ---- B1: attention scores, one item per (key/value head, 32 positions) -------------------------------------------------
     {
-      const size_t cache_l = static_cast<size_t>(l) * a.ctx * a.n_kvw;
-      const float *qg = a.qkv, *kg = a.qkv + a.n_q, *vg = a.qkv + a.n_q + a.n_kvw;
-      // QK-norm over the whole vector (olmoe): the scales of q and of k
+      const float *qg = a.qkv, *kg = a.qkv + nq, *vg = a.qkv + nq + nk;
       float qscale = 1.f, kscale = 1.f;
-      if (a.qk_mode == 1) {
+      if (a.qk_mode == 1) {   // QK-norm over the whole vector (olmoe): the scales of q and of k
         double sq = 0.0, sk = 0.0;
-        for (int i = tid; i < a.n_q; i += FWD_THREADS) { const double v = __ldcg(qg + i); sq += v * v; }
-        for (int i = tid; i < a.n_kvw; i += FWD_THREADS) { const double v = __ldcg(kg + i); sk += v * v; }
+        for (int i = tid; i < nq; i += FWD_THREADS) { const double v = __ldcg(qg + i); sq += v * v; }
+        for (int i = tid; i < nk; i += FWD_THREADS) { const double v = __ldcg(kg + i); sk += v * v; }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) { sq += __shfl_xor_sync(FULL, sq, o); sk += __shfl_xor_sync(FULL, sk, o); }
         __syncthreads();
@@ -310,17 +372,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         __syncthreads();
         double tq = 0.0, tk = 0.0;
         for (int k = 0; k < NW; ++k) { tq += s_red[k]; tk += reinterpret_cast<double *>(terms)[k]; }
-        qscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tq / a.n_q), a.eps)));
-        kscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tk / a.n_kvw), a.eps)));
+        qscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tq / nq), a.eps)));
+        kscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tk / nk), a.eps)));
       }
-      constexpr int SB = 32;
       const int nsb = (pos + 1 + SB - 1) / SB;
       for (int item = c; item < a.n_kv * nsb; item += G) {
         const int g = item / nsb, t0 = (item - g * nsb) * SB, n = min(SB, pos + 1 - t0);
         const bool has_pos = t0 + n == pos + 1;
         __syncthreads();   // the scratch of the previous item
-        // the group's query heads (warps 0..GRP-1) and, in the block of the new position, the key head (warp GRP):
-        // QK-norm, rotary embedding (c/src/forward.c:905-915); the new key and value into the cache (kv_put, :563-572)
+        // the group's query heads (warps 0..GRP-1) and, in the block of the new position, the key head (warp GRP)
         for (int h = warp; h < GRP + (has_pos ? 1 : 0); h += NW) {
           const bool isk = h == GRP;
           const float *src = isk ? kg + g * hd : qg + (g * GRP + h) * hd;
@@ -333,20 +393,20 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
             for (int e = 0; e < EPL; ++e) ss += static_cast<double>(v[e]) * v[e];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
-            const float sc1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(ss / hd), a.eps)));
+            const float s1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(ss / hd), a.eps)));
             const float *w = isk ? Ly.kn : Ly.qn;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], sc1), __ldg(w + lane + 32 * e));
-          } else if (a.qk_mode == 1) {   // over the whole projected vector
-            const float sc1 = isk ? kscale : qscale;
+            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), __ldg(w + lane + 32 * e));
+          } else if (a.qk_mode == 1) {
+            const float s1 = isk ? kscale : qscale;
             const float *w = isk ? Ly.kn + g * hd : Ly.qn + (g * GRP + h) * hd;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], sc1), __ldg(w + lane + 32 * e));
+            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), __ldg(w + lane + 32 * e));
           }
-          rope_warp<EPL>(v, hd, pos, a.rope_base, a.rope_pairs != 0);
+          rope_warp<EPL>(v, a.rope_cs + static_cast<size_t>(pos) * hd, a.rope_pairs != 0);
           if (isk) {
-            __half *kd = a.kc + cache_l + static_cast<size_t>(pos) * a.n_kvw + g * hd;
-            __half *vd = a.vc + cache_l + static_cast<size_t>(pos) * a.n_kvw + g * hd;
+            __half *kd = a.kc + cache_l + static_cast<size_t>(pos) * nk + g * hd;
+            __half *vd = a.vc + cache_l + static_cast<size_t>(pos) * nk + g * hd;
 #pragma unroll
             for (int e = 0; e < EPL; ++e) {
               kd[lane + 32 * e] = __float2half_rn(v[e]);
@@ -358,19 +418,27 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
           }
         }
         __syncthreads();
-        // scores: the reference's dotf_h (c/src/forward.c:492-510: eight running sums over the head, combined
-        // ((0+1)+(2+3))+((4+5)+(6+7))) times the attention scale; two threads per (head, position), sums 0-3 and 4-7
+        // the block's keys into shared memory, all loads in flight at once
         const __half *kb = a.kc + cache_l + g * hd;
+        for (int i = tid; i < n * (hd / 8); i += FWD_THREADS) {
+          const int t = i / (hd / 8), q = i - t * (hd / 8);
+          reinterpret_cast<uint4 *>(kvs)[i] = __ldcg(reinterpret_cast<const uint4 *>(kb + static_cast<size_t>(t0 + t) * nk) + q);
+        }
+        __syncthreads();
+        trace_stamp(a.trace, 15);
+        // the reference's dotf_h (c/src/forward.c:492-510): eight running sums over the head, combined
+        // ((0+1)+(2+3))+((4+5)+(6+7)), times the attention scale; two threads per (head, position), sums 0-3 and 4-7
         const int half = tid & 1;
         for (int p = tid >> 1; p < GRP * SB; p += FWD_THREADS / 2) {
           const int j = p / SB, tt = p - j * SB;
           const bool valid = tt < n;
           float s4[4] = {0.f, 0.f, 0.f, 0.f};
           if (valid) {
-            const __half *kr = kb + static_cast<size_t>(t0 + tt) * a.n_kvw + 4 * half;
+            const __half *kr = kvs + tt * hd + 4 * half;
             const float *q = qs_h + j * hd + 4 * half;
+#pragma unroll
             for (int i = 0; i < hd; i += 8) {
-              const uint2 kk = __ldcg(reinterpret_cast<const uint2 *>(kr + i));
+              const uint2 kk = *reinterpret_cast<const uint2 *>(kr + i);
               const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.x));
               const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.y));
               const float4 qq = *reinterpret_cast<const float4 *>(q + i);
@@ -390,24 +458,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     if (!(ok = grid.sync())) break;
 
     // ---- B2: softmax and weighted values in the reference's order --------------------------------------------------------
-    // grouped (c/src/forward.c:665-737): an item per (key/value head, chunk of 256 positions): per query head the chunk's
-    // maximum m, e_t = expf(s_t - m), the sum l in position order, o = sum_t e_t v_t in position order; one chunk gives
-    // o * (1 / l) directly, more are merged below. plain (c/src/forward.c:584-627): an item per query head over every
-    // position: the maximum, e_t, their sum in order, then o = sum_t (e_t / sum) v_t in order.
+    // grouped: an item per (key/value head, chunk of 256 positions): per query head the chunk's maximum m,
+    // e_t = expf(s_t - m), their sum l in position order, o = sum_t e_t v_t in position order; one chunk gives
+    // o * (1 / l) directly, more are merged below. plain: an item per query head over every position: the maximum, e_t,
+    // their sum in order, then o = sum_t (e_t / sum) v_t in order.
     {
-      const size_t cache_l = static_cast<size_t>(l) * a.ctx * a.n_kvw;
       const int items = grouped ? a.n_kv * nchunk : a.n_head;
-      float *hm = reinterpret_cast<float *>(probs);   // [16] maxima, [16] sums
-      float *ob = qs_h;                               // [NH][hd] value sums
+      float *hm = probs;   // [16] maxima, [16] sums
       for (int item = c; item < items; item += G) {
         const int g = grouped ? item / nchunk : item / GRP;
         const int ch = grouped ? item - g * nchunk : 0;
-        const int j0 = grouped ? 0 : item - g * GRP, NH = grouped ? GRP : 1;
+        const int jb = grouped ? 0 : item - g * GRP, NH = grouped ? GRP : 1;
         const int t0 = ch * FWD_ATT_CHUNK, n = grouped ? min(FWD_ATT_CHUNK, pos + 1 - t0) : pos + 1;
         __syncthreads();
         for (int i = tid; i < NH * n; i += FWD_THREADS) {
           const int jj = i / n, t = i - jj * n;
-          sc[i] = __ldcg(a.scores + static_cast<size_t>(g * GRP + j0 + jj) * a.ctx + t0 + t);
+          sc[i] = __ldcg(a.scores + static_cast<size_t>(g * GRP + jb + jj) * a.ctx + t0 + t);
         }
         __syncthreads();
         for (int jj = warp; jj < NH; jj += NW) {   // a warp per head: the maximum, then e_t
@@ -415,7 +481,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
           for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sc[jj * n + t]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-          for (int t = lane; t < n; t += 32) sc[jj * n + t] = expf_cr(__fsub_rn(sc[jj * n + t], mx));
+          for (int t = lane; t < n; t += 32) sc[jj * n + t] = exp_cr(__fsub_rn(sc[jj * n + t], mx));
           if (lane == 0) hm[jj] = mx;
         }
         __syncthreads();
@@ -427,37 +493,50 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         if (!grouped) {
           __syncthreads();
           for (int t = tid; t < n; t += FWD_THREADS) sc[t] = __fdiv_rn(sc[t], hm[16]);   // p_t = e_t / sum
-          __syncthreads();
         }
-        // o[jj][i] = sum over t in order of w_t * v_t[i] (w = e, grouped; w = p, plain)
+        trace_stamp(a.trace, 16);
+        // o[jj][i] = sum over t in order of w_t * v_t[i] (w = e grouped, p plain); values staged VB positions at a time
+        constexpr int MAXC = FWD_MAX_GROUP * hd / FWD_THREADS > 0 ? FWD_MAX_GROUP * hd / FWD_THREADS : 1;
+        float o[MAXC];
+#pragma unroll
+        for (int u = 0; u < MAXC; ++u) o[u] = 0.f;
         const __half *vb = a.vc + cache_l + g * hd;
-        for (int oi = tid; oi < NH * hd; oi += FWD_THREADS) {
-          const int jj = oi / hd, i = oi - jj * hd;
-          const float *w = sc + jj * n;
-          const __half *vcol = vb + i;
-          float o = 0.f;
-          int t = 0;
-          for (; t + 4 <= n; t += 4) {
-            float vv[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) vv[u] = __half2float(__ldcg(vcol + static_cast<size_t>(t0 + t + u) * a.n_kvw));
-#pragma unroll
-            for (int u = 0; u < 4; ++u) o = __fadd_rn(o, __fmul_rn(w[t + u], vv[u]));
+        for (int b0 = 0; b0 < n; b0 += VB) {
+          const int cnt = min(VB, n - b0);
+          __syncthreads();   // the previous block's readers are done
+          for (int i = tid; i < cnt * (hd / 8); i += FWD_THREADS) {
+            const int t = i / (hd / 8), q = i - t * (hd / 8);
+            reinterpret_cast<uint4 *>(kvs)[i] = __ldcg(reinterpret_cast<const uint4 *>(vb + static_cast<size_t>(t0 + b0 + t) * nk) + q);
           }
-          for (; t < n; ++t) o = __fadd_rn(o, __fmul_rn(w[t], __half2float(__ldcg(vcol + static_cast<size_t>(t0 + t) * a.n_kvw))));
-          ob[oi] = o;
+          __syncthreads();
+#pragma unroll
+          for (int u = 0; u < MAXC; ++u) {
+            const int oi = tid + u * FWD_THREADS;
+            if (oi < NH * hd) {
+              const int jj = oi / hd, i = oi - jj * hd;
+              const float *w = sc + jj * n + b0;
+              float acc = o[u];
+              for (int t = 0; t < cnt; ++t) acc = __fadd_rn(acc, __fmul_rn(w[t], __half2float(kvs[t * hd + i])));
+              o[u] = acc;
+            }
+          }
         }
         __syncthreads();
-        for (int oi = tid; oi < NH * hd; oi += FWD_THREADS) {
-          const int jj = oi / hd, i = oi - jj * hd, h = g * GRP + j0 + jj;
-          if (!grouped) {
-            __stcg(a.att + h * hd + i, ob[oi]);
-          } else if (nchunk == 1) {   // the merge of one chunk: weight expf(0) = 1, so o * (1 / l)
-            __stcg(a.att + h * hd + i, __fmul_rn(ob[oi], __fdiv_rn(1.0f, hm[16 + jj])));
-          } else {
-            float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + jj) * (2 + hd);
-            if (i == 0) { __stcg(pp, hm[jj]); __stcg(pp + 1, hm[16 + jj]); }
-            __stcg(pp + 2 + i, ob[oi]);
+        trace_stamp(a.trace, 17);
+#pragma unroll
+        for (int u = 0; u < MAXC; ++u) {
+          const int oi = tid + u * FWD_THREADS;
+          if (oi < NH * hd) {
+            const int jj = oi / hd, i = oi - jj * hd, h = g * GRP + jb + jj;
+            if (!grouped) {
+              __stcg(a.att + h * hd + i, o[u]);
+            } else if (nchunk == 1) {   // the merge of one chunk: weight expf(0) = 1, so o * (1 / l)
+              __stcg(a.att + h * hd + i, __fmul_rn(o[u], __fdiv_rn(1.0f, hm[16 + jj])));
+            } else {
+              float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + jj) * (2 + hd);
+              if (i == 0) { __stcg(pp, hm[jj]); __stcg(pp + 1, hm[16 + jj]); }
+              __stcg(pp + 2 + i, o[u]);
+            }
           }
         }
       }
@@ -472,7 +551,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
           float L = 0.f, o = 0.f;
           for (int ch = 0; ch < nchunk; ++ch) {
             const float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + j) * (2 + hd);
-            const float w = expf_cr(__fsub_rn(__ldcg(pp), M));
+            const float w = exp_cr(__fsub_rn(__ldcg(pp), M));
             L = __fadd_rn(L, __fmul_rn(w, __ldcg(pp + 1)));
             o = __fadd_rn(o, __fmul_rn(w, __ldcg(pp + 2 + d)));
           }
@@ -484,10 +563,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     trace_stamp(a.trace, 4);
 
     // ---- C: attention output: x += resid * wo att, this CTA's rows ------------------------------------------------------
-    q8k_quantize_global(a.att, a.n_q / 256, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
+    quant_global(a.att, nq / 256, xq_qs, xq_d, xq_bs, warp, NW, lane);
     __syncthreads();
-    gemv_rows(Ly.wo, a.n_q / 256, i0, i1, xq_qs, xq_d, xq_bs,
-              [&](int r, float v) { a.x[r] = __fadd_rn(__ldcg(a.x + r), __fmul_rn(a.resid_scale, v)); });
+    gemv_rows(Ly.wo.type, slots + dense_offset(Ly, dr0, dr1, 3) + lo16(Ly.wo.p + static_cast<size_t>(i0) * Ly.wo.rb), Ly.wo.rb, nq / 256, nd,
+              xq_qs, xq_d, xq_bs, a.x + i0, 1, a.resid_scale);
     trace_stamp(a.trace, 5);
     if (!(ok = grid.sync())) break;
     trace_stamp(a.trace, 6);
@@ -495,7 +574,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     // ---- D: mixture of experts -------------------------------------------------------------------------------------------
     rmsnorm_to_smem(a.x, Ly.ffn_norm, xn, E, a.eps, s_red);
     for (int i = i0 + tid; i < i1; i += FWD_THREADS) xr[i - i0] = __ldcg(a.x + i);
-    if (s_flag[1] && !mbar_wait_bounded(&bars[K], par)) { set_error(&st->err, ERR_WAIT_COPY); }
+    if (s_flag[1] && !mbar_wait_bounded(rbar, par)) set_error(&st->err, ERR_WAIT_COPY);
     for (int m = 0; m < nre; ++m)   // the router products, laid out for the strided sums
       for (int i = tid; i < E; i += FWD_THREADS) rprod[(m * 8 + (i & 7)) * RS + (i >> 3)] = __fmul_rn(rrows[m * E + i], xn[i]);
     __syncthreads();
@@ -504,9 +583,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       if (nre > 0 && l + 1 < a.n_layer) {
         s_flag[3] = (l + 1) & 1;
         fence_proxy_async();   // the generic reads of rrows before the bulk copy's writes
-        mbar_arrive_expect_tx(&bars[K], static_cast<uint32_t>(nre) * E * 4u);
+        mbar_arrive_expect_tx(rbar, static_cast<uint32_t>(nre) * E * 4u);
         for (int m = 0; m < nre; ++m)
-          bulk_copy_g2s(rrows + static_cast<size_t>(m) * E, a.layers[l + 1].router + static_cast<size_t>(c + m * G) * E, E * 4u, &bars[K]);
+          bulk_copy_g2s_hint(rrows + static_cast<size_t>(m) * E, a.layers[l + 1].router + static_cast<size_t>(c + m * G) * E, E * 4u, rbar, l2_evict_first());
         s_flag[1] = 1;
       }
     }
@@ -535,22 +614,25 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         }
         __syncwarp();
         if (lane == 0) red_release_add(&st->sync[1], static_cast<uint32_t>(nre));
+        if (lane == 0) trace_stamp_here(a.trace, 19);
       }
     } else {
-      q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, RW, lane, true);
+      quant_smem(xn, E, xq_qs, xq_d, xq_bs, warp, RW, lane);
     }
     trace_stamp(a.trace, 7);
     if (warp == 0) {   // softmax (c/src/forward.c:954-958)
       if (lane == 0) {
         const uint32_t target = static_cast<uint32_t>(NE) * static_cast<uint32_t>(l + 1);
         bool got = false;
-        for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
+  #pragma unroll 1
+      for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
           if (ld_acquire(&st->sync[1]) >= target) { got = true; break; }
           if ((i & 127) == 127 && ld_volatile(&st->err)) break;
           if (i > 4096) __nanosleep(64);
         }
         if (!got) set_error(&st->err, ERR_WAIT_ROUTER);
         s_flag[2] = got;
+        trace_stamp_here(a.trace, 20);
       }
       __syncwarp();
       if (s_flag[2]) {
@@ -565,12 +647,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+#pragma unroll 1
+        for (int j = 0; j < PER; ++j) probs[lane + 32 * j] = lane + 32 * j < NE ? exp_cr(__fsub_rn(lg[j], mx)) : 0.f;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) ev[j] = probs[lane + 32 * j];
         double part[PER];
 #pragma unroll
-        for (int j = 0; j < PER; ++j) {
-          ev[j] = lane + 32 * j < NE ? expf_cr(__fsub_rn(lg[j], mx)) : 0.f;
-          part[j] = static_cast<double>(ev[j]);
-        }
+        for (int j = 0; j < PER; ++j) part[j] = static_cast<double>(ev[j]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
@@ -578,11 +661,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         double tot = 0.0;
 #pragma unroll
         for (int j = 0; j < PER; ++j) tot += part[j];
-#pragma unroll
+#pragma unroll 1
         for (int j = 0; j < PER; ++j) {
           const int e = lane + 32 * j;
-          if (e < ((NE + 3) & ~3)) probs[e] = e < NE ? __double2float_rn(__ddiv_rn(static_cast<double>(ev[j]), tot)) : -1.0f;
+          if (e < ((NE + 3) & ~3)) probs[e] = e < NE ? div_d(probs[e], tot) : -1.0f;
         }
+        trace_stamp(a.trace, 21);
       }
     }
     __syncthreads();
@@ -603,6 +687,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       if (e < NE && part == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = pe; }
     }
     __syncthreads();
+    trace_stamp(a.trace, 22);
     if (tid < K) {   // renormalisation (c/src/forward.c:984)
       float w = s_wt[tid];
       if (a.norm_topk) {
@@ -623,7 +708,6 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       return q == 0 ? Ly.gate + e * Ly.gate_slab + static_cast<size_t>(j0) * a.grb : Ly.up + e * Ly.up_slab + static_cast<size_t>(j0) * a.grb;
     };
     auto dn_src = [&](int k) -> const uint8_t * { return Ly.down + static_cast<size_t>(s_sel[k]) * Ly.down_slab + static_cast<size_t>(i0) * a.drb; };
-    auto lo16 = [](const void *p) { return static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 15u); };
     if (tid == 0) s_flag[4] = l;   // read at the exit only
     if (lane == 0 && warp < K) {
       const int k = warp;
@@ -633,28 +717,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       const uint32_t len[3] = {static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(nd) * a.drb};
       uint32_t n16[3], total = 0;
       for (int q = 0; q < 3; ++q) { n16[q] = len[q] ? (lo16(src[q]) + len[q] + 15u) & ~15u : 0u; total += n16[q]; }
-      fence_proxy_async();   // the generic accesses of these buffers (attention scratch, last layer's rows) come first
+      fence_proxy_async();   // the generic accesses of these buffers (attention scratch, dense rows) come first
       mbar_arrive_expect_tx(&bars[k], total);
       for (int q = 0; q < 3; ++q)
-        if (n16[q]) bulk_copy_g2s(dst[q], src[q] - lo16(src[q]), n16[q], &bars[k]);
-    }
-    if (tid == 32 * K && l + 1 < a.n_layer) {   // the next layer's dense rows of this CTA into L2
-      const FwdLayer &Nx = a.layers[l + 1];
-      const FwdMat mats[3] = {Nx.wq, Nx.wk, Nx.wv};
-      const int lo[3] = {0, a.n_q, a.n_q + a.n_kvw}, cnt[3] = {a.n_q, a.n_kvw, a.n_kvw};
-      for (int q = 0; q < 3; ++q) {
-        const int r0 = max(qr0 - lo[q], 0), r1 = min(qr1 - lo[q], cnt[q]);
-        if (r1 > r0) {
-          const uintptr_t b = reinterpret_cast<uintptr_t>(mats[q].p + static_cast<size_t>(r0) * mats[q].rb) & ~uintptr_t(15);
-          const uintptr_t e = (reinterpret_cast<uintptr_t>(mats[q].p + static_cast<size_t>(r1) * mats[q].rb) + 15) & ~uintptr_t(15);
-          prefetch_l2(reinterpret_cast<const void *>(b), static_cast<uint32_t>(e - b));
-        }
-      }
-      if (nd > 0) {
-        const uintptr_t b = reinterpret_cast<uintptr_t>(Nx.wo.p + static_cast<size_t>(i0) * Nx.wo.rb) & ~uintptr_t(15);
-        const uintptr_t e = (reinterpret_cast<uintptr_t>(Nx.wo.p + static_cast<size_t>(i1) * Nx.wo.rb) + 15) & ~uintptr_t(15);
-        prefetch_l2(reinterpret_cast<const void *>(b), static_cast<uint32_t>(e - b));
-      }
+        if (n16[q]) bulk_copy_g2s_hint(dst[q], src[q] - lo16(src[q]), n16[q], &bars[k], l2_evict_first());
     }
     // gate and up rows: a group of lanes per (expert, row), one lane per block
     {
@@ -662,7 +728,6 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       const int lg = lane & (GL - 1), gpw = 32 / GL, ngroups = NW * gpw, gid = warp * gpw + lane / GL;
       const int tasks = K * ngu, base = lane - lg;
       const bool has_blk = lg < nb;
-      const SmemAct act{xq_qs, xq_bs, xq_d};
       int waited = -1;
       for (int t0 = 0; t0 < tasks; t0 += ngroups) {
         const int t = t0 + gid;
@@ -676,12 +741,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
           }
           if (has_blk) {
             const uint8_t *gs = slots + static_cast<size_t>(k) * a.slot_bytes;
-#pragma unroll 1
-            for (int m = 0; m < 2; ++m) {
-              const uint8_t *row = gs + m * a.gseg + lo16(gu_src(k, m)) + static_cast<uint32_t>(j) * a.grb;
-              const float v = kq_block_s(Ly.gate_type, row, lg, act, lg);
-              if (m == 0) tg = v; else tu = v;
-            }
+            tg = blk_dot(Ly.gate_type, gs + lo16(gu_src(k, 0)) + static_cast<uint32_t>(j) * a.grb, lg, xq_qs, xq_bs, xq_d, lg);
+            tu = blk_dot(Ly.gate_type, gs + a.gseg + lo16(gu_src(k, 1)) + static_cast<uint32_t>(j) * a.grb, lg, xq_qs, xq_bs, xq_d, lg);
           }
         }
         float sg = 0.f, su = 0.f;
@@ -689,14 +750,20 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
           sg = __fadd_rn(sg, __shfl_sync(FULL, tg, base + b));
           su = __fadd_rn(su, __shfl_sync(FULL, tu, base + b));
         }
-        if (valid && lg == 0) __stcg(a.hg + static_cast<size_t>(k) * FF + j0 + j, silu_mul(sg, su));
+        if (valid && lg == 0) __stcg(a.hg + static_cast<size_t>(k) * FF + j0 + j, swiglu(sg, su));
       }
     }
     trace_stamp(a.trace, 9);
     if (!(ok = grid.sync())) break;
     trace_stamp(a.trace, 10);
+    if (tid == 0 && l + 1 < a.n_layer) {   // the next layer's dense rows into the slots, whose gate/up rows are consumed
+      issue_dense(a.layers[l + 1], slots, dbar, dr0, dr1);
+      s_flag[5] = 1;
+      s_flag[6] = (l + 1) & 1;
+    }
     // every expert's hg as Q8_K blocks; this CTA's down rows; the combine in rank order and the residual
-    q8k_quantize_global(a.hg, K * FF / 256, hq_qs, hq_d, hq_bs, warp, NW, lane, true);
+    quant_global(a.hg, K * FF / 256, hq_qs, hq_d, hq_bs, warp, NW, lane);
+    trace_stamp(a.trace, 23);
     for (int k = 0; k < K; ++k)
       if (!mbar_wait_bounded(&bars[k], par)) set_error(&st->err, ERR_WAIT_COPY);
     __syncthreads();
@@ -704,9 +771,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       const int C = K * nbd, combo = tid % C, grp = tid / C, ngrp = FWD_THREADS / C;
       if (grp < ngrp) {
         const int blk = combo / K, k = combo - blk * K;
-        const SmemAct dact{hq_qs, hq_bs, hq_d};   // expert k's hg is blocks k * nbd ...
         const uint8_t *drows = dslots + static_cast<size_t>(k) * a.dslot_bytes + lo16(dn_src(k));
-        for (int r = grp; r < nd; r += ngrp) terms[(r * K + k) * nbd + blk] = kq_block_s(Ly.down_type, drows + static_cast<size_t>(r) * a.drb, blk, dact, k * nbd + blk);
+        for (int r = grp; r < nd; r += ngrp)
+          terms[(r * K + k) * nbd + blk] = blk_dot(Ly.down_type, drows + static_cast<size_t>(r) * a.drb, blk, hq_qs, hq_bs, hq_d, k * nbd + blk);
       }
     }
     __syncthreads();
@@ -727,48 +794,54 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   if (ok) {
     trace_stamp(a.trace, 12);
     rmsnorm_to_smem(a.x, a.out_norm, xn, E, a.eps, s_red);
-    q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane, true);
+    quant_smem(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane);
     __syncthreads();
     const int v0 = static_cast<int>(static_cast<uint64_t>(a.vocab) * uc / uG), v1 = static_cast<int>(static_cast<uint64_t>(a.vocab) * (uc + 1) / uG);
-    const int nrows = v1 - v0, nst = (nrows + HEAD_ROWS - 1) / HEAD_ROWS;
+    const int nst = (v1 - v0 + HEAD_ROWS - 1) / HEAD_ROWS;
     // a stage holds HEAD_ROWS rows copied from the 16-byte boundary at or below their start (rows of a Q6_K matrix may
-    // start anywhere), so it is 32 bytes longer than the rows and they begin lo(s) bytes into it
+    // start anywhere), so it is 32 bytes longer than the rows and they begin lo16 bytes into it; the stages use the
+    // slots and dslots together. Two stages are computed at a time (half the lane groups each), HEAD_STAGES in flight.
     const uint32_t rb = a.output.rb, stage_bytes = (HEAD_ROWS * rb + 32 + 15) & ~15u;
-    uint64_t *hb = bars + K + 1;
-    auto stage_lo = [&](int s) { return static_cast<uint32_t>(reinterpret_cast<uintptr_t>(a.output.p + static_cast<size_t>(v0 + s * HEAD_ROWS) * rb) & 15u); };
-    auto issue = [&](int s) {   // stage s of this CTA's rows into buffer s % HEAD_STAGES
-      const int r0 = v0 + s * HEAD_ROWS, cnt = min(HEAD_ROWS, v1 - r0);
-      const uint8_t *src = a.output.p + static_cast<size_t>(r0) * rb;
-      const uint32_t lo = stage_lo(s), n16 = (lo + static_cast<uint32_t>(cnt) * rb + 15u) & ~15u;
+    auto stage_src = [&](int s) { return a.output.p + static_cast<size_t>(v0 + s * HEAD_ROWS) * rb; };
+    auto issue = [&](int s) {
+      const int cnt = min(HEAD_ROWS, v1 - (v0 + s * HEAD_ROWS));
+      const uint8_t *src = stage_src(s);
+      const uint32_t n16 = (lo16(src) + static_cast<uint32_t>(cnt) * rb + 15u) & ~15u;
       uint64_t *b = &hb[s % HEAD_STAGES];
       fence_proxy_async();
       mbar_arrive_expect_tx(b, n16);
-      bulk_copy_g2s(slots + static_cast<size_t>(s % HEAD_STAGES) * stage_bytes, src - lo, n16, b);
+      bulk_copy_g2s_hint(slots + static_cast<size_t>(s % HEAD_STAGES) * stage_bytes, src - lo16(src), n16, b, l2_evict_first());
     };
     if (tid == 0)
       for (int s = 0; s < min(nst, HEAD_STAGES); ++s) issue(s);
-    const int GL = lanes_for(nb), lg = lane & (GL - 1), gpw = 32 / GL, gid = warp * gpw + lane / GL, base = lane - lg;
+    const int GL = lanes_for(nb), lg = lane & (GL - 1), gpw = 32 / GL, ngroups = NW * gpw, gid = warp * gpw + lane / GL, base = lane - lg;
+    const int half = ngroups / 2, side = gid / half, hg = gid - side * half;   // which of the two stages, and the group in it
     const bool has_blk = lg < nb;
-    const SmemAct act{xq_qs, xq_bs, xq_d};
     unsigned long long best = 0;
-    for (int s = 0; s < nst; ++s) {
-      const uint32_t hpar = static_cast<uint32_t>((s / HEAD_STAGES) & 1);
-      if (!mbar_wait_bounded(&hb[s % HEAD_STAGES], hpar)) set_error(&st->err, ERR_WAIT_COPY);
-      const int r0 = v0 + s * HEAD_ROWS, cnt = min(HEAD_ROWS, v1 - r0);
-      const uint8_t *buf = slots + static_cast<size_t>(s % HEAD_STAGES) * stage_bytes + stage_lo(s);
-      // HEAD_ROWS rows, a group of lanes each (NW * gpw >= HEAD_ROWS groups)
-      const bool valid = gid < cnt;
-      float t = 0.f;
-      if (valid && has_blk) t = kq_block_s(a.output.type, buf + static_cast<size_t>(gid) * rb, lg, act, lg);
-      float sum = 0.f;
-      for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, __shfl_sync(FULL, t, base + b));
-      if (valid && lg == 0) {
-        const float v = a.logit_scale != 1.0f ? __fdiv_rn(sum, a.logit_scale) : sum;
-        __stcg(a.logits + r0 + gid, v);
-        if (v == v) best = max(best, argmax_key(v, r0 + gid));
+    for (int s0 = 0; s0 < nst; s0 += 2) {
+      const int s = s0 + side;
+      const bool live = s < nst;
+      if (live && !mbar_wait_bounded(&hb[s % HEAD_STAGES], static_cast<uint32_t>((s / HEAD_STAGES) & 1))) set_error(&st->err, ERR_WAIT_COPY);
+      const int r0 = v0 + s * HEAD_ROWS, cnt = live ? min(HEAD_ROWS, v1 - r0) : 0;
+      const uint8_t *buf = slots + static_cast<size_t>(s % HEAD_STAGES) * stage_bytes + (live ? lo16(stage_src(s)) : 0u);
+      for (int q0 = 0; q0 < HEAD_ROWS; q0 += half) {   // the same trip count in every warp
+        const int q = q0 + hg;
+        const bool valid = q < cnt;
+        float t = 0.f;
+        if (valid && has_blk) t = blk_dot_fast(a.output.type, buf + static_cast<size_t>(q) * rb, lg, xq_qs, xq_bs, xq_d, lg);
+        float sum = 0.f;
+        for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, __shfl_sync(FULL, t, base + b));
+        if (valid && lg == 0) {
+          const float v = a.logit_scale != 1.0f ? __fdiv_rn(sum, a.logit_scale) : sum;
+          __stcg(a.logits + r0 + q, v);
+          if (v == v) best = max(best, argmax_key(v, r0 + q));
+        }
       }
-      __syncthreads();   // the buffer is free again
-      if (tid == 0 && s + HEAD_STAGES < nst) issue(s + HEAD_STAGES);
+      __syncthreads();   // both buffers are free again
+      if (tid == 0) {
+        if (s0 + HEAD_STAGES < nst) issue(s0 + HEAD_STAGES);
+        if (s0 + 1 + HEAD_STAGES < nst) issue(s0 + 1 + HEAD_STAGES);
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(FULL, best, o));
@@ -776,7 +849,6 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     __syncthreads();
     if (tid == 0) {
       for (int w = 1; w < NW; ++w) best = max(best, s_best[w]);
-      best = max(best, s_best[0]);
       atomicMax(&st->best, best);
     }
     trace_stamp(a.trace, 13);
@@ -785,7 +857,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   // ---- exit: copies in flight land first; the last CTA out advances the sequence and resets the counters ----------------------
   __syncthreads();
   if (tid == 0) {
-    if (s_flag[1]) mbar_wait_bounded(&bars[K], static_cast<uint32_t>(s_flag[3]));   // an unconsumed router copy
+    if (s_flag[1]) mbar_wait_bounded(rbar, static_cast<uint32_t>(s_flag[3]));   // an unconsumed router copy
+    if (s_flag[5]) mbar_wait_bounded(dbar, static_cast<uint32_t>(s_flag[6]));   // an unconsumed dense copy
     if (s_flag[4] >= 0)   // the last layer's expert copies (waited already unless a wait gave up)
       for (int k = 0; k < K; ++k) mbar_wait_bounded(&bars[k], static_cast<uint32_t>(s_flag[4] & 1));
     __threadfence();

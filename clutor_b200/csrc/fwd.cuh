@@ -12,6 +12,8 @@ constexpr int FWD_MAX_K = 16;       // experts used per token (one warp issues e
 constexpr int FWD_MAX_NE = 128;     // experts per layer the kernel ranks (four threads per expert)
 constexpr int FWD_ATT_CHUNK = 256;  // positions per attention work item
 constexpr int FWD_MAX_GROUP = 16;   // query heads per key/value head
+constexpr int HEAD_ROWS = 24;       // output-matrix rows per shared-memory stage
+constexpr int HEAD_STAGES = 4;      // stages in flight (they span the slots and the dslots); two are computed at a time
 
 // A quantized weight matrix on the device, GGUF blocks as in the file: rows x cols, row r at p + r * rb.
 struct FwdMat {
@@ -69,6 +71,9 @@ struct FwdArgs {
   // per-CTA shared-memory plan (host-computed)
   uint32_t grb, drb, gseg, slot_bytes, dslot_bytes;
   uint32_t off_bars, off_xn, off_xq, off_misc, off_router, off_rprod, off_terms, off_hq, off_xr, off_slots, off_dslots, smem_bytes;
+  uint32_t off_kvstage;        // staged key / value rows of the attention, from off_dslots
+  const float *rope_cs;        // [ctx][hd]: per position hd / 2 cosines then hd / 2 sines of the rotary angles, as the
+                               // reference computes them (c/src/forward.c:428-435)
   int rgu_max, rd_max, nre_max;
   unsigned long long *trace;   // per-CTA phase trace (32 entries per CTA) or null
 };

@@ -47,8 +47,6 @@ const ArchSpec ARCHS[] = {
     {"granitemoe", 0, 1, 1, 0, 1},
 };
 
-constexpr int HEAD_ROWS = 16, HEAD_STAGES = 4;   // fwd.cu's output-matrix stages
-
 float half_to_float(uint16_t h) {
   const uint32_t s = (h >> 15) & 1, e = (h >> 10) & 31, m = h & 1023;
   float v;
@@ -204,6 +202,7 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   const size_t o_rl = take(a.NE * 4), o_hg = take(static_cast<size_t>(a.K) * a.FF * 4), o_lg = take(static_cast<size_t>(a.vocab) * 4);
   const size_t o_rs = take(static_cast<size_t>(a.n_layer) * a.K * 4), o_rw = take(static_cast<size_t>(a.n_layer) * a.K * 4);
   const size_t o_gen = take(static_cast<size_t>(a.ctx) * 4), o_layers = take(sizeof(FwdLayer) * a.n_layer), o_st = take(sizeof(FwdState));
+  const size_t o_rope = take(static_cast<size_t>(a.ctx) * hd * 4);
 
   // ---- the shared-memory plan -------------------------------------------------------------------------------------------
   const int G = c->sms, NW = FWD_THREADS / 32;
@@ -225,7 +224,7 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   const int XQW = std::max(a.E, a.n_q);
   size_t o = 0;
   auto st_take = [&](size_t bytes, size_t align = 16) { const size_t at = al(o, align); o = at + bytes; return static_cast<uint32_t>(at); };
-  a.off_bars = st_take(8 * (a.K + 1 + HEAD_STAGES));
+  a.off_bars = st_take(8 * (a.K + 2 + HEAD_STAGES));
   a.off_xn = st_take(static_cast<size_t>(a.E) * 4);
   a.off_xq = st_take(XQW + 2 * (XQW / 16) + 4 * (XQW / 256));
   a.off_misc = st_take(NW * 8 + 8 * 4 + 3 * 32 * 4 + FWD_MAX_NE * 4 + NW * 8);
@@ -234,12 +233,38 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   a.off_terms = st_take(std::max<size_t>(static_cast<size_t>(a.rd_max) * a.K * nbd * 4, 2 * NW * 8));
   a.off_hq = st_take(static_cast<size_t>(a.K) * a.FF + 2 * (static_cast<size_t>(a.K) * a.FF / 16) + 4 * (static_cast<size_t>(a.K) * a.FF / 256));
   a.off_xr = st_take(static_cast<size_t>(a.rd_max) * 4);
-  const size_t head_need = static_cast<size_t>(HEAD_STAGES) * al(HEAD_ROWS * row_bytes(out->type, a.E) + 32, 16);   // fwd.cu's stages
-  a.off_slots = st_take(std::max<size_t>(static_cast<size_t>(a.K) * a.slot_bytes, head_need), 128);
-  // fwd.cu's attention scratch: queries / value sums [GROUP][hd], then one item's scores: a 256-position chunk of every
-  // head of a group, or (a group of one head: the per-head form at every position) the whole context of one head
-  const size_t att_need = static_cast<size_t>(GRP) * hd * 4 + std::max<size_t>(static_cast<size_t>(GRP) * FWD_ATT_CHUNK, GRP < 2 ? a.ctx : 64) * 4;
-  a.off_dslots = st_take(std::max<size_t>(static_cast<size_t>(a.K) * a.dslot_bytes, att_need), 128);
+  // the slots hold a layer's dense rows (each CTA's rows of wq, wk, wv, wo, one segment after another: fwd.cu's
+  // dense_offset) and then the chosen experts' gate/up rows
+  size_t dense_need = 0;
+  {
+    uint64_t rbmax[4] = {0, 0, 0, 0};
+    for (int l = 0; l < a.n_layer; ++l)
+      for (int q = 0; q < 4; ++q) rbmax[q] = std::max<uint64_t>(rbmax[q], gguf_row_bytes(lo[static_cast<size_t>(l)].t[q]->type, lo[static_cast<size_t>(l)].t[q]->dims[0]));
+    const int QKVR = a.n_q + 2 * a.n_kvw;
+    for (int cc = 0; cc < G; ++cc) {
+      const int q0 = static_cast<int>(static_cast<int64_t>(QKVR) * cc / G), q1 = static_cast<int>(static_cast<int64_t>(QKVR) * (cc + 1) / G);
+      const int e0 = static_cast<int>(static_cast<int64_t>(a.E) * cc / G), e1 = static_cast<int>(static_cast<int64_t>(a.E) * (cc + 1) / G);
+      const int cnt[4] = {std::max(0, std::min(q1, a.n_q) - std::max(q0, 0)),
+                          std::max(0, std::min(q1 - a.n_q, a.n_kvw) - std::max(q0 - a.n_q, 0)),
+                          std::max(0, std::min(q1 - a.n_q - a.n_kvw, a.n_kvw) - std::max(q0 - a.n_q - a.n_kvw, 0)), e1 - e0};
+      size_t need = 0;
+      for (int q = 0; q < 4; ++q) need += al(static_cast<size_t>(cnt[q]) * rbmax[q] + 32, 16);
+      dense_need = std::max(dense_need, need);
+    }
+  }
+  const size_t slots_size = al(std::max<size_t>(static_cast<size_t>(a.K) * a.slot_bytes, dense_need), 128);
+  a.off_slots = st_take(slots_size, 128);
+  // the dslots, right after the slots, hold the chosen experts' down rows, or the attention scratch: queries / value sums
+  // [GROUP][hd], one item's scores (a 256-position chunk of every head of a group, or for a group of one head the whole
+  // context of that head), and the staged key / value rows (64 positions); the output matrix's stages span both regions
+  const size_t att_scores = static_cast<size_t>(GRP) * hd * 4 + std::max<size_t>(static_cast<size_t>(GRP) * FWD_ATT_CHUNK, GRP < 2 ? a.ctx : 64) * 4;
+  a.off_kvstage = static_cast<uint32_t>(al(att_scores, 16));
+  const size_t att_need = a.off_kvstage + static_cast<size_t>(64) * hd * 2;
+  const size_t head_need = static_cast<size_t>(HEAD_STAGES) * al(HEAD_ROWS * row_bytes(out->type, a.E) + 32, 16);
+  const size_t dslots_size = std::max<size_t>(std::max<size_t>(static_cast<size_t>(a.K) * a.dslot_bytes, att_need),
+                                              head_need > slots_size ? head_need - slots_size : 0);
+  a.off_dslots = st_take(dslots_size, 128);
+  if (a.off_dslots != a.off_slots + slots_size) { errf(err, errlen, "internal: the slots and dslots are not adjacent"); return 1; }
   a.smem_bytes = static_cast<uint32_t>(o + 16);
   (void)nb;
   if (a.smem_bytes > static_cast<uint32_t>(c->max_smem)) {
@@ -287,6 +312,20 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   a.att = reinterpret_cast<float *>(m->dev + o_att);
   a.part = reinterpret_cast<float *>(m->dev + o_part);
   a.scores = reinterpret_cast<float *>(m->dev + o_scores);
+  {   // the rotary angles' cosines and sines exactly as the reference computes them (c/src/forward.c:420-435): the same
+      // float expression and the same C library's powf, cosf and sinf, for every position of the context
+    const int H = hd / 2;
+    std::vector<float> freq(static_cast<size_t>(H)), cs(static_cast<size_t>(a.ctx) * hd);
+    for (int i = 0; i < H; ++i) freq[static_cast<size_t>(i)] = powf(a.rope_base, -2.0f * static_cast<float>(i) / static_cast<float>(hd));
+    for (int p = 0; p < a.ctx; ++p)
+      for (int i = 0; i < H; ++i) {
+        const float theta = static_cast<float>(p) * freq[static_cast<size_t>(i)];
+        cs[static_cast<size_t>(p) * hd + i] = cosf(theta);
+        cs[static_cast<size_t>(p) * hd + H + i] = sinf(theta);
+      }
+    CUDA_OR(cudaMemcpy(m->dev + o_rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "uploading the rotary tables");
+    a.rope_cs = reinterpret_cast<const float *>(m->dev + o_rope);
+  }
   a.rlogits = reinterpret_cast<float *>(m->dev + o_rl);
   a.hg = reinterpret_cast<float *>(m->dev + o_hg);
   a.logits = reinterpret_cast<float *>(m->dev + o_lg);

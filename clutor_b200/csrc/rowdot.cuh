@@ -345,13 +345,16 @@ struct SmemAct {
 CLB_DEV int4 act_chunk(const SmemAct &a, int blk, int j) {
   return *reinterpret_cast<const int4 *>(a.qs + q8k_chunk_off(blk, j, true));
 }
+// (The outer loops of these two stay rolled: kernels that run every phase once per layer are bound by fetching their
+// code, not by these loops' overhead.)
+template <bool COMPACT = true>
 CLB_DEV float q4k_block_s(const uint8_t *bp, const SmemAct &a, int blk) {
   const uint32_t dm = lds_u32(bp), w0 = lds_u32(bp + 4), w1 = lds_u32(bp + 8), w2 = lds_u32(bp + 12);
   const uint32_t scA = w0 & 0x3f3f3f3fu, mnA = w1 & 0x3f3f3f3fu;
   const uint32_t scB = (w2 & 0x0f0f0f0fu) | (((w0 >> 6) & 0x03030303u) << 4);
   const uint32_t mnB = ((w2 >> 4) & 0x0f0f0f0fu) | (((w1 >> 6) & 0x03030303u) << 4);
   int sumi = 0;
-#pragma unroll
+#pragma unroll(COMPACT ? 1 : 4)
   for (int g = 0; g < 4; ++g) {
     const uint4 x0 = reinterpret_cast<const uint4 *>(bp + 16 + 32 * g)[0];
     const uint4 x1 = reinterpret_cast<const uint4 *>(bp + 16 + 32 * g)[1];
@@ -370,16 +373,17 @@ CLB_DEV float q4k_block_s(const uint8_t *bp, const SmemAct &a, int blk) {
   }
   const int16_t *b16 = a.bsums + 16 * blk;
   int summs = 0;
-#pragma unroll
+#pragma unroll(COMPACT ? 1 : 8)
   for (int j = 0; j < 8; ++j) summs += byte_of(j < 4 ? mnA : mnB, j & 3) * (b16[2 * j] + b16[2 * j + 1]);
   const float d = f16_bits_to_f32(static_cast<uint16_t>(dm & 0xffffu)), dmin = f16_bits_to_f32(static_cast<uint16_t>(dm >> 16));
   return __fmul_rn(a.dd[blk], __fsub_rn(__fmul_rn(d, static_cast<float>(sumi)), __fmul_rn(dmin, static_cast<float>(summs))));
 }
+template <bool COMPACT = true>
 CLB_DEV float q6k_block_s(const uint8_t *bp, const SmemAct &a, int blk) {
   const int8_t *sc = reinterpret_cast<const int8_t *>(bp + 192);
   const int16_t *b16 = a.bsums + 16 * blk;
   int sumi = 0;
-#pragma unroll
+#pragma unroll(COMPACT ? 1 : 2)
   for (int h = 0; h < 2; ++h) {
     int dot[8];
 #pragma unroll
@@ -412,19 +416,22 @@ CLB_DEV float q6k_block_s(const uint8_t *bp, const SmemAct &a, int blk) {
   return __fmul_rn(__fmul_rn(d, a.dd[blk]), static_cast<float>(sumi));
 }
 // Weight block blk of `row` times activation block ablk (the swizzle key of the array: its index in the whole array).
+// COMPACT keeps the outer loops rolled (small code for code run once per phase); else they are unrolled (hot loops).
+template <bool COMPACT = true>
 CLB_DEV float kq_block_s(uint32_t type, const uint8_t *row, int blk, const SmemAct &a, int ablk) {
-  return type == T_Q4_K ? q4k_block_s(row + 144 * blk, a, ablk) : q6k_block_s(row + 210 * blk, a, ablk);
+  return type == T_Q4_K ? q4k_block_s<COMPACT>(row + 144 * blk, a, ablk) : q6k_block_s<COMPACT>(row + 210 * blk, a, ablk);
 }
 
 // Q8_K quantization of nblocks 256-blocks of floats in global memory (written by other CTAs; read through L2) into shared
-// qs/d/bsums. Each warp takes blocks warp, warp + nwarps, ...; a lane issues the loads of up to four blocks before the first
-// reduction, so their round trips overlap.
+// qs/d/bsums. Each warp takes blocks warp, warp + nwarps, ...; a lane issues the loads of up to BATCH blocks before the
+// first reduction, so their round trips overlap.
+template <int BATCH = 4>
 CLB_DEV void q8k_quantize_global(const float *src, int nblocks, int8_t *qs, float *dd, int16_t *bsums, int warp, int nwarps,
                                  int lane, bool swz = false) {
-  for (int b0 = warp; b0 < nblocks; b0 += 4 * nwarps) {
-    float4 v[4][2];
+  for (int b0 = warp; b0 < nblocks; b0 += BATCH * nwarps) {
+    float4 v[BATCH][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < BATCH; ++j) {
       const int b = b0 + j * nwarps;
       if (b < nblocks) {
         const float4 *p = reinterpret_cast<const float4 *>(src + 256 * b + 8 * lane);
@@ -433,7 +440,7 @@ CLB_DEV void q8k_quantize_global(const float *src, int nblocks, int8_t *qs, floa
       }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < BATCH; ++j) {
       const int b = b0 + j * nwarps;
       if (b >= nblocks) break;
       const float vals[8] = {v[j][0].x, v[j][0].y, v[j][0].z, v[j][0].w, v[j][1].x, v[j][1].y, v[j][1].z, v[j][1].w};
