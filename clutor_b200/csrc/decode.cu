@@ -14,7 +14,8 @@
 //   2  the last warp forms this CTA's router logits as the reference's dotf does (c/src/forward.c:574-581): eight lanes per
 //      expert, eight strided float sums in element order, combined ((0+1)+(2+3))+((4+5)+(6+7)); logits to global memory,
 //      counter 0 += experts scored. Meanwhile the other warps form the Q8_K blocks of xn;
-//   3  when counter 0 reaches NE, warp 0 forms the softmax (double sum, c/src/forward.c:954-958); every thread then ranks
+//   3  when counter 0 reaches NE, DECODE_THREADS / 4 threads form the softmax, one expert each (double sum,
+//      c/src/forward.c:954-958); every thread then ranks
 //      a quarter of an expert's competitors (ties to the lower id: the order of the reference's repeated arg-max,
 //      c/src/forward.c:975-980); warp 0 renormalises (c/src/forward.c:984). Every CTA does this itself;
 //   4  one lane per chosen expert issues the bulk copies of this CTA's share of it: gate and up rows [FF*c/G, FF*(c+1)/G),
@@ -166,7 +167,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     trace_stamp(a.trace, 6);
   }
 
-  // ---- 3: softmax (warp 0), top-k by rank counting (every thread), renormalisation (c/src/forward.c:954-984) ------------
+  // ---- 3: softmax, top-k by rank counting (every thread), renormalisation (c/src/forward.c:954-984) ----------------------
   if (a.mode == 2) {   // the routing is given, renormalised already
     if (tid < K) {
       const int e = a.sel_in[tid];
@@ -175,47 +176,37 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       s_wt[tid] = a.wt_in[tid];
       s_wn[tid] = a.wt_in[tid];
     }
-  } else if (warp == 0) {
-    if (lane == 0 && !wait_counter(&a.sync[0], static_cast<uint32_t>(NE))) {
-      set_error(a.err, ERR_WAIT_ROUTER);
-      s_flag[0] = 1;
-    }
-    __syncwarp();
-    trace_stamp(a.trace, 7);
-    if (!s_flag[0]) {
-      constexpr int PER = DECODE_THREADS / 4 / 32;   // experts per lane (NE <= DECODE_THREADS / 4)
-      float l[PER], ev[PER];
-      float mx = -INFINITY;
+  } else if (tid == 0 && !wait_counter(&a.sync[0], static_cast<uint32_t>(NE))) {
+    set_error(a.err, ERR_WAIT_ROUTER);
+    s_flag[0] = 1;
+  }
+  __syncthreads();
+  trace_stamp(a.trace, 7);
+  if (a.mode != 2 && !s_flag[0]) {   // the softmax over DECODE_THREADS / 4 threads, one expert each
+    constexpr int SW = DECODE_THREADS / 4 / 32;   // softmax warps
+    float *wmax = s_wt;                           // [SW] (s_wt is written after the ranking)
+    const float lv = tid < NE ? __ldcg(a.logits + tid) : -INFINITY;
+    float mx = lv;
 #pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        const int e = lane + 32 * j;
-        l[j] = e < NE ? __ldcg(a.logits + e) : -INFINITY;
-        mx = fmaxf(mx, l[j]);
-      }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    if (lane == 0 && warp < SW) wmax[warp] = mx;
+    __syncthreads();
+    mx = wmax[0];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-      trace_stamp(a.trace, 8);
-      double part[PER];
+    for (int w = 1; w < SW; ++w) mx = fmaxf(mx, wmax[w]);
+    trace_stamp(a.trace, 8);
+    const float ev = tid < NE ? expf_cr(__fsub_rn(lv, mx)) : 0.f;
+    double part = static_cast<double>(ev);   // each warp's 32 experts by a shuffle tree, then the warps in order
 #pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        ev[j] = lane + 32 * j < NE ? expf_cr(__fsub_rn(l[j], mx)) : 0.f;
-        part[j] = static_cast<double>(ev[j]);
-      }
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(FULL, part, o);
+    if (lane == 0 && warp < SW) s_red[warp] = part;
+    __syncthreads();
+    double tot = 0.0;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int j = 0; j < PER; ++j) part[j] += __shfl_xor_sync(FULL, part[j], o);
-      double tot = 0.0;   // the 32-expert partial sums in expert order
-#pragma unroll
-      for (int j = 0; j < PER; ++j) tot += part[j];
-      trace_stamp(a.trace, 9);
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        const int e = lane + 32 * j;
-        if (e < ((NE + 3) & ~3)) probs[e] = e < NE ? __double2float_rn(__ddiv_rn(static_cast<double>(ev[j]), tot)) : -1.0f;
-      }
-      trace_stamp(a.trace, 10);
-    }
+    for (int w = 0; w < SW; ++w) tot += s_red[w];
+    trace_stamp(a.trace, 9);
+    if (tid < ((NE + 3) & ~3)) probs[tid] = tid < NE ? __double2float_rn(__ddiv_rn(static_cast<double>(ev), tot)) : -1.0f;
+    trace_stamp(a.trace, 10);
   }
   __syncthreads();
   if (a.mode != 2 && !s_flag[0]) {   // rank = experts ahead of this one in the reference's arg-max order; four threads per expert

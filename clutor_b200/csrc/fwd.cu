@@ -38,25 +38,24 @@ constexpr int VB = 64;       // positions of values staged at a time
 
 CLB_DEV int ld_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
 
-// ---- out-of-line steps (one copy of their code for every call) and small inline ones --------------------------------------------------------------
-__device__ __noinline__ float blk_dot(uint32_t type, const uint8_t *row, int blk, const int8_t *qs, const int16_t *bs,
+// ---- steps used in several phases (inline: a call would save registers to local memory, which is L2 here) --------------------------------------------------------------
+CLB_DEV float blk_dot(uint32_t type, const uint8_t *row, int blk, const int8_t *qs, const int16_t *bs,
                                       const float *dd, int ablk) {
   return kq_block_s(type, row, blk, SmemAct{qs, bs, dd}, ablk);
 }
-__device__ __noinline__ float blk_dot_fast(uint32_t type, const uint8_t *row, int blk, const int8_t *qs, const int16_t *bs,
+CLB_DEV float blk_dot_fast(uint32_t type, const uint8_t *row, int blk, const int8_t *qs, const int16_t *bs,
                                            const float *dd, int ablk) {
   return kq_block_s<false>(type, row, blk, SmemAct{qs, bs, dd}, ablk);
 }
-__device__ __noinline__ void quant_smem(const float *x, int n, int8_t *qs, float *dd, int16_t *bs, int warp, int nwarps, int lane) {
+CLB_DEV void quant_smem(const float *x, int n, int8_t *qs, float *dd, int16_t *bs, int warp, int nwarps, int lane) {
   q8k_quantize_block(x, n, qs, dd, bs, warp, nwarps, lane, true);
 }
-__device__ __noinline__ void quant_global(const float *src, int nblocks, int8_t *qs, float *dd, int16_t *bs, int warp, int nwarps,
+CLB_DEV void quant_global(const float *src, int nblocks, int8_t *qs, float *dd, int16_t *bs, int warp, int nwarps,
                                           int lane) {
   q8k_quantize_global<2>(src, nblocks, qs, dd, bs, warp, nwarps, lane, true);
 }
 CLB_DEV float exp_cr(float x) { return expf_cr(x); }
 CLB_DEV float swiglu(float g, float u) { return silu_mul(g, u); }
-CLB_DEV float div_d(float a, double b) { return __double2float_rn(__ddiv_rn(static_cast<double>(a), b)); }
 
 // The block of one grid barrier: every CTA arrives, then waits for all G (bounded; returns early when any CTA has
 // recorded an error). Returns false on a timeout or a recorded error.
@@ -90,7 +89,7 @@ struct Grid {
 // x * (1 / sqrtf(mean(x^2) + eps)) * w, the mean of squares in double. red: NW doubles of shared scratch.
 CLB_DEV void rmsnorm_to_smem(const float *x, const float *w, float *xn, int n, float eps, double *red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int XV = 4096 / 4 / FWD_THREADS;
+  constexpr int XV = (4096 / 4 + FWD_THREADS - 1) / FWD_THREADS;
   float4 xv[XV];
   double ss = 0.0;
 #pragma unroll
@@ -128,7 +127,7 @@ CLB_DEV int lanes_for(int nb) { return nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 :
 // vector in shared memory: a group of lanes per row, one lane per block, the block terms added in block order at the
 // group's first lane. mode 0: dst[i] = value; mode 1: dst[i] = dst[i] + scale * value (the residual update). Call from
 // all threads.
-__device__ __noinline__ void gemv_rows(uint32_t type, const uint8_t *rows, uint32_t rb, int nb, int n, const int8_t *qs,
+CLB_DEV void gemv_rows(uint32_t type, const uint8_t *rows, uint32_t rb, int nb, int n, const int8_t *qs,
                                        const float *dd, const int16_t *bs, float *dst, int mode, float scale) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int GL = lanes_for(nb), lg = lane & (GL - 1), gpw = 32 / GL, ngroups = NW * gpw, gid = warp * gpw + lane / GL;
@@ -222,7 +221,9 @@ CLB_DEV uint32_t lo16(const void *p) { return static_cast<uint32_t>(reinterpret_
 CLB_DEV uint32_t dense_offset(const FwdLayer &Ly, const int (&r0)[4], const int (&r1)[4], int q) {
   const FwdMat mats[4] = {Ly.wq, Ly.wk, Ly.wv, Ly.wo};
   uint32_t off = 0;
-  for (int i = 0; i < q; ++i) off += (static_cast<uint32_t>(r1[i] - r0[i]) * mats[i].rb + 32u + 15u) & ~15u;
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+    if (i < q) off += (static_cast<uint32_t>(r1[i] - r0[i]) * mats[i].rb + 32u + 15u) & ~15u;
   return off;
 }
 
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     {
       const FwdMat mats[3] = {Ly.wq, Ly.wk, Ly.wv};
       float *outs[3] = {a.qkv + dr0[0], a.qkv + nq + dr0[1], a.qkv + nq + nk + dr0[2]};
-#pragma unroll 1
+#pragma unroll
       for (int q = 0; q < 3; ++q) {
         const uint8_t *rows = slots + dense_offset(Ly, dr0, dr1, q) + lo16(mats[q].p + static_cast<size_t>(dr0[q]) * mats[q].rb);
         gemv_rows(mats[q].type, rows, mats[q].rb, nb, dr1[q] - dr0[q], xq_qs, xq_d, xq_bs, outs[q], 0, 0.f);
@@ -496,7 +497,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         }
         trace_stamp(a.trace, 16);
         // o[jj][i] = sum over t in order of w_t * v_t[i] (w = e grouped, p plain); values staged VB positions at a time
-        constexpr int MAXC = FWD_MAX_GROUP * hd / FWD_THREADS > 0 ? FWD_MAX_GROUP * hd / FWD_THREADS : 1;
+        constexpr int MAXC = (FWD_MAX_GROUP * hd + FWD_THREADS - 1) / FWD_THREADS;   // value sums per thread
         float o[MAXC];
 #pragma unroll
         for (int u = 0; u < MAXC; ++u) o[u] = 0.f;
@@ -509,15 +510,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
             reinterpret_cast<uint4 *>(kvs)[i] = __ldcg(reinterpret_cast<const uint4 *>(vb + static_cast<size_t>(t0 + b0 + t) * nk) + q);
           }
           __syncthreads();
+          // the thread's sums advance together, one position at a time (independent chains, in position order each)
+          for (int t = 0; t < cnt; ++t) {
 #pragma unroll
-          for (int u = 0; u < MAXC; ++u) {
-            const int oi = tid + u * FWD_THREADS;
-            if (oi < NH * hd) {
-              const int jj = oi / hd, i = oi - jj * hd;
-              const float *w = sc + jj * n + b0;
-              float acc = o[u];
-              for (int t = 0; t < cnt; ++t) acc = __fadd_rn(acc, __fmul_rn(w[t], __half2float(kvs[t * hd + i])));
-              o[u] = acc;
+            for (int u = 0; u < MAXC; ++u) {
+              const int oi = tid + u * FWD_THREADS;
+              if (oi < NH * hd) {
+                const int jj = oi / hd, i = oi - jj * hd;
+                o[u] = __fadd_rn(o[u], __fmul_rn(sc[jj * n + b0 + t], __half2float(kvs[t * hd + i])));
+              }
             }
           }
         }
@@ -620,59 +621,51 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       quant_smem(xn, E, xq_qs, xq_d, xq_bs, warp, RW, lane);
     }
     trace_stamp(a.trace, 7);
-    if (warp == 0) {   // softmax (c/src/forward.c:954-958)
-      if (lane == 0) {
-        const uint32_t target = static_cast<uint32_t>(NE) * static_cast<uint32_t>(l + 1);
-        bool got = false;
-  #pragma unroll 1
+    // softmax (c/src/forward.c:954-958) over FWD_MAX_NE threads, one expert each: the maximum, e = expf(l - max), the sum
+    // in double (each warp's 32 experts by a shuffle tree, then the warps in order), p = (float)(e / sum)
+    if (tid == 0) {
+      const uint32_t target = static_cast<uint32_t>(NE) * static_cast<uint32_t>(l + 1);
+      bool got = false;
+#pragma unroll 1
       for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
-          if (ld_acquire(&st->sync[1]) >= target) { got = true; break; }
-          if ((i & 127) == 127 && ld_volatile(&st->err)) break;
-          if (i > 4096) __nanosleep(64);
-        }
-        if (!got) set_error(&st->err, ERR_WAIT_ROUTER);
-        s_flag[2] = got;
-        trace_stamp_here(a.trace, 20);
+        if (ld_acquire(&st->sync[1]) >= target) { got = true; break; }
+        if ((i & 127) == 127 && ld_volatile(&st->err)) break;
+        if (i > 4096) __nanosleep(64);
       }
-      __syncwarp();
-      if (s_flag[2]) {
-        constexpr int PER = FWD_MAX_NE / 32;
-        float lg[PER], ev[PER];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < PER; ++j) {
-          const int e = lane + 32 * j;
-          lg[j] = e < NE ? __ldcg(a.rlogits + e) : -INFINITY;
-          mx = fmaxf(mx, lg[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-#pragma unroll 1
-        for (int j = 0; j < PER; ++j) probs[lane + 32 * j] = lane + 32 * j < NE ? exp_cr(__fsub_rn(lg[j], mx)) : 0.f;
-#pragma unroll
-        for (int j = 0; j < PER; ++j) ev[j] = probs[lane + 32 * j];
-        double part[PER];
-#pragma unroll
-        for (int j = 0; j < PER; ++j) part[j] = static_cast<double>(ev[j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-          for (int j = 0; j < PER; ++j) part[j] += __shfl_xor_sync(FULL, part[j], o);
-        double tot = 0.0;
-#pragma unroll
-        for (int j = 0; j < PER; ++j) tot += part[j];
-#pragma unroll 1
-        for (int j = 0; j < PER; ++j) {
-          const int e = lane + 32 * j;
-          if (e < ((NE + 3) & ~3)) probs[e] = e < NE ? div_d(probs[e], tot) : -1.0f;
-        }
-        trace_stamp(a.trace, 21);
-      }
+      if (!got) set_error(&st->err, ERR_WAIT_ROUTER);
+      s_flag[2] = got;
+      trace_stamp_here(a.trace, 20);
     }
     __syncthreads();
     if (!s_flag[2]) { ok = false; break; }
+    {
+      constexpr int SW = FWD_MAX_NE / 32;   // softmax warps
+      float *wmax = s_wt;                   // [SW] (s_wt is written after the ranking)
+      const float lgv = tid < NE ? __ldcg(a.rlogits + tid) : -INFINITY;
+      float mx = lgv;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+      if (lane == 0 && warp < SW) wmax[warp] = mx;
+      __syncthreads();
+      mx = wmax[0];
+#pragma unroll
+      for (int w = 1; w < SW; ++w) mx = fmaxf(mx, wmax[w]);
+      const float ev = tid < NE ? exp_cr(__fsub_rn(lgv, mx)) : 0.f;
+      double part = static_cast<double>(ev);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(FULL, part, o);
+      if (lane == 0 && warp < SW) s_red[warp] = part;
+      __syncthreads();
+      double tot = 0.0;
+#pragma unroll
+      for (int w = 0; w < SW; ++w) tot += s_red[w];
+      if (tid < ((NE + 3) & ~3)) probs[tid] = tid < NE ? __double2float_rn(__ddiv_rn(static_cast<double>(ev), tot)) : -1.0f;
+      trace_stamp(a.trace, 21);
+    }
+    __syncthreads();
     {   // top-k by rank counting, ties to the lower id (c/src/forward.c:975-980)
-      const int e = tid >> 2, part = tid & 3, n4 = (NE + 3) / 4, per = (n4 + 3) / 4;
+      constexpr int TPE = FWD_THREADS / FWD_MAX_NE;   // threads per expert, each a share of its competitors
+      const int e = tid / TPE, part = tid % TPE, n4 = (NE + 3) / 4, per = (n4 + TPE - 1) / TPE;
       const float pe = e < NE ? probs[e] : 0.f;
       int rank = 0;
       const float4 *p4 = reinterpret_cast<const float4 *>(probs);
@@ -682,8 +675,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         rank += (q.x > pe || (q.x == pe && f < e)) + (q.y > pe || (q.y == pe && f + 1 < e)) +
                 (q.z > pe || (q.z == pe && f + 2 < e)) + (q.w > pe || (q.w == pe && f + 3 < e));
       }
-      rank += __shfl_xor_sync(FULL, rank, 1);
-      rank += __shfl_xor_sync(FULL, rank, 2);
+#pragma unroll
+      for (int o = 1; o < TPE; o <<= 1) rank += __shfl_xor_sync(FULL, rank, o);
       if (e < NE && part == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = pe; }
     }
     __syncthreads();
@@ -709,8 +702,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     };
     auto dn_src = [&](int k) -> const uint8_t * { return Ly.down + static_cast<size_t>(s_sel[k]) * Ly.down_slab + static_cast<size_t>(i0) * a.drb; };
     if (tid == 0) s_flag[4] = l;   // read at the exit only
-    if (lane == 0 && warp < K) {
-      const int k = warp;
+    for (int k = warp; lane == 0 && k < K; k += NW) {
       uint8_t *gs = slots + static_cast<size_t>(k) * a.slot_bytes, *ds = dslots + static_cast<size_t>(k) * a.dslot_bytes;
       const uint8_t *src[3] = {gu_src(k, 0), gu_src(k, 1), dn_src(k)};
       uint8_t *dst[3] = {gs, gs + a.gseg, ds};
