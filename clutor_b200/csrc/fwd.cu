@@ -34,7 +34,6 @@ namespace {
 constexpr int NW = FWD_THREADS / 32;
 constexpr int RW = NW - 1;   // the router warp
 constexpr int SB = 32;       // positions per attention-score item
-constexpr int VB = 64;       // positions of values staged at a time
 
 CLB_DEV int ld_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
 
@@ -459,85 +458,92 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     if (!(ok = grid.sync())) break;
 
     // ---- B2: softmax and weighted values in the reference's order --------------------------------------------------------
-    // grouped: an item per (key/value head, chunk of 256 positions): per query head the chunk's maximum m,
-    // e_t = expf(s_t - m), their sum l in position order, o = sum_t e_t v_t in position order; one chunk gives
-    // o * (1 / l) directly, more are merged below. plain: an item per query head over every position: the maximum, e_t,
-    // their sum in order, then o = sum_t (e_t / sum) v_t in order.
+    // grouped: an item per (key/value head, chunk of 256 positions, quarter of the head dimension): per query head the
+    // chunk's maximum m, e_t = expf(s_t - m), their sum l in position order, o = sum_t e_t v_t in position order; one chunk
+    // gives o * (1 / l) directly, more are merged below. plain: an item per (query head, quarter of the head dimension)
+    // over every position: the maximum, e_t, their sum in order, then o = sum_t (e_t / sum) v_t in order. Every value sum
+    // is one thread's chain over the positions; the quarters spread an item's chains over four CTAs.
     {
-      const int items = grouped ? a.n_kv * nchunk : a.n_head;
+      constexpr int DQ = 4, HQ = hd / DQ;   // quarters of the head dimension, and their width
+      const int items = (grouped ? a.n_kv * nchunk : a.n_head) * DQ;
       float *hm = probs;   // [16] maxima, [16] sums
       for (int item = c; item < items; item += G) {
-        const int g = grouped ? item / nchunk : item / GRP;
-        const int ch = grouped ? item - g * nchunk : 0;
-        const int jb = grouped ? 0 : item - g * GRP, NH = grouped ? GRP : 1;
+        const int it = item / DQ, dq = item - it * DQ;
+        const int g = grouped ? it / nchunk : it / GRP;
+        const int ch = grouped ? it - g * nchunk : 0;
+        const int jb = grouped ? 0 : it - g * GRP, NH = grouped ? GRP : 1;
         const int t0 = ch * FWD_ATT_CHUNK, n = grouped ? min(FWD_ATT_CHUNK, pos + 1 - t0) : pos + 1;
         __syncthreads();
+        // the quarter of the values of (up to FWD_ATT_CHUNK) positions into shared memory, loads in flight while the
+        // weights form
+        const __half *vb = a.vc + cache_l + g * hd + dq * HQ;
+        auto stage_values = [&](int b0, int cnt) {
+          for (int i = tid; i < cnt * (HQ / 8); i += FWD_THREADS) {
+            const int t = i / (HQ / 8), q = i - t * (HQ / 8);
+            reinterpret_cast<uint4 *>(kvs)[i] = __ldcg(reinterpret_cast<const uint4 *>(vb + static_cast<size_t>(t0 + b0 + t) * nk) + q);
+          }
+        };
+        stage_values(0, min(n, FWD_ATT_CHUNK));
         for (int i = tid; i < NH * n; i += FWD_THREADS) {
           const int jj = i / n, t = i - jj * n;
           sc[i] = __ldcg(a.scores + static_cast<size_t>(g * GRP + jb + jj) * a.ctx + t0 + t);
         }
         __syncthreads();
-        for (int jj = warp; jj < NH; jj += NW) {   // a warp per head: the maximum, then e_t
+        for (int jj = warp; jj < NH; jj += NW) {   // a warp per head: the maximum
           float mx = -INFINITY;
           for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sc[jj * n + t]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-          for (int t = lane; t < n; t += 32) sc[jj * n + t] = exp_cr(__fsub_rn(sc[jj * n + t], mx));
           if (lane == 0) hm[jj] = mx;
         }
         __syncthreads();
-        if (tid < NH) {   // the sums, in position order
-          float sum = 0.f;
-          for (int t = 0; t < n; ++t) sum = __fadd_rn(sum, sc[tid * n + t]);
-          hm[16 + tid] = sum;
-        }
-        if (!grouped) {
-          __syncthreads();
-          for (int t = tid; t < n; t += FWD_THREADS) sc[t] = __fdiv_rn(sc[t], hm[16]);   // p_t = e_t / sum
-        }
+        for (int i = tid; i < NH * n; i += FWD_THREADS) sc[i] = exp_cr(__fsub_rn(sc[i], hm[i / n]));   // e_t, every thread
+        __syncthreads();
         trace_stamp(a.trace, 16);
-        // o[jj][i] = sum over t in order of w_t * v_t[i] (w = e grouped, p plain); values staged VB positions at a time
-        constexpr int MAXC = (FWD_MAX_GROUP * hd + FWD_THREADS - 1) / FWD_THREADS;   // value sums per thread
-        float o[MAXC];
-#pragma unroll
-        for (int u = 0; u < MAXC; ++u) o[u] = 0.f;
-        const __half *vb = a.vc + cache_l + g * hd;
-        for (int b0 = 0; b0 < n; b0 += VB) {
-          const int cnt = min(VB, n - b0);
-          __syncthreads();   // the previous block's readers are done
-          for (int i = tid; i < cnt * (hd / 8); i += FWD_THREADS) {
-            const int t = i / (hd / 8), q = i - t * (hd / 8);
-            reinterpret_cast<uint4 *>(kvs)[i] = __ldcg(reinterpret_cast<const uint4 *>(vb + static_cast<size_t>(t0 + b0 + t) * nk) + q);
+        // thread (jj, i): the chain of head jj, dimension dq * HQ + i; threads jj < NH also form head jj's sum l
+        const int jj = tid / HQ, i = tid - jj * HQ;
+        const bool chain = jj < NH;
+        float o = 0.f, l = 0.f;
+        if (!grouped) {   // plain: the sum first, then p_t = e_t / sum
+          if (tid == 0) {
+            for (int t = 0; t < n; ++t) l = __fadd_rn(l, sc[t]);
+            hm[16] = l;
           }
           __syncthreads();
-          // the thread's sums advance together, one position at a time (independent chains, in position order each)
-          for (int t = 0; t < cnt; ++t) {
-#pragma unroll
-            for (int u = 0; u < MAXC; ++u) {
-              const int oi = tid + u * FWD_THREADS;
-              if (oi < NH * hd) {
-                const int jj = oi / hd, i = oi - jj * hd;
-                o[u] = __fadd_rn(o[u], __fmul_rn(sc[jj * n + b0 + t], __half2float(kvs[t * hd + i])));
-              }
+          for (int t = tid; t < n; t += FWD_THREADS) sc[t] = __fdiv_rn(sc[t], hm[16]);
+          __syncthreads();
+          for (int b0 = 0; b0 < n; b0 += FWD_ATT_CHUNK) {   // one head may span many chunks' worth of positions
+            const int cnt = min(FWD_ATT_CHUNK, n - b0);
+            if (b0 > 0) {
+              __syncthreads();
+              stage_values(b0, cnt);
+              __syncthreads();
             }
+            if (chain)
+              for (int t = 0; t < cnt; ++t) o = __fadd_rn(o, __fmul_rn(sc[b0 + t], __half2float(kvs[t * HQ + i])));
           }
+        } else if (chain) {   // n <= FWD_ATT_CHUNK: every value is staged
+          const float *w = sc + jj * n;
+          const bool sums = tid < NH;   // also the sum of head tid
+          const float *ws = sc + tid * n;
+          for (int t = 0; t < n; ++t) {
+            o = __fadd_rn(o, __fmul_rn(w[t], __half2float(kvs[t * HQ + i])));
+            if (sums) l = __fadd_rn(l, ws[t]);
+          }
+          if (sums) hm[16 + tid] = l;
         }
         __syncthreads();
         trace_stamp(a.trace, 17);
-#pragma unroll
-        for (int u = 0; u < MAXC; ++u) {
-          const int oi = tid + u * FWD_THREADS;
-          if (oi < NH * hd) {
-            const int jj = oi / hd, i = oi - jj * hd, h = g * GRP + jb + jj;
-            if (!grouped) {
-              __stcg(a.att + h * hd + i, o[u]);
-            } else if (nchunk == 1) {   // the merge of one chunk: weight expf(0) = 1, so o * (1 / l)
-              __stcg(a.att + h * hd + i, __fmul_rn(o[u], __fdiv_rn(1.0f, hm[16 + jj])));
-            } else {
-              float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + jj) * (2 + hd);
-              if (i == 0) { __stcg(pp, hm[jj]); __stcg(pp + 1, hm[16 + jj]); }
-              __stcg(pp + 2 + i, o[u]);
-            }
+        if (chain) {
+          const int h = g * GRP + jb + jj, d = dq * HQ + i;
+          if (!grouped) {
+            __stcg(a.att + h * hd + d, o);
+          } else if (nchunk == 1) {   // the merge of one chunk: weight expf(0) = 1, so o * (1 / l)
+            __stcg(a.att + h * hd + d, __fmul_rn(o, __fdiv_rn(1.0f, hm[16 + jj])));
+          } else {
+            float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + jj) * (2 + hd);
+            if (dq == 0 && i == 0) { __stcg(pp, hm[jj]); __stcg(pp + 1, hm[16 + jj]); }
+            __stcg(pp + 2 + d, o);
           }
         }
       }

@@ -233,6 +233,7 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   a.off_terms = st_take(std::max<size_t>(static_cast<size_t>(a.rd_max) * a.K * nbd * 4, 2 * NW * 8));
   a.off_hq = st_take(static_cast<size_t>(a.K) * a.FF + 2 * (static_cast<size_t>(a.K) * a.FF / 16) + 4 * (static_cast<size_t>(a.K) * a.FF / 256));
   a.off_xr = st_take(static_cast<size_t>(a.rd_max) * 4);
+  constexpr int SB_KEYS = 32;   // fwd.cu's positions of keys staged per score item
   // the slots hold a layer's dense rows (each CTA's rows of wq, wk, wv, wo, one segment after another: fwd.cu's
   // dense_offset) and then the chosen experts' gate/up rows
   size_t dense_need = 0;
@@ -259,7 +260,7 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   // context of that head), and the staged key / value rows (64 positions); the output matrix's stages span both regions
   const size_t att_scores = static_cast<size_t>(GRP) * hd * 4 + std::max<size_t>(static_cast<size_t>(GRP) * FWD_ATT_CHUNK, GRP < 2 ? a.ctx : 64) * 4;
   a.off_kvstage = static_cast<uint32_t>(al(att_scores, 16));
-  const size_t att_need = a.off_kvstage + static_cast<size_t>(64) * hd * 2;
+  const size_t att_need = a.off_kvstage + static_cast<size_t>(std::max(SB_KEYS * hd, FWD_ATT_CHUNK * (hd / 4))) * 2;
   const size_t head_need = static_cast<size_t>(HEAD_STAGES) * al(HEAD_ROWS * row_bytes(out->type, a.E) + 32, 16);
   const size_t dslots_size = std::max<size_t>(std::max<size_t>(static_cast<size_t>(a.K) * a.dslot_bytes, att_need),
                                               head_need > slots_size ? head_need - slots_size : 0);
