@@ -14,6 +14,7 @@ value = all ranks' layer-tokens / the slowest rank's time. --impl reference time
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -458,6 +459,8 @@ def run_model(a, wl: dict) -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     spec = sm.QWEN3_30B_A3B
+    if a.layers:   # a shorter stack of the same layers (small ncu captures); the default is the whole model
+        spec = dataclasses.replace(spec, n_layer=a.layers)
     t_img = time.perf_counter()
     image = sm.image(spec, seed=1)
     t_img = time.perf_counter() - t_img
@@ -522,7 +525,7 @@ def run_model(a, wl: dict) -> None:
                 "warmup": W, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate; fp32 attention, fp16 key/value cache",
                 "data": "synthetic (seeded random GGUF weights with the model's shapes and types)",
-                "config": {"workload": wl["desc"], "model_bytes": mb["total"], "positions": [W, W + K - 1],
+                "config": {"workload": wl["desc"], "layers": spec.n_layer, "model_bytes": mb["total"], "positions": [W, W + K - 1],
                            "parallelism": f"replicas x{world}", "l2": "inputs larger than L2: 2.0 GB of weights per token",
                            "image_seconds": round(t_img, 1)},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": K, "clocks": clk.summary(),

@@ -765,6 +765,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     for (int k = 0; k < K; ++k)
       if (!mbar_wait_bounded(&bars[k], par)) set_error(&st->err, ERR_WAIT_COPY);
     __syncthreads();
+    trace_stamp(a.trace, 24);
     {
       const int C = K * nbd, combo = tid % C, grp = tid / C, ngrp = FWD_THREADS / C;
       if (grp < ngrp) {
@@ -775,6 +776,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       }
     }
     __syncthreads();
+    trace_stamp(a.trace, 25);
     for (int r = tid; r < nd; r += FWD_THREADS) {
       float moe = 0.f;
       for (int k = 0; k < K; ++k) {

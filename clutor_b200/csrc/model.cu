@@ -1,5 +1,5 @@
 // Whole models: a GGUF file (or image in memory) uploaded to HBM in its own block format, and the one-token step of
-// fwd.cu behind the reference's forward-pass interface (c/src/forward.h:114-124: cl_fwd_open, cl_fwd_step, cl_fwd_reset,
+// fwd.cu behind the reference's forward-pass interface (c/src/forward.h:113-117: cl_fwd_open, cl_fwd_step, cl_fwd_reset,
 // cl_fwd_close). Host code.
 #include <fcntl.h>
 #include <sys/mman.h>

@@ -1,4 +1,4 @@
-"""Whole models on the device: the reference's forward-pass interface (c/src/forward.h:114-124) over clb200_model_*."""
+"""Whole models on the device: the reference's forward-pass interface (c/src/forward.h:113-117) over clb200_model_*."""
 from __future__ import annotations
 
 import ctypes as C

@@ -225,14 +225,14 @@ typedef struct {
   uint64_t device_bytes;   /* HBM the model holds: weights, cache, scratch */
   uint32_t smem_bytes;     /* shared memory per CTA of the step */
 } clb200_model_info;
-/* cl_fwd_open (forward.h:114): from a file path, or a GGUF image in host memory. n_ctx <= 0: 512 (capped at the model's). */
+/* cl_fwd_open (forward.h:113): from a file path, or a GGUF image in host memory. n_ctx <= 0: 512 (capped at the model's). */
 clb200_model *clb200_model_open(clb200_ctx *c, const char *path, int n_ctx, char *err, size_t errlen);
 clb200_model *clb200_model_open_image(clb200_ctx *c, const void *image, size_t bytes, int n_ctx, char *err, size_t errlen);
-void clb200_model_close(clb200_model *m);                          /* cl_fwd_close (forward.h:115) */
-void clb200_model_reset(clb200_model *m);                          /* cl_fwd_reset (forward.h:116): back to position 0 */
+void clb200_model_close(clb200_model *m);                          /* cl_fwd_close (forward.h:114) */
+void clb200_model_reset(clb200_model *m);                          /* cl_fwd_reset (forward.h:115): back to position 0 */
 int clb200_model_pos(const clb200_model *m);                       /* the reference's f->pos */
 int clb200_model_get_info(const clb200_model *m, clb200_model_info *out);
-/* cl_fwd_step (forward.h:117-118): runs `token` at the current position and advances it. logits (host, n_vocab floats),
+/* cl_fwd_step (forward.h:116-117): runs `token` at the current position and advances it. logits (host, n_vocab floats),
  * next_token (the arg-max, lowest id on ties), sel_out / wt_out (host, n_layer * n_used: each layer's experts in rank order
  * and their weights, the reference's cl_fwd_route) may each be NULL. Returns 0, or 1 with err set. */
 int clb200_model_step(clb200_model *m, int token, float *logits, int *next_token, int *sel_out, float *wt_out, char *err,
