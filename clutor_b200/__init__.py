@@ -83,6 +83,29 @@ class StoreStats(C.Structure):
 _lib: C.CDLL | None = None
 
 
+class Smart(C.Structure):
+    """clb200_smart (the layout of the reference's cl_smart, c/src/route.h:14)."""
+    _fields_ = [("enabled", C.c_int), ("J", C.c_int), ("M", C.c_int), ("tau", C.c_double)]
+
+
+class RouteResult(C.Structure):
+    """clb200_route_result (the layout of cl_route_result, c/src/route.h:16-22)."""
+    _fields_ = [("selected", C.c_int * 32), ("k", C.c_int), ("substituted", C.c_int), ("dropped_mass", C.c_double),
+                ("max_delta", C.c_double)]
+
+    def as_dict(self) -> dict:
+        return {"selected": list(self.selected[:self.k]), "substituted": self.substituted,
+                "dropped_mass": self.dropped_mass, "max_delta": self.max_delta}
+
+
+class SmartStats(C.Structure):
+    _fields_ = [("substituted", C.c_uint64), ("expert_slots", C.c_uint64), ("dropped_mass", C.c_double),
+                ("max_delta", C.c_double)]
+
+    def as_dict(self) -> dict:
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
+
 def header_functions() -> list[str]:
     """Names of the functions include/clb200.h declares."""
     text = open(HEADER).read()
@@ -154,6 +177,14 @@ def lib() -> C.CDLL:
                                             C.c_char_p, C.c_size_t]
         L.clb200_moe_experts_stored.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                                 C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_route.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p,
+                                   C.c_size_t]
+        L.clb200_route_dev.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                       C.c_void_p, C.c_void_p]
+        L.clb200_store_set_smart.argtypes = [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_store_smart_stats.argtypes = [C.c_void_p]
+        L.clb200_store_smart_stats.restype = SmartStats
+        L.clb200_store_route.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
         _lib = L
     return _lib
 
@@ -275,6 +306,30 @@ class Context:
         """Phase trace of the one-token kernel (clb200_set_trace): buf is a torch uint64/int64 CUDA tensor of 32 entries per
         SM, or None to stop."""
         lib().clb200_set_trace(self.handle, _ptr(buf))
+
+
+    def route(self, logits: np.ndarray, K: int, smart: tuple | None = None, resident: np.ndarray | None = None) -> dict | None:
+        """cl_route on the GPU (clb200_route): logits [E] float32 (host); smart = (J, M, tau) or None; resident [E] bytes
+        or None. Returns the result as a dict, or None when the arguments are out of range (as cl_route's -1)."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        res = None if resident is None else np.ascontiguousarray(resident, np.uint8)
+        sm = Smart(1, *smart) if smart else None
+        out = RouteResult()
+        rc = lib().clb200_route(self.handle, lg.ctypes.data, lg.shape[0], K, C.addressof(sm) if sm else None,
+                                None if res is None else res.ctypes.data, C.addressof(out), self._err, 512)
+        if rc < 0:
+            return None
+        self._check(rc)
+        return out.as_dict()
+
+    def route_dev(self, logits, K: int, smart: tuple | None, resident, out, resident_stride: int = 0, stream=None) -> int:
+        """clb200_route_dev on torch CUDA tensors: logits [T, E] float32, resident uint8 or None, out a uint8 tensor of
+        T * 152 bytes (clb200_route_result each). Returns the C return code."""
+        sm = Smart(1, *smart) if smart else None
+        T, E = logits.shape
+        return lib().clb200_route_dev(self.handle, _ptr(logits), T, E, K, C.addressof(sm) if sm else None,
+                                      None if resident is None else _ptr(resident), resident_stride, _ptr(out),
+                                      C.c_void_p(_stream(stream)))
 
 
 def backend() -> Backend:
@@ -406,6 +461,26 @@ class Store:
                                         stream if isinstance(stream, int) else _stream(stream), self._err, 512):
             raise ClutorError(self._err.value.decode())
         return sel, wt
+
+    def set_smart(self, smart: tuple | None) -> None:
+        """SMART-ROUTE in moe_ffn / route (clb200_store_set_smart): (J, M, tau), or None for plain routing."""
+        sm = Smart(1, *smart) if smart else None
+        if self.L.clb200_store_set_smart(self.h, C.addressof(sm) if sm else None, self._err, 512):
+            raise ClutorError(self._err.value.decode())
+
+    def smart_stats(self) -> dict:
+        return self.L.clb200_store_smart_stats(self.h).as_dict()
+
+    def route(self, layer: int, logits: np.ndarray) -> dict:
+        """Routing of `layer` from host logits against the store's resident set (clb200_store_route)."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        out = RouteResult()
+        if self.L.clb200_store_route(self.ctx.handle, self.h, layer, lg.ctypes.data, C.addressof(out), self._err, 512):
+            raise ClutorError(self._err.value.decode())
+        return out.as_dict()
+
+    def resident(self, layer: int, expert: int) -> bool:
+        return bool(self.L.clb200_store_resident(self.h, layer, expert))
 
     def experts(self, layer: int, x, sel: np.ndarray, wt: np.ndarray, next_pred: np.ndarray | None = None, stream=None):
         """The experts of a given routing (host arrays) through the store; x a device tensor, updated in place."""

@@ -161,7 +161,8 @@ static const char *device_error_text(int code) {
 }
 
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
-               const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen) {
+               const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
+               const SmartRoute *smart) {
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
   DecodeArgs a{};
   if (plan_decode(c, L, a)) { errf(err, errlen, "the one-token kernel does not take this layer (K-quant experts only)"); return 1; }
@@ -182,6 +183,17 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   a.err = c->small;
   a.trace = c->trace;
   a.mode = mode;
+  if (mode == 1 && smart) {
+    if (NE > ROUTE_SMEM_MAX_NE || static_cast<size_t>(NE) * 13 + 64 > static_cast<size_t>(K) * a.slot_bytes) {
+      errf(err, errlen, "SMART-ROUTE in the one-token kernel takes at most %d experts", ROUTE_SMEM_MAX_NE);
+      return 1;
+    }
+    a.resident = smart->resident;
+    a.smart_J = smart->J;
+    a.smart_M = smart->M;
+    a.smart_tau = smart->tau;
+    a.smart_stats = smart->stats;
+  }
   if (mode == 2)
     for (int k = 0; k < K; ++k) {
       a.sel_in[k] = sel_in[k];
@@ -245,6 +257,7 @@ void clb200_close(clb200_ctx *c) {
   for (auto &l : c->layers) if (l.block) cudaFree(l.block);
   if (c->scratch) cudaFree(c->scratch);
   if (c->small) cudaFree(c->small);
+  if (c->route_buf) cudaFree(c->route_buf);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
 }

@@ -101,13 +101,26 @@ struct clb200_ctx {
   float *hx = nullptr;                             // host-call staging of x / sel / wt on the device (in scratch)
   uint64_t bytes = 0;
   bool attrs_set = false;
-  unsigned long long *trace = nullptr;             // phase trace of the one-token kernel (device, 16 per CTA) or null
+  unsigned long long *trace = nullptr;             // phase trace of the one-token kernel (device, 32 per CTA) or null
+  uint8_t *route_buf = nullptr;                    // clb200_route: logits, residency and result on the device
 };
+constexpr size_t ROUTE_BUF_BYTES = 1024 * 5 + 256;
 
 namespace clb {
 // The one-token kernel on layer L (device pointers) and x [n_embd] (device) in `mode` (DecodeArgs::mode); for mode 2,
 // sel_in / wt_in [n_used] (host) and slabs [n_used] (device addresses, or null entries for L's own tensors). Returns 1 with
 // err set when the layer does not suit the one-token kernel or the launch fails.
+// smart (mode 1 only, may be null): SMART-ROUTE with the residency and settings it holds (DecodeArgs::resident ...).
+struct SmartRoute {
+  const uint8_t *resident;   // device-visible [n_expert] bytes
+  int J, M;
+  double tau;
+  void *stats;               // device-visible RouteStats
+};
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
-               const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen);
+               const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
+               const SmartRoute *smart = nullptr);
+// The routing kernel of route.cu: T tokens, one CTA each; returns non-zero when the launch fails.
+int launch_route_kernel(const float *logits, int T, int E, int K, const clb200_smart *smart, const uint8_t *resident,
+                        int rstride, clb200_route_result *out, cudaStream_t st);
 }  // namespace clb

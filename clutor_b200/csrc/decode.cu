@@ -27,6 +27,7 @@
 //      moe = sum over experts in rank order of wt * hd; x = x + resid_scale * moe; the last CTA out resets the counters.
 #include "common.cuh"
 #include "decode.cuh"
+#include "route.cuh"
 #include "rowdot.cuh"
 
 namespace clb {
@@ -226,6 +227,17 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   }
   __syncthreads();
   trace_stamp(a.trace, 11);
+  if (a.mode == 1 && a.resident && c == 0 && !s_flag[0]) {
+    // SMART-ROUTE (c/src/forward.c:961-969): cl_route's choice against the layer's resident set, each chosen expert weighted
+    // by its own router probability; scratch in the expert slots, which routing-only launches leave unused
+    double *rp = reinterpret_cast<double *>(slots);
+    int *rorder = reinterpret_cast<int *>(rp + NE);
+    uint8_t *rtaken = reinterpret_cast<uint8_t *>(rorder + NE);
+    const SmartCfg cfg{1, a.smart_J, a.smart_M, a.smart_tau};
+    route_cta(a.logits, NE, K, cfg, a.resident, rp, rorder, rtaken, s_red, s_sel, static_cast<RouteStats *>(a.smart_stats));
+    if (tid < K) s_wt[tid] = probs[s_sel[tid]];
+    __syncthreads();
+  }
   if (a.mode != 2 && !s_flag[0] && tid < K) {   // renormalise: each of K threads forms the same sum in rank order
     float w = s_wt[tid];
     if (a.norm_topk) {

@@ -9,6 +9,7 @@ namespace clb {
 constexpr int DECODE_THREADS = 512;
 constexpr int DECODE_MAX_NE = 256;   // experts per layer the one-token kernel ranks
 constexpr int DECODE_MAX_K = 32;     // experts used per token
+constexpr int ROUTE_SMEM_MAX_NE = 256;   // SMART-ROUTE inside the one-token kernel: experts per layer
 
 struct DecodeArgs {
   const float *x_in;
@@ -36,6 +37,12 @@ struct DecodeArgs {
   int rgu_max, rd_max;
   uint32_t grb, drb, gseg, dseg, slot_bytes;
   uint32_t off_bars, off_xn, off_norm, off_xq, off_router, off_rprod, off_misc, off_terms, off_hq, off_xr, off_slots, smem_bytes;
+  // SMART-ROUTE in mode 1 (resident null: off): the residency of the layer's experts ([NE] bytes, device-visible), the
+  // settings (c/src/route.h:14) and the counters of the routing (a RouteStats, device-visible), written by CTA 0
+  const uint8_t *resident;
+  int smart_J, smart_M;
+  double smart_tau;
+  void *smart_stats;
   // phase trace (null: off): thread 0 of CTA c writes its SM's cycle counter at phase boundary i to trace[32 * c + i] and the global
   // nanosecond timer at entry and exit to trace[32 * c + 30] and [31]
   unsigned long long *trace;

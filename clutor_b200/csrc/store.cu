@@ -15,11 +15,15 @@
 #include <vector>
 
 #include "ctx.cuh"
+#include "route.cuh"
 
 using namespace clb;
 
 namespace {
 enum { S_EMPTY = 0, S_LOADING = 1, S_READY = 2 };
+// the SMART-ROUTE block of the store: residency, counters, logits, result
+constexpr size_t SMART_RES = 0, SMART_STATS = 256, SMART_LOGITS = 512, SMART_OUT = SMART_LOGITS + 4 * 1024,
+                 SMART_HOST_BYTES = SMART_OUT + 256;
 uint64_t now_ns() {
   return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now().time_since_epoch()).count());
 }
@@ -44,6 +48,11 @@ struct clb200_store {
   cudaStream_t copy = nullptr;
   int *sel_host = nullptr;               // pinned, device-visible: the routing kernel's choice
   float *wt_host = nullptr;
+  // SMART-ROUTE: settings, counters, and a pinned device-visible block: the residency of the layer being routed [256
+  // bytes], the routing kernel's counters (RouteStats), logits handed in by the host [1024 floats], a routing result
+  uint8_t *smart_host = nullptr;
+  clb200_smart smart{};
+  clb200_smart_stats smart_st{};
   std::vector<int> prev_sel;             // [n_layer * K] the previous token's choice, -1 before the first
   int prefetch = 1;
   clb200_store_stats st{};
@@ -60,6 +69,13 @@ void log_op(clb200_store *s, int op, int64_t a, int64_t r) {
     s->oplog.push_back(a);
     s->oplog.push_back(r);
   }
+}
+
+// The reference's SMART counters (c/src/forward.c:968-969): substitutions and probability moved, summed; the largest delta.
+void count_smart(clb200_store *s, const RouteStats &r) {
+  s->smart_st.substituted += static_cast<uint64_t>(r.substituted);
+  s->smart_st.dropped_mass += r.dropped_mass;
+  if (r.max_delta > s->smart_st.max_delta) s->smart_st.max_delta = r.max_delta;
 }
 
 void count_copy(clb200_store *s, int buf) {   // the fill of `buf` has completed: add its duration to copy_ns once
@@ -85,6 +101,15 @@ void poll(clb200_store *s) {
   }
   s->staged.resize(keep);
   cudaGetLastError();   // a "not ready" answer is not an error
+}
+
+// cl_xs_resident (c/src/xs.c:179-186) for every expert of `layer`, into the pinned residency bytes the kernels read.
+void fill_resident(clb200_store *s, int layer) {
+  poll(s);
+  for (int e = 0; e < s->NE; ++e) {
+    const int slot = clb200_cache_find(s->cache, static_cast<uint32_t>(layer * s->NE + e));
+    s->smart_host[SMART_RES + e] = static_cast<uint8_t>(slot >= 0 && s->state[slot] == S_READY);
+  }
 }
 
 void fill(clb200_store *s, int buf, int layer, int expert, bool prefetch) {
@@ -139,6 +164,7 @@ clb200_store *clb200_store_open(clb200_ctx *c, const clb200_moe_layer *shape, in
             cudaMalloc(&s->dense, dense_per * n_layer) == cudaSuccess &&
             cudaHostAlloc(reinterpret_cast<void **>(&s->sel_host), 64 * sizeof(int), cudaHostAllocMapped) == cudaSuccess &&
             cudaHostAlloc(reinterpret_cast<void **>(&s->wt_host), 64 * sizeof(float), cudaHostAllocMapped) == cudaSuccess &&
+            cudaHostAlloc(reinterpret_cast<void **>(&s->smart_host), SMART_HOST_BYTES, cudaHostAllocMapped) == cudaSuccess &&
             cudaStreamCreateWithFlags(&s->copy, cudaStreamNonBlocking) == cudaSuccess;
   s->state.assign(nbuf, S_EMPTY);
   s->used_set.assign(nbuf, 0);
@@ -181,6 +207,7 @@ void clb200_store_close(clb200_store *s) {
   if (s->host) cudaFreeHost(s->host);
   if (s->sel_host) cudaFreeHost(s->sel_host);
   if (s->wt_host) cudaFreeHost(s->wt_host);
+  if (s->smart_host) cudaFreeHost(s->smart_host);
   if (s->cache) clb200_cache_free(s->cache);
   delete s;
 }
@@ -298,6 +325,7 @@ clb200_store_stats clb200_store_get_stats(const clb200_store *s) {
 void clb200_store_reset_stats(clb200_store *s) {
   if (!s) return;
   s->st = clb200_store_stats{};
+  s->smart_st = clb200_smart_stats{};
 }
 
 void clb200_store_log(clb200_store *s, int on) {
@@ -362,8 +390,21 @@ int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, i
       const int e = s->prev_sel[static_cast<size_t>(layer + 1) * K + k];
       if (e >= 0) clb200_store_prefetch(s, layer + 1, e);
     }
-  if (launch_one(c, s->layer[layer], x, 1, nullptr, nullptr, nullptr, s->sel_host, s->wt_host, st, err, errlen)) return 1;
+  SmartRoute sr{};
+  const bool smart = s->smart.enabled != 0;
+  if (smart) {   // the layer's resident set as the routing starts (c/src/forward.c:963-966 asks cl_xs_resident)
+    fill_resident(s, layer);
+    sr.resident = s->smart_host + SMART_RES;
+    sr.J = s->smart.J;
+    sr.M = s->smart.M;
+    sr.tau = s->smart.tau;
+    sr.stats = s->smart_host + SMART_STATS;
+  }
+  if (launch_one(c, s->layer[layer], x, 1, nullptr, nullptr, nullptr, s->sel_host, s->wt_host, st, err, errlen, smart ? &sr : nullptr))
+    return 1;
   CUDA_OR(cudaStreamSynchronize(st), "routing");
+  if (smart) count_smart(s, *reinterpret_cast<const RouteStats *>(s->smart_host + SMART_STATS));
+  s->smart_st.expert_slots += static_cast<uint64_t>(K);
   int sel[DECODE_MAX_K];
   float wt[DECODE_MAX_K];
   for (int k = 0; k < K; ++k) {
@@ -374,6 +415,48 @@ int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, i
   if (experts_stored(c, s, layer, x, sel, wt, nullptr, st, err, errlen)) return 1;
   if (sel_out) std::memcpy(sel_out, sel, K * sizeof(int));
   if (wt_out) std::memcpy(wt_out, wt, K * sizeof(float));
+  return 0;
+}
+
+int clb200_store_set_smart(clb200_store *s, const clb200_smart *smart, char *err, size_t errlen) {
+  if (!s) { errf(err, errlen, "no store"); return 1; }
+  if (!smart || !smart->enabled) {
+    s->smart = clb200_smart{};
+    return 0;
+  }
+  if (smart->J < 0 || smart->M < 1 || !(smart->tau >= 0.0)) { errf(err, errlen, "SMART-ROUTE wants J >= 0, M >= 1 and tau >= 0"); return 1; }
+  if (s->NE > ROUTE_SMEM_MAX_NE || s->K > ROUTE_MAX_K) { errf(err, errlen, "SMART-ROUTE takes at most %d experts and %d used", ROUTE_SMEM_MAX_NE, ROUTE_MAX_K); return 1; }
+  s->smart = *smart;
+  s->smart.enabled = 1;
+  return 0;
+}
+
+clb200_smart_stats clb200_store_smart_stats(const clb200_store *s) { return s ? s->smart_st : clb200_smart_stats{}; }
+
+int clb200_store_route(clb200_ctx *c, clb200_store *s, int layer, const float *logits, clb200_route_result *out, char *err,
+                       size_t errlen) {
+  if (!c || !s || s->ctx != c) { errf(err, errlen, "no context or store, or a store of another context"); return 1; }
+  if (layer < 0 || layer >= s->n_layer) { errf(err, errlen, "layer %d is outside the store", layer); return 1; }
+  if (!logits || !out) { errf(err, errlen, "no logits or result"); return 1; }
+  if (s->NE > ROUTE_MAX_E) { errf(err, errlen, "too many experts to route"); return 1; }
+  cudaSetDevice(c->device);
+  const bool smart = s->smart.enabled != 0;
+  if (smart) fill_resident(s, layer);
+  std::memcpy(s->smart_host + SMART_LOGITS, logits, static_cast<size_t>(s->NE) * 4);
+  auto *res = reinterpret_cast<clb200_route_result *>(s->smart_host + SMART_OUT);
+  if (launch_route_kernel(reinterpret_cast<const float *>(s->smart_host + SMART_LOGITS), 1, s->NE, s->K, smart ? &s->smart : nullptr,
+                          smart ? s->smart_host + SMART_RES : nullptr, 0, res, c->stream)) {
+    errf(err, errlen, "launching the routing kernel: %s", cudaGetErrorString(cudaGetLastError()));
+    return 1;
+  }
+  CUDA_OR(cudaStreamSynchronize(c->stream), "routing");
+  *out = *res;
+  RouteStats r{};
+  r.substituted = res->substituted;
+  r.dropped_mass = res->dropped_mass;
+  r.max_delta = res->max_delta;
+  if (smart) count_smart(s, r);
+  s->smart_st.expert_slots += static_cast<uint64_t>(s->K);
   return 0;
 }
 

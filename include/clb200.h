@@ -192,6 +192,43 @@ int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, i
 int clb200_moe_experts_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, const int *sel, const float *wt,
                               const int *next_pred, void *stream, char *err, size_t errlen);
 
+/* ---- SMART-ROUTE: cache-aware routing (c/src/route.h, c/src/route.c:13-52) ------------------------------------------------- */
+typedef struct { int enabled; int J, M; double tau; } clb200_smart;   /* cl_smart (route.h:14), same layout */
+typedef struct {                                                      /* cl_route_result (route.h:16-22), same layout */
+  int selected[32];
+  int k;
+  int substituted;      /* slots filled with a different expert than the router's own choice */
+  double dropped_mass;  /* sum over substitutions of (p of the expert replaced - p of the one used) */
+  double max_delta;     /* largest single such difference; never exceeds tau */
+} clb200_route_result;
+/* cl_route (route.h:26) on the GPU, synchronous, host pointers: logits [E]; resident [E] bytes, non-zero where the expert
+ * is in memory (the reference's resident callback asked for every expert), or NULL for plain routing, as is smart NULL or
+ * smart->enabled 0. Returns 0; -1 when E or K is out of range (E > 1024, K > 32, K > E, or not positive), as cl_route does;
+ * 1 with err set on a CUDA error. */
+int clb200_route(clb200_ctx *c, const float *logits, int E, int K, const clb200_smart *smart, const uint8_t *resident,
+                 clb200_route_result *out, char *err, size_t errlen);
+/* The same for T tokens on device pointers, queued on `stream` (NULL: the context's): logits [T][E]; resident [E] bytes per
+ * token at resident_stride (0: one set for all tokens) or NULL; out [T]. Returns 0, -1 for arguments out of range, 1 when
+ * the launch fails. */
+int clb200_route_dev(clb200_ctx *c, const float *logits, int T, int E, int K, const clb200_smart *smart,
+                     const uint8_t *resident, int resident_stride, clb200_route_result *out, void *stream);
+/* SMART-ROUTE in the store's decode step (the reference's cl_fwd_opts.smart, forward.h:100, applied at forward.c:961-969):
+ * with smart->enabled, clb200_moe_ffn_stored routes on the device with the store's resident set of that layer (cl_xs_resident
+ * for every expert, read when the step starts) and weights each chosen expert by its own router probability (renormalised
+ * over the K where the architecture does). smart NULL or enabled 0: plain routing. Returns 0, or 1 with err set for settings
+ * the reference's command line refuses (J < 0, M < 1, tau < 0; c/src/main.c:152). */
+int clb200_store_set_smart(clb200_store *s, const clb200_smart *smart, char *err, size_t errlen);
+typedef struct {   /* the reference's f->subs, f->expert_slots, f->dropped_mass, f->max_delta (forward.h:57-58) */
+  uint64_t substituted, expert_slots;
+  double dropped_mass, max_delta;
+} clb200_smart_stats;
+clb200_smart_stats clb200_store_smart_stats(const clb200_store *s);
+/* Routing of `layer` from logits computed elsewhere (HOST, [n_expert]) against the store's resident set, as the reference's
+ * stress harness routes its synthetic logits (c/src/stream.c:288-291); the choice lands in out and the store's SMART
+ * counters. Synchronous. Returns 0, or 1 with err set. */
+int clb200_store_route(clb200_ctx *c, clb200_store *s, int layer, const float *logits, clb200_route_result *out, char *err,
+                       size_t errlen);
+
 /* ---- the plugin seam: a cl_backend for cl_matvec_batch ------------------------------------------------------------------- */
 /* Layout-compatible copies of the reference's cl_q8k, cl_xq and cl_mv (c/src/quant.h:22-34) and cl_backend (backend.h:9-13). */
 typedef struct { float d; int8_t qs[256]; int16_t bsums[16]; } clb200_q8k;

@@ -320,3 +320,72 @@ class RefModel:
 
     def __del__(self):
         self.close()
+
+
+class RouteResult(C.Structure):
+    """cl_route_result (c/src/route.h:16-22) and clb200_route_result: the same layout."""
+    _fields_ = [("selected", C.c_int * 32), ("k", C.c_int), ("substituted", C.c_int), ("dropped_mass", C.c_double),
+                ("max_delta", C.c_double)]
+
+
+class Smart(C.Structure):
+    """cl_smart (c/src/route.h:14) and clb200_smart."""
+    _fields_ = [("enabled", C.c_int), ("J", C.c_int), ("M", C.c_int), ("tau", C.c_double)]
+
+
+_RESIDENT_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int)
+
+
+def smart_route(logits: np.ndarray, K: int, smart: tuple | None = None, resident: np.ndarray | None = None,
+                which: str = "oracle") -> dict | None:
+    """cl_route (c/src/route.c:13-52) of one token: ``which`` "oracle" (orc_smart_route, the restatement) or "ref" (the
+    reference's own cl_route, its resident callback reading ``resident``). smart = (J, M, tau) or None (plain routing).
+    Returns {"selected": [K] ints, "substituted", "dropped_mass", "max_delta"}, or None when cl_route refuses the arguments."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    E = lg.shape[0]
+    res = None if resident is None else np.ascontiguousarray(resident, dtype=np.uint8)
+    if which == "oracle":
+        sel = (C.c_int * 32)()
+        subs, dropped, maxd = C.c_int(0), C.c_double(0), C.c_double(0)
+        J, M, tau = smart if smart else (0, 0, 0.0)
+        lib = oracle_lib()
+        lib.orc_smart_route.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_double, C.c_void_p,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        rc = lib.orc_smart_route(lg.ctypes.data, E, K, 1 if smart else 0, J, M, tau,
+                                 None if res is None else res.ctypes.data, C.addressof(sel), C.addressof(subs),
+                                 C.addressof(dropped), C.addressof(maxd))
+        if rc:
+            return None
+        return {"selected": list(sel[:K]), "substituted": subs.value, "dropped_mass": dropped.value, "max_delta": maxd.value}
+    L = ref_lib()
+    L.cl_route.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, _RESIDENT_FN, C.c_void_p, C.POINTER(RouteResult)]
+    L.cl_route.restype = C.c_int
+    out = RouteResult()
+    cb = _RESIDENT_FN(lambda ctx, e: int(res[e]) if res is not None and 0 <= e < E else 0)
+    sm = Smart(1, *smart) if smart else None
+    rc = L.cl_route(lg.ctypes.data, E, K, C.addressof(sm) if sm else None, cb if res is not None else _RESIDENT_FN(),
+                    None, C.byref(out))
+    if rc:
+        return None
+    return {"selected": list(out.selected[:K]), "substituted": out.substituted, "dropped_mass": out.dropped_mass,
+            "max_delta": out.max_delta}
+
+
+def router_probs(layer, x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """The router of one token (c/src/forward.c:950-958): logits = dotf(router row, rmsnorm(x)) and the float softmax
+    probabilities, by the restatement. layer: a clutor_b200.synth.HostLayer. -> (logits [NE], probs [NE]) float32."""
+    lib = oracle_lib()
+    lib.orc_rmsnorm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float]
+    lib.orc_dotf.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    lib.orc_dotf.restype = C.c_float
+    lib.orc_route.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    x = np.ascontiguousarray(x, np.float32)
+    xn = np.zeros(layer.E, np.float32)
+    lib.orc_rmsnorm(xn.ctypes.data, x.ctypes.data, _ptr(layer.ffn_norm), layer.E, layer.rms_eps)
+    router = np.ascontiguousarray(layer.router, np.float32).reshape(layer.NE, layer.E)
+    logits = np.array([lib.orc_dotf(router[e].ctypes.data, xn.ctypes.data, layer.E) for e in range(layer.NE)], np.float32)
+    probs = logits.copy()
+    sel = np.zeros(layer.K, np.int32)
+    wt = np.zeros(layer.K, np.float32)
+    lib.orc_route(probs.ctypes.data, layer.NE, layer.K, layer.norm_topk, sel.ctypes.data, wt.ctypes.data)
+    return logits, probs

@@ -210,6 +210,57 @@ void orc_route(float *rl, int NE, int K, int norm_topk, int *sel, float *wt) {
   if (norm_topk) { float z = 0; for (int k = 0; k < K; k++) z += wt[k]; if (z > 0) for (int k = 0; k < K; k++) wt[k] /= z; }
 }
 
+/* SMART-ROUTE (c/src/route.c:13-52): the experts ranked by their double softmax probability (exp of logit minus the
+ * maximum, divided by the sum taken in expert order), best first and ties to the lower id; the first K are the plain choice.
+ * With smart_on and a residency array, the ranks below J and the resident experts stay; each other rank, in rank order,
+ * takes the lowest rank j < M (clamped to [K, E]) whose expert is resident, unused and no more than tau below it in
+ * probability, else keeps its own expert. Returns -1 for E or K out of range (E > 1024, K > 32, K > E, or < 1), else 0. */
+typedef struct { int id; double p; } orc_ranked;
+static int orc_rank_cmp(const void *a, const void *b) {
+  const orc_ranked *x = (const orc_ranked *)a, *y = (const orc_ranked *)b;
+  if (x->p > y->p) return -1;
+  if (x->p < y->p) return 1;
+  return (x->id > y->id) - (x->id < y->id);
+}
+int orc_smart_route(const float *logits, int E, int K, int smart_on, int J, int M, double tau, const uint8_t *resident,
+                    int *selected, int *substituted, double *dropped, double *max_delta) {
+  if (E < 1 || E > 1024 || K < 1 || K > 32 || K > E) return -1;
+  orc_ranked rk[1024];
+  double mx = logits[0], sum = 0.0;
+  for (int i = 1; i < E; i++) mx = logits[i] > mx ? logits[i] : mx;
+  for (int i = 0; i < E; i++) { rk[i].id = i; rk[i].p = exp((double)logits[i] - mx); sum += rk[i].p; }
+  for (int i = 0; i < E; i++) rk[i].p = rk[i].p / sum;
+  qsort(rk, (size_t)E, sizeof rk[0], orc_rank_cmp);
+  *substituted = 0; *dropped = 0.0; *max_delta = 0.0;
+  for (int k = 0; k < K; k++) selected[k] = rk[k].id;
+  if (!smart_on || !resident) return 0;
+  if (J < 0) J = 0;
+  if (J > K) J = K;
+  if (M < K) M = K;
+  if (M > E) M = E;
+  unsigned char used[1024];
+  memset(used, 0, sizeof used);
+  int cold[32], nc = 0;
+  for (int k = 0; k < K; k++) {
+    if (k < J || resident[rk[k].id]) used[rk[k].id] = 1;
+    else cold[nc++] = k;
+  }
+  for (int c = 0; c < nc; c++) {
+    const int k = cold[c];
+    int j = 0;
+    for (; j < M; j++)
+      if (j != k && !used[rk[j].id] && resident[rk[j].id] && !(rk[k].p - rk[j].p > tau)) break;
+    if (j == M) { used[rk[k].id] = 1; continue; }
+    const double d = rk[k].p - rk[j].p;
+    used[rk[j].id] = 1;
+    selected[k] = rk[j].id;
+    *substituted += 1;
+    *dropped += d;
+    if (d > *max_delta) *max_delta = d;
+  }
+  return 0;
+}
+
 static float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
 /* One MoE layer, mirroring the reference's types: fused expert tensors with rows-per-expert and byte slabs (c/src/forward.h:18-29). */

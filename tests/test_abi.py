@@ -35,14 +35,16 @@ def test_ctypes_mirror_matches_header():
 
 @pytest.mark.skipif(not os.path.isdir(oracle.REF_DIR_DEFAULT), reason="needs the reference headers")
 def test_struct_layouts_equal_the_reference():
-    """clb200_w / clb200_q8k / clb200_xq / clb200_mv / clb200_backend_t have the layout of the reference's cl_w (forward.h:18),
-    cl_q8k / cl_xq / cl_mv (quant.h:22-34) and cl_backend (backend.h:9-13), so the reference can pass its own structs."""
+    """clb200_w / clb200_q8k / clb200_xq / clb200_mv / clb200_backend_t / clb200_smart / clb200_route_result have the layout of
+    the reference's cl_w (forward.h:18), cl_q8k / cl_xq / cl_mv (quant.h:22-34), cl_backend (backend.h:9-13), cl_smart and
+    cl_route_result (route.h:14-22), so the reference can pass its own structs."""
     src = r"""
 #include <stddef.h>
 #include <stdio.h>
 #include "clb200.h"
 #include "backend.h"
 #include "forward.h"
+#include "route.h"
 #define S(a, b) printf("%s %zu %zu\n", #a, sizeof(a), sizeof(b))
 #define O(a, b, f) printf("%s.%s %zu %zu\n", #a, #f, offsetof(a, f), offsetof(b, f))
 int main(void) {
@@ -52,6 +54,10 @@ int main(void) {
   S(clb200_mv, cl_mv); O(clb200_mv, cl_mv, w); O(clb200_mv, cl_mv, xf); O(clb200_mv, cl_mv, xq); O(clb200_mv, cl_mv, out);
   O(clb200_mv, cl_mv, nb); O(clb200_mv, cl_mv, xf_stride); O(clb200_mv, cl_mv, out_stride);
   S(clb200_backend_t, cl_backend); O(clb200_backend_t, cl_backend, supports); O(clb200_backend_t, cl_backend, matvec_batch);
+  S(clb200_smart, cl_smart); O(clb200_smart, cl_smart, J); O(clb200_smart, cl_smart, M); O(clb200_smart, cl_smart, tau);
+  S(clb200_route_result, cl_route_result); O(clb200_route_result, cl_route_result, k);
+  O(clb200_route_result, cl_route_result, substituted); O(clb200_route_result, cl_route_result, dropped_mass);
+  O(clb200_route_result, cl_route_result, max_delta);
   return 0;
 }
 """
