@@ -258,10 +258,17 @@ def run_cache(a, wl: dict) -> None:
     sel = np.zeros((NL, ntok, K), np.int32)
     wt = np.zeros((NL, ntok, K), np.float32)
     pred = np.zeros((NL, ntok, K), np.int32)
+    lg_all = np.zeros((NL, ntok, NE), np.float32)
     for l in range(NL):
-        sel[l], p = synth.route_topk(gen.logits(toks, l), K)
+        lg_all[l] = gen.logits(toks, l)
+        sel[l], p = synth.route_topk(lg_all[l], K)
         wt[l] = p / p.sum(axis=1, keepdims=True, dtype=np.float32)
         pred[l] = synth.route_topk(gen.logits(toks, l, predicted=True), K)[0]
+    smart = tuple(t(v) for t, v in zip((int, int, float), a.smart.split(","))) if a.smart else None
+    if smart:   # SMART-ROUTE (c/src/stream.c:288-291): each (token, layer) routed on the device against the resident set
+        store.set_smart(smart)
+        pz = np.exp(lg_all.astype(np.float64) - lg_all.max(axis=2, keepdims=True))
+        probs = (pz / pz.sum(axis=2, keepdims=True)).astype(np.float32)
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
     x = torch.from_numpy(synth.activations(1, E, seed=11)).cuda()[0]
@@ -269,7 +276,13 @@ def run_cache(a, wl: dict) -> None:
 
     def token(t):
         for l in range(NL):
-            store.experts(l, x, sel[l, t], wt[l, t], pred[l + 1, t] if l + 1 < NL else None, stream=sp)
+            nxt = pred[l + 1, t] if l + 1 < NL else None
+            if smart:
+                s = np.array(store.route(l, lg_all[l, t])["selected"], np.int32)
+                w = probs[l, t, s]
+                store.experts(l, x, s, (w / w.sum(dtype=np.float32)).astype(np.float32), nxt, stream=sp)
+            else:
+                store.experts(l, x, sel[l, t], wt[l, t], nxt, stream=sp)
 
     for t in range(a.warmup):
         token(t)
@@ -334,7 +347,8 @@ def run_cache(a, wl: dict) -> None:
                       "prefetch_wasted": st["prefetch_wasted"], "evictions": st["evictions"],
                       "prefetch_overlap": round(1.0 - st["wait_ns"] / max(st["copy_ns"], 1), 4),
                       "copy_ms": round(st["copy_ns"] / 1e6, 3), "wait_ms": round(st["wait_ns"] / 1e6, 3),
-                      "policy_replay_on_reference": f"{len(log)} operations, {mism} mismatches"},
+                      "policy_replay_on_reference": f"{len(log)} operations, {mism} mismatches",
+                      "smart_route": None if not smart else dict(J=smart[0], M=smart[1], tau=smart[2], **store.smart_stats())},
             "roofline": {"bound": "h2d", "achieved": round(h2d, 2), "peak": round(link, 2), "unit": "GB/s",
                          "frac": round(h2d / link, 4), "traffic": None, "peak_kind": "measured here: one 1 GiB pinned copy"},
             "cpu_baseline": cpu,
@@ -548,6 +562,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--smart", default=None, help="cache workload: SMART-ROUTE J,M,TAU (for example 2,12,0.015)")
     a = ap.parse_args()
     wl = dict(WORKLOADS[a.workload])
     if a.layers:
