@@ -42,6 +42,10 @@ WORKLOADS = {
                   desc="Qwen3-30B-A3B whole model, greedy decode at batch 1 from a 1-token prompt: 48 layers, GQA 32/4 heads "
                        "x 128, QK-norm, NEOX rotary (base 1e6), fp16 key/value cache, Q4_K_M mix (Q4_K embedding, attn_q/k/o and "
                        "gate/up experts; Q6_K attn_v, down experts and the 151,936-row output matrix)"),
+    "prompt": dict(T=64, gate="q4_k", down="q6_k", E=2048, FF=768, NE=128, K=8, layers=48, P=512,
+                   desc="Qwen3-30B-A3B whole model, a 512-token prompt fed through the batched prompt path (the reference's "
+                        "cl_fwd_prefill / run_std) in batches of 64 tokens (its batch for a model in memory), logits after "
+                        "the last token; same model as 'model'"),
     "cache": dict(T=1, gate="q4_k", down="q4_k", E=2048, FF=768, NE=128, K=8, layers=48, budget=0.4, locality=1.78,
                   desc="expert-cache stress: 48 Qwen3-30B-A3B MoE layers (Q4_K), HBM cache of 40% of expert bytes, the rest "
                        "in pinned host memory, Zipf(1.1)-skewed routing with topics drifting every 16 tokens"),
@@ -194,8 +198,111 @@ def model_reference(image, n_ctx: int, seconds: float, threads: int | None = Non
                       f"/dev/shm", "ms_per_token": 1000 * dt / max(n, 1)}
 
 
+PROMPT_METRIC = "prompt tokens/s (Qwen3-30B-A3B, Q4_K_M mix, 512-token prompt, batches of 64)"
+
+
+def prompt_reference(image, P: int, threads: int | None = None) -> dict:
+    """The reference's cl_fwd_prefill of the same P-token prompt (run_std in batches of 64), all host threads (up to 16)."""
+    import numpy as np
+
+    import oracle
+    if not oracle.ref_available():
+        oracle.build()
+    nthreads = threads or min(os.cpu_count() or 1, 16)
+    oracle.set_ref_threads(nthreads)
+    image.tofile(SHM_MODEL)
+    try:
+        prompt = np.random.default_rng(3).integers(0, 151936, P).astype(np.int32)
+        ref = oracle.RefModel(SHM_MODEL, P + 16)
+        ref.prefill(prompt[:8], logits=False)   # pages the weights in
+        ref.close()
+        ref = oracle.RefModel(SHM_MODEL, P + 16)
+        t0 = time.perf_counter()
+        ref.prefill(prompt)
+        dt = time.perf_counter() - t0
+        ref.close()
+    finally:
+        os.unlink(SHM_MODEL)
+    return {"value": P / dt, "unit": "tokens/s", "cores": nthreads, "kind": "reference",
+            "sample": f"one {P}-token prompt through the reference's cl_fwd_prefill (run_std, batches of 64) in {dt:.1f} s on "
+                      f"{nthreads} threads; built from its sources (oracle/_ref), model mapped from /dev/shm"}
+
+
+def run_prompt(a, wl: dict) -> None:
+    """The batched prompt path of the whole model: a step is one P-token prompt from position 0 (clb200_model_prefill, batches
+    of wl["T"] tokens), logits of the last token copied out. The call is synchronous (one synchronization per batch), so it is
+    timed on the host clock around the call, after a device synchronize; there are no inputs but the token ids."""
+    import numpy as np
+    import torch
+
+    import clutor_b200 as cb
+    from clutor_b200 import synth_model as sm
+    from clutor_b200.model import Model
+
+    torch.cuda.set_device(0)
+    spec = sm.QWEN3_30B_A3B
+    if a.layers:
+        spec = dataclasses.replace(spec, n_layer=a.layers)
+    image = sm.image(spec, seed=1)
+    ctx = cb.Context(0)
+    P, B = wl["P"], wl["T"]
+    model = Model(ctx, image, P + 16)
+    model.set_batch(B)
+    prompt = np.random.default_rng(3).integers(0, spec.vocab, P).astype(np.int32)
+
+    def timed(exact: bool, n: int) -> float:
+        ctx.set_exact(exact)
+        for _ in range(a.warmup):
+            model.reset()
+            model.prefill(prompt)
+        ts = []
+        for _ in range(n):
+            model.reset()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            model.prefill(prompt)
+            ts.append(time.perf_counter() - t0)
+        return max(ts)
+
+    with Clocks(0) as clk:
+        dt = timed(False, a.steps)
+    dt_exact = timed(True, max(1, a.steps // 4))
+    ctx.set_exact(False)
+    cpu = None
+    if not a.no_cpu_baseline:
+        cpu = prompt_reference(image, P)
+    mb = sm.model_bytes(spec)
+    line = {"metric": PROMPT_METRIC, "value": round(P / dt, 2), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(1000 * dt, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 dot (Q8_K x K-quant) for dense products; Q4_K experts on tcgen05 from fp16 "
+            "hi/lo operands (fp32 accumulate); fp32 attention, fp16 key/value cache",
+            "data": "synthetic (seeded random GGUF weights with the model's shapes and types; seeded random prompt)",
+            "config": {"workload": wl["desc"], "layers": spec.n_layer, "prompt_tokens": P, "batch": B,
+                       "timing": "host clock around the synchronous call (slowest of the timed steps)",
+                       "model_bytes": mb["total"], "parallelism": "single GPU"},
+            "integer_path_value": round(P / dt_exact, 2),
+            "roofline": None, "cpu_baseline": cpu,
+            "e2e": {"value": round(P / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * P, "d2h_bytes_per_step": 4 * spec.vocab,
+                    "api": "clb200_model_prefill (host token ids in, host logits out)"},
+            "gpu_launches": None, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    model.close()
+    ctx.close()
+
+
 def run_reference_arm(a, wl, rank: int) -> None:
     if rank != 0:
+        return
+    if a.workload == "prompt":
+        from clutor_b200 import synth_model as sm
+        cb = prompt_reference(sm.image(sm.QWEN3_30B_A3B, seed=1), wl["P"])
+        line = {"impl": "reference", "metric": PROMPT_METRIC, "value": round(cb["value"], 3), "unit": "tokens/s",
+                "n_gpus": a.gpus, "steps": 1, "warmup": 0, "ms_per_step": round(1000 * wl["P"] / cb["value"], 1),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot (Q8_K x K-quant), fp32",
+                "data": "synthetic (seeded random GGUF)", "config": {"workload": wl["desc"]},
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": round(cb["value"], 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
         return
     if a.workload == "model":
         from clutor_b200 import synth_model as sm
@@ -575,6 +682,9 @@ def main() -> None:
         return
     if a.workload == "cache":
         run_cache(a, wl)
+        return
+    if a.workload == "prompt":
+        run_prompt(a, wl)
         return
     if a.workload == "ep235b":
         run_ep(a, wl)

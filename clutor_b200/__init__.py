@@ -132,6 +132,7 @@ def lib() -> C.CDLL:
         L.clb200_device_bytes.restype = C.c_uint64
         L.clb200_device_bytes.argtypes = [C.c_void_p]
         L.clb200_set_trace.argtypes = [C.c_void_p, C.c_void_p]
+        L.clb200_set_exact.argtypes = [C.c_void_p, C.c_int]
         L.clb200_backend.restype = C.POINTER(Backend)
         L.clb200_cache_new.restype = C.c_void_p
         L.clb200_cache_new.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.c_uint32]
@@ -301,6 +302,10 @@ class Context:
 
     def device_bytes(self) -> int:
         return int(lib().clb200_device_bytes(self.handle))
+
+    def set_exact(self, on: bool) -> None:
+        """clb200_set_exact: batched expert products on the integer path only (bit-exact), or on the tensor cores."""
+        lib().clb200_set_exact(self.handle, int(on))
 
     def set_trace(self, buf=None) -> None:
         """Phase trace of the one-token kernel (clb200_set_trace): buf is a torch uint64/int64 CUDA tensor of 32 entries per

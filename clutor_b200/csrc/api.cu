@@ -264,6 +264,10 @@ void clb200_close(clb200_ctx *c) {
 
 uint64_t clb200_device_bytes(const clb200_ctx *c) { return c ? c->bytes : 0; }
 
+void clb200_set_exact(clb200_ctx *c, int on) {
+  if (c) c->exact = on != 0;
+}
+
 void clb200_set_trace(clb200_ctx *c, void *dev_buf) {
   if (c) c->trace = static_cast<unsigned long long *>(dev_buf);
 }
@@ -363,8 +367,9 @@ static BatchArgs batch_args(clb200_ctx *c, const clb200_moe_layer &L, float *x, 
   b.sel_out = sel; b.wt_out = wt;
   b.err = c->small;
   // tensor-core expert products where the types allow (Q8_0 down needs the hg planes a tensor-core gate/up writes)
-  const bool tcg = L.gate.type == L.up.type && tc_type_supported(L.gate.type, L.gate.p, E, FF) && tc_type_supported(L.up.type, L.up.p, E, FF);
-  const bool tcd = tc_type_supported(L.down.type, L.down.p, E, FF) && (L.down.type != T_Q8_0 || (tcg && L.gate.type == T_Q8_0));
+  const bool tcg = !c->exact && L.gate.type == L.up.type && tc_type_supported(L.gate.type, L.gate.p, E, FF) &&
+                   tc_type_supported(L.up.type, L.up.p, E, FF);
+  const bool tcd = !c->exact && tc_type_supported(L.down.type, L.down.p, E, FF) && (L.down.type != T_Q8_0 || (tcg && L.gate.type == T_Q8_0));
   if (tcg || tcd) b.rs = reinterpret_cast<float *>(sc + s.off_rs);
   if (tcg) {
     b.tc_gu = 1;
@@ -507,3 +512,10 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
 }
 
 }  // extern "C"
+
+namespace clb {
+int run_moe_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,
+                  size_t errlen) {
+  return run_block(c, dl, x, T, sel, wt, st, err, errlen);
+}
+}  // namespace clb

@@ -18,9 +18,13 @@ namespace clb {
 constexpr int MV_THREADS = 256;
 constexpr int MV_ROWS = 16;
 
-// out[b * rows + r] = row r of w times activation b, for rows [16*blockIdx.x, +16).
+// out[b * rows + r] = row r of w times activation b, for rows [16*blockIdx.x, +16). K-quant activations come as the
+// reference's cl_q8k blocks (xq_aos) or as plain arrays (sqs [nb][cols], sdd [nb][cols / 256], sbs [nb][cols / 16]);
+// accum: out = out + scale * value (a residual update) instead of out = value.
 __global__ void __launch_bounds__(MV_THREADS) mv_kernel(const uint8_t *w, uint32_t type, int rows, int cols, int nb,
-                                                          const uint8_t *xq_aos, const float *xf, float *out, int *err) {
+                                                          const uint8_t *xq_aos, const float *xf, float *out, int *err,
+                                                          const int8_t *sqs = nullptr, const float *sdd = nullptr,
+                                                          const int16_t *sbs = nullptr, int accum = 0, float scale = 1.f) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = blockIdx.x * MV_ROWS, R = min(MV_ROWS, rows - r0);
@@ -51,6 +55,11 @@ __global__ void __launch_bounds__(MV_THREADS) mv_kernel(const uint8_t *w, uint32
     __syncthreads();
     if (q80) {
       for (int j = tid; j < cols; j += MV_THREADS) xs[j] = xf[static_cast<size_t>(b) * cols + j];
+    } else if (sqs) {
+      const int4 *q4 = reinterpret_cast<const int4 *>(sqs + static_cast<size_t>(b) * cols);
+      for (int j = tid; j < cols / 16; j += MV_THREADS) reinterpret_cast<int4 *>(qs)[j] = q4[j];
+      for (int j = tid; j < cols / 256; j += MV_THREADS) dd[j] = sdd[static_cast<size_t>(b) * (cols / 256) + j];
+      for (int j = tid; j < cols / 16; j += MV_THREADS) bs[j] = sbs[static_cast<size_t>(b) * (cols / 16) + j];
     } else {   // unpack the caller's cl_q8k blocks {float d; int8 qs[256]; int16 bsums[16]} (292 bytes each)
       const uint8_t *blocks = xq_aos + static_cast<size_t>(b) * (cols / 256) * 292;
       for (int j = tid; j < cols; j += MV_THREADS) qs[j] = static_cast<int8_t>(blocks[(j / 256) * 292 + 4 + (j % 256)]);
@@ -66,7 +75,10 @@ __global__ void __launch_bounds__(MV_THREADS) mv_kernel(const uint8_t *w, uint32
       const bool active = sub < rs.RPW && r < R;
       const uint8_t *row = wrows + static_cast<size_t>(active ? r : 0) * rb;
       const float v = q80 ? q80_row(row, nblk, rs, lig, sub * rs.LG, xs, active) : kq_row(type, row, nblk, rs, lig, sub * rs.LG, act, active);
-      if (active && lig == 0) out[static_cast<size_t>(b) * rows + r0 + r] = v;
+      if (active && lig == 0) {
+        float *o = out + static_cast<size_t>(b) * rows + r0 + r;
+        *o = accum ? __fadd_rn(*o, __fmul_rn(scale, v)) : v;
+      }
     }
   }
 }
@@ -173,6 +185,27 @@ void be_matvec_batch(const clb200_mv *jobs, int n) {
 const clb200_backend_t kBackend = {"b200", be_supports, be_matvec_batch};
 
 }  // namespace
+
+size_t mv_smem_bytes(uint32_t type, int cols) {
+  return 16 + ((static_cast<size_t>(cols) * 4 + 127) & ~size_t(127)) + ((MV_ROWS * rbytes(type, cols) + 32 + 15) & ~size_t(15)) + 16;
+}
+
+int launch_mv_dev(const uint8_t *w, uint32_t type, int rows, int cols, int nb, const int8_t *qs, const float *dd,
+                  const int16_t *bs, float *out, int accum, float scale, int *err, cudaStream_t st) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(mv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set[dev] = true;
+  }
+  const size_t smem = mv_smem_bytes(type, cols);
+  if (smem > 200 * 1024) return static_cast<int>(cudaErrorInvalidValue);
+  mv_kernel<<<(rows + MV_ROWS - 1) / MV_ROWS, MV_THREADS, smem, st>>>(w, type, rows, cols, nb, nullptr, nullptr, out, err, qs, dd, bs,
+                                                                     accum, scale);
+  return static_cast<int>(cudaGetLastError());
+}
 }  // namespace clb
 
 extern "C" const clb200_backend_t *clb200_backend(void) { return &clb::kBackend; }

@@ -103,6 +103,7 @@ struct clb200_ctx {
   bool attrs_set = false;
   unsigned long long *trace = nullptr;             // phase trace of the one-token kernel (device, 32 per CTA) or null
   uint8_t *route_buf = nullptr;                    // clb200_route: logits, residency and result on the device
+  bool exact = false;                              // batched expert products on the integer path only (no tensor cores)
 };
 constexpr size_t ROUTE_BUF_BYTES = 1024 * 5 + 256;
 
@@ -120,6 +121,10 @@ struct SmartRoute {
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
                const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
                const SmartRoute *smart = nullptr);
+// The MoE block of layer dl on T tokens of device data x (updated in place), queued on st: the one-token kernel for T = 1,
+// the batched kernels otherwise; sel / wt (device, [T * n_used]) may be null.
+int run_moe_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,
+                  size_t errlen);
 // The routing kernel of route.cu: T tokens, one CTA each; returns non-zero when the launch fails.
 int launch_route_kernel(const float *logits, int T, int E, int K, const clb200_smart *smart, const uint8_t *resident,
                         int rstride, clb200_route_result *out, cudaStream_t st);

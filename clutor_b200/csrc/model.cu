@@ -15,6 +15,7 @@
 #include "ctx.cuh"
 #include "fwd.cuh"
 #include "gguf.h"
+#include "prefill.cuh"
 
 using namespace clb;
 
@@ -31,6 +32,12 @@ struct clb200_model {
   int ctas = 0;
   int pos = 0;
   cudaGraphExec_t gen_graph = nullptr;   // one step that feeds its own choice back (generation)
+  // the batched prompt path (clb200_model_prefill)
+  std::vector<FwdLayer> hl;        // host copy of the layer table
+  std::vector<DevLayer> moe;       // each layer's MoE block as the batched kernels take it
+  int pf_cap = 64;                 // tokens per batch: the reference's batch for a model in memory (c/src/forward.c:1048)
+  int pf_alloc = 0;                // the batch the buffers below hold
+  uint8_t *pf = nullptr;           // device: tokens, X, Q, K, V, rotated Q, attention, Q8_K activations
 };
 
 namespace {
@@ -302,6 +309,28 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
     if (row_bytes(y.gate_type, a.E) > a.grb || row_bytes(y.down_type, a.FF) > a.drb) { errf(err, errlen, "layer %d: expert row wider than planned", l); return 1; }
   }
   CUDA_OR(cudaMemcpy(m->dev + o_layers, layers.data(), sizeof(FwdLayer) * layers.size(), cudaMemcpyHostToDevice), "uploading the layer table");
+  m->hl = layers;
+  m->moe.resize(layers.size());
+  for (size_t l = 0; l < layers.size(); ++l) {   // the MoE block of each layer for the batched kernels (device pointers)
+    const FwdLayer &y = layers[l];
+    clb200_moe_layer &d = m->moe[l].d;
+    d.ffn_norm_f = y.ffn_norm;
+    d.router_f = y.router;
+    d.gate = clb200_w{y.gate, y.gate_type, a.FF, a.E};
+    d.up = clb200_w{y.up, y.gate_type, a.FF, a.E};
+    d.down = clb200_w{y.down, y.down_type, a.E, a.FF};
+    d.gate_slab = y.gate_slab;
+    d.up_slab = y.up_slab;
+    d.down_slab = y.down_slab;
+    d.n_embd = a.E;
+    d.n_ff_exp = a.FF;
+    d.n_expert = a.NE;
+    d.n_used = a.K;
+    d.norm_topk = a.norm_topk;
+    d.resid_scale = a.resid_scale;
+    d.rms_eps = a.eps;
+    m->moe[l].live = true;
+  }
   a.tok_embd = mat(o_emb, emb);
   a.output = mat(o_out, out);
   a.out_norm = reinterpret_cast<const float *>(m->dev + o_onorm);
@@ -382,6 +411,7 @@ void clb200_model_close(clb200_model *m) {
   if (m->dev) cudaFree(m->dev);
   if (m->st_host) cudaFreeHost(m->st_host);
   if (m->route_host) cudaFreeHost(m->route_host);
+  if (m->pf) cudaFree(m->pf);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }
@@ -502,6 +532,117 @@ int clb200_model_tokens(clb200_model *m, int start, int n, int *tokens_out, char
   CUDA_OR(cudaMemcpy(tokens_out, m->args.gen_out + start, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost), "tokens download");
   CUDA_OR(cudaMemcpy(m->st_host, m->args.st, sizeof(FwdState), cudaMemcpyDeviceToHost), "state download");
   if (m->st_host->err) { errf(err, errlen, "device error %d: %s", m->st_host->err, fwd_error_text(m->st_host->err)); return 1; }
+  return 0;
+}
+
+// ---- the batched prompt path: the reference's cl_fwd_prefill / run_std (c/src/forward.c:1078-1225, 1256-1282) ----------
+
+// Buffers of the batched path for batches of up to `cap` tokens, carved from one device block.
+struct PfBufs {
+  int *tok;
+  float *X, *Q, *K, *V, *Qr, *att;
+  int8_t *qs;
+  float *dd;
+  int16_t *bs;
+  size_t total;
+};
+static PfBufs pf_layout(const FwdArgs &a, int cap, uint8_t *base) {
+  PfBufs b{};
+  size_t o = 0;
+  auto take = [&](size_t n) { const size_t at = o; o += (n + 255) & ~size_t(255); return base + at; };
+  const size_t C = static_cast<size_t>(cap), W = static_cast<size_t>(std::max(a.E, a.n_q));
+  b.tok = reinterpret_cast<int *>(take(C * 4));
+  b.X = reinterpret_cast<float *>(take(C * a.E * 4));
+  b.Q = reinterpret_cast<float *>(take(C * a.n_q * 4));
+  b.K = reinterpret_cast<float *>(take(C * a.n_kvw * 4));
+  b.V = reinterpret_cast<float *>(take(C * a.n_kvw * 4));
+  b.Qr = reinterpret_cast<float *>(take(C * a.n_q * 4));
+  b.att = reinterpret_cast<float *>(take(C * a.n_q * 4));
+  b.qs = reinterpret_cast<int8_t *>(take(C * W));
+  b.dd = reinterpret_cast<float *>(take(C * W / 256 * 4));
+  b.bs = reinterpret_cast<int16_t *>(take(C * W / 16 * 2));
+  b.total = o;
+  return b;
+}
+
+#define PF_OR(call, msg)                                                                                              \
+  do {                                                                                                                \
+    const int e_ = static_cast<int>(call);                                                                            \
+    if (e_) { errf(err, errlen, "%s: %s", msg, cudaGetErrorString(static_cast<cudaError_t>(e_))); return 1; }         \
+  } while (0)
+
+// nb tokens (2 <= nb <= the batch) at positions pos .. pos + nb - 1 through every layer together; the logits after the last
+// one into `logits` (host) when it is not null.
+static int prefill_batch(clb200_model *m, const int *tokens, int nb, float *logits, char *err, size_t errlen) {
+  const FwdArgs &a = m->args;
+  const int E = a.E, NQ = a.n_q, KW = a.n_kvw, pos0 = m->pos;
+  const cudaStream_t st = m->stream;
+  const PfBufs b = pf_layout(a, m->pf_alloc, m->pf);
+  int *errw = m->ctx->small;
+  CUDA_OR(cudaMemcpyAsync(b.tok, tokens, static_cast<size_t>(nb) * 4, cudaMemcpyHostToDevice, st), "tokens upload");
+  PF_OR(pf_embed(a.tok_embd, b.tok, nb, E, a.embed_scale, b.X, st), "the embedding");
+  for (int l = 0; l < a.n_layer; ++l) {
+    const FwdLayer &y = m->hl[static_cast<size_t>(l)];
+    __half *kc = a.kc + static_cast<size_t>(l) * a.ctx * KW, *vc = a.vc + static_cast<size_t>(l) * a.ctx * KW;
+    // attention (c/src/forward.c:1096-1123): norm, Q/K/V products, QK-norm + rotation + cache, attention, O product
+    PF_OR(pf_norm_q8k(b.X, 0, nb, E, y.attn_norm, a.eps, b.qs, b.dd, b.bs, st), "the attention norm");
+    PF_OR(launch_mv_dev(y.wq.p, y.wq.type, NQ, E, nb, b.qs, b.dd, b.bs, b.Q, 0, 1.f, errw, st), "the Q product");
+    PF_OR(launch_mv_dev(y.wk.p, y.wk.type, KW, E, nb, b.qs, b.dd, b.bs, b.K, 0, 1.f, errw, st), "the K product");
+    PF_OR(launch_mv_dev(y.wv.p, y.wv.type, KW, E, nb, b.qs, b.dd, b.bs, b.V, 0, 1.f, errw, st), "the V product");
+    PfQkArgs qa{b.Q, b.K, b.V, b.Qr, y.qn, y.kn, kc, vc, a.rope_cs, nb, pos0, a.n_head, a.n_kv, a.hd, a.qk_mode, a.rope_pairs, a.eps};
+    PF_OR(pf_qk(qa, st), "QK-norm and rotation");
+    PfAttnArgs aa{b.Qr, kc, vc, b.att, nb, pos0, a.n_head, a.n_kv, a.hd, KW, a.attn_scale};
+    PF_OR(pf_attn(aa, st), "the attention");
+    PF_OR(pf_q8k(b.att, nb, NQ, b.qs, b.dd, b.bs, st), "quantizing the attention");
+    PF_OR(launch_mv_dev(y.wo.p, y.wo.type, E, NQ, nb, b.qs, b.dd, b.bs, b.X, 1, a.resid_scale, errw, st), "the O product");
+    // the mixture of experts over the batch (c/src/forward.c:1131-1210): the batched kernels
+    if (run_moe_block(m->ctx, m->moe[static_cast<size_t>(l)], b.X, nb, nullptr, nullptr, st, err, errlen)) return 1;
+  }
+  if (logits) {   // the distribution after the last token (c/src/forward.c:1218-1222)
+    PF_OR(pf_norm_q8k(b.X, nb - 1, 1, E, a.out_norm, a.eps, b.qs, b.dd, b.bs, st), "the output norm");
+    PF_OR(launch_mv_dev(a.output.p, a.output.type, a.vocab, E, 1, b.qs, b.dd, b.bs, a.logits, 0, 1.f, errw, st), "the output product");
+    CUDA_OR(cudaMemcpyAsync(logits, a.logits, static_cast<size_t>(a.vocab) * 4, cudaMemcpyDeviceToHost, st), "logits download");
+  }
+  CUDA_OR(cudaStreamSynchronize(st), "running the batch");
+  int code = 0;
+  CUDA_OR(cudaMemcpy(&code, errw, 4, cudaMemcpyDeviceToHost), "reading the device error word");
+  if (code) { errf(err, errlen, "device error %d in the batched prompt path", code); cudaMemset(errw, 0, 4096); return 1; }
+  if (logits && a.logit_scale != 1.0f)
+    for (int i = 0; i < a.vocab; ++i) logits[i] /= a.logit_scale;
+  m->pos += nb;
+  return 0;
+}
+
+int clb200_model_set_batch(clb200_model *m, int tokens) {
+  if (!m || tokens < 1 || tokens > PF_MAX_BATCH) return 1;
+  m->pf_cap = tokens;
+  return 0;
+}
+
+int clb200_model_prefill(clb200_model *m, const int *tokens, int n, float *logits, char *err, size_t errlen) {
+  if (!m) { errf(err, errlen, "no model"); return 1; }
+  const FwdArgs &a = m->args;
+  if (n < 1 || !tokens) { errf(err, errlen, "nothing to feed"); return 1; }
+  if (m->pos + n > a.ctx) { errf(err, errlen, "the context is full (%d tokens)", a.ctx); return 1; }
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= a.vocab) { errf(err, errlen, "token %d is outside the vocabulary", tokens[i]); return 1; }
+  if (m->pos + n > PF_MAX_CTX) { errf(err, errlen, "the batched prompt path takes at most %d positions", PF_MAX_CTX); return 1; }
+  cudaSetDevice(m->device);
+  const int cap = m->pf_cap;
+  if (n > 1 && m->pf_alloc < cap) {
+    if (m->pf) { CUDA_OR(cudaStreamSynchronize(m->stream), "waiting for the device"); cudaFree(m->pf); m->pf = nullptr; m->pf_alloc = 0; }
+    CUDA_OR(cudaMalloc(&m->pf, pf_layout(a, cap, nullptr).total), "allocating the batched prompt buffers");
+    m->pf_alloc = cap;
+  }
+  for (int i = 0; i < n; i += cap) {   // batches of cap tokens; a batch of one is a step (c/src/forward.c:1263-1266)
+    const int nb = std::min(cap, n - i);
+    float *lg = i + nb == n ? logits : nullptr;
+    if (nb == 1) {
+      if (clb200_model_step(m, tokens[i], lg, nullptr, nullptr, nullptr, err, errlen)) return 1;
+    } else if (prefill_batch(m, tokens + i, nb, lg, err, errlen)) {
+      return 1;
+    }
+  }
   return 0;
 }
 

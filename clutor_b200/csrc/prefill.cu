@@ -1,0 +1,230 @@
+// Per-token kernels of the batched prompt path (run_std, c/src/forward.c:1078-1225): the embedding, rmsnorm + Q8_K,
+// QK-norm + rotary embedding + the key/value store, and the plain attention of every (token, head). Every float operation
+// the reference rounds is one explicitly rounded operation here, in the reference's order, as in the one-token step.
+#include "common.cuh"
+#include "modelops.cuh"
+#include "prefill.cuh"
+#include "rowdot.cuh"
+
+namespace clb {
+namespace {
+
+constexpr int PT = 256;          // threads of the per-token kernels
+constexpr int PNW = PT / 32;
+constexpr int AT = 128;          // threads of an attention task
+
+__global__ void __launch_bounds__(PT) embed_kernel(FwdMat emb, const int *tok, int E, float scale, float *X) {
+  float *x = X + static_cast<size_t>(blockIdx.x) * E;
+  embed_row(emb, tok[blockIdx.x], E, x);
+  if (scale != 1.0f)   // c/src/forward.c:1087: x[i] *= embed_scale (each thread scales the elements it wrote)
+    for (int i = threadIdx.x; i < E; i += blockDim.x) x[i] = __fmul_rn(x[i], scale);
+}
+
+// rmsnorm (double sum of squares: per thread, a shuffle tree, then the warps in order) into shared memory, then Q8_K
+__global__ void __launch_bounds__(PT) norm_q8k_kernel(const float *X, int row0, int E, const float *w, float eps, int8_t *qs,
+                                                      float *dd, int16_t *bs) {
+  __shared__ __align__(16) float xn[4096];
+  __shared__ double red[PNW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, b = blockIdx.x;
+  const float *x = X + static_cast<size_t>(row0 + b) * E;
+  double ss = 0.0;
+  for (int i = tid; i < E; i += PT) {
+    const float v = x[i];
+    ss += static_cast<double>(v) * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  double tot = 0.0;
+  for (int k = 0; k < PNW; ++k) tot += red[k];
+  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(__ddiv_rn(tot, static_cast<double>(E))), eps)));
+  for (int i = tid; i < E; i += PT) xn[i] = __fmul_rn(__fmul_rn(x[i], s), w[i]);
+  __syncthreads();
+  q8k_quantize_block(xn, E, qs + static_cast<size_t>(b) * E, dd + static_cast<size_t>(b) * (E / 256),
+                     bs + static_cast<size_t>(b) * (E / 16), warp, PNW, lane, false);
+}
+
+__global__ void __launch_bounds__(PT) q8k_kernel(const float *src, int cols, int8_t *qs, float *dd, int16_t *bs) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, b = blockIdx.x;
+  q8k_quantize_global(src + static_cast<size_t>(b) * cols, cols / 256, qs + static_cast<size_t>(b) * cols,
+                      dd + static_cast<size_t>(b) * (cols / 256), bs + static_cast<size_t>(b) * (cols / 16), warp, PNW, lane, false);
+  (void)tid;
+}
+
+// One token per CTA; a warp per head (query heads, then key heads).
+template <int EPL>
+__global__ void __launch_bounds__(PT) qk_kernel(const PfQkArgs a) {
+  __shared__ double red[2][PNW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, b = blockIdx.x, hd = a.hd;
+  const int nq = a.n_head * hd, nk = a.n_kv * hd, pos = a.pos0 + b, GRP = a.n_head / a.n_kv;
+  const float *q = a.Q + static_cast<size_t>(b) * nq, *k = a.K + static_cast<size_t>(b) * nk, *v = a.V + static_cast<size_t>(b) * nk;
+  float qscale = 1.f, kscale = 1.f;
+  if (a.qk_mode == 1) {   // QK-norm over the whole query and the whole key (c/src/forward.c:1106): their scales
+    double sq = 0.0, sk = 0.0;
+    for (int i = tid; i < nq; i += PT) { const double t = q[i]; sq += t * t; }
+    for (int i = tid; i < nk; i += PT) { const double t = k[i]; sk += t * t; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) { sq += __shfl_xor_sync(FULL, sq, o); sk += __shfl_xor_sync(FULL, sk, o); }
+    if (lane == 0) { red[0][warp] = sq; red[1][warp] = sk; }
+    __syncthreads();
+    double tq = 0.0, tk = 0.0;
+    for (int w = 0; w < PNW; ++w) { tq += red[0][w]; tk += red[1][w]; }
+    qscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tq / nq), a.eps)));
+    kscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tk / nk), a.eps)));
+  }
+  const float *cs = a.rope_cs + static_cast<size_t>(pos) * hd;
+  for (int h = warp; h < a.n_head + a.n_kv; h += PNW) {
+    const bool isk = h >= a.n_head;
+    const int head = isk ? h - a.n_head : h;
+    const float *src = (isk ? k : q) + head * hd;
+    float x[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) x[e] = src[lane + 32 * e];
+    if (a.qk_mode == 2) {   // per head, one weight vector shared by the heads (c/src/forward.c:1105)
+      double ss = 0.0;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) ss += static_cast<double>(x[e]) * x[e];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
+      const float s1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(ss / hd), a.eps)));
+      const float *w = isk ? a.kn : a.qn;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], s1), w[lane + 32 * e]);
+    } else if (a.qk_mode == 1) {
+      const float s1 = isk ? kscale : qscale;
+      const float *w = (isk ? a.kn : a.qn) + head * hd;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) x[e] = __fmul_rn(__fmul_rn(x[e], s1), w[lane + 32 * e]);
+    }
+    rope_warp<EPL>(x, cs, a.rope_pairs != 0);
+    if (isk) {   // kv_put (c/src/forward.c:563-565): the key and the value, rounded to half
+      __half *kd = a.kc + static_cast<size_t>(pos) * nk + head * hd, *vd = a.vc + static_cast<size_t>(pos) * nk + head * hd;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        kd[lane + 32 * e] = __float2half_rn(x[e]);
+        vd[lane + 32 * e] = __float2half_rn(v[head * hd + lane + 32 * e]);
+      }
+    } else {
+      float *dst = a.Qr + static_cast<size_t>(b) * nq + head * hd;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) dst[lane + 32 * e] = x[e];
+    }
+  }
+  (void)GRP;
+}
+
+// One (query head, token) per CTA. Shared memory: the query [hd] and the scores [pos + 1].
+__global__ void __launch_bounds__(AT) attn_kernel(const PfAttnArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ float red[AT / 32];
+  __shared__ float s_sum;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = blockIdx.x, b = blockIdx.y, hd = a.hd, nq = a.n_head * hd, KW = a.n_kvw;
+  const int pos = a.pos0 + b, n = pos + 1, g = h / (a.n_head / a.n_kv);
+  float *q = sm, *sc = sm + hd;
+  for (int i = tid; i < hd; i += AT) q[i] = a.Qr[static_cast<size_t>(b) * nq + h * hd + i];
+  __syncthreads();
+  // scores: the reference's dotf_h (c/src/forward.c:492-510), eight running sums combined ((0+1)+(2+3))+((4+5)+(6+7))
+  float mx = -INFINITY;
+  const __half *kb = a.kc + g * hd;
+  for (int t = tid; t < n; t += AT) {
+    const __half *kr = kb + static_cast<size_t>(t) * KW;
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < hd; i += 8) {
+      const uint4 raw = *reinterpret_cast<const uint4 *>(kr + i);
+      const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 f = __half22float2(h2[u]);
+        s[2 * u] = __fadd_rn(s[2 * u], __fmul_rn(q[i + 2 * u], f.x));
+        s[2 * u + 1] = __fadd_rn(s[2 * u + 1], __fmul_rn(q[i + 2 * u + 1], f.y));
+      }
+    }
+    const float d = __fadd_rn(__fadd_rn(__fadd_rn(s[0], s[1]), __fadd_rn(s[2], s[3])), __fadd_rn(__fadd_rn(s[4], s[5]), __fadd_rn(s[6], s[7])));
+    const float v = __fmul_rn(d, a.attn_scale);
+    sc[t] = v;
+    if (v > mx) mx = v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < AT / 32; ++w) mx = fmaxf(mx, red[w]);
+  for (int t = tid; t < n; t += AT) sc[t] = expf_cr(__fsub_rn(sc[t], mx));
+  __syncthreads();
+  if (tid == 0) {   // the float sum in position order (c/src/forward.c:602-603)
+    float sum = 0.f;
+    for (int t = 0; t < n; ++t) sum = __fadd_rn(sum, sc[t]);
+    s_sum = sum;
+  }
+  __syncthreads();
+  const float sum = s_sum;
+  for (int t = tid; t < n; t += AT) sc[t] = __fdiv_rn(sc[t], sum);
+  __syncthreads();
+  // values: axpy_h (c/src/forward.c:512-521) in position order, one thread per element of the head
+  const __half *vb = a.vc + g * hd;
+  for (int d = tid; d < hd; d += AT) {
+    float o = 0.f;
+    int t = 0;
+    for (; t + 4 <= n; t += 4) {
+      const float v0 = __half2float(vb[static_cast<size_t>(t) * KW + d]), v1 = __half2float(vb[static_cast<size_t>(t + 1) * KW + d]);
+      const float v2 = __half2float(vb[static_cast<size_t>(t + 2) * KW + d]), v3 = __half2float(vb[static_cast<size_t>(t + 3) * KW + d]);
+      o = __fadd_rn(o, __fmul_rn(sc[t], v0));
+      o = __fadd_rn(o, __fmul_rn(sc[t + 1], v1));
+      o = __fadd_rn(o, __fmul_rn(sc[t + 2], v2));
+      o = __fadd_rn(o, __fmul_rn(sc[t + 3], v3));
+    }
+    for (; t < n; ++t) o = __fadd_rn(o, __fmul_rn(sc[t], __half2float(vb[static_cast<size_t>(t) * KW + d])));
+    a.att[static_cast<size_t>(b) * nq + h * hd + d] = o;
+  }
+}
+
+}  // namespace
+
+cudaError_t pf_embed(const FwdMat &emb, const int *tok, int nb, int E, float embed_scale, float *X, cudaStream_t st) {
+  embed_kernel<<<nb, PT, 0, st>>>(emb, tok, E, embed_scale, X);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_norm_q8k(const float *X, int row0, int nb, int E, const float *w, float eps, int8_t *qs, float *dd, int16_t *bs,
+                        cudaStream_t st) {
+  if (E > 4096 || E % 256) return cudaErrorInvalidValue;
+  norm_q8k_kernel<<<nb, PT, 0, st>>>(X, row0, E, w, eps, qs, dd, bs);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_q8k(const float *src, int nb, int cols, int8_t *qs, float *dd, int16_t *bs, cudaStream_t st) {
+  if (cols % 256) return cudaErrorInvalidValue;
+  q8k_kernel<<<nb, PT, 0, st>>>(src, cols, qs, dd, bs);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_qk(const PfQkArgs &a, cudaStream_t st) {
+  switch (a.hd) {
+    case 64: qk_kernel<2><<<a.nb, PT, 0, st>>>(a); break;
+    case 128: qk_kernel<4><<<a.nb, PT, 0, st>>>(a); break;
+    case 256: qk_kernel<8><<<a.nb, PT, 0, st>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t pf_attn(const PfAttnArgs &a, cudaStream_t st) {
+  const int n = a.pos0 + a.nb;
+  if (n > PF_MAX_CTX || a.hd % 8) return cudaErrorInvalidValue;
+  const size_t smem = (static_cast<size_t>(a.hd) + n) * 4;
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (PF_MAX_CTX + 256) * 4);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  attn_kernel<<<dim3(a.n_head, a.nb), AT, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace clb

@@ -31,6 +31,8 @@ def _bind(L) -> None:
     L.clb200_model_generate.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_char_p, C.c_size_t]
     L.clb200_model_generate_async.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_char_p, C.c_size_t]
     L.clb200_model_tokens.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_char_p, C.c_size_t]
+    L.clb200_model_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_char_p, C.c_size_t]
+    L.clb200_model_set_batch.argtypes = [C.c_void_p, C.c_int]
     L._model_bound = True
 
 
@@ -82,6 +84,19 @@ class Model:
                                     sel.ctypes.data if route else None, wt.ctypes.data if route else None, self._err, 512):
             raise ClutorError(self._err.value.decode())
         return lg, nxt.value, ((sel, wt) if route else None)
+
+    def prefill(self, tokens, logits: bool = True):
+        """cl_fwd_prefill (clb200_model_prefill): the tokens in batches; the logits after the last one, or None."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        lg = np.zeros(self.n_vocab, np.float32) if logits else None
+        if self.L.clb200_model_prefill(self.h, t.ctypes.data, len(t), lg.ctypes.data if lg is not None else None, self._err, 512):
+            raise ClutorError(self._err.value.decode())
+        return lg
+
+    def set_batch(self, tokens: int) -> None:
+        """Tokens per prefill batch (the reference's CLUTOR_PS_B), 1..512."""
+        if self.L.clb200_model_set_batch(self.h, tokens):
+            raise ClutorError(f"a prefill batch of {tokens} tokens is out of range")
 
     def generate(self, token: int, n: int) -> list[int]:
         """Greedy generation on the device: feeds `token`, then each arg-max; returns the n chosen tokens."""

@@ -116,6 +116,10 @@ uint64_t clb200_device_bytes(const clb200_ctx *c);
  * each CTA write the SM cycle counter at its phase boundaries (entries 0-29 of its row) and the global nanosecond timer at
  * entry and exit (entries 30, 31). NULL turns it off. */
 void clb200_set_trace(clb200_ctx *c, void *dev_buf);
+/* on = 1: batched calls (T > 1, and the batched prompt path of a model opened on this context) compute every expert product
+ * on the integer path, which gives the reference's numbers bit for bit; on = 0 (the default): Q8_0 and Q4_K expert products
+ * run on the tensor cores from fp16 hi/lo operands, within ~2e-5 of them and several times faster. */
+void clb200_set_exact(clb200_ctx *c, int on);
 
 /* ---- the expert cache policy (host) -------------------------------------------------------------------------------------- */
 /* Which expert occupies which HBM slot: the reference's cl_cache (c/src/cache.h:11-47, c/src/cache.c), same decisions, same
@@ -281,6 +285,15 @@ int clb200_model_generate(clb200_model *m, int token, int n, int *tokens_out, ch
  * tokens of positions [start, start + n) afterwards with clb200_model_tokens. */
 int clb200_model_generate_async(clb200_model *m, int token, int n, void *stream, char *err, size_t errlen);
 int clb200_model_tokens(clb200_model *m, int start, int n, int *tokens_out, char *err, size_t errlen);
+/* cl_fwd_prefill (forward.h:121, c/src/forward.c:1256-1282): feeds n tokens at the current position in batches (run_std,
+ * :1078-1225): every dense matrix is multiplied with the whole batch, each token routes as it would alone and each chosen
+ * expert runs once over the tokens that chose it; the attention of each token sees the positions up to its own. logits
+ * (host, n_vocab floats) may be NULL, else it receives the distribution after the last token. A batch of one token is a
+ * step, as in the reference. Returns 0, or 1 with err set. */
+int clb200_model_prefill(clb200_model *m, const int *tokens, int n, float *logits, char *err, size_t errlen);
+/* Tokens per batch of clb200_model_prefill, 1..512 (the reference's CLUTOR_PS_B; default 64, its batch for a model held in
+ * memory, c/src/forward.c:1048). Returns 0, or 1 for a value out of range. */
+int clb200_model_set_batch(clb200_model *m, int tokens);
 
 #ifdef __cplusplus
 }

@@ -286,6 +286,7 @@ class RefModel:
         L.ref_fwd_info.argtypes = [C.c_void_p, C.c_void_p]
         L.ref_fwd_step.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
         L.ref_fwd_close.argtypes = [C.c_void_p]
+        L.ref_fwd_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_char_p, C.c_size_t]
         self.L = L
         self.err = C.create_string_buffer(512)
         self.h = L.ref_fwd_open(path.encode(), n_ctx, self.err, 512)
@@ -303,6 +304,14 @@ class RefModel:
         if self.L.ref_fwd_step(self.h, token, logits.ctypes.data, sel.ctypes.data, wt.ctypes.data, self.err, 512):
             raise RuntimeError(self.err.value.decode())
         return logits, sel, wt
+
+    def prefill(self, tokens, logits: bool = True):
+        """cl_fwd_prefill: the tokens in batches (CLUTOR_PS_B in the environment shrinks them); the logits after the last."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(self.n_vocab, np.float32) if logits else None
+        if self.L.ref_fwd_prefill(self.h, t.ctypes.data, len(t), None if out is None else out.ctypes.data, self.err, 512):
+            raise RuntimeError(self.err.value.decode())
+        return out
 
     def greedy(self, first: int, n: int) -> list[int]:
         """The reference's generate loop (c/src/main.c:342-360) on ids: feed `first`, then each arg-max, n tokens."""

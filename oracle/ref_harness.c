@@ -143,6 +143,10 @@ int ref_fwd_step(void *h, int token, float *logits, int *sel, float *wt, char *e
   cl_fwd_route rt = {sel, wt, NULL, f->n_layer, f->n_used};
   return cl_fwd_step(f, token, logits, sel && wt ? &rt : NULL, err, errlen);
 }
+/* cl_fwd_prefill (c/src/forward.h:121): n tokens in batches (run_std); logits [n_vocab] after the last one (may be NULL). */
+int ref_fwd_prefill(void *h, const int *tokens, int n, float *logits, char *err, size_t errlen) {
+  return cl_fwd_prefill(h, tokens, n, logits, err, errlen);
+}
 void ref_fwd_close(void *h) {
   if (!h) return;
   cl_fwd_close(h);
