@@ -586,15 +586,15 @@ static int prefill_batch(clb200_model *m, const int *tokens, int nb, float *logi
     __half *kc = a.kc + static_cast<size_t>(l) * a.ctx * KW, *vc = a.vc + static_cast<size_t>(l) * a.ctx * KW;
     // attention (c/src/forward.c:1096-1123): norm, Q/K/V products, QK-norm + rotation + cache, attention, O product
     PF_OR(pf_norm_q8k(b.X, 0, nb, E, y.attn_norm, a.eps, b.qs, b.dd, b.bs, st), "the attention norm");
-    PF_OR(launch_mv_dev(y.wq.p, y.wq.type, NQ, E, nb, b.qs, b.dd, b.bs, b.Q, 0, 1.f, errw, st), "the Q product");
-    PF_OR(launch_mv_dev(y.wk.p, y.wk.type, KW, E, nb, b.qs, b.dd, b.bs, b.K, 0, 1.f, errw, st), "the K product");
-    PF_OR(launch_mv_dev(y.wv.p, y.wv.type, KW, E, nb, b.qs, b.dd, b.bs, b.V, 0, 1.f, errw, st), "the V product");
+    PF_OR(pf_mv(y.wq, NQ, E, nb, b.qs, b.dd, b.bs, b.Q, 0, 1.f, errw, st), "the Q product");
+    PF_OR(pf_mv(y.wk, KW, E, nb, b.qs, b.dd, b.bs, b.K, 0, 1.f, errw, st), "the K product");
+    PF_OR(pf_mv(y.wv, KW, E, nb, b.qs, b.dd, b.bs, b.V, 0, 1.f, errw, st), "the V product");
     PfQkArgs qa{b.Q, b.K, b.V, b.Qr, y.qn, y.kn, kc, vc, a.rope_cs, nb, pos0, a.n_head, a.n_kv, a.hd, a.qk_mode, a.rope_pairs, a.eps};
     PF_OR(pf_qk(qa, st), "QK-norm and rotation");
     PfAttnArgs aa{b.Qr, kc, vc, b.att, nb, pos0, a.n_head, a.n_kv, a.hd, KW, a.attn_scale};
     PF_OR(pf_attn(aa, st), "the attention");
     PF_OR(pf_q8k(b.att, nb, NQ, b.qs, b.dd, b.bs, st), "quantizing the attention");
-    PF_OR(launch_mv_dev(y.wo.p, y.wo.type, E, NQ, nb, b.qs, b.dd, b.bs, b.X, 1, a.resid_scale, errw, st), "the O product");
+    PF_OR(pf_mv(y.wo, E, NQ, nb, b.qs, b.dd, b.bs, b.X, 1, a.resid_scale, errw, st), "the O product");
     // the mixture of experts over the batch (c/src/forward.c:1131-1210): the batched kernels
     if (run_moe_block(m->ctx, m->moe[static_cast<size_t>(l)], b.X, nb, nullptr, nullptr, st, err, errlen)) return 1;
   }

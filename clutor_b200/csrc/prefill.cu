@@ -181,7 +181,100 @@ __global__ void __launch_bounds__(AT) attn_kernel(const PfAttnArgs a) {
   }
 }
 
+// Dense products of a batch: out [nb][rows] (= or += scale *) w [rows][cols] (Q4_K / Q6_K) times plain Q8_K activations.
+// A CTA stages MT_ROWS rows (one bulk copy) and MT_TOK tokens' activations (swizzled Q8_K, each token's row padded by 16
+// bytes so the lanes of a warp, one token each, read different banks); a warp takes a row at a time and every lane forms
+// that row's dot product with its own token: the block terms of the reference (exact integer sums per 256-block) added in
+// block order. The weights are read once per CTA (a broadcast to the warp's lanes).
+constexpr int MT_ROWS = 32, MT_TOK = 32, MT_THREADS = 256;
+
+struct MtLayout {
+  uint32_t w, act, bs, dd, total, act_stride, bs_stride, dd_stride;
+};
+__host__ __device__ inline MtLayout mt_layout(uint32_t rb, int cols) {
+  MtLayout L{};
+  const uint32_t nblk = static_cast<uint32_t>(cols) / 256;
+  L.w = 16;
+  L.act = (L.w + MT_ROWS * rb + 32 + 15) & ~15u;
+  L.act_stride = static_cast<uint32_t>(cols) + 16;
+  L.bs = L.act + MT_TOK * L.act_stride;
+  L.bs_stride = static_cast<uint32_t>(cols) / 16 + 2;   // int16 units: an odd number of words per token
+  L.dd = (L.bs + MT_TOK * L.bs_stride * 2 + 15) & ~15u;
+  L.dd_stride = nblk + 1;                               // floats: an odd number of words per token when nblk is even
+  L.total = L.dd + MT_TOK * L.dd_stride * 4;
+  return L;
+}
+
+__global__ void __launch_bounds__(MT_THREADS) mvt_kernel(const uint8_t *w, uint32_t type, uint32_t rb, int rows, int cols, int nb,
+                                                         const int8_t *qs, const float *dd, const int16_t *bs, float *out,
+                                                         int accum, float scale, int *err) {
+  extern __shared__ __align__(128) uint8_t mt_sm[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = blockIdx.x * MT_ROWS, R = min(MT_ROWS, rows - r0);
+  const int t0 = blockIdx.y * MT_TOK, nt = min(MT_TOK, nb - t0);
+  const int nblk = cols / 256;
+  const MtLayout L = mt_layout(rb, cols);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(mt_sm);
+  const uint8_t *src = w + static_cast<size_t>(r0) * rb;
+  const uint32_t lo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(src) & 15u);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+    const uint32_t n16 = (lo + static_cast<uint32_t>(R) * rb + 15u) & ~15u;
+    mbar_arrive_expect_tx(bar, n16);
+    bulk_copy_g2s(mt_sm + L.w, src - lo, n16, bar);
+  }
+  // this chunk's activations: values swizzled per 256-block (q8k_chunk_off), group sums and scales, rows padded
+  const int chunks = cols / 16;
+  for (int i = tid; i < nt * chunks; i += MT_THREADS) {
+    const int t = i / chunks, c = i - t * chunks;
+    const int4 v = *reinterpret_cast<const int4 *>(qs + static_cast<size_t>(t0 + t) * cols + 16 * c);
+    *reinterpret_cast<int4 *>(mt_sm + L.act + t * L.act_stride + q8k_chunk_off(c >> 4, c & 15, true)) = v;
+  }
+  int16_t *sbs = reinterpret_cast<int16_t *>(mt_sm + L.bs);
+  for (int i = tid; i < nt * chunks; i += MT_THREADS) {
+    const int t = i / chunks, g = i - t * chunks;
+    sbs[t * L.bs_stride + g] = bs[static_cast<size_t>(t0 + t) * chunks + g];
+  }
+  float *sdd = reinterpret_cast<float *>(mt_sm + L.dd);
+  for (int i = tid; i < nt * nblk; i += MT_THREADS) {
+    const int t = i / nblk, b = i - t * nblk;
+    sdd[t * L.dd_stride + b] = dd[static_cast<size_t>(t0 + t) * nblk + b];
+  }
+  __syncthreads();
+  if (!mbar_wait_bounded(bar, 0)) { set_error(err, ERR_WAIT_COPY); return; }
+  if (lane >= nt) return;
+  const SmemAct act{reinterpret_cast<const int8_t *>(mt_sm + L.act + lane * L.act_stride), sbs + lane * L.bs_stride, sdd + lane * L.dd_stride};
+  const uint8_t *wrows = mt_sm + L.w + lo;
+  for (int r = warp; r < R; r += MT_THREADS / 32) {
+    const uint8_t *row = wrows + static_cast<size_t>(r) * rb;
+    float sum = 0.f;
+    for (int b = 0; b < nblk; ++b) sum = __fadd_rn(sum, kq_block_s<false>(type, row, b, act, b));
+    float *o = out + static_cast<size_t>(t0 + lane) * rows + r0 + r;
+    *o = accum ? __fadd_rn(*o, __fmul_rn(scale, sum)) : sum;
+  }
+}
+
 }  // namespace
+
+int pf_mv(const FwdMat &m, int rows, int cols, int nb, const int8_t *qs, const float *dd, const int16_t *bs, float *out, int accum,
+          float scale, int *err, cudaStream_t st) {
+  if (nb < 8 || (m.type != T_Q4_K && m.type != T_Q6_K))
+    return launch_mv_dev(m.p, m.type, rows, cols, nb, qs, dd, bs, out, accum, scale, err, st);
+  const MtLayout L = mt_layout(m.rb, cols);
+  if (L.total > 227 * 1024) return launch_mv_dev(m.p, m.type, rows, cols, nb, qs, dd, bs, out, accum, scale, err, st);
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(mvt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr[dev] = true;
+  }
+  const dim3 grid((rows + MT_ROWS - 1) / MT_ROWS, (nb + MT_TOK - 1) / MT_TOK);
+  mvt_kernel<<<grid, MT_THREADS, L.total, st>>>(m.p, m.type, m.rb, rows, cols, nb, qs, dd, bs, out, accum, scale, err);
+  return static_cast<int>(cudaGetLastError());
+}
 
 cudaError_t pf_embed(const FwdMat &emb, const int *tok, int nb, int E, float embed_scale, float *X, cudaStream_t st) {
   embed_kernel<<<nb, PT, 0, st>>>(emb, tok, E, embed_scale, X);

@@ -45,6 +45,10 @@ struct PfAttnArgs {
 };
 cudaError_t pf_attn(const PfAttnArgs &a, cudaStream_t st);
 
+// A dense product of a batch, out [nb][rows] (= or += scale *) m [rows][cols] times plain Q8_K activations: a CTA per 32
+// rows and 32 tokens for batches of 8 or more tokens, else the product kernel of backend.cu. Returns a CUDA error code.
+int pf_mv(const FwdMat &m, int rows, int cols, int nb, const int8_t *qs, const float *dd, const int16_t *bs, float *out, int accum,
+          float scale, int *err, cudaStream_t st);
 // The dense product kernel of backend.cu: out [nb][rows] (= or += scale *) w [rows][cols] times plain Q8_K activations.
 int launch_mv_dev(const uint8_t *w, uint32_t type, int rows, int cols, int nb, const int8_t *qs, const float *dd,
                   const int16_t *bs, float *out, int accum, float scale, int *err, cudaStream_t st);
