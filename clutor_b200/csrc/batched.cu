@@ -388,27 +388,117 @@ __global__ void __launch_bounds__(BT) down_kernel(const BatchArgs a) {
   }
 }
 
-// K-quant down rows of the integer path for experts with several tokens: one thread per row (DR rows of expert e staged by
-// one bulk copy), every token of the expert against it in chunks of DTOK (their Q8_K hg rows in shared memory, read by all
-// threads at once), so each weight word is unpacked once for all the chunk's tokens. The reference's block term per token
-// (exact integer sums; Q6_K: d * d_a * sum_g sc_g (dot_g - 32 bsum_g); Q4_K: d_a * (d * sum_j sc_j dot_j - dmin *
-// sum_j mn_j bsum_j)), added in block order.
-constexpr int DR = 128, DTOK = 16;
+// K-quant down rows of the integer path for experts with several tokens: two threads per row (DR rows of expert e staged by
+// one bulk copy; each thread takes half of every block's groups), every token of the expert against the row in passes of
+// 8, 4, 2 or 1 tokens (their Q8_K hg rows in shared memory, read by all threads at once), so each weight word is unpacked
+// once per pass. The two halves' exact integer sums meet by a shuffle; then the reference's block term per token (Q6_K:
+// d * d_a * sum_g sc_g (dot_g - 32 bsum_g); Q4_K: d_a * (d * sum_j sc_j dot_j - dmin * sum_j mn_j bsum_j)), added in
+// block order.
+constexpr int DR = 128, DRT = 2 * DR, DCH = 32;   // rows, threads, tokens staged at once
 
-__host__ __device__ inline size_t down_rows_act_bytes(int FF) { return static_cast<size_t>(DTOK) * (FF + FF / 256 * 4 + FF / 16 * 2); }
+__host__ __device__ inline size_t down_rows_act_bytes(int FF) { return static_cast<size_t>(DCH) * (FF + FF / 256 * 4 + FF / 16 * 2); }
+
+// One pass of NT tokens (staged rows t0 .. t0 + NT - 1) over the row: writes their outputs to hd (thread half 0).
+template <uint32_t DT, int NT>
+CLB_DEV void down_pass(const BatchArgs &a, const uint8_t *row, int half, const int8_t *aq, const int16_t *ab, const float *ad,
+                       int t0, size_t pos0, int col, bool store) {
+  const int FF = a.FF, nbd = FF / 256, nbs = FF / 16;
+  float acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+  for (int blk = 0; blk < nbd; ++blk) {
+    int si[NT], mi[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) si[t] = mi[t] = 0;
+    const int8_t *xq = aq + static_cast<size_t>(t0) * FF + 256 * blk;
+    const int16_t *xb = ab + t0 * nbs + 16 * blk;
+    if (DT == T_Q6_K) {
+      const uint8_t *bp = row + 210 * blk;
+      const int8_t *sc = reinterpret_cast<const int8_t *>(bp + 192);
+#pragma unroll 2
+      for (int g = 8 * half; g < 8 * half + 8; ++g) {   // 16-groups: half h, part (which 32 of the half), which 16
+        const int h = g >> 3, part = (g & 7) >> 1, l0 = 16 * (g & 1);
+        const uint8_t *ql = bp + 64 * h + l0 + 32 * (part & 1), *qh = bp + 128 + 32 * h + l0;
+        uint32_t v[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const uint32_t L = lds_u32_unaligned(ql + 4 * w), H = lds_u32_unaligned(qh + 4 * w);
+          v[w] = ((part >= 2 ? (L >> 4) : L) & 0x0f0f0f0fu) | (((H >> (2 * part)) & 0x03030303u) << 4);
+        }
+        const int s = sc[g];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const int4 x = reinterpret_cast<const int4 *>(xq + t * FF)[g];
+          int d = __dp4a(static_cast<int>(v[0]), x.x, 0);
+          d = __dp4a(static_cast<int>(v[1]), x.y, d);
+          d = __dp4a(static_cast<int>(v[2]), x.z, d);
+          d = __dp4a(static_cast<int>(v[3]), x.w, d);
+          si[t] += s * (d - 32 * xb[t * nbs + g]);
+        }
+      }
+    } else {   // Q4_K: 64-value groups g4 (low nibbles sub-block 2 g4, high nibbles 2 g4 + 1), two per thread
+      const uint8_t *bp = row + 144 * blk;
+#pragma unroll 1
+      for (int g4 = 2 * half; g4 < 2 * half + 2; ++g4) {
+        int sc0, mn0, sc1, mn1;
+        q4k_scale_min(bp + 4, 2 * g4, sc0, mn0);
+        q4k_scale_min(bp + 4, 2 * g4 + 1, sc1, mn1);
+        uint32_t wq[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) wq[w] = lds_u32_unaligned(bp + 16 + 32 * g4 + 4 * w);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const int4 *xa = reinterpret_cast<const int4 *>(xq + t * FF + 64 * g4);
+          const int4 x0 = xa[0], x1 = xa[1], x2 = xa[2], x3 = xa[3];
+          const int xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w}, xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+          int l = 0, hh = 0;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            l = __dp4a(static_cast<int>(wq[w] & 0x0f0f0f0fu), xl[w], l);
+            hh = __dp4a(static_cast<int>((wq[w] >> 4) & 0x0f0f0f0fu), xh[w], hh);
+          }
+          const int16_t *b16 = xb + t * nbs + 4 * g4;
+          si[t] += sc0 * l + sc1 * hh;
+          mi[t] += mn0 * (b16[0] + b16[1]) + mn1 * (b16[2] + b16[3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {   // the row's two halves: exact integer sums, any order
+      si[t] += __shfl_xor_sync(0xffffffffu, si[t], 1);
+      if (DT == T_Q4_K) mi[t] += __shfl_xor_sync(0xffffffffu, mi[t], 1);
+    }
+    if (DT == T_Q6_K) {
+      const float dw = f16_bits_to_f32(lds_u16(row + 210 * blk + 208));
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, ad[(t0 + t) * nbd + blk]), static_cast<float>(si[t])));
+    } else {
+      const uint8_t *bp = row + 144 * blk;
+      const float dw = f16_bits_to_f32(lds_u16(bp)), dmin = f16_bits_to_f32(lds_u16(bp + 2));
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        acc[t] = __fadd_rn(acc[t], __fmul_rn(ad[(t0 + t) * nbd + blk], __fsub_rn(__fmul_rn(dw, static_cast<float>(si[t])),
+                                                                               __fmul_rn(dmin, static_cast<float>(mi[t])))));
+    }
+  }
+  if (store) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) a.hd[(pos0 + t) * a.E + col] = acc[t];
+  }
+}
 
 template <uint32_t DT>
-__global__ void __launch_bounds__(DR) down_rows_kernel(const BatchArgs a) {
+__global__ void __launch_bounds__(DRT) down_rows_kernel(const BatchArgs a) {
   const int e = blockIdx.x, n = a.counts[e];
   if (n == 0) return;
   extern __shared__ __align__(128) uint8_t sm[];
-  const int tid = threadIdx.x, E = a.E, FF = a.FF, nbd = FF / 256;
+  const int tid = threadIdx.x, half = tid & 1, rr = tid >> 1, E = a.E, FF = a.FF, nbd = FF / 256;
   const int r0 = blockIdx.y * DR, R = min(DR, E - r0);
   const uint32_t drb = a.drb;
   uint64_t *bar = reinterpret_cast<uint64_t *>(sm);
-  int8_t *aq = reinterpret_cast<int8_t *>(sm + 16);                               // [DTOK][FF]
-  float *ad = reinterpret_cast<float *>(aq + DTOK * FF);                          // [DTOK][nbd]
-  int16_t *ab = reinterpret_cast<int16_t *>(ad + DTOK * nbd);                     // [DTOK][FF / 16]
+  int8_t *aq = reinterpret_cast<int8_t *>(sm + 16);                               // [DCH][FF]
+  float *ad = reinterpret_cast<float *>(aq + DCH * FF);                           // [DCH][nbd]
+  int16_t *ab = reinterpret_cast<int16_t *>(ad + DCH * nbd);                      // [DCH][FF / 16]
   uint8_t *wbuf = sm + ((16 + down_rows_act_bytes(FF) + 15) & ~size_t(15));
   const uint8_t *src = a.down + static_cast<size_t>(e) * a.down_slab + static_cast<size_t>(r0) * drb;
   const uint32_t lo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(src) & 15u);
@@ -425,97 +515,25 @@ __global__ void __launch_bounds__(DR) down_rows_kernel(const BatchArgs a) {
   if (bad && tid == 0) set_error(a.err, ERR_BAD_EXPERT);
   if (!mbar_wait_bounded(bar, 0)) { set_error(a.err, ERR_WAIT_COPY); return; }
   if (bad) return;
-  const uint8_t *row = wbuf + lo + static_cast<size_t>(tid < R ? tid : 0) * drb;
-  for (int c0 = 0; c0 < n; c0 += DTOK) {
-    const int nc = min(DTOK, n - c0);
-    __syncthreads();   // the previous chunk's activations are consumed
-    for (int i = tid; i < nc * (FF / 16); i += DR) {
+  const bool live = rr < R;
+  const uint8_t *row = wbuf + lo + static_cast<size_t>(live ? rr : 0) * drb;
+  for (int s0 = 0; s0 < n; s0 += DCH) {
+    const int ns = min(DCH, n - s0);
+    __syncthreads();   // the previous tokens' activations are consumed
+    for (int i = tid; i < ns * (FF / 16); i += DRT) {
       const int t = i / (FF / 16), c = i - t * (FF / 16);
-      reinterpret_cast<int4 *>(aq + t * FF)[c] = reinterpret_cast<const int4 *>(a.hq_qs + static_cast<size_t>(p0 + c0 + t) * FF)[c];
-      ab[t * (FF / 16) + c] = a.hq_bs[static_cast<size_t>(p0 + c0 + t) * (FF / 16) + c];
+      reinterpret_cast<int4 *>(aq + t * FF)[c] = reinterpret_cast<const int4 *>(a.hq_qs + static_cast<size_t>(p0 + s0 + t) * FF)[c];
+      ab[t * (FF / 16) + c] = a.hq_bs[static_cast<size_t>(p0 + s0 + t) * (FF / 16) + c];
     }
-    for (int i = tid; i < nc * nbd; i += DR) ad[i] = a.hq_d[static_cast<size_t>(p0 + c0) * nbd + i];
+    for (int i = tid; i < ns * nbd; i += DRT) ad[i] = a.hq_d[static_cast<size_t>(p0 + s0) * nbd + i];
     __syncthreads();
-    if (tid >= R) continue;
-    float acc[DTOK];
-#pragma unroll
-    for (int t = 0; t < DTOK; ++t) acc[t] = 0.f;
-    for (int blk = 0; blk < nbd; ++blk) {
-      int si[DTOK];
-#pragma unroll
-      for (int t = 0; t < DTOK; ++t) si[t] = 0;
-      if (DT == T_Q6_K) {
-        const uint8_t *bp = row + 210 * blk;
-        const int8_t *sc = reinterpret_cast<const int8_t *>(bp + 192);
-#pragma unroll 1
-        for (int g = 0; g < 16; ++g) {   // 16-groups: half h, part (which 32 of the half), which 16 of the part
-          const int h = g >> 3, part = (g & 7) >> 1, l0 = 16 * (g & 1);
-          const uint8_t *ql = bp + 64 * h + l0 + 32 * (part & 1), *qh = bp + 128 + 32 * h + l0;
-          uint32_t v[4];
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t L = lds_u32_unaligned(ql + 4 * w), H = lds_u32_unaligned(qh + 4 * w);
-            v[w] = ((part >= 2 ? (L >> 4) : L) & 0x0f0f0f0fu) | (((H >> (2 * part)) & 0x03030303u) << 4);
-          }
-          const int s = sc[g];
-#pragma unroll
-          for (int t = 0; t < DTOK; ++t) {
-            if (t < nc) {
-              const int4 x = reinterpret_cast<const int4 *>(aq + t * FF + 256 * blk)[g];
-              int d = __dp4a(static_cast<int>(v[0]), x.x, 0);
-              d = __dp4a(static_cast<int>(v[1]), x.y, d);
-              d = __dp4a(static_cast<int>(v[2]), x.z, d);
-              d = __dp4a(static_cast<int>(v[3]), x.w, d);
-              si[t] += s * (d - 32 * ab[t * (FF / 16) + 16 * blk + g]);
-            }
-          }
-        }
-        const float dw = f16_bits_to_f32(lds_u16(bp + 208));
-#pragma unroll
-        for (int t = 0; t < DTOK; ++t)
-          if (t < nc) acc[t] = __fadd_rn(acc[t], __fmul_rn(__fmul_rn(dw, ad[t * nbd + blk]), static_cast<float>(si[t])));
-      } else {   // Q4_K
-        const uint8_t *bp = row + 144 * blk;
-        int mi[DTOK];
-#pragma unroll
-        for (int t = 0; t < DTOK; ++t) mi[t] = 0;
-#pragma unroll 1
-        for (int g4 = 0; g4 < 4; ++g4) {   // 64-value groups: low nibbles are sub-block 2 g4, high nibbles 2 g4 + 1
-          int sc0, mn0, sc1, mn1;
-          q4k_scale_min(bp + 4, 2 * g4, sc0, mn0);
-          q4k_scale_min(bp + 4, 2 * g4 + 1, sc1, mn1);
-          uint32_t wq[8];
-#pragma unroll
-          for (int w = 0; w < 8; ++w) wq[w] = lds_u32_unaligned(bp + 16 + 32 * g4 + 4 * w);
-#pragma unroll
-          for (int t = 0; t < DTOK; ++t) {
-            if (t < nc) {
-              const int4 *xa = reinterpret_cast<const int4 *>(aq + t * FF + 256 * blk + 64 * g4);
-              const int4 x0 = xa[0], x1 = xa[1], x2 = xa[2], x3 = xa[3];
-              const int xl[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w}, xh[8] = {x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-              int l = 0, hh = 0;
-#pragma unroll
-              for (int w = 0; w < 8; ++w) {
-                l = __dp4a(static_cast<int>(wq[w] & 0x0f0f0f0fu), xl[w], l);
-                hh = __dp4a(static_cast<int>((wq[w] >> 4) & 0x0f0f0f0fu), xh[w], hh);
-              }
-              const int16_t *b16 = ab + t * (FF / 16) + 16 * blk + 4 * g4;
-              si[t] += sc0 * l + sc1 * hh;
-              mi[t] += mn0 * (b16[0] + b16[1]) + mn1 * (b16[2] + b16[3]);
-            }
-          }
-        }
-        const float dw = f16_bits_to_f32(lds_u16(bp)), dmin = f16_bits_to_f32(lds_u16(bp + 2));
-#pragma unroll
-        for (int t = 0; t < DTOK; ++t)
-          if (t < nc)
-            acc[t] = __fadd_rn(acc[t], __fmul_rn(ad[t * nbd + blk], __fsub_rn(__fmul_rn(dw, static_cast<float>(si[t])),
-                                                                              __fmul_rn(dmin, static_cast<float>(mi[t])))));
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < DTOK; ++t)
-      if (t < nc) a.hd[static_cast<size_t>(p0 + c0 + t) * E + r0 + tid] = acc[t];
+    const bool store = live && half == 0;
+    const size_t pos = static_cast<size_t>(p0 + s0);
+    int t = 0;   // passes of 8, then 4, 2, 1 tokens: the same sequence in every thread (the shuffles)
+    for (; t + 8 <= ns; t += 8) down_pass<DT, 8>(a, row, half, aq, ab, ad, t, pos + t, r0 + rr, store);
+    if (t + 4 <= ns) { down_pass<DT, 4>(a, row, half, aq, ab, ad, t, pos + t, r0 + rr, store); t += 4; }
+    if (t + 2 <= ns) { down_pass<DT, 2>(a, row, half, aq, ab, ad, t, pos + t, r0 + rr, store); t += 2; }
+    if (t < ns) down_pass<DT, 1>(a, row, half, aq, ab, ad, t, pos + t, r0 + rr, store);
   }
 }
 
@@ -612,8 +630,8 @@ int launch_experts(const BatchArgs &a, void *stream_) {
     const size_t dr_smem = align16(16 + down_rows_act_bytes(FF)) + align16(DR * a.drb + 32);
     if (dr_smem > 200 * 1024) return static_cast<int>(cudaErrorInvalidValue);
     const dim3 grid(NE, (E + DR - 1) / DR);
-    if (a.down_type == T_Q6_K) down_rows_kernel<T_Q6_K><<<grid, DR, dr_smem, st>>>(a);
-    else down_rows_kernel<T_Q4_K><<<grid, DR, dr_smem, st>>>(a);
+    if (a.down_type == T_Q6_K) down_rows_kernel<T_Q6_K><<<grid, DRT, dr_smem, st>>>(a);
+    else down_rows_kernel<T_Q4_K><<<grid, DRT, dr_smem, st>>>(a);
   } else {
     const size_t dn_smem = 16 + FF * 4 + align16(ROWS_PER_CTA * a.drb + 32) + 16;
     down_kernel<<<dim3(NE, (E + ROWS_PER_CTA - 1) / ROWS_PER_CTA), BT, dn_smem, st>>>(a);
