@@ -5,12 +5,11 @@
 // global memory behind one grid barrier counter (bounded waits; any CTA's error ends every CTA's wait). Per layer:
 //   A  attention input: x (global) -> rmsnorm -> Q8_K blocks (every CTA); this CTA's rows of the stacked [wq; wk; wv]
 //      from shared memory (exact integer block sums, the reference's float block terms in block order)       | barrier
-//   B1 attention scores, one item per (key/value head, 32 positions) over all CTAs: QK-norm and rotary embedding of the
-//      item's query heads (c/src/forward.c:905-915), in the block of the new position also of its key, which goes into
-//      the half-precision cache with the value (kv_put, :563-572); the reference's dotf_h per (head, position)  | barrier
-//   B2 softmax and weighted values in the reference's order: per (key/value head, 256-position chunk) when a group has
-//      2..16 query heads and the context is 64 positions or more (c/src/forward.c:665-737), else per query head over
-//      every position (:584-627); several chunks are merged afterwards (:719-737)                           | barrier(s)
+//   B  attention, one CTA per query head and no exchange between CTAs: QK-norm and rotary embedding of its query and of
+//      its key/value head's new key (c/src/forward.c:905-915), the new key and value into the half-precision cache
+//      (kv_put, :563-572, by the group's first head), the reference's dotf_h against every position, then the softmax
+//      and weighted values in the reference's order: per 256-position chunk, merged, when a group has 2..16 query heads
+//      and the context is 64 positions or more (c/src/forward.c:665-737), else over every position (:584-627) | barrier
 //   C  attention output: Q8_K of the attention vector (every CTA); this CTA's rows of wo; x += resid * wo att | barrier
 //   D  mixture of experts as the one-token MoE kernel (decode.cu) does it: rmsnorm, router (the reference's dotf),
 //      softmax, top-k, renormalisation, this CTA's share of every chosen expert's gate/up rows (bulk copies into shared
@@ -34,7 +33,6 @@ namespace {
 
 constexpr int NW = FWD_THREADS / 32;
 constexpr int RW = NW - 1;   // the router warp
-constexpr int SB = 32;       // positions per attention-score item
 
 CLB_DEV int ld_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
 
@@ -223,9 +221,6 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   uint8_t *slots = smem + a.off_slots;     // dense rows of the layer, then the chosen experts' gate/up rows; output stages
   uint8_t *dslots = smem + a.off_dslots;   // down rows of the chosen experts; the attention scratch
   const int GRP = a.n_head / a.n_kv;
-  float *qs_h = reinterpret_cast<float *>(dslots);                     // attention: [GROUP][hd] queries
-  float *sc = qs_h + GRP * hd;                                         // attention: scores / weights of an item
-  __half *kvs = reinterpret_cast<__half *>(dslots + a.off_kvstage);    // attention: staged key / value rows
 
   const uint32_t uG = static_cast<uint32_t>(G), uc = static_cast<uint32_t>(c);
   const int j0 = static_cast<int>(FF * uc / uG), j1 = static_cast<int>(FF * (uc + 1) / uG);
@@ -298,33 +293,42 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     if (!(ok = grid.sync())) break;
     trace_stamp(a.trace, 2);
 
-    // ---- B1: attention scores, one item per (key/value head, 32 positions) -------------------------------------------------
+    // ---- B: attention, one CTA per query head, no exchange between CTAs -----------------------------------------------------
+    // CTA c takes query head c (and c + G, ...): its query and its key/value head's new key and value (QK-norm, rotation,
+    // half rounding), the new pair stored by the group's first head; scores against every cached position and the new key
+    // (the reference's dotf_h: eight running sums, two threads per position); then, as the reference chooses
+    // (c/src/forward.c:740-757): plain: the maximum, e_t = expf(s_t - max), their sum in position order, the values added
+    // in position order with weight e_t / sum; grouped: per 256-position chunk its maximum m, e_t = expf(s_t - m), their
+    // sum l and the values added with weight e_t, in position order, then the chunks merged (c/src/forward.c:719-737).
     {
       const float *qg = a.qkv, *kg = a.qkv + nq, *vg = a.qkv + nq + nk;
-      float qscale = 1.f, kscale = 1.f;
-      if (a.qk_mode == 1) {   // QK-norm over the whole vector (olmoe): the scales of q and of k
-        double sq = 0.0, sk = 0.0;
-        for (int i = tid; i < nq; i += FWD_THREADS) { const double v = __ldcg(qg + i); sq += v * v; }
-        for (int i = tid; i < nk; i += FWD_THREADS) { const double v = __ldcg(kg + i); sk += v * v; }
+      float *qf = reinterpret_cast<float *>(dslots);                       // [hd] the query
+      __half *knew = reinterpret_cast<__half *>(qf + hd);                  // [hd] the new key, rounded to half
+      __half *vnew = knew + hd;                                            // [hd] the new value
+      __half *kvst = vnew + hd;                                            // [FWD_ATT_BLOCK][hd + 8] staged keys or values
+      float *scs = reinterpret_cast<float *>(kvst + FWD_ATT_BLOCK * (hd + 8));   // [a chunk] scores, then weights
+      float *part = scs + (grouped ? FWD_ATT_CHUNK : ((pos + 1 + 3) & ~3));     // per chunk: maximum, sum, [hd] value sums
+      float *s_wmax = s_wt;                                                // [NW] (s_wt is written in the MoE phase)
+      for (int h = c; h < a.n_head; h += G) {
+        const int g = h / GRP, j = h - g * GRP;
+        float qscale = 1.f, kscale = 1.f;
+        __syncthreads();   // the scratch of the previous head
+        if (a.qk_mode == 1) {   // QK-norm over the whole query and the whole key (olmoe): their scales
+          double sq = 0.0, sk = 0.0;
+          for (int i = tid; i < nq; i += FWD_THREADS) { const double v = __ldcg(qg + i); sq += v * v; }
+          for (int i = tid; i < nk; i += FWD_THREADS) { const double v = __ldcg(kg + i); sk += v * v; }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) { sq += __shfl_xor_sync(FULL, sq, o); sk += __shfl_xor_sync(FULL, sk, o); }
-        __syncthreads();
-        if (lane == 0) { s_red[warp] = sq; reinterpret_cast<double *>(terms)[warp] = sk; }
-        __syncthreads();
-        double tq = 0.0, tk = 0.0;
-        for (int k = 0; k < NW; ++k) { tq += s_red[k]; tk += reinterpret_cast<double *>(terms)[k]; }
-        qscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tq / nq), a.eps)));
-        kscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tk / nk), a.eps)));
-      }
-      const int nsb = (pos + 1 + SB - 1) / SB;
-      for (int item = c; item < a.n_kv * nsb; item += G) {
-        const int g = item / nsb, t0 = (item - g * nsb) * SB, n = min(SB, pos + 1 - t0);
-        const bool has_pos = t0 + n == pos + 1;
-        __syncthreads();   // the scratch of the previous item
-        // the group's query heads (warps 0..GRP-1) and, in the block of the new position, the key head (warp GRP)
-        for (int h = warp; h < GRP + (has_pos ? 1 : 0); h += NW) {
-          const bool isk = h == GRP;
-          const float *src = isk ? kg + g * hd : qg + (g * GRP + h) * hd;
+          for (int o = 16; o > 0; o >>= 1) { sq += __shfl_xor_sync(FULL, sq, o); sk += __shfl_xor_sync(FULL, sk, o); }
+          if (lane == 0) { s_red[warp] = sq; reinterpret_cast<double *>(terms)[warp] = sk; }
+          __syncthreads();
+          double tq = 0.0, tk = 0.0;
+          for (int k = 0; k < NW; ++k) { tq += s_red[k]; tk += reinterpret_cast<double *>(terms)[k]; }
+          qscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tq / nq), a.eps)));
+          kscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(tk / nk), a.eps)));
+        }
+        if (warp < 2) {   // warp 0: the query head; warp 1: the key head (and the value)
+          const bool isk = warp == 1;
+          const float *src = isk ? kg + g * hd : qg + h * hd;
           float v[EPL];
 #pragma unroll
           for (int e = 0; e < EPL; ++e) v[e] = __ldcg(src + lane + 32 * e);
@@ -340,7 +344,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
             for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), __ldg(w + lane + 32 * e));
           } else if (a.qk_mode == 1) {
             const float s1 = isk ? kscale : qscale;
-            const float *w = isk ? Ly.kn + g * hd : Ly.qn + (g * GRP + h) * hd;
+            const float *w = isk ? Ly.kn + g * hd : Ly.qn + h * hd;
 #pragma unroll
             for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), __ldg(w + lane + 32 * e));
           }
@@ -350,164 +354,123 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
             __half *vd = a.vc + cache_l + static_cast<size_t>(pos) * nk + g * hd;
 #pragma unroll
             for (int e = 0; e < EPL; ++e) {
-              kd[lane + 32 * e] = __float2half_rn(v[e]);
-              vd[lane + 32 * e] = __float2half_rn(__ldcg(vg + g * hd + lane + 32 * e));
+              const __half kh = __float2half_rn(v[e]), vh = __float2half_rn(__ldcg(vg + g * hd + lane + 32 * e));
+              knew[lane + 32 * e] = kh;
+              vnew[lane + 32 * e] = vh;
+              if (j == 0) { kd[lane + 32 * e] = kh; vd[lane + 32 * e] = vh; }   // kv_put (c/src/forward.c:563-565)
             }
           } else {
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) qs_h[h * hd + lane + 32 * e] = v[e];
+            for (int e = 0; e < EPL; ++e) qf[lane + 32 * e] = v[e];
           }
         }
         __syncthreads();
-        // the block's keys into shared memory, all loads in flight at once
-        const __half *kb = a.kc + cache_l + g * hd;
-        for (int i = tid; i < n * (hd / 8); i += FWD_THREADS) {
-          const int t = i / (hd / 8), q = i - t * (hd / 8);
-          reinterpret_cast<uint4 *>(kvs)[i] = __ldcg(reinterpret_cast<const uint4 *>(kb + static_cast<size_t>(t0 + t) * nk) + q);
-        }
-        __syncthreads();
-        trace_stamp(a.trace, 15);
-        // the reference's dotf_h (c/src/forward.c:492-510): eight running sums over the head, combined
-        // ((0+1)+(2+3))+((4+5)+(6+7)), times the attention scale; two threads per (head, position), sums 0-3 and 4-7
-        const int half = tid & 1;
-        for (int p = tid >> 1; p < GRP * SB; p += FWD_THREADS / 2) {
-          const int j = p / SB, tt = p - j * SB;
-          const bool valid = tt < n;
-          float s4[4] = {0.f, 0.f, 0.f, 0.f};
-          if (valid) {
-            const __half *kr = kvs + tt * hd + 4 * half;
-            const float *q = qs_h + j * hd + 4 * half;
+        // keys and values pass through shared memory FWD_ATT_BLOCK positions at a time, rows padded by 16 bytes so that
+        // consecutive positions (the scores) or consecutive dimensions (the values) fall in different banks
+        const __half *kb = a.kc + cache_l + g * hd, *vb = a.vc + cache_l + g * hd;
+        const int KS = hd + 8, n = pos + 1;
+        auto stage = [&](const __half *base, const __half *fresh, int b0, int cnt) {
+          __syncthreads();   // the previous block is consumed
+          for (int i = tid; i < cnt * (hd / 8); i += FWD_THREADS) {
+            const int t = i / (hd / 8), q = i - t * (hd / 8);
+            const uint4 v = b0 + t == pos ? reinterpret_cast<const uint4 *>(fresh)[q]
+                                          : __ldcg(reinterpret_cast<const uint4 *>(base + static_cast<size_t>(b0 + t) * nk) + q);
+            *reinterpret_cast<uint4 *>(kvst + t * KS + 8 * q) = v;
+          }
+          __syncthreads();
+        };
+        // chunk by chunk (grouped: 256 positions; plain: one chunk of every position): scores, one thread per position, the
+        // reference's eight running sums combined ((0+1)+(2+3))+((4+5)+(6+7)); the chunk's maximum, e_t, their sum in
+        // position order (plain: then e_t / sum); the values in position order, one chain per dimension (thread d)
+        const int nchk = grouped ? nchunk : 1, clen = grouped ? FWD_ATT_CHUNK : n;
+        for (int ch = 0; ch < nchk; ++ch) {
+          const int t0 = ch * clen, t1 = min(n, t0 + clen), m = t1 - t0;
+          for (int b0 = t0; b0 < t1; b0 += FWD_ATT_BLOCK) {
+            const int cnt = min(FWD_ATT_BLOCK, t1 - b0);
+            stage(kb, knew, b0, cnt);
+            if (tid < cnt) {
+              const __half *kr = kvst + tid * KS;
+              float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int i = 0; i < hd; i += 8) {
-              const uint2 kk = *reinterpret_cast<const uint2 *>(kr + i);
-              const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.x));
-              const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kk.y));
-              const float4 qq = *reinterpret_cast<const float4 *>(q + i);
-              s4[0] = __fadd_rn(s4[0], __fmul_rn(qq.x, k01.x));
-              s4[1] = __fadd_rn(s4[1], __fmul_rn(qq.y, k01.y));
-              s4[2] = __fadd_rn(s4[2], __fmul_rn(qq.z, k23.x));
-              s4[3] = __fadd_rn(s4[3], __fmul_rn(qq.w, k23.y));
+              for (int i = 0; i < hd; i += 8) {
+                const uint4 kk = *reinterpret_cast<const uint4 *>(kr + i);
+                const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
+                const float4 q0 = *reinterpret_cast<const float4 *>(qf + i), q1 = *reinterpret_cast<const float4 *>(qf + i + 4);
+                const float2 k01 = __half22float2(k2[0]), k23 = __half22float2(k2[1]), k45 = __half22float2(k2[2]), k67 = __half22float2(k2[3]);
+                s8[0] = __fadd_rn(s8[0], __fmul_rn(q0.x, k01.x));
+                s8[1] = __fadd_rn(s8[1], __fmul_rn(q0.y, k01.y));
+                s8[2] = __fadd_rn(s8[2], __fmul_rn(q0.z, k23.x));
+                s8[3] = __fadd_rn(s8[3], __fmul_rn(q0.w, k23.y));
+                s8[4] = __fadd_rn(s8[4], __fmul_rn(q1.x, k45.x));
+                s8[5] = __fadd_rn(s8[5], __fmul_rn(q1.y, k45.y));
+                s8[6] = __fadd_rn(s8[6], __fmul_rn(q1.z, k67.x));
+                s8[7] = __fadd_rn(s8[7], __fmul_rn(q1.w, k67.y));
+              }
+              const float d = __fadd_rn(__fadd_rn(__fadd_rn(s8[0], s8[1]), __fadd_rn(s8[2], s8[3])),
+                                        __fadd_rn(__fadd_rn(s8[4], s8[5]), __fadd_rn(s8[6], s8[7])));
+              scs[b0 - t0 + tid] = __fmul_rn(d, a.attn_scale);
             }
           }
-          const float part = __fadd_rn(__fadd_rn(s4[0], s4[1]), __fadd_rn(s4[2], s4[3]));
-          const float other = __shfl_xor_sync(FULL, part, 1);
-          if (valid && half == 0) __stcg(a.scores + static_cast<size_t>(g * GRP + j) * a.ctx + t0 + tt, __fmul_rn(__fadd_rn(part, other), a.attn_scale));
-        }
-      }
-    }
-    trace_stamp(a.trace, 3);
-    if (!(ok = grid.sync())) break;
-
-    // ---- B2: softmax and weighted values in the reference's order --------------------------------------------------------
-    // grouped: an item per (key/value head, chunk of 256 positions, quarter of the head dimension): per query head the
-    // chunk's maximum m, e_t = expf(s_t - m), their sum l in position order, o = sum_t e_t v_t in position order; one chunk
-    // gives o * (1 / l) directly, more are merged below. plain: an item per (query head, quarter of the head dimension)
-    // over every position: the maximum, e_t, their sum in order, then o = sum_t (e_t / sum) v_t in order. Every value sum
-    // is one thread's chain over the positions; the quarters spread an item's chains over four CTAs.
-    {
-      constexpr int DQ = 4, HQ = hd / DQ;   // quarters of the head dimension, and their width
-      const int items = (grouped ? a.n_kv * nchunk : a.n_head) * DQ;
-      float *hm = probs;   // [16] maxima, [16] sums
-      for (int item = c; item < items; item += G) {
-        const int it = item / DQ, dq = item - it * DQ;
-        const int g = grouped ? it / nchunk : it / GRP;
-        const int ch = grouped ? it - g * nchunk : 0;
-        const int jb = grouped ? 0 : it - g * GRP, NH = grouped ? GRP : 1;
-        const int t0 = ch * FWD_ATT_CHUNK, n = grouped ? min(FWD_ATT_CHUNK, pos + 1 - t0) : pos + 1;
-        __syncthreads();
-        // the quarter of the values of (up to FWD_ATT_CHUNK) positions into shared memory, loads in flight while the
-        // weights form
-        const __half *vb = a.vc + cache_l + g * hd + dq * HQ;
-        auto stage_values = [&](int b0, int cnt) {
-          for (int i = tid; i < cnt * (HQ / 8); i += FWD_THREADS) {
-            const int t = i / (HQ / 8), q = i - t * (HQ / 8);
-            reinterpret_cast<uint4 *>(kvs)[i] = __ldcg(reinterpret_cast<const uint4 *>(vb + static_cast<size_t>(t0 + b0 + t) * nk) + q);
-          }
-        };
-        stage_values(0, min(n, FWD_ATT_CHUNK));
-        for (int i = tid; i < NH * n; i += FWD_THREADS) {
-          const int jj = i / n, t = i - jj * n;
-          sc[i] = __ldcg(a.scores + static_cast<size_t>(g * GRP + jb + jj) * a.ctx + t0 + t);
-        }
-        __syncthreads();
-        for (int jj = warp; jj < NH; jj += NW) {   // a warp per head: the maximum
-          float mx = -INFINITY;
-          for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sc[jj * n + t]);
+          __syncthreads();
+          trace_stamp(a.trace, 15);
+          float mx = -INFINITY;   // the chunk's maximum: every thread's share, each warp's, then the warps'
+          for (int t = tid; t < m; t += FWD_THREADS) mx = fmaxf(mx, scs[t]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-          if (lane == 0) hm[jj] = mx;
-        }
-        __syncthreads();
-        for (int i = tid; i < NH * n; i += FWD_THREADS) sc[i] = exp_cr(__fsub_rn(sc[i], hm[i / n]));   // e_t, every thread
-        __syncthreads();
-        trace_stamp(a.trace, 16);
-        // thread (jj, i): the chain of head jj, dimension dq * HQ + i; threads jj < NH also form head jj's sum l
-        const int jj = tid / HQ, i = tid - jj * HQ;
-        const bool chain = jj < NH;
-        float o = 0.f, l = 0.f;
-        if (!grouped) {   // plain: the sum first, then p_t = e_t / sum
-          if (tid == 0) {
-            for (int t = 0; t < n; ++t) l = __fadd_rn(l, sc[t]);
-            hm[16] = l;
+          if (lane == 0) s_wmax[warp] = mx;
+          __syncthreads();
+          mx = s_wmax[0];
+          for (int w = 1; w < NW; ++w) mx = fmaxf(mx, s_wmax[w]);
+          for (int t = tid; t < m; t += FWD_THREADS) scs[t] = exp_cr(__fsub_rn(scs[t], mx));
+          __syncthreads();
+          if (tid == 0) {   // the sum in position order
+            float l = 0.f;
+            for (int t = 0; t < m; ++t) l = __fadd_rn(l, scs[t]);
+            part[ch * (2 + hd)] = mx;
+            part[ch * (2 + hd) + 1] = l;
           }
+          trace_stamp(a.trace, 16);
+          if (!grouped) {   // plain: p_t = e_t / sum
+            __syncthreads();
+            const float sum = part[1];
+            for (int t = tid; t < m; t += FWD_THREADS) scs[t] = __fdiv_rn(scs[t], sum);
+          }
+          float o = 0.f;
+          for (int b0 = t0; b0 < t1; b0 += FWD_ATT_BLOCK) {
+            const int cnt = min(FWD_ATT_BLOCK, t1 - b0);
+            stage(vb, vnew, b0, cnt);
+            if (tid < hd)
+              for (int t = 0; t < cnt; ++t) o = __fadd_rn(o, __fmul_rn(scs[b0 - t0 + t], __half2float(kvst[t * KS + tid])));
+          }
+          if (tid < hd) {
+            if (!grouped) __stcg(a.att + h * hd + tid, o);
+            else part[ch * (2 + hd) + 2 + tid] = o;
+          }
+          __syncthreads();   // scs and the staging buffer are reused by the next chunk
+        }
+        if (grouped) {
           __syncthreads();
-          for (int t = tid; t < n; t += FWD_THREADS) sc[t] = __fdiv_rn(sc[t], hm[16]);
-          __syncthreads();
-          for (int b0 = 0; b0 < n; b0 += FWD_ATT_CHUNK) {   // one head may span many chunks' worth of positions
-            const int cnt = min(FWD_ATT_CHUNK, n - b0);
-            if (b0 > 0) {
-              __syncthreads();
-              stage_values(b0, cnt);
-              __syncthreads();
+          for (int d = tid; d < hd; d += FWD_THREADS) {
+            if (nchk == 1) {   // the merge of one chunk: weight expf(0) = 1, so o * (1 / l)
+              __stcg(a.att + h * hd + d, __fmul_rn(part[2 + d], __fdiv_rn(1.0f, part[1])));
+            } else {
+              float M = -INFINITY;
+              for (int ch = 0; ch < nchk; ++ch) M = fmaxf(M, part[ch * (2 + hd)]);
+              float L = 0.f, o = 0.f;
+              for (int ch = 0; ch < nchk; ++ch) {
+                const float *pp = part + ch * (2 + hd);
+                const float w = exp_cr(__fsub_rn(pp[0], M));
+                L = __fadd_rn(L, __fmul_rn(w, pp[1]));
+                o = __fadd_rn(o, __fmul_rn(w, pp[2 + d]));
+              }
+              __stcg(a.att + h * hd + d, __fmul_rn(o, __fdiv_rn(1.0f, L)));
             }
-            if (chain)
-              for (int t = 0; t < cnt; ++t) o = __fadd_rn(o, __fmul_rn(sc[b0 + t], __half2float(kvs[t * HQ + i])));
           }
-        } else if (chain) {   // n <= FWD_ATT_CHUNK: every value is staged
-          const float *w = sc + jj * n;
-          const bool sums = tid < NH;   // also the sum of head tid
-          const float *ws = sc + tid * n;
-          for (int t = 0; t < n; ++t) {
-            o = __fadd_rn(o, __fmul_rn(w[t], __half2float(kvs[t * HQ + i])));
-            if (sums) l = __fadd_rn(l, ws[t]);
-          }
-          if (sums) hm[16 + tid] = l;
         }
-        __syncthreads();
         trace_stamp(a.trace, 17);
-        if (chain) {
-          const int h = g * GRP + jb + jj, d = dq * HQ + i;
-          if (!grouped) {
-            __stcg(a.att + h * hd + d, o);
-          } else if (nchunk == 1) {   // the merge of one chunk: weight expf(0) = 1, so o * (1 / l)
-            __stcg(a.att + h * hd + d, __fmul_rn(o, __fdiv_rn(1.0f, hm[16 + jj])));
-          } else {
-            float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + jj) * (2 + hd);
-            if (dq == 0 && i == 0) { __stcg(pp, hm[jj]); __stcg(pp + 1, hm[16 + jj]); }
-            __stcg(pp + 2 + d, o);
-          }
-        }
       }
     }
     if (!(ok = grid.sync())) break;
-    if (grouped && nchunk > 1) {   // merge the chunks of each query head (c/src/forward.c:719-737)
-      for (int h = c; h < a.n_head; h += G) {
-        const int g = h / GRP, j = h - g * GRP;
-        for (int d = tid; d < hd; d += FWD_THREADS) {
-          float M = -INFINITY;
-          for (int ch = 0; ch < nchunk; ++ch) M = fmaxf(M, __ldcg(a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + j) * (2 + hd)));
-          float L = 0.f, o = 0.f;
-          for (int ch = 0; ch < nchunk; ++ch) {
-            const float *pp = a.part + (static_cast<size_t>(g * nchunk + ch) * GRP + j) * (2 + hd);
-            const float w = exp_cr(__fsub_rn(__ldcg(pp), M));
-            L = __fadd_rn(L, __fmul_rn(w, __ldcg(pp + 1)));
-            o = __fadd_rn(o, __fmul_rn(w, __ldcg(pp + 2 + d)));
-          }
-          __stcg(a.att + h * hd + d, __fmul_rn(o, __fdiv_rn(1.0f, L)));
-        }
-      }
-      if (!(ok = grid.sync())) break;
-    }
     trace_stamp(a.trace, 4);
 
     // ---- C: attention output: x += resid * wo att, this CTA's rows ------------------------------------------------------

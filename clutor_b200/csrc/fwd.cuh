@@ -10,7 +10,8 @@ namespace clb {
 constexpr int FWD_THREADS = 512;
 constexpr int FWD_MAX_K = 16;       // experts used per token (one warp issues each expert's copies)
 constexpr int FWD_MAX_NE = 128;     // experts per layer the kernel ranks (four threads per expert)
-constexpr int FWD_ATT_CHUNK = 256;  // positions per attention work item
+constexpr int FWD_ATT_CHUNK = 256;  // positions per attention chunk (the reference's ATT_CHUNK)
+constexpr int FWD_ATT_BLOCK = 128;  // positions of keys or values staged in shared memory at once
 constexpr int FWD_MAX_GROUP = 16;   // query heads per key/value head
 constexpr int HEAD_ROWS = 24;       // output-matrix rows per shared-memory stage
 constexpr int HEAD_STAGES = 4;      // stages in flight (they span the slots and the dslots); two are computed at a time
@@ -59,8 +60,6 @@ struct FwdArgs {
   float *x;          // [E] the residual stream
   float *qkv;        // [n_q + 2 n_kvw]
   float *att;        // [n_q]
-  float *scores;     // attention scores [n_head][ctx] of the step
-  float *part;       // attention partials [n_kv][nchunk][GROUP][2 + hd]
   float *rlogits;    // [NE] router logits
   float *hg;         // [K * FF]
   float *logits;     // [vocab]
@@ -71,7 +70,6 @@ struct FwdArgs {
   // per-CTA shared-memory plan (host-computed)
   uint32_t grb, drb, gseg, slot_bytes, dslot_bytes;
   uint32_t off_bars, off_xn, off_xq, off_misc, off_router, off_rprod, off_terms, off_hq, off_xr, off_slots, off_dslots, smem_bytes;
-  uint32_t off_kvstage;        // staged key / value rows of the attention, from off_dslots
   const float *rope_cs;        // [ctx][hd]: per position hd / 2 cosines then hd / 2 sines of the rotary angles, as the
                                // reference computes them (c/src/forward.c:428-435)
   int rgu_max, rd_max, nre_max;

@@ -200,12 +200,9 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   }
   // key/value cache and scratch
   const size_t kv_elems = static_cast<size_t>(a.n_layer) * a.ctx * a.n_kvw;
-  const int GRP = a.n_head / a.n_kv, maxchunk = (a.ctx + FWD_ATT_CHUNK - 1) / FWD_ATT_CHUNK;
   auto take = [&](size_t bytes) { total = al(total, 256); const size_t at = total; total += bytes + 64; return at; };
   const size_t o_kc = take(kv_elems * 2), o_vc = take(kv_elems * 2);
   const size_t o_x = take(a.E * 4), o_qkv = take((a.n_q + 2 * a.n_kvw) * 4), o_att = take(a.n_q * 4);
-  const size_t o_part = take(static_cast<size_t>(a.n_kv) * maxchunk * GRP * (2 + hd) * 4);
-  const size_t o_scores = take(static_cast<size_t>(a.n_head) * a.ctx * 4);
   const size_t o_rl = take(a.NE * 4), o_hg = take(static_cast<size_t>(a.K) * a.FF * 4), o_lg = take(static_cast<size_t>(a.vocab) * 4);
   const size_t o_rs = take(static_cast<size_t>(a.n_layer) * a.K * 4), o_rw = take(static_cast<size_t>(a.n_layer) * a.K * 4);
   const size_t o_gen = take(static_cast<size_t>(a.ctx) * 4), o_layers = take(sizeof(FwdLayer) * a.n_layer), o_st = take(sizeof(FwdState));
@@ -240,7 +237,6 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   a.off_terms = st_take(std::max<size_t>(static_cast<size_t>(a.rd_max) * a.K * nbd * 4, 2 * NW * 8));
   a.off_hq = st_take(static_cast<size_t>(a.K) * a.FF + 2 * (static_cast<size_t>(a.K) * a.FF / 16) + 4 * (static_cast<size_t>(a.K) * a.FF / 256));
   a.off_xr = st_take(static_cast<size_t>(a.rd_max) * 4);
-  constexpr int SB_KEYS = 32;   // fwd.cu's positions of keys staged per score item
   // the slots hold a layer's dense rows (each CTA's rows of wq, wk, wv, wo, one segment after another: fwd.cu's
   // dense_offset) and then the chosen experts' gate/up rows
   size_t dense_need = 0;
@@ -262,12 +258,15 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   }
   const size_t slots_size = al(std::max<size_t>(static_cast<size_t>(a.K) * a.slot_bytes, dense_need), 128);
   a.off_slots = st_take(slots_size, 128);
-  // the dslots, right after the slots, hold the chosen experts' down rows, or the attention scratch: queries / value sums
-  // [GROUP][hd], one item's scores (a 256-position chunk of every head of a group, or for a group of one head the whole
-  // context of that head), and the staged key / value rows (64 positions); the output matrix's stages span both regions
-  const size_t att_scores = static_cast<size_t>(GRP) * hd * 4 + std::max<size_t>(static_cast<size_t>(GRP) * FWD_ATT_CHUNK, GRP < 2 ? a.ctx : 64) * 4;
-  a.off_kvstage = static_cast<uint32_t>(al(att_scores, 16));
-  const size_t att_need = a.off_kvstage + static_cast<size_t>(std::max(SB_KEYS * hd, FWD_ATT_CHUNK * (hd / 4))) * 2;
+  // the dslots, right after the slots, hold the chosen experts' down rows, or the attention scratch of a query head: its
+  // query [hd] floats, the new key and value [hd] halves each, FWD_ATT_BLOCK staged key or value rows, the scores of every
+  // position, and per 256-position chunk its maximum, sum and [hd] value sums; the output matrix's stages span both regions
+  const int grp = a.n_head / a.n_kv;
+  const bool can_group = grp >= 2 && grp <= FWD_MAX_GROUP;   // else every step takes the plain path over the whole context
+  const size_t att_chunks = can_group ? (static_cast<size_t>(a.ctx) + FWD_ATT_CHUNK - 1) / FWD_ATT_CHUNK : 1;
+  const size_t att_scores = can_group ? FWD_ATT_CHUNK : (static_cast<size_t>(a.ctx) + 3) & ~size_t(3);
+  const size_t att_need = static_cast<size_t>(hd) * 8 + static_cast<size_t>(FWD_ATT_BLOCK) * (hd + 8) * 2 + att_scores * 4 +
+                          att_chunks * (2 + hd) * 4;
   const size_t head_need = static_cast<size_t>(HEAD_STAGES) * al(HEAD_ROWS * row_bytes(out->type, a.E) + 32, 16);
   const size_t dslots_size = std::max<size_t>(std::max<size_t>(static_cast<size_t>(a.K) * a.dslot_bytes, att_need),
                                               head_need > slots_size ? head_need - slots_size : 0);
@@ -340,8 +339,6 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   a.x = reinterpret_cast<float *>(m->dev + o_x);
   a.qkv = reinterpret_cast<float *>(m->dev + o_qkv);
   a.att = reinterpret_cast<float *>(m->dev + o_att);
-  a.part = reinterpret_cast<float *>(m->dev + o_part);
-  a.scores = reinterpret_cast<float *>(m->dev + o_scores);
   {   // the rotary angles' cosines and sines exactly as the reference computes them (c/src/forward.c:420-435): the same
       // float expression and the same C library's powf, cosf and sinf, for every position of the context
     const int H = hd / 2;
