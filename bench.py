@@ -198,7 +198,7 @@ def model_reference(image, n_ctx: int, seconds: float, threads: int | None = Non
                       f"/dev/shm", "ms_per_token": 1000 * dt / max(n, 1)}
 
 
-PROMPT_METRIC = "prompt tokens/s (Qwen3-30B-A3B, Q4_K_M mix, 512-token prompt, batches of 64)"
+PROMPT_METRIC = "prompt tokens/s (Qwen3-30B-A3B, Q4_K_M mix, 512-token prompt)"
 
 
 def prompt_reference(image, P: int, threads: int | None = None) -> dict:
@@ -245,7 +245,7 @@ def run_prompt(a, wl: dict) -> None:
         spec = dataclasses.replace(spec, n_layer=a.layers)
     image = sm.image(spec, seed=1)
     ctx = cb.Context(0)
-    P, B = wl["P"], wl["T"]
+    P, B = wl["P"], (a.batch or wl["T"])
     model = Model(ctx, image, P + 16)
     model.set_batch(B)
     prompt = np.random.default_rng(3).integers(0, spec.vocab, P).astype(np.int32)
@@ -670,6 +670,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--smart", default=None, help="cache workload: SMART-ROUTE J,M,TAU (for example 2,12,0.015)")
+    ap.add_argument("--batch", type=int, default=None, help="prompt workload: tokens per batch (the reference's CLUTOR_PS_B, 1..512)")
     a = ap.parse_args()
     wl = dict(WORKLOADS[a.workload])
     if a.layers:
