@@ -108,6 +108,10 @@ int launch_experts(const BatchArgs &a, void *stream);
 // The Q8_0 / Q4_K expert products on tcgen05 (grouped_tc.cu): gate/up (writes hg, and hgh/hgl for Q8_0 down) or down
 // (writes hd).
 int launch_tc(const BatchArgs &a, void *stream, bool gateup);
+// A dense Q4_K matrix times nb tokens' plain Q8_K rows on the tensor cores (grouped_tc.cu): out [nb][rows]; co holds the
+// device ints {nb, 0, nb}; ph / pl [nb][cols] halves and rs [nb] are scratch. Returns a CUDA error code.
+int launch_tc_dense(const uint8_t *w, uint32_t rb, int rows, int cols, int nb, const int8_t *qs, const float *dd, int *co,
+                    __half *ph, __half *pl, float *rs, float *out, int *err, cudaStream_t st);
 // Whether the tensor-core path takes experts of this type at w (Q8_0 or Q4_K, 16-byte aligned, E and FF multiples of 256).
 bool tc_type_supported(uint32_t type, const void *w, int E, int FF);
 

@@ -63,7 +63,7 @@ struct TcShape {
   static constexpr int N_BARS = 2 * RAW_STAGES + 2 * B_STAGES + 2 * A_STAGES + 3;
   static constexpr uint32_t SMEM = RAW_STAGES * RAW_STAGE + B_STAGES * B_STAGE + 8 * N_BARS + 16 + 1024;
   static_assert(A_STAGES >= 2, "TMEM budget");
-  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(SMEM + (3 * 1024 + 1) * 4 <= 232448, "shared memory budget (with the work list)");
   static_assert(CHUNK % 16 == 0, "TMA boxes are 16-byte multiples");
 };
 
@@ -149,17 +149,32 @@ CLB_DEV void dequant_q4k(const uint32_t (&w)[36], int j, uint32_t (&hi)[16], uin
   }
 }
 
-// Calls f(e, m, pos0, nt) for this CTA's tiles: expert e, row tile m, tokens at dispatch positions [pos0, pos0 + nt).
+// The CTA's work items: (expert e, row tile m, token chunk) for every expert with tokens, numbered expert by expert, row tile
+// by row tile, the chunks of a tile consecutive (so CTAs running side by side share a weight tile in L2); item w goes to CTA
+// w mod gridDim. pre[e] = the items of experts before e (pre[NE] = all), cnt / off = each expert's tokens and first dispatch
+// position (experts with an out-of-range dispatch range have none), all in shared memory.
+constexpr int TC_MAX_NE = 1024;
+struct TileList {
+  const int *pre, *cnt, *off;
+  int NE;
+};
+
+// Calls f(e, m, pos0, nt) for this CTA's items: expert e, row tile m, tokens at dispatch positions [pos0, pos0 + nt).
 // Every role of the CTA walks the same sequence. Stops (false) as soon as f fails.
 template <int NT, class F>
-CLB_DEV bool for_each_tile(const BatchArgs &a, int MT, F &&f) {
-  const int TK = a.T * a.K;
-  for (int w = blockIdx.x; w < a.NE * MT; w += gridDim.x) {
-    const int e = w / MT, m = w - e * MT;
-    const int n_e = a.counts[e], p0 = a.offsets[e];
-    if (n_e <= 0 || p0 < 0 || p0 + n_e > TK) continue;
-    for (int n0 = 0; n0 < n_e; n0 += NT)
-      if (!f(e, m, p0 + n0, min(NT, n_e - n0))) return false;
+CLB_DEV bool for_each_tile(const TileList &L, int MT, F &&f) {
+  const int total = L.pre[L.NE];
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    int lo = 0, hi = L.NE - 1;   // the last expert whose items start at or before w (it has items: pre[e + 1] > w)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (L.pre[mid] <= w) lo = mid;
+      else hi = mid - 1;
+    }
+    const int e = lo, n_e = L.cnt[e], nch = (n_e + NT - 1) / NT, local = w - L.pre[e];
+    const int m = local / nch, n0 = (local - m * nch) * NT;
+    if (m >= MT || n0 >= n_e) continue;   // cannot happen for a consistent list
+    if (!f(e, m, L.off[e] + n0, min(NT, n_e - n0))) return false;
   }
   return true;
 }
@@ -191,6 +206,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int nchunk = (GATEUP ? a.E : a.FF) / 256;
   const int rows_e = GATEUP ? a.FF : a.E;       // weight rows per expert
 
+  __shared__ int s_pre[TC_MAX_NE + 1], s_cnt[TC_MAX_NE], s_off[TC_MAX_NE];
+  {   // the work list: each expert's tokens (none for an out-of-range dispatch range), then the prefix of its items
+    const int TK = a.T * a.K;
+    for (int e = threadIdx.x; e < a.NE; e += blockDim.x) {
+      const int n_e = a.counts[e], p0 = a.offsets[e];
+      const bool good = n_e > 0 && p0 >= 0 && p0 + n_e <= TK;
+      s_cnt[e] = good ? n_e : 0;
+      s_off[e] = good ? p0 : 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      for (int e = 0; e < a.NE; ++e) {
+        s_pre[e] = acc;
+        acc += MT * ((s_cnt[e] + NT - 1) / NT);
+      }
+      s_pre[a.NE] = acc;
+    }
+  }
+  const TileList tl{s_pre, s_cnt, s_off, a.NE};
   if (threadIdx.x == 0) {
     for (int i = 0; i < RAW_STAGES; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_free[i], 4); }
     for (int i = 0; i < B_STAGES; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_free[i], 2); }
@@ -210,7 +245,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == W_RAW) {
     if (lane == 0) {
       uint32_t u = 0;   // half-stages issued: (chunk, matrix) in order
-      ok = for_each_tile<NT>(a, MT, [&](int e, int m, int, int) {
+      ok = for_each_tile<NT>(tl, MT, [&](int e, int m, int, int) {
         for (int c = 0; c < nchunk; ++c) {
           for (int mA = 0; mA < 2; ++mA, ++u) {
             const uint32_t s = u % RAW_STAGES;
@@ -229,7 +264,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == W_ACT) {
     if (lane == 0) {
       uint32_t t = 0;   // atoms issued
-      ok = for_each_tile<NT>(a, MT, [&](int, int, int pos0, int nt) {
+      ok = for_each_tile<NT>(tl, MT, [&](int, int, int pos0, int nt) {
         const int NTt = (nt + 15) & ~15;
         for (int c = 0; c < nchunk; ++c) {
           for (int at = 0; at < 4; ++at, ++t) {
@@ -253,7 +288,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int mA = warp == W_MMA0 ? 0 : 1;
       const uint32_t acc = tmem + 2 * NT * mA;
       uint32_t t = 0, it = 0;
-      ok = for_each_tile<NT>(a, MT, [&](int, int, int, int nt) {
+      ok = for_each_tile<NT>(tl, MT, [&](int, int, int, int nt) {
         const uint32_t idesc = tc::idesc_f16_f32(128, 2 * ((nt + 15) & ~15));
         if (it > 0 && !mbar_wait_bounded(acc_free, (it - 1) & 1)) return false;
         tc::fence_after_sync();
@@ -285,7 +320,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int mA = warp >> 2, q = warp & 3, r = 32 * q + lane;
     const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
     uint32_t g = 0, t = 0, it = 0;   // chunks, atoms, tiles consumed
-    ok = for_each_tile<NT>(a, MT, [&](int, int m, int pos0, int nt) {
+    ok = for_each_tile<NT>(tl, MT, [&](int, int m, int pos0, int nt) {
       for (int c = 0; c < nchunk; ++c, ++g) {
         const uint32_t u = 2 * g + mA, s = u % RAW_STAGES;
         if (!mbar_wait_bounded(&raw_full[s], (u / RAW_STAGES) & 1)) return false;
@@ -478,14 +513,16 @@ static int launch_kernel(const BatchArgs &a, cudaStream_t st, const CUtensorMap 
     cudaFuncSetAttribute(group_tc_kernel<GATEUP, WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcShape<WT>::SMEM);
     cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   }
-  const int tiles = a.NE * (GATEUP ? a.FF / 128 : a.E / 256);
-  const int grid = tiles < sms[dev] ? tiles : sms[dev];
+  const long chunks = (static_cast<long>(a.T) * a.K + TcShape<WT>::NT - 1) / TcShape<WT>::NT;   // an expert's at most
+  const long items = static_cast<long>(a.NE) * (GATEUP ? a.FF / 128 : a.E / 256) * chunks;
+  const int grid = items < sms[dev] ? static_cast<int>(items) : sms[dev];
   group_tc_kernel<GATEUP, WT><<<grid, TC_THREADS, TcShape<WT>::SMEM, st>>>(a, tw0, tw1, tbh, tbl);
   return static_cast<int>(cudaGetLastError());
 }
 
 int launch_tc(const BatchArgs &a, void *stream_, bool gateup) {
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (a.NE > TC_MAX_NE || a.NE < 1) return static_cast<int>(cudaErrorInvalidValue);
   const int TK = a.T * a.K;
   const uint32_t wt = gateup ? a.gate_type : a.down_type;
   const uint32_t chunk = wt == T_Q8_0 ? TcShape<T_Q8_0>::CHUNK : TcShape<T_Q4_K>::CHUNK;
@@ -504,6 +541,36 @@ int launch_tc(const BatchArgs &a, void *stream_, bool gateup) {
   if (!ok) return static_cast<int>(cudaErrorInvalidValue);
   if (gateup) return wt == T_Q8_0 ? launch_kernel<true, T_Q8_0>(a, st, tw0, tw1, tbh, tbl) : launch_kernel<true, T_Q4_K>(a, st, tw0, tw1, tbh, tbl);
   return wt == T_Q8_0 ? launch_kernel<false, T_Q8_0>(a, st, tw0, tw1, tbh, tbl) : launch_kernel<false, T_Q4_K>(a, st, tw0, tw1, tbh, tbl);
+}
+
+// A dense Q4_K matrix (rows x cols, row stride rb) times nb tokens' plain Q8_K rows on the tensor cores: the grouped kernel
+// with one "expert" holding every token (the down role: row tiles of 256, token chunks spread over the CTAs, the
+// activations as fp16 hi/lo planes scaled by a power of two per token). co: device ints {nb, 0, nb} (the expert's count
+// and offsets). out [nb][rows].
+int launch_tc_dense(const uint8_t *w, uint32_t rb, int rows, int cols, int nb, const int8_t *qs, const float *dd, int *co,
+                    __half *ph, __half *pl, float *rs, float *out, int *err, cudaStream_t st) {
+  if (!tc_type_supported(T_Q4_K, w, rows, cols) || nb < 1) return static_cast<int>(cudaErrorInvalidValue);
+  BatchArgs b{};
+  b.T = nb;
+  b.K = 1;
+  b.NE = 1;
+  b.E = rows;
+  b.FF = cols;
+  b.down = w;
+  b.down_type = T_Q4_K;
+  b.drb = rb;
+  b.down_slab = static_cast<uint64_t>(rows) * rb;
+  b.counts = co;
+  b.offsets = co + 1;
+  b.hq_qs = const_cast<int8_t *>(qs);
+  b.hq_d = const_cast<float *>(dd);
+  b.hgh = ph;
+  b.hgl = pl;
+  b.rs = rs;
+  b.hd = out;
+  b.err = err;
+  b.tc_dn = 1;
+  return launch_tc(b, st, false);
 }
 
 }  // namespace clb

@@ -541,6 +541,7 @@ struct PfBufs {
   int8_t *qs;
   float *dd;
   int16_t *bs;
+  PfTc tc;
   size_t total;
 };
 static PfBufs pf_layout(const FwdArgs &a, int cap, uint8_t *base) {
@@ -558,6 +559,11 @@ static PfBufs pf_layout(const FwdArgs &a, int cap, uint8_t *base) {
   b.qs = reinterpret_cast<int8_t *>(take(C * W));
   b.dd = reinterpret_cast<float *>(take(C * W / 256 * 4));
   b.bs = reinterpret_cast<int16_t *>(take(C * W / 16 * 2));
+  b.tc.co = reinterpret_cast<int *>(take(16));
+  b.tc.ph = reinterpret_cast<__half *>(take(C * W * 2));
+  b.tc.pl = reinterpret_cast<__half *>(take(C * W * 2));
+  b.tc.rs = reinterpret_cast<float *>(take(C * 4));
+  b.tc.tmp = reinterpret_cast<float *>(take(C * W * 4));
   b.total = o;
   return b;
 }
@@ -583,15 +589,21 @@ static int prefill_batch(clb200_model *m, const int *tokens, int nb, float *logi
     __half *kc = a.kc + static_cast<size_t>(l) * a.ctx * KW, *vc = a.vc + static_cast<size_t>(l) * a.ctx * KW;
     // attention (c/src/forward.c:1096-1123): norm, Q/K/V products, QK-norm + rotation + cache, attention, O product
     PF_OR(pf_norm_q8k(b.X, 0, nb, E, y.attn_norm, a.eps, b.qs, b.dd, b.bs, st), "the attention norm");
-    PF_OR(pf_mv(y.wq, NQ, E, nb, b.qs, b.dd, b.bs, b.Q, 0, 1.f, errw, st), "the Q product");
-    PF_OR(pf_mv(y.wk, KW, E, nb, b.qs, b.dd, b.bs, b.K, 0, 1.f, errw, st), "the K product");
-    PF_OR(pf_mv(y.wv, KW, E, nb, b.qs, b.dd, b.bs, b.V, 0, 1.f, errw, st), "the V product");
+    // the dense products: Q4_K on the tensor cores unless the integer path is asked for (clb200_set_exact)
+    const bool tc = !m->ctx->exact;
+    auto dense = [&](const FwdMat &w, int rows, int cols, float *out, int accum, float scale) {
+      return tc ? pf_mv_tc(w, rows, cols, nb, b.qs, b.dd, b.bs, out, accum, scale, b.tc, errw, st)
+                : pf_mv(w, rows, cols, nb, b.qs, b.dd, b.bs, out, accum, scale, errw, st);
+    };
+    PF_OR(dense(y.wq, NQ, E, b.Q, 0, 1.f), "the Q product");
+    PF_OR(dense(y.wk, KW, E, b.K, 0, 1.f), "the K product");
+    PF_OR(dense(y.wv, KW, E, b.V, 0, 1.f), "the V product");
     PfQkArgs qa{b.Q, b.K, b.V, b.Qr, y.qn, y.kn, kc, vc, a.rope_cs, nb, pos0, a.n_head, a.n_kv, a.hd, a.qk_mode, a.rope_pairs, a.eps};
     PF_OR(pf_qk(qa, st), "QK-norm and rotation");
     PfAttnArgs aa{b.Qr, kc, vc, b.att, nb, pos0, a.n_head, a.n_kv, a.hd, KW, a.attn_scale};
     PF_OR(pf_attn(aa, st), "the attention");
     PF_OR(pf_q8k(b.att, nb, NQ, b.qs, b.dd, b.bs, st), "quantizing the attention");
-    PF_OR(pf_mv(y.wo, E, NQ, nb, b.qs, b.dd, b.bs, b.X, 1, a.resid_scale, errw, st), "the O product");
+    PF_OR(dense(y.wo, E, NQ, b.X, 1, a.resid_scale), "the O product");
     // the mixture of experts over the batch (c/src/forward.c:1131-1210): the batched kernels
     if (run_moe_block(m->ctx, m->moe[static_cast<size_t>(l)], b.X, nb, nullptr, nullptr, st, err, errlen)) return 1;
   }

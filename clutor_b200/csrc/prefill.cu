@@ -1,7 +1,10 @@
 // Per-token kernels of the batched prompt path (run_std, c/src/forward.c:1078-1225): the embedding, rmsnorm + Q8_K,
 // QK-norm + rotary embedding + the key/value store, and the plain attention of every (token, head). Every float operation
 // the reference rounds is one explicitly rounded operation here, in the reference's order, as in the one-token step.
+#include <algorithm>
+
 #include "common.cuh"
+#include "decode.cuh"
 #include "modelops.cuh"
 #include "prefill.cuh"
 #include "rowdot.cuh"
@@ -181,6 +184,116 @@ __global__ void __launch_bounds__(AT) attn_kernel(const PfAttnArgs a) {
   }
 }
 
+// The same attention with one CTA per (key/value head, token) for all of the group's query heads: the keys and values pass
+// through shared memory GA_BLK positions at a time (rows padded by 16 bytes, so the lanes of a warp, consecutive
+// positions, read different banks), read once for the whole group. Scores: one thread per (head, position), the eight
+// running sums of dotf_h; the maximum per head (a warp per head), e_t, the float sum in position order (a thread per head),
+// p_t = e_t / sum; values: thread (head, d) chains in position order, a thread taking the same d of several heads so each
+// staged value is read once for them. Shared memory: the group's queries [GRP][hd], the scores [GRP][pos + 1], the stage.
+constexpr int GA_THREADS = 256, GA_BLK = 64;
+
+__host__ __device__ inline size_t ga_smem(int grp, int hd, int n) {
+  return static_cast<size_t>(grp) * hd * 4 + static_cast<size_t>(GA_BLK) * (hd + 8) * 2 + static_cast<size_t>(grp) * ((n + 3) & ~3) * 4 + 64;
+}
+
+__global__ void __launch_bounds__(GA_THREADS) attn_group_kernel(const PfAttnArgs a) {
+  extern __shared__ __align__(16) uint8_t ga_sm[];
+  __shared__ float s_mx[FWD_MAX_GROUP], s_sum[FWD_MAX_GROUP];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = blockIdx.x, b = blockIdx.y, hd = a.hd, nq = a.n_head * hd, KW = a.n_kvw, GRP = a.n_head / a.n_kv;
+  const int pos = a.pos0 + b, n = pos + 1, ns = (n + 3) & ~3, KS = hd + 8;
+  float *qf = reinterpret_cast<float *>(ga_sm);                             // [GRP][hd]
+  __half *kv = reinterpret_cast<__half *>(qf + GRP * hd);                   // [GA_BLK][hd + 8]
+  float *sc = reinterpret_cast<float *>(kv + GA_BLK * KS);                  // [GRP][ns]
+  for (int i = tid; i < GRP * hd; i += GA_THREADS) qf[i] = a.Qr[static_cast<size_t>(b) * nq + g * GRP * hd + i];
+  const __half *kb = a.kc + g * hd, *vb = a.vc + g * hd;
+  auto stage = [&](const __half *base, int b0, int cnt) {
+    __syncthreads();
+    for (int i = tid; i < cnt * (hd / 8); i += GA_THREADS) {
+      const int t = i / (hd / 8), q = i - t * (hd / 8);
+      *reinterpret_cast<uint4 *>(kv + t * KS + 8 * q) = reinterpret_cast<const uint4 *>(base + static_cast<size_t>(b0 + t) * KW)[q];
+    }
+    __syncthreads();
+  };
+  for (int b0 = 0; b0 < n; b0 += GA_BLK) {   // scores, the reference's dotf_h (c/src/forward.c:492-510)
+    const int cnt = min(GA_BLK, n - b0);
+    stage(kb, b0, cnt);
+    for (int p = tid; p < GRP * GA_BLK; p += GA_THREADS) {
+      const int j = p / GA_BLK, t = p - j * GA_BLK;
+      if (t < cnt) {
+        const __half *kr = kv + t * KS;
+        const float *q = qf + j * hd;
+        float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int i = 0; i < hd; i += 8) {
+          const uint4 kk = *reinterpret_cast<const uint4 *>(kr + i);
+          const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float2 f = __half22float2(k2[u]);
+            s8[2 * u] = __fadd_rn(s8[2 * u], __fmul_rn(q[i + 2 * u], f.x));
+            s8[2 * u + 1] = __fadd_rn(s8[2 * u + 1], __fmul_rn(q[i + 2 * u + 1], f.y));
+          }
+        }
+        const float d = __fadd_rn(__fadd_rn(__fadd_rn(s8[0], s8[1]), __fadd_rn(s8[2], s8[3])),
+                                  __fadd_rn(__fadd_rn(s8[4], s8[5]), __fadd_rn(s8[6], s8[7])));
+        sc[j * ns + b0 + t] = __fmul_rn(d, a.attn_scale);
+      }
+    }
+  }
+  __syncthreads();
+  for (int j = warp; j < GRP; j += GA_THREADS / 32) {   // each head's maximum
+    float mx = -INFINITY;
+    for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sc[j * ns + t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    if (lane == 0) s_mx[j] = mx;
+  }
+  __syncthreads();
+  for (int i = tid; i < GRP * n; i += GA_THREADS) {
+    const int j = i / n, t = i - j * n;
+    sc[j * ns + t] = expf_cr(__fsub_rn(sc[j * ns + t], s_mx[j]));
+  }
+  __syncthreads();
+  if (tid < GRP) {   // the float sum in position order (c/src/forward.c:602-603)
+    float sum = 0.f;
+    for (int t = 0; t < n; ++t) sum = __fadd_rn(sum, sc[tid * ns + t]);
+    s_sum[tid] = sum;
+  }
+  __syncthreads();
+  for (int i = tid; i < GRP * n; i += GA_THREADS) {
+    const int j = i / n, t = i - j * n;
+    sc[j * ns + t] = __fdiv_rn(sc[j * ns + t], s_sum[j]);
+  }
+  // values (axpy_h, c/src/forward.c:512-521): thread d of the head dimension takes heads j = jr, jr + JS, ...
+  const int pairs = GRP * hd, JS = GA_THREADS / hd > 0 ? GA_THREADS / hd : 1;
+  const int d = tid % hd, jr = tid / hd;
+  constexpr int MAXJ = FWD_MAX_GROUP;
+  float o[MAXJ];
+#pragma unroll
+  for (int k = 0; k < MAXJ; ++k) o[k] = 0.f;
+  for (int b0 = 0; b0 < n; b0 += GA_BLK) {
+    const int cnt = min(GA_BLK, n - b0);
+    stage(vb, b0, cnt);
+    if (tid < pairs && jr < JS) {
+      for (int t = 0; t < cnt; ++t) {
+        const float v = __half2float(kv[t * KS + d]);
+#pragma unroll
+        for (int k = 0; k < MAXJ; ++k) {
+          const int j = jr + k * JS;
+          if (j < GRP) o[k] = __fadd_rn(o[k], __fmul_rn(sc[j * ns + b0 + t], v));
+        }
+      }
+    }
+  }
+  if (tid < pairs && jr < JS) {
+#pragma unroll
+    for (int k = 0; k < MAXJ; ++k) {
+      const int j = jr + k * JS;
+      if (j < GRP) a.att[static_cast<size_t>(b) * nq + (g * GRP + j) * hd + d] = o[k];
+    }
+  }
+}
+
 // Dense products of a batch: out [nb][rows] (= or += scale *) w [rows][cols] (Q4_K / Q6_K) times plain Q8_K activations.
 // A CTA stages MT_ROWS rows (one bulk copy) and MT_TOK tokens' activations (swizzled Q8_K, each token's row padded by 16
 // bytes so the lanes of a warp, one token each, read different banks); a warp takes a row at a time and every lane forms
@@ -255,7 +368,35 @@ __global__ void __launch_bounds__(MT_THREADS) mvt_kernel(const uint8_t *w, uint3
   }
 }
 
+__global__ void counts_kernel(int *co, int nb) {
+  co[0] = nb;
+  co[1] = 0;
+  co[2] = nb;
+}
+
+__global__ void resid_add_kernel(float *x, const float *v, size_t n, float scale) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    x[i] = __fadd_rn(x[i], __fmul_rn(scale, v[i]));
+}
+
 }  // namespace
+
+int pf_mv_tc(const FwdMat &m, int rows, int cols, int nb, const int8_t *qs, const float *dd, const int16_t *bs, float *out, int accum,
+             float scale, const PfTc &tc, int *err, cudaStream_t st) {
+  // the grouped kernel gives a dense matrix one CTA per (256-row tile, 64-token chunk): below 256 tokens too few to beat
+  // the CUDA-core kernel's CTA per (32 rows, 32 tokens)
+  if (m.type != T_Q4_K || nb < 256 || !tc_type_supported(T_Q4_K, m.p, rows, cols))
+    return pf_mv(m, rows, cols, nb, qs, dd, bs, out, accum, scale, err, st);
+  counts_kernel<<<1, 1, 0, st>>>(tc.co, nb);
+  float *dst = accum ? tc.tmp : out;
+  const int rc = launch_tc_dense(m.p, m.rb, rows, cols, nb, qs, dd, tc.co, tc.ph, tc.pl, tc.rs, dst, err, st);
+  if (rc) return rc;
+  if (accum) {
+    const size_t n = static_cast<size_t>(nb) * rows;
+    resid_add_kernel<<<static_cast<int>(std::min<size_t>((n + 255) / 256, 1184)), 256, 0, st>>>(out, tc.tmp, n, scale);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
 
 int pf_mv(const FwdMat &m, int rows, int cols, int nb, const int8_t *qs, const float *dd, const int16_t *bs, float *out, int accum,
           float scale, int *err, cudaStream_t st) {
@@ -307,6 +448,20 @@ cudaError_t pf_qk(const PfQkArgs &a, cudaStream_t st) {
 cudaError_t pf_attn(const PfAttnArgs &a, cudaStream_t st) {
   const int n = a.pos0 + a.nb;
   if (n > PF_MAX_CTX || a.hd % 8) return cudaErrorInvalidValue;
+  const int grp = a.n_head / a.n_kv;
+  const size_t gsm = ga_smem(grp, a.hd, n);
+  if (grp <= FWD_MAX_GROUP && a.hd <= GA_THREADS && GA_THREADS % a.hd == 0 && gsm <= 200 * 1024) {   // the group kernel
+    static bool gattr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !gattr[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(attn_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (e != cudaSuccess) return e;
+      gattr[dev] = true;
+    }
+    attn_group_kernel<<<dim3(a.n_kv, a.nb), GA_THREADS, gsm, st>>>(a);
+    return cudaGetLastError();
+  }
   const size_t smem = (static_cast<size_t>(a.hd) + n) * 4;
   static bool attr[64] = {};
   int dev = 0;

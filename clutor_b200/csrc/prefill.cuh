@@ -49,6 +49,17 @@ cudaError_t pf_attn(const PfAttnArgs &a, cudaStream_t st);
 // rows and 32 tokens for batches of 8 or more tokens, else the product kernel of backend.cu. Returns a CUDA error code.
 int pf_mv(const FwdMat &m, int rows, int cols, int nb, const int8_t *qs, const float *dd, const int16_t *bs, float *out, int accum,
           float scale, int *err, cudaStream_t st);
+// Scratch of the tensor-core dense products: the count/offsets triple, fp16 hi/lo activation planes [nb][cols], a power of
+// two per token, and a product buffer [nb][rows] for products added into a residual.
+struct PfTc {
+  int *co;
+  __half *ph, *pl;
+  float *rs, *tmp;
+};
+// The same product with a Q4_K matrix on the tensor cores (fp16 hi/lo operands, ~1e-6 from the integer product) for
+// batches of 256 or more tokens; other types and smaller batches through pf_mv. Returns a CUDA error code.
+int pf_mv_tc(const FwdMat &m, int rows, int cols, int nb, const int8_t *qs, const float *dd, const int16_t *bs, float *out, int accum,
+             float scale, const PfTc &tc, int *err, cudaStream_t st);
 // The dense product kernel of backend.cu: out [nb][rows] (= or += scale *) w [rows][cols] times plain Q8_K activations.
 int launch_mv_dev(const uint8_t *w, uint32_t type, int rows, int cols, int nb, const int8_t *qs, const float *dd,
                   const int16_t *bs, float *out, int accum, float scale, int *err, cudaStream_t st);

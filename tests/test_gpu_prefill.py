@@ -85,6 +85,15 @@ def test_prefill_parity(ctx, tmp_path, name, exact):
     print(f"{name}: worst logits rel L2 {worst:.3g}")
 
 
+def test_prefill_large_batch_tensor_cores(ctx, tmp_path):
+    """300 tokens in one batch: the Q4_K dense products (256 tokens and more) run on the tensor cores too."""
+    name = "qwen3moe_gqa8_q4k_down"
+    rng = np.random.default_rng(17)
+    prompt = rng.integers(0, SHAPES[name].vocab, 300).tolist()
+    worst = run(ctx, tmp_path, SHAPES[name], prompt, batch=512, exact=False, steps=4)
+    print(f"{name}, one batch of 300: worst logits rel L2 {worst:.3g}")
+
+
 @pytest.mark.parametrize("n,batch", [(100, 16), (65, 64), (130, 64), (9, 1), (2, 512)])
 def test_prefill_batch_boundaries(ctx, tmp_path, n, batch):
     """Batches of the reference's CLUTOR_PS_B sizes: several full batches and a short last one, a last batch of one token
