@@ -114,6 +114,10 @@ CLB_DEV void dequant_q80(const uint32_t (&w)[68], int b, uint32_t (&hi)[16], uin
   for (int i = 0; i < 8; ++i) dequant4(word_at(w, 34 * b + 2 + 4 * i), d2, hi[2 * i], hi[2 * i + 1], lo[2 * i], lo[2 * i + 1]);
 }
 
+// SwiGLU through one out-of-line copy: the epilogue's unrolled loop would otherwise hold sixteen copies of the double
+// exponential, code that runs once per tile and so is fetched again for every tile.
+__device__ __noinline__ float silu_mul_once(float g, float u) { return silu_mul(g, u); }
+
 CLB_DEV float half_bits(uint32_t bits16) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16))); }
 CLB_DEV uint32_t pack_half2(float a, float b) { return as_u32(__floats2half2_rn(a, b)); }   // a in the low half
 
@@ -383,7 +387,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             v1[j] = __fmul_rn(v1[j], sc);
           }
           if (GATEUP) {
-            const float hv = silu_mul(v0[j], v1[j]);
+            const float hv = silu_mul_once(v0[j], v1[j]);
             const size_t o = pos * a.FF + 128 * m + r;
             a.hg[o] = hv;
             if (a.tc_dn && a.down_type == T_Q8_0) {   // the Q8_0 down product's activations
