@@ -59,7 +59,6 @@ struct TcShape {
   static constexpr uint32_t B_STAGE = 2 * B_TILE;   // hi rows [0, NT), lo rows [NT, 2 NT)
   static constexpr uint32_t ACC_COLS = 4 * NT;
   static constexpr int A_STAGES = static_cast<int>((TMEM_COLS - ACC_COLS) / A_COLS);
-  static constexpr int WORDS = CHUNK / 4;
   static constexpr int N_BARS = 2 * RAW_STAGES + 2 * B_STAGES + 2 * A_STAGES + 3;
   static constexpr uint32_t SMEM = RAW_STAGES * RAW_STAGE + B_STAGES * B_STAGE + 8 * N_BARS + 16 + 1024;
   static_assert(A_STAGES >= 2, "TMEM budget");
@@ -106,12 +105,14 @@ CLB_DEV void dequant4(uint32_t qw, __half2 d2, uint32_t &hi01, uint32_t &hi23, u
   lo23 = as_u32(__hfma2(q23, d2, __hneg2(h23)));
 }
 
-// Q8_0 block b (0..7) of a 272-byte chunk as 16 columns of packed fp16 pairs, hi and lo planes.
-CLB_DEV void dequant_q80(const uint32_t (&w)[68], int b, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
-  const uint32_t dw = w[(34 * b) >> 2];   // the block's fp16 scale at byte 34b (2-byte aligned)
-  const __half2 d2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(((34 * b) & 3) == 0 ? (dw & 0xffffu) : (dw >> 16))));
+// Dequantization of one atom (64 values), its words read from shared memory per atom so the atom loop can stay rolled and
+// its code small. Q8_0: blocks 2 at and 2 at + 1 of a 272-byte chunk (68 bytes as 17 words), piece bb of them, as 16
+// columns of packed fp16 pairs, hi and lo planes.
+CLB_DEV void dequant_q80_atom(const uint32_t (&w)[17], int bb, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+  const uint32_t dw = w[(34 * bb) >> 2];
+  const __half2 d2 = __half2half2(__ushort_as_half(static_cast<unsigned short>(((34 * bb) & 3) == 0 ? (dw & 0xffffu) : (dw >> 16))));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) dequant4(word_at(w, 34 * b + 2 + 4 * i), d2, hi[2 * i], hi[2 * i + 1], lo[2 * i], lo[2 * i + 1]);
+  for (int i = 0; i < 8; ++i) dequant4(word_at(w, 34 * bb + 2 + 4 * i), d2, hi[2 * i], hi[2 * i + 1], lo[2 * i], lo[2 * i + 1]);
 }
 
 // SwiGLU through one out-of-line copy: the epilogue's unrolled loop would otherwise hold sixteen copies of the double
@@ -121,12 +122,16 @@ __device__ __noinline__ float silu_mul_once(float g, float u) { return silu_mul(
 CLB_DEV float half_bits(uint32_t bits16) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16))); }
 CLB_DEV uint32_t pack_half2(float a, float b) { return as_u32(__floats2half2_rn(a, b)); }   // a in the low half
 
-// Sub-block j (0..7) of a Q4_K block (144 bytes as 36 words: d, dmin, 12 scale bytes, 128 quant bytes) as 16 columns of
-// packed fp16 pairs of w = d*sc*q - dmin*mn, hi and lo planes. Sub-block j's values are the low (j even) or high (j odd)
-// nibbles of quant bytes 32*(j/2) .. +31; scales and mins unpack as in c/src/quant.c:36-40.
-CLB_DEV void dequant_q4k(const uint32_t (&w)[36], int j, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
-  const float d = half_bits(w[0] & 0xffffu), dmin = half_bits(w[0] >> 16);
-  auto sbyte = [&](int i) -> int { return static_cast<int>((w[1 + (i >> 2)] >> (8 * (i & 3))) & 0xffu); };   // scale byte i
+// Q4_K: sub-block j (0..7) of a block from its header words (d, dmin, 12 scale bytes) and the 8 quant words of its
+// 64-value group (quant bytes 32*(j/2) .. +31), as 16 columns of packed fp16 pairs of w = d*sc*q - dmin*mn, hi and lo
+// planes. Sub-block j's values are the low (j even) or high (j odd) nibbles; scales and mins unpack as in
+// c/src/quant.c:36-40.
+CLB_DEV void dequant_q4k_atom(const uint32_t (&hdr)[4], const uint32_t (&qw8)[8], int j, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+  const float d = half_bits(hdr[0] & 0xffffu), dmin = half_bits(hdr[0] >> 16);
+  auto sbyte = [&](int i) -> int {   // scale byte i (0..11)
+    const uint32_t wd = i < 4 ? hdr[1] : i < 8 ? hdr[2] : hdr[3];
+    return static_cast<int>((wd >> (8 * (i & 3))) & 0xffu);
+  };
   int sc, mn;
   if (j < 4) {
     sc = sbyte(j) & 63;
@@ -138,8 +143,8 @@ CLB_DEV void dequant_q4k(const uint32_t (&w)[36], int j, uint32_t (&hi)[16], uin
   const float a1 = __fmul_rn(d, static_cast<float>(sc)), a0 = __fmul_rn(dmin, static_cast<float>(mn));   // both exact
   const int shift = (j & 1) ? 4 : 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {   // quant bytes 4i .. 4i+3 of the group: elements 4i .. 4i+3
-    const uint32_t qw = w[4 + 8 * (j >> 1) + i] >> shift;
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t qw = qw8[i] >> shift;
     float v[4], h[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -152,6 +157,7 @@ CLB_DEV void dequant_q4k(const uint32_t (&w)[36], int j, uint32_t (&hi)[16], uin
     lo[2 * i + 1] = pack_half2(__fsub_rn(v[2], h[2]), __fsub_rn(v[3], h[3]));
   }
 }
+
 
 // The CTA's work items: (expert e, row tile m, token chunk) for every expert with tokens, numbered expert by expert, row tile
 // by row tile, the chunks of a tile consecutive (so CTAs running side by side share a weight tile in L2); item w goes to CTA
@@ -328,17 +334,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int c = 0; c < nchunk; ++c, ++g) {
         const uint32_t u = 2 * g + mA, s = u % RAW_STAGES;
         if (!mbar_wait_bounded(&raw_full[s], (u / RAW_STAGES) & 1)) return false;
-        uint32_t w[S::WORDS];
-        const uint4 *src = reinterpret_cast<const uint4 *>(raw + s * RAW_STAGE + r * S::CHUNK);
-#pragma unroll
-        for (int i = 0; i < S::WORDS / 4; ++i) {
-          const uint4 v = src[i];
-          w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+        // this thread's weight row of the chunk, read from the stage atom by atom (the stage is released after the last)
+        const uint32_t *rw = reinterpret_cast<const uint32_t *>(raw + s * RAW_STAGE + r * S::CHUNK);
+        uint32_t hdr[4] = {0, 0, 0, 0};
+        if constexpr (WT != T_Q8_0) {
+          const uint4 h4 = *reinterpret_cast<const uint4 *>(rw);
+          hdr[0] = h4.x; hdr[1] = h4.y; hdr[2] = h4.z; hdr[3] = h4.w;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_free[s]);
-#pragma unroll
+#pragma unroll 1
         for (int at = 0; at < 4; ++at, ++t) {
+          constexpr int AW = WT == T_Q8_0 ? 17 : 8;
+          uint32_t aw[AW];
+          if constexpr (WT == T_Q8_0) {
+#pragma unroll
+            for (int i = 0; i < 17; ++i) aw[i] = rw[17 * at + i];
+          } else {
+            const uint4 *p4 = reinterpret_cast<const uint4 *>(rw + 4 + 8 * at);
+            const uint4 x0 = p4[0], x1 = p4[1];
+            aw[0] = x0.x; aw[1] = x0.y; aw[2] = x0.z; aw[3] = x0.w; aw[4] = x1.x; aw[5] = x1.y; aw[6] = x1.z; aw[7] = x1.w;
+          }
           const uint32_t sa = t % A_STAGES;
           if (t >= A_STAGES && !mbar_wait_bounded(&a_free[sa], (t / A_STAGES - 1) & 1)) return false;
           tc::fence_after_sync();
@@ -346,8 +360,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int bb = 0; bb < 2; ++bb) {   // two 32-element pieces: Q8_0 blocks, Q4_K sub-blocks
             uint32_t hi[16], lo[16];
-            if constexpr (WT == T_Q8_0) dequant_q80(w, 2 * at + bb, hi, lo);
-            else dequant_q4k(w, 2 * at + bb, hi, lo);
+            if constexpr (WT == T_Q8_0) dequant_q80_atom(aw, bb, hi, lo);
+            else dequant_q4k_atom(hdr, aw, 2 * at + bb, hi, lo);
             tc::st_x16(col + 16 * bb, hi);
             tc::st_x16(col + 32 + 16 * bb, lo);
           }
@@ -356,6 +370,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[sa]);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_free[s]);
       }
       // epilogue: warps of matrix 0 take tokens [0, NT/2), those of matrix 1 [NT/2, NT), 16 at a time; each reads both
       // accumulators, whose column n holds the x hi products and column NTt + n the x lo products of token n
