@@ -77,6 +77,20 @@ static int ensure_scratch(clb200_ctx *c, size_t need, char *err, size_t errlen) 
   return 0;
 }
 
+static int ensure_hstage(clb200_ctx *c, size_t need, char *err, size_t errlen) {
+  if (need <= c->hstage_cap) return 0;
+  if (c->hstage) {
+    CUDA_OR(cudaStreamSynchronize(c->stream), "waiting for the device before growing host staging");
+    cudaFreeHost(c->hstage);
+  }
+  c->hstage = nullptr;
+  c->hstage_cap = 0;
+  const size_t cap = al(need, 1 << 16);
+  CUDA_OR(cudaHostAlloc(reinterpret_cast<void **>(&c->hstage), cap, cudaHostAllocDefault), "pinning host staging");
+  c->hstage_cap = cap;
+  return 0;
+}
+
 // Shared-memory plan of the one-token kernel for a layer on a device with `sms` SMs and `max_smem` bytes of opt-in shared
 // memory per block; 0 when it fits.
 int plan_decode_shape(int sms, int max_smem, const clb200_moe_layer &L, DecodeArgs &a) {
@@ -205,9 +219,13 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
     c->attrs_set = true;
   }
   const DecodeFn fn = decode_kernel_for(a.gate_type, a.down_type);
-  int occ = 0;
-  CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DECODE_THREADS, a.smem_bytes), "occupancy");
-  if (occ < 1) { errf(err, errlen, "the one-token kernel does not fit on an SM (%u bytes of shared memory)", a.smem_bytes); return 1; }
+  if (reinterpret_cast<const void *>(fn) != c->occ_fn || a.smem_bytes != c->occ_smem) {   // checked once per kernel and size
+    int occ = 0;
+    CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DECODE_THREADS, a.smem_bytes), "occupancy");
+    if (occ < 1) { errf(err, errlen, "the one-token kernel does not fit on an SM (%u bytes of shared memory)", a.smem_bytes); return 1; }
+    c->occ_fn = reinterpret_cast<const void *>(fn);
+    c->occ_smem = a.smem_bytes;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(c->sms);
   cfg.blockDim = dim3(DECODE_THREADS);
@@ -258,6 +276,7 @@ void clb200_close(clb200_ctx *c) {
   if (c->scratch) cudaFree(c->scratch);
   if (c->small) cudaFree(c->small);
   if (c->route_buf) cudaFree(c->route_buf);
+  if (c->hstage) cudaFreeHost(c->hstage);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
 }
@@ -460,18 +479,22 @@ int clb200_ep_experts(clb200_ctx *c, int layer, int T, const int8_t *xq_qs, cons
   return 0;
 }
 
+// 1 with err set when the device error word read back is non-zero; the word and the counters a failed kernel may have left
+// behind are cleared.
+static int report_device_error(clb200_ctx *c, int code, char *err, size_t errlen) {
+  if (!code) return 0;
+  errf(err, errlen, "device error %d: %s", code, device_error_text(code));
+  cudaMemset(c->small, 0, 4096);
+  return 1;
+}
+
 int clb200_status(clb200_ctx *c, char *err, size_t errlen) {
   if (!c) { errf(err, errlen, "no context"); return 1; }
   cudaSetDevice(c->device);
   CUDA_OR(cudaDeviceSynchronize(), "device");
   int code = 0;
   CUDA_OR(cudaMemcpy(&code, c->small, 4, cudaMemcpyDeviceToHost), "reading the device error word");
-  if (code) {
-    errf(err, errlen, "device error %d: %s", code, device_error_text(code));
-    cudaMemset(c->small, 0, 4096);   // clear the error and the counters a failed kernel may have left behind
-    return 1;
-  }
-  return 0;
+  return report_device_error(c, code, err, errlen);
 }
 
 int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, int *sel_out, float *wt_out, char *err,
@@ -502,13 +525,25 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
   int *dsel = reinterpret_cast<int *>(c->scratch + s.off_sel);
   float *dwt = reinterpret_cast<float *>(c->scratch + s.off_wt);
   const size_t xb = static_cast<size_t>(T) * E * 4, kb = static_cast<size_t>(T) * K * 4;
+  // The results come back through pinned staging: x (up to 1 MB; larger x goes straight to the caller's buffer), sel and wt,
+  // which lie in that order at the start of scratch, as one copy, and the error word as a second; then one wait on the
+  // stream. A copy per buffer and a device-wide synchronisation to read the error word cost more than the kernel at T = 1.
+  const bool stage_x = xb <= (size_t(1) << 20);
+  const size_t lo = stage_x ? s.off_x : s.off_sel, span = s.off_wt + kb - lo, at_err = al(span, 16);
+  if (ensure_hstage(c, at_err + 16, err, errlen)) return 1;
   CUDA_OR(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, c->stream), "copying x to the device");
   if (run_block(c, dl, dx, T, dsel, dwt, c->stream, err, errlen)) return 1;
-  CUDA_OR(cudaMemcpyAsync(x, dx, xb, cudaMemcpyDeviceToHost, c->stream), "copying x back");
-  if (sel_out) CUDA_OR(cudaMemcpyAsync(sel_out, dsel, kb, cudaMemcpyDeviceToHost, c->stream), "copying the routing back");
-  if (wt_out) CUDA_OR(cudaMemcpyAsync(wt_out, dwt, kb, cudaMemcpyDeviceToHost, c->stream), "copying the weights back");
+  if (!stage_x) CUDA_OR(cudaMemcpyAsync(x, dx, xb, cudaMemcpyDeviceToHost, c->stream), "copying x back");
+  CUDA_OR(cudaMemcpyAsync(c->hstage, c->scratch + lo, span, cudaMemcpyDeviceToHost, c->stream), "copying the results back");
+  CUDA_OR(cudaMemcpyAsync(c->hstage + at_err, c->small, 4, cudaMemcpyDeviceToHost, c->stream), "reading the device error word");
   CUDA_OR(cudaStreamSynchronize(c->stream), "running the MoE block");
-  return clb200_status(c, err, errlen);
+  int code = 0;
+  std::memcpy(&code, c->hstage + at_err, 4);
+  if (report_device_error(c, code, err, errlen)) return 1;
+  if (stage_x) std::memcpy(x, c->hstage + (s.off_x - lo), xb);
+  if (sel_out) std::memcpy(sel_out, c->hstage + (s.off_sel - lo), kb);
+  if (wt_out) std::memcpy(wt_out, c->hstage + (s.off_wt - lo), kb);
+  return 0;
 }
 
 }  // extern "C"

@@ -98,7 +98,10 @@ struct clb200_ctx {
   int *small = nullptr;                            // [0] device error word, [64..] counters of the one-token kernel
   uint8_t *scratch = nullptr;
   size_t scratch_cap = 0;
-  float *hx = nullptr;                             // host-call staging of x / sel / wt on the device (in scratch)
+  uint8_t *hstage = nullptr;                       // pinned host staging of a host call's results and the error word
+  size_t hstage_cap = 0;
+  const void *occ_fn = nullptr;                    // the one-token kernel and shared size last found to fit an SM
+  uint32_t occ_smem = 0;
   uint64_t bytes = 0;
   bool attrs_set = false;
   unsigned long long *trace = nullptr;             // phase trace of the one-token kernel (device, 32 per CTA) or null
