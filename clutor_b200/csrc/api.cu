@@ -84,10 +84,12 @@ static int ensure_hstage(clb200_ctx *c, size_t need, char *err, size_t errlen) {
     cudaFreeHost(c->hstage);
   }
   c->hstage = nullptr;
+  c->hstage_dev = nullptr;
   c->hstage_cap = 0;
   const size_t cap = al(need, 1 << 16);
-  CUDA_OR(cudaHostAlloc(reinterpret_cast<void **>(&c->hstage), cap, cudaHostAllocDefault), "pinning host staging");
+  CUDA_OR(cudaHostAlloc(reinterpret_cast<void **>(&c->hstage), cap, cudaHostAllocMapped | cudaHostAllocPortable), "pinning host staging");
   c->hstage_cap = cap;
+  CUDA_OR(cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->hstage_dev), c->hstage, 0), "mapping host staging");
   return 0;
 }
 
@@ -176,14 +178,15 @@ static const char *device_error_text(int code) {
 
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
                const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
-               const SmartRoute *smart) {
+               const SmartRoute *smart, float *x_out, int *err_out) {
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
   DecodeArgs a{};
   if (plan_decode(c, L, a)) { errf(err, errlen, "the one-token kernel does not take this layer (K-quant experts only)"); return 1; }
   const Scratch s = plan_scratch(1, E, FF, NE, K, false);
   if (ensure_scratch(c, s.total, err, errlen)) return 1;
   uint8_t *sc = c->scratch;
-  a.x_in = x; a.x_out = x;
+  a.x_in = x; a.x_out = x_out ? x_out : x;
+  a.err_out = err_out;
   a.norm = L.ffn_norm_f; a.router = L.router_f;
   a.gate = L.gate.p; a.up = L.up.p; a.down = L.down.p;
   a.gate_slab = L.gate_slab; a.up_slab = L.up_slab; a.down_slab = L.down_slab;
@@ -497,6 +500,35 @@ int clb200_status(clb200_ctx *c, char *err, size_t errlen) {
   return report_device_error(c, code, err, errlen);
 }
 
+// One token of a host call through the one-token kernel, with no copy-engine transfer: x is copied into the mapped pinned
+// staging on the host and read from there by a small kernel; the one-token kernel writes x, sel and wt into the staging
+// and its last CTA the error word; one wait on the stream. (Each copy-engine transfer costs several microseconds of
+// latency, as much as a quarter of the kernel at one token.)
+static int host_call_one(clb200_ctx *c, const DevLayer &dl, float *x, int *sel_out, float *wt_out, char *err, size_t errlen) {
+  const clb200_moe_layer &L = dl.d;
+  const int E = L.n_embd, K = L.n_used;
+  const size_t xb = static_cast<size_t>(E) * 4, kb = static_cast<size_t>(K) * 4;
+  const size_t o_out = al(xb), o_sel = o_out + al(xb), o_wt = o_sel + al(kb), o_err = o_wt + al(kb);
+  if (ensure_hstage(c, o_err + 256, err, errlen)) return 1;
+  const Scratch s = plan_scratch(1, E, L.n_ff_exp, L.n_expert, K, false);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  float *dx = reinterpret_cast<float *>(c->scratch + s.off_x);
+  uint8_t *h = c->hstage, *hd = c->hstage_dev;
+  volatile int *herr = reinterpret_cast<volatile int *>(h + o_err);
+  *herr = 0;
+  std::memcpy(h, x, xb);
+  CUDA_OR(launch_stage_in(reinterpret_cast<const float *>(hd), dx, E, c->stream), "staging x");
+  if (launch_one(c, L, dx, 0, nullptr, nullptr, nullptr, reinterpret_cast<int *>(hd + o_sel), reinterpret_cast<float *>(hd + o_wt),
+                 c->stream, err, errlen, nullptr, reinterpret_cast<float *>(hd + o_out), reinterpret_cast<int *>(hd + o_err)))
+    return 1;
+  CUDA_OR(cudaStreamSynchronize(c->stream), "running the MoE block");
+  if (report_device_error(c, *herr, err, errlen)) return 1;
+  std::memcpy(x, h + o_out, xb);
+  if (sel_out) std::memcpy(sel_out, h + o_sel, kb);
+  if (wt_out) std::memcpy(wt_out, h + o_wt, kb);
+  return 0;
+}
+
 int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, int *sel_out, float *wt_out, char *err,
                    size_t errlen) {
   if (!c) { errf(err, errlen, "no context"); return 1; }
@@ -518,6 +550,8 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
     if (h < 0) return 1;
   }
   const DevLayer &dl = c->layers[h];
+  DecodeArgs probe{};
+  if (T == 1 && plan_decode(c, dl.d, probe) == 0) return host_call_one(c, dl, x, sel_out, wt_out, err, errlen);
   const int E = L->n_embd, K = L->n_used;
   const Scratch s = plan_scratch(T, E, L->n_ff_exp, L->n_expert, K, true);   // the staging buffers lead either plan
   if (ensure_scratch(c, s.total, err, errlen)) return 1;

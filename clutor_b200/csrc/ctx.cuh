@@ -98,7 +98,8 @@ struct clb200_ctx {
   int *small = nullptr;                            // [0] device error word, [64..] counters of the one-token kernel
   uint8_t *scratch = nullptr;
   size_t scratch_cap = 0;
-  uint8_t *hstage = nullptr;                       // pinned host staging of a host call's results and the error word
+  uint8_t *hstage = nullptr;                       // pinned, mapped host staging of a host call's x, results and error word
+  uint8_t *hstage_dev = nullptr;                   // its device address
   size_t hstage_cap = 0;
   const void *occ_fn = nullptr;                    // the one-token kernel and shared size last found to fit an SM
   uint32_t occ_smem = 0;
@@ -115,6 +116,7 @@ namespace clb {
 // sel_in / wt_in [n_used] (host) and slabs [n_used] (device addresses, or null entries for L's own tensors). Returns 1 with
 // err set when the layer does not suit the one-token kernel or the launch fails.
 // smart (mode 1 only, may be null): SMART-ROUTE with the residency and settings it holds (DecodeArgs::resident ...).
+// x_out (null: x itself) receives the result; err_out (null: none) is DecodeArgs::err_out.
 struct SmartRoute {
   const uint8_t *resident;   // device-visible [n_expert] bytes
   int J, M;
@@ -123,7 +125,7 @@ struct SmartRoute {
 };
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
                const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
-               const SmartRoute *smart = nullptr);
+               const SmartRoute *smart = nullptr, float *x_out = nullptr, int *err_out = nullptr);
 // The MoE block of layer dl on T tokens of device data x (updated in place), queued on st: the one-token kernel for T = 1,
 // the batched kernels otherwise; sel / wt (device, [T * n_used]) may be null.
 int run_moe_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,

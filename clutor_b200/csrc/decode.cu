@@ -371,14 +371,36 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     if (s_flag[1] && s_flag[0])   // an error path may leave copies unwaited; the normal path waited in phase 6
       for (int k = 0; k < K; ++k)
         if (!mbar_wait_bounded(&bars[k], 0)) set_error(a.err, ERR_WAIT_COPY);
+    if (a.err_out) __threadfence();   // the CTA's error-word writes (ordered by the block barrier) before its count
     const uint32_t prev = atomicAdd(&a.sync[2], 1u);
     if (prev == static_cast<uint32_t>(G) - 1) {
+      if (a.err_out) {
+        __threadfence();
+        *reinterpret_cast<volatile int *>(a.err_out) = atomicOr(a.err, 0);
+      }
       atomicExch(&a.sync[0], 0u);
       atomicExch(&a.sync[1], 0u);
       atomicExch(&a.sync[2], 0u);
       __threadfence();
     }
   }
+}
+
+__global__ void __launch_bounds__(256) stage_in_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst, int n4) {
+  grid_launch_dependents();
+  float4 v[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)   // every load in flight before the first store: one round trip over the bus
+    if (threadIdx.x + 256 * u < n4) v[u] = src[threadIdx.x + 256 * u];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    if (threadIdx.x + 256 * u < n4) dst[threadIdx.x + 256 * u] = v[u];
+}
+
+cudaError_t launch_stage_in(const float *src, float *dst, int n, cudaStream_t st) {
+  if (n % 4 || n > 4096) return cudaErrorInvalidValue;
+  stage_in_kernel<<<1, 256, 0, st>>>(reinterpret_cast<const float4 *>(src), reinterpret_cast<float4 *>(dst), n / 4);
+  return cudaGetLastError();
 }
 
 cudaError_t decode_allow_smem(int bytes) {

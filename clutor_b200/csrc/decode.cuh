@@ -26,6 +26,8 @@ struct DecodeArgs {
   float *wt_out;                 // [K] or null
   uint32_t *sync;                // [0] logits written, [1] CTAs whose hg rows are written, [2] CTAs finished; zero on entry
   int *err;                      // first device error
+  int *err_out;                  // null, or host-mapped: the last CTA out copies the error word there (a host call reads it
+                                 // after its one wait instead of copying it back)
   // 0: the whole block; 1: routing only (sel_out / wt_out; x unchanged); 2: the experts of a given routing (sel_in / wt_in,
   // renormalised already), each expert's weights at slab[k] (gate, up and down slabs back to back) or, where slab[k] is
   // null, in gate / up / down
@@ -50,6 +52,10 @@ struct DecodeArgs {
 
 // The one-token kernel for experts of these types (gate/up share one type), or null when it has none.
 using DecodeFn = void (*)(DecodeArgs);
+// n floats (n a multiple of 4, at most 4096) from host-mapped src to device dst on st, by one small CTA that lets the next
+// kernel launch at once (programmatic dependent launch): a host call's x reaches the one-token kernel without a
+// copy-engine transfer.
+cudaError_t launch_stage_in(const float *src, float *dst, int n, cudaStream_t st);
 DecodeFn decode_kernel_for(uint32_t gate_type, uint32_t down_type);
 // Lets every instantiation use `bytes` of dynamic shared memory (on the current device).
 cudaError_t decode_allow_smem(int bytes);
