@@ -119,7 +119,8 @@ int plan_decode_shape(int sms, int max_smem, const clb200_moe_layer &L, DecodeAr
   a.off_norm = take(static_cast<size_t>(E) * 4);
   a.off_xq = take(static_cast<size_t>(E) + 2 * (E / 16) + 4 * (E / 256));
   a.off_router = take(static_cast<size_t>(nre) * E * 4);
-  a.off_rprod = take(static_cast<size_t>(nre) * 8 * (E / 8 + 4) * 4);   // products, one padded row per strided sum
+  // products, one padded row per strided sum; later the weighted expert outputs of this CTA's rows, [rd_max][K]
+  a.off_rprod = take(std::max(static_cast<size_t>(nre) * 8 * (E / 8 + 4), static_cast<size_t>(a.rd_max) * K) * 4);
   a.off_misc = take(NW * 8 + 16 + 3 * 32 * 4 + (DECODE_THREADS / 4) * 4);   // probs: one per expert the kernel can rank
   a.off_terms = take(static_cast<size_t>(a.rd_max) * K * nbd * 4);
   a.off_hq = take(static_cast<size_t>(K) * FF + 2 * (static_cast<size_t>(K) * FF / 16) + 4 * (static_cast<size_t>(K) * FF / 256));

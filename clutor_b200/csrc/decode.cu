@@ -15,16 +15,17 @@
 //      expert, eight strided float sums in element order, combined ((0+1)+(2+3))+((4+5)+(6+7)); logits to global memory,
 //      counter 0 += experts scored. Meanwhile the other warps form the Q8_K blocks of xn;
 //   3  when counter 0 reaches NE, DECODE_THREADS / 4 threads form the softmax, one expert each (double sum,
-//      c/src/forward.c:954-958); every thread then ranks
-//      a quarter of an expert's competitors (ties to the lower id: the order of the reference's repeated arg-max,
-//      c/src/forward.c:975-980); warp 0 renormalises (c/src/forward.c:984). Every CTA does this itself;
+//      c/src/forward.c:954-958); every thread then ranks a quarter of an expert's competitors (ties to the lower id: the
+//      order of the reference's repeated arg-max, c/src/forward.c:975-980); warp 0 renormalises (c/src/forward.c:984).
+//      Every CTA does this itself;
 //   4  one lane per chosen expert issues the bulk copies of this CTA's share of it: gate and up rows [FF*c/G, FF*(c+1)/G),
 //      down rows [E*c/G, E*(c+1)/G);
 //   5  a group of lanes per (expert, row): one lane per 256-element block (exact integer sums, the reference's float block
 //      term) for the gate row and the up row, the terms added in block order across the group by shuffles, SwiGLU
 //      (c/src/forward.c:1018) at the group's first lane, hg to global memory; counter 1 += 1 per CTA;
-//   6  when counter 1 reaches G: the Q8_K blocks of every expert's hg; down rows (same arithmetic); per output row
-//      moe = sum over experts in rank order of wt * hd; x = x + resid_scale * moe; the last CTA out resets the counters.
+//   6  when counter 1 reaches G: the Q8_K blocks of every expert's hg; down rows (same arithmetic; a group of lanes per
+//      (expert, block), one row each); wt * hd per (row, expert), then per output row moe = their sum in rank order;
+//      x = x + resid_scale * moe; the last CTA out resets the counters.
 #include "common.cuh"
 #include "decode.cuh"
 #include "route.cuh"
@@ -142,16 +143,24 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       for (int m0 = 0; m0 < nre; m0 += 4) {   // four experts per pass, eight lanes each
         const int m = m0 + grp;
         float s = 0.f;
-        if (m < nre) {   // lane l8 adds products l8, l8 + 8, l8 + 16, ... in order: its row of rprod, four at a time
+        if (m < nre) {   // lane l8 adds products l8, l8 + 8, l8 + 16, ... in order: its row of rprod, four float4 at a time,
+                         // the next four loaded while these are added (E / 32, the float4 per lane, is a multiple of 8)
           const float4 *p4 = reinterpret_cast<const float4 *>(rprod + (m * 8 + l8) * RS);
-          for (int q = 0; q < E / 32; q += 4) {
-            float4 v[4];
+          float4 v[4], w[4];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) v[t] = p4[q + t];
+          for (int t = 0; t < 4; ++t) v[t] = w[t] = p4[t];
+          for (int q = 0; q < E / 32; q += 4) {
+            if (q + 4 < E / 32) {
+#pragma unroll
+              for (int t = 0; t < 4; ++t) w[t] = p4[q + 4 + t];
+            }
 #pragma unroll
             for (int t = 0; t < 4; ++t) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[t].x), v[t].y), v[t].z), v[t].w);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) v[t] = w[t];
           }
         }
+        if (lane == 0 && m0 == 0) trace_stamp_here(a.trace, 24);
         float p8[8];
 #pragma unroll
         for (int l = 0; l < 8; ++l) p8[l] = __shfl_sync(FULL, s, (lane & ~7) + l);
@@ -210,19 +219,25 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     trace_stamp(a.trace, 10);
   }
   __syncthreads();
+  trace_stamp(a.trace, 20);
   if (a.mode != 2 && !s_flag[0]) {   // rank = experts ahead of this one in the reference's arg-max order; four threads per expert
     const int e = tid >> 2, part = tid & 3, n4 = (NE + 3) / 4, per = (n4 + 3) / 4;
     const float pe = e < NE ? probs[e] : 0.f;
-    int rank = 0;
     const float4 *p4 = reinterpret_cast<const float4 *>(probs);
-    for (int j = part * per; j < min(n4, (part + 1) * per); ++j) {
-      const float4 q = p4[j];
-      const int f = 4 * j;
-      rank += (q.x > pe || (q.x == pe && f < e)) + (q.y > pe || (q.y == pe && f + 1 < e)) +
-              (q.z > pe || (q.z == pe && f + 2 < e)) + (q.w > pe || (q.w == pe && f + 3 < e));
+    float4 q[8];   // per <= 8 (NE <= 128): every load in flight before the first comparison; -1 (below every probability) past the end
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      q[u] = u < per && part * per + u < n4 ? p4[part * per + u] : make_float4(-1.f, -1.f, -1.f, -1.f);
+    int rank = 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int f = 4 * (part * per + u);
+      rank += (q[u].x > pe || (q[u].x == pe && f < e)) + (q[u].y > pe || (q[u].y == pe && f + 1 < e)) +
+              (q[u].z > pe || (q[u].z == pe && f + 2 < e)) + (q[u].w > pe || (q[u].w == pe && f + 3 < e));
     }
     rank += __shfl_xor_sync(FULL, rank, 1);
     rank += __shfl_xor_sync(FULL, rank, 2);
+    trace_stamp(a.trace, 21);
     if (e < NE && part == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = pe; }
   }
   __syncthreads();
@@ -238,18 +253,20 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     if (tid < K) s_wt[tid] = probs[s_sel[tid]];
     __syncthreads();
   }
-  if (a.mode != 2 && !s_flag[0] && tid < K) {   // renormalise: each of K threads forms the same sum in rank order
-    float w = s_wt[tid];
-    if (a.norm_topk) {
-      float z = 0.f;
-      for (int k = 0; k < K; ++k) z = __fadd_rn(z, s_wt[k]);
-      if (z > 0.f) w = __fdiv_rn(w, z);
+  if (a.mode != 2 && !s_flag[0] && warp == 0) {   // renormalise: every lane forms the same sum in rank order, by shuffles
+    const float wk = lane < K ? s_wt[lane] : 0.f;
+    float z = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < K; ++k) z = __fadd_rn(z, __shfl_sync(FULL, wk, k));
+    if (lane < K) {
+      const float w = a.norm_topk && z > 0.f ? __fdiv_rn(wk, z) : wk;
+      s_wn[lane] = w;   // read after the next block barrier
+      if (c == 0) {
+        if (a.sel_out) a.sel_out[lane] = s_sel[lane];
+        if (a.wt_out) a.wt_out[lane] = w;
+      }
     }
-    s_wn[tid] = w;   // read after the next block barrier
-    if (c == 0) {
-      if (a.sel_out) a.sel_out[tid] = s_sel[tid];
-      if (a.wt_out) a.wt_out[tid] = w;
-    }
+    trace_stamp(a.trace, 22);
   }
 
   // ---- 4: bulk copies of this CTA's share of each chosen expert, one lane per expert ------------------------------------------
@@ -284,6 +301,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       total += n16[q];
     }
     mbar_arrive_expect_tx(&bars[k], total);
+    trace_stamp(a.trace, 23);
     for (int q = 0; q < 3; ++q)
       if (n16[q]) bulk_copy_g2s(dst[q], src[q] - lo[q], n16[q], &bars[k]);
     if (k == 0) s_flag[1] = 1;
@@ -308,6 +326,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
         while (waited < k) {   // slots land in rank order; wait for each once
           ++waited;
           if (!mbar_wait_bounded(&bars[waited], 0)) set_error(a.err, ERR_WAIT_COPY);
+          if (waited == 0) trace_stamp(a.trace, 25);
         }
         if (has_blk) {
 #pragma unroll 1
@@ -316,6 +335,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
             if (m == 0) tg = t; else tu = t;
           }
         }
+        if (t0 == 0) trace_stamp(a.trace, 26);
       }
       float sg = 0.f, su = 0.f;   // the row's block terms in block order
       for (int b = 0; b < nb; ++b) {
@@ -341,24 +361,31 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       if (!mbar_wait_bounded(&bars[k], 0)) set_error(a.err, ERR_WAIT_COPY);
     __syncthreads();
     trace_stamp(a.trace, 17);
-    const int C = K * nbd;                       // (block, expert) combinations, expert fastest (different banks)
-    const int combo = tid % C, grp = tid / C, ngrp = DECODE_THREADS / C;
-    if (grp < ngrp) {
-      const int blk = combo / K, k = combo - blk * K;
+    // (expert, block) pairs, LP lanes each, one row per lane: a pair's activation block is the same address for its lanes,
+    // so its register copy costs one broadcast read per warp instead of one read per row
+    const int C = K * nbd, LP = nd > 16 ? 32 : 16, ppw = 32 / LP, lp = lane & (LP - 1);
+    for (int p = warp * ppw + lane / LP; p < C; p += NW * ppw) {
+      const int k = p / nbd, blk = p - k * nbd;
       BlockAct dact;
-      load_block_act(hq_qs, hq_d, hq_bs, k * nbd + blk, dact);   // block index over all experts: the swizzle key
+      load_block_act(hq_qs, hq_d, hq_bs, p, dact);   // block index over all experts (k * nbd + blk): the swizzle key
       const uint8_t *drows = slots + seg_off(k, 2);
-      for (int r = grp; r < nd; r += ngrp) terms[(r * K + k) * nbd + blk] = kq_block(DT, drows + static_cast<size_t>(r) * drb, blk, dact);
+      for (int r = lp; r < nd; r += LP) terms[(r * K + k) * nbd + blk] = kq_block(DT, drows + static_cast<size_t>(r) * drb, blk, dact);
     }
     __syncthreads();
     trace_stamp(a.trace, 18);
-    for (int r = tid; r < nd; r += DECODE_THREADS) {   // hd[r][k] as the block terms in block order; moe in rank order
+    float *wprod = rprod;   // [nd][K] (the router products are done with)
+    for (int q = tid; q < nd * K; q += DECODE_THREADS) {   // wt[k] * hd[r][k], hd as the block terms in block order
+      const float *tq = terms + q * nbd;
+      float hd = 0.f;
+#pragma unroll 4
+      for (int b = 0; b < nbd; ++b) hd = __fadd_rn(hd, tq[b]);
+      wprod[q] = __fmul_rn(s_wn[q % K], hd);
+    }
+    __syncthreads();
+    for (int r = tid; r < nd; r += DECODE_THREADS) {   // moe in rank order
       float moe = 0.f;
-      for (int k = 0; k < K; ++k) {
-        float hd = 0.f;
-        for (int b = 0; b < nbd; ++b) hd = __fadd_rn(hd, terms[(r * K + k) * nbd + b]);
-        moe = __fadd_rn(moe, __fmul_rn(s_wn[k], hd));
-      }
+#pragma unroll 8
+      for (int k = 0; k < K; ++k) moe = __fadd_rn(moe, wprod[r * K + k]);
       a.x_out[i0 + r] = __fadd_rn(xr[r], __fmul_rn(a.resid_scale, moe));
     }
   }
