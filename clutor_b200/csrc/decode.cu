@@ -13,7 +13,7 @@
 //   1  x (in registers), the double sum of squares, xn = rmsnorm(x) (c/src/forward.c:412-417);
 //   2  the last warp forms this CTA's router logits as the reference's dotf does (c/src/forward.c:574-581): eight lanes per
 //      expert, eight strided float sums in element order, combined ((0+1)+(2+3))+((4+5)+(6+7)); logits to global memory,
-//      counter 0 += experts scored. Meanwhile the other warps form the Q8_K blocks of xn;
+//      counter 0 += experts scored. Meanwhile the warps of the other SM sub-partitions form the Q8_K blocks of xn;
 //   3  when counter 0 reaches NE, DECODE_THREADS / 4 threads form the softmax, one expert each (double sum,
 //      c/src/forward.c:954-958); every thread then ranks a quarter of an expert's competitors (ties to the lower id: the
 //      order of the reference's repeated arg-max, c/src/forward.c:975-980); warp 0 renormalises (c/src/forward.c:984).
@@ -172,8 +172,11 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       if (lane == 0) red_release_add(&a.sync[0], static_cast<uint32_t>(nre));   // release: the warp's logits, ordered by bar.warp.sync
       if (lane == 0) trace_stamp_here(a.trace, 5);
     }
-  } else {
-    q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, warp, RW, lane, true);
+  } else if ((warp & 3) != (RW & 3)) {
+    // the warps of the other three SM sub-partitions form the Q8_K blocks of xn, so none competes with the router warp's
+    // chains for issue slots (a warp's sub-partition is its index mod 4)
+    const int qw = (warp >> 2) * 3 + ((warp & 3) < (RW & 3) ? (warp & 3) : (warp & 3) - 1);
+    q8k_quantize_block(xn, E, xq_qs, xq_d, xq_bs, qw, NW / 4 * 3, lane, true);
     trace_stamp(a.trace, 6);
   }
 
