@@ -520,8 +520,10 @@ static int host_call_one(clb200_ctx *c, const DevLayer &dl, float *x, int *sel_o
   std::memcpy(h, x, xb);
   CUDA_OR(launch_stage_in(reinterpret_cast<const float *>(hd), dx, E, c->stream), "staging x");
   if (launch_one(c, L, dx, 0, nullptr, nullptr, nullptr, reinterpret_cast<int *>(hd + o_sel), reinterpret_cast<float *>(hd + o_wt),
-                 c->stream, err, errlen, nullptr, reinterpret_cast<float *>(hd + o_out), reinterpret_cast<int *>(hd + o_err)))
+                 c->stream, err, errlen, nullptr, reinterpret_cast<float *>(hd + o_out), reinterpret_cast<int *>(hd + o_err))) {
+    cudaStreamSynchronize(c->stream);   // the staging kernel may still read the staging, which the next call rewrites
     return 1;
+  }
   CUDA_OR(cudaStreamSynchronize(c->stream), "running the MoE block");
   if (report_device_error(c, *herr, err, errlen)) return 1;
   std::memcpy(x, h + o_out, xb);
