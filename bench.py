@@ -302,6 +302,7 @@ def run_reference_arm(a, wl, rank: int) -> None:
                 "data": "synthetic (seeded random GGUF)", "config": {"workload": wl["desc"]},
                 "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": round(cb["value"], 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        line["cpu_baseline"]["value"] = line["value"]   # the line's own value, as rounded
         print(json.dumps(line), flush=True)
         return
     if a.workload == "model":
@@ -316,6 +317,7 @@ def run_reference_arm(a, wl, rank: int) -> None:
                 "config": {"workload": wl["desc"]},
                 "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": round(cb["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        line["cpu_baseline"]["value"] = line["value"]   # the line's own value, as rounded
         print(json.dumps(line), flush=True)
         return
     secs = max(5.0, min(60.0, 2.0 * a.steps))
@@ -327,6 +329,7 @@ def run_reference_arm(a, wl, rank: int) -> None:
             "data": "synthetic (seeded)", "config": {"workload": wl["desc"], "tokens_per_call": wl["T"]},
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(cb["value"], 3), "unit": "layer-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    line["cpu_baseline"]["value"] = line["value"]
     print(json.dumps(line), flush=True)
 
 
