@@ -1,0 +1,108 @@
+"""Phase trace of the one-token MoE kernel (clb200_set_trace) over a chain of layers replayed from a CUDA graph.
+
+    python -m clutor_b200.trace [--layers 48] [--down q4_k]
+
+Each layer's launch gets its own trace buffer (32 entries per CTA): thread 0 of every CTA writes its SM's cycle counter at
+each phase boundary and the global nanosecond timer at entry and exit (decode.cu). The summary gives, per phase, the
+median over CTAs 0-127 and over the layers after the first eight of the cycles between consecutive boundaries, in
+microseconds at the SM clock the trace itself gives (cycles over global-timer nanoseconds from entry to exit); and,
+from the global timer, the launch span and the gap between launches.
+"""
+from __future__ import annotations
+
+import argparse
+
+import numpy as np
+
+# thread 0's boundaries in the order it passes them (decode.cu)
+PHASES = [
+    (1, "dependency wait"), (2, "x, sum of squares"), (3, "router rows landed"), (4, "rmsnorm, router products"),
+    (6, "Q8_K of xn"), (7, "all logits visible"), (8, "softmax max"), (9, "exponentials, double sum"), (10, "probabilities"),
+    (20, "barrier"), (21, "rank"), (11, "barrier"), (22, "renormalisation"), (23, "copy addresses"), (12, "copies issued"),
+    (25, "first expert slot landed"), (26, "first gate/up block"), (13, "gate/up rows"), (14, "hg rows released"),
+    (15, "all hg visible"), (16, "Q8_K of hg"), (17, "down rows landed"), (18, "down rows"), (19, "combine, residual"),
+]
+
+
+def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20) -> dict:
+    import torch
+
+    import clutor_b200 as cb
+    from clutor_b200 import synth
+
+    ctx = cb.Context(0)
+    try:
+        layers = [synth.device_layer(E=2048, FF=768, NE=128, K=8, gate_type=synth.T_Q4_K, down_type=synth.TYPE_NAMES[down],
+                                     seed=i + 1, router_scale=0.02) for i in range(n_layers)]
+        handles = [ctx.bind(L) for L in layers]
+        x0 = torch.from_numpy(synth.activations(1, 2048, seed=11)).cuda()
+        x = x0.clone()
+        sel = torch.zeros((n_layers, 1, 8), dtype=torch.int32, device="cuda")
+        wt = torch.zeros((n_layers, 1, 8), dtype=torch.float32, device="cuda")
+        G = torch.cuda.get_device_properties(0).multi_processor_count
+        tr = torch.zeros((n_layers, G, 32), dtype=torch.int64, device="cuda")
+        st = torch.cuda.Stream()
+
+        def step():
+            for i, h in enumerate(handles):
+                ctx.set_trace(tr[i])
+                ctx.moe_ffn_dev(h, x, sel[i], wt[i], stream=st)
+            ctx.set_trace(None)
+
+        with torch.cuda.stream(st):
+            step()
+        ctx.status()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            step()
+        for _ in range(5):
+            g.replay()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            ev0.record(st)
+            for _ in range(replays):
+                g.replay()
+            ev1.record(st)
+        torch.cuda.synchronize()
+        ctx.status()
+        us_per_layer = ev0.elapsed_time(ev1) * 1000.0 / replays / n_layers
+        t = tr.cpu().numpy().astype(np.int64)
+        del g
+    finally:
+        ctx.close()
+    lay = slice(min(8, n_layers - 1), n_layers - 1)
+    cta = slice(0, min(128, t.shape[1]))
+    # the SM clock from the trace itself: cycles between the first and last boundary over nanoseconds between entry and exit
+    mhz = float(np.median((t[lay, cta, 19] - t[lay, cta, 0]) / (t[lay, cta, 31] - t[lay, cta, 30]))) * 1000.0
+    to_us = 1.0 / mhz   # cycles -> us
+    rows, prev = [], 0
+    for b, name in PHASES:
+        d = (t[lay, cta, b] - t[lay, cta, prev]) * to_us
+        rows.append((name, float(np.median(d)), float(np.percentile(d, 90))))
+        prev = b
+    router = float(np.median((t[lay, cta, 5] - t[lay, cta, 4]) * to_us))
+    ent, ex = t[:, :, 30], t[:, :, 31]
+    span = float(np.median(((ex.max(1) - ent.min(1)) / 1000.0)[lay]))
+    gap = float(np.median(((ent[1:].min(1) - ex[:-1].max(1)) / 1000.0)[lay]))
+    return {"us_per_layer": us_per_layer, "sm_mhz": mhz, "phases": rows, "router_warp_us": router, "launch_span_us": span,
+            "gap_to_next_launch_us": gap}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--down", default="q4_k", choices=["q4_k", "q6_k"])
+    a = ap.parse_args()
+    r = run(a.layers, a.down)
+    print(f"{r['us_per_layer']:.2f} us per layer (CUDA events, traced graph), SM clock {r['sm_mhz']:.0f} MHz (from the trace)")
+    print("| phase (thread 0 of each CTA) | median us | p90 us |")
+    print("|---|---|---|")
+    for name, med, p90 in r["phases"]:
+        print(f"| {name} | {med:.3f} | {p90:.3f} |")
+    print(f"router warp (products done to logits stored): {r['router_warp_us']:.3f} us; launch span {r['launch_span_us']:.3f} us, "
+          f"gap to the next launch {r['gap_to_next_launch_us']:.3f} us")
+
+
+if __name__ == "__main__":
+    main()
