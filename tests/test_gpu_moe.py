@@ -95,6 +95,18 @@ def test_decode_full_size_chain(ctx, gt, dt):
     print(f"{gt}/{dt}: worst per-layer relative L2 {worst:.3e}, chain of 4 {e:.3e}")
 
 
+@pytest.mark.parametrize("T", [1, 3])
+def test_zero_activations(ctx, T):
+    """x = 0: every router logit is 0, so all experts tie and the lowest ids win; every Q8_K block has amax 0 (scale 0,
+    quants 0), and the update is exactly 0, as in the reference."""
+    L = synth.host_layer(E=1024, FF=512, NE=64, K=6, seed=5)
+    x = np.zeros((T, 1024), np.float32)
+    got, want = ctx.moe_ffn(L, x), oracle.moe_ffn(L, x, "oracle")
+    check(x, got, want, f"zero x, T={T}")
+    assert np.array_equal(got[1], np.tile(np.arange(6, dtype=got[1].dtype), (T, 1)))
+    assert not np.any(got[0])
+
+
 def test_repeated_calls_reset_their_counters(ctx):
     """The one-token kernel's cross-CTA counters are reset by its last CTA: many calls in a row stay correct."""
     L = synth.host_layer(E=1024, FF=512, NE=64, K=6, seed=9)
