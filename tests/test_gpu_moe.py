@@ -107,6 +107,18 @@ def test_zero_activations(ctx, T):
     assert not np.any(got[0])
 
 
+@pytest.mark.parametrize("T", [1, 5])
+def test_tied_router_rows(ctx, T):
+    """Experts 9 and 3 (and 40 and 12) have identical router rows, scaled up so they lead: their logits and probabilities
+    tie exactly, and the lower id must come first (the reference's repeated arg-max)."""
+    L = synth.host_layer(E=1024, FF=512, NE=64, K=6, seed=8)
+    L.router[3] = L.router[9] = 4.0 * L.router[0]
+    L.router[12] = L.router[40] = 3.0 * L.router[1]
+    x = synth.activations(T, 1024, seed=77)
+    got, want = ctx.moe_ffn(L, x), oracle.moe_ffn(L, x, "oracle")
+    check(x, got, want, f"tied rows, T={T}")
+
+
 def test_repeated_calls_reset_their_counters(ctx):
     """The one-token kernel's cross-CTA counters are reset by its last CTA: many calls in a row stay correct."""
     L = synth.host_layer(E=1024, FF=512, NE=64, K=6, seed=9)
