@@ -119,6 +119,15 @@ def test_tied_router_rows(ctx, T):
     check(x, got, want, f"tied rows, T={T}")
 
 
+@pytest.mark.parametrize("T", [1, 3])
+def test_smallest_shapes_every_expert_no_renorm(ctx, T):
+    """The smallest widths (one 256-block per row, one or two rows per CTA), every expert chosen (K = NE = 8), no
+    renormalisation of the weights and a residual scale of 0.5."""
+    L = synth.host_layer(E=256, FF=256, NE=8, K=8, seed=31, norm_topk=0, resid_scale=0.5)
+    x = synth.activations(T, 256, seed=32)
+    check(x, ctx.moe_ffn(L, x), oracle.moe_ffn(L, x, "oracle"), f"smallest, T={T}")
+
+
 def test_repeated_calls_reset_their_counters(ctx):
     """The one-token kernel's cross-CTA counters are reset by its last CTA: many calls in a row stay correct."""
     L = synth.host_layer(E=1024, FF=512, NE=64, K=6, seed=9)
