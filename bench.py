@@ -141,7 +141,7 @@ def cpu_reference(wl: dict, seconds: float, threads: int | None = None) -> dict:
     import oracle
     from clutor_b200 import synth
     if not oracle.ref_available():
-        oracle.build()
+        oracle.build(need_ref=True)
     nthreads = threads or min(os.cpu_count() or 1, 16)
     oracle.set_ref_threads(nthreads)
     L = synth.host_layer(E=wl["E"], FF=wl["FF"], NE=wl["NE"], K=wl["K"], gate_type=synth.TYPE_NAMES[wl["gate"]],
@@ -173,7 +173,7 @@ def model_reference(image, n_ctx: int, seconds: float, threads: int | None = Non
 
     import oracle
     if not oracle.ref_available():
-        oracle.build()
+        oracle.build(need_ref=True)
     nthreads = threads or min(os.cpu_count() or 1, 16)
     oracle.set_ref_threads(nthreads)
     image.tofile(SHM_MODEL)
@@ -207,7 +207,7 @@ def prompt_reference(image, P: int, threads: int | None = None) -> dict:
 
     import oracle
     if not oracle.ref_available():
-        oracle.build()
+        oracle.build(need_ref=True)
     nthreads = threads or min(os.cpu_count() or 1, 16)
     oracle.set_ref_threads(nthreads)
     image.tofile(SHM_MODEL)

@@ -129,6 +129,8 @@ def lib() -> C.CDLL:
         L.clb200_layer_release.argtypes = [C.c_void_p, C.c_int]
         L.clb200_moe_ffn_decode_noalloc.argtypes = [C.POINTER(MoELayer), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                                     C.c_char_p, C.c_size_t]
+        L.clb200_moe_dispatch.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
         L.clb200_device_bytes.restype = C.c_uint64
         L.clb200_device_bytes.argtypes = [C.c_void_p]
         L.clb200_set_trace.argtypes = [C.c_void_p, C.c_void_p]
@@ -299,6 +301,19 @@ class Context:
 
     def status(self) -> None:
         self._check(lib().clb200_status(self.handle, self._err, 512))
+
+    def dispatch(self, sel, wt, n_expert: int, stream=None):
+        """clb200_moe_dispatch on torch CUDA tensors sel [T, K] int32 and wt [T, K] float32. Returns device tensors
+        (todo [n_expert + 1], offsets [n_expert + 1], pos_token [T * K], pos_wt [T * K]); asynchronous."""
+        import torch
+        T, K = sel.shape
+        todo = torch.full((n_expert + 1,), -1, dtype=torch.int32, device=sel.device)
+        offsets = torch.full((n_expert + 1,), -1, dtype=torch.int32, device=sel.device)
+        pos_token = torch.full((T * K,), -1, dtype=torch.int32, device=sel.device)
+        pos_wt = torch.zeros((T * K,), dtype=torch.float32, device=sel.device)
+        self._check(lib().clb200_moe_dispatch(self.handle, T, n_expert, K, _ptr(sel), _ptr(wt), _ptr(todo), _ptr(offsets),
+                                              _ptr(pos_token), _ptr(pos_wt), C.c_void_p(_stream(stream)), self._err, 512))
+        return todo, offsets, pos_token, pos_wt
 
     def device_bytes(self) -> int:
         return int(lib().clb200_device_bytes(self.handle))

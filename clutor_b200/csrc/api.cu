@@ -19,7 +19,7 @@ namespace clb {
 struct Scratch {
   size_t off_logits, off_hg, off_x, off_sel, off_wt, total;
   // batched
-  size_t off_xn, off_xq_qs, off_xq_d, off_xq_bs, off_bsel, off_bwt, off_counts, off_offsets, off_first, off_pos_token,
+  size_t off_xn, off_xq_qs, off_xq_d, off_xq_bs, off_bsel, off_bwt, off_counts, off_offsets, off_first, off_todo, off_pos_token,
       off_pos_wt, off_slot_pos, off_bhg, off_hq_qs, off_hq_d, off_hq_bs, off_hd, off_xh, off_xl, off_hgh, off_hgl, off_xdh, off_xdl, off_rs;
 };
 
@@ -44,6 +44,7 @@ static Scratch plan_scratch(int T, int E, int FF, int NE, int K, bool batched) {
     s.off_counts = take(static_cast<size_t>(NE) * 4);
     s.off_offsets = take(static_cast<size_t>(NE + 1) * 4);
     s.off_first = take(static_cast<size_t>(NE) * 4);
+    s.off_todo = take(static_cast<size_t>(NE + 1) * 4);
     s.off_pos_token = take(TK * 4);
     s.off_pos_wt = take(TK * 4);
     s.off_slot_pos = take(TK * 4);
@@ -379,6 +380,7 @@ static BatchArgs batch_args(clb200_ctx *c, const clb200_moe_layer &L, float *x, 
   b.counts = reinterpret_cast<int *>(sc + s.off_counts);
   b.offsets = reinterpret_cast<int *>(sc + s.off_offsets);
   b.first = reinterpret_cast<int *>(sc + s.off_first);
+  b.todo = reinterpret_cast<int *>(sc + s.off_todo);
   b.pos_token = reinterpret_cast<int *>(sc + s.off_pos_token);
   b.pos_wt = reinterpret_cast<float *>(sc + s.off_pos_wt);
   b.slot_pos = reinterpret_cast<int *>(sc + s.off_slot_pos);
@@ -480,6 +482,33 @@ int clb200_ep_experts(clb200_ctx *c, int layer, int T, const int8_t *xq_qs, cons
   b.xq_bs = const_cast<int16_t *>(xq_bs);
   const int rc = launch_experts(b, stream ? static_cast<cudaStream_t>(stream) : c->stream);
   if (rc) { errf(err, errlen, "launching the expert kernels: %s", cudaGetErrorString(static_cast<cudaError_t>(rc))); return 1; }
+  return 0;
+}
+
+int clb200_moe_dispatch(clb200_ctx *c, int T, int n_expert, int n_used, const int *sel, const float *wt, int *todo, int *offsets,
+                        int *pos_token, float *pos_wt, void *stream, char *err, size_t errlen) {
+  if (!c) { errf(err, errlen, "no context"); return 1; }
+  if (T < 1 || T > 32768 || n_expert < 1 || n_expert > DECODE_MAX_NE || n_used < 1 || n_used > DECODE_MAX_K || n_used > n_expert) {
+    errf(err, errlen, "dispatch of %d tokens, %d experts, %d used: takes 1 to 32768 tokens, at most %d experts and %d used", T,
+         n_expert, n_used, DECODE_MAX_NE, DECODE_MAX_K);
+    return 1;
+  }
+  if (!sel || !wt || !todo || !offsets || !pos_token || !pos_wt) { errf(err, errlen, "a buffer is missing"); return 1; }
+  cudaSetDevice(c->device);
+  const size_t TK = static_cast<size_t>(T) * n_used, o_first = al(static_cast<size_t>(n_expert) * 4),
+               o_slot = o_first + al(static_cast<size_t>(n_expert) * 4);
+  if (ensure_scratch(c, o_slot + al(TK * 4), err, errlen)) return 1;
+  BatchArgs b{};
+  b.T = T; b.NE = n_expert; b.K = n_used;
+  b.sel = const_cast<int *>(sel);
+  b.wt = const_cast<float *>(wt);
+  b.counts = reinterpret_cast<int *>(c->scratch);
+  b.first = reinterpret_cast<int *>(c->scratch + o_first);
+  b.slot_pos = reinterpret_cast<int *>(c->scratch + o_slot);
+  b.offsets = offsets; b.todo = todo; b.pos_token = pos_token; b.pos_wt = pos_wt;
+  b.err = c->small;
+  const int rc = launch_dispatch(b, stream ? static_cast<cudaStream_t>(stream) : c->stream);
+  if (rc) { errf(err, errlen, "launching the dispatch: %s", cudaGetErrorString(static_cast<cudaError_t>(rc))); return 1; }
   return 0;
 }
 

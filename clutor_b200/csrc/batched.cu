@@ -4,7 +4,8 @@
 //   router_kernel    per (8 tokens, 32 experts): the reference's dotf logits, each router row read once for the 8 tokens
 //   topk_kernel      per token: softmax (double sum), top-k by repeated arg-max with ties to the lower id, renormalisation
 //   dispatch_kernel  counting sort of the T*K (token, expert) slots by expert; each expert's tokens in ascending token order
-//                    (the reference's who[] list, c/src/forward.c:1189-1190), plus each expert's first appearance
+//                    (the reference's who[] list, c/src/forward.c:1189-1190), plus each expert's first appearance and the
+//                    experts in that order (the reference's todo[], c/src/forward.c:1163)
 //   gateup_kernel    per (expert, 16 rows): gate and up row dots for every token of that expert (weights read once, staged
 //                    in shared memory by a bulk copy), SwiGLU -> hg by dispatch position
 //   hq_kernel        Q8_K of each hg row (K-quant down weights)
@@ -258,8 +259,24 @@ __global__ void __launch_bounds__(1024) dispatch_kernel(const BatchArgs a) {
     if (lane == 0) off[NE] = base;
   }
   __syncthreads();
-  for (int e = tid; e < NE; e += blockDim.x) { a.counts[e] = cnt[e]; a.offsets[e] = off[e]; a.first[e] = first[e]; }
+  for (int e = tid; e < NE; e += blockDim.x) {
+    a.counts[e] = cnt[e];
+    a.offsets[e] = off[e];
+    a.first[e] = first[e];
+    if (a.todo && cnt[e] > 0) {   // todo position = experts with tokens that appeared earlier (first slots are distinct)
+      int r = 0;
+      for (int f = 0; f < NE; ++f) r += cnt[f] > 0 && first[f] < first[e];
+      a.todo[r] = e;
+    }
+  }
   if (tid == 0) a.offsets[NE] = off[NE];
+  if (a.todo && warp == 0) {
+    int n = 0;
+    for (int e = lane; e < NE; e += 32) n += cnt[e] > 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(FULL, n, o);
+    if (lane == 0) a.todo[NE] = n;
+  }
   for (int s = tid; s < T * K; s += blockDim.x) {
     const int t = s / K, e = a.sel[s];
     if (e < 0 || e >= NE) continue;
@@ -595,6 +612,15 @@ int launch_route(const BatchArgs &a, void *stream_) {
 int launch_batched(const BatchArgs &a, void *stream_) {
   const int rc = launch_route(a, stream_);
   return rc ? rc : launch_experts(a, stream_);
+}
+
+int launch_dispatch(const BatchArgs &a, void *stream_) {
+  const int nw = (a.T + 31) / 32;
+  const size_t disp_smem = static_cast<size_t>(a.NE) * nw * 8 + (3 * a.NE + 1) * 4;
+  if (disp_smem > 200 * 1024) return static_cast<int>(cudaErrorInvalidValue);   // tokens x experts beyond one CTA's bit matrix
+  cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  dispatch_kernel<<<1, 1024, disp_smem, static_cast<cudaStream_t>(stream_)>>>(a);
+  return static_cast<int>(cudaGetLastError());
 }
 
 int launch_experts(const BatchArgs &a, void *stream_) {

@@ -82,6 +82,8 @@ struct BatchArgs {
   int *counts;          // [NE]
   int *offsets;         // [NE + 1]
   int *first;           // [NE] first appearance (slot index t*K+k) of each expert
+  int *todo;            // [NE + 1] the experts with tokens in order of first appearance (the reference's todo[]), their count
+                        // at [NE]
   int *pos_token;       // [T * K] dispatch position -> token
   float *pos_wt;        // [T * K] dispatch position -> routing weight
   int *slot_pos;        // [T * K] (t, k) -> dispatch position
@@ -111,6 +113,8 @@ int launch_batched(const BatchArgs &a, void *stream);
 // Its two halves: rmsnorm + Q8_K + router + top-k (sel / wt), and everything from the dispatch on (given sel / wt / xq).
 int launch_route(const BatchArgs &a, void *stream);
 int launch_experts(const BatchArgs &a, void *stream);
+// The dispatch alone (sel / wt -> counts, offsets, first, todo, pos_token, pos_wt, slot_pos).
+int launch_dispatch(const BatchArgs &a, void *stream);
 // The Q8_0 / Q4_K expert products on tcgen05 (grouped_tc.cu): gate/up (writes hg, and hgh/hgl for Q8_0 down) or down
 // (writes hd).
 int launch_tc(const BatchArgs &a, void *stream, bool gateup);

@@ -6,6 +6,10 @@
 // inputs and outputs and cannot give this library a context with scratch. clb200_moe_ffn_decode_noalloc runs the same
 // one-token kernel as clb200_moe_ffn_dev with its scratch -- the router logits, the experts' hg rows, three grid counters
 // and the error word -- in a fixed array of this file that every device holds from the moment it loads the library.
+//
+// The array's device address is looked up once per device (on the first call with that device current) and kept for the
+// life of the process: after cudaDeviceReset the module is loaded again and the array may move, so this entry point must
+// not be used across a device reset.
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -17,6 +21,7 @@
 namespace clb {
 
 int plan_decode_shape(int sms, int max_smem, const clb200_moe_layer &L, DecodeArgs &a);   // api.cu
+int validate(const clb200_moe_layer *L, char *err, size_t errlen);                           // api.cu
 
 namespace {
 
@@ -30,6 +35,8 @@ struct DeviceSetup {
   bool ready = false;
   uint8_t *scratch = nullptr;   // device address of g_noalloc_scratch on this device
   int sms = 0, max_smem = 0;
+  const void *occ_fn = nullptr;   // the kernel and shared size last found to fit an SM on this device
+  uint32_t occ_smem = 0;
 };
 std::mutex g_setup_mu;
 DeviceSetup g_setup[64];
@@ -72,13 +79,10 @@ extern "C" int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x
     }
     su = s;
   }
+  // the checks of the context path first (widths 256..4096, types, gate/up sharing a type, slab sizes), then this entry
+  // point's own limits
+  if (validate(L, err, errlen)) return 1;
   const int E = L->n_embd, FF = L->n_ff_exp, NE = L->n_expert, K = L->n_used;
-  if (E < 256 || E % 256 || FF < 256 || FF % 256 || L->gate.rows != FF || L->gate.cols != E || L->up.rows != FF ||
-      L->up.cols != E || L->down.rows != E || L->down.cols != FF || !L->gate.p || !L->up.p || !L->down.p || !L->router_f ||
-      !L->ffn_norm_f) {
-    errf(err, errlen, "layer shapes or tensors are inconsistent");
-    return 1;
-  }
   if (NE < 1 || NE > 128 || K < 1 || K > NE || static_cast<size_t>(K) * FF > NOALLOC_MAX_HG) {
     errf(err, errlen, "%d experts, %d used, expert width %d: the allocation-free entry point takes at most 128 experts and "
          "n_used * n_ff_exp <= %zu (its fixed scratch is %zu bytes)", NE, K, FF, NOALLOC_MAX_HG, NOALLOC_BYTES);
@@ -88,6 +92,21 @@ extern "C" int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x
   if (plan_decode_shape(su.sms, su.max_smem, *L, a)) {
     errf(err, errlen, "this layer shape or weight type is not one the one-token kernel takes (K-quant experts, at most 16 used)");
     return 1;
+  }
+  const DecodeFn fn = decode_kernel_for(L->gate.type, L->down.type);
+  {
+    std::lock_guard<std::mutex> lock(g_setup_mu);   // checked once per device, kernel and shared size
+    DeviceSetup &s = g_setup[dev];
+    if (reinterpret_cast<const void *>(fn) != s.occ_fn || a.smem_bytes != s.occ_smem) {
+      int occ = 0;
+      const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, DECODE_THREADS, a.smem_bytes);
+      if (e != cudaSuccess || occ < 1) {
+        errf(err, errlen, "the one-token kernel does not fit on an SM of device %d (%u bytes of shared memory)", dev, a.smem_bytes);
+        return 1;
+      }
+      s.occ_fn = reinterpret_cast<const void *>(fn);
+      s.occ_smem = a.smem_bytes;
+    }
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   a.x_in = x; a.x_out = x;
@@ -115,13 +134,14 @@ extern "C" int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, decode_kernel_for(a.gate_type, a.down_type), a);
+  e = cudaLaunchKernelEx(&cfg, fn, a);
   if (e != cudaSuccess) { errf(err, errlen, "launching the one-token kernel: %s", cudaGetErrorString(e)); return 1; }
+  // the error word comes back on the caller's stream (a copy on the legacy stream would also wait for other streams' work)
+  int code = 0;
+  e = cudaMemcpyAsync(&code, su.scratch, sizeof code, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) { errf(err, errlen, "reading the device error word: %s", cudaGetErrorString(e)); return 1; }
   e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) { errf(err, errlen, "running the one-token kernel: %s", cudaGetErrorString(e)); return 1; }
-  int code = 0;
-  e = cudaMemcpy(&code, su.scratch, sizeof code, cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) { errf(err, errlen, "reading the device error word: %s", cudaGetErrorString(e)); return 1; }
   if (code) { errf(err, errlen, "device error %d (a bounded wait ran out)", code); return 1; }
   return 0;
 }

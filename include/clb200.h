@@ -89,9 +89,20 @@ int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, floa
  * n_used * n_ff_exp <= 16384; larger layers are refused with a message. The first call on a device locates the array and
  * sets the kernel's shared-memory limit on that device (make it before any stream capture). Synchronous: it returns after
  * the kernel, with the device's error word read. Every call shares the one array, so calls that overlap on the GPU (from
- * several host threads or streams) race; serialise them. 0 on success, 1 with err set otherwise. */
+ * several host threads or streams) race; serialise them. The array's address is looked up once per device and kept, so do
+ * not use this entry point across a cudaDeviceReset. The layer is checked as clb200_layer_bind checks it (widths 256..4096,
+ * gate and up of one type, slab sizes) before anything is launched. 0 on success, 1 with err set otherwise. */
 int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x, int *sel_out, float *wt_out, void *stream, char *err,
                                   size_t errlen);
+/* The dispatch step of the batched block on its own (c/src/forward.c:1162-1163 and :1188-1189), on DEVICE pointers: the
+ * routing of T tokens, sel / wt [T x n_used] (expert ids, -1 never), becomes the reference's per-expert work lists.
+ * todo [n_expert + 1] receives the experts that have tokens in order of first appearance in sel (the reference's todo[])
+ * and, at todo[n_expert], how many there are; offsets [n_expert + 1] the start of expert e's entries in pos_token / pos_wt
+ * [T x n_used] (offsets[n_expert] = the total), which hold its tokens in ascending order and their routing weights (the
+ * reference's who[] / wgt[] for that expert). T up to 32768 (while n_expert x T / 32 words fit one CTA's shared memory).
+ * Asynchronous on `stream` (NULL: the context's stream); an expert id out of range is reported by clb200_status. */
+int clb200_moe_dispatch(clb200_ctx *c, int T, int n_expert, int n_used, const int *sel, const float *wt, int *todo,
+                        int *offsets, int *pos_token, float *pos_wt, void *stream, char *err, size_t errlen);
 /* ---- expert parallelism: the two halves of the batched block, around an exchange ------------------------------------------
  * No single counterpart in the reference (it runs on one machine); together with an all-to-all they are its batched block
  * (c/src/forward.c:1132-1210) with the experts spread over GPUs. Asynchronous on `stream`; K-quant gate/up experts; T up to

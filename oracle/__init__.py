@@ -20,7 +20,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libclref.so")
-REF_DIR_DEFAULT = "/root/reference/c/src"
+
+def ref_dir() -> str | None:
+    """The reference engine's c/src directory, from the CLUTOR_REF_DIR environment variable (None when it is unset)."""
+    d = os.environ.get("CLUTOR_REF_DIR")
+    return d or None
 
 T_F32, T_F16, T_Q8_0, T_Q4_K, T_Q6_K = 0, 1, 8, 12, 14
 
@@ -37,13 +41,17 @@ class Layer(C.Structure):
     ]
 
 
-def build(ref_dir: str | None = None, quiet: bool = True) -> None:
-    """Compiles liboracle.so, and _ref/libclref.so when the reference sources are present."""
-    ref_dir = ref_dir or os.environ.get("CLUTOR_REF_DIR", REF_DIR_DEFAULT)
+def build(src: str | None = None, quiet: bool = True, need_ref: bool = False) -> None:
+    """Compiles liboracle.so, and _ref/libclref.so from the reference's c/src directory `src` (default: CLUTOR_REF_DIR).
+    Without a directory only liboracle.so is built; with need_ref that is an error."""
+    src = src or ref_dir()
     out = subprocess.DEVNULL if quiet else None
     subprocess.run(["make", "-C", HERE, "liboracle.so"], check=True, stdout=out)
-    if os.path.isdir(ref_dir):
-        subprocess.run(["make", "-C", HERE, "ref", f"REF_DIR={ref_dir}"], check=True, stdout=out)
+    if src and os.path.isdir(src):
+        subprocess.run(["make", "-C", HERE, "ref", f"REF_DIR={src}"], check=True, stdout=out)
+    elif need_ref and not ref_available():
+        raise RuntimeError("oracle/_ref is not built and no reference sources are given: set CLUTOR_REF_DIR to the "
+                           "reference engine's c/src directory")
 
 
 _libs: dict[str, C.CDLL] = {}
@@ -190,6 +198,38 @@ def moe_ffn(layer, x: np.ndarray, which: str = "oracle"):
     if rc:
         raise RuntimeError(f"{which} moe_ffn failed")
     return x, sel, wt
+
+
+def ref_route_batch(layer, x: np.ndarray):
+    """The reference's routing of T tokens alone (rmsnorm, dotf, softmax, top-k, renormalisation; c/src/forward.c:1065-1072,
+    1135-1157): (sel [T, K] int32, wt [T, K] float32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T = x.shape[0]
+    sel = np.zeros((T, layer.K), np.int32)
+    wt = np.zeros((T, layer.K), np.float32)
+    s = make_struct(layer)
+    if ref_lib().ref_route_batch(C.byref(s), C.c_void_p(_ptr(x)), T, C.c_void_p(_ptr(sel)), C.c_void_p(_ptr(wt))):
+        raise RuntimeError("ref_route_batch failed")
+    return sel, wt
+
+
+def ref_dispatch(sel: np.ndarray, wt: np.ndarray, n_expert: int):
+    """The batched block's dispatch as the reference forms it (c/src/forward.c:1162-1163, 1188-1189): returns (todo, lists)
+    with todo the experts in order of first appearance and lists[e] = (who, wgt) for each of them: its tokens ascending and
+    their weights."""
+    sel = np.ascontiguousarray(sel, dtype=np.int32)
+    wt = np.ascontiguousarray(wt, dtype=np.float32)
+    T, K = sel.shape
+    todo = np.zeros(n_expert, np.int32)
+    woff = np.zeros(n_expert + 1, np.int32)
+    who = np.zeros(T * K, np.int32)
+    wgt = np.zeros(T * K, np.float32)
+    n = ref_lib().ref_dispatch(C.c_void_p(_ptr(sel)), C.c_void_p(_ptr(wt)), T, K, n_expert, C.c_void_p(_ptr(todo)),
+                               C.c_void_p(_ptr(woff)), C.c_void_p(_ptr(who)), C.c_void_p(_ptr(wgt)))
+    if n < 0:
+        raise RuntimeError("ref_dispatch failed")
+    lists = {int(todo[i]): (who[woff[i]:woff[i + 1]].copy(), wgt[woff[i]:woff[i + 1]].copy()) for i in range(n)}
+    return todo[:n].copy(), lists
 
 
 def set_ref_threads(n: int) -> None:

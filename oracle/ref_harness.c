@@ -73,15 +73,52 @@ static int decode_one(const ref_layer *L, float *x, int *sel, float *wt) {
   return ok ? 0 : 1;
 }
 
+/* The batched block's dispatch, statement for statement: todo[] = the experts in order of first appearance over the
+ * (token, rank) slots (c/src/forward.c:1162-1163); for todo[i], who[] / wgt[] = the tokens that chose it, ascending, with the
+ * weight of the first slot naming it (:1188-1189). Here the per-expert lists are laid end to end: todo[i]'s entries are
+ * [woff[i], woff[i+1]) of who / wgt. Returns the number of experts in todo. */
+static int dispatch_lists(const int *sel, const float *wt, int nb, int NU, int NE, int *todo, int *woff, int *who, float *wgt) {
+  char *seen = calloc((size_t)NE, 1);
+  int n_todo = 0;
+  if (!seen) return -1;
+  for (int b = 0; b < nb; b++) for (int k = 0; k < NU; k++) { const int e = sel[(size_t)b * NU + k]; if (!seen[e]) { seen[e] = 1; todo[n_todo++] = e; } }
+  int ni = 0;
+  for (int i = 0; i < n_todo; i++) {
+    const int e = todo[i];
+    woff[i] = ni;
+    for (int b = 0; b < nb; b++) for (int k = 0; k < NU; k++) if (sel[(size_t)b * NU + k] == e) { who[ni] = b; wgt[ni] = wt[(size_t)b * NU + k]; ni++; break; }
+  }
+  woff[n_todo] = ni;
+  free(seen);
+  return n_todo;
+}
+
+int ref_dispatch(const int *sel, const float *wt, int nb, int NU, int NE, int *todo, int *woff, int *who, float *wgt) {
+  return dispatch_lists(sel, wt, nb, NU, NE, todo, woff, who, wgt);
+}
+
+/* Routing alone for T tokens (the batched block's route step and per-token softmax/top-k, c/src/forward.c:1065-1072 and
+ * :1135-1157): sel / wt [T x K]. */
+int ref_route_batch(const ref_layer *L, const float *X, int T, int *sel, float *wt) {
+  float *xn = malloc((size_t)L->E * 4), *rl = malloc((size_t)L->NE * 4);
+  if (!xn || !rl) { free(xn); free(rl); return 1; }
+  for (int b = 0; b < T; b++) {
+    rmsnorm(xn, X + (size_t)b * L->E, L->ffn_norm, L->E, L->rms_eps);
+    for (int e = 0; e < L->NE; e++) rl[e] = dotf(L->router + (size_t)e * L->E, xn, L->E);
+    route_one(rl, L->NE, L->K, L->norm_topk, sel + (size_t)b * L->K, wt + (size_t)b * L->K);
+  }
+  free(xn); free(rl);
+  return 0;
+}
+
 static int batch(const ref_layer *L, float *X, int nb, int *sel, float *wt) {
   const int E = L->E, FF = L->FF, NE = L->NE, NU = L->K;
   float *XN = malloc((size_t)nb * E * 4), *XG = malloc((size_t)nb * E * 4), *MOE = calloc((size_t)nb * E, 4), *rl = malloc((size_t)NE * 4);
   float *HG = malloc((size_t)nb * FF * 4), *HU = malloc((size_t)nb * FF * 4), *HDE = malloc((size_t)nb * E * 4);
   cl_xq *xqe = calloc((size_t)nb, sizeof(cl_xq)), *xqf = calloc((size_t)nb, sizeof(cl_xq)), *sub = calloc((size_t)nb, sizeof(cl_xq));
-  int *who = malloc((size_t)nb * sizeof(int)), *todo = malloc((size_t)NE * sizeof(int));
-  float *wgt = malloc((size_t)nb * 4);
-  char *seen = calloc((size_t)NE, 1);
-  int ok = XN && XG && MOE && rl && HG && HU && HDE && xqe && xqf && sub && who && todo && wgt && seen;
+  int *who = malloc((size_t)nb * NU * sizeof(int)), *todo = malloc((size_t)NE * sizeof(int)), *woff = malloc((size_t)(NE + 1) * sizeof(int));
+  float *wgt = malloc((size_t)nb * NU * 4);
+  int ok = XN && XG && MOE && rl && HG && HU && HDE && xqe && xqf && sub && who && todo && woff && wgt;
   for (int b = 0; ok && b < nb; b++) ok = cl_xq_init(&xqe[b], E) && cl_xq_init(&xqf[b], FF);
   if (ok) {
     for (int b = 0; b < nb; b++) {   /* route_task (c/src/forward.c:1065-1072), then the per-token softmax/top-k (:1135-1157) */
@@ -91,13 +128,13 @@ static int batch(const ref_layer *L, float *X, int nb, int *sel, float *wt) {
       for (int e = 0; e < NE; e++) rl[e] = dotf(L->router + (size_t)e * E, xn, E);
       route_one(rl, NE, NU, L->norm_topk, sel + (size_t)b * NU, wt + (size_t)b * NU);
     }
-    int n_todo = 0;
-    for (int b = 0; b < nb; b++) for (int k = 0; k < NU; k++) { const int e = sel[(size_t)b * NU + k]; if (!seen[e]) { seen[e] = 1; todo[n_todo++] = e; } }
+    const int n_todo = dispatch_lists(sel, wt, nb, NU, NE, todo, woff, who, wgt);
+    ok = n_todo >= 0;
     for (int i = 0; i < n_todo; i++) {
-      const int e = todo[i];
-      int ni = 0;
-      for (int b = 0; b < nb; b++) for (int k = 0; k < NU; k++) if (sel[(size_t)b * NU + k] == e) { who[ni] = b; wgt[ni] = wt[(size_t)b * NU + k]; ni++; break; }
-      for (int t = 0; t < ni; t++) { sub[t] = xqe[who[t]]; memcpy(XG + (size_t)t * E, XN + (size_t)who[t] * E, (size_t)E * 4); }
+      const int e = todo[i], ni = woff[i + 1] - woff[i];
+      const int *whoi = who + woff[i];
+      const float *wgti = wgt + woff[i];
+      for (int t = 0; t < ni; t++) { sub[t] = xqe[whoi[t]]; memcpy(XG + (size_t)t * E, XN + (size_t)whoi[t] * E, (size_t)E * 4); }
       cl_mv j[2] = {{L->gate_type, L->gate + (size_t)e * L->gate_slab, FF, E, XG, sub, HG, ni, (size_t)E, (size_t)FF},
                     {L->up_type, L->up + (size_t)e * L->up_slab, FF, E, XG, sub, HU, ni, (size_t)E, (size_t)FF}};
       cl_matvec_batch(j, 2);
@@ -108,12 +145,12 @@ static int batch(const ref_layer *L, float *X, int nb, int *sel, float *wt) {
       }
       cl_mv d = {L->down_type, L->down + (size_t)e * L->down_slab, E, FF, HG, xqf, HDE, ni, (size_t)FF, (size_t)E};
       cl_matvec_batch(&d, 1);
-      for (int t = 0; t < ni; t++) { float *m = MOE + (size_t)who[t] * E; const float *h = HDE + (size_t)t * E; for (int q = 0; q < E; q++) m[q] += wgt[t] * h[q]; }
+      for (int t = 0; t < ni; t++) { float *m = MOE + (size_t)whoi[t] * E; const float *h = HDE + (size_t)t * E; for (int q = 0; q < E; q++) m[q] += wgti[t] * h[q]; }
     }
     for (size_t i = 0; i < (size_t)nb * E; i++) X[i] += L->resid_scale * MOE[i];
   }
   for (int b = 0; b < nb; b++) { if (xqe) cl_xq_free(&xqe[b]); if (xqf) cl_xq_free(&xqf[b]); }
-  free(XN); free(XG); free(MOE); free(rl); free(HG); free(HU); free(HDE); free(xqe); free(xqf); free(sub); free(who); free(todo); free(wgt); free(seen);
+  free(XN); free(XG); free(MOE); free(rl); free(HG); free(HU); free(HDE); free(xqe); free(xqf); free(sub); free(who); free(todo); free(woff); free(wgt);
   return ok ? 0 : 1;
 }
 

@@ -9,6 +9,13 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 
+# The reference engine's sources, where this machine has them (the CPU tests that compile against its headers, and the
+# on-demand build of oracle/_ref, read them there); a GPU machine without them uses the prebuilt oracle/_ref.
+REFERENCE_SRC = "/root/reference/c/src"
+if not os.environ.get("CLUTOR_REF_DIR") and os.path.isdir(REFERENCE_SRC):
+    os.environ["CLUTOR_REF_DIR"] = REFERENCE_SRC
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (a B200)")
 
@@ -16,7 +23,7 @@ def pytest_configure(config):
 @pytest.fixture(scope="session", autouse=True)
 def _oracle_built():
     import oracle
-    if not os.path.exists(oracle.ORACLE_SO) or (not oracle.ref_available() and os.path.isdir(oracle.REF_DIR_DEFAULT)):
+    if not os.path.exists(oracle.ORACLE_SO) or (not oracle.ref_available() and oracle.ref_dir()):
         oracle.build()
     yield
 

@@ -33,7 +33,7 @@ def test_ctypes_mirror_matches_header():
     assert C.sizeof(cb.MV) == 72
 
 
-@pytest.mark.skipif(not os.path.isdir(oracle.REF_DIR_DEFAULT), reason="needs the reference headers")
+@pytest.mark.skipif(not (oracle.ref_dir() and os.path.isdir(oracle.ref_dir())), reason="needs the reference headers (CLUTOR_REF_DIR)")
 def test_struct_layouts_equal_the_reference():
     """clb200_w / clb200_q8k / clb200_xq / clb200_mv / clb200_backend_t / clb200_smart / clb200_route_result have the layout of
     the reference's cl_w (forward.h:18), cl_q8k / cl_xq / cl_mv (quant.h:22-34), cl_backend (backend.h:9-13), cl_smart and
@@ -65,7 +65,7 @@ int main(void) {
         c = os.path.join(d, "layout.c")
         exe = os.path.join(d, "layout")
         open(c, "w").write(src)
-        subprocess.run(["gcc", "-std=c11", f"-I{ROOT}/include", f"-I{oracle.REF_DIR_DEFAULT}", c, "-o", exe], check=True)
+        subprocess.run(["gcc", "-std=c11", f"-I{ROOT}/include", f"-I{oracle.ref_dir()}", c, "-o", exe], check=True)
         out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout
     for line in out.strip().splitlines():
         name, a, b = line.split()

@@ -68,3 +68,39 @@ def test_noalloc_refuses_layers_beyond_its_scratch():
     x = torch.zeros((1, 256), device="cuda")
     rc = lib.clb200_moe_ffn_decode_noalloc(C.byref(s), x.data_ptr(), None, None, None, err, 512)
     assert rc == 1 and b"n_used * n_ff_exp" in err.value
+
+
+def _refused(s, x):
+    import clutor_b200 as cb
+    err = C.create_string_buffer(512)
+    before = x.clone()
+    rc = cb.lib().clb200_moe_ffn_decode_noalloc(C.byref(s), x.data_ptr(), None, None, None, err, 512)
+    import torch
+    torch.cuda.synchronize()
+    assert rc == 1, "the entry point accepted a layer it cannot run"
+    assert torch.equal(x, before), "the kernel ran on a refused layer"
+    return err.value.decode()
+
+
+def test_noalloc_refuses_what_the_context_path_refuses():
+    """Widths beyond the kernel's 4096, gate and up of different types, and slab sizes that do not match rows x row bytes
+    are refused before anything is launched, with the context path's messages."""
+    import torch
+
+    import clutor_b200 as cb
+    layer = synth.device_layer(E=512, FF=256, NE=16, K=4, seed=6)
+    x = torch.ones((1, 512), device="cuda")
+    s = cb.layer_struct(layer)                       # E = 8192 with K = 1: fits the scratch, not the kernel
+    s.n_embd, s.n_used = 8192, 1
+    s.gate.cols = s.up.cols = s.down.rows = 8192
+    assert "between 256 and 4096" in _refused(s, x)
+    s = cb.layer_struct(layer)                       # FF = 8192 with K = 1
+    s.n_ff_exp, s.n_used = 8192, 1
+    s.gate.rows = s.up.rows = s.down.cols = 8192
+    assert "between 256 and 4096" in _refused(s, x)
+    s = cb.layer_struct(layer)                       # a Q4_K gate with a Q6_K up
+    s.up.type = synth.T_Q6_K
+    assert "share a type" in _refused(s, x)
+    s = cb.layer_struct(layer)                       # a gate slab one row short
+    s.gate_slab -= 144 * 2
+    assert "slab sizes" in _refused(s, x)
