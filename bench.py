@@ -228,7 +228,7 @@ def prompt_reference(image, P: int, threads: int | None = None) -> dict:
                       f"{nthreads} threads; built from its sources (oracle/_ref), model mapped from /dev/shm"}
 
 
-def run_prompt(a, wl: dict) -> None:
+def run_prompt(a, wl: dict) -> dict:
     """The batched prompt path of the whole model: a step is one P-token prompt from position 0 (clb200_model_prefill, batches
     of wl["T"] tokens), logits of the last token copied out. The call is synchronous (one synchronization per batch), so it is
     timed on the host clock around the call, after a device synchronize; there are no inputs but the token ids."""
@@ -285,9 +285,9 @@ def run_prompt(a, wl: dict) -> None:
             "e2e": {"value": round(P / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * P, "d2h_bytes_per_step": 4 * spec.vocab,
                     "api": "clb200_model_prefill (host token ids in, host logits out)"},
             "gpu_launches": None, "clocks": clk.summary()}
-    print(json.dumps(line), flush=True)
     model.close()
     ctx.close()
+    return line
 
 
 def run_reference_arm(a, wl, rank: int) -> None:
@@ -326,14 +326,14 @@ def run_reference_arm(a, wl, rank: int) -> None:
             "value": round(cb["value"], 3), "unit": "layer-tokens/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": round(cb["ms_per_call"], 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate" if wl["gate"] != "q8_0" else "f32",
-            "data": "synthetic (seeded)", "config": {"workload": wl["desc"], "tokens_per_call": wl["T"]},
+            "data": "synthetic (seeded)", "config": layers_config(wl, int(os.environ.get("WORLD_SIZE", "1"))),
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(cb["value"], 3), "unit": "layer-tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     line["cpu_baseline"]["value"] = line["value"]
     print(json.dumps(line), flush=True)
 
 
-def run_cache(a, wl: dict) -> None:
+def run_cache(a, wl: dict) -> dict:
     """The expert-cache stress workload through the HBM expert store. A step is one decode token through every layer; the
     routing of each (token, layer) comes from the reference stress harness's synthetic router (c/src/stream.c:114-140,
     restated in clutor_b200.synth.ExpertStream), top-8 of its logits, and the predictor's logits (correlation 0.8) choose
@@ -465,33 +465,36 @@ def run_cache(a, wl: dict) -> None:
             "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0,
                     "note": "the step is host-driven already: routing on the host, the public C entry point per layer"},
             "gpu_launches": NL * a.steps, "clocks": clk.summary()}
-    print(json.dumps(line), flush=True)
     store.close()
     ctx.close()
+    del store, ctx
+    torch.cuda.empty_cache()
+    return line
 
 
-def run_ep(a, wl: dict) -> None:
-    """Expert-parallel MoE layers of the Qwen3-235B-A22B shape: each of the N ranks (one per GPU) holds the router and
-    128/N experts of every layer and routes its own 2048 tokens; a step is those tokens through `layers` layers (one
-    all-to-all each way per layer). Weak scaling: value = all ranks' layer-tokens / the slowest rank's time."""
-    import datetime
+EP_METRIC = "MoE-layer tokens/s (Qwen3-235B-A22B layer, prefill 2048 tokens/GPU, Q4_K, expert-parallel)"
 
+
+def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=None, layers: int | None = None,
+               clocks: bool = False) -> dict | None:
+    """Expert-parallel MoE layers of the Qwen3-235B-A22B shape on the `world` ranks of the process
+    group, one per GPU: each rank holds the router and 128/N experts of every layer. A step is one pass of the tokens through
+    `layers` layers, one all-to-all each way per layer (NCCL over NVLink). Two runs: weak scaling (2048 tokens routed by
+    every rank) and strong scaling (the config's one 2048-token prefill split over the ranks). Rank 0 also times the phases
+    of one step, counts the bytes it sends to the other ranks, and checks its tokens of layer 0 against the single-GPU
+    block on the whole layer (top-k identical, relative L2 <= 1e-5). Every rank takes the same collective steps; rank 0
+    returns the summary, the others None."""
+    import numpy as np
     import torch
-    import torch.distributed as dist
 
     import clutor_b200 as cb
     from clutor_b200 import ep, synth
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-    T, NL, K, E, FF, NE = wl["T"], wl["layers"], wl["K"], wl["E"], wl["FF"], wl["NE"]
+    wl = WORKLOADS["ep235b"]
+    T, NL, K, E, FF, NE = wl["T"], layers or wl["layers"], wl["K"], wl["E"], wl["FF"], wl["NE"]
     n_local = NE // world
     ctx = cb.Context(local)
-    comps, keep = [], []
+    comps, keep, full0 = [], [], None
     for i in range(NL):
         L = synth.device_layer(E=E, FF=FF, NE=NE, K=K, gate_type=synth.TYPE_NAMES[wl["gate"]],
                                down_type=synth.TYPE_NAMES[wl["down"]], seed=i + 1, router_scale=0.02)
@@ -503,66 +506,141 @@ def run_ep(a, wl: dict) -> None:
         shard_layer = mk(n_local, sh.router.clone())
         keep.append((route_layer, shard_layer))
         comps.append(ep.GpuCompute(ctx, ctx.bind(route_layer), ctx.bind(shard_layer), E, K))
+        if i == 0 and rank == 0:
+            full0 = (L, ctx.bind(L))                # rank 0 keeps layer 0 whole for the parity check
         del L, sh
         torch.cuda.empty_cache()
-    x0 = torch.from_numpy(synth.activations(T, E, seed=11 + rank)).cuda()
-    x = x0.clone()
-    phases: dict = {}
 
-    def step(timed=None):
-        x.copy_(x0)
-        for c in comps:
-            ep.moe_layer(x, c, n_local, 1.0, timings=timed)
+    def timed_run(Tr: int, seed: int):
+        x0 = torch.from_numpy(synth.activations(Tr, E, seed=seed + rank)).cuda()
+        x = x0.clone()
 
-    for _ in range(a.warmup):
-        step()
-    torch.cuda.synchronize()
-    ctx.status()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with Clocks(local) as clk:
+        def step(timed=None):
+            x.copy_(x0)
+            for c in comps:
+                ep.moe_layer(x, c, n_local, 1.0, timings=timed)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        ctx.status()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
         ev0.record()
-        for _ in range(a.steps):
+        for _ in range(steps):
             step()
         ev1.record()
         torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    ctx.status()
-    step(phases)   # one more step with the phase events (not timed above)
+        ms = ev0.elapsed_time(ev1)
+        ctx.status()
+        phases: dict = {}
+        step(phases)   # one more step with the phase events (not timed above)
+        torch.cuda.synchronize()
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, phases
+
+    with Clocks(local) if clocks else _NoClocks() as clk:
+        ms_w, ph_w = timed_run(T, 11)
+        ms_s, ph_s = timed_run(T // world, 31)
+    parity = None
+    if dist:
+        dist.barrier()
+    # the parity step is a collective (every rank runs layer 0 on 256 tokens of its own); rank 0 checks its tokens against
+    # the whole layer on its own GPU
+    xr = torch.from_numpy(synth.activations(256, E, seed=77 + rank)).cuda()
+    xe = xr.clone()
+    sel_e, _ = ep.moe_layer(xe, comps[0], n_local, 1.0)
     torch.cuda.synchronize()
-    ph = {k: round(sum(ev[0].elapsed_time(ev[1]) for ev in v) / NL, 3) for k, v in phases.items() if k != "rows"}
-    rows = phases.get("rows", [0])
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = NL * T * a.steps * world / (ms / 1000.0)
-    flop = T * K * 3 * 2 * E * FF                      # per layer per rank (weak scaling: each rank's assignments)
-    achieved = flop * NL * a.steps / (ms / 1000.0) / 1e12
-    pk, pk_kind = peaks()
-    if rank == 0:
-        line = {"metric": "MoE-layer tokens/s (Qwen3-235B-A22B layer, prefill 2048 tokens/GPU, Q4_K, expert-parallel)",
-                "value": round(value, 3), "unit": "layer-tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
-                "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "int8 dot (Q8_K x Q4_K), fp32 accumulate", "data": "synthetic (seeded random GGUF blocks)",
-                "config": {"workload": wl["desc"], "tokens_per_gpu": T, "layers_per_step": NL, "hidden": E, "experts": NE,
-                           "experts_per_gpu": n_local, "top_k": K, "ff": FF, "parallelism": f"ep{world}",
-                           "l2": f"inputs larger than L2: {NL} layers, {NE * E * FF * 3 * 144 / 256 / 1e9 * NL / world:.2f} GB of experts per GPU"},
-                "phases_ms_per_layer_rank0": ph, "rows_received_rank0": int(sum(rows) / max(len(rows), 1)),
-                "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk.get("bf16_tflops"), "unit": "TFLOP/s",
-                             "frac": round(achieved / pk.get("bf16_tflops", 1.0), 4), "traffic": None, "peak_kind": pk_kind,
-                             "note": "expert products as tcgen05 grouped GEMMs (fp16 hi/lo planes, 4 MMAs per algorithmic product); FLOPs counted algorithmically; bf16 dense peak"},
-                "cpu_baseline": None, "e2e": None, "gpu_launches": NL * a.steps * 9, "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
-    del comps
+    if full0 is not None:
+        L, h = full0
+        xb = xr.clone()
+        selb = torch.zeros((256, K), dtype=torch.int32, device="cuda")
+        ctx.moe_ffn_dev(h, xb, selb)
+        ctx.status()
+        err = float(torch.linalg.norm((xe - xb).double()) / torch.linalg.norm((xb - xr).double()))
+        parity = {"tokens": 256, "layer": 0, "topk_identical": bool(torch.equal(sel_e, selb)), "rel_l2": err,
+                  "bar": 1e-5, "ok": bool(torch.equal(sel_e, selb) and err <= 1e-5),
+                  "against": "the single-GPU block on the whole layer (clb200_moe_ffn_dev)"}
+    del comps, keep, full0
     ctx.close()
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    pk, pk_kind = peaks()
+
+    def summary(ms: float, Tr: int, ph: dict, scaling: str) -> dict:
+        value = NL * Tr * steps * world / (ms / 1000.0)
+        flop = Tr * K * 3 * 2 * E * FF * NL * steps * world   # algorithmic expert FLOPs of all ranks
+        achieved = flop / (ms / 1000.0) / 1e12 / world      # per GPU
+        per = {k: round(sum(ev[0].elapsed_time(ev[1]) for ev in v) / NL, 4) for k, v in ph.items() if k not in ("rows", "xbytes")}
+        xb = float(np.mean(ph.get("xbytes", [0])))
+        xms = per.get("dispatch", 0.0) + per.get("combine", 0.0)
+        return {"value": round(value, 3), "unit": "layer-tokens/s", "ms_per_step": round(ms / steps, 4), "scaling": scaling,
+                "tokens_per_gpu": Tr, "tokens_total": Tr * world, "phases_ms_per_layer_rank0": per,
+                "rows_received_rank0": int(np.mean(ph.get("rows", [0]))),
+                "exchange_rank0": {"bytes_per_layer": int(xb), "exchange_ms_per_layer": round(xms, 4),
+                                   "gbs": round(xb / (xms * 1e-3) / 1e9, 2) if xms > 0 else None,
+                                   "note": "bytes rank 0 sends to the other ranks per layer (dispatched Q8_K rows out, "
+                                           "partial sums back) over the dispatch + combine all-to-all time"},
+                "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk.get("bf16_tflops"),
+                             "unit": "TFLOP/s per GPU", "frac": round(achieved / pk.get("bf16_tflops", 1.0), 4),
+                             "peak_kind": pk_kind}}
+
+    return {"workload": wl["desc"], "metric": EP_METRIC, "n_gpus": world, "layers_per_step": NL, "steps": steps,
+            "warmup": warmup, "hidden": E, "experts": NE, "experts_per_gpu": n_local, "top_k": K, "ff": FF,
+            "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single (counts, rows, partial sums)",
+            "weak": summary(ms_w, T, ph_w, "weak"), "strong": summary(ms_s, T // world, ph_s, "strong"),
+            "parity_rank0": parity, "clocks": clk.summary() if clocks else None,
+            "gpu_launches_per_layer": 9, "dtype": "int8 dot (Q8_K x Q4_K) exact router; Q4_K experts on tcgen05 from fp16 hi/lo "
+            "operands, fp32 accumulate"}
+
+
+class _NoClocks:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def run_ep(a, wl: dict) -> None:
+    """The expert-parallel workload alone (--workload ep235b, under torchrun for N > 1): its weak-scaling figures as the
+    line's value."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    r = ep_measure(a.steps, a.warmup, rank, world, local, dist if world > 1 else None, layers=a.layers, clocks=True)
+    if rank == 0:
+        w = r["weak"]
+        line = {"metric": EP_METRIC, "value": w["value"], "unit": "layer-tokens/s", "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": w["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": r["dtype"], "data": "synthetic (seeded random GGUF blocks)",
+                "config": {"workload": wl["desc"], "tokens_per_gpu": wl["T"], "layers_per_step": r["layers_per_step"],
+                           "hidden": wl["E"], "experts": wl["NE"], "experts_per_gpu": r["experts_per_gpu"], "top_k": wl["K"],
+                           "ff": wl["FF"], "parallelism": f"ep{world}",
+                           "l2": f"inputs larger than L2: {r['layers_per_step']} layers, "
+                                 f"{wl['NE'] * wl['E'] * wl['FF'] * 3 * 144 / 256 / 1e9 * r['layers_per_step'] / world:.2f} GB of experts per GPU"},
+                "roofline": w["roofline"], "ep": r, "cpu_baseline": None, "e2e": None,
+                "gpu_launches": r["layers_per_step"] * a.steps * 9, "clocks": r["clocks"]}
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def run_model(a, wl: dict) -> None:
+def run_model(a, wl: dict, own_group: bool = True) -> dict | None:
     """The whole model, one token per step: the persistent one-step kernel (fwd.cu) replayed from a graph, each step
     feeding the previous step's greedy choice. Every rank runs its own replica (the model does not shard)."""
     import numpy as np
@@ -581,7 +659,8 @@ def run_model(a, wl: dict) -> None:
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        if own_group:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     spec = sm.QWEN3_30B_A3B
     if a.layers:   # a shorter stack of the same layers (small ncu captures); the default is the whole model
         spec = dataclasses.replace(spec, n_layer=a.layers)
@@ -654,62 +733,34 @@ def run_model(a, wl: dict) -> None:
                            "image_seconds": round(t_img, 1)},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": K, "clocks": clk.summary(),
                 "tokens": toks[:16]}
-        print(json.dumps(line), flush=True)
     model.close()
     ctx.close()
-    if dist:
+    del model, ctx, image
+    torch.cuda.empty_cache()
+    if dist and own_group:
         dist.destroy_process_group()
+    return line if rank == 0 else None
 
 
-def main() -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
-    ap.add_argument("--layers", type=int, default=None, help="distinct layers in the pool (default: the workload's)")
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--smart", default=None, help="cache workload: SMART-ROUTE J,M,TAU (for example 2,12,0.015)")
-    ap.add_argument("--batch", type=int, default=None, help="prompt workload: tokens per batch (the reference's CLUTOR_PS_B, 1..512)")
-    a = ap.parse_args()
-    wl = dict(WORKLOADS[a.workload])
-    if a.layers:
-        wl["layers"] = a.layers
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if a.impl == "reference":
-        run_reference_arm(a, wl, rank)
-        return
-    if a.workload == "cache":
-        run_cache(a, wl)
-        return
-    if a.workload == "prompt":
-        run_prompt(a, wl)
-        return
-    if a.workload == "ep235b":
-        run_ep(a, wl)
-        return
-    if a.workload == "model":
-        run_model(a, wl)
-        return
+def layers_config(wl: dict, world: int) -> dict:
+    """The config object of the layer-pool workloads (decode, prefill64), shared by both arms of the bench."""
+    from clutor_b200 import synth
+    g, d = synth.TYPE_NAMES[wl["gate"]], synth.TYPE_NAMES[wl["down"]]
+    expert = 2 * wl["FF"] * synth.row_bytes(g, wl["E"]) + wl["E"] * synth.row_bytes(d, wl["FF"])
+    return {"workload": wl["desc"], "tokens_per_call": wl["T"], "layers_per_step": wl["layers"], "hidden": wl["E"],
+            "experts": wl["NE"], "top_k": wl["K"], "ff": wl["FF"], "parallelism": f"replicas x{world}",
+            "l2": f"inputs larger than L2: {wl['layers']} distinct layers, {wl['layers'] * wl['NE'] * expert / 1e9:.1f} GB of experts"}
 
+
+def run_layers(a, wl: dict, rank: int, world: int, local: int, dist) -> dict | None:
+    """The layer-pool workloads (decode: BASELINE config 1; prefill64: config 2): a step is the tokens through `layers`
+    distinct layers, chained, replayed from a CUDA graph; every rank runs its own replica (the layer does not shard)."""
     import numpy as np
     import torch
 
     import clutor_b200 as cb
     from clutor_b200 import synth
 
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     T, NL, K = wl["T"], wl["layers"], wl["K"]
     ctx = cb.Context(local)
     layers = [synth.device_layer(E=wl["E"], FF=wl["FF"], NE=wl["NE"], K=K, gate_type=synth.TYPE_NAMES[wl["gate"]],
@@ -801,22 +852,103 @@ def main() -> None:
     if rank == 0 and not a.no_cpu_baseline:
         cpu = cpu_reference(wl, a.cpu_seconds)
         cpu.pop("ms_per_call", None)
+    line = None
     if rank == 0:
         line = {"metric": METRIC if a.workload == "decode" else METRIC.replace("decode", "T=64").replace("Q4_K", "Q8_0"),
                 "value": round(value, 3), "unit": "layer-tokens/s", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate" if wl["gate"] != "q8_0" else "f32",
-                "data": "synthetic (seeded random GGUF blocks)",
-                "config": {"workload": wl["desc"], "tokens_per_call": T, "layers_per_step": NL, "hidden": wl["E"],
-                           "experts": wl["NE"], "top_k": K, "ff": wl["FF"], "parallelism": f"replicas x{world}",
-                           "l2": f"inputs larger than L2: {NL} distinct layers, {NL * layers[0].NE * layers[0].expert_bytes / 1e9:.1f} GB of experts"},
+                "data": "synthetic (seeded random GGUF blocks)", "config": layers_config(wl, world),
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * a.steps,
                 "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
-    del graph
+    del graph, layers, handles
     ctx.close()
+    torch.cuda.empty_cache()
+    return line
+
+
+def secondary(a) -> list:
+    """The other configurations on one GPU, each as its own line (value, roofline, the reference's CPU figure, clocks) with
+    shorter runs: T = 64 with Q8_0 experts, the whole model's decode (config 3) and the expert-cache
+    stress (config 5, its 4096 decode steps)."""
+    out = []
+    for name, steps, warmup in (("prefill64", 20, 3), ("model", 32, 3), ("cache", 4096, 16)):
+        b = argparse.Namespace(**vars(a))
+        b.workload, b.steps, b.warmup, b.layers, b.cpu_seconds, b.smart = name, steps, warmup, None, 5.0, None
+        wl = dict(WORKLOADS[name])
+        t0 = time.perf_counter()
+        try:
+            line = {"prefill64": lambda: run_layers(b, wl, 0, 1, 0, None), "model": lambda: run_model(b, wl, own_group=False),
+                    "cache": lambda: run_cache(b, wl)}[name]()
+            line["workload"] = name
+            line["wall_s"] = round(time.perf_counter() - t0, 1)
+        except Exception as e:   # one configuration failing must not lose the headline line
+            line = {"workload": name, "error": f"{type(e).__name__}: {e}"}
+        out.append(line)
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--layers", type=int, default=None, help="distinct layers in the pool (default: the workload's)")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--smart", default=None, help="cache workload: SMART-ROUTE J,M,TAU (for example 2,12,0.015)")
+    ap.add_argument("--batch", type=int, default=None, help="prompt workload: tokens per batch (the reference's CLUTOR_PS_B, 1..512)")
+    ap.add_argument("--no-ep", action="store_true", help="decode workload: leave out the expert-parallel figures")
+    ap.add_argument("--no-secondary", action="store_true", help="decode workload at N=1: leave out the other configurations")
+    a = ap.parse_args()
+    wl = dict(WORKLOADS[a.workload])
+    if a.layers:
+        wl["layers"] = a.layers
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference_arm(a, wl, rank)
+        return
+    if a.workload == "cache":
+        print(json.dumps(run_cache(a, wl)), flush=True)
+        return
+    if a.workload == "prompt":
+        print(json.dumps(run_prompt(a, wl)), flush=True)
+        return
+    if a.workload == "ep235b":
+        run_ep(a, wl)
+        return
+    if a.workload == "model":
+        line = run_model(a, wl)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    line = run_layers(a, wl, rank, world, local, dist)
+    if a.workload == "decode" and not a.no_ep:   # the sharded configuration (config 4) at this N, every rank taking part
+        ep = ep_measure(5, 2, rank, world, local, dist)
+        if rank == 0:
+            line["ep"] = ep
+    if a.workload == "decode" and world == 1 and not a.no_secondary:
+        line["secondary"] = secondary(a)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if dist:
+        dist.barrier()
         dist.destroy_process_group()
+
 
 
 if __name__ == "__main__":

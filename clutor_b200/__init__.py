@@ -135,6 +135,7 @@ def lib() -> C.CDLL:
         L.clb200_device_bytes.argtypes = [C.c_void_p]
         L.clb200_set_trace.argtypes = [C.c_void_p, C.c_void_p]
         L.clb200_set_exact.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_set_option.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.clb200_backend.restype = C.POINTER(Backend)
         L.clb200_cache_new.restype = C.c_void_p
         L.clb200_cache_new.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.c_uint32]
@@ -321,6 +322,14 @@ class Context:
     def set_exact(self, on: bool) -> None:
         """clb200_set_exact: batched expert products on the integer path only (bit-exact), or on the tensor cores."""
         lib().clb200_set_exact(self.handle, int(on))
+
+    OPT_DECODE_KERNEL, OPT_TEST_SPECULATION_MISS = 1, 2
+
+    def set_option(self, option: int, value: int) -> None:
+        """clb200_set_option: OPT_DECODE_KERNEL (0 expert-group kernel where it fits, 1 grid-wide kernel, the default) or
+        the OPT_TEST_SPECULATION_MISS test hook."""
+        if lib().clb200_set_option(self.handle, option, int(value)):
+            raise ClutorError(f"option {option} = {value} refused")
 
     def set_trace(self, buf=None) -> None:
         """Phase trace of the one-token kernel (clb200_set_trace): buf is a torch uint64/int64 CUDA tensor of 32 entries per

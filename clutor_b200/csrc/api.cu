@@ -178,10 +178,65 @@ static const char *device_error_text(int code) {
   }
 }
 
+// The expert-group kernel (group.cu) on layer L and x (device), with the plan g already made.
+static int launch_group(clb200_ctx *c, const clb200_moe_layer &L, GroupArgs &g, float *x, int *sel_out, float *wt_out,
+                        cudaStream_t st, char *err, size_t errlen, float *x_out, int *err_out) {
+  if (!c->gbuf) {
+    CUDA_OR(cudaMalloc(&c->gbuf, GROUP_BUF_BYTES), "allocating the expert-group exchange buffer");
+    c->bytes += GROUP_BUF_BYTES;
+    CUDA_OR(cudaMemset(c->gbuf, 0, GROUP_BUF_BYTES), "clearing the expert-group exchange buffer");
+  }
+  if (group_buffer_bytes(c->sms, L.n_embd, L.n_ff_exp, L.n_expert, L.n_used) > GROUP_BUF_BYTES) {
+    errf(err, errlen, "the expert-group exchange buffer is too small for this layer");
+    return 1;
+  }
+  g.x_in = x; g.x_out = x_out ? x_out : x;
+  g.err_out = err_out;
+  g.norm = L.ffn_norm_f; g.router = L.router_f;
+  g.gate = L.gate.p; g.up = L.up.p; g.down = L.down.p;
+  g.gate_slab = L.gate_slab; g.up_slab = L.up_slab; g.down_slab = L.down_slab;
+  g.E = L.n_embd; g.FF = L.n_ff_exp; g.NE = L.n_expert; g.K = L.n_used; g.norm_topk = L.norm_topk;
+  g.resid_scale = L.resid_scale; g.eps = L.rms_eps;
+  group_set_buffer(g, c->gbuf, c->sms);   // after the shape: the layout follows NE, K, FF and E
+  g.err = c->small;
+  g.sel_out = sel_out; g.wt_out = wt_out;
+  g.force_miss = c->force_miss;
+  g.trace = c->trace;
+  if (!c->group_attrs_set) {
+    CUDA_OR(group_allow_smem(c->max_smem), "kernel attribute");
+    c->group_attrs_set = true;
+  }
+  const GroupFn fn = group_kernel_for(L.gate.type, L.down.type);
+  if (reinterpret_cast<const void *>(fn) != c->gocc_fn || g.smem_bytes != c->gocc_smem) {   // once per kernel and size
+    int occ = 0;
+    CUDA_OR(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, GROUP_THREADS, g.smem_bytes), "occupancy");
+    if (occ < 1) { errf(err, errlen, "the expert-group kernel does not fit on an SM (%u bytes of shared memory)", g.smem_bytes); return 1; }
+    c->gocc_fn = reinterpret_cast<const void *>(fn);
+    c->gocc_smem = g.smem_bytes;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(c->sms);
+  cfg.blockDim = dim3(GROUP_THREADS);
+  cfg.dynamicSmemBytes = g.smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUDA_OR(cudaLaunchKernelEx(&cfg, fn, g), "launching the expert-group kernel");
+  return 0;
+}
+
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
                const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
                const SmartRoute *smart, float *x_out, int *err_out) {
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+  if (mode == 0 && !smart && c->decode_kernel == 0) {
+    GroupArgs g{};
+    if (plan_group_shape(c->sms, c->max_smem, E, FF, NE, K, L.gate.type, L.up.type, L.down.type, g) == 0)
+      return launch_group(c, L, g, x, sel_out, wt_out, st, err, errlen, x_out, err_out);
+  }
   DecodeArgs a{};
   if (plan_decode(c, L, a)) { errf(err, errlen, "the one-token kernel does not take this layer (K-quant experts only)"); return 1; }
   const Scratch s = plan_scratch(1, E, FF, NE, K, false);
@@ -281,6 +336,7 @@ void clb200_close(clb200_ctx *c) {
   if (c->scratch) cudaFree(c->scratch);
   if (c->small) cudaFree(c->small);
   if (c->route_buf) cudaFree(c->route_buf);
+  if (c->gbuf) cudaFree(c->gbuf);
   if (c->hstage) cudaFreeHost(c->hstage);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
@@ -290,6 +346,15 @@ uint64_t clb200_device_bytes(const clb200_ctx *c) { return c ? c->bytes : 0; }
 
 void clb200_set_exact(clb200_ctx *c, int on) {
   if (c) c->exact = on != 0;
+}
+
+int clb200_set_option(clb200_ctx *c, int option, int value) {
+  if (!c) return 1;
+  switch (option) {
+    case CLB200_OPT_DECODE_KERNEL: if (value < 0 || value > 1) return 1; c->decode_kernel = value; return 0;
+    case CLB200_OPT_TEST_SPECULATION_MISS: c->force_miss = value != 0; return 0;
+    default: return 1;
+  }
 }
 
 void clb200_set_trace(clb200_ctx *c, void *dev_buf) {
@@ -518,6 +583,7 @@ static int report_device_error(clb200_ctx *c, int code, char *err, size_t errlen
   if (!code) return 0;
   errf(err, errlen, "device error %d: %s", code, device_error_text(code));
   cudaMemset(c->small, 0, 4096);
+  if (c->gbuf) cudaMemset(c->gbuf, 0, GROUP_BUF_BYTES);   // a failed launch may leave words the next one could take as its own
   return 1;
 }
 

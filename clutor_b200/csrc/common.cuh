@@ -96,6 +96,39 @@ CLB_DEV bool wait_counter(const uint32_t *p, uint32_t target) {
 }
 CLB_DEV void set_error(int *err, int code) { atomicCAS(err, 0, code); }
 
+// ---- self-tagged words: a 32-bit value and the tag of the launch that wrote it, stored and loaded as one 64-bit word, so
+// a reader that sees the tag it expects holds the value too (no separate flag, no ordering between two stores) ----------
+CLB_DEV void st_word(unsigned long long *p, uint32_t tag, uint32_t bits) {
+  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | bits;
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+CLB_DEV unsigned long long ld_word(const unsigned long long *p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Waits (bounded) until the word at p carries `tag`; returns false when the limit ran out. *bits receives the value.
+CLB_DEV bool wait_word(const unsigned long long *p, uint32_t tag, uint32_t *bits) {
+#pragma unroll 1
+  for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
+    const unsigned long long w = ld_word(p);
+    if (static_cast<uint32_t>(w >> 32) == tag) { *bits = static_cast<uint32_t>(w); return true; }
+    if (i > 4096) __nanosleep(64);
+  }
+  return false;
+}
+CLB_DEV uint32_t ld_relaxed(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Acquire-release add; returns the old value.
+CLB_DEV uint32_t atom_add_acq_rel(uint32_t *p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // ---- phase trace -------------------------------------------------------------------------------------------------------------
 CLB_DEV unsigned long long global_ns() {
   unsigned long long t;

@@ -108,7 +108,14 @@ struct clb200_ctx {
   unsigned long long *trace = nullptr;             // phase trace of the one-token kernel (device, 32 per CTA) or null
   uint8_t *route_buf = nullptr;                    // clb200_route: logits, residency and result on the device
   bool exact = false;                              // batched expert products on the integer path only (no tensor cores)
+  uint8_t *gbuf = nullptr;                         // the expert-group kernel's exchange buffer (zeroed once, its alone)
+  bool group_attrs_set = false;
+  const void *gocc_fn = nullptr;                   // the expert-group kernel and shared size last found to fit an SM
+  uint32_t gocc_smem = 0;
+  int decode_kernel = 1;                           // CLB200_OPT_DECODE_KERNEL
+  int force_miss = 0;                              // CLB200_OPT_TEST_SPECULATION_MISS
 };
+constexpr size_t GROUP_BUF_BYTES = size_t(4) << 20;   // >= group_buffer_bytes() of every shape the kernel takes
 constexpr size_t ROUTE_BUF_BYTES = 1024 * 5 + 256;
 
 namespace clb {

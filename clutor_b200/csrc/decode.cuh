@@ -60,6 +60,48 @@ DecodeFn decode_kernel_for(uint32_t gate_type, uint32_t down_type);
 // Lets every instantiation use `bytes` of dynamic shared memory (on the current device).
 cudaError_t decode_allow_smem(int bytes);
 
+// ---- the expert-group one-token kernel (group.cu) -----------------------------------------------------------------------
+constexpr int GROUP_THREADS = 512;
+constexpr int GROUP_MAX_RG = 31;   // gate/up row groups per CTA (one mbarrier and one copy pair each)
+constexpr int GROUP_MAX_NE = 256;
+
+struct GroupArgs {
+  const float *x_in;
+  float *x_out;                  // may equal x_in
+  const float *norm, *router;
+  const uint8_t *gate, *up, *down;
+  uint64_t gate_slab, up_slab, down_slab;
+  int E, FF, NE, K, norm_topk;
+  float resid_scale, eps;
+  // the kernel's own exchange buffer (zero when first used, written by nothing else): sync [0] the launch generation; lw [NE]
+  // logit words; hw [K * FF] hg words, then [K * E] words of each group's weighted down rows
+  uint32_t *sync;
+  unsigned long long *lw, *hw;
+  int *err;                      // first device error
+  int *err_out;                  // null, or host-mapped: the last CTA out copies the error word there
+  int *sel_out;                  // [K] or null
+  float *wt_out;                 // [K] or null
+  int force_miss;                // test hook: the copies of rank K - 1 first go out for the expert ranked K, so the correction runs
+  // plan (host-computed, plan_group_shape)
+  int ne;                        // CTAs per expert group; the grid is K * ne workers plus CTAs that only score experts
+  int GL;                        // lanes per gate/up row (a power of two >= E / 256)
+  int nrg_max, ngu_max, nd_max, nre;
+  uint32_t grb, drb, rg_bytes, rstride;
+  uint32_t off_bars, off_x, off_norm, off_xn, off_xq, off_router, off_prod, off_lg, off_ev, off_p, off_misc, off_hg, off_hq,
+      off_terms, off_own, off_gath, off_gu, off_dn, smem_bytes;
+  unsigned long long *trace;     // as DecodeArgs::trace
+};
+using GroupFn = void (*)(GroupArgs);
+// Bytes of the exchange buffer a layer of this shape needs.
+size_t group_buffer_bytes(int sms, int E, int FF, int NE, int K);
+// The plan for a layer on a device with `sms` SMs and `max_smem` bytes of opt-in shared memory; 0 when the kernel takes it.
+int plan_group_shape(int sms, int max_smem, int E, int FF, int NE, int K, uint32_t gate_type, uint32_t up_type,
+                     uint32_t down_type, GroupArgs &a);
+GroupFn group_kernel_for(uint32_t gate_type, uint32_t down_type);
+cudaError_t group_allow_smem(int bytes);
+// Points the args at an exchange buffer of group_buffer_bytes() bytes (laid out by a.NE, a.K, a.FF and a.E: set them first).
+void group_set_buffer(GroupArgs &a, uint8_t *buf, int sms);
+
 // ---- batched path ------------------------------------------------------------------------------------------------------
 struct BatchArgs {
   const float *x_in;

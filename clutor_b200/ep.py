@@ -152,6 +152,7 @@ def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, 
     send = fmt.pack(qs=torch.cat([qs[i] for i in idx]), d=torch.cat([d[i] for i in idx]), bs=torch.cat([bs[i] for i in idx]),
                     sel=torch.cat(lsel), wt=torch.cat([wt[i] for i in idx]))
     scount = torch.tensor([len(i) for i in idx], dtype=torch.int64, device=x.device)
+    me = dist.get_rank(group) if n > 1 else 0
     if n > 1:
         rcount = torch.empty_like(scount)
         dist.all_to_all_single(rcount, scount, group=group)
@@ -168,6 +169,9 @@ def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, 
     close("experts")
     if timings is not None:
         timings.setdefault("rows", []).append(int(recv.shape[0]))
+        # bytes this rank sends to the other ranks: its dispatched rows, then the partial sums of the rows it received
+        timings.setdefault("xbytes", []).append(sum(c for d, c in enumerate(sc) if d != me) * fmt.nbytes +
+                                                sum(c for d, c in enumerate(rc) if d != me) * E * 4)
     mark("combine")
     if n > 1:
         back = torch.empty((sum(sc), E), dtype=torch.float32, device=x.device)

@@ -1,9 +1,10 @@
-"""Phase trace of the one-token MoE kernel (clb200_set_trace) over a chain of layers replayed from a CUDA graph.
+"""Phase trace of the one-token MoE kernels (clb200_set_trace) over a chain of layers replayed from a CUDA graph.
 
-    python -m clutor_b200.trace [--layers 48] [--down q4_k]
+    python -m clutor_b200.trace [--layers 48] [--down q4_k] [--kernel group|grid]
 
-Each layer's launch gets its own trace buffer (32 entries per CTA): thread 0 of every CTA writes its SM's cycle counter at
-each phase boundary and the global nanosecond timer at entry and exit (decode.cu). The summary gives, per phase, the
+--kernel group (the default) traces the expert-group kernel (group.cu), grid the grid-wide one (decode.cu). Each layer's
+launch gets its own trace buffer (32 entries per CTA): thread 0 of every CTA writes its SM's cycle counter at each phase
+boundary and the global nanosecond timer at entry and exit. The summary gives, per phase, the
 median over CTAs 0-127 and over the layers after the first eight of the cycles between consecutive boundaries, in
 microseconds at the SM clock the trace itself gives (cycles over global-timer nanoseconds from entry to exit); and,
 from the global timer, the launch span and the gap between launches.
@@ -14,7 +15,20 @@ import argparse
 
 import numpy as np
 
-# thread 0's boundaries in the order it passes them (decode.cu)
+# thread 0's boundaries in the order it passes them (group.cu), and the boundary the scoring warp stamps after its logits
+GROUP_PHASES = [
+    (1, "dependency wait"), (2, "x, sum of squares, norm weights landed"), (3, "rmsnorm"), (5, "all logits gathered"),
+    (6, "ranking by logit"), (7, "copies issued"), (8, "softmax, probability order, weights"), (9, "gate/up rows (warp 0)"),
+    (10, "the group's hg gathered"), (11, "Q8_K of hg, down rows landed"), (12, "down rows"), (13, "weighted rows published"),
+    (19, "chunk combine, exit"),
+]
+GROUP_ROUTER = (3, 4)
+# finer points inside the group kernel's phases: (name, from boundary, to boundary); 28 is the softmax warp's lane 0
+GROUP_DETAIL = [("thread 0's logit polls", 3, 21), ("gather barrier", 21, 5), ("rank loop", 5, 22), ("rank barrier", 22, 23),
+                ("copy issue (thread 0)", 6, 24), ("first row group landed, from the copies", 24, 25),
+                ("named barrier wait (warp 0)", 25, 26), ("gate/up loop end (warp 0)", 25, 27),
+                ("round barrier", 27, 8), ("softmax warp: copies issued to verdict", 7, 28)]
+# the same for the grid-wide kernel (decode.cu)
 PHASES = [
     (1, "dependency wait"), (2, "x, sum of squares"), (3, "router rows landed"), (4, "rmsnorm, router products"),
     (6, "Q8_K of xn"), (7, "all logits visible"), (8, "softmax max"), (9, "exponentials, double sum"), (10, "probabilities"),
@@ -22,15 +36,19 @@ PHASES = [
     (25, "first expert slot landed"), (26, "first gate/up block"), (13, "gate/up rows"), (14, "hg rows released"),
     (15, "all hg visible"), (16, "Q8_K of hg"), (17, "down rows landed"), (18, "down rows"), (19, "combine, residual"),
 ]
+GRID_ROUTER = (4, 5)
+KERNELS = {"group": (0, GROUP_PHASES, GROUP_ROUTER), "grid": (1, PHASES, GRID_ROUTER)}
 
 
-def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20) -> dict:
+def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20, kernel: str = "group") -> dict:
     import torch
 
     import clutor_b200 as cb
     from clutor_b200 import synth
 
+    option, phases, (rb0, rb1) = KERNELS[kernel]
     ctx = cb.Context(0)
+    ctx.set_option(ctx.OPT_DECODE_KERNEL, option)
     try:
         layers = [synth.device_layer(E=2048, FF=768, NE=128, K=8, gate_type=synth.T_Q4_K, down_type=synth.TYPE_NAMES[down],
                                      seed=i + 1, router_scale=0.02) for i in range(n_layers)]
@@ -77,30 +95,38 @@ def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20) -> dict:
     mhz = float(np.median((t[lay, cta, 19] - t[lay, cta, 0]) / (t[lay, cta, 31] - t[lay, cta, 30]))) * 1000.0
     to_us = 1.0 / mhz   # cycles -> us
     rows, prev = [], 0
-    for b, name in PHASES:
+    for b, name in phases:
         d = (t[lay, cta, b] - t[lay, cta, prev]) * to_us
         rows.append((name, float(np.median(d)), float(np.percentile(d, 90))))
         prev = b
-    router = float(np.median((t[lay, cta, 5] - t[lay, cta, 4]) * to_us))
+    router = float(np.median((t[lay, cta, rb1] - t[lay, cta, rb0]) * to_us))
+    detail = []
+    if kernel == "group":
+        for name, b0, b1 in GROUP_DETAIL:
+            d = (t[lay, cta, b1] - t[lay, cta, b0]) * to_us
+            detail.append((name, float(np.median(d)), float(np.percentile(d, 90))))
     ent, ex = t[:, :, 30], t[:, :, 31]
     span = float(np.median(((ex.max(1) - ent.min(1)) / 1000.0)[lay]))
     gap = float(np.median(((ent[1:].min(1) - ex[:-1].max(1)) / 1000.0)[lay]))
     return {"us_per_layer": us_per_layer, "sm_mhz": mhz, "phases": rows, "router_warp_us": router, "launch_span_us": span,
-            "gap_to_next_launch_us": gap}
+            "gap_to_next_launch_us": gap, "detail": detail}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--down", default="q4_k", choices=["q4_k", "q6_k"])
+    ap.add_argument("--kernel", default="group", choices=sorted(KERNELS))
     a = ap.parse_args()
-    r = run(a.layers, a.down)
+    r = run(a.layers, a.down, kernel=a.kernel)
     print(f"{r['us_per_layer']:.2f} us per layer (CUDA events, traced graph), SM clock {r['sm_mhz']:.0f} MHz (from the trace)")
     print("| phase (thread 0 of each CTA) | median us | p90 us |")
     print("|---|---|---|")
     for name, med, p90 in r["phases"]:
         print(f"| {name} | {med:.3f} | {p90:.3f} |")
-    print(f"router warp (products done to logits stored): {r['router_warp_us']:.3f} us; launch span {r['launch_span_us']:.3f} us, "
+    for name, med, p90 in r.get("detail", []):
+        print(f"| (detail) {name} | {med:.3f} | {p90:.3f} |")
+    print(f"scoring warp (from the boundary before its products to its logits stored): {r['router_warp_us']:.3f} us; launch span {r['launch_span_us']:.3f} us, "
           f"gap to the next launch {r['gap_to_next_launch_us']:.3f} us")
 
 

@@ -80,6 +80,16 @@ int clb200_layer_release(clb200_ctx *c, int layer);
  * context's scratch has been sized by an earlier call with the same or larger T. */
 int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, float *wt, void *stream, char *err,
                        size_t errlen);
+/* Switches of a context (0 on success, 1 for an unknown option or value). No counterpart in the reference.
+ *   CLB200_OPT_DECODE_KERNEL: which kernel runs the one-token block. 0: the expert-group kernel wherever the layer's shape
+ *     allows it (each chosen expert streamed by its own group of SMs; no grid-wide wait after the routing); 1 (default): the
+ *     grid-wide kernel (every SM streams a share of every chosen expert), which the expert store's calls use in any case.
+ *     Both give the same results.
+ *   CLB200_OPT_TEST_SPECULATION_MISS: a test hook. 1: the expert-group kernel first fetches the expert ranked K + 1 in place
+ *     of the one ranked K, as if two probabilities had tied at rank K, so that its correction path runs on every call; the
+ *     results must not change. 0 (default): off. */
+enum { CLB200_OPT_DECODE_KERNEL = 1, CLB200_OPT_TEST_SPECULATION_MISS = 2 };
+int clb200_set_option(clb200_ctx *c, int option, int value);
 /* No counterpart in the reference: an entry point for hosts that cannot allocate device memory once they run (their
  * device memory is carved out up front by another allocator, or cudaMalloc's device-wide synchronisation would break a
  * decode latency budget). The one-token block of clb200_moe_ffn_dev on DEVICE pointers (layer tensors, x [n_embd]

@@ -36,6 +36,7 @@ def test_reference_arm_line():
     assert cb["kind"] == "reference" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert d["config"]["workload"] == bench.WORKLOADS["decode"]["desc"]
+    assert d["config"] == bench.layers_config(dict(bench.WORKLOADS["decode"]), 1)   # the GPU arm's config, key for key
 
 
 def test_reference_arm_other_ranks_are_silent():
