@@ -834,12 +834,18 @@ def run_layers(a, wl: dict, rank: int, world: int, local: int, dist) -> dict | N
         xn, sn, wn = xh.numpy(), selh.numpy(), wth.numpy()
         for s in structs:                # the first call of each layer uploads its weights
             ctx.moe_ffn_inplace(s, xn, sn, wn)
+        # the calls as a C host makes them: the argument values prepared once (ctypes converts nothing per call)
+        import ctypes as C
+        fn, errb = cb.lib().clb200_moe_ffn, C.create_string_buffer(512)
+        calls = [(C.c_void_p(ctx.handle), C.byref(s), C.c_void_p(xn.ctypes.data), T, C.c_void_p(sn.ctypes.data),
+                  C.c_void_p(wn.ctypes.data), errb, 512) for s in structs]
         if dist:
             dist.barrier()
         t0 = time.perf_counter()
         for _ in range(a.steps):
-            for s in structs:
-                ctx.moe_ffn_inplace(s, xn, sn, wn)
+            for args in calls:
+                if fn(*args):
+                    raise cb.ClutorError(errb.value.decode())
         dt = time.perf_counter() - t0
         if dist:
             tt = torch.tensor([dt], device="cuda")

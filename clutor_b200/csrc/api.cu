@@ -74,6 +74,7 @@ static int ensure_scratch(clb200_ctx *c, size_t need, char *err, size_t errlen) 
   const size_t cap = al(need, 1 << 20);
   CUDA_OR(cudaMalloc(&c->scratch, cap), "allocating scratch");
   c->scratch_cap = cap;
+  ++c->graph_gen;
   c->bytes += cap;
   return 0;
 }
@@ -91,6 +92,7 @@ static int ensure_hstage(clb200_ctx *c, size_t need, char *err, size_t errlen) {
   CUDA_OR(cudaHostAlloc(reinterpret_cast<void **>(&c->hstage), cap, cudaHostAllocMapped | cudaHostAllocPortable), "pinning host staging");
   c->hstage_cap = cap;
   CUDA_OR(cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->hstage_dev), c->hstage, 0), "mapping host staging");
+  ++c->graph_gen;
   return 0;
 }
 
@@ -234,9 +236,12 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
   if (mode == 0 && !smart && c->decode_kernel == 0) {
     GroupArgs g{};
-    if (plan_group_shape(c->sms, c->max_smem, E, FF, NE, K, L.gate.type, L.up.type, L.down.type, g) == 0)
+    if (plan_group_shape(c->sms, c->max_smem, E, FF, NE, K, L.gate.type, L.up.type, L.down.type, g) == 0) {
+      c->signals_done = false;   // its error word reaches err_out only on a failure
       return launch_group(c, L, g, x, sel_out, wt_out, st, err, errlen, x_out, err_out);
+    }
   }
+  c->signals_done = err_out != nullptr;
   DecodeArgs a{};
   if (plan_decode(c, L, a)) { errf(err, errlen, "the one-token kernel does not take this layer (K-quant experts only)"); return 1; }
   const Scratch s = plan_scratch(1, E, FF, NE, K, false);
@@ -332,7 +337,10 @@ void clb200_close(clb200_ctx *c) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
-  for (auto &l : c->layers) if (l.block) cudaFree(l.block);
+  for (auto &l : c->layers) {
+    if (l.block) cudaFree(l.block);
+    if (l.host_graph) cudaGraphExecDestroy(l.host_graph);
+  }
   if (c->scratch) cudaFree(c->scratch);
   if (c->small) cudaFree(c->small);
   if (c->route_buf) cudaFree(c->route_buf);
@@ -351,14 +359,16 @@ void clb200_set_exact(clb200_ctx *c, int on) {
 int clb200_set_option(clb200_ctx *c, int option, int value) {
   if (!c) return 1;
   switch (option) {
-    case CLB200_OPT_DECODE_KERNEL: if (value < 0 || value > 1) return 1; c->decode_kernel = value; return 0;
-    case CLB200_OPT_TEST_SPECULATION_MISS: c->force_miss = value != 0; return 0;
+    case CLB200_OPT_DECODE_KERNEL: if (value < 0 || value > 1) return 1; c->decode_kernel = value; ++c->graph_gen; return 0;
+    case CLB200_OPT_TEST_SPECULATION_MISS: c->force_miss = value != 0; ++c->graph_gen; return 0;
     default: return 1;
   }
 }
 
 void clb200_set_trace(clb200_ctx *c, void *dev_buf) {
-  if (c) c->trace = static_cast<unsigned long long *>(dev_buf);
+  if (!c) return;
+  c->trace = static_cast<unsigned long long *>(dev_buf);
+  ++c->graph_gen;
 }
 
 int clb200_layer_bind(clb200_ctx *c, const clb200_moe_layer *L, int on_device, char *err, size_t errlen) {
@@ -416,6 +426,7 @@ int clb200_layer_release(clb200_ctx *c, int layer) {
   auto it = c->by_gate.find(dl.hkey[2]);
   if (it != c->by_gate.end() && it->second == layer) c->by_gate.erase(it);
   if (dl.block) { cudaFree(dl.block); c->bytes -= dl.bytes; }
+  if (dl.host_graph) cudaGraphExecDestroy(dl.host_graph);
   dl = DevLayer();
   return 0;
 }
@@ -600,7 +611,7 @@ int clb200_status(clb200_ctx *c, char *err, size_t errlen) {
 // staging on the host and read from there by a small kernel; the one-token kernel writes x, sel and wt into the staging
 // and its last CTA the error word; one wait on the stream. (Each copy-engine transfer costs several microseconds of
 // latency, as much as a quarter of the kernel at one token.)
-static int host_call_one(clb200_ctx *c, const DevLayer &dl, float *x, int *sel_out, float *wt_out, char *err, size_t errlen) {
+static int host_call_one(clb200_ctx *c, DevLayer &dl, float *x, int *sel_out, float *wt_out, char *err, size_t errlen) {
   const clb200_moe_layer &L = dl.d;
   const int E = L.n_embd, K = L.n_used;
   const size_t xb = static_cast<size_t>(E) * 4, kb = static_cast<size_t>(K) * 4;
@@ -611,16 +622,60 @@ static int host_call_one(clb200_ctx *c, const DevLayer &dl, float *x, int *sel_o
   float *dx = reinterpret_cast<float *>(c->scratch + s.off_x);
   uint8_t *h = c->hstage, *hd = c->hstage_dev;
   volatile int *herr = reinterpret_cast<volatile int *>(h + o_err);
-  *herr = 0;
+  constexpr int PENDING = -1;   // device error codes are >= 0
+  *herr = PENDING;
   std::memcpy(h, x, xb);
-  CUDA_OR(launch_stage_in(reinterpret_cast<const float *>(hd), dx, E, c->stream), "staging x");
-  if (launch_one(c, L, dx, 0, nullptr, nullptr, nullptr, reinterpret_cast<int *>(hd + o_sel), reinterpret_cast<float *>(hd + o_wt),
-                 c->stream, err, errlen, nullptr, reinterpret_cast<float *>(hd + o_out), reinterpret_cast<int *>(hd + o_err))) {
+  // Every argument of the two launches is fixed for a layer (x goes through the staging), so from the layer's second call
+  // on they are one graph launch: the first call sets the kernels' attributes and the exchange buffers up eagerly.
+  if (dl.host_graph && dl.host_graph_gen != c->graph_gen) {
+    cudaGraphExecDestroy(dl.host_graph);
+    dl.host_graph = nullptr;
+  }
+  auto launches = [&]() -> int {
+    CUDA_OR(launch_stage_in(reinterpret_cast<const float *>(hd), dx, E, c->stream), "staging x");
+    return launch_one(c, L, dx, 0, nullptr, nullptr, nullptr, reinterpret_cast<int *>(hd + o_sel), reinterpret_cast<float *>(hd + o_wt),
+                      c->stream, err, errlen, nullptr, reinterpret_cast<float *>(hd + o_out), reinterpret_cast<int *>(hd + o_err));
+  };
+  if (!dl.host_graph && dl.host_calls >= 1) {
+    cudaGraph_t g = nullptr;
+    CUDA_OR(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "capturing the host call");
+    const int rc = launches();
+    const cudaError_t ec = cudaStreamEndCapture(c->stream, &g);
+    if (rc || ec != cudaSuccess || cudaGraphInstantiate(&dl.host_graph, g, 0) != cudaSuccess) {
+      dl.host_graph = nullptr;
+      cudaGetLastError();   // a failed capture leaves no sticky error; this call runs its launches directly below
+    } else {
+      dl.host_graph_gen = c->graph_gen;
+    }
+    if (g) cudaGraphDestroy(g);
+  }
+  ++dl.host_calls;
+  if (dl.host_graph) {
+    CUDA_OR(cudaGraphLaunch(dl.host_graph, c->stream), "launching the host call's graph");
+  } else if (launches()) {
     cudaStreamSynchronize(c->stream);   // the staging kernel may still read the staging, which the next call rewrites
     return 1;
   }
-  CUDA_OR(cudaStreamSynchronize(c->stream), "running the MoE block");
-  if (report_device_error(c, *herr, err, errlen)) return 1;
+  int code = PENDING;
+  if (c->signals_done) {
+    // The grid-wide kernel's last CTA writes the error word into the mapped staging after a system-wide fence, so the
+    // results are in host memory once it arrives: spin on it, and ask the stream now and then (a launch that failed writes
+    // nothing), instead of a blocking synchronisation.
+    for (uint32_t n = 1;; ++n) {
+      code = *herr;
+      if (code != PENDING) break;
+      if ((n & 4095) == 0 && cudaStreamQuery(c->stream) != cudaErrorNotReady) {
+        code = *herr;
+        break;
+      }
+    }
+  }
+  if (code == PENDING) {
+    CUDA_OR(cudaStreamSynchronize(c->stream), "running the MoE block");
+    code = *herr;
+    if (code == PENDING) code = 0;   // a kernel that reports its error word only on a failure
+  }
+  if (report_device_error(c, code, err, errlen)) return 1;
   std::memcpy(x, h + o_out, xb);
   if (sel_out) std::memcpy(sel_out, h + o_sel, kb);
   if (wt_out) std::memcpy(wt_out, h + o_wt, kb);
@@ -638,7 +693,7 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
   if (it != c->by_gate.end()) {
     const DevLayer &dl = c->layers[it->second];
     if (dl.hkey[0] == L->ffn_norm_f && dl.hkey[1] == L->router_f && dl.hkey[3] == L->up.p && dl.hkey[4] == L->down.p &&
-        validate(L, err, errlen) == 0 && dl.fp == fingerprint(L))
+        dl.fp == fingerprint(L))   // the shape fields are inside the fingerprint; the layer was validated when it was bound
       h = it->second;
     else
       clb200_layer_release(c, it->second);   // the host memory now holds something else: drop the stale upload
@@ -647,7 +702,9 @@ int clb200_moe_ffn(clb200_ctx *c, const clb200_moe_layer *L, float *x, int T, in
     h = clb200_layer_bind(c, L, 0, err, errlen);
     if (h < 0) return 1;
   }
-  const DevLayer &dl = c->layers[h];
+  DevLayer &dl = c->layers[h];
+  dl.d.resid_scale = L->resid_scale;   // the scalars the fingerprint leaves out follow the caller's struct
+  dl.d.rms_eps = L->rms_eps;
   DecodeArgs probe{};
   if (T == 1 && plan_decode(c, dl.d, probe) == 0) return host_call_one(c, dl, x, sel_out, wt_out, err, errlen);
   const int E = L->n_embd, K = L->n_used;

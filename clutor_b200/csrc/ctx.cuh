@@ -59,10 +59,16 @@ struct DevLayer {
   void *block = nullptr;             // the owned device copy (upload), else null
   size_t bytes = 0;
   bool live = false;
+  // a host call's launches at one token (stage-in and one-token kernel), as a graph: captured on the layer's second host call
+  // and replayed while the context's launch state (graph_gen) is unchanged
+  cudaGraphExec_t host_graph = nullptr;
+  uint64_t host_graph_gen = 0;
+  int host_calls = 0;
 };
 
-// FNV-1a over the layer's shape fields and the first and last 64 bytes of each host tensor: a cheap check that a host
-// pointer seen before still holds the weights that were uploaded from it (a freed and reused buffer usually does not).
+// FNV-1a over the layer's shape fields and the first and last 16 bytes of each host tensor: a cheap check, made on every
+// host call, that a host pointer seen before still holds the weights that were uploaded from it (a freed and reused buffer
+// usually does not).
 inline uint64_t fingerprint(const clb200_moe_layer *L) {
   uint64_t h = 1469598103934665603ull;
   auto mix = [&](const void *p, size_t n) {
@@ -76,7 +82,7 @@ inline uint64_t fingerprint(const clb200_moe_layer *L) {
   const void *ptr[5] = {L->ffn_norm_f, L->router_f, L->gate.p, L->up.p, L->down.p};
   const size_t sz[5] = {E * 4, NE * E * 4, NE * L->gate_slab, NE * L->up_slab, NE * L->down_slab};
   for (int i = 0; i < 5; ++i) {
-    const size_t n = sz[i] < 64 ? sz[i] : 64;
+    const size_t n = sz[i] < 16 ? sz[i] : 16;
     mix(ptr[i], n);
     mix(static_cast<const uint8_t *>(ptr[i]) + sz[i] - n, n);
   }
@@ -112,7 +118,10 @@ struct clb200_ctx {
   bool group_attrs_set = false;
   const void *gocc_fn = nullptr;                   // the expert-group kernel and shared size last found to fit an SM
   uint32_t gocc_smem = 0;
+  uint64_t graph_gen = 1;                          // bumped whenever a captured host-call graph would go stale (scratch or
+                                                   // staging moved, a trace buffer or an option set)
   int decode_kernel = 1;                           // CLB200_OPT_DECODE_KERNEL
+  bool signals_done = false;                       // the last one-token launch writes its error word to host memory on exit
   int force_miss = 0;                              // CLB200_OPT_TEST_SPECULATION_MISS
 };
 constexpr size_t GROUP_BUF_BYTES = size_t(4) << 20;   // >= group_buffer_bytes() of every shape the kernel takes

@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     s_flag[0] = 0;
     s_flag[1] = 0;
   }
+  __syncthreads();          // the mbarriers are initialised before any thread waits on one
   grid_dependency_wait();   // x, the scratch and the counters belong to the previous kernel until here
   grid_launch_dependents();
 
@@ -401,11 +402,13 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     if (s_flag[1] && s_flag[0])   // an error path may leave copies unwaited; the normal path waited in phase 6
       for (int k = 0; k < K; ++k)
         if (!mbar_wait_bounded(&bars[k], 0)) set_error(a.err, ERR_WAIT_COPY);
-    if (a.err_out) __threadfence();   // the CTA's error-word writes (ordered by the block barrier) before its count
+    // a host call reads the results from host-mapped memory as soon as the error word arrives there: the CTA's writes
+    // (x, sel and wt included, ordered by the block barrier) reach the host before its count
+    if (a.err_out) __threadfence_system();
     const uint32_t prev = atomicAdd(&a.sync[2], 1u);
     if (prev == static_cast<uint32_t>(G) - 1) {
       if (a.err_out) {
-        __threadfence();
+        __threadfence_system();
         *reinterpret_cast<volatile int *>(a.err_out) = atomicOr(a.err, 0);
       }
       atomicExch(&a.sync[0], 0u);

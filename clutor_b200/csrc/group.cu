@@ -49,6 +49,7 @@ constexpr int NJ_MAX = GROUP_MAX_NE / 32;  // experts per lane in the warp-regis
 struct GroupMisc {
   double red[NW];
   int flag[4];                   // [0] failed, [1] rounds of copies issued, [2] generation advanced, [3] expert to refetch + 1
+  int tiny;                      // a softmax term below 2^-22: the double sum is taken in expert order
   int spec[DECODE_MAX_K + 1];    // experts by logit rank (rank K kept for the test hook)
   int top;                       // the expert with the largest logit
   int tru[DECODE_MAX_K];         // experts by probability rank (the reference's order)
@@ -58,6 +59,30 @@ struct GroupMisc {
 };
 
 CLB_DEV uint32_t fbits(float v) { return __float_as_uint(v); }
+
+// Words i in [0, n) (at addr(i)) into dst(i) (floats), by `nt` threads from thread `t`: each thread polls its words (up to
+// 8) together, so the round trips overlap. False when the limit ran out.
+template <typename Addr, typename Dst>
+CLB_DEV bool gather_words(Addr addr, Dst dst, int n, uint32_t tag, int t, int nt) {
+  constexpr int MAXW = 8;
+  uint32_t have = 0, want = 0;
+#pragma unroll
+  for (int q = 0; q < MAXW; ++q)
+    if (t + q * nt < n) want |= 1u << q;
+#pragma unroll 1
+  for (uint32_t it = 0; it < SPIN_LIMIT && have != want; ++it) {
+#pragma unroll
+    for (int q = 0; q < MAXW; ++q) {
+      const int i = t + q * nt;
+      if (((want & ~have) >> q) & 1u) {
+        const unsigned long long v = ld_word(addr(i));
+        if (static_cast<uint32_t>(v >> 32) == tag) { *dst(i) = __uint_as_float(static_cast<uint32_t>(v)); have |= 1u << q; }
+      }
+    }
+    if (it > 4096 && have != want) __nanosleep(64);
+  }
+  return have == want;
+}
 CLB_DEV void named_sync(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
 CLB_DEV void named_arrive(int n) { asm volatile("bar.arrive 1, %0;" ::"r"(n) : "memory"); }
 CLB_DEV void fail(const GroupArgs &a, GroupMisc &m, int code) {
@@ -72,12 +97,12 @@ __device__ __noinline__ void rank_all_candidates(GroupMisc &m, const float *sp, 
   for (int e = 0; e < NE; ++e) {
     const float pe = sp[e];
     if (!(pe >= pk)) continue;   // warp-uniform
-    int cnt = 0;
-    for (int f = lane; f < NE; f += 32) {
-      const float pf = sp[f];
-      cnt += pf > pe || (pf == pe && f < e);
+    int rank = 0;
+    for (int f0 = 0; f0 < NE; f0 += 32) {
+      const int f = f0 + lane;
+      const float pf = f < NE ? sp[f] : -1.f;
+      rank += __popc(__ballot_sync(FULL, f < NE && (pf > pe || (pf == pe && f < e))));
     }
-    const int rank = __reduce_add_sync(FULL, cnt);
     if (lane == 0 && rank < K) m.tru[rank] = e;
   }
 }
@@ -87,24 +112,27 @@ __device__ __noinline__ void q8k_blocks(const float *x, int n, int8_t *qs, float
   q8k_quantize_block(x, n, qs, dd, bsums, warp, nwarps, lane, true);
 }
 
-// The softmax warp: probabilities, the reference's top-k order, the weights and which group streams which expert
-// (c/src/forward.c:954-984). lg [NE] logits; kg this CTA's group. The loops stay rolled: this code runs once a launch.
+// The softmax warps (the warps without gate/up rows; the last of them finishes alone): probabilities, the reference's top-k
+// order, the weights and which group streams which expert (c/src/forward.c:954-984). lg [NE] logits; kg this CTA's group;
+// st = this thread's index among the nst softmax threads. The loops stay rolled: this code runs once a launch.
 __device__ __noinline__ void softmax_verdict(const GroupArgs &a, GroupMisc &m, const float *lg, float *sev, float *sp, int kg,
-                                             int lane, bool cta0) {
-  const int NE = a.NE, K = a.K;
+                                             int st, int nst, bool cta0) {
+  const int NE = a.NE, K = a.K, lane = st & 31;
   const float mx = lg[m.top];
   bool tiny = false;
 #pragma unroll 1
-  for (int e = lane; e < NE; e += 32) {
+  for (int e = st; e < NE; e += nst) {
     const float v = expf_cr(__fsub_rn(lg[e], mx));
     sev[e] = v;
     tiny |= !(v >= 0x1p-22f);
   }
-  __syncwarp();
+  if (tiny) m.tiny = 1;
+  asm volatile("bar.sync 2, %0;" ::"r"(nst) : "memory");
   // Every term a multiple of 2^-45 (each is a float >= 2^-22) and the sum below 2^8: every partial sum is exact in any
-  // order, so a tree gives the reference's sequential double sum; otherwise lane 0 adds them in expert order.
+  // order, so a tree gives the reference's sequential double sum; otherwise it is added in expert order. Every softmax
+  // warp forms the same sum.
   double sum = 0.0;
-  if (!__any_sync(FULL, tiny)) {
+  if (!m.tiny) {
 #pragma unroll 1
     for (int e = lane; e < NE; e += 32) sum += static_cast<double>(sev[e]);
 #pragma unroll
@@ -115,8 +143,9 @@ __device__ __noinline__ void softmax_verdict(const GroupArgs &a, GroupMisc &m, c
     sum = __shfl_sync(FULL, sum, 0);
   }
 #pragma unroll 1
-  for (int e = lane; e < NE; e += 32) sp[e] = __double2float_rn(__ddiv_rn(static_cast<double>(sev[e]), sum));
-  __syncwarp();
+  for (int e = st; e < NE; e += nst) sp[e] = __double2float_rn(__ddiv_rn(static_cast<double>(sev[e]), sum));
+  asm volatile("bar.sync 2, %0;" ::"r"(nst) : "memory");
+  if (st >= 32) return;   // the last warp alone from here (st < 32 is the last softmax warp)
   // The true top k lies among the experts whose probability is at least that of the logit order's k-th (probability is
   // monotone in the logit); rank those by (probability down, id up). Candidate c goes to lane c.
   const float pk = sp[m.spec[K - 1]];
@@ -159,33 +188,27 @@ __device__ __noinline__ void softmax_verdict(const GroupArgs &a, GroupMisc &m, c
     }
   }
   __syncwarp();
-  if (lane == 0) {   // which group streams each true expert; a group whose expert is outside the true top k takes a
-                     // missing one (both in order), so every CTA of that group refetches the same expert
-    uint32_t orphan = 0, missing = 0;
-    for (int g = 0; g < K; ++g) {
-      bool in = false;
-      for (int k = 0; k < K; ++k) in |= m.tru[k] == m.spec[g];
-      if (!in) orphan |= 1u << g;
-    }
-    for (int k = 0; k < K; ++k) {
-      int g = -1;
-      for (int h = 0; h < K; ++h) if (m.spec[h] == m.tru[k]) g = h;
-      m.slot[k] = g;
-      if (g < 0) missing |= 1u << k;
-    }
-    while (missing && orphan) {
-      const int k = __ffs(missing) - 1, g = __ffs(orphan) - 1;
-      m.slot[k] = g;
-      if (g == kg) m.flag[3] = m.tru[k] + 1;
-      missing &= missing - 1;
-      orphan &= orphan - 1;
-    }
-    m.mine = 0.f;
-    for (int k = 0; k < K; ++k) {
-      if (m.slot[k] < 0 || m.tru[k] < 0) fail(a, m, ERR_BAD_EXPERT);   // cannot happen: two sets of K experts each
-      if (m.slot[k] == kg) m.mine = m.w[k];
-    }
+  // which group streams each true expert (lane k for rank k); a group whose expert is outside the true top k takes a
+  // missing one (both in order), so every CTA of that group refetches the same expert
+  int gk = -1;
+  const int tk = lane < K ? m.tru[lane] : -2;
+  for (int h = 0; h < K; ++h) gk = m.spec[h] == tk ? h : gk;
+  const int sg = lane < K ? m.spec[lane] : -2;   // lane g: is group g's expert in the true top k?
+  bool in = false;
+  for (int k = 0; k < K; ++k) in |= m.tru[k] == sg;
+  const uint32_t orphan = __ballot_sync(FULL, lane < K && !in), missing = __ballot_sync(FULL, lane < K && gk < 0);
+  if (lane < K && gk < 0) {   // the missing rank's position among the missing ranks pairs it with the orphan group at the
+                              // same position
+    const int pos = __popc(missing & ((1u << lane) - 1u));
+    uint32_t o = orphan;
+    for (int t = 0; t < pos && o; ++t) o &= o - 1u;
+    gk = o ? __ffs(o) - 1 : -1;
+    if (gk == kg) m.flag[3] = tk + 1;
   }
+  if (lane < K) m.slot[lane] = gk;
+  if (lane < K && (gk < 0 || tk < 0)) fail(a, m, ERR_BAD_EXPERT);   // cannot happen: two sets of K experts each
+  const uint32_t mine = __ballot_sync(FULL, lane < K && gk == kg);
+  if (lane == 0) m.mine = mine ? m.w[__ffs(mine) - 1] : 0.f;
   __syncwarp();
 }
 
@@ -248,9 +271,11 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
         bulk_copy_g2s(srow + static_cast<size_t>(q) * a.rstride, a.router + static_cast<size_t>(c + q * G) * E, rb, bar_in);
     }
     m.flag[0] = m.flag[1] = m.flag[2] = m.flag[3] = 0;
+    m.tiny = 0;
   }
   if (tid <= DECODE_MAX_K) m.spec[tid] = -1;
   if (tid < DECODE_MAX_K) m.tru[tid] = -1;
+  __syncthreads();          // the mbarriers are initialised before any thread waits on one
   grid_dependency_wait();   // x and the exchange buffer belong to the previous kernel until here
   grid_launch_dependents();
   const bool active = worker || nre > 0;
@@ -289,6 +314,7 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
         const float nn[4] = {__fmul_rn(__fmul_rn(v.x, scale), w.x), __fmul_rn(__fmul_rn(v.y, scale), w.y),
                              __fmul_rn(__fmul_rn(v.z, scale), w.z), __fmul_rn(__fmul_rn(v.w, scale), w.w)};
         reinterpret_cast<float4 *>(sxn + i)[0] = make_float4(nn[0], nn[1], nn[2], nn[3]);
+#pragma unroll 1
         for (int q = 0; q < nre; ++q) {   // product i goes to chain i % 8, position i / 8
           const float4 r = reinterpret_cast<const float4 *>(srow + static_cast<size_t>(q) * a.rstride + i)[0];
           const float rr[4] = {r.x, r.y, r.z, r.w};
@@ -339,36 +365,43 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
       if (lane == 0) trace_stamp_here(a.trace, 4);
     }
   } else if (worker) {
-    q8k_blocks(sxn, E, xq_qs, xq_d, xq_bs, warp, SW, lane);
+    // the warps of the three SM sub-partitions without the scoring warp (a warp's sub-partition is its index mod 4), so
+    // none competes with its chains for issue slots
+    if ((warp & 3) != (SW & 3))
+      q8k_blocks(sxn, E, xq_qs, xq_d, xq_bs, (warp >> 2) * 3 + ((warp & 3) < (SW & 3) ? (warp & 3) : (warp & 3) - 1), NW / 4 * 3, lane);
   }
   if (!worker) goto done;   // a CTA that only scores experts is finished
 
-  // ---- 3: every logit (warp 0 gathers them), the ranking by logit (ties to the lower id) -----------------------------------
-  if (warp == 0) {
-    for (int e = lane; e < NE; e += 32) {
-      uint32_t bits = 0;
-      if (!wait_word(a.lw + e, tag, &bits)) fail(a, m, ERR_WAIT_ROUTER);
-      slg[e] = __uint_as_float(bits);
-    }
-    trace_stamp(a.trace, 21);
-  }
+  // ---- 3: every logit, the ranking by logit (ties to the lower id) ---------------------------------------------------------
+  if (!gather_words([&](int i) { return a.lw + i; }, [&](int i) { return slg + i; }, NE, tag, tid, GROUP_THREADS))
+    fail(a, m, ERR_WAIT_ROUTER);
+  if (tid < ((NE + 3) & ~3) - NE) slg[NE + tid] = -INFINITY;
+  trace_stamp(a.trace, 21);
   __syncthreads();
   trace_stamp(a.trace, 5);
   if (!m.flag[0]) {
-    const int NJ = (NE + 31) / 32;
-    float v[NJ_MAX];
-#pragma unroll
-    for (int j = 0; j < NJ_MAX; ++j) v[j] = j < NJ && lane + 32 * j < NE ? slg[lane + 32 * j] : 0.f;
-    for (int e = warp; e < NE; e += NW) {   // rank = the experts ahead of e in the order (logit down, id up)
-      const float le = slg[e];
-      int cnt = 0;
-#pragma unroll
-      for (int j = 0; j < NJ_MAX; ++j) {
-        const int f = lane + 32 * j;
-        cnt += j < NJ && f < NE && (v[j] > le || (v[j] == le && f < e));
+    // rank = the experts ahead of e in the order (logit down, id up): four threads per expert, each a quarter of the
+    // rivals by broadcast float4 loads (the logits past NE read as -inf)
+    const int n4 = (NE + 3) / 4, per = (n4 + 3) / 4;
+#pragma unroll 1
+    for (int e0 = 0; e0 < NE; e0 += GROUP_THREADS / 4) {
+      const int e = e0 + (tid >> 2), part = tid & 3;
+      const float le = e < NE ? slg[e] : 0.f;
+      const float4 *l4 = reinterpret_cast<const float4 *>(slg);
+      int rank = 0;
+#pragma unroll 1
+      for (int u = 0; u < per; ++u) {
+        const int q = part * per + u;
+        if (q < n4) {
+          const float4 v = l4[q];
+          const int f = 4 * q;
+          rank += (v.x > le || (v.x == le && f < e)) + (v.y > le || (v.y == le && f + 1 < e)) +
+                  (v.z > le || (v.z == le && f + 2 < e)) + (v.w > le || (v.w == le && f + 3 < e));
+        }
       }
-      const int rank = __reduce_add_sync(FULL, cnt);
-      if (lane == 0) {
+      rank += __shfl_xor_sync(FULL, rank, 1);
+      rank += __shfl_xor_sync(FULL, rank, 2);
+      if (e < NE && part == 0) {
         if (rank <= K) m.spec[rank] = e;
         if (rank == 0) m.top = e;
       }
@@ -387,33 +420,36 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
 
   {
     // ---- 4: the copies of this CTA's rows of its group's expert ------------------------------------------------------------
-    const uint64_t pol = l2_evict_first();   // expert weights are read once a layer
     auto src = [&](int e, int q, int row) -> const uint8_t * {   // q: 0 gate, 1 up, 2 down
       const size_t ee = static_cast<size_t>(e);
       return q == 0 ? a.gate + ee * a.gate_slab + static_cast<size_t>(row) * grb
            : q == 1 ? a.up + ee * a.up_slab + static_cast<size_t>(row) * grb
                     : a.down + ee * a.down_slab + static_cast<size_t>(row) * drb;
     };
-    auto issue = [&](int e) {   // lane g < nrg: row group g's gate and up rows; lane 31: the down rows
-      if (warp != 0) return;
-      if (lane < nrg) {
-        const int g = lane, ra = j0 + g * RPW, rb = min(j1, ra + RPW);
+    auto issue = [&](int e) {   // lane 0 of warp w: row groups w, w + NW, ...; lane 0 of the last warp also the down rows
+      if (lane != 0) return;
+#pragma unroll 1
+      for (int g = warp; g < nrg; g += NW) {
+        const int ra = j0 + g * RPW, rb = min(j1, ra + RPW);
         const uint32_t len = static_cast<uint32_t>(rb - ra) * grb;
         const uint8_t *s0 = src(e, 0, ra), *s1 = src(e, 1, ra);
         const uint32_t lo0 = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(s0) & 15u),
                        lo1 = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(s1) & 15u);
         const uint32_t n0 = (lo0 + len + 15u) & ~15u, n1 = (lo1 + len + 15u) & ~15u;
         mbar_arrive_expect_tx(&bars[g], n0 + n1);
-        bulk_copy_g2s_hint(sgu + static_cast<size_t>(g) * a.rg_bytes, s0 - lo0, n0, &bars[g], pol);
-        bulk_copy_g2s_hint(sgu + static_cast<size_t>(a.nrg_max + g) * a.rg_bytes, s1 - lo1, n1, &bars[g], pol);
-      } else if (lane == 31) {
+        bulk_copy_g2s(sgu + static_cast<size_t>(g) * a.rg_bytes, s0 - lo0, n0, &bars[g]);
+        bulk_copy_g2s(sgu + static_cast<size_t>(a.nrg_max + g) * a.rg_bytes, s1 - lo1, n1, &bars[g]);
+      }
+      if (warp == NW - 1) {
         const uint8_t *s2 = src(e, 2, r0);
         const uint32_t lo2 = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(s2) & 15u);
         const uint32_t n2 = (lo2 + static_cast<uint32_t>(nd) * drb + 15u) & ~15u;
         mbar_arrive_expect_tx(bar_dn, n2);
-        bulk_copy_g2s_hint(sdn, s2 - lo2, n2, bar_dn, pol);
+        bulk_copy_g2s(sdn, s2 - lo2, n2, bar_dn);
       }
     };
+    if (tid == 0 && !m.flag[0] && (m.top < 0 || m.top >= NE || m.spec[kg] < 0 || m.spec[kg] >= NE)) fail(a, m, ERR_BAD_EXPERT);
+    __syncthreads();
     const bool go = !m.flag[0];   // uniform: read after a block barrier
     int e_mine = m.spec[kg];
     uint32_t ph = 0;
@@ -436,18 +472,19 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
       if (round == 0) trace_stamp(a.trace, 24);
       if (tid == 0) m.flag[1] = round + 1;
       if (round == 0) trace_stamp(a.trace, 7);
-      if (warp == SW) {
+      if (warp >= nwg) {   // the softmax warps; the last one hands the verdict to the gate/up warps
         if (round == 0) {
-          softmax_verdict(a, m, slg, sev, sp, kg, lane, c == 0);
-          if (lane == 0) trace_stamp_here(a.trace, 28);
-          named_arrive(nbar);
+          softmax_verdict(a, m, slg, sev, sp, kg, (SW - warp) * 32 + lane, (NW - nwg) * 32, c == 0);
+          if (warp == SW && lane == 0) trace_stamp_here(a.trace, 28);
+          if (warp == SW) named_arrive(nbar);
         }
-      } else if (warp < nwg) {   // row groups warp, warp + SW, ...
+      } else {   // row groups warp, warp + SW, ...
         const int lg = lane & (GL - 1), rw = lane / GL, base = lane - lg;
         const bool has_blk = lg < nb;
         BlockAct act;
         if (has_blk) load_block_act(xq_qs, xq_d, xq_bs, lg, act);
         bool synced = round > 0;
+#pragma unroll 1
         for (int g = warp; g < nrg; g += SW) {   // the same trip count in every lane of a warp
           if (!mbar_wait_bounded(&bars[g], ph)) fail(a, m, ERR_WAIT_COPY);
           if (g == 0 && round == 0) trace_stamp(a.trace, 25);
@@ -466,6 +503,7 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
             }
           }
           float sg = 0.f, su = 0.f;   // the row's block terms in block order
+#pragma unroll 1
           for (int b = 0; b < nb; ++b) {
             sg = __fadd_rn(sg, __shfl_sync(FULL, tg, base + b));
             su = __fadd_rn(su, __shfl_sync(FULL, tu, base + b));
@@ -483,11 +521,9 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
 
     // ---- 7: the group's hg, its Q8_K blocks, the down rows' terms, wt * hd -----------------------------------------------
     if (!m.flag[0]) {
-      for (int j = tid; j < FF; j += GROUP_THREADS) {
-        uint32_t bits = 0;
-        if (!wait_word(a.hw + static_cast<size_t>(kg) * FF + j, tag, &bits)) fail(a, m, ERR_WAIT_EXPERT);
-        shg[j] = __uint_as_float(bits);
-      }
+      const unsigned long long *hwk = a.hw + static_cast<size_t>(kg) * FF;
+      if (!gather_words([&](int i) { return hwk + i; }, [&](int i) { return shg + i; }, FF, tag, tid, GROUP_THREADS))
+        fail(a, m, ERR_WAIT_EXPERT);
       __syncthreads();
       trace_stamp(a.trace, 10);
     }
@@ -499,6 +535,7 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
     }
     if (!m.flag[0]) {
       const uint32_t lo2 = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(src(e_mine, 2, r0)) & 15u);
+#pragma unroll 1
       for (int t0 = 0; t0 < nd * nbd; t0 += GROUP_THREADS) {   // block-major: a warp's lanes mostly share one activation block
         const int t = t0 + tid;
         const int b = min(t / nd, nbd - 1), r = t - b * nd;
@@ -510,8 +547,10 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
       trace_stamp(a.trace, 12);
       const float wk = m.mine;
       const bool combiner = kg == ci % K;
+#pragma unroll 1
       for (int r = tid; r < nd; r += GROUP_THREADS) {
         float hd = 0.f;
+#pragma unroll 1
         for (int b = 0; b < nbd; ++b) hd = __fadd_rn(hd, sterms[r * nbd + b]);
         const float v = __fmul_rn(wk, hd);
         if (combiner) sown[r] = v;
@@ -521,19 +560,21 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1) moe_group_kernel(const Group
       // ---- 8: the chunk's combine in rank order and the residual (c/src/forward.c:1026-1032) ---------------------------------
       if (combiner) {
         const unsigned long long *wpw = a.hw + static_cast<size_t>(K) * FF;   // the weighted rows' words follow the hg words
-        for (int t = tid; t < K * nd; t += GROUP_THREADS) {
-          const int g = t / nd, r = t - g * nd;
-          if (g == kg) continue;
-          uint32_t bits = 0;
-          if (!wait_word(wpw + static_cast<size_t>(g) * E + r0 + r, tag, &bits)) fail(a, m, ERR_WAIT_EXPERT);
-          sgath[g * a.nd_max + r] = __uint_as_float(bits);
-        }
+        // the other groups' words of the chunk, all in one pass (this CTA's own rows are in sown): index i -> group g of the
+        // K - 1 others, row r
+        const int nd_ = nd, kg_ = kg, ndm = a.nd_max;
+        auto wa = [&](int i) { const int q = i / nd_, g = q + (q >= kg_); return wpw + static_cast<size_t>(g) * E + r0 + (i - q * nd_); };
+        auto wd = [&](int i) { const int q = i / nd_, g = q + (q >= kg_); return sgath + g * ndm + (i - q * nd_); };
+        if (!gather_words(wa, wd, (K - 1) * nd, tag, tid, GROUP_THREADS)) fail(a, m, ERR_WAIT_EXPERT);
         __syncthreads();
         if (!m.flag[0]) {
+#pragma unroll 1
           for (int r = tid; r < nd; r += GROUP_THREADS) {
             float moe = 0.f;
+#pragma unroll 1
             for (int k = 0; k < K; ++k) {
               const int g = m.slot[k];
+              if (g < 0 || g >= K) { fail(a, m, ERR_BAD_EXPERT); break; }
               moe = __fadd_rn(moe, g == kg ? sown[r] : sgath[g * a.nd_max + r]);
             }
             a.x_out[r0 + r] = __fadd_rn(sx[r0 + r], __fmul_rn(a.resid_scale, moe));
