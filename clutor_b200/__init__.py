@@ -189,6 +189,8 @@ def lib() -> C.CDLL:
         L.clb200_store_smart_stats.argtypes = [C.c_void_p]
         L.clb200_store_smart_stats.restype = SmartStats
         L.clb200_store_route.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_store_failed.argtypes = [C.c_void_p]
+        L.clb200_store_inject_fill_failure.argtypes = [C.c_void_p, C.c_int]
         _lib = L
     return _lib
 
@@ -323,7 +325,7 @@ class Context:
         """clb200_set_exact: batched expert products on the integer path only (bit-exact), or on the tensor cores."""
         lib().clb200_set_exact(self.handle, int(on))
 
-    OPT_DECODE_KERNEL, OPT_TEST_SPECULATION_MISS = 1, 2
+    OPT_DECODE_KERNEL, OPT_TEST_SPECULATION_MISS, OPT_TEST_STALL_WAIT = 1, 2, 3
 
     def set_option(self, option: int, value: int) -> None:
         """clb200_set_option: OPT_DECODE_KERNEL (0 expert-group kernel where it fits, 1 grid-wide kernel, the default) or
@@ -507,6 +509,13 @@ class Store:
         if self.L.clb200_store_route(self.ctx.handle, self.h, layer, lg.ctypes.data, C.addressof(out), self._err, 512):
             raise ClutorError(self._err.value.decode())
         return out.as_dict()
+
+    def failed(self) -> bool:
+        return bool(self.L.clb200_store_failed(self.h))
+
+    def inject_fill_failure(self, n: int) -> None:
+        """Test hook: the n-th fill from now copies nothing and fails (clb200_store_inject_fill_failure)."""
+        self.L.clb200_store_inject_fill_failure(self.h, n)
 
     def resident(self, layer: int, expert: int) -> bool:
         return bool(self.L.clb200_store_resident(self.h, layer, expert))

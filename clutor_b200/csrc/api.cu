@@ -221,11 +221,13 @@ static int launch_group(clb200_ctx *c, const clb200_moe_layer &L, GroupArgs &g, 
   cfg.blockDim = dim3(GROUP_THREADS);
   cfg.dynamicSmemBytes = g.smem_bytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];   // cooperative: every CTA resident at once (they wait on one another), or no launch
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   CUDA_OR(cudaLaunchKernelEx(&cfg, fn, g), "launching the expert-group kernel");
   return 0;
 }
@@ -234,7 +236,7 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
                const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
                const SmartRoute *smart, float *x_out, int *err_out) {
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
-  if (mode == 0 && !smart && c->decode_kernel == 0) {
+  if (mode == 0 && !smart && c->decode_kernel == 0 && !c->stall_wait) {
     GroupArgs g{};
     if (plan_group_shape(c->sms, c->max_smem, E, FF, NE, K, L.gate.type, L.up.type, L.down.type, g) == 0) {
       c->signals_done = false;   // its error word reaches err_out only on a failure
@@ -262,6 +264,7 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   a.err = c->small;
   a.trace = c->trace;
   a.mode = mode;
+  a.stall_wait = mode == 0 ? c->stall_wait : 0u;
   if (mode == 1 && smart) {
     if (NE > ROUTE_SMEM_MAX_NE || static_cast<size_t>(NE) * 13 + 64 > static_cast<size_t>(K) * a.slot_bytes) {
       errf(err, errlen, "SMART-ROUTE in the one-token kernel takes at most %d experts", ROUTE_SMEM_MAX_NE);
@@ -296,11 +299,15 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   cfg.blockDim = dim3(DECODE_THREADS);
   cfg.dynamicSmemBytes = a.smem_bytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  // cooperative: the driver guarantees that every CTA is resident at once (the kernel's CTAs wait on one another), or
+  // refuses the launch; programmatic dependent launch lets its prologue overlap the previous kernel's tail
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   CUDA_OR(cudaLaunchKernelEx(&cfg, fn, a), "launching the one-token kernel");
   return 0;
 }
@@ -361,6 +368,7 @@ int clb200_set_option(clb200_ctx *c, int option, int value) {
   switch (option) {
     case CLB200_OPT_DECODE_KERNEL: if (value < 0 || value > 1) return 1; c->decode_kernel = value; ++c->graph_gen; return 0;
     case CLB200_OPT_TEST_SPECULATION_MISS: c->force_miss = value != 0; ++c->graph_gen; return 0;
+    case CLB200_OPT_TEST_STALL_WAIT: if (value < 0) return 1; c->stall_wait = static_cast<uint32_t>(value); ++c->graph_gen; return 0;
     default: return 1;
   }
 }

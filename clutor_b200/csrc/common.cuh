@@ -85,10 +85,10 @@ CLB_DEV uint32_t ld_acquire(const uint32_t *p) {
 CLB_DEV void red_release_add(uint32_t *p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Waits until *p >= target (bounded). Call from one thread.
-CLB_DEV bool wait_counter(const uint32_t *p, uint32_t target) {
+// Waits until *p >= target, for at most `limit` polls (about a second at SPIN_LIMIT). Call from one thread.
+CLB_DEV bool wait_counter(const uint32_t *p, uint32_t target, uint32_t limit = SPIN_LIMIT) {
 #pragma unroll 1
-  for (uint32_t i = 0; i < SPIN_LIMIT; ++i) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (ld_acquire(p) >= target) return true;
     if (i > 4096) __nanosleep(64);   // poll flat out for the first few microseconds: these waits are on the critical path
   }

@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       s_wt[tid] = a.wt_in[tid];
       s_wn[tid] = a.wt_in[tid];
     }
-  } else if (tid == 0 && !wait_counter(&a.sync[0], static_cast<uint32_t>(NE))) {
+  } else if (tid == 0 && !(a.stall_wait ? wait_counter(&a.sync[0], static_cast<uint32_t>(NE) + 1u, a.stall_wait)
+                                         : wait_counter(&a.sync[0], static_cast<uint32_t>(NE)))) {
     set_error(a.err, ERR_WAIT_ROUTER);
     s_flag[0] = 1;
   }

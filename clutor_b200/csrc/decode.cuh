@@ -32,6 +32,9 @@ struct DecodeArgs {
   // renormalised already), each expert's weights at slab[k] (gate, up and down slabs back to back) or, where slab[k] is
   // null, in gate / up / down
   int mode;
+  // test hook (0: off): the wait for the router logits targets a count that no CTA reaches, polled `stall_wait` times, so it
+  // runs out and the launch reports ERR_WAIT_ROUTER without a hang or a fault
+  uint32_t stall_wait;
   int sel_in[DECODE_MAX_K];
   float wt_in[DECODE_MAX_K];
   const uint8_t *slab[DECODE_MAX_K];

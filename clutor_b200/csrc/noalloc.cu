@@ -129,11 +129,13 @@ extern "C" int clb200_moe_ffn_decode_noalloc(const clb200_moe_layer *L, float *x
   cfg.blockDim = dim3(DECODE_THREADS);
   cfg.dynamicSmemBytes = a.smem_bytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];   // cooperative: every CTA resident at once (they wait on one another), or no launch
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, fn, a);
   if (e != cudaSuccess) { errf(err, errlen, "launching the one-token kernel: %s", cudaGetErrorString(e)); return 1; }
   // the error word comes back on the caller's stream (a copy on the legacy stream would also wait for other streams' work)

@@ -59,6 +59,11 @@ struct clb200_store {
   uint64_t dev_bytes = 0;                // device memory counted in the context's total
   bool logging = false;
   std::vector<int64_t> oplog;
+  // a fill that failed makes every later wait fail (the reference's sticky failed flag, c/src/xs.c:79, :160); fail_in > 0:
+  // test hook, the fail_in-th fill from now does not copy and fails
+  bool failed = false;
+  int fail_in = 0;
+  std::vector<uint8_t> fill_failed;
 };
 
 namespace {
@@ -91,8 +96,14 @@ void poll(clb200_store *s) {
   for (size_t i = 0; i < s->staged.size(); ++i) {
     const int b = s->staged[i];
     if (cudaEventQuery(s->filled[b]) == cudaSuccess) {
-      s->state[b] = S_READY;
-      count_copy(s, b);
+      if (s->fill_failed[b]) {   // a failed read leaves the slot empty (c/src/xs.c:79-80)
+        s->fill_failed[b] = 0;
+        s->failed = true;
+        s->state[b] = S_EMPTY;
+      } else {
+        s->state[b] = S_READY;
+        count_copy(s, b);
+      }
       clb200_cache_unpin(s->cache, b);
       log_op(s, 3, b, 0);
     } else {
@@ -115,8 +126,12 @@ void fill_resident(clb200_store *s, int layer) {
 void fill(clb200_store *s, int buf, int layer, int expert, bool prefetch) {
   if (s->used_set[buf]) cudaStreamWaitEvent(s->copy, s->used[buf], 0);   // the previous expert's readers are done
   cudaEventRecord(s->started[buf], s->copy);
-  cudaMemcpyAsync(s->arena + static_cast<size_t>(buf) * s->stride,
-                  s->host + (static_cast<size_t>(layer) * s->NE + expert) * s->stride, s->expert_bytes, cudaMemcpyHostToDevice, s->copy);
+  if (s->fail_in > 0 && --s->fail_in == 0) {   // test hook: this fill reads nothing and fails
+    s->fill_failed[buf] = 1;
+  } else {
+    cudaMemcpyAsync(s->arena + static_cast<size_t>(buf) * s->stride,
+                    s->host + (static_cast<size_t>(layer) * s->NE + expert) * s->stride, s->expert_bytes, cudaMemcpyHostToDevice, s->copy);
+  }
   cudaEventRecord(s->filled[buf], s->copy);
   s->state[buf] = S_LOADING;
   s->timed[buf] = 0;
@@ -167,6 +182,7 @@ clb200_store *clb200_store_open(clb200_ctx *c, const clb200_moe_layer *shape, in
             cudaHostAlloc(reinterpret_cast<void **>(&s->smart_host), SMART_HOST_BYTES, cudaHostAllocMapped) == cudaSuccess &&
             cudaStreamCreateWithFlags(&s->copy, cudaStreamNonBlocking) == cudaSuccess;
   s->state.assign(nbuf, S_EMPTY);
+  s->fill_failed.assign(nbuf, 0);
   s->used_set.assign(nbuf, 0);
   s->timed.assign(nbuf, 1);
   s->started.assign(nbuf, nullptr);
@@ -270,15 +286,28 @@ int clb200_store_request(clb200_store *s, int layer, int expert) {
 
 const void *clb200_store_wait(clb200_store *s, int h) {
   if (!s || h < 0 || h >= static_cast<int>(s->total + s->nbypass)) return nullptr;
-  if (s->state[h] != S_READY) {
+  if (s->state[h] != S_READY && !s->failed) {
     const uint64_t t0 = now_ns();
-    if (cudaEventSynchronize(s->filled[h]) != cudaSuccess) return nullptr;
+    const cudaError_t e = cudaEventSynchronize(s->filled[h]);
     s->st.wait_ns += now_ns() - t0;
+    if (e != cudaSuccess || s->fill_failed[h]) {   // a failed read: the slot stays empty, and so does every later wait
+      s->fill_failed[h] = 0;
+      s->failed = true;
+      s->state[h] = S_EMPTY;
+      return nullptr;
+    }
     s->state[h] = S_READY;
   }
+  if (s->state[h] != S_READY) return nullptr;   // the store has failed (c/src/xs.c:160-167)
   count_copy(s, h);
   return s->arena + static_cast<size_t>(h) * s->stride;
 }
+
+void clb200_store_inject_fill_failure(clb200_store *s, int n) {
+  if (s) s->fail_in = n > 0 ? n : 0;
+}
+
+int clb200_store_failed(const clb200_store *s) { return s && s->failed ? 1 : 0; }
 
 void clb200_store_release(clb200_store *s, int h, void *stream) {
   if (!s || h < 0 || h >= static_cast<int>(s->total + s->nbypass)) return;
@@ -360,7 +389,11 @@ static int experts_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, c
     for (int k = 0; k < K; ++k) clb200_store_prefetch(s, layer + 1, next_pred[k]);
   for (int k = 0; k < K; ++k) {
     ptr[k] = static_cast<const uint8_t *>(clb200_store_wait(s, h[k]));
-    if (!ptr[k]) { errf(err, errlen, "filling an expert slot failed: %s", cudaGetErrorString(cudaGetLastError())); return 1; }
+    if (!ptr[k]) {   // every handle of the layer goes back before the error (c/src/forward.c:1000-1001)
+      errf(err, errlen, "reading expert %d of layer %d into HBM failed", sel[k], layer);
+      for (int j = 0; j < K; ++j) clb200_store_release(s, h[j], st);
+      return 1;
+    }
   }
   const int rc = launch_one(c, s->layer[layer], x, 2, sel, wt, ptr, nullptr, nullptr, st, err, errlen);
   for (int k = 0; k < K; ++k) clb200_store_release(s, h[k], st);

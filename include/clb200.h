@@ -87,8 +87,12 @@ int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, floa
  *     Both give the same results.
  *   CLB200_OPT_TEST_SPECULATION_MISS: a test hook. 1: the expert-group kernel first fetches the expert ranked K + 1 in place
  *     of the one ranked K, as if two probabilities had tied at rank K, so that its correction path runs on every call; the
- *     results must not change. 0 (default): off. */
-enum { CLB200_OPT_DECODE_KERNEL = 1, CLB200_OPT_TEST_SPECULATION_MISS = 2 };
+ *     results must not change. 0 (default): off.
+ *   CLB200_OPT_TEST_STALL_WAIT: a test hook for the failure path. N > 0: the grid-wide kernel's wait for the router logits
+ *     targets a count that no CTA reaches and gives up after N polls (1 << 14 is about a millisecond), so every CTA takes its
+ *     error path and the launch ends with the device error word set (ERR_WAIT_ROUTER, reported by clb200_status or the host
+ *     call) instead of a hang; 0 (default): off. */
+enum { CLB200_OPT_DECODE_KERNEL = 1, CLB200_OPT_TEST_SPECULATION_MISS = 2, CLB200_OPT_TEST_STALL_WAIT = 3 };
 int clb200_set_option(clb200_ctx *c, int option, int value);
 /* No counterpart in the reference: an entry point for hosts that cannot allocate device memory once they run (their
  * device memory is carved out up front by another allocator, or cudaMalloc's device-wide synchronisation would break a
@@ -206,6 +210,12 @@ void clb200_store_set_prefetch(clb200_store *s, int on);
  * slot, 3 unpin slot), and read the record (returns its length; copies at most cap values). */
 void clb200_store_log(clb200_store *s, int on);
 int64_t clb200_store_read_log(const clb200_store *s, int64_t *dst, int64_t cap);
+/* A fill that fails (a copy error, or the test hook below) leaves its slot empty and makes the store failed: that wait and
+ * every later one return NULL, and the stored entry points return 1 after releasing every handle of the layer, as the
+ * reference's store does after a failed read (c/src/xs.c:79-80, :160-167; c/src/forward.c:1000-1001). */
+int clb200_store_failed(const clb200_store *s);
+/* Test hook: the n-th fill from now (n >= 1; 0 cancels) copies nothing and fails. */
+void clb200_store_inject_fill_failure(clb200_store *s, int n);
 /* The one-token MoE block of `layer` with its experts served by the store (c/src/forward.c:888-1033 with an expert store):
  * x [n_embd] DEVICE, updated in place; sel_out / wt_out HOST arrays [n_used] or NULL. Returns after the experts are
  * enqueued on `stream` (NULL: the context's stream); the routing is read back to the host on the way. */

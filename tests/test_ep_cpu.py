@@ -117,3 +117,55 @@ def test_dispatch_plan_covers_every_slot_once():
     back = fmt.unpack(fmt.pack(**cols))
     for k, v in cols.items():
         assert torch.equal(back[k], v)
+
+
+class StubCompute(ep.Compute):
+    """Cheap halves for the exchange-only tests: a fixed routing per token, experts that return zeros."""
+
+    def __init__(self, n_experts):
+        self.NE = n_experts
+
+    def route(self, x):
+        T = x.shape[0]
+        sel = torch.stack([torch.arange(T) % self.NE, (torch.arange(T) + 1) % self.NE], 1).to(torch.int32)
+        wt = torch.full((T, K), 0.5)
+        return sel, wt, torch.zeros((T, E), dtype=torch.int8), torch.ones((T, E // 256)), torch.zeros((T, E // 16), dtype=torch.int16)
+
+    def experts(self, qs, d, bs, sel_local, wt):
+        return torch.zeros((qs.shape[0], E))
+
+
+def _leaving_rank(rank, world, port, outdir):
+    """Every rank takes one exchange step; rank 1 then leaves (its process ends without another collective). The others'
+    next step must end in an error within the process group's timeout, not hang."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    comp = StubCompute(NE)
+    x = torch.from_numpy(synth.activations(T, E, seed=rank))
+    ep.moe_layer(x, comp, NE // world, 1.0)
+    if rank == 1:
+        return   # leaves between steps, with no step of its own in flight
+    import time
+    t0 = time.monotonic()
+    try:
+        ep.moe_layer(x, comp, NE // world, 1.0)
+        outcome = "completed"
+    except Exception as e:   # the exchange with the departed rank fails
+        outcome = f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}"
+    with open(os.path.join(outdir, f"rank{rank}"), "w") as f:
+        f.write(outcome)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_a_rank_that_leaves_ends_the_next_exchange_with_an_error(world, tmp_path):
+    import torch.multiprocessing as mp
+    mp.start_processes(_leaving_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True, start_method="spawn")
+    for r in range(world):
+        if r == 1:
+            continue
+        outcome = (tmp_path / f"rank{r}").read_text()
+        assert outcome.startswith("error"), f"rank {r}: {outcome}"
+        assert float(outcome.split()[2]) < 60.0, f"rank {r}: {outcome}"
