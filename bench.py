@@ -354,6 +354,7 @@ def run_cache(a, wl: dict) -> dict:
     expert_bytes = first.expert_bytes
     budget = int(wl["budget"] * NL * NE * expert_bytes)
     store = cb.Store(ctx, first, NL, cache_bytes=budget, stage_slots=2 * K, policy=cb.WTINYLFU)
+    store.set_prefetch_depth(a.prefetch_depth)
     store.load_layer(0, first)
     del first
     for i in range(1, NL):
@@ -450,7 +451,7 @@ def run_cache(a, wl: dict) -> dict:
             "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate", "data": "synthetic (seeded GGUF blocks; routing from the reference harness's synthetic router)",
             "config": {"workload": wl["desc"], "layers": NL, "experts": NE, "top_k": K, "hidden": E, "ff": wl["FF"],
                        "expert_bytes": expert_bytes, "hbm_cache_bytes": budget, "cache_slots": store.cache_slots(),
-                       "stage_slots": 2 * K, "policy": "W-TinyLFU", "locality": wl["locality"], "predict_corr": 0.8,
+                       "stage_slots": 2 * K, "prefetch_depth": a.prefetch_depth, "policy": "W-TinyLFU", "locality": wl["locality"], "predict_corr": 0.8,
                        "parallelism": "single GPU", "l2": "expert bytes 16 GB, far beyond L2"},
             "cache": {"hit_rate": round(hit, 4), "stage_hits": st["stage_hits"], "misses": st["misses"],
                       "prefetch_issued": st["prefetch_issued"], "prefetch_late": st["prefetch_late"],
@@ -905,6 +906,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--prefetch-depth", type=int, default=2, help="cache workload: prefetch fills in flight at once")
     ap.add_argument("--smart", default=None, help="cache workload: SMART-ROUTE J,M,TAU (for example 2,12,0.015)")
     ap.add_argument("--batch", type=int, default=None, help="prompt workload: tokens per batch (the reference's CLUTOR_PS_B, 1..512)")
     ap.add_argument("--no-ep", action="store_true", help="decode workload: leave out the expert-parallel figures")

@@ -74,7 +74,7 @@ class StoreStats(C.Structure):
     """clb200_store_stats (the reference's cl_xs_stats, c/src/xs.h:14-17, with copy_ns for read_ns)."""
     _fields_ = [(n, C.c_uint64) for n in ("accesses", "hits", "stage_hits", "misses", "bypass", "prefetch_issued",
                                          "prefetch_late", "prefetch_wasted", "admit_rejects", "evictions", "demand_bytes",
-                                         "prefetch_bytes", "copy_ns", "wait_ns")]
+                                         "prefetch_bytes", "copy_ns", "wait_ns", "pred_total", "pred_hit")]
 
     def as_dict(self) -> dict:
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -168,6 +168,8 @@ def lib() -> C.CDLL:
         L.clb200_store_get_stats.restype = StoreStats
         L.clb200_store_reset_stats.argtypes = [C.c_void_p]
         L.clb200_store_set_prefetch.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_store_set_prefetch_n.argtypes = [C.c_void_p, C.c_int]
+        L.clb200_store_set_prefetch_depth.argtypes = [C.c_void_p, C.c_int]
         L.clb200_store_log.argtypes = [C.c_void_p, C.c_int]
         L.clb200_store_read_log.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
         L.clb200_store_read_log.restype = C.c_int64
@@ -472,8 +474,22 @@ class Store:
     def reset_stats(self) -> None:
         self.L.clb200_store_reset_stats(self.h)
 
-    def set_prefetch(self, on: bool) -> None:
-        self.L.clb200_store_set_prefetch(self.h, int(on))
+    PREFETCH_OFF, PREFETCH_PREV, PREFETCH_AHEAD = 0, 1, 2
+
+    def set_prefetch_depth(self, depth: int) -> None:
+        self.L.clb200_store_set_prefetch_depth(self.h, int(depth))
+
+    def prefetch(self, layer: int, expert: int) -> None:
+        """Stages one expert (clb200_store_prefetch, the reference's cl_xs_prefetch)."""
+        self.L.clb200_store_prefetch(self.h, int(layer), int(expert))
+
+    def set_prefetch(self, mode: int, n: int = 0, depth: int | None = None) -> None:
+        """mode 0 off, 1 prev (the previous token's choice), 2 ahead (the next layer's router on this x); n experts staged per
+        prediction (0: n_used); depth: prefetch fills in flight at once."""
+        self.L.clb200_store_set_prefetch(self.h, int(mode))
+        self.L.clb200_store_set_prefetch_n(self.h, int(n))
+        if depth is not None:
+            self.L.clb200_store_set_prefetch_depth(self.h, int(depth))
 
     def log(self, on: bool) -> None:
         self.L.clb200_store_log(self.h, int(on))

@@ -32,7 +32,7 @@ static Scratch plan_scratch(int T, int E, int FF, int NE, int K, bool batched) {
   s.off_x = take(static_cast<size_t>(T) * E * 4);
   s.off_sel = take(TK * 4);
   s.off_wt = take(TK * 4);
-  s.off_logits = take(static_cast<size_t>(T) * NE * 4);
+  s.off_logits = take(static_cast<size_t>(T < 2 ? 2 : T) * NE * 4);   // one token: router-ahead's logits follow the layer's
   s.off_hg = take(static_cast<size_t>(K) * FF * 4);
   if (batched) {
     s.off_xn = take(static_cast<size_t>(T) * E * 4);
@@ -234,7 +234,7 @@ static int launch_group(clb200_ctx *c, const clb200_moe_layer &L, GroupArgs &g, 
 
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
                const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
-               const SmartRoute *smart, float *x_out, int *err_out) {
+               const SmartRoute *smart, float *x_out, int *err_out, const AheadRoute *ahead) {
   const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
   if (mode == 0 && !smart && c->decode_kernel == 0 && !c->stall_wait) {
     GroupArgs g{};
@@ -275,6 +275,18 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
     a.smart_M = smart->M;
     a.smart_tau = smart->tau;
     a.smart_stats = smart->stats;
+  }
+  if (mode == 1 && ahead && ahead->n > 0) {   // the next layer's rows, products and logits must fit in the free expert slots
+    const size_t nre = static_cast<size_t>((NE + c->sms - 1) / c->sms);
+    const size_t need = (static_cast<size_t>(E) + nre * E + nre * 8 * (E / 8 + 4) + static_cast<size_t>(NE)) * 4;
+    if (need > static_cast<size_t>(K) * a.slot_bytes || ahead->n > NE) {
+      errf(err, errlen, "router-ahead does not fit this layer's one-token plan (%zu bytes, %d experts)", need, ahead->n);
+      return 1;
+    }
+    a.ahead_norm = ahead->norm;
+    a.ahead_router = ahead->router;
+    a.ahead_n = ahead->n;
+    a.ahead_out = ahead->out;
   }
   if (mode == 2)
     for (int k = 0; k < K; ++k) {

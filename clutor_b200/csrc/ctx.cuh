@@ -140,9 +140,16 @@ struct SmartRoute {
   double tau;
   void *stats;               // device-visible RouteStats
 };
+// Router-ahead for a routing-only launch (c/src/forward.c:937-946): the next layer's norm and router (device), and where
+// its top n experts go (device-visible [n]).
+struct AheadRoute {
+  const float *norm, *router;
+  int n;
+  int *out;
+};
 int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, const int *sel_in, const float *wt_in,
                const uint8_t *const *slabs, int *sel_out, float *wt_out, cudaStream_t st, char *err, size_t errlen,
-               const SmartRoute *smart = nullptr, float *x_out = nullptr, int *err_out = nullptr);
+               const SmartRoute *smart = nullptr, float *x_out = nullptr, int *err_out = nullptr, const AheadRoute *ahead = nullptr);
 // The MoE block of layer dl on T tokens of device data x (updated in place), queued on st: the one-token kernel for T = 1,
 // the batched kernels otherwise; sel / wt (device, [T * n_used]) may be null.
 int run_moe_block(clb200_ctx *c, const DevLayer &dl, float *x, int T, int *sel, float *wt, cudaStream_t st, char *err,

@@ -14,6 +14,9 @@
 //   2  the last warp forms this CTA's router logits as the reference's dotf does (c/src/forward.c:574-581): eight lanes per
 //      expert, eight strided float sums in element order, combined ((0+1)+(2+3))+((4+5)+(6+7)); logits to global memory,
 //      counter 0 += experts scored. Meanwhile the warps of the other SM sub-partitions form the Q8_K blocks of xn;
+//      In mode 1 with router-ahead, the next layer's norm and router rows stream into the free expert slots too, and the
+//      idle warp of the router warp's sub-partition forms the next layer's logits on this x the same way (counter 0 then
+//      counts 2 NE); CTA 0 ranks them after phase 3 (c/src/forward.c:937-946);
 //   3  when counter 0 reaches NE, DECODE_THREADS / 4 threads form the softmax, one expert each (double sum,
 //      c/src/forward.c:954-958); every thread then ranks a quarter of an expert's competitors (ties to the lower id: the
 //      order of the reference's repeated arg-max, c/src/forward.c:975-980); warp 0 renormalises (c/src/forward.c:984).
@@ -74,6 +77,12 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   const int nre = (a.mode != 2 && c < NE) ? (NE - c + G - 1) / G : 0;   // experts this CTA scores: c, c+G, ...
   const uint32_t grb = a.grb, drb = a.drb, gseg = a.gseg;
   const int RS = E / 8 + 4;   // row stride of rprod (floats): the eight rows start in different banks
+  // router-ahead (mode 1 only): the next layer's norm weights, router rows, products and logits in the expert slots
+  const bool ahead = a.mode == 1 && a.ahead_n > 0;
+  float *wn2 = reinterpret_cast<float *>(slots);
+  float *rrows2 = wn2 + E;
+  float *rprod2 = rrows2 + static_cast<size_t>(nre) * E;
+  float *lg2 = rprod2 + static_cast<size_t>(nre) * 8 * RS;
 
   trace_time(a.trace, 30);
   trace_stamp(a.trace, 0);
@@ -81,10 +90,15 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   if (tid == 0) {
     for (int s = 0; s <= K; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
-    mbar_arrive_expect_tx(&bars[K], static_cast<uint32_t>(nre + 1) * E * 4u);
+    mbar_arrive_expect_tx(&bars[K], static_cast<uint32_t>(nre + 1) * E * 4u * (ahead ? 2u : 1u));
     bulk_copy_g2s(wn, a.norm, E * 4u, &bars[K]);
     for (int m = 0; m < nre; ++m)
       bulk_copy_g2s(rrows + static_cast<size_t>(m) * E, a.router + static_cast<size_t>(c + m * G) * E, E * 4u, &bars[K]);
+    if (ahead) {
+      bulk_copy_g2s(wn2, a.ahead_norm, E * 4u, &bars[K]);
+      for (int m = 0; m < nre; ++m)
+        bulk_copy_g2s(rrows2 + static_cast<size_t>(m) * E, a.ahead_router + static_cast<size_t>(c + m * G) * E, E * 4u, &bars[K]);
+    }
     s_flag[0] = 0;
     s_flag[1] = 0;
   }
@@ -131,6 +145,14 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
         for (int m = 0; m < nre; ++m)   // the router products, laid out for the strided sums of phase 2
 #pragma unroll
           for (int q = 0; q < 4; ++q) rprod[(m * 8 + ((i + q) & 7)) * RS + ((i + q) >> 3)] = __fmul_rn(rrows[m * E + i + q], nn[q]);
+        if (ahead) {   // the next layer's rmsnorm of the same x (the same scale), and its router products
+          const float4 w2 = reinterpret_cast<const float4 *>(wn2 + i)[0];
+          const float n2[4] = {__fmul_rn(__fmul_rn(v.x, scale), w2.x), __fmul_rn(__fmul_rn(v.y, scale), w2.y),
+                               __fmul_rn(__fmul_rn(v.z, scale), w2.z), __fmul_rn(__fmul_rn(v.w, scale), w2.w)};
+          for (int m = 0; m < nre; ++m)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) rprod2[(m * 8 + ((i + q) & 7)) * RS + ((i + q) >> 3)] = __fmul_rn(rrows2[m * E + i + q], n2[q]);
+        }
       }
     }
     __syncthreads();
@@ -138,41 +160,47 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
 
   trace_stamp(a.trace, 4);
   // ---- 2: this CTA's router logits (last warp), the Q8_K blocks of xn (the other warps) ------------------------------------
+  // one warp forms this CTA's logits from a product buffer: eight lanes per expert, four experts per pass
+  auto score = [&](const float *prod, float *out, bool stamp) {
+    const int grp = lane >> 3, l8 = lane & 7;
+    for (int m0 = 0; m0 < nre; m0 += 4) {   // four experts per pass, eight lanes each
+      const int m = m0 + grp;
+      float s = 0.f;
+      if (m < nre) {   // lane l8 adds products l8, l8 + 8, l8 + 16, ... in order: its row of the products, four float4 at a
+                       // time, the next four loaded while these are added (E / 32, the float4 per lane, is a multiple of 8)
+        const float4 *p4 = reinterpret_cast<const float4 *>(prod + (m * 8 + l8) * RS);
+        float4 v[4], w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v[t] = w[t] = p4[t];
+        for (int q = 0; q < E / 32; q += 4) {
+          if (q + 4 < E / 32) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) w[t] = p4[q + 4 + t];
+          }
+#pragma unroll
+          for (int t = 0; t < 4; ++t) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[t].x), v[t].y), v[t].z), v[t].w);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = w[t];
+        }
+      }
+      if (stamp && lane == 0 && m0 == 0) trace_stamp_here(a.trace, 24);
+      float p8[8];
+#pragma unroll
+      for (int l = 0; l < 8; ++l) p8[l] = __shfl_sync(FULL, s, (lane & ~7) + l);
+      if (m < nre && l8 == 0)
+        out[c + m * G] = __fadd_rn(__fadd_rn(__fadd_rn(p8[0], p8[1]), __fadd_rn(p8[2], p8[3])),
+                                   __fadd_rn(__fadd_rn(p8[4], p8[5]), __fadd_rn(p8[6], p8[7])));
+    }
+    __syncwarp();
+    if (lane == 0) red_release_add(&a.sync[0], static_cast<uint32_t>(nre));   // release: the warp's logits, ordered by bar.warp.sync
+  };
   if (warp == RW) {
     if (nre > 0) {
-      const int grp = lane >> 3, l8 = lane & 7;
-      for (int m0 = 0; m0 < nre; m0 += 4) {   // four experts per pass, eight lanes each
-        const int m = m0 + grp;
-        float s = 0.f;
-        if (m < nre) {   // lane l8 adds products l8, l8 + 8, l8 + 16, ... in order: its row of rprod, four float4 at a time,
-                         // the next four loaded while these are added (E / 32, the float4 per lane, is a multiple of 8)
-          const float4 *p4 = reinterpret_cast<const float4 *>(rprod + (m * 8 + l8) * RS);
-          float4 v[4], w[4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) v[t] = w[t] = p4[t];
-          for (int q = 0; q < E / 32; q += 4) {
-            if (q + 4 < E / 32) {
-#pragma unroll
-              for (int t = 0; t < 4; ++t) w[t] = p4[q + 4 + t];
-            }
-#pragma unroll
-            for (int t = 0; t < 4; ++t) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[t].x), v[t].y), v[t].z), v[t].w);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) v[t] = w[t];
-          }
-        }
-        if (lane == 0 && m0 == 0) trace_stamp_here(a.trace, 24);
-        float p8[8];
-#pragma unroll
-        for (int l = 0; l < 8; ++l) p8[l] = __shfl_sync(FULL, s, (lane & ~7) + l);
-        if (m < nre && l8 == 0)
-          a.logits[c + m * G] = __fadd_rn(__fadd_rn(__fadd_rn(p8[0], p8[1]), __fadd_rn(p8[2], p8[3])),
-                                          __fadd_rn(__fadd_rn(p8[4], p8[5]), __fadd_rn(p8[6], p8[7])));
-      }
-      __syncwarp();
-      if (lane == 0) red_release_add(&a.sync[0], static_cast<uint32_t>(nre));   // release: the warp's logits, ordered by bar.warp.sync
+      score(rprod, a.logits, true);
       if (lane == 0) trace_stamp_here(a.trace, 5);
     }
+  } else if (warp == RW - 4 && ahead) {   // idle in mode 1: the router warp's sub-partition, the next layer's logits
+    if (nre > 0) score(rprod2, a.logits + NE, false);
   } else if ((warp & 3) != (RW & 3)) {
     // the warps of the other three SM sub-partitions form the Q8_K blocks of xn, so none competes with the router warp's
     // chains for issue slots (a warp's sub-partition is its index mod 4)
@@ -191,7 +219,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       s_wn[tid] = a.wt_in[tid];
     }
   } else if (tid == 0 && !(a.stall_wait ? wait_counter(&a.sync[0], static_cast<uint32_t>(NE) + 1u, a.stall_wait)
-                                         : wait_counter(&a.sync[0], static_cast<uint32_t>(NE)))) {
+                                         : wait_counter(&a.sync[0], static_cast<uint32_t>(NE) * (ahead ? 2u : 1u)))) {
     set_error(a.err, ERR_WAIT_ROUTER);
     s_flag[0] = 1;
   }
@@ -247,6 +275,23 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   }
   __syncthreads();
   trace_stamp(a.trace, 11);
+  if (ahead && c == 0 && !s_flag[0]) {
+    // router-ahead's choice (c/src/forward.c:940-945): repeated arg-max over the next layer's logits, ties to the lower
+    // id, is the order of rank = experts with a larger logit + equal logits of lower ids
+    if (tid < NE) lg2[tid] = __ldcg(a.logits + NE + tid);
+    __syncthreads();
+    if (tid < NE) {
+      const float v = lg2[tid];
+      int rank = 0;
+#pragma unroll 4
+      for (int f = 0; f < NE; ++f) {
+        const float u = lg2[f];
+        rank += (u > v) || (u == v && f < tid);
+      }
+      if (rank < a.ahead_n) a.ahead_out[rank] = tid;
+    }
+    __syncthreads();   // the slots are SMART-ROUTE's scratch next
+  }
   if (a.mode == 1 && a.resident && c == 0 && !s_flag[0]) {
     // SMART-ROUTE (c/src/forward.c:961-969): cl_route's choice against the layer's resident set, each chosen expert weighted
     // by its own router probability; scratch in the expert slots, which routing-only launches leave unused

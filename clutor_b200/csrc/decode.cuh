@@ -20,7 +20,7 @@ struct DecodeArgs {
   uint32_t gate_type, up_type, down_type;
   int E, FF, NE, K, norm_topk;
   float resid_scale, eps;
-  float *logits;                 // [NE] scratch
+  float *logits;                 // [NE] scratch ([2 NE] with router-ahead)
   float *hg;                     // [K * FF] scratch
   int *sel_out;                  // [K] or null
   float *wt_out;                 // [K] or null
@@ -48,6 +48,12 @@ struct DecodeArgs {
   int smart_J, smart_M;
   double smart_tau;
   void *smart_stats;
+  // router-ahead in mode 1 (ahead_n 0: off; c/src/forward.c:937-946): the next layer's norm and router applied to this x
+  // (logits to logits[NE, 2 NE)); CTA 0 writes the next layer's top ahead_n experts by logit, ties to the lower id, to
+  // ahead_out (device-visible). Its rows and products use the expert slots, which routing-only launches leave free.
+  const float *ahead_norm, *ahead_router;
+  int ahead_n;
+  int *ahead_out;
   // phase trace (null: off): thread 0 of CTA c writes its SM's cycle counter at phase boundary i to trace[32 * c + i] and the global
   // nanosecond timer at entry and exit to trace[32 * c + 30] and [31]
   unsigned long long *trace;

@@ -10,6 +10,14 @@
 // (c/src/forward.c:888-1033 with an expert store): stage the next layer's experts as the previous token chose them, route
 // (the one-token kernel in routing mode; its choice comes back to the host), request the chosen experts resident ones first
 // (c/src/forward.c:992-997), wait, run the experts from their slots (the one-token kernel in given-routing mode), release.
+// Prefetch modes follow the reference's --prefetch: 1 (prev) stages the next layer's experts as the previous token chose
+// them (c/src/forward.c:889, :894); 2 (ahead) applies the next layer's norm and router to this layer's x inside the same
+// routing launch and stages its top prefetch_n (c/src/forward.c:937-946).
+//
+// Copies: demand fills go on the copy stream at once; prefetch fills wait on the host until fewer than `depth` prefetch
+// fills are in flight, so a demand fill queues behind at most that many (the reference's I/O workers take every demand read
+// before any prefetch read, c/src/xs.c:34-47). A demand for an expert whose prefetch is still waiting sends it at once.
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <vector>
@@ -54,7 +62,13 @@ struct clb200_store {
   clb200_smart smart{};
   clb200_smart_stats smart_st{};
   std::vector<int> prev_sel;             // [n_layer * K] the previous token's choice, -1 before the first
-  int prefetch = 1;
+  std::vector<int> pred_sel;             // [n_layer * K] what was staged for this token's layer, -1 for none
+  int prefetch = 1;                      // 0 off, 1 prev, 2 ahead
+  int prefetch_n = 0;                    // experts a prediction stages (0: n_used)
+  int depth = 2;                         // prefetch fills on the copy stream at once
+  struct Pending { int buf, layer, expert; };
+  std::vector<Pending> pending;          // prefetch fills decided, not yet on the copy stream (oldest first)
+  int *ahead_host = nullptr;             // pinned, device-visible: router-ahead's choice
   clb200_store_stats st{};
   uint64_t dev_bytes = 0;                // device memory counted in the context's total
   bool logging = false;
@@ -90,7 +104,34 @@ void count_copy(clb200_store *s, int buf) {   // the fill of `buf` has completed
   s->timed[buf] = 1;
 }
 
-// Staging fills that have landed: ready, and unpinned (the reference's I/O worker does this when a prefetch read ends).
+void fill(clb200_store *s, int buf, int layer, int expert, bool prefetch);
+
+// Prefetch fills go on the copy stream while fewer than `depth` are in flight there.
+void pump(clb200_store *s) {
+  size_t i = 0;
+  while (i < s->pending.size() && static_cast<int>(s->staged.size()) < s->depth) {
+    const clb200_store::Pending p = s->pending[i++];
+    fill(s, p.buf, p.layer, p.expert, true);
+    s->staged.push_back(p.buf);
+  }
+  s->pending.erase(s->pending.begin(), s->pending.begin() + static_cast<long>(i));
+}
+
+// A prefetch of `buf` still waiting on the host goes on the copy stream now (a demand needs it); false if none waits.
+bool promote(clb200_store *s, int buf) {
+  for (size_t i = 0; i < s->pending.size(); ++i)
+    if (s->pending[i].buf == buf) {
+      const clb200_store::Pending p = s->pending[i];
+      s->pending.erase(s->pending.begin() + static_cast<long>(i));
+      fill(s, p.buf, p.layer, p.expert, true);
+      s->staged.push_back(p.buf);
+      return true;
+    }
+  return false;
+}
+
+// Staging fills that have landed: ready, and unpinned (the reference's I/O worker does this when a prefetch read ends);
+// then waiting prefetch fills take the places freed.
 void poll(clb200_store *s) {
   size_t keep = 0;
   for (size_t i = 0; i < s->staged.size(); ++i) {
@@ -112,6 +153,7 @@ void poll(clb200_store *s) {
   }
   s->staged.resize(keep);
   cudaGetLastError();   // a "not ready" answer is not an error
+  pump(s);
 }
 
 // cl_xs_resident (c/src/xs.c:179-186) for every expert of `layer`, into the pinned residency bytes the kernels read.
@@ -164,6 +206,7 @@ clb200_store *clb200_store_open(clb200_ctx *c, const clb200_moe_layer *shape, in
   s->layer.assign(n_layer, *shape);
   s->loaded.assign(n_layer, 0);
   s->prev_sel.assign(static_cast<size_t>(n_layer) * s->K, -1);
+  s->pred_sel.assign(static_cast<size_t>(n_layer) * s->K, -1);
   uint32_t slots = static_cast<uint32_t>(cache_bytes / s->stride);
   if (slots < static_cast<uint32_t>(s->K)) slots = static_cast<uint32_t>(s->K);   // a layer's experts must fit at once (xs.c:103)
   s->cache = clb200_cache_new(slots, stage_slots < 0 ? 0u : static_cast<uint32_t>(stage_slots),
@@ -180,6 +223,7 @@ clb200_store *clb200_store_open(clb200_ctx *c, const clb200_moe_layer *shape, in
             cudaHostAlloc(reinterpret_cast<void **>(&s->sel_host), 64 * sizeof(int), cudaHostAllocMapped) == cudaSuccess &&
             cudaHostAlloc(reinterpret_cast<void **>(&s->wt_host), 64 * sizeof(float), cudaHostAllocMapped) == cudaSuccess &&
             cudaHostAlloc(reinterpret_cast<void **>(&s->smart_host), SMART_HOST_BYTES, cudaHostAllocMapped) == cudaSuccess &&
+            cudaHostAlloc(reinterpret_cast<void **>(&s->ahead_host), 64 * sizeof(int), cudaHostAllocMapped) == cudaSuccess &&
             cudaStreamCreateWithFlags(&s->copy, cudaStreamNonBlocking) == cudaSuccess;
   s->state.assign(nbuf, S_EMPTY);
   s->fill_failed.assign(nbuf, 0);
@@ -224,6 +268,7 @@ void clb200_store_close(clb200_store *s) {
   if (s->sel_host) cudaFreeHost(s->sel_host);
   if (s->wt_host) cudaFreeHost(s->wt_host);
   if (s->smart_host) cudaFreeHost(s->smart_host);
+  if (s->ahead_host) cudaFreeHost(s->ahead_host);
   if (s->cache) clb200_cache_free(s->cache);
   delete s;
 }
@@ -257,7 +302,11 @@ int clb200_store_load_layer(clb200_store *s, int layer, const clb200_moe_layer *
 
 uint32_t clb200_store_cache_slots(const clb200_store *s) { return s ? s->total : 0; }
 uint64_t clb200_store_slot_bytes(const clb200_store *s) { return s ? s->stride : 0; }
-void clb200_store_set_prefetch(clb200_store *s, int on) { if (s) s->prefetch = on; }
+void clb200_store_set_prefetch(clb200_store *s, int mode) { if (s) s->prefetch = mode < 0 ? 0 : mode > 2 ? 2 : mode; }
+
+void clb200_store_set_prefetch_n(clb200_store *s, int n) { if (s) s->prefetch_n = n < 0 ? 0 : n; }
+
+void clb200_store_set_prefetch_depth(clb200_store *s, int depth) { if (s) s->depth = depth < 1 ? 1 : depth; }
 
 int clb200_store_request(clb200_store *s, int layer, int expert) {
   if (!valid_expert(s, layer, expert)) return -1;
@@ -273,6 +322,7 @@ int clb200_store_request(clb200_store *s, int layer, int expert) {
     ++s->st.stage_hits;
     ++s->st.hits;
     if (s->state[slot] != S_READY) ++s->st.prefetch_late;
+    promote(s, slot);
   } else {
     ++s->st.misses;
     if (r == -1) {   // nothing evictable: a bypass buffer outside the cache (xs.c:160-163)
@@ -287,6 +337,7 @@ int clb200_store_request(clb200_store *s, int layer, int expert) {
 const void *clb200_store_wait(clb200_store *s, int h) {
   if (!s || h < 0 || h >= static_cast<int>(s->total + s->nbypass)) return nullptr;
   if (s->state[h] != S_READY && !s->failed) {
+    poll(s);   // prefetch fills freed by landed ones join the copy stream behind this one
     const uint64_t t0 = now_ns();
     const cudaError_t e = cudaEventSynchronize(s->filled[h]);
     s->st.wait_ns += now_ns() - t0;
@@ -335,9 +386,10 @@ void clb200_store_prefetch(clb200_store *s, int layer, int expert) {
   const int slot = clb200_cache_stage(s->cache, key);
   log_op(s, 2, key, slot);
   if (slot < 0) return;
-  fill(s, slot, layer, expert, true);
-  s->staged.push_back(slot);
+  s->state[slot] = S_LOADING;
+  s->pending.push_back({slot, layer, expert});
   ++s->st.prefetch_issued;
+  pump(s);
 }
 
 clb200_store_stats clb200_store_get_stats(const clb200_store *s) {
@@ -416,12 +468,21 @@ int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, i
   if (!x) { errf(err, errlen, "no activations"); return 1; }
   cudaSetDevice(c->device);
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-  const int K = s->K;
-  // the next layer's experts as the previous token chose them, read while this layer routes and computes
-  if (s->prefetch && layer + 1 < s->n_layer && s->loaded[layer + 1])
-    for (int k = 0; k < K; ++k) {
+  const int K = s->K, pn = s->prefetch_n > 0 && s->prefetch_n < K ? s->prefetch_n : K;
+  int *pred_next = layer + 1 < s->n_layer ? s->pred_sel.data() + static_cast<size_t>(layer + 1) * K : nullptr;
+  if (layer == 0) {   // a new token (c/src/forward.c:888-889): nothing predicted yet; layer 0 as the previous token chose it
+    std::fill(s->pred_sel.begin(), s->pred_sel.end(), -1);
+    if (s->prefetch)
+      for (int k = 0; k < pn; ++k) {
+        clb200_store_prefetch(s, 0, s->prev_sel[k]);
+        s->pred_sel[k] = s->prev_sel[k];
+      }
+  }
+  if (s->prefetch == 1 && pred_next)   // the next layer as the previous token chose it (c/src/forward.c:894)
+    for (int k = 0; k < pn; ++k) {
       const int e = s->prev_sel[static_cast<size_t>(layer + 1) * K + k];
-      if (e >= 0) clb200_store_prefetch(s, layer + 1, e);
+      clb200_store_prefetch(s, layer + 1, e);
+      pred_next[k] = e;
     }
   SmartRoute sr{};
   const bool smart = s->smart.enabled != 0;
@@ -433,9 +494,23 @@ int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, i
     sr.tau = s->smart.tau;
     sr.stats = s->smart_host + SMART_STATS;
   }
-  if (launch_one(c, s->layer[layer], x, 1, nullptr, nullptr, nullptr, s->sel_host, s->wt_host, st, err, errlen, smart ? &sr : nullptr))
+  AheadRoute ar{};
+  const bool ahead = s->prefetch == 2 && pred_next && s->loaded[layer + 1];
+  if (ahead) {   // the next layer's router on this x, in the same routing launch
+    ar.norm = s->layer[layer + 1].ffn_norm_f;
+    ar.router = s->layer[layer + 1].router_f;
+    ar.n = pn;
+    ar.out = s->ahead_host;
+  }
+  if (launch_one(c, s->layer[layer], x, 1, nullptr, nullptr, nullptr, s->sel_host, s->wt_host, st, err, errlen, smart ? &sr : nullptr,
+                 nullptr, nullptr, ahead ? &ar : nullptr))
     return 1;
   CUDA_OR(cudaStreamSynchronize(st), "routing");
+  if (ahead)   // staged before this layer's requests, in the reference's order; their copies follow the demand fills
+    for (int k = 0; k < pn; ++k) {
+      clb200_store_prefetch(s, layer + 1, s->ahead_host[k]);
+      pred_next[k] = s->ahead_host[k];
+    }
   if (smart) count_smart(s, *reinterpret_cast<const RouteStats *>(s->smart_host + SMART_STATS));
   s->smart_st.expert_slots += static_cast<uint64_t>(K);
   int sel[DECODE_MAX_K];
@@ -444,6 +519,13 @@ int clb200_moe_ffn_stored(clb200_ctx *c, clb200_store *s, int layer, float *x, i
     sel[k] = s->sel_host[k];
     wt[k] = s->wt_host[k];
     s->prev_sel[static_cast<size_t>(layer) * K + k] = sel[k];
+  }
+  for (int k = 0; k < pn; ++k) {   // how many staged experts the router then chose (c/src/forward.c:978-983)
+    const int pe = s->pred_sel[static_cast<size_t>(layer) * K + k];
+    if (pe < 0) continue;
+    ++s->st.pred_total;
+    for (int j = 0; j < K; ++j)
+      if (sel[j] == pe) { ++s->st.pred_hit; break; }
   }
   if (experts_stored(c, s, layer, x, sel, wt, nullptr, st, err, errlen)) return 1;
   if (sel_out) std::memcpy(sel_out, sel, K * sizeof(int));

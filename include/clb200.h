@@ -183,6 +183,8 @@ uint32_t clb200_cache_count(const clb200_cache *c);                        /* cl
 typedef struct {   /* cl_xs_stats (xs.h:14-17); copy_ns = time the copy engine spent filling slots (cl_xs_stats.read_ns) */
   uint64_t accesses, hits, stage_hits, misses, bypass, prefetch_issued, prefetch_late, prefetch_wasted, admit_rejects, evictions;
   uint64_t demand_bytes, prefetch_bytes, copy_ns, wait_ns;
+  uint64_t pred_total, pred_hit;   /* clb200_moe_ffn_stored: experts staged for a layer, and how many of them its router chose
+                                      (the forward pass's pred_total / pred_hit, c/src/forward.h:63) */
 } clb200_store_stats;
 typedef struct clb200_store clb200_store;
 /* cl_xs_open (xs.c:89-120): n_layer layers shaped like `shape`, HBM slots for cache_bytes (at least n_used slots), stage_slots
@@ -203,9 +205,16 @@ int clb200_store_resident(clb200_store *s, int layer, int expert);              
 void clb200_store_prefetch(clb200_store *s, int layer, int expert);               /* cl_xs_prefetch */
 clb200_store_stats clb200_store_get_stats(const clb200_store *s);                 /* cl_xs_get_stats */
 void clb200_store_reset_stats(clb200_store *s);                                   /* cl_xs_reset_stats */
-/* 1: clb200_moe_ffn_stored stages the next layer's experts as the previous token chose them (the reference's --prefetch, on
- * by default); 0: no prefetch. */
-void clb200_store_set_prefetch(clb200_store *s, int on);
+/* The prefetch mode of clb200_moe_ffn_stored (the reference's --prefetch, c/src/chat.c:229): 0 off; 1 (prev, the default)
+ * stages the next layer's experts as the previous token chose them (c/src/forward.c:889, :894); 2 (ahead) applies the next
+ * layer's norm and router to this layer's x inside the routing launch and stages its top prefetch_n experts
+ * (c/src/forward.c:937-946). */
+void clb200_store_set_prefetch(clb200_store *s, int mode);
+/* Experts a prediction stages (--prefetch-n; 0 or >= n_used: n_used, c/src/forward.c:305). */
+void clb200_store_set_prefetch_n(clb200_store *s, int n);
+/* Prefetch fills in flight on the copy stream at once (default 2, at least 1): prefetch fills decided beyond that wait on the
+ * host, so a demand fill queues behind at most this many (the reference's I/O queue takes demand reads first, xs.c:34-47). */
+void clb200_store_set_prefetch_depth(clb200_store *s, int depth);
 /* Test hooks: record every cache operation the store makes (triples: 1 access key -> code*65536+slot or -1, 2 stage key ->
  * slot, 3 unpin slot), and read the record (returns its length; copies at most cap values). */
 void clb200_store_log(clb200_store *s, int on);

@@ -438,3 +438,20 @@ def router_probs(layer, x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     wt = np.zeros(layer.K, np.float32)
     lib.orc_route(probs.ctypes.data, layer.NE, layer.K, layer.norm_topk, sel.ctypes.data, wt.ctypes.data)
     return logits, probs
+
+
+def router_ahead(next_layer, x: np.ndarray, n: int) -> np.ndarray:
+    """Router-ahead (c/src/forward.c:937-946): the NEXT layer's norm and router applied to this layer's x, and its top n
+    experts by raw logit, by repeated arg-max with ties to the lower id (a pure-Python loop: NE is small). next_layer: a
+    clutor_b200.synth.HostLayer. -> [n] int32 expert ids in pick order."""
+    logits, _ = router_probs(next_layer, x)
+    taken = np.zeros(next_layer.NE, bool)
+    picks = []
+    for _k in range(n):
+        best = -1
+        for e in range(next_layer.NE):
+            if not taken[e] and (best < 0 or logits[e] > logits[best]):
+                best = e
+        taken[best] = True
+        picks.append(best)
+    return np.array(picks, np.int32)
