@@ -327,7 +327,7 @@ class Context:
         """clb200_set_exact: batched expert products on the integer path only (bit-exact), or on the tensor cores."""
         lib().clb200_set_exact(self.handle, int(on))
 
-    OPT_DECODE_KERNEL, OPT_TEST_SPECULATION_MISS, OPT_TEST_STALL_WAIT = 1, 2, 3
+    OPT_DECODE_KERNEL, OPT_TEST_SPECULATION_MISS, OPT_TEST_STALL_WAIT, OPT_COOPERATIVE = 1, 2, 3, 4
 
     def set_option(self, option: int, value: int) -> None:
         """clb200_set_option: OPT_DECODE_KERNEL (0 expert-group kernel where it fits, 1 grid-wide kernel, the default) or

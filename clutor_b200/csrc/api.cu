@@ -117,14 +117,15 @@ int plan_decode_shape(int sms, int max_smem, const clb200_moe_layer &L, DecodeAr
   constexpr int NW = DECODE_THREADS / 32;
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = al(o + bytes, 16); return static_cast<uint32_t>(at); };
-  a.off_bars = take(8 * (K + 1));
+  a.off_bars = take(8 * (2 * K + 1));
   a.off_xn = take(static_cast<size_t>(E) * 4);
   a.off_norm = take(static_cast<size_t>(E) * 4);
   a.off_xq = take(static_cast<size_t>(E) + 2 * (E / 16) + 4 * (E / 256));
   a.off_router = take(static_cast<size_t>(nre) * E * 4);
   // products, one padded row per strided sum; later the weighted expert outputs of this CTA's rows, [rd_max][K]
   a.off_rprod = take(std::max(static_cast<size_t>(nre) * 8 * (E / 8 + 4), static_cast<size_t>(a.rd_max) * K) * 4);
-  a.off_misc = take(NW * 8 + 16 + 3 * 32 * 4 + (DECODE_THREADS / 4) * 4);   // probs: one per expert the kernel can rank
+  // reductions, flags, sel / wt / weights, probabilities and logits (one per expert the kernel can rank), slot tables
+  a.off_misc = take(NW * 8 + 16 + 3 * 32 * 4 + 2 * (DECODE_THREADS / 4) * 4 + (DECODE_MAX_K + 4) * 4 + 4 * DECODE_MAX_K * 4);
   a.off_terms = take(static_cast<size_t>(a.rd_max) * K * nbd * 4);
   a.off_hq = take(static_cast<size_t>(K) * FF + 2 * (static_cast<size_t>(K) * FF / 16) + 4 * (static_cast<size_t>(K) * FF / 256));
   a.off_xr = take(static_cast<size_t>(a.rd_max) * 4);
@@ -227,8 +228,37 @@ static int launch_group(clb200_ctx *c, const clb200_moe_layer &L, GroupArgs &g, 
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = c->cooperative ? 2 : 1;
   CUDA_OR(cudaLaunchKernelEx(&cfg, fn, g), "launching the expert-group kernel");
+  return 0;
+}
+
+// The one-token kernel's arguments for layer L (device pointers) in `mode`: plan, scratch, outputs and options (the
+// mode-specific inputs are the caller's).
+static int decode_args(clb200_ctx *c, const clb200_moe_layer &L, const float *x, int mode, int *sel_out, float *wt_out,
+                       float *x_out, int *err_out, DecodeArgs &a, char *err, size_t errlen) {
+  const int E = L.n_embd, FF = L.n_ff_exp, NE = L.n_expert, K = L.n_used;
+  if (plan_decode(c, L, a)) { errf(err, errlen, "the one-token kernel does not take this layer (K-quant experts only)"); return 1; }
+  const Scratch s = plan_scratch(1, E, FF, NE, K, false);
+  if (ensure_scratch(c, s.total, err, errlen)) return 1;
+  uint8_t *sc = c->scratch;
+  a.x_in = x; a.x_out = x_out ? x_out : const_cast<float *>(x);
+  a.err_out = err_out;
+  a.norm = L.ffn_norm_f; a.router = L.router_f;
+  a.gate = L.gate.p; a.up = L.up.p; a.down = L.down.p;
+  a.gate_slab = L.gate_slab; a.up_slab = L.up_slab; a.down_slab = L.down_slab;
+  a.gate_type = L.gate.type; a.up_type = L.up.type; a.down_type = L.down.type;
+  a.E = E; a.FF = FF; a.NE = NE; a.K = K; a.norm_topk = L.norm_topk;
+  a.resid_scale = L.resid_scale; a.eps = L.rms_eps;
+  a.logits = reinterpret_cast<float *>(sc + s.off_logits);
+  a.hg = reinterpret_cast<float *>(sc + s.off_hg);
+  a.sel_out = sel_out; a.wt_out = wt_out;
+  a.sync = reinterpret_cast<uint32_t *>(c->small + 64);
+  a.err = c->small;
+  a.trace = c->trace;
+  a.mode = mode;
+  a.stall_wait = mode == 0 ? c->stall_wait : 0u;
+  a.force_miss = mode == 0 ? c->force_miss : 0;
   return 0;
 }
 
@@ -245,26 +275,7 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   }
   c->signals_done = err_out != nullptr;
   DecodeArgs a{};
-  if (plan_decode(c, L, a)) { errf(err, errlen, "the one-token kernel does not take this layer (K-quant experts only)"); return 1; }
-  const Scratch s = plan_scratch(1, E, FF, NE, K, false);
-  if (ensure_scratch(c, s.total, err, errlen)) return 1;
-  uint8_t *sc = c->scratch;
-  a.x_in = x; a.x_out = x_out ? x_out : x;
-  a.err_out = err_out;
-  a.norm = L.ffn_norm_f; a.router = L.router_f;
-  a.gate = L.gate.p; a.up = L.up.p; a.down = L.down.p;
-  a.gate_slab = L.gate_slab; a.up_slab = L.up_slab; a.down_slab = L.down_slab;
-  a.gate_type = L.gate.type; a.up_type = L.up.type; a.down_type = L.down.type;
-  a.E = E; a.FF = FF; a.NE = NE; a.K = K; a.norm_topk = L.norm_topk;
-  a.resid_scale = L.resid_scale; a.eps = L.rms_eps;
-  a.logits = reinterpret_cast<float *>(sc + s.off_logits);
-  a.hg = reinterpret_cast<float *>(sc + s.off_hg);
-  a.sel_out = sel_out; a.wt_out = wt_out;
-  a.sync = reinterpret_cast<uint32_t *>(c->small + 64);
-  a.err = c->small;
-  a.trace = c->trace;
-  a.mode = mode;
-  a.stall_wait = mode == 0 ? c->stall_wait : 0u;
+  if (decode_args(c, L, x, mode, sel_out, wt_out, x_out, err_out, a, err, errlen)) return 1;
   if (mode == 1 && smart) {
     if (NE > ROUTE_SMEM_MAX_NE || static_cast<size_t>(NE) * 13 + 64 > static_cast<size_t>(K) * a.slot_bytes) {
       errf(err, errlen, "SMART-ROUTE in the one-token kernel takes at most %d experts", ROUTE_SMEM_MAX_NE);
@@ -319,7 +330,7 @@ int launch_one(clb200_ctx *c, const clb200_moe_layer &L, float *x, int mode, con
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = c->cooperative ? 2 : 1;
   CUDA_OR(cudaLaunchKernelEx(&cfg, fn, a), "launching the one-token kernel");
   return 0;
 }
@@ -381,6 +392,7 @@ int clb200_set_option(clb200_ctx *c, int option, int value) {
     case CLB200_OPT_DECODE_KERNEL: if (value < 0 || value > 1) return 1; c->decode_kernel = value; ++c->graph_gen; return 0;
     case CLB200_OPT_TEST_SPECULATION_MISS: c->force_miss = value != 0; ++c->graph_gen; return 0;
     case CLB200_OPT_TEST_STALL_WAIT: if (value < 0) return 1; c->stall_wait = static_cast<uint32_t>(value); ++c->graph_gen; return 0;
+    case CLB200_OPT_COOPERATIVE: c->cooperative = value != 0; ++c->graph_gen; return 0;
     default: return 1;
   }
 }

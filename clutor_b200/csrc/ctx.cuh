@@ -123,6 +123,7 @@ struct clb200_ctx {
   int decode_kernel = 1;                           // CLB200_OPT_DECODE_KERNEL
   bool signals_done = false;                       // the last one-token launch writes its error word to host memory on exit
   int force_miss = 0;                              // CLB200_OPT_TEST_SPECULATION_MISS
+  bool cooperative = true;                         // CLB200_OPT_COOPERATIVE
   uint32_t stall_wait = 0;                         // CLB200_OPT_TEST_STALL_WAIT
 };
 constexpr size_t GROUP_BUF_BYTES = size_t(4) << 20;   // >= group_buffer_bytes() of every shape the kernel takes

@@ -49,7 +49,8 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   const int E = a.E, FF = a.FF, NE = a.NE, K = a.K;
   const int nb = E / 256, nbd = FF / 256;
 
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);   // [K] expert slots, [K] router rows + norm weights
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);   // [K] slots' gate/up rows, [K] router rows + norm weights
+  uint64_t *dbar = bars + K + 1;                                       // [K] slots' down rows
   float *xn = reinterpret_cast<float *>(smem + a.off_xn);             // [E] xn
   float *wn = reinterpret_cast<float *>(smem + a.off_norm);           // [E] norm weights
   int8_t *xq_qs = reinterpret_cast<int8_t *>(smem + a.off_xq);        // Q8_K of xn: qs [E], bsums [E/16], d [E/256]
@@ -58,11 +59,17 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   float *rrows = reinterpret_cast<float *>(smem + a.off_router);      // [nre][E] router rows
   float *rprod = reinterpret_cast<float *>(smem + a.off_rprod);       // [nre][8][E/8 + 4]: product i in row i % 8, column i / 8
   double *s_red = reinterpret_cast<double *>(smem + a.off_misc);      // [NW]
-  int *s_flag = reinterpret_cast<int *>(s_red + NW);                   // [0] failed, [1] copies issued
+  int *s_flag = reinterpret_cast<int *>(s_red + NW);                   // [0] failed, [2] probability order differs
   int *s_sel = s_flag + 4;                                             // [32] chosen experts, rank order
   float *s_wt = reinterpret_cast<float *>(s_sel + 32);                 // [32] their router probabilities
   float *s_wn = s_wt + 32;                                             // [32] the weights the combine uses
   float *probs = s_wn + 32;                                            // [DECODE_THREADS / 4]
+  float *s_lg = probs + DECODE_THREADS / 4;                            // [DECODE_THREADS / 4] logits, -inf past NE
+  int *s_spec = reinterpret_cast<int *>(s_lg + DECODE_THREADS / 4);   // [DECODE_MAX_K + 1] slot k: the expert it streams
+  int *s_slot = s_spec + DECODE_MAX_K + 4;                             // [K] rank -> the slot streaming that expert
+  int *s_par = s_slot + DECODE_MAX_K;                                  // [K] parity of the phase the slot's copies complete
+  int *s_iss = s_par + DECODE_MAX_K;                                   // [K] copies issued into the slot: 1 gate/up, 2 down
+  int *s_fix = s_iss + DECODE_MAX_K;                                   // [K] expert + 1 to fetch into the slot again, or 0
   float *terms = reinterpret_cast<float *>(smem + a.off_terms);       // block terms of the down rows
   int8_t *hq_qs = reinterpret_cast<int8_t *>(smem + a.off_hq);        // Q8_K of every expert's hg: qs [K*FF], bsums, d
   int16_t *hq_bs = reinterpret_cast<int16_t *>(smem + a.off_hq + K * FF);
@@ -88,7 +95,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   trace_stamp(a.trace, 0);
   // ---- 0: barriers, router rows and norm weights (weights only, so before the dependency wait) ------------------------------
   if (tid == 0) {
-    for (int s = 0; s <= K; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s <= 2 * K; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
     mbar_arrive_expect_tx(&bars[K], static_cast<uint32_t>(nre + 1) * E * 4u * (ahead ? 2u : 1u));
     bulk_copy_g2s(wn, a.norm, E * 4u, &bars[K]);
@@ -100,7 +107,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
         bulk_copy_g2s(rrows2 + static_cast<size_t>(m) * E, a.ahead_router + static_cast<size_t>(c + m * G) * E, E * 4u, &bars[K]);
     }
     s_flag[0] = 0;
-    s_flag[1] = 0;
+    s_flag[2] = 0;
   }
   __syncthreads();          // the mbarriers are initialised before any thread waits on one
   grid_dependency_wait();   // x, the scratch and the counters belong to the previous kernel until here
@@ -209,7 +216,11 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     trace_stamp(a.trace, 6);
   }
 
-  // ---- 3: softmax, top-k by rank counting (every thread), renormalisation (c/src/forward.c:954-984) ----------------------
+  // ---- 3: routing (c/src/forward.c:954-984). Mode 0 ranks the experts by logit first and sends the expert copies out on
+  // that order at once: softmax is monotone, so it is the probability order except where two different logits round to
+  // the same probability. The softmax, the probability order and the weights follow while the copies fly; a slot whose
+  // expert turns out not to be chosen (a probability tie at rank K) fetches the missing one. -----------------------------
+  const bool spec = a.mode == 0;
   if (a.mode == 2) {   // the routing is given, renormalised already
     if (tid < K) {
       const int e = a.sel_in[tid];
@@ -217,33 +228,143 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       s_sel[tid] = e;
       s_wt[tid] = a.wt_in[tid];
       s_wn[tid] = a.wt_in[tid];
+      s_spec[tid] = e;
+      s_slot[tid] = tid;
     }
   } else if (tid == 0 && !(a.stall_wait ? wait_counter(&a.sync[0], static_cast<uint32_t>(NE) + 1u, a.stall_wait)
                                          : wait_counter(&a.sync[0], static_cast<uint32_t>(NE) * (ahead ? 2u : 1u)))) {
     set_error(a.err, ERR_WAIT_ROUTER);
     s_flag[0] = 1;
   }
+  if (tid < DECODE_MAX_K) { s_par[tid] = 0; s_iss[tid] = 0; s_fix[tid] = 0; }
+  if (a.mode != 2 && tid < DECODE_MAX_K) s_sel[tid] = -1;
+  if (spec && tid <= DECODE_MAX_K) s_spec[tid] = -1;
   __syncthreads();
   trace_stamp(a.trace, 7);
-  if (a.mode != 2 && !s_flag[0]) {   // the softmax over DECODE_THREADS / 4 threads, one expert each
-    constexpr int SW = DECODE_THREADS / 4 / 32;   // softmax warps
-    float *wmax = s_wt;                           // [SW] (s_wt is written after the ranking)
-    const float lv = tid < NE ? __ldcg(a.logits + tid) : -INFINITY;
-    float mx = lv;
+  constexpr int SW = DECODE_THREADS / 4 / 32;   // softmax warps, one expert per thread
+  float lv = -INFINITY, mx = -INFINITY, ev = 0.f;
+  if (a.mode != 2 && !s_flag[0]) {
+    lv = tid < NE ? __ldcg(a.logits + tid) : -INFINITY;
+    mx = lv;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-    if (lane == 0 && warp < SW) wmax[warp] = mx;
-    __syncthreads();
-    mx = wmax[0];
+    if (lane == 0 && warp < SW) s_wt[warp] = mx;   // s_wt is written after the ranking
+    // NaN ranks as -inf here, so the ranks by logit are a permutation and every slot gets one expert (a NaN routing then
+    // fails in the probability check below, with every copy accounted for)
+    if (spec && tid < DECODE_THREADS / 4) s_lg[tid] = lv == lv ? lv : -INFINITY;
+  }
+  __syncthreads();
+  trace_stamp(a.trace, 8);
+  if (a.mode != 2 && !s_flag[0]) {
+    mx = s_wt[0];
 #pragma unroll
-    for (int w = 1; w < SW; ++w) mx = fmaxf(mx, wmax[w]);
-    trace_stamp(a.trace, 8);
-    const float ev = tid < NE ? expf_cr(__fsub_rn(lv, mx)) : 0.f;
+    for (int w = 1; w < SW; ++w) mx = fmaxf(mx, s_wt[w]);
+  }
+  // rank of expert tid / 4 = experts ahead of it in the reference's arg-max order (ties to the lower id), counted by four
+  // threads over every fourth float4 of the values each (so the four read different banks; v padded with `pad`, below
+  // every value, to a multiple of 4)
+  auto rank4 = [&](const float *v, float pad) -> int {
+    const int e = tid >> 2, part = tid & 3, n4 = (NE + 3) / 4;
+    const float pe = e < NE ? v[e] : 0.f;
+    const float4 *p4 = reinterpret_cast<const float4 *>(v);
+    float4 q[8];   // n4 <= 32 (NE <= 128): every load in flight before the first comparison
+#pragma unroll
+    for (int u = 0; u < 8; ++u) q[u] = 4 * u + part < n4 ? p4[4 * u + part] : make_float4(pad, pad, pad, pad);
+    int rank = 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int f = 4 * (4 * u + part);
+      rank += (q[u].x > pe || (q[u].x == pe && f < e)) + (q[u].y > pe || (q[u].y == pe && f + 1 < e)) +
+              (q[u].z > pe || (q[u].z == pe && f + 2 < e)) + (q[u].w > pe || (q[u].w == pe && f + 3 < e));
+    }
+    rank += __shfl_xor_sync(FULL, rank, 1);
+    rank += __shfl_xor_sync(FULL, rank, 2);
+    return rank;
+  };
+  int my_rank = DECODE_MAX_K + 1;   // spec path: this thread's expert's rank by logit, if it owns one (tid % 4 == 0)
+  if (spec && !s_flag[0]) {   // the logit order through rank K
+    int rank = rank4(s_lg, -INFINITY);
+    if (a.force_miss && K < NE) rank = rank == K - 1 ? K : rank == K ? K - 1 : rank;   // test hook: ranks K - 1 and K swap
+    if ((tid >> 2) < NE && (tid & 3) == 0 && rank <= K) {
+      s_spec[rank] = tid >> 2;
+      my_rank = rank;
+    }
+  }
+  trace_stamp(a.trace, 21);
+
+  // ---- 4: bulk copies of this CTA's share of each slot's expert: gate and up rows [FF*c/G, FF*(c+1)/G) on the slot's first
+  // mbarrier, down rows [E*c/G, E*(c+1)/G) on its second; every gate/up request goes out before any down request ------------
+  auto seg_src = [&](int k, int q) -> const uint8_t * {
+    if (a.mode == 2 && a.slab[k]) {   // the store's copy: gate, up and down slabs back to back
+      const uint8_t *b = a.slab[k];
+      return q == 0 ? b + static_cast<size_t>(j0) * grb
+           : q == 1 ? b + a.gate_slab + static_cast<size_t>(j0) * grb
+                    : b + a.gate_slab + a.up_slab + static_cast<size_t>(i0) * drb;
+    }
+    const size_t e = static_cast<size_t>(s_spec[k]);
+    return q == 0 ? a.gate + e * a.gate_slab + static_cast<size_t>(j0) * grb
+         : q == 1 ? a.up + e * a.up_slab + static_cast<size_t>(j0) * grb
+                  : a.down + e * a.down_slab + static_cast<size_t>(i0) * drb;
+  };
+  auto seg_off = [&](int k, int q) -> uint32_t {   // shared offset (from slots) of row 0 of segment q of slot k
+    return static_cast<uint32_t>(k) * a.slot_bytes + (q == 0 ? 0u : q == 1 ? gseg : 2 * gseg) +
+           static_cast<uint32_t>(reinterpret_cast<uintptr_t>(seg_src(k, q)) & 15u);
+  };
+  auto issue = [&](int k, bool down) {   // one thread: slot k's gate and up segments, or its down segment
+    uint8_t *slot = slots + static_cast<size_t>(k) * a.slot_bytes;
+    uint64_t *bar = down ? &dbar[k] : &bars[k];
+    const int q0 = down ? 2 : 0, q1 = down ? 3 : 2;
+    uint32_t total = 0;
+    for (int q = q0; q < q1; ++q) {
+      const uint32_t len = q < 2 ? static_cast<uint32_t>(ngu) * grb : static_cast<uint32_t>(nd) * drb;
+      const uint32_t lo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(seg_src(k, q)) & 15u);
+      total += len ? (lo + len + 15u) & ~15u : 0u;
+    }
+    mbar_arrive_expect_tx(bar, total);
+    for (int q = q0; q < q1; ++q) {
+      const uint32_t len = q < 2 ? static_cast<uint32_t>(ngu) * grb : static_cast<uint32_t>(nd) * drb;
+      const uint8_t *src = seg_src(k, q);
+      const uint32_t lo = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(src) & 15u);
+      if (len) bulk_copy_g2s(slot + (q == 0 ? 0u : q == 1 ? gseg : 2 * gseg), src - lo, (lo + len + 15u) & ~15u, bar);
+    }
+  };
+  if (my_rank < K) {   // the thread that ranked a chosen expert sends its gate and up rows at once
+    issue(my_rank, false);
+    s_iss[my_rank] = 1;
+  }
+  trace_stamp(a.trace, 23);
+  __syncthreads();
+  trace_stamp(a.trace, 11);
+  const bool go = !s_flag[0] && a.mode != 1;
+  // one thread per slot: the down rows after every gate/up request of the CTA, from warps that take no part in the softmax
+  // where there are enough of them (an issue can wait while the copy unit takes the requests before it)
+  const int k_iss = SW + K <= NW ? warp - SW : warp;
+  if (go && k_iss >= 0 && k_iss < K && lane == 0) {
+    const int k = k_iss;
+    if (s_spec[k] < 0 || s_spec[k] >= NE || (spec && !(s_iss[k] & 1))) {   // logits that do not order (NaN)
+      set_error(a.err, ERR_BAD_EXPERT);
+      s_flag[0] = 1;
+    } else {
+      if (!spec) {
+        issue(k, false);
+        s_iss[k] = 1;
+      }
+      issue(k, true);
+      s_iss[k] |= 2;
+    }
+  }
+  trace_stamp(a.trace, 12);
+
+  // ---- 3 (continued): softmax (double sum, c/src/forward.c:954-958), the probability order, the weights -----------------------
+  if (a.mode != 2 && !s_flag[0]) {
+    ev = tid < NE ? expf_cr(__fsub_rn(lv, mx)) : 0.f;
     double part = static_cast<double>(ev);   // each warp's 32 experts by a shuffle tree, then the warps in order
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(FULL, part, o);
     if (lane == 0 && warp < SW) s_red[warp] = part;
-    __syncthreads();
+  }
+  __syncthreads();
+  if (a.mode != 2 && !s_flag[0]) {
     double tot = 0.0;
 #pragma unroll
     for (int w = 0; w < SW; ++w) tot += s_red[w];
@@ -253,28 +374,30 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   }
   __syncthreads();
   trace_stamp(a.trace, 20);
-  if (a.mode != 2 && !s_flag[0]) {   // rank = experts ahead of this one in the reference's arg-max order; four threads per expert
-    const int e = tid >> 2, part = tid & 3, n4 = (NE + 3) / 4, per = (n4 + 3) / 4;
-    const float pe = e < NE ? probs[e] : 0.f;
-    const float4 *p4 = reinterpret_cast<const float4 *>(probs);
-    float4 q[8];   // per <= 8 (NE <= 128): every load in flight before the first comparison; -1 (below every probability) past the end
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      q[u] = u < per && part * per + u < n4 ? p4[part * per + u] : make_float4(-1.f, -1.f, -1.f, -1.f);
-    int rank = 0;
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int f = 4 * (part * per + u);
-      rank += (q[u].x > pe || (q[u].x == pe && f < e)) + (q[u].y > pe || (q[u].y == pe && f + 1 < e)) +
-              (q[u].z > pe || (q[u].z == pe && f + 2 < e)) + (q[u].w > pe || (q[u].w == pe && f + 3 < e));
+  bool need_rank = a.mode == 1;
+  if (spec && !s_flag[0]) {
+    if (warp == 0) {   // strictly falling probabilities along the logit order through rank K: that order is the reference's
+      const int n = K < NE ? K + 1 : K;
+      const int se = lane < n ? s_spec[lane] : 0;
+      const float pl = lane < n && se >= 0 ? probs[se] : 0.f;
+      const float pn = __shfl_down_sync(FULL, pl, 1);
+      const bool strict = __all_sync(FULL, se >= 0 && (lane + 1 >= n || pl > pn));
+      if (strict && lane < K) {
+        s_sel[lane] = se;
+        s_wt[lane] = pl;
+        s_slot[lane] = lane;
+      }
+      if (lane == 0) s_flag[2] = strict ? 0 : 1;
     }
-    rank += __shfl_xor_sync(FULL, rank, 1);
-    rank += __shfl_xor_sync(FULL, rank, 2);
-    trace_stamp(a.trace, 21);
-    if (e < NE && part == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = pe; }
+    __syncthreads();
+    need_rank = s_flag[2] != 0;
+  }
+  if (need_rank && !s_flag[0]) {   // the full probability order
+    const int e = tid >> 2;
+    const int rank = rank4(probs, -1.0f);
+    if (e < NE && (tid & 3) == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = probs[e]; }
   }
   __syncthreads();
-  trace_stamp(a.trace, 11);
   if (ahead && c == 0 && !s_flag[0]) {
     // router-ahead's choice (c/src/forward.c:940-945): repeated arg-max over the next layer's logits, ties to the lower
     // id, is the order of rank = experts with a larger logit + equal logits of lower ids
@@ -303,6 +426,44 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     if (tid < K) s_wt[tid] = probs[s_sel[tid]];
     __syncthreads();
   }
+  if (spec && need_rank && !s_flag[0]) {
+    // which slot holds each chosen expert; a slot holding an expert outside the top k takes a missing one (both in order)
+    const int tk0 = tid < K ? s_sel[tid] : 0;
+    if (warp == 0 && __any_sync(FULL, tk0 < 0 || tk0 >= NE)) {   // logits that do not order (NaN): no expert to fetch
+      if (lane == 0) { set_error(a.err, ERR_BAD_EXPERT); s_flag[0] = 1; }
+    } else if (warp == 0) {
+      int gk = -1;
+      const int tk = lane < K ? s_sel[lane] : -2;
+      for (int h = 0; h < K; ++h) gk = s_spec[h] == tk ? h : gk;
+      const int sg = lane < K ? s_spec[lane] : -2;
+      bool in = false;
+      for (int k = 0; k < K; ++k) in |= s_sel[k] == sg;
+      const uint32_t orphan = __ballot_sync(FULL, lane < K && !in), missing = __ballot_sync(FULL, lane < K && gk < 0);
+      if (lane < K && gk < 0) {   // the missing rank's position among the missing ranks pairs it with the orphan at the same position
+        const int pos = __popc(missing & ((1u << lane) - 1u));
+        uint32_t o = orphan;
+        for (int t = 0; t < pos && o; ++t) o &= o - 1u;
+        gk = o ? __ffs(o) - 1 : -1;
+        if (gk >= 0) s_fix[gk] = tk + 1;
+      }
+      if (lane < K) s_slot[lane] = gk;
+      if (lane < K && (gk < 0 || tk < 0)) { set_error(a.err, ERR_BAD_EXPERT); s_flag[0] = 1; }   // two sets of K: cannot happen
+    }
+    __syncthreads();
+    if (warp < K && lane == 0 && s_fix[warp] && !s_flag[0]) {   // the wrong copies land first; then the right expert's
+      const int k = warp;
+      if (mbar_wait_bounded(&bars[k], 0) && mbar_wait_bounded(&dbar[k], 0)) {
+        s_spec[k] = s_fix[k] - 1;
+        issue(k, false);
+        issue(k, true);
+        s_par[k] = 1;
+      } else {
+        set_error(a.err, ERR_WAIT_COPY);
+        s_flag[0] = 1;
+      }
+    }
+    __syncthreads();
+  }
   if (a.mode != 2 && !s_flag[0] && warp == 0) {   // renormalise: every lane forms the same sum in rank order, by shuffles
     const float wk = lane < K ? s_wt[lane] : 0.f;
     float z = 0.f;
@@ -319,47 +480,9 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     trace_stamp(a.trace, 22);
   }
 
-  // ---- 4: bulk copies of this CTA's share of each chosen expert, one lane per expert ------------------------------------------
-  auto seg_src = [&](int k, int q) -> const uint8_t * {
-    if (a.mode == 2 && a.slab[k]) {   // the store's copy: gate, up and down slabs back to back
-      const uint8_t *b = a.slab[k];
-      return q == 0 ? b + static_cast<size_t>(j0) * grb
-           : q == 1 ? b + a.gate_slab + static_cast<size_t>(j0) * grb
-                    : b + a.gate_slab + a.up_slab + static_cast<size_t>(i0) * drb;
-    }
-    const size_t e = static_cast<size_t>(s_sel[k]);
-    return q == 0 ? a.gate + e * a.gate_slab + static_cast<size_t>(j0) * grb
-         : q == 1 ? a.up + e * a.up_slab + static_cast<size_t>(j0) * grb
-                  : a.down + e * a.down_slab + static_cast<size_t>(i0) * drb;
-  };
-  auto seg_off = [&](int k, int q) -> uint32_t {   // shared offset (from slots) of row 0 of segment q of expert k
-    return static_cast<uint32_t>(k) * a.slot_bytes + (q == 0 ? 0u : q == 1 ? gseg : 2 * gseg) +
-           static_cast<uint32_t>(reinterpret_cast<uintptr_t>(seg_src(k, q)) & 15u);
-  };
-  const bool go = !s_flag[0] && a.mode != 1;
-  if (go && lane == 0 && warp < K) {   // one warp per expert: their copy requests go out in parallel
-    const int k = warp;
-    uint8_t *slot = slots + static_cast<size_t>(k) * a.slot_bytes;
-    const uint32_t len[3] = {static_cast<uint32_t>(ngu) * grb, static_cast<uint32_t>(ngu) * grb, static_cast<uint32_t>(nd) * drb};
-    uint8_t *dst[3] = {slot, slot + gseg, slot + 2 * gseg};
-    uint32_t total = 0, lo[3], n16[3];
-    const uint8_t *src[3];
-    for (int q = 0; q < 3; ++q) {
-      src[q] = seg_src(k, q);
-      lo[q] = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(src[q]) & 15u);
-      n16[q] = len[q] ? (lo[q] + len[q] + 15u) & ~15u : 0u;
-      total += n16[q];
-    }
-    mbar_arrive_expect_tx(&bars[k], total);
-    trace_stamp(a.trace, 23);
-    for (int q = 0; q < 3; ++q)
-      if (n16[q]) bulk_copy_g2s(dst[q], src[q] - lo[q], n16[q], &bars[k]);
-    if (k == 0) s_flag[1] = 1;
-  }
-  trace_stamp(a.trace, 12);
-
   // ---- 5: gate and up rows: a group of lanes per (expert, row), one lane per block -------------------------------------------
-  if (go) {
+  const bool run = go && !s_flag[0];   // read after the last block barrier: the same in every thread
+  if (run) {
     const int GL = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : nb <= 8 ? 8 : 16;   // lanes per group
     const int lg = lane & (GL - 1), gpw = 32 / GL, ngroups = NW * gpw, gid = warp * gpw + lane / GL;
     const int tasks = K * ngu, base = lane - lg;
@@ -375,7 +498,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
       if (valid) {
         while (waited < k) {   // slots land in rank order; wait for each once
           ++waited;
-          if (!mbar_wait_bounded(&bars[waited], 0)) set_error(a.err, ERR_WAIT_COPY);
+          if (!mbar_wait_bounded(&bars[waited], static_cast<uint32_t>(s_par[waited]))) set_error(a.err, ERR_WAIT_COPY);
           if (waited == 0) trace_stamp(a.trace, 25);
         }
         if (has_blk) {
@@ -401,14 +524,14 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   trace_stamp(a.trace, 14);
 
   // ---- 6: every expert's hg, down rows, combine in rank order, residual ------------------------------------------------------
-  if (go && tid == 0 && !wait_counter(&a.sync[1], static_cast<uint32_t>(G))) { set_error(a.err, ERR_WAIT_EXPERT); s_flag[0] = 1; }
+  if (run && tid == 0 && !wait_counter(&a.sync[1], static_cast<uint32_t>(G))) { set_error(a.err, ERR_WAIT_EXPERT); s_flag[0] = 1; }
   __syncthreads();
   trace_stamp(a.trace, 15);
-  if (go && !s_flag[0]) {
+  if (run && !s_flag[0]) {
     q8k_quantize_global(a.hg, K * FF / 256, hq_qs, hq_d, hq_bs, warp, NW, lane, true);
     trace_stamp(a.trace, 16);
     for (int k = 0; k < K; ++k)   // every copy has landed (a CTA with no gate/up rows has not waited yet)
-      if (!mbar_wait_bounded(&bars[k], 0)) set_error(a.err, ERR_WAIT_COPY);
+      if (!mbar_wait_bounded(&dbar[k], static_cast<uint32_t>(s_par[k]))) set_error(a.err, ERR_WAIT_COPY);
     __syncthreads();
     trace_stamp(a.trace, 17);
     // (expert, block) pairs, LP lanes each, one row per lane: a pair's activation block is the same address for its lanes,
@@ -424,12 +547,13 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     __syncthreads();
     trace_stamp(a.trace, 18);
     float *wprod = rprod;   // [nd][K] (the router products are done with)
-    for (int q = tid; q < nd * K; q += DECODE_THREADS) {   // wt[k] * hd[r][k], hd as the block terms in block order
-      const float *tq = terms + q * nbd;
+    for (int q = tid; q < nd * K; q += DECODE_THREADS) {   // wt[k] * hd[r][k] for rank k, hd as the block terms in block order
+      const int r = q / K, rk = q - r * K;
+      const float *tq = terms + (r * K + s_slot[rk]) * nbd;   // the terms are by slot
       float hd = 0.f;
 #pragma unroll 4
       for (int b = 0; b < nbd; ++b) hd = __fadd_rn(hd, tq[b]);
-      wprod[q] = __fmul_rn(s_wn[q % K], hd);
+      wprod[q] = __fmul_rn(s_wn[q % K], hd);   // q = row * K + rank
     }
     __syncthreads();
     for (int r = tid; r < nd; r += DECODE_THREADS) {   // moe in rank order
@@ -445,9 +569,11 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
   trace_stamp(a.trace, 19);
   trace_time(a.trace, 31);
   if (tid == 0) {
-    if (s_flag[1] && s_flag[0])   // an error path may leave copies unwaited; the normal path waited in phase 6
+    if (s_flag[0])   // an error path may leave copies unwaited; the normal path waited in phase 6
       for (int k = 0; k < K; ++k)
-        if (!mbar_wait_bounded(&bars[k], 0)) set_error(a.err, ERR_WAIT_COPY);
+        if (((s_iss[k] & 1) && !mbar_wait_bounded(&bars[k], static_cast<uint32_t>(s_par[k]))) ||
+            ((s_iss[k] & 2) && !mbar_wait_bounded(&dbar[k], static_cast<uint32_t>(s_par[k]))))
+          set_error(a.err, ERR_WAIT_COPY);
     // a host call reads the results from host-mapped memory as soon as the error word arrives there: the CTA's writes
     // (x, sel and wt included, ordered by the block barrier) reach the host before its count
     if (a.err_out) __threadfence_system();
@@ -464,6 +590,7 @@ __global__ void __launch_bounds__(DECODE_THREADS, 1) moe_decode_kernel(const Dec
     }
   }
 }
+
 
 __global__ void __launch_bounds__(256) stage_in_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst, int n4) {
   grid_launch_dependents();

@@ -35,6 +35,8 @@ struct DecodeArgs {
   // test hook (0: off): the wait for the router logits targets a count that no CTA reaches, polled `stall_wait` times, so it
   // runs out and the launch reports ERR_WAIT_ROUTER without a hang or a fault
   uint32_t stall_wait;
+  // test hook (mode 0): the copies of rank K - 1 first go out for the expert ranked K, so the slot correction runs
+  int force_miss;
   int sel_in[DECODE_MAX_K];
   float wt_in[DECODE_MAX_K];
   const uint8_t *slab[DECODE_MAX_K];

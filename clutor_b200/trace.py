@@ -31,16 +31,16 @@ GROUP_DETAIL = [("thread 0's logit polls", 3, 21), ("gather barrier", 21, 5), ("
 # the same for the grid-wide kernel (decode.cu)
 PHASES = [
     (1, "dependency wait"), (2, "x, sum of squares"), (3, "router rows landed"), (4, "rmsnorm, router products"),
-    (6, "Q8_K of xn"), (7, "all logits visible"), (8, "softmax max"), (9, "exponentials, double sum"), (10, "probabilities"),
-    (20, "barrier"), (21, "rank"), (11, "barrier"), (22, "renormalisation"), (23, "copy addresses"), (12, "copies issued"),
-    (25, "first expert slot landed"), (26, "first gate/up block"), (13, "gate/up rows"), (14, "hg rows released"),
+    (6, "Q8_K of xn"), (7, "all logits visible"), (8, "logits staged, max"), (21, "rank by logit"),
+    (23, "gate/up copies issued"), (11, "barrier"), (12, "down copies issued"), (9, "exponentials, double sum"), (10, "probabilities"),
+    (20, "barrier"), (22, "probability order checked, weights"), (25, "first expert slot landed"), (26, "first gate/up block"), (13, "gate/up rows"), (14, "hg rows released"),
     (15, "all hg visible"), (16, "Q8_K of hg"), (17, "down rows landed"), (18, "down rows"), (19, "combine, residual"),
 ]
 GRID_ROUTER = (4, 5)
 KERNELS = {"group": (0, GROUP_PHASES, GROUP_ROUTER), "grid": (1, PHASES, GRID_ROUTER)}
 
 
-def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20, kernel: str = "group") -> dict:
+def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20, kernel: str = "group", cooperative: bool = True) -> dict:
     import torch
 
     import clutor_b200 as cb
@@ -49,6 +49,7 @@ def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20, kernel: str =
     option, phases, (rb0, rb1) = KERNELS[kernel]
     ctx = cb.Context(0)
     ctx.set_option(ctx.OPT_DECODE_KERNEL, option)
+    ctx.set_option(ctx.OPT_COOPERATIVE, int(cooperative))
     try:
         layers = [synth.device_layer(E=2048, FF=768, NE=128, K=8, gate_type=synth.T_Q4_K, down_type=synth.TYPE_NAMES[down],
                                      seed=i + 1, router_scale=0.02) for i in range(n_layers)]
@@ -117,8 +118,9 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--down", default="q4_k", choices=["q4_k", "q6_k"])
     ap.add_argument("--kernel", default="group", choices=sorted(KERNELS))
+    ap.add_argument("--plain-launch", action="store_true", help="launch without the cooperative attribute")
     a = ap.parse_args()
-    r = run(a.layers, a.down, kernel=a.kernel)
+    r = run(a.layers, a.down, kernel=a.kernel, cooperative=not a.plain_launch)
     print(f"{r['us_per_layer']:.2f} us per layer (CUDA events, traced graph), SM clock {r['sm_mhz']:.0f} MHz (from the trace)")
     print("| phase (thread 0 of each CTA) | median us | p90 us |")
     print("|---|---|---|")

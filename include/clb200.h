@@ -85,14 +85,18 @@ int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, floa
  *     allows it (each chosen expert streamed by its own group of SMs; no grid-wide wait after the routing); 1 (default): the
  *     grid-wide kernel (every SM streams a share of every chosen expert), which the expert store's calls use in any case.
  *     Both give the same results.
- *   CLB200_OPT_TEST_SPECULATION_MISS: a test hook. 1: the expert-group kernel first fetches the expert ranked K + 1 in place
- *     of the one ranked K, as if two probabilities had tied at rank K, so that its correction path runs on every call; the
+ *   CLB200_OPT_TEST_SPECULATION_MISS: a test hook. 1: both one-token kernels first fetch the expert ranked K + 1 in place of
+ *     the one ranked K, as if two probabilities had tied at rank K, so that their correction paths run on every call; the
  *     results must not change. 0 (default): off.
  *   CLB200_OPT_TEST_STALL_WAIT: a test hook for the failure path. N > 0: the grid-wide kernel's wait for the router logits
  *     targets a count that no CTA reaches and gives up after N polls (1 << 14 is about a millisecond), so every CTA takes its
  *     error path and the launch ends with the device error word set (ERR_WAIT_ROUTER, reported by clb200_status or the host
- *     call) instead of a hang; 0 (default): off. */
-enum { CLB200_OPT_DECODE_KERNEL = 1, CLB200_OPT_TEST_SPECULATION_MISS = 2, CLB200_OPT_TEST_STALL_WAIT = 3 };
+ *     call) instead of a hang; 0 (default): off.
+ *   CLB200_OPT_COOPERATIVE: 1 (default): the one-token kernels are launched cooperatively, so the driver places every CTA
+ *     at once or refuses the launch (their CTAs wait on one another). 0: plain launches, one CTA per SM, which costs less per
+ *     launch; for hosts that own the whole device (no other kernel can hold an SM while a launch starts). Either way a CTA
+ *     that waits too long ends the launch with a device error, not a hang. */
+enum { CLB200_OPT_DECODE_KERNEL = 1, CLB200_OPT_TEST_SPECULATION_MISS = 2, CLB200_OPT_TEST_STALL_WAIT = 3, CLB200_OPT_COOPERATIVE = 4 };
 int clb200_set_option(clb200_ctx *c, int option, int value);
 /* No counterpart in the reference: an entry point for hosts that cannot allocate device memory once they run (their
  * device memory is carved out up front by another allocator, or cudaMalloc's device-wide synchronisation would break a

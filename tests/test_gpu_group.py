@@ -2,8 +2,9 @@
 
 Both kernels compute the reference's arithmetic in the reference's order, so their results must agree bit for bit: routing,
 weights and every output value. The expert-group kernel also ranks experts by logit to issue its copies before the softmax
-is done; the test hook CLB200_OPT_TEST_SPECULATION_MISS makes that first choice wrong at rank K - 1 on every call, so its
-correction path (wait for the wrong copies, fetch the right expert) runs, and the results must still be the same bits.
+is done, as the grid-wide kernel does too; the test hook CLB200_OPT_TEST_SPECULATION_MISS makes that first choice wrong at
+rank K - 1 on every call, so the correction path (wait for the wrong copies, fetch the right expert) runs, and the results
+must still be the same bits.
 """
 import numpy as np
 import pytest
@@ -67,14 +68,18 @@ def test_group_kernel_equals_grid_kernel(ctx, E, FF, NE, K, gt, dt):
         assert np.linalg.norm(d - rd) <= TOL_REL_L2 * max(np.linalg.norm(rd), 1e-30)
 
 
+@pytest.mark.parametrize("kernel", [0, 1])
 @pytest.mark.parametrize("E,FF,NE,K,gt,dt", [SHAPES[0], SHAPES[1], SHAPES[4], SHAPES[5], SHAPES[6]])
-def test_speculation_correction_path(ctx, E, FF, NE, K, gt, dt):
-    """The copies of rank K - 1 first go out for the expert ranked K + 1; the group that holds it must fetch the right
-    expert and the result must not change by a bit."""
+def test_speculation_correction_path(ctx, kernel, E, FF, NE, K, gt, dt):
+    """The copies of rank K - 1 first go out for the expert ranked K + 1; the group (kernel 0) or the slot (kernel 1, the
+    grid-wide kernel) that holds it must fetch the right expert and the result must not change by a bit."""
     L = synth.host_layer(E=E, FF=FF, NE=NE, K=K, gate_type=gt, down_type=dt, seed=7 * E + K)
     for s in range(3):
         x = synth.activations(1, E, seed=300 + s)
-        same_bits(run(ctx, L, x, 0, miss=1), run(ctx, L, x, 0), f"correction E={E} K={K}")
+        same_bits(run(ctx, L, x, kernel, miss=1), run(ctx, L, x, kernel), f"correction kernel {kernel} E={E} K={K}")
+        if kernel == 1:
+            _, rsel, _ = oracle.moe_ffn(L, x, "oracle")
+            assert np.array_equal(run(ctx, L, x, 1, miss=1)[1], rsel)
 
 
 def test_many_calls_and_shared_scratch(ctx):
