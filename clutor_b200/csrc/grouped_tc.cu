@@ -43,21 +43,25 @@ namespace {
 constexpr int DQ_WARPS = 8;                         // dequantizing warps, one weight row per thread
 constexpr int W_RAW = DQ_WARPS, W_MMA0 = DQ_WARPS + 1, W_ACT = DQ_WARPS + 2, W_MMA1 = DQ_WARPS + 3;
 constexpr int TC_THREADS = 32 * (DQ_WARPS + 4);
-constexpr int B_STAGES = 4;                         // activation stages, one 64-column atom each
 constexpr uint32_t A_COLS = 128, TMEM_COLS = 512;   // A stage: [m0 hi 32][m0 lo 32][m1 hi 32][m1 lo 32] TMEM columns
 
-// Per weight type: bytes of a row's 256-element chunk, tokens per tile, ring depths. TMEM columns: the accumulators
-// (2 NT each: x hi products, then x lo products) of matrix 0 at [0, 2NT) and matrix 1 at [2NT, 4NT); A stage j at
-// 4NT + 128 j (64 fp16 of K per row, two per column).
+// Per weight type: bytes of a row's 256-element chunk, tokens per tile, ring depths, and how the x hi / x lo products
+// are kept. Q8_0 (STACK): an accumulator of 2 NT columns per matrix, x hi products then x lo products (one MMA of width
+// 2 NT per A plane: at a few tokens an expert the count of MMAs counts), matrix 0 at [0, 2NT), matrix 1 at [2NT, 4NT).
+// Q4_K: 128 tokens a tile, so each weight is dequantized once per 128 tokens; an accumulator of NT columns per matrix
+// ([0, NT) and [NT, 2NT)) that takes w hi x hi, w hi x lo and w lo x hi in turn (w lo x lo, about 2^-22 of the product, is
+// left out). A stage j at ACC_COLS + 128 j (64 fp16 of K per row, two per column).
 template <uint32_t WT>
 struct TcShape {
+  static constexpr bool STACK = WT == T_Q8_0;
   static constexpr uint32_t CHUNK = WT == T_Q8_0 ? 272u : 144u;
-  static constexpr int NT = WT == T_Q8_0 ? 32 : 64;
+  static constexpr int NT = WT == T_Q8_0 ? 32 : 128;
   static constexpr int RAW_STAGES = WT == T_Q8_0 ? 5 : 6;
+  static constexpr int B_STAGES = WT == T_Q8_0 ? 4 : 3;   // activation stages, one 64-column atom each
   static constexpr uint32_t RAW_STAGE = 128 * CHUNK;
   static constexpr uint32_t B_TILE = NT * 128;      // NT tokens x 64 fp16, 128-byte swizzle
   static constexpr uint32_t B_STAGE = 2 * B_TILE;   // hi rows [0, NT), lo rows [NT, 2 NT)
-  static constexpr uint32_t ACC_COLS = 4 * NT;
+  static constexpr uint32_t ACC_COLS = (STACK ? 4 : 2) * NT;
   static constexpr int A_STAGES = static_cast<int>((TMEM_COLS - ACC_COLS) / A_COLS);
   static constexpr int N_BARS = 2 * RAW_STAGES + 2 * B_STAGES + 2 * A_STAGES + 3;
   static constexpr uint32_t SMEM = RAW_STAGES * RAW_STAGE + B_STAGES * B_STAGE + 8 * N_BARS + 16 + 1024;
@@ -196,7 +200,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     group_tc_kernel(const BatchArgs a, const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                     const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl) {
   using S = TcShape<WT>;
-  constexpr int NT = S::NT, RAW_STAGES = S::RAW_STAGES, A_STAGES = S::A_STAGES;
+  constexpr int NT = S::NT, RAW_STAGES = S::RAW_STAGES, A_STAGES = S::A_STAGES, B_STAGES = S::B_STAGES;
+  constexpr bool STACK = S::STACK;
   constexpr uint32_t RAW_STAGE = S::RAW_STAGE, B_STAGE = S::B_STAGE, ACC_COLS = S::ACC_COLS;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -296,10 +301,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == W_MMA0 || warp == W_MMA1) {
     if (lane == 0) {
       const int mA = warp == W_MMA0 ? 0 : 1;
-      const uint32_t acc = tmem + 2 * NT * mA;
+      const uint32_t acc = tmem + (STACK ? 2 : 1) * NT * mA;
       uint32_t t = 0, it = 0;
       ok = for_each_tile<NT>(tl, MT, [&](int, int, int, int nt) {
-        const uint32_t idesc = tc::idesc_f16_f32(128, 2 * ((nt + 15) & ~15));
+        const int NTt = (nt + 15) & ~15;
+        const uint32_t idesc = tc::idesc_f16_f32(128, (STACK ? 2 : 1) * NTt);
         if (it > 0 && !mbar_wait_bounded(acc_free, (it - 1) & 1)) return false;
         tc::fence_after_sync();
         for (int c = 0; c < nchunk; ++c) {
@@ -310,10 +316,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc::fence_after_sync();
             const uint64_t bdesc = tc::sw128_desc(smem_addr(bst + sb * B_STAGE));
             const uint32_t ah = tmem + ACC_COLS + A_COLS * sa + 64 * mA;
+            if constexpr (STACK) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {   // K step: +8 TMEM columns of A, +32 bytes (2 descriptor units) of B
-              tc::mma_f16_ts(acc, ah + 8 * kk, bdesc + 2 * kk, idesc, c != 0 || at != 0 || kk != 0);
-              tc::mma_f16_ts(acc, ah + 32 + 8 * kk, bdesc + 2 * kk, idesc, true);
+              for (int kk = 0; kk < 4; ++kk) {   // K step: +8 TMEM columns of A, +32 bytes (2 descriptor units) of B
+                tc::mma_f16_ts(acc, ah + 8 * kk, bdesc + 2 * kk, idesc, c != 0 || at != 0 || kk != 0);
+                tc::mma_f16_ts(acc, ah + 32 + 8 * kk, bdesc + 2 * kk, idesc, true);
+              }
+            } else {
+              // x lo rows start 128 NTt bytes in: a multiple of 2048, so a fresh 128-byte-swizzle tile
+              const uint64_t bdesc_lo = tc::sw128_desc(smem_addr(bst + sb * B_STAGE + 128 * NTt));
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                tc::mma_f16_ts(acc, ah + 8 * kk, bdesc + 2 * kk, idesc, c != 0 || at != 0 || kk != 0);   // w hi x hi
+                tc::mma_f16_ts(acc, ah + 8 * kk, bdesc_lo + 2 * kk, idesc, true);                         // w hi x lo
+                tc::mma_f16_ts(acc, ah + 32 + 8 * kk, bdesc + 2 * kk, idesc, true);                       // w lo x hi
+              }
             }
             tc::commit(&a_free[sa]);
             tc::commit(&b_free[sb]);
@@ -374,7 +391,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) mbar_arrive(&raw_free[s]);
       }
       // epilogue: warps of matrix 0 take tokens [0, NT/2), those of matrix 1 [NT/2, NT), 16 at a time; each reads both
-      // accumulators, whose column n holds the x hi products and column NTt + n the x lo products of token n
+      // accumulators (STACK: column n holds the x hi products and column NTt + n the x lo products of token n)
       if (!mbar_wait_bounded(acc_full, it & 1)) return false;
       tc::fence_after_sync();
       const int NTt = (nt + 15) & ~15;
@@ -383,7 +400,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int c0 = (NT / 2) * mA + 16 * h;
         if (c0 >= nt) break;   // warp-uniform
         float v0[16], v1[16];
-        {
+        if constexpr (STACK) {
           float l0[16], l1[16];
           tc::ld_x16(tmem + lane_base + c0, v0);
           tc::ld_x16(tmem + lane_base + NTt + c0, l0);
@@ -391,6 +408,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc::ld_x16(tmem + lane_base + 2 * NT + NTt + c0, l1);
 #pragma unroll
           for (int j = 0; j < 16; ++j) { v0[j] = __fadd_rn(v0[j], l0[j]); v1[j] = __fadd_rn(v1[j], l1[j]); }
+        } else {
+          tc::ld_x16(tmem + lane_base + c0, v0);
+          tc::ld_x16(tmem + lane_base + NT + c0, v1);
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
