@@ -123,6 +123,33 @@ CLB_DEV void dequant_q80_atom(const uint32_t (&w)[17], int bb, uint32_t (&hi)[16
 // exponential, code that runs once per tile and so is fetched again for every tile.
 __device__ __noinline__ float silu_mul_once(float g, float u) { return silu_mul(g, u); }
 
+// Two fp32 lanes per instruction (sm_100): each lane rounded once, as the scalar operation.
+CLB_DEV unsigned long long f2_pack(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+CLB_DEV float2 f2_unpack(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+CLB_DEV float2 ffma2(float2 a, float2 b, float2 c) {   // a * b + c
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)), "l"(f2_pack(c)));
+  return f2_unpack(r);
+}
+CLB_DEV float2 fadd2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(r);
+}
+CLB_DEV float2 fsub2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(r);
+}
+
 CLB_DEV float half_bits(uint32_t bits16) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16))); }
 CLB_DEV uint32_t pack_half2(float a, float b) { return as_u32(__floats2half2_rn(a, b)); }   // a in the low half
 
@@ -145,20 +172,23 @@ CLB_DEV void dequant_q4k_atom(const uint32_t (&hdr)[4], const uint32_t (&qw8)[8]
     mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
   }
   const float a1 = __fmul_rn(d, static_cast<float>(sc)), a0 = __fmul_rn(dmin, static_cast<float>(mn));   // both exact
+  // w = a1*q - a0 with one rounding, two values per instruction: q comes in as the float 2^23 + q (its bits 0x4B000000 | q,
+  // one byte permute), a1*(2^23 + q) - a1*2^23 = a1*q exactly (at most 21 significant bits), then - a0 rounds once
+  const float2 A1 = make_float2(a1, a1), NA1M = make_float2(-a1 * 8388608.0f, -a1 * 8388608.0f), NA0 = make_float2(-a0, -a0);
+  const uint32_t magic = 0x4B000000u;
   const int shift = (j & 1) ? 4 : 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const uint32_t qw = qw8[i] >> shift;
-    float v[4], h[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v[k] = __fmaf_rn(a1, static_cast<float>((qw >> (8 * k)) & 15u), -a0);   // d*sc*q exact; one rounding
-      h[k] = __half2float(__float2half_rn(v[k]));
-    }
-    hi[2 * i] = pack_half2(h[0], h[1]);
-    hi[2 * i + 1] = pack_half2(h[2], h[3]);
-    lo[2 * i] = pack_half2(__fsub_rn(v[0], h[0]), __fsub_rn(v[1], h[1]));
-    lo[2 * i + 1] = pack_half2(__fsub_rn(v[2], h[2]), __fsub_rn(v[3], h[3]));
+    const uint32_t m = (qw8[i] >> shift) & 0x0F0F0F0Fu;   // the four values of this word, one per byte
+    const float2 q01 = make_float2(__uint_as_float(__byte_perm(m, magic, 0x7440)), __uint_as_float(__byte_perm(m, magic, 0x7441)));
+    const float2 q23 = make_float2(__uint_as_float(__byte_perm(m, magic, 0x7442)), __uint_as_float(__byte_perm(m, magic, 0x7443)));
+    const float2 v01 = fadd2(ffma2(A1, q01, NA1M), NA0), v23 = fadd2(ffma2(A1, q23, NA1M), NA0);
+    const __half2 h01 = __floats2half2_rn(v01.x, v01.y), h23 = __floats2half2_rn(v23.x, v23.y);
+    const float2 l01 = fsub2(v01, __half22float2(h01)), l23 = fsub2(v23, __half22float2(h23));   // exact remainders
+    hi[2 * i] = as_u32(h01);
+    hi[2 * i + 1] = as_u32(h23);
+    lo[2 * i] = as_u32(__floats2half2_rn(l01.x, l01.y));
+    lo[2 * i + 1] = as_u32(__floats2half2_rn(l23.x, l23.y));
   }
 }
 
