@@ -111,16 +111,31 @@ class GpuCompute(Compute):
         return out
 
 
+def flat_plan(sel: torch.Tensor, n_ranks: int, n_local: int):
+    """The dispatch on the device with one host synchronisation (the counts, which the exchange needs on the host anyway):
+    (t_idx [S], r_idx [S], lsel [S, K], counts [n_ranks] as a list), the (token, destination) pairs a token goes to --
+    once per rank that holds at least one of its experts -- in destination order, tokens ascending within a destination;
+    lsel the token's expert ids made local to the destination, -1 where the expert is elsewhere."""
+    T = sel.shape[0]
+    dev = sel.device
+    owner = torch.div(sel, n_local, rounding_mode="floor").long()
+    hit = torch.zeros((T, n_ranks + 1), dtype=torch.bool, device=dev)   # the last column: experts no rank holds
+    if T:
+        hit.scatter_(1, owner.clamp(0, n_ranks), True)
+    hit = hit[:, :n_ranks]
+    counts = hit.sum(0).tolist()
+    key = torch.where(hit, torch.arange(n_ranks, device=dev)[None, :] * T + torch.arange(T, device=dev)[:, None], n_ranks * T)
+    order = torch.argsort(key.reshape(-1), stable=True)[:sum(counts)]
+    t_idx, r_idx = order // n_ranks, order % n_ranks
+    lsel = torch.where(owner[t_idx] == r_idx[:, None], sel[t_idx] - (r_idx[:, None] * n_local).to(sel.dtype),
+                       torch.full_like(sel[t_idx], -1))
+    return t_idx, r_idx, lsel, counts
+
+
 def dispatch_plan(sel: torch.Tensor, n_ranks: int, n_local: int):
     """Per destination rank: the ascending indices of the tokens that go there and their local sel (-1 elsewhere)."""
-    owner = torch.div(sel, n_local, rounding_mode="floor")
-    idx, lsel = [], []
-    for r in range(n_ranks):
-        here = owner == r
-        ti = torch.nonzero(here.any(dim=1)).squeeze(1)
-        idx.append(ti)
-        lsel.append(torch.where(here[ti], sel[ti] - r * n_local, torch.full_like(sel[ti], -1)))
-    return idx, lsel
+    t_idx, _, lsel, counts = flat_plan(sel, n_ranks, n_local)
+    return list(torch.split(t_idx, counts)), list(torch.split(lsel, counts))
 
 
 def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, group=None, timings: dict | None = None):
@@ -148,19 +163,18 @@ def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, 
     mark("dispatch")
     K = sel.shape[1]
     fmt = RowFormat(E, K)
-    idx, lsel = dispatch_plan(sel, n, n_local)
-    send = fmt.pack(qs=torch.cat([qs[i] for i in idx]), d=torch.cat([d[i] for i in idx]), bs=torch.cat([bs[i] for i in idx]),
-                    sel=torch.cat(lsel), wt=torch.cat([wt[i] for i in idx]))
-    scount = torch.tensor([len(i) for i in idx], dtype=torch.int64, device=x.device)
+    t_idx, _, lsel, sc = flat_plan(sel, n, n_local)
+    send = fmt.pack(qs=qs[t_idx], d=d[t_idx], bs=bs[t_idx], sel=lsel, wt=wt[t_idx])
     me = dist.get_rank(group) if n > 1 else 0
     if n > 1:
+        scount = torch.tensor(sc, dtype=torch.int64, device=x.device)
         rcount = torch.empty_like(scount)
         dist.all_to_all_single(rcount, scount, group=group)
-        sc, rc = scount.tolist(), rcount.tolist()
+        rc = rcount.tolist()
         recv = torch.empty((sum(rc), fmt.nbytes), dtype=torch.uint8, device=x.device)
         dist.all_to_all_single(recv, send, rc, sc, group=group)
     else:
-        sc = rc = scount.tolist()
+        rc = sc
         recv = send
     close("dispatch")
     r = fmt.unpack(recv)
@@ -180,9 +194,10 @@ def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, 
         back = partial
     msum = torch.zeros_like(x)
     o = 0
-    for ri, i in enumerate(idx):   # ranks in order; a token appears at most once per rank
-        msum[i] += back[o:o + len(i)]
-        o += len(i)
+    for c in sc:   # ranks in order; a token appears at most once per rank, so each addition is one per token
+        if c:
+            msum[t_idx[o:o + c]] += back[o:o + c]
+        o += c
     x += resid_scale * msum
     close("combine")
     if timings is not None:
