@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 SOURCES = ["api.cu", "decode.cu", "group.cu", "batched.cu", "backend.cu", "noalloc.cu", "grouped_tc.cu", "cache.cpp", "store.cu", "gguf.cpp",
-           "fwd.cu", "model.cu", "route.cu", "prefill.cu"]
+           "fwd.cu", "model.cu", "route.cu", "prefill.cu", "epx.cu"]
 LIB = os.path.join(HERE, "libclutor_b200.so")
 
 

@@ -70,6 +70,23 @@ class Compute:
         """-> partial [R,E] f32: per row, the weighted sum of its present local experts."""
         raise NotImplementedError
 
+    def pack(self, fmt: "RowFormat", sel, wt, qs, d, bs, n_ranks: int, n_local: int):
+        """The rows each token sends: -> (send [S, nbytes] uint8 in destination order, tokens ascending within one;
+        plan, an opaque value for combine; counts per destination as a list)."""
+        t_idx, _, lsel, counts = flat_plan(sel, n_ranks, n_local)
+        return fmt.pack(qs=qs[t_idx], d=d[t_idx], bs=bs[t_idx], sel=lsel, wt=wt[t_idx]), t_idx, counts
+
+    def combine(self, x, back, plan, counts, resid_scale: float) -> None:
+        """x += resid_scale * (each token's returned partial sums added in rank order)."""
+        t_idx = plan
+        msum = torch.zeros_like(x)
+        o = 0
+        for c in counts:   # ranks in order; a token appears at most once per rank, so each addition is one per token
+            if c:
+                msum[t_idx[o:o + c]] += back[o:o + c]
+            o += c
+        x += resid_scale * msum
+
 
 class GpuCompute(Compute):
     """The CUDA kernels: a context, the full layer bound for routing and this rank's expert shard bound for the experts."""
@@ -82,6 +99,9 @@ class GpuCompute(Compute):
         L = self.L
         L.clb200_ep_route.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int] + [C.c_void_p] * 6 + [C.c_char_p, C.c_size_t]
         L.clb200_ep_experts.argtypes = [C.c_void_p, C.c_int, C.c_int] + [C.c_void_p] * 7 + [C.c_char_p, C.c_size_t]
+        L.clb200_ep_pack.argtypes = [C.c_void_p] + [C.c_int] * 5 + [C.c_void_p] * 9 + [C.c_char_p, C.c_size_t]
+        L.clb200_ep_combine.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                                        C.c_void_p, C.c_char_p, C.c_size_t]
 
     def _s(self):   # ordered with the torch work around each call
         from . import _stream
@@ -109,6 +129,26 @@ class GpuCompute(Compute):
                                     wt.data_ptr(), out.data_ptr(), self._s(), self._err, 512):
             raise RuntimeError(self._err.value.decode())
         return out
+
+    def pack(self, fmt, sel, wt, qs, d, bs, n_ranks, n_local):
+        """The plan and the rows in two launches (clb200_ep_pack); one host synchronisation for the counts."""
+        T, K = sel.shape
+        dev = sel.device
+        send = torch.empty((T * n_ranks, fmt.nbytes), dtype=torch.uint8, device=dev)
+        slot = torch.empty((T, n_ranks), dtype=torch.int32, device=dev)
+        counts = torch.zeros(n_ranks, dtype=torch.int32, device=dev)
+        if self.L.clb200_ep_pack(self.ctx.handle, T, self.E, K, n_ranks, n_local, sel.data_ptr(), wt.data_ptr(), qs.data_ptr(),
+                                 d.data_ptr(), bs.data_ptr(), send.data_ptr(), slot.data_ptr(), counts.data_ptr(), self._s(),
+                                 self._err, 512):
+            raise RuntimeError(self._err.value.decode())
+        cl = counts.tolist()
+        return send[:sum(cl)], slot, cl
+
+    def combine(self, x, back, plan, counts, resid_scale):
+        slot = plan
+        if self.L.clb200_ep_combine(self.ctx.handle, x.shape[0], self.E, slot.shape[1], slot.data_ptr(), back.data_ptr(), x.data_ptr(),
+                                    resid_scale, self._s(), self._err, 512):
+            raise RuntimeError(self._err.value.decode())
 
 
 def flat_plan(sel: torch.Tensor, n_ranks: int, n_local: int):
@@ -163,8 +203,7 @@ def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, 
     mark("dispatch")
     K = sel.shape[1]
     fmt = RowFormat(E, K)
-    t_idx, _, lsel, sc = flat_plan(sel, n, n_local)
-    send = fmt.pack(qs=qs[t_idx], d=d[t_idx], bs=bs[t_idx], sel=lsel, wt=wt[t_idx])
+    send, plan, sc = comp.pack(fmt, sel, wt, qs, d, bs, n, n_local)
     me = dist.get_rank(group) if n > 1 else 0
     if n > 1:
         scount = torch.tensor(sc, dtype=torch.int64, device=x.device)
@@ -192,13 +231,7 @@ def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, 
         dist.all_to_all_single(back, partial, sc, rc, group=group)
     else:
         back = partial
-    msum = torch.zeros_like(x)
-    o = 0
-    for c in sc:   # ranks in order; a token appears at most once per rank, so each addition is one per token
-        if c:
-            msum[t_idx[o:o + c]] += back[o:o + c]
-        o += c
-    x += resid_scale * msum
+    comp.combine(x, back, plan, sc, resid_scale)
     close("combine")
     if timings is not None:
         timings.pop("_open", None)

@@ -136,6 +136,18 @@ int clb200_ep_route(clb200_ctx *c, int layer, float *x, int T, int *sel, float *
  * (c/src/forward.c:1160-1208 without the residual add). All DEVICE pointers. */
 int clb200_ep_experts(clb200_ctx *c, int layer, int T, const int8_t *xq_qs, const float *xq_d, const int16_t *xq_bs, const int *sel,
                       const float *wt, float *partial, void *stream, char *err, size_t errlen);
+/* The exchange between those two halves on the device (no reference counterpart). clb200_ep_pack: the rows each of T tokens
+ * sends -- once to every one of n_ranks ranks (of n_local experts each) that holds one of its experts -- into send
+ * ([T * n_ranks] rows of E + E/64 + E/8 + 8 * n_used bytes: Q8_K qs, d and bsums, the expert ids made local to the
+ * destination with -1 elsewhere, the weights), ranks in order and tokens ascending within a rank; slot [T * n_ranks]: the
+ * send row of (token, rank) or -1; counts [n_ranks]: the rows for each rank (device memory; the all-to-all wants them on
+ * the host). clb200_ep_combine: x [T, E] += resid_scale * the sum over ranks, in rank order, of back[slot] (the partial
+ * sums returned in send order). Both asynchronous on stream. */
+int clb200_ep_pack(clb200_ctx *c, int T, int E, int n_used, int n_ranks, int n_local, const int *sel, const float *wt, const int8_t *xq_qs,
+                   const float *xq_d, const int16_t *xq_bs, uint8_t *send, int *slot, int *counts, void *stream, char *err,
+                   size_t errlen);
+int clb200_ep_combine(clb200_ctx *c, int T, int E, int n_ranks, const int *slot, const float *back, float *x, float resid_scale,
+                      void *stream, char *err, size_t errlen);
 /* Waits for the context's work and reports a device-side error recorded since the last call (0: none). */
 int clb200_status(clb200_ctx *c, char *err, size_t errlen);
 /* Bytes of device memory the context holds for layers and scratch. */

@@ -62,3 +62,34 @@ def test_sharded_experts_match_the_block(ctx, shards):
     dd, wd = (x - x0).double(), (xb - x0).double()
     err = float(torch.linalg.norm(dd - wd) / torch.linalg.norm(wd))
     assert err <= 1e-5, err
+
+
+@pytest.mark.parametrize("n_ranks", [1, 2, 3, 8])
+def test_device_exchange_equals_the_host_form(ctx, n_ranks):
+    """clb200_ep_pack gives the torch form's rows byte for byte (destination order, tokens ascending) and clb200_ep_combine
+    its bits; experts past the last rank (128 experts over 3 ranks of 42) go nowhere in both."""
+    import torch
+    T, E, K, NE = 300, 1024, 8, 128
+    n_local = NE // n_ranks
+    g = torch.Generator().manual_seed(n_ranks)
+    sel = torch.stack([torch.randperm(NE, generator=g)[:K] for _ in range(T)]).to(torch.int32).cuda()
+    wt = torch.rand((T, K), generator=g).cuda()
+    qs = torch.randint(-127, 128, (T, E), dtype=torch.int8, generator=g).cuda()
+    d = torch.rand((T, E // 256), generator=g).cuda()
+    bs = torch.randint(-2000, 2000, (T, E // 16), dtype=torch.int16, generator=g).cuda()
+    fmt = ep.RowFormat(E, K)
+    host = ep.Compute()
+    gpu = ep.GpuCompute(ctx, -1, -1, E, K)
+    send_h, plan_h, counts_h = host.pack(fmt, sel, wt, qs, d, bs, n_ranks, n_local)
+    send_d, plan_d, counts_d = gpu.pack(fmt, sel, wt, qs, d, bs, n_ranks, n_local)
+    torch.cuda.synchronize()
+    assert counts_d == counts_h
+    assert torch.equal(send_d, send_h)
+    S = sum(counts_h)
+    back = torch.randn((S, E), generator=g).cuda()
+    x0 = torch.randn((T, E), generator=g).cuda()
+    xh, xd = x0.clone(), x0.clone()
+    host.combine(xh, back, plan_h, counts_h, 0.75)
+    gpu.combine(xd, back, plan_d, counts_d, 0.75)
+    torch.cuda.synchronize()
+    assert torch.equal(xd.view(torch.int32), xh.view(torch.int32))
