@@ -154,6 +154,36 @@ CLB_DEV void trace_stamp(unsigned long long *trace, int i) {
   if (threadIdx.x == 0) trace_stamp_here(trace, i);
 }
 
+// ---- packed fp32 (sm_100) ------------------------------------------------------------------------------------------------
+// Two fp32 lanes per instruction (sm_100): each lane rounded once, as the scalar operation. There is deliberately no packed
+// multiply: measured on the device, a packed multiply whose only use is a packed add came out fused (the router's dotf
+// chains lost their bits), so products whose rounding matters stay scalar.
+CLB_DEV unsigned long long f2_pack(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+CLB_DEV float2 f2_unpack(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+CLB_DEV float2 ffma2(float2 a, float2 b, float2 c) {   // a * b + c
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)), "l"(f2_pack(c)));
+  return f2_unpack(r);
+}
+CLB_DEV float2 fadd2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(r);
+}
+CLB_DEV float2 fsub2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(r);
+}
+
 // ---- the reference's scalar steps, exactly rounded ---------------------------------------------------------------------------
 // fp16 bits to float: exact (every half is a float).
 CLB_DEV float f16_bits_to_f32(uint16_t h) {

@@ -123,33 +123,6 @@ CLB_DEV void dequant_q80_atom(const uint32_t (&w)[17], int bb, uint32_t (&hi)[16
 // exponential, code that runs once per tile and so is fetched again for every tile.
 __device__ __noinline__ float silu_mul_once(float g, float u) { return silu_mul(g, u); }
 
-// Two fp32 lanes per instruction (sm_100): each lane rounded once, as the scalar operation.
-CLB_DEV unsigned long long f2_pack(float2 v) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
-  return r;
-}
-CLB_DEV float2 f2_unpack(unsigned long long r) {
-  float2 v;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
-  return v;
-}
-CLB_DEV float2 ffma2(float2 a, float2 b, float2 c) {   // a * b + c
-  unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)), "l"(f2_pack(c)));
-  return f2_unpack(r);
-}
-CLB_DEV float2 fadd2(float2 a, float2 b) {
-  unsigned long long r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
-  return f2_unpack(r);
-}
-CLB_DEV float2 fsub2(float2 a, float2 b) {
-  unsigned long long r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
-  return f2_unpack(r);
-}
-
 CLB_DEV float half_bits(uint32_t bits16) { return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16))); }
 CLB_DEV uint32_t pack_half2(float a, float b) { return as_u32(__floats2half2_rn(a, b)); }   // a in the low half
 
