@@ -385,6 +385,17 @@ def run_cache(a, wl: dict) -> dict:
     x = torch.from_numpy(synth.activations(1, E, seed=11)).cuda()[0]
     store.log(True)
 
+    # the store's C entry point called as a C host calls it: argument values prepared once, the routing arrays addressed
+    # in place (sel / wt / pred are C-contiguous [layer, token, K])
+    import ctypes as C
+    fn, errb = cb.lib().clb200_moe_experts_stored, C.create_string_buffer(512)
+    sel, wt, pred = (np.ascontiguousarray(v) for v in (sel, wt, pred))
+    if 0 < a.prefetch_n < K:   # stage only the predictor's top prefetch_n (the reference's --prefetch-n); -1 stages nothing
+        pred[:, :, a.prefetch_n:] = -1
+    row = K * 4
+    ctx_h, store_h, xp = C.c_void_p(ctx.handle), C.c_void_p(store.h), C.c_void_p(x.data_ptr())
+    sel0, wt0, pred0 = sel.ctypes.data, wt.ctypes.data, pred.ctypes.data
+
     def token(t):
         for l in range(NL):
             nxt = pred[l + 1, t] if l + 1 < NL else None
@@ -393,7 +404,9 @@ def run_cache(a, wl: dict) -> dict:
                 w = probs[l, t, s]
                 store.experts(l, x, s, (w / w.sum(dtype=np.float32)).astype(np.float32), nxt, stream=sp)
             else:
-                store.experts(l, x, sel[l, t], wt[l, t], nxt, stream=sp)
+                o = (l * ntok + t) * row
+                if fn(ctx_h, store_h, l, xp, sel0 + o, wt0 + o, pred0 + ((l + 1) * ntok + t) * row if l + 1 < NL else None, sp, errb, 512):
+                    raise cb.ClutorError(errb.value.decode())
 
     for t in range(a.warmup):
         token(t)
@@ -451,7 +464,7 @@ def run_cache(a, wl: dict) -> dict:
             "dtype": "int8 dot (Q8_K x K-quant), fp32 accumulate", "data": "synthetic (seeded GGUF blocks; routing from the reference harness's synthetic router)",
             "config": {"workload": wl["desc"], "layers": NL, "experts": NE, "top_k": K, "hidden": E, "ff": wl["FF"],
                        "expert_bytes": expert_bytes, "hbm_cache_bytes": budget, "cache_slots": store.cache_slots(),
-                       "stage_slots": 2 * K, "prefetch_depth": a.prefetch_depth, "policy": "W-TinyLFU", "locality": wl["locality"], "predict_corr": 0.8,
+                       "stage_slots": 2 * K, "prefetch_depth": a.prefetch_depth, "prefetch_n": a.prefetch_n or K, "policy": "W-TinyLFU", "locality": wl["locality"], "predict_corr": 0.8,
                        "parallelism": "single GPU", "l2": "expert bytes 16 GB, far beyond L2"},
             "cache": {"hit_rate": round(hit, 4), "stage_hits": st["stage_hits"], "misses": st["misses"],
                       "prefetch_issued": st["prefetch_issued"], "prefetch_late": st["prefetch_late"],
@@ -907,6 +920,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--prefetch-depth", type=int, default=2, help="cache workload: prefetch fills in flight at once")
+    ap.add_argument("--prefetch-n", type=int, default=4,
+                    help="cache workload: experts a prediction stages (the reference's --prefetch-n; 0: n_used). 4 is the "
+                         "fastest measured: on a link-bound workload every wrong prediction costs a 2.65 MB copy")
     ap.add_argument("--smart", default=None, help="cache workload: SMART-ROUTE J,M,TAU (for example 2,12,0.015)")
     ap.add_argument("--batch", type=int, default=None, help="prompt workload: tokens per batch (the reference's CLUTOR_PS_B, 1..512)")
     ap.add_argument("--no-ep", action="store_true", help="decode workload: leave out the expert-parallel figures")
