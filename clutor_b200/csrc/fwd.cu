@@ -11,9 +11,10 @@
 //      and weighted values in the reference's order: per 256-position chunk, merged, when a group has 2..16 query heads
 //      and the context is 64 positions or more (c/src/forward.c:665-737), else over every position (:584-627) | barrier
 //   C  attention output: Q8_K of the attention vector (every CTA); this CTA's rows of wo; x += resid * wo att | barrier
-//   D  mixture of experts as the one-token MoE kernel (decode.cu) does it: rmsnorm, router (the reference's dotf),
-//      softmax, top-k, renormalisation, this CTA's share of every chosen expert's gate/up rows (bulk copies into shared
-//      memory), SwiGLU                                                                                       | barrier
+//   D  mixture of experts as the one-token MoE kernel (decode.cu) does it: rmsnorm, router (the reference's dotf), the
+//      experts ranked by logit and this CTA's share of the first K sent out at once (bulk copies of gate/up and down rows
+//      into shared memory), then softmax, the probability order (a slot fetches again where a tie moves an expert out of
+//      the top k), renormalisation, the gate/up rows, SwiGLU                                                  | barrier
 //      the Q8_K blocks of every expert's hg, this CTA's down rows, x += resid * sum_k wt_k hd_k in rank order  | barrier
 // then the output norm and this CTA's rows of the output matrix, streamed through shared memory, their logits and the
 // greedy arg-max (lowest id on ties, c/src/main.c:349-350). The last CTA out advances the sequence state.
@@ -203,14 +204,19 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   int16_t *xq_bs = reinterpret_cast<int16_t *>(smem + a.off_xq + XQW);
   float *xq_d = reinterpret_cast<float *>(smem + a.off_xq + XQW + 2 * (XQW / 16));
   double *s_red = reinterpret_cast<double *>(smem + a.off_misc);      // [NW]
-  // [0] barrier verdict, [1] a router copy in flight, [2] the router logits arrived, [3] its parity, [4] the layer whose
-  // expert copies went out last (-1: none), [5] a dense copy in flight, [6] its parity
+  // [0] barrier verdict, [1] a router copy in flight, [2] the router logits arrived, [3] its parity, [5] a dense copy in
+  // flight, [6] its parity, [7] the probability order differs from the logit order
   int *s_flag = reinterpret_cast<int *>(s_red + NW);
   int *s_sel = s_flag + 8;                                             // [32]
   float *s_wt = reinterpret_cast<float *>(s_sel + 32);                 // [32]
   float *s_wn = s_wt + 32;                                             // [32]
   float *probs = s_wn + 32;                                            // [FWD_MAX_NE]
   unsigned long long *s_best = reinterpret_cast<unsigned long long *>(probs + FWD_MAX_NE);   // [NW]
+  float *s_lg = reinterpret_cast<float *>(s_best + NW);                // [FWD_MAX_NE] logits, -inf past NE
+  int *s_spec = reinterpret_cast<int *>(s_lg + FWD_MAX_NE);           // [32] slot k: the expert it streams
+  int *s_slot = s_spec + 32;                                           // [32] rank -> the slot streaming that expert
+  int *s_cnt = s_slot + 32;                                            // [32] phases begun on the slot's mbarrier
+  int *s_fix = s_cnt + 32;                                             // [32] expert + 1 to fetch into the slot again, or 0
   float *rrows = reinterpret_cast<float *>(smem + a.off_router);      // [nre][E]
   float *rprod = reinterpret_cast<float *>(smem + a.off_rprod);       // [nre][8][E/8 + 4]
   float *terms = reinterpret_cast<float *>(smem + a.off_terms);
@@ -249,7 +255,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     issue_dense(a.layers[0], slots, dbar, dr0, dr1);   // layer 0's dense rows
     s_flag[1] = nre > 0;
     s_flag[3] = 0;
-    s_flag[4] = -1;
+    for (int k = 0; k < 32; ++k) s_cnt[k] = 0;
     s_flag[5] = 1;
     s_flag[6] = 0;
   }
@@ -548,20 +554,75 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     }
     __syncthreads();
     if (!s_flag[2]) { ok = false; break; }
+    // routing (c/src/forward.c:954-984) with this CTA's share of the experts sent out on the logit order at once: softmax is
+    // monotone, so that is the probability order except where two different logits round to the same probability. The
+    // softmax (double sum), the probability order and the weights follow while the copies fly; a slot whose expert turns
+    // out not to be chosen (a probability tie at rank K) fetches the missing one on its mbarrier's next phase. Slot k holds
+    // expert s_spec[k]; the expert of rank r sits in slot s_slot[r].
+    constexpr int SW = FWD_MAX_NE / 32;   // softmax warps, one expert per thread
+    const float lgv = tid < NE ? __ldcg(a.rlogits + tid) : -INFINITY;
+    float mx = lgv;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    if (lane == 0 && warp < SW) s_wt[warp] = mx;   // s_wt is written after the ranking
+    // NaN ranks as -inf here, so the ranks by logit are a permutation and every slot gets one expert (a NaN routing then
+    // fails in the probability check below, with every copy accounted for)
+    if (tid < FWD_MAX_NE) s_lg[tid] = lgv == lgv ? lgv : -INFINITY;
+    if (tid <= FWD_MAX_K) s_spec[tid] = -1;
+    if (tid < FWD_MAX_K) s_fix[tid] = 0;
+    __syncthreads();
+    mx = s_wt[0];
+#pragma unroll
+    for (int w = 1; w < SW; ++w) mx = fmaxf(mx, s_wt[w]);
+    // rank of expert tid / 4 = experts ahead of it in the reference's arg-max order (ties to the lower id), counted by four
+    // threads over every fourth float4 of the values each (v padded with `pad`, below every value, to a multiple of 4)
+    auto rank4 = [&](const float *v, float pad) -> int {
+      const int e = tid >> 2, part = tid & 3, n4 = (NE + 3) / 4;
+      const float pe = e < NE ? v[e] : 0.f;
+      const float4 *p4 = reinterpret_cast<const float4 *>(v);
+      float4 q[8];   // n4 <= 32 (NE <= 128): every load in flight before the first comparison
+#pragma unroll
+      for (int u = 0; u < 8; ++u) q[u] = 4 * u + part < n4 ? p4[4 * u + part] : make_float4(pad, pad, pad, pad);
+      int rank = 0;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int f = 4 * (4 * u + part);
+        rank += (q[u].x > pe || (q[u].x == pe && f < e)) + (q[u].y > pe || (q[u].y == pe && f + 1 < e)) +
+                (q[u].z > pe || (q[u].z == pe && f + 2 < e)) + (q[u].w > pe || (q[u].w == pe && f + 3 < e));
+      }
+      rank += __shfl_xor_sync(FULL, rank, 1);
+      rank += __shfl_xor_sync(FULL, rank, 2);
+      return rank;
+    };
+    // one thread: expert e's share for this CTA into slot k (gate and up rows into the slots, down rows into the dslots),
+    // on the slot's mbarrier; s_cnt[k] counts the slot's phases (its parity is the one to wait for)
+    auto issue = [&](int k, int e) {
+      uint8_t *gs = slots + static_cast<size_t>(k) * a.slot_bytes, *ds = dslots + static_cast<size_t>(k) * a.dslot_bytes;
+      const size_t ex = static_cast<size_t>(e);
+      const uint8_t *src[3] = {Ly.gate + ex * Ly.gate_slab + static_cast<size_t>(j0) * a.grb,
+                               Ly.up + ex * Ly.up_slab + static_cast<size_t>(j0) * a.grb,
+                               Ly.down + ex * Ly.down_slab + static_cast<size_t>(i0) * a.drb};
+      uint8_t *dst[3] = {gs, gs + a.gseg, ds};
+      const uint32_t len[3] = {static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(nd) * a.drb};
+      uint32_t n16[3], total = 0;
+      for (int q = 0; q < 3; ++q) { n16[q] = len[q] ? (lo16(src[q]) + len[q] + 15u) & ~15u : 0u; total += n16[q]; }
+      fence_proxy_async();   // the generic accesses of these buffers (attention scratch, dense rows) come first
+      mbar_arrive_expect_tx(&bars[k], total);
+      for (int q = 0; q < 3; ++q)
+        if (n16[q]) bulk_copy_g2s_hint(dst[q], src[q] - lo16(src[q]), n16[q], &bars[k], l2_evict_first());
+      s_cnt[k] += 1;
+    };
     {
-      constexpr int SW = FWD_MAX_NE / 32;   // softmax warps
-      float *wmax = s_wt;                   // [SW] (s_wt is written after the ranking)
-      const float lgv = tid < NE ? __ldcg(a.rlogits + tid) : -INFINITY;
-      float mx = lgv;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-      if (lane == 0 && warp < SW) wmax[warp] = mx;
-      __syncthreads();
-      mx = wmax[0];
-#pragma unroll
-      for (int w = 1; w < SW; ++w) mx = fmaxf(mx, wmax[w]);
+      const int rank = rank4(s_lg, -INFINITY);
+      if ((tid >> 2) < NE && (tid & 3) == 0 && rank <= K) {
+        s_spec[rank] = tid >> 2;
+        if (rank < K) issue(rank, tid >> 2);
+      }
+    }
+    trace_stamp(a.trace, 21);
+    {
       const float ev = tid < NE ? exp_cr(__fsub_rn(lgv, mx)) : 0.f;
-      double part = static_cast<double>(ev);
+      double part = static_cast<double>(ev);   // each warp's 32 experts by a shuffle tree, then the warps in order
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(FULL, part, o);
       if (lane == 0 && warp < SW) s_red[warp] = part;
@@ -570,27 +631,65 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
 #pragma unroll
       for (int w = 0; w < SW; ++w) tot += s_red[w];
       if (tid < ((NE + 3) & ~3)) probs[tid] = tid < NE ? __double2float_rn(__ddiv_rn(static_cast<double>(ev), tot)) : -1.0f;
-      trace_stamp(a.trace, 21);
-    }
-    __syncthreads();
-    {   // top-k by rank counting, ties to the lower id (c/src/forward.c:975-980)
-      constexpr int TPE = FWD_THREADS / FWD_MAX_NE;   // threads per expert, each a share of its competitors
-      const int e = tid / TPE, part = tid % TPE, n4 = (NE + 3) / 4, per = (n4 + TPE - 1) / TPE;
-      const float pe = e < NE ? probs[e] : 0.f;
-      int rank = 0;
-      const float4 *p4 = reinterpret_cast<const float4 *>(probs);
-      for (int j = part * per; j < min(n4, (part + 1) * per); ++j) {
-        const float4 q = p4[j];
-        const int f = 4 * j;
-        rank += (q.x > pe || (q.x == pe && f < e)) + (q.y > pe || (q.y == pe && f + 1 < e)) +
-                (q.z > pe || (q.z == pe && f + 2 < e)) + (q.w > pe || (q.w == pe && f + 3 < e));
-      }
-#pragma unroll
-      for (int o = 1; o < TPE; o <<= 1) rank += __shfl_xor_sync(FULL, rank, o);
-      if (e < NE && part == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = pe; }
     }
     __syncthreads();
     trace_stamp(a.trace, 22);
+    if (warp == 0) {   // strictly falling probabilities along the logit order through rank K: that order is the reference's
+      const int n = K < NE ? K + 1 : K;
+      const int se = lane < n ? s_spec[lane] : 0;
+      const float pl = lane < n && se >= 0 ? probs[se] : 0.f;
+      const float pn = __shfl_down_sync(FULL, pl, 1);
+      const bool strict = __all_sync(FULL, se >= 0 && (lane + 1 >= n || pl > pn));
+      if (strict && lane < K) {
+        s_sel[lane] = se;
+        s_wt[lane] = pl;
+        s_slot[lane] = lane;
+      }
+      if (lane == 0) s_flag[7] = strict ? 0 : 1;
+    }
+    __syncthreads();
+    trace_stamp(a.trace, 27);
+    if (s_flag[7]) {   // the full probability order (c/src/forward.c:975-980), then every chosen expert into a slot
+      const int e = tid >> 2;
+      const int rank = rank4(probs, -1.0f);
+      if (e < NE && (tid & 3) == 0 && rank < K) { s_sel[rank] = e; s_wt[rank] = probs[e]; }
+      __syncthreads();
+      const int tk0 = tid < K ? s_sel[tid] : 0;
+      if (warp == 0 && __any_sync(FULL, tk0 < 0 || tk0 >= NE)) {   // logits that do not order (NaN): no expert to fetch
+        if (lane == 0) set_error(&st->err, ERR_BAD_EXPERT);
+      } else if (warp == 0) {
+        // a slot holding an expert outside the top k takes a missing one: the missing rank's position among the missing
+        // ranks pairs it with the orphan slot at the same position
+        int gk = -1;
+        const int tk = lane < K ? s_sel[lane] : -2;
+        for (int h = 0; h < K; ++h) gk = s_spec[h] == tk ? h : gk;
+        const int sg = lane < K ? s_spec[lane] : -2;
+        bool in = false;
+        for (int k = 0; k < K; ++k) in |= s_sel[k] == sg;
+        const uint32_t orphan = __ballot_sync(FULL, lane < K && !in), missing = __ballot_sync(FULL, lane < K && gk < 0);
+        if (lane < K && gk < 0) {
+          const int at = __popc(missing & ((1u << lane) - 1u));
+          uint32_t o = orphan;
+          for (int t = 0; t < at && o; ++t) o &= o - 1u;
+          gk = o ? __ffs(o) - 1 : -1;
+          if (gk >= 0) s_fix[gk] = tk + 1;
+        }
+        if (lane < K) s_slot[lane] = gk >= 0 ? gk : 0;
+        if (lane < K && (gk < 0 || tk < 0)) set_error(&st->err, ERR_BAD_EXPERT);   // two sets of K: cannot happen
+      }
+      __syncthreads();
+      trace_stamp(a.trace, 26);
+      if (warp < K && lane == 0 && s_fix[warp]) {   // the wrong copies land first; then the right expert's
+        const int k = warp;
+        if (mbar_wait_bounded(&bars[k], static_cast<uint32_t>((s_cnt[k] - 1) & 1))) {
+          s_spec[k] = s_fix[k] - 1;
+          issue(k, s_spec[k]);
+        } else {
+          set_error(&st->err, ERR_WAIT_COPY);
+        }
+      }
+      __syncthreads();
+    }
     if (tid < K) {   // renormalisation (c/src/forward.c:984)
       float w = s_wt[tid];
       if (a.norm_topk) {
@@ -604,26 +703,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         a.route_wt[l * K + tid] = w;
       }
     }
+    __syncthreads();   // s_wn, s_slot and s_spec for every thread
     trace_stamp(a.trace, 8);
-    // this CTA's share of every chosen expert: gate/up rows into slots, down rows into dslots
-    auto gu_src = [&](int k, int q) -> const uint8_t * {
-      const size_t e = static_cast<size_t>(s_sel[k]);
+    auto gu_src = [&](int k, int q) -> const uint8_t * {   // slot k's gate (q 0) or up (q 1) rows in global memory
+      const size_t e = static_cast<size_t>(s_spec[k]);
       return q == 0 ? Ly.gate + e * Ly.gate_slab + static_cast<size_t>(j0) * a.grb : Ly.up + e * Ly.up_slab + static_cast<size_t>(j0) * a.grb;
     };
-    auto dn_src = [&](int k) -> const uint8_t * { return Ly.down + static_cast<size_t>(s_sel[k]) * Ly.down_slab + static_cast<size_t>(i0) * a.drb; };
-    if (tid == 0) s_flag[4] = l;   // read at the exit only
-    for (int k = warp; lane == 0 && k < K; k += NW) {
-      uint8_t *gs = slots + static_cast<size_t>(k) * a.slot_bytes, *ds = dslots + static_cast<size_t>(k) * a.dslot_bytes;
-      const uint8_t *src[3] = {gu_src(k, 0), gu_src(k, 1), dn_src(k)};
-      uint8_t *dst[3] = {gs, gs + a.gseg, ds};
-      const uint32_t len[3] = {static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(ngu) * a.grb, static_cast<uint32_t>(nd) * a.drb};
-      uint32_t n16[3], total = 0;
-      for (int q = 0; q < 3; ++q) { n16[q] = len[q] ? (lo16(src[q]) + len[q] + 15u) & ~15u : 0u; total += n16[q]; }
-      fence_proxy_async();   // the generic accesses of these buffers (attention scratch, dense rows) come first
-      mbar_arrive_expect_tx(&bars[k], total);
-      for (int q = 0; q < 3; ++q)
-        if (n16[q]) bulk_copy_g2s_hint(dst[q], src[q] - lo16(src[q]), n16[q], &bars[k], l2_evict_first());
-    }
+    auto dn_src = [&](int k) -> const uint8_t * { return Ly.down + static_cast<size_t>(s_spec[k]) * Ly.down_slab + static_cast<size_t>(i0) * a.drb; };
     // gate and up rows: a group of lanes per (expert, row), one lane per block
     {
       const int GL = lanes_for(nb);
@@ -639,7 +725,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         if (valid) {
           while (waited < k) {
             ++waited;
-            if (!mbar_wait_bounded(&bars[waited], par)) set_error(&st->err, ERR_WAIT_COPY);
+            if (!mbar_wait_bounded(&bars[waited], static_cast<uint32_t>((s_cnt[waited] - 1) & 1))) set_error(&st->err, ERR_WAIT_COPY);
           }
           if (has_blk) {
             const uint8_t *gs = slots + static_cast<size_t>(k) * a.slot_bytes;
@@ -667,28 +753,37 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     quant_global(a.hg, K * FF / 256, hq_qs, hq_d, hq_bs, warp, NW, lane);
     trace_stamp(a.trace, 23);
     for (int k = 0; k < K; ++k)
-      if (!mbar_wait_bounded(&bars[k], par)) set_error(&st->err, ERR_WAIT_COPY);
+      if (!mbar_wait_bounded(&bars[k], static_cast<uint32_t>((s_cnt[k] - 1) & 1))) set_error(&st->err, ERR_WAIT_COPY);
     __syncthreads();
     trace_stamp(a.trace, 24);
-    {
-      const int C = K * nbd, combo = tid % C, grp = tid / C, ngrp = FWD_THREADS / C;
-      if (grp < ngrp) {
-        const int blk = combo / K, k = combo - blk * K;
+    {   // down rows: a group of lanes per (expert, block), one row per lane, so the group's activation reads are broadcasts
+      const int C = K * nbd, LP = nd > 16 ? 32 : 16, ppw = 32 / LP, lp = lane & (LP - 1);
+      for (int p = warp * ppw + lane / LP; p < C; p += NW * ppw) {
+        const int k = p / nbd, blk = p - k * nbd;
         const uint8_t *drows = dslots + static_cast<size_t>(k) * a.dslot_bytes + lo16(dn_src(k));
-        for (int r = grp; r < nd; r += ngrp)
-          terms[(r * K + k) * nbd + blk] = blk_dot(Ly.down_type, drows + static_cast<size_t>(r) * a.drb, blk, hq_qs, hq_bs, hq_d, k * nbd + blk);
+        for (int r = lp; r < nd; r += LP)   // p = k * nbd + blk: the block's index in the Q8_K of every expert's hg
+          terms[(r * K + k) * nbd + blk] = blk_dot(Ly.down_type, drows + static_cast<size_t>(r) * a.drb, blk, hq_qs, hq_bs, hq_d, p);
       }
     }
     __syncthreads();
     trace_stamp(a.trace, 25);
-    for (int r = tid; r < nd; r += FWD_THREADS) {
-      float moe = 0.f;
-      for (int k = 0; k < K; ++k) {
+    {   // wt * hd per (row, rank), hd the block terms in block order; then per row their sum in rank order, the residual
+      float *wprod = rprod;   // [nd][K] (the router products are done with)
+      for (int q = tid; q < nd * K; q += FWD_THREADS) {   // q = row * K + rank; the terms are by slot
+        const int r = q / K, k = q - r * K;
+        const float *tq = terms + (r * K + s_slot[k]) * nbd;
         float h = 0.f;
-        for (int b = 0; b < nbd; ++b) h = __fadd_rn(h, terms[(r * K + k) * nbd + b]);
-        moe = __fadd_rn(moe, __fmul_rn(s_wn[k], h));
+#pragma unroll 4
+        for (int b = 0; b < nbd; ++b) h = __fadd_rn(h, tq[b]);
+        wprod[q] = __fmul_rn(s_wn[k], h);
       }
-      a.x[i0 + r] = __fadd_rn(xr[r], __fmul_rn(a.resid_scale, moe));
+      __syncthreads();
+      for (int r = tid; r < nd; r += FWD_THREADS) {
+        float moe = 0.f;
+#pragma unroll 8
+        for (int k = 0; k < K; ++k) moe = __fadd_rn(moe, wprod[r * K + k]);
+        a.x[i0 + r] = __fadd_rn(xr[r], __fmul_rn(a.resid_scale, moe));
+      }
     }
     trace_stamp(a.trace, 11);
     if (!(ok = grid.sync())) break;
@@ -763,8 +858,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   if (tid == 0) {
     if (s_flag[1]) mbar_wait_bounded(rbar, static_cast<uint32_t>(s_flag[3]));   // an unconsumed router copy
     if (s_flag[5]) mbar_wait_bounded(dbar, static_cast<uint32_t>(s_flag[6]));   // an unconsumed dense copy
-    if (s_flag[4] >= 0)   // the last layer's expert copies (waited already unless a wait gave up)
-      for (int k = 0; k < K; ++k) mbar_wait_bounded(&bars[k], static_cast<uint32_t>(s_flag[4] & 1));
+    for (int k = 0; k < K; ++k)   // each slot's last copies (waited already unless a wait gave up)
+      if (s_cnt[k] > 0) mbar_wait_bounded(&bars[k], static_cast<uint32_t>((s_cnt[k] - 1) & 1));
     __threadfence();
     const uint32_t prev = atomicAdd(&st->sync[2], 1u);
     if (prev == uG - 1) {

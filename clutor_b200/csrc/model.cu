@@ -231,9 +231,10 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   a.off_bars = st_take(8 * (a.K + 2 + HEAD_STAGES));
   a.off_xn = st_take(static_cast<size_t>(a.E) * 4);
   a.off_xq = st_take(XQW + 2 * (XQW / 16) + 4 * (XQW / 256));
-  a.off_misc = st_take(NW * 8 + 8 * 4 + 3 * 32 * 4 + FWD_MAX_NE * 4 + NW * 8);
+  a.off_misc = st_take(NW * 8 + 8 * 4 + 3 * 32 * 4 + FWD_MAX_NE * 4 + NW * 8 + FWD_MAX_NE * 4 + 4 * 32 * 4);
   a.off_router = st_take(static_cast<size_t>(a.nre_max) * a.E * 4);
-  a.off_rprod = st_take(static_cast<size_t>(a.nre_max) * 8 * (a.E / 8 + 4) * 4);
+  // the router products, then each row's weighted expert outputs [rd_max][K]
+  a.off_rprod = st_take(std::max<size_t>(static_cast<size_t>(a.nre_max) * 8 * (a.E / 8 + 4), static_cast<size_t>(a.rd_max) * a.K) * 4);
   a.off_terms = st_take(std::max<size_t>(static_cast<size_t>(a.rd_max) * a.K * nbd * 4, 2 * NW * 8));
   a.off_hq = st_take(static_cast<size_t>(a.K) * a.FF + 2 * (static_cast<size_t>(a.K) * a.FF / 16) + 4 * (static_cast<size_t>(a.K) * a.FF / 256));
   a.off_xr = st_take(static_cast<size_t>(a.rd_max) * 4);

@@ -38,6 +38,20 @@ PHASES = [
 ]
 GRID_ROUTER = (4, 5)
 KERNELS = {"group": (0, GROUP_PHASES, GROUP_ROUTER), "grid": (1, PHASES, GRID_ROUTER)}
+# the whole-model step (fwd.cu), one layer: thread 0's boundaries in order; the attention CTAs' own steps (query heads
+# c, c + G, ...); the step's last boundary (12: after the last layer's closing grid barrier)
+MODEL_PHASES = [
+    (14, "rmsnorm, Q8_K, dense rows landed"), (1, "QKV rows"), (2, "grid barrier"), (4, "attention (32 CTAs), grid barrier"),
+    (5, "Q8_K of att, O rows, residual"), (6, "grid barrier"), (7, "ffn rmsnorm, router products, Q8_K of xn"),
+    (20, "all logits visible"), (21, "rank by logit, copies issued"), (22, "softmax"), (8, "probability order, weights"),
+    (9, "gate/up rows"),
+    (10, "grid barrier"), (23, "Q8_K of hg"), (24, "down rows landed"), (25, "down rows"), (11, "combine, residual"),
+    (12, "grid barrier"),
+]
+ASSUMED_MHZ = 1950.0
+MODEL_DETAIL = [("(MoE) probability check", 22, 27), ("(MoE) renormalisation", 27, 8)]
+MODEL_ATTENTION = [("(attention CTAs) q, k, v, scores", 2, 15), ("(attention CTAs) softmax", 15, 16),
+                   ("(attention CTAs) values", 16, 17), ("(attention CTAs) to the barrier's end", 17, 4)]
 
 
 def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20, kernel: str = "group", cooperative: bool = True) -> dict:
@@ -113,13 +127,78 @@ def run(n_layers: int = 48, down: str = "q4_k", replays: int = 20, kernel: str =
             "gap_to_next_launch_us": gap, "detail": detail}
 
 
+def run_model(n_layers: int = 48, warm: int = 60, steps: int = 12) -> dict:
+    """The whole-model step (fwd.cu) at positions warm .. warm + steps - 1: each step launched alone with the trace on;
+    the stamps of its last layer (every layer overwrites them), medians over CTAs 0-127 and the steps."""
+    import dataclasses
+
+    import torch
+
+    import clutor_b200 as cb
+    from clutor_b200 import synth_model as sm
+    from clutor_b200.model import Model
+
+    spec = dataclasses.replace(sm.QWEN3_30B_A3B, n_layer=n_layers)
+    image = sm.image(spec, seed=1)
+    ctx = cb.Context(0)
+    try:
+        model = Model(ctx, image, warm + steps + 8)
+        tok = model.generate(1, warm)[-1]
+        G = torch.cuda.get_device_properties(0).multi_processor_count
+        tr = torch.zeros((steps, G, 32), dtype=torch.int64, device="cuda")
+        for i in range(steps):
+            ctx.set_trace(tr[i])
+            _, tok, _ = model.step(tok, logits=False)
+        ctx.set_trace(None)
+        torch.cuda.synchronize()
+        t = tr.cpu().numpy().astype(np.int64)
+        n_head = spec.n_head
+        model.close()
+    finally:
+        ctx.close()
+    cta = slice(0, min(128, t.shape[1]))
+    # the boundaries are SM cycles and only the step's entry and exit are global time, so the cycles are read at the
+    # clock these B200s hold under this load (1,945-1,965 MHz in every bench's clock record)
+    ns = (t[:, cta, 31] - t[:, cta, 30]).astype(np.float64)
+    to_us = 1.0 / ASSUMED_MHZ
+    rows, prev = [], 0
+    for b, name in MODEL_PHASES:
+        d = (t[:, cta, b] - t[:, cta, prev]) * to_us
+        rows.append((name, float(np.median(d)), float(np.percentile(d, 90))))
+        prev = b
+    att = slice(0, min(n_head, t.shape[1]))
+    detail = []
+    for name, b0, b1 in MODEL_ATTENTION:
+        d = (t[:, att, b1] - t[:, att, b0]) * to_us
+        detail.append((name, float(np.median(d)), float(np.percentile(d, 90))))
+    layer = float(np.median((t[:, cta, 12] - t[:, cta, 0]) * to_us))
+    for name, b0, b1 in MODEL_DETAIL:
+        d = (t[:, cta, b1] - t[:, cta, b0]) * to_us
+        detail.append((name, float(np.median(d)), float(np.percentile(d, 90))))
+    reranked = float(np.mean(t[:, cta, 26] != 0))
+    return {"step_us": float(np.median(ns)) / 1000.0, "layer_us": layer, "phases": rows, "attention": detail,
+            "reranked": reranked}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--down", default="q4_k", choices=["q4_k", "q6_k"])
-    ap.add_argument("--kernel", default="group", choices=sorted(KERNELS))
+    ap.add_argument("--kernel", default="group", choices=sorted(KERNELS) + ["model"])
     ap.add_argument("--plain-launch", action="store_true", help="launch without the cooperative attribute")
     a = ap.parse_args()
+    if a.kernel == "model":
+        r = run_model(a.layers)
+        print(f"whole step {r['step_us']:.1f} us (global timer, entry to exit, traced); last layer {r['layer_us']:.2f} us at an "
+              "assumed 1950 MHz SM clock")
+        print("| phase (thread 0 of each CTA, last layer) | median us | p90 us |")
+        print("|---|---|---|")
+        for name, med, p90 in r["phases"]:
+            print(f"| {name} | {med:.3f} | {p90:.3f} |")
+        for name, med, p90 in r["attention"]:
+            print(f"| (detail) {name} | {med:.3f} | {p90:.3f} |")
+        print(f"last layers ranked again by probability (a tie on the logit order): {100 * r['reranked']:.1f} %")
+        return
     r = run(a.layers, a.down, kernel=a.kernel, cooperative=not a.plain_launch)
     print(f"{r['us_per_layer']:.2f} us per layer (CUDA events, traced graph), SM clock {r['sm_mhz']:.0f} MHz (from the trace)")
     print("| phase (thread 0 of each CTA) | median us | p90 us |")
