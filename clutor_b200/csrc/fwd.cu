@@ -195,17 +195,19 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   const int nb = E / 256, nbd = FF / 256;
   FwdState *st = a.st;
 
-  // [0, K) experts, [K] router rows, [K+1] dense rows, [K+2, K+2+HEAD_STAGES) output stages
+  // [0, K) experts, [K] router rows, [K+1] dense rows, [K+2, K+2+HEAD_STAGES) output stages, [K+2+HEAD_STAGES] the
+  // attention head's prefetch
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);
-  uint64_t *rbar = bars + K, *dbar = bars + K + 1, *hb = bars + K + 2;
+  uint64_t *rbar = bars + K, *dbar = bars + K + 1, *hb = bars + K + 2, *abar = bars + K + 2 + HEAD_STAGES;
   float *xn = reinterpret_cast<float *>(smem + a.off_xn);             // [E]
   int8_t *xq_qs = reinterpret_cast<int8_t *>(smem + a.off_xq);        // Q8_K of the current vector (up to n_q wide)
   const int XQW = a.n_q > E ? a.n_q : E;
   int16_t *xq_bs = reinterpret_cast<int16_t *>(smem + a.off_xq + XQW);
   float *xq_d = reinterpret_cast<float *>(smem + a.off_xq + XQW + 2 * (XQW / 16));
   double *s_red = reinterpret_cast<double *>(smem + a.off_misc);      // [NW]
-  // [0] barrier verdict, [1] a router copy in flight, [2] the router logits arrived, [3] its parity, [5] a dense copy in
-  // flight, [6] its parity, [7] the probability order differs from the logit order
+  // [0] barrier verdict, [1] a router copy in flight, [2] the router logits arrived, [3] its parity, [4] the layer of the
+  // last attention prefetch (-1: none), [5] a dense copy in flight, [6] its parity, [7] the probability order differs
+  // from the logit order
   int *s_flag = reinterpret_cast<int *>(s_red + NW);
   int *s_sel = s_flag + 8;                                             // [32]
   float *s_wt = reinterpret_cast<float *>(s_sel + 32);                 // [32]
@@ -245,7 +247,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   trace_time(a.trace, 30);
 
   if (tid == 0) {
-    for (int s = 0; s < K + 2 + HEAD_STAGES; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < K + 3 + HEAD_STAGES; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
     if (nre > 0) {   // layer 0's router rows
       mbar_arrive_expect_tx(rbar, static_cast<uint32_t>(nre) * E * 4u);
@@ -256,6 +258,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     s_flag[1] = nre > 0;
     s_flag[3] = 0;
     for (int k = 0; k < 32; ++k) s_cnt[k] = 0;
+    s_flag[4] = -1;
     s_flag[5] = 1;
     s_flag[6] = 0;
   }
@@ -279,6 +282,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     const uint32_t par = static_cast<uint32_t>(l & 1);
     const size_t cache_l = static_cast<size_t>(l) * a.ctx * a.n_kvw;
     trace_stamp(a.trace, 0);
+    // the attention head's inputs that do not depend on this layer's activations, into its scratch while phase A runs:
+    // the position's rotary row and the QK-norm weights
+    if (c < a.n_head && warp == 0 && lane < 3) {
+      const bool qkn = a.qk_mode != 0;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(abar, static_cast<uint32_t>(hd) * 4u * (qkn ? 3u : 1u));
+        s_flag[4] = l;
+      }
+      __syncwarp(7u);
+      fence_proxy_async();   // the generic accesses of the scratch (the previous layer's down rows) come first
+      float *pre_f = reinterpret_cast<float *>(dslots) + hd;   // rope row, qn, kn (the head's scratch layout below)
+      if (lane == 0) bulk_copy_g2s(pre_f, a.rope_cs + static_cast<size_t>(pos) * hd, hd * 4u, abar);
+      else if (qkn)
+        bulk_copy_g2s(pre_f + lane * hd, lane == 1 ? (a.qk_mode == 1 ? Ly.qn + static_cast<size_t>(c) * hd : Ly.qn)
+                                                   : (a.qk_mode == 1 ? Ly.kn + static_cast<size_t>(c / GRP) * hd : Ly.kn), hd * 4u, abar);
+    }
     // ---- A: attention input; this CTA's rows of [wq; wk; wv] --------------------------------------------------------
     rmsnorm_to_smem(a.x, Ly.attn_norm, xn, E, a.eps, s_red);
     quant_smem(xn, E, xq_qs, xq_d, xq_bs, warp, NW, lane);
@@ -309,7 +328,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
     {
       const float *qg = a.qkv, *kg = a.qkv + nq, *vg = a.qkv + nq + nk;
       float *qf = reinterpret_cast<float *>(dslots);                       // [hd] the query
-      __half *knew = reinterpret_cast<__half *>(qf + hd);                  // [hd] the new key, rounded to half
+      float *rope_s = qf + hd;                                             // [hd] the position's rotary row (prefetched)
+      float *qnw = rope_s + hd, *knw = qnw + hd;                           // [hd] each: the QK-norm weights (prefetched)
+      __half *knew = reinterpret_cast<__half *>(knw + hd);                 // [hd] the new key, rounded to half
       __half *vnew = knew + hd;                                            // [hd] the new value
       __half *kvst = vnew + hd;                                            // [FWD_ATT_BLOCK][hd + 8] staged keys or values
       float *scs = reinterpret_cast<float *>(kvst + FWD_ATT_BLOCK * (hd + 8));   // [a chunk] scores, then weights
@@ -317,8 +338,10 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
       float *s_wmax = s_wt;                                                // [NW] (s_wt is written in the MoE phase)
       for (int h = c; h < a.n_head; h += G) {
         const int g = h / GRP, j = h - g * GRP;
+        const bool pre = h == c;   // the first head's rotary row and norm weights are prefetched
         float qscale = 1.f, kscale = 1.f;
         __syncthreads();   // the scratch of the previous head
+        if (pre && !mbar_wait_bounded(abar, par)) set_error(&st->err, ERR_WAIT_COPY);
         if (a.qk_mode == 1) {   // QK-norm over the whole query and the whole key (olmoe): their scales
           double sq = 0.0, sk = 0.0;
           for (int i = tid; i < nq; i += FWD_THREADS) { const double v = __ldcg(qg + i); sq += v * v; }
@@ -335,9 +358,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
         if (warp < 2) {   // warp 0: the query head; warp 1: the key head (and the value)
           const bool isk = warp == 1;
           const float *src = isk ? kg + g * hd : qg + h * hd;
-          float v[EPL];
+          float v[EPL], vv[EPL];   // the query or the new key; the new value (warp 1), loaded together
 #pragma unroll
-          for (int e = 0; e < EPL; ++e) v[e] = __ldcg(src + lane + 32 * e);
+          for (int e = 0; e < EPL; ++e) {
+            v[e] = __ldcg(src + lane + 32 * e);
+            vv[e] = isk ? __ldcg(vg + g * hd + lane + 32 * e) : 0.f;
+          }
           if (a.qk_mode == 2) {   // per head, one shared weight
             double ss = 0.0;
 #pragma unroll
@@ -345,22 +371,22 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
             const float s1 = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(ss / hd), a.eps)));
-            const float *w = isk ? Ly.kn : Ly.qn;
+            const float *w = pre ? (isk ? knw : qnw) : isk ? Ly.kn : Ly.qn;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), __ldg(w + lane + 32 * e));
+            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), w[lane + 32 * e]);
           } else if (a.qk_mode == 1) {
             const float s1 = isk ? kscale : qscale;
-            const float *w = isk ? Ly.kn + g * hd : Ly.qn + h * hd;
+            const float *w = pre ? (isk ? knw : qnw) : isk ? Ly.kn + g * hd : Ly.qn + h * hd;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), __ldg(w + lane + 32 * e));
+            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], s1), w[lane + 32 * e]);
           }
-          rope_warp<EPL>(v, a.rope_cs + static_cast<size_t>(pos) * hd, a.rope_pairs != 0);
+          rope_warp<EPL>(v, pre ? rope_s : a.rope_cs + static_cast<size_t>(pos) * hd, a.rope_pairs != 0);
           if (isk) {
             __half *kd = a.kc + cache_l + static_cast<size_t>(pos) * nk + g * hd;
             __half *vd = a.vc + cache_l + static_cast<size_t>(pos) * nk + g * hd;
 #pragma unroll
             for (int e = 0; e < EPL; ++e) {
-              const __half kh = __float2half_rn(v[e]), vh = __float2half_rn(__ldcg(vg + g * hd + lane + 32 * e));
+              const __half kh = __float2half_rn(v[e]), vh = __float2half_rn(vv[e]);
               knew[lane + 32 * e] = kh;
               vnew[lane + 32 * e] = vh;
               if (j == 0) { kd[lane + 32 * e] = kh; vd[lane + 32 * e] = vh; }   // kv_put (c/src/forward.c:563-565)
@@ -858,6 +884,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1) fwd_kernel(const FwdArgs a) {
   if (tid == 0) {
     if (s_flag[1]) mbar_wait_bounded(rbar, static_cast<uint32_t>(s_flag[3]));   // an unconsumed router copy
     if (s_flag[5]) mbar_wait_bounded(dbar, static_cast<uint32_t>(s_flag[6]));   // an unconsumed dense copy
+    if (s_flag[4] >= 0) mbar_wait_bounded(abar, static_cast<uint32_t>(s_flag[4] & 1));   // the last attention prefetch
     for (int k = 0; k < K; ++k)   // each slot's last copies (waited already unless a wait gave up)
       if (s_cnt[k] > 0) mbar_wait_bounded(&bars[k], static_cast<uint32_t>((s_cnt[k] - 1) & 1));
     __threadfence();

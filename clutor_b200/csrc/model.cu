@@ -228,7 +228,7 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   const int XQW = std::max(a.E, a.n_q);
   size_t o = 0;
   auto st_take = [&](size_t bytes, size_t align = 16) { const size_t at = al(o, align); o = at + bytes; return static_cast<uint32_t>(at); };
-  a.off_bars = st_take(8 * (a.K + 2 + HEAD_STAGES));
+  a.off_bars = st_take(8 * (a.K + 3 + HEAD_STAGES));
   a.off_xn = st_take(static_cast<size_t>(a.E) * 4);
   a.off_xq = st_take(XQW + 2 * (XQW / 16) + 4 * (XQW / 256));
   a.off_misc = st_take(NW * 8 + 8 * 4 + 3 * 32 * 4 + FWD_MAX_NE * 4 + NW * 8 + FWD_MAX_NE * 4 + 4 * 32 * 4);
@@ -260,13 +260,14 @@ static int model_setup(clb200_model *m, const Gguf &g, int n_ctx, char *err, siz
   const size_t slots_size = al(std::max<size_t>(static_cast<size_t>(a.K) * a.slot_bytes, dense_need), 128);
   a.off_slots = st_take(slots_size, 128);
   // the dslots, right after the slots, hold the chosen experts' down rows, or the attention scratch of a query head: its
-  // query [hd] floats, the new key and value [hd] halves each, FWD_ATT_BLOCK staged key or value rows, the scores of every
-  // position, and per 256-position chunk its maximum, sum and [hd] value sums; the output matrix's stages span both regions
+  // query, rotary row and QK-norm weights [hd] floats each, the new key and value [hd] halves each, FWD_ATT_BLOCK staged
+  // key or value rows, the scores of every position, and per 256-position chunk its maximum, sum and [hd] value sums; the
+  // output matrix's stages span both regions
   const int grp = a.n_head / a.n_kv;
   const bool can_group = grp >= 2 && grp <= FWD_MAX_GROUP;   // else every step takes the plain path over the whole context
   const size_t att_chunks = can_group ? (static_cast<size_t>(a.ctx) + FWD_ATT_CHUNK - 1) / FWD_ATT_CHUNK : 1;
   const size_t att_scores = can_group ? FWD_ATT_CHUNK : (static_cast<size_t>(a.ctx) + 3) & ~size_t(3);
-  const size_t att_need = static_cast<size_t>(hd) * 8 + static_cast<size_t>(FWD_ATT_BLOCK) * (hd + 8) * 2 + att_scores * 4 +
+  const size_t att_need = static_cast<size_t>(hd) * 20 + static_cast<size_t>(FWD_ATT_BLOCK) * (hd + 8) * 2 + att_scores * 4 +
                           att_chunks * (2 + hd) * 4;
   const size_t head_need = static_cast<size_t>(HEAD_STAGES) * al(HEAD_ROWS * row_bytes(out->type, a.E) + 32, 16);
   const size_t dslots_size = std::max<size_t>(std::max<size_t>(static_cast<size_t>(a.K) * a.dslot_bytes, att_need),

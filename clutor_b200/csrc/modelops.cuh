@@ -44,7 +44,7 @@ CLB_DEV void embed_row(const FwdMat &m, int token, int E, float *y) {
 // Rotary embedding of one head held by a warp, EPL = hd / 32 elements per lane at i = lane + 32 e. NEOX pairs (i, i + hd/2)
 // (c/src/forward.c:428-435) or adjacent pairs (2i, 2i + 1) (:420-426). The angle's cosine and sine come from tables the
 // host filled with the reference's own expressions and C library (cosf / sinf of pos * powf(base, -2i / hd)): cs holds
-// [hd / 2] cosines then [hd / 2] sines for this position.
+// [hd / 2] cosines then [hd / 2] sines for this position (global or shared memory).
 template <int EPL>
 CLB_DEV void rope_warp(float (&v)[EPL], const float *cs, bool pairs) {
   constexpr int H = 16 * EPL;   // hd / 2
@@ -52,7 +52,7 @@ CLB_DEV void rope_warp(float (&v)[EPL], const float *cs, bool pairs) {
   if (!pairs) {
 #pragma unroll
     for (int e = 0; e < EPL / 2; ++e) {
-      const float c = __ldg(cs + lane + 32 * e), s = __ldg(cs + H + lane + 32 * e);
+      const float c = cs[lane + 32 * e], s = cs[H + lane + 32 * e];
       const float a = v[e], b = v[e + EPL / 2];
       v[e] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
       v[e + EPL / 2] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
@@ -61,7 +61,7 @@ CLB_DEV void rope_warp(float (&v)[EPL], const float *cs, bool pairs) {
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
       const int i = lane + 32 * e;
-      const float c = __ldg(cs + i / 2), s = __ldg(cs + H + i / 2);
+      const float c = cs[i / 2], s = cs[H + i / 2];
       const float other = __shfl_xor_sync(FULL, v[e], 1);
       const float a = (i & 1) ? other : v[e], b = (i & 1) ? v[e] : other;
       v[e] = (i & 1) ? __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c)) : __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
