@@ -1,7 +1,8 @@
 // The batched MoE block (T > 1 tokens): the reference's c/src/forward.c:1132-1210.
 //
 //   norm_kernel      per token: rmsnorm (double sum of squares), xn, Q8_K of xn
-//   router_kernel    per (8 tokens, 32 experts): the reference's dotf logits, each router row read once for the 8 tokens
+//   router_kernel    per (2 tokens, 32 experts), up to 512 tokens; router_chunked_kernel per (32 tokens, 32 experts)
+//                    beyond: the reference's dotf logits, each router row read once for the CTA's tokens
 //   topk_kernel      per token: softmax (double sum), top-k by repeated arg-max with ties to the lower id, renormalisation
 //   dispatch_kernel  counting sort of the T*K (token, expert) slots by expert; each expert's tokens in ascending token order
 //                    (the reference's who[] list, c/src/forward.c:1189-1190), plus each expert's first appearance and the
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(BT) norm_kernel(const BatchArgs a) {
 // xn rows sit in shared memory transposed by chain -- element i of token t at [t][i % 8][i / 8], rows padded by 4 floats so
 // the eight chains fall in different banks -- so a lane reads its chain's next four elements with one 16-byte load, and a
 // router row is read once for all the tokens.
-// ROUTER_TOKENS: 8 tokens a CTA for large batches (fewer router reads), 2 for small ones (more CTAs).
+// ROUTER_TOKENS: 2 tokens a CTA for batches up to 512 tokens (more CTAs); larger batches take router_chunked_kernel.
 CLB_DEV int router_row(int E) { return E / 8 + 4; }   // floats per chain row
 template <int ROUTER_TOKENS>
 __global__ void __launch_bounds__(BT) router_kernel(const BatchArgs a) {
@@ -136,6 +137,75 @@ __global__ void __launch_bounds__(BT) router_kernel(const BatchArgs a) {
   }
 #pragma unroll
   for (int t = 0; t < ROUTER_TOKENS; ++t) {
+    float p[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) p[l] = __shfl_sync(FULL, s[t], (lane & ~7) + l);
+    if (t < nt && e < a.NE && l8 == 0)
+      a.logits[static_cast<size_t>(t0 + t) * a.NE + e] =
+          __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])), __fadd_rn(__fadd_rn(p[4], p[5]), __fadd_rn(p[6], p[7])));
+  }
+}
+
+// Router logits for large batches: 32 tokens x 32 experts per CTA, so each router value is read once for 32 tokens. The
+// tokens' xn rows pass through shared memory 512 elements at a time, transposed by chain as above; a lane's chain for
+// each of the 32 tokens carries from one chunk to the next, so every chain adds its products in element order, the
+// reference's dotf (c/src/forward.c:574-581), and the logits are the same bits as router_kernel's.
+constexpr int RC_TOKENS = 32, RC_CHUNK = 512, RC_ROW = RC_CHUNK / 8 + 4;   // RC_ROW: floats per chain row of a chunk
+constexpr int RC_SMEM = RC_TOKENS * 8 * RC_ROW * 4;
+__global__ void __launch_bounds__(BT, 2) router_chunked_kernel(const BatchArgs a) {
+  extern __shared__ __align__(16) float xs[];   // [RC_TOKENS][8][RC_ROW]
+  const int E = a.E, t0 = blockIdx.x * RC_TOKENS, nt = min(RC_TOKENS, a.T - t0);
+  const int tid = threadIdx.x, lane = tid & 31, grp = tid >> 3, l8 = tid & 7, e = blockIdx.y * ROUTE_EXPERTS + grp;
+  const float *w = a.router + static_cast<size_t>(min(e, a.NE - 1)) * E;   // rows past NE read the last row, unused
+  float s[RC_TOKENS];
+#pragma unroll
+  for (int t = 0; t < RC_TOKENS; ++t) s[t] = 0.f;
+  for (int c0 = 0; c0 < E; c0 += RC_CHUNK) {
+    const int ce = min(RC_CHUNK, E - c0), n4 = ce / 4;   // E is a multiple of 256: ce is 512 or 256
+    __syncthreads();   // the previous chunk is consumed
+    {   // every token's chunk: all loads in flight before the transposing stores
+      constexpr int PER = RC_TOKENS * RC_CHUNK / 4 / BT;
+      float4 r[PER];
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int v = u * BT + tid, t = v / n4, k4 = v - t * n4;
+        r[u] = (t < nt) ? __ldcg(reinterpret_cast<const float4 *>(a.xn + static_cast<size_t>(t0 + t) * E + c0) + k4)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int v = u * BT + tid, t = v / n4, k = 4 * (v - t * n4);   // k a multiple of 4: chains k%8 .. k%8+3, step k/8
+        if (t < RC_TOKENS) {
+          float *d = xs + t * 8 * RC_ROW + (k & 7) * RC_ROW + (k >> 3);
+          d[0] = r[u].x;
+          d[RC_ROW] = r[u].y;
+          d[2 * RC_ROW] = r[u].z;
+          d[3 * RC_ROW] = r[u].w;
+        }
+      }
+    }
+    __syncthreads();
+    if (e < a.NE) {
+      for (int j0 = 0; j0 < ce / 8; j0 += 16) {   // chain steps j0 .. j0+15 of the chunk: 16 router loads in flight
+        float wv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) wv[j] = __ldg(w + c0 + l8 + 8 * (j0 + j));
+#pragma unroll
+        for (int j4 = 0; j4 < 4; ++j4) {
+#pragma unroll
+          for (int t = 0; t < RC_TOKENS; ++t) {
+            const float4 xv = *reinterpret_cast<const float4 *>(xs + t * 8 * RC_ROW + l8 * RC_ROW + j0 + 4 * j4);
+            s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4], xv.x));
+            s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4 + 1], xv.y));
+            s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4 + 2], xv.z));
+            s[t] = __fadd_rn(s[t], __fmul_rn(wv[4 * j4 + 3], xv.w));
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < RC_TOKENS; ++t) {
     float p[8];
 #pragma unroll
     for (int l = 0; l < 8; ++l) p[l] = __shfl_sync(FULL, s[t], (lane & ~7) + l);
@@ -597,14 +667,14 @@ int launch_route(const BatchArgs &a, void *stream_) {
   cudaGetDevice(&dev);
   static bool attr[64] = {};
   if (dev < 64 && !attr[dev]) {
-    cudaFuncSetAttribute(router_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 8 * (4096 / 8 + 4) * 4);
+    cudaFuncSetAttribute(router_chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RC_SMEM);
     cudaFuncSetAttribute(router_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8 * (4096 / 8 + 4) * 4);
     attr[dev] = true;
   }
   norm_kernel<<<a.T, BT, 0, st>>>(a);
-  const dim3 rg8((a.T + 7) / 8, (a.NE + ROUTE_EXPERTS - 1) / ROUTE_EXPERTS), rg2((a.T + 1) / 2, rg8.y);
-  if (a.T > 512) router_kernel<8><<<rg8, BT, 8 * 8 * (a.E / 8 + 4) * 4, st>>>(a);
-  else router_kernel<2><<<rg2, BT, 2 * 8 * (a.E / 8 + 4) * 4, st>>>(a);
+  const int eg = (a.NE + ROUTE_EXPERTS - 1) / ROUTE_EXPERTS;
+  if (a.T > 512) router_chunked_kernel<<<dim3((a.T + RC_TOKENS - 1) / RC_TOKENS, eg), BT, RC_SMEM, st>>>(a);
+  else router_kernel<2><<<dim3((a.T + 1) / 2, eg), BT, 2 * 8 * (a.E / 8 + 4) * 4, st>>>(a);
   topk_kernel<<<a.T, 32, 0, st>>>(a);
   return static_cast<int>(cudaGetLastError());
 }
