@@ -74,6 +74,7 @@ struct FwdArgs {
                                // reference computes them (c/src/forward.c:428-435)
   int rgu_max, rd_max, nre_max;
   unsigned long long *trace;   // per-CTA phase trace (32 entries per CTA) or null
+  int force_miss;              // test hook: the copies of rank K - 1 first go out for the expert ranked K (0: off)
 };
 
 // Launches one step on `stream` with `ctas` CTAs (one per SM, all co-resident: a cooperative launch).

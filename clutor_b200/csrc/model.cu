@@ -447,6 +447,7 @@ static int launch_step(clb200_model *m, int token, int feed, char *err, size_t e
   FwdArgs a = m->args;
   a.feed = feed;
   a.trace = m->ctx->trace;
+  a.force_miss = m->ctx->force_miss;
   CUDA_OR(fwd_launch(a, m->ctas, m->stream), "launching the step");
   return 0;
 }
@@ -487,6 +488,7 @@ int clb200_model_generate(clb200_model *m, int token, int n, int *tokens_out, ch
     FwdArgs g = a;
     g.feed = 1;
     g.trace = nullptr;
+    g.force_miss = m->ctx->force_miss;   // as the graph is captured
     cudaGraph_t graph = nullptr;
     CUDA_OR(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "capturing the step");
     const cudaError_t le = fwd_launch(g, m->ctas, m->stream);

@@ -85,9 +85,10 @@ int clb200_moe_ffn_dev(clb200_ctx *c, int layer, float *x, int T, int *sel, floa
  *     allows it (each chosen expert streamed by its own group of SMs; no grid-wide wait after the routing); 1 (default): the
  *     grid-wide kernel (every SM streams a share of every chosen expert), which the expert store's calls use in any case.
  *     Both give the same results.
- *   CLB200_OPT_TEST_SPECULATION_MISS: a test hook. 1: both one-token kernels first fetch the expert ranked K + 1 in place of
- *     the one ranked K, as if two probabilities had tied at rank K, so that their correction paths run on every call; the
- *     results must not change. 0 (default): off.
+ *   CLB200_OPT_TEST_SPECULATION_MISS: a test hook. 1: both one-token kernels, and the whole-model step of models opened on
+ *     the context, first fetch the expert ranked K + 1 in place of the one ranked K, as if two probabilities had tied at
+ *     rank K, so that their correction paths run on every call (every layer); the results must not change. 0 (default):
+ *     off.
  *   CLB200_OPT_TEST_STALL_WAIT: a test hook for the failure path. N > 0: the grid-wide kernel's wait for the router logits
  *     targets a count that no CTA reaches and gives up after N polls (1 << 14 is about a millisecond), so every CTA takes its
  *     error path and the launch ends with the device error word set (ERR_WAIT_ROUTER, reported by clb200_status or the host
