@@ -127,6 +127,54 @@ def test_dispatch_c4_shape_2048_tokens(ctx):
     print(f"T={T}: {n} experts dispatched, lists identical to the reference's")
 
 
+def ep_routed(ctx, E, NE, K, T, seed):
+    """The routing of T tokens through the expert-parallel route entry point (clb200_ep_route, the batched block's first
+    half; the experts are never read, so the layer carries placeholders): (sel, wt) device tensors, the layer's router and
+    norm as host arrays, and the tokens."""
+    import ctypes as C
+
+    import torch
+
+    import clutor_b200 as cb
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    dummy = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    L = synth.DeviceLayer(E=E, FF=1536, NE=NE, K=K, gate_type=synth.T_Q4_K, up_type=synth.T_Q4_K, down_type=synth.T_Q4_K,
+                          ffn_norm=(1.0 + 0.1 * torch.randn(E, device="cuda", generator=gen)).float(),
+                          router=(0.02 * torch.randn(NE, E, device="cuda", generator=gen)).float(),
+                          gate=dummy, up=dummy, down=dummy)
+    h = ctx.bind(L)
+    x0 = synth.activations(T, E, seed=seed)
+    x = torch.from_numpy(x0).cuda()
+    sel = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    wt = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    qs = torch.empty((T, E), dtype=torch.int8, device="cuda")
+    d = torch.empty((T, E // 256), dtype=torch.float32, device="cuda")
+    bs = torch.empty((T, E // 16), dtype=torch.int16, device="cuda")
+    lib = cb.lib()
+    lib.clb200_ep_route.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int] + [C.c_void_p] * 6 + [C.c_char_p, C.c_size_t]
+    err = C.create_string_buffer(512)
+    assert lib.clb200_ep_route(ctx.handle, h, x.data_ptr(), T, sel.data_ptr(), wt.data_ptr(), qs.data_ptr(), d.data_ptr(),
+                               bs.data_ptr(), C.c_void_p(cb._stream(None)), err, 512) == 0, err.value.decode()
+    ctx.status()
+    ctx.release(h)
+    hl = synth.HostLayer(E=E, FF=1536, NE=NE, K=K, gate_type=synth.T_Q4_K, up_type=synth.T_Q4_K, down_type=synth.T_Q4_K,
+                         ffn_norm=L.ffn_norm.cpu().numpy(), router=L.router.cpu().numpy(),
+                         gate=dummy.cpu().numpy(), up=dummy.cpu().numpy(), down=dummy.cpu().numpy())
+    return sel, wt, hl, x0
+
+
+@pytest.mark.parametrize("T,E,NE,K", [(513, 2048, 128, 8), (600, 1280, 40, 6)])
+def test_large_batch_router_chunks(ctx, T, E, NE, K):
+    """Past 512 tokens (the expert-parallel route entry point takes any batch) the router takes 32 tokens a CTA and streams
+    their rows through shared memory 512 elements at a time, each chain carrying across the chunks: T = 513 leaves one
+    token in the last CTA; E = 1280 ends on a 256-element chunk; 40 experts leave a partial group of 32. The top-k equals
+    the reference's, the weights within TOL_WT."""
+    sel, wt, hl, x0 = ep_routed(ctx, E, NE, K, T, seed=T + E)
+    want_sel, want_wt = oracle.ref_route_batch(hl, x0)
+    check_routing(sel, wt, want_sel, want_wt)
+
+
 @pytest.mark.parametrize("T,NE,K", [(300, 128, 8), (2048, 128, 8), (33, 16, 4)])
 def test_dispatch_one_expert_takes_every_token(ctx, T, NE, K):
     """Expert 7 is in every token's choice (at a rank that moves with the token), the rest of each row is a seeded draw of
