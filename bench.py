@@ -489,7 +489,7 @@ def run_cache(a, wl: dict) -> dict:
 EP_METRIC = "MoE-layer tokens/s (Qwen3-235B-A22B layer, prefill 2048 tokens/GPU, Q4_K, expert-parallel)"
 
 
-def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=None, layers: int | None = None,
+def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=None, layers: int | None = None, exchange: str = "peer",
                clocks: bool = False) -> dict | None:
     """Expert-parallel MoE layers of the Qwen3-235B-A22B shape on the `world` ranks of the process
     group, one per GPU: each rank holds the router and 128/N experts of every layer. A step is one pass of the tokens through
@@ -525,6 +525,9 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
         del L, sh
         torch.cuda.empty_cache()
 
+    # the exchange: stores into the other GPUs' memory from the library's kernels (default), or NCCL all-to-alls
+    xchg = ep.PeerExchange(ctx, T, E, K) if dist and exchange == "peer" else None
+
     def timed_run(Tr: int, seed: int):
         x0 = torch.from_numpy(synth.activations(Tr, E, seed=seed + rank)).cuda()
         x = x0.clone()
@@ -532,7 +535,7 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
         def step(timed=None):
             x.copy_(x0)
             for c in comps:
-                ep.moe_layer(x, c, n_local, 1.0, timings=timed)
+                ep.moe_layer(x, c, n_local, 1.0, timings=timed, xchg=xchg)
 
         for _ in range(warmup):
             step()
@@ -568,7 +571,7 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
     # the whole layer on its own GPU
     xr = torch.from_numpy(synth.activations(256, E, seed=77 + rank)).cuda()
     xe = xr.clone()
-    sel_e, _ = ep.moe_layer(xe, comps[0], n_local, 1.0)
+    sel_e, _ = ep.moe_layer(xe, comps[0], n_local, 1.0, xchg=xchg)
     torch.cuda.synchronize()
     if full0 is not None:
         L, h = full0
@@ -580,6 +583,8 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
         parity = {"tokens": 256, "layer": 0, "topk_identical": bool(torch.equal(sel_e, selb)), "rel_l2": err,
                   "bar": 1e-5, "ok": bool(torch.equal(sel_e, selb) and err <= 1e-5),
                   "against": "the single-GPU block on the whole layer (clb200_moe_ffn_dev)"}
+    if xchg is not None:
+        xchg.close()
     del comps, keep, full0
     ctx.close()
     torch.cuda.empty_cache()
@@ -607,7 +612,10 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
 
     return {"workload": wl["desc"], "metric": EP_METRIC, "n_gpus": world, "layers_per_step": NL, "steps": steps,
             "warmup": warmup, "hidden": E, "experts": NE, "experts_per_gpu": n_local, "top_k": K, "ff": FF,
-            "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single (counts, rows, partial sums)",
+            "parallelism": f"ep{world}",
+            "exchange": ("stores into the other GPUs' memory from the library's kernels (CUDA IPC mappings), arrival signals "
+                         "waited on in a kernel; no host synchronisation" if exchange == "peer" else
+                         "NCCL all_to_all_single (counts, rows, partial sums)") if world > 1 else "none (one GPU)",
             "weak": summary(ms_w, T, ph_w, "weak"), "strong": summary(ms_s, T // world, ph_s, "strong"),
             "parity_rank0": parity, "clocks": clk.summary() if clocks else None,
             "gpu_launches_per_layer": 9, "dtype": "int8 dot (Q8_K x Q4_K) exact router; Q4_K experts on tcgen05 from fp16 hi/lo "
@@ -636,7 +644,8 @@ def run_ep(a, wl: dict) -> None:
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-    r = ep_measure(a.steps, a.warmup, rank, world, local, dist if world > 1 else None, layers=a.layers, clocks=True)
+    r = ep_measure(a.steps, a.warmup, rank, world, local, dist if world > 1 else None, layers=a.layers, clocks=True,
+                   exchange=a.ep_exchange)
     if rank == 0:
         w = r["weak"]
         line = {"metric": EP_METRIC, "value": w["value"], "unit": "layer-tokens/s", "n_gpus": world, "steps": a.steps,
@@ -926,6 +935,8 @@ def main() -> None:
     ap.add_argument("--smart", default=None, help="cache workload: SMART-ROUTE J,M,TAU (for example 2,12,0.015)")
     ap.add_argument("--batch", type=int, default=None, help="prompt workload: tokens per batch (the reference's CLUTOR_PS_B, 1..512)")
     ap.add_argument("--no-ep", action="store_true", help="decode workload: leave out the expert-parallel figures")
+    ap.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
+                    help="expert parallelism over N > 1 GPUs: stores into peer memory from the library's kernels, or NCCL")
     ap.add_argument("--no-secondary", action="store_true", help="decode workload at N=1: leave out the other configurations")
     a = ap.parse_args()
     wl = dict(WORKLOADS[a.workload])
@@ -962,7 +973,7 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     line = run_layers(a, wl, rank, world, local, dist)
     if a.workload == "decode" and not a.no_ep:   # the sharded configuration (config 4) at this N, every rank taking part
-        ep = ep_measure(5, 2, rank, world, local, dist)
+        ep = ep_measure(5, 2, rank, world, local, dist, exchange=a.ep_exchange)
         if rank == 0:
             line["ep"] = ep
     if a.workload == "decode" and world == 1 and not a.no_secondary:

@@ -177,6 +177,7 @@ static const char *device_error_text(int code) {
     case ERR_WAIT_EXPERT: return "timed out waiting for an expert's gate/up rows from other CTAs";
     case ERR_WAIT_COPY: return "timed out waiting for a bulk copy into shared memory";
     case ERR_BAD_EXPERT: return "an expert id out of range reached the dispatch";
+    case ERR_WAIT_PEER: return "timed out waiting for another GPU's rows or partial sums (does every rank take the same steps?)";
     default: return "unknown device error";
   }
 }

@@ -649,6 +649,7 @@ __global__ void __launch_bounds__(BT) combine_kernel(const BatchArgs a) {
   }
   __syncthreads();
   const int n = s_n;
+  if (a.ep && n == 0) return;   // a row with no expert here (an exchange's unused row): nothing reads its partial sum
   for (int j = 0; j < n; ++j)
     if (s_pos[j] < 0 || s_pos[j] >= a.T * K) { if (threadIdx.x == 0) set_error(a.err, ERR_BAD_EXPERT); return; }
   for (int i = i0 + threadIdx.x; i < i1; i += BT) {

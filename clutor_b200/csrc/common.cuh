@@ -16,7 +16,8 @@ namespace clb {
 constexpr uint32_t T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14;
 
 // Device error codes written to the context's error word (first error wins).
-enum : int { ERR_NONE = 0, ERR_WAIT_ROUTER = 1, ERR_WAIT_EXPERT = 2, ERR_WAIT_COPY = 3, ERR_BAD_EXPERT = 4, ERR_WAIT_GRID = 5 };
+enum : int { ERR_NONE = 0, ERR_WAIT_ROUTER = 1, ERR_WAIT_EXPERT = 2, ERR_WAIT_COPY = 3, ERR_BAD_EXPERT = 4, ERR_WAIT_GRID = 5,
+             ERR_WAIT_PEER = 6 };
 
 // A spin on a flag written by another CTA gives up after this many polls (each with a short sleep): about a second.
 constexpr uint32_t SPIN_LIMIT = 1u << 22;

@@ -1,5 +1,6 @@
 """Expert parallelism for the batched MoE block: the experts of a layer spread over the GPUs of one node, one process per
-GPU, with one exchange each way over NCCL (NVLink / NVSwitch).
+GPU, with one exchange each way over NVLink / NVSwitch: by default stores straight into the other GPUs' memory from the
+library's own kernels (PeerExchange: no library collective and no host synchronisation), or NCCL all-to-alls.
 
 Every rank holds the router (replicated) and experts [r * n_local, (r + 1) * n_local). A layer step for a rank's own T
 tokens:
@@ -8,12 +9,13 @@ tokens:
    the single-GPU arithmetic, so the routing is bit-identical;
 2. dispatch: each token goes once to every rank that holds at least one of its experts: its Q8_K row (the input every
    K-quant expert reads), its K expert ids made local (-1 where the expert is elsewhere) and its K weights, packed as one
-   byte row per (token, destination), in ascending token order per destination; one all-to-all of the counts, one of the
-   rows;
+   byte row per (token, destination), in ascending token order per destination; PeerExchange: a kernel stores each
+   destination's rows into that GPU's receive area and signals it with their count (the receiver waits on the signal in a
+   kernel); NCCL: one all-to-all of the counts, one of the rows;
 3. expert side (clb200_ep_experts): the received rows of all sources as one batch through the local experts; per row the
    weighted sum of its present experts (no residual);
-4. combine: one all-to-all back of those partial sums; the source adds them per token in rank order and applies the
-   residual, x += resid_scale * sum.
+4. combine: the partial sums go back the same way (a store kernel and a signal, or one all-to-all); the source adds them
+   per token in rank order and applies the residual, x += resid_scale * sum.
 
 Compared with the single-GPU block only the order of the fp32 additions over a token's experts differs (per-rank partial
 sums, then ranks in order), so outputs agree to about 1e-7 relative and the top-k is identical.
@@ -25,6 +27,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass
+from typing import Optional
 
 import numpy as np
 import torch
@@ -102,6 +105,8 @@ class GpuCompute(Compute):
         L.clb200_ep_pack.argtypes = [C.c_void_p] + [C.c_int] * 5 + [C.c_void_p] * 9 + [C.c_char_p, C.c_size_t]
         L.clb200_ep_combine.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
                                         C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_ep_combine_regions.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                C.c_void_p, C.c_float, C.c_void_p, C.c_char_p, C.c_size_t]
 
     def _s(self):   # ordered with the torch work around each call
         from . import _stream
@@ -144,11 +149,130 @@ class GpuCompute(Compute):
         cl = counts.tolist()
         return send[:sum(cl)], slot, cl
 
+    def pack_device(self, fmt, sel, wt, qs, d, bs, n_ranks, n_local):
+        """The plan and the rows (clb200_ep_pack) with the counts left on the device: (send [T * n_ranks, nbytes], slot,
+        counts [n_ranks] int32 device tensor)."""
+        T, K = sel.shape
+        dev = sel.device
+        send = torch.empty((max(T, 1) * n_ranks, fmt.nbytes), dtype=torch.uint8, device=dev)
+        slot = torch.empty((T, n_ranks), dtype=torch.int32, device=dev)
+        counts = torch.zeros(n_ranks, dtype=torch.int32, device=dev)
+        if T and self.L.clb200_ep_pack(self.ctx.handle, T, self.E, K, n_ranks, n_local, sel.data_ptr(), wt.data_ptr(), qs.data_ptr(),
+                                       d.data_ptr(), bs.data_ptr(), send.data_ptr(), slot.data_ptr(), counts.data_ptr(), self._s(),
+                                       self._err, 512):
+            raise RuntimeError(self._err.value.decode())
+        return send, slot, counts
+
+    def combine_regions(self, x, back, slot, counts, t_max, resid_scale):
+        """x += resid_scale * (each token's partial sums from the exchange's back area, ranks in order)."""
+        if x.shape[0] and self.L.clb200_ep_combine_regions(self.ctx.handle, x.shape[0], self.E, slot.shape[1], t_max, slot.data_ptr(),
+                                                           counts.data_ptr(), back.data_ptr(), x.data_ptr(), resid_scale, self._s(),
+                                                           self._err, 512):
+            raise RuntimeError(self._err.value.decode())
+
     def combine(self, x, back, plan, counts, resid_scale):
         slot = plan
         if self.L.clb200_ep_combine(self.ctx.handle, x.shape[0], self.E, slot.shape[1], slot.data_ptr(), back.data_ptr(), x.data_ptr(),
                                     resid_scale, self._s(), self._err, 512):
             raise RuntimeError(self._err.value.decode())
+
+
+class _DeviceBytes:
+    """A view of `nbytes` of device memory at `ptr` that torch can wrap without copying (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """The exchange over peer memory for one process group: this rank's exchange buffer (clb200_ep_xbuf_alloc) and every
+    other rank's, mapped here through CUDA IPC; rows and partial sums go out by the library's store kernels
+    (clb200_ep_push / clb200_ep_push_back) and arrive behind (step, rows) signals that a kernel waits on
+    (clb200_ep_wait), so a layer step needs no host synchronisation. t_max bounds the tokens any rank sends in one step.
+    Every rank of the group constructs it (a collective) and closes it (a collective)."""
+
+    def __init__(self, ctx, t_max: int, E: int, K: int, group=None):
+        import torch.distributed as dist
+        from . import lib
+        self.ctx, self.L, self.t_max, self.E, self.K, self.group = ctx, lib(), t_max, E, K, group
+        self.n, self.me = dist.get_world_size(group), dist.get_rank(group)
+        self.fmt = RowFormat(E, K)
+        self.seq = 0
+        self._err = C.create_string_buffer(512)
+        L = self.L
+        L.clb200_ep_xbuf_layout.restype = None
+        L.clb200_ep_xbuf_layout.argtypes = [C.c_int] * 4 + [C.POINTER(C.c_size_t)] * 3
+        L.clb200_ep_xbuf_alloc.argtypes = [C.c_void_p] + [C.c_int] * 4 + [C.POINTER(C.c_void_p), C.c_char_p, C.c_char_p, C.c_size_t]
+        L.clb200_ep_xbuf_open.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]
+        L.clb200_ep_xbuf_close.argtypes = [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_ep_xbuf_free.argtypes = [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_ep_push.argtypes = [C.c_void_p] + [C.c_int] * 5 + [C.c_void_p] * 3 + [C.c_uint, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_ep_wait.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+        L.clb200_ep_push_back.argtypes = L.clb200_ep_push.argtypes
+        size, roff, boff = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        L.clb200_ep_xbuf_layout(self.n, t_max, E, K, C.byref(size), C.byref(roff), C.byref(boff))
+        self.size, self.recv_off, self.back_off = size.value, roff.value, boff.value
+        own, handle = C.c_void_p(), C.create_string_buffer(64)
+        self._check(L.clb200_ep_xbuf_alloc(ctx.handle, self.n, t_max, E, K, C.byref(own), handle, self._err, 512))
+        self.own = own.value
+        handles = [None] * self.n
+        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        self.mapped, bases = [], []
+        for r in range(self.n):
+            if r == self.me:
+                bases.append(self.own)
+                continue
+            p = C.c_void_p()
+            self._check(L.clb200_ep_xbuf_open(ctx.handle, handles[r], C.byref(p), self._err, 512))
+            self.mapped.append(p.value)
+            bases.append(p.value)
+        self.bases = (C.c_void_p * self.n)(*bases)
+        whole = torch.as_tensor(_DeviceBytes(self.own, self.size), device=f"cuda:{torch.cuda.current_device()}")
+        R = self.n * t_max
+        self.recv = whole[self.recv_off:self.recv_off + R * self.fmt.nbytes].view(R, self.fmt.nbytes)
+        self.back = whole[self.back_off:self.back_off + R * E * 4].view(torch.float32).view(R, E)
+        self.rcounts = torch.zeros(self.n, dtype=torch.int32, device=whole.device)
+        self._whole = whole
+        dist.barrier(group=group)   # every rank mapped every buffer before anyone pushes
+
+    def _check(self, rc):
+        if rc:
+            raise RuntimeError(self._err.value.decode())
+
+    def next_step(self) -> None:
+        self.seq = self.seq % 0xFFFFFFFE + 1   # 1, 2, ...: a zeroed header carries step 0, which no step uses
+
+    def push(self, send, counts, stream) -> None:
+        self._check(self.L.clb200_ep_push(self.ctx.handle, self.me, self.n, self.t_max, self.E, self.K, self.bases, send.data_ptr(),
+                                          counts.data_ptr(), self.seq, stream, self._err, 512))
+
+    def wait_rows(self, stream) -> torch.Tensor:
+        self._check(self.L.clb200_ep_wait(self.ctx.handle, self.own, self.n, 0, self.seq, self.rcounts.data_ptr(), stream,
+                                          self._err, 512))
+        return self.rcounts
+
+    def push_back(self, partial, stream) -> None:
+        self._check(self.L.clb200_ep_push_back(self.ctx.handle, self.me, self.n, self.t_max, self.E, self.K, self.bases,
+                                               partial.data_ptr(), self.rcounts.data_ptr(), self.seq, stream, self._err, 512))
+
+    def wait_back(self, stream) -> None:
+        self._check(self.L.clb200_ep_wait(self.ctx.handle, self.own, self.n, 1, self.seq, None, stream, self._err, 512))
+
+    def close(self) -> None:
+        """A collective: every rank stops using the mapped buffers, unmaps them, and frees its own once every rank has."""
+        import torch.distributed as dist
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.mapped:
+            self.L.clb200_ep_xbuf_close(self.ctx.handle, p, self._err, 512)
+        self.mapped = []
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.recv = self.back = self._whole = None
+        self.L.clb200_ep_xbuf_free(self.ctx.handle, self.own, self._err, 512)
+        self.own = None
 
 
 def flat_plan(sel: torch.Tensor, n_ranks: int, n_local: int):
@@ -178,8 +302,10 @@ def dispatch_plan(sel: torch.Tensor, n_ranks: int, n_local: int):
     return list(torch.split(t_idx, counts)), list(torch.split(lsel, counts))
 
 
-def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, group=None, timings: dict | None = None):
-    """One expert-parallel MoE layer step on this rank's tokens x [T, E] (updated in place); returns (sel, wt)."""
+def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, group=None, timings: dict | None = None,
+              xchg: Optional[PeerExchange] = None):
+    """One expert-parallel MoE layer step on this rank's tokens x [T, E] (updated in place); returns (sel, wt). With
+    xchg (a PeerExchange of the same group) the rows and partial sums move over peer memory, else by NCCL all-to-alls."""
     import torch.distributed as dist
     n = dist.get_world_size(group) if dist.is_initialized() else 1
     T, E = x.shape
@@ -203,6 +329,8 @@ def moe_layer(x: torch.Tensor, comp: Compute, n_local: int, resid_scale: float, 
     mark("dispatch")
     K = sel.shape[1]
     fmt = RowFormat(E, K)
+    if xchg is not None and n > 1:
+        return _moe_layer_peer(x, comp, n_local, resid_scale, xchg, fmt, sel, wt, qs, d, bs, mark, close, timings)
     send, plan, sc = comp.pack(fmt, sel, wt, qs, d, bs, n, n_local)
     me = dist.get_rank(group) if n > 1 else 0
     if n > 1:
@@ -253,3 +381,36 @@ def shard_layer(layer, rank: int, n_ranks: int):
     s.router = layer.router[e0:e1]   # unused on the expert side; consistent with n_expert
     s.NE = n_local
     return s
+
+
+def _moe_layer_peer(x, comp, n_local, resid_scale, xchg: PeerExchange, fmt, sel, wt, qs, d, bs, mark, close, timings):
+    """The rest of moe_layer over peer memory: pack, push, wait for every sender's rows, the local experts over the whole
+    receive area (rows past a sender's count are left from earlier steps and get no expert), push the partial sums
+    back, wait for every rank's, combine."""
+    n, T = xchg.n, x.shape[0]
+    if T > xchg.t_max:
+        raise ValueError(f"{T} tokens: the exchange was set up for at most {xchg.t_max}")
+    st = comp._s()
+    send, slot, counts = comp.pack_device(fmt, sel, wt, qs, d, bs, n, n_local)
+    xchg.next_step()
+    xchg.push(send, counts, st)
+    rcounts = xchg.wait_rows(st)
+    close("dispatch")
+    r = fmt.unpack(xchg.recv)
+    live = (torch.arange(xchg.t_max, device=x.device)[None, :] < rcounts[:, None].to(torch.int64)).reshape(-1, 1)
+    mark("experts")
+    partial = comp.experts(r["qs"], r["d"], r["bs"], torch.where(live, r["sel"], -1), r["wt"])
+    close("experts")
+    mark("combine")
+    xchg.push_back(partial, st)
+    xchg.wait_back(st)
+    comp.combine_regions(x, xchg.back, slot, counts, xchg.t_max, resid_scale)
+    close("combine")
+    if timings is not None:   # a measured step: the counts are read on the host here (the timed steps never do)
+        sc, rc = counts.tolist(), rcounts.tolist()
+        me = xchg.me
+        timings.setdefault("rows", []).append(int(sum(rc)))
+        timings.setdefault("xbytes", []).append(sum(c for dd, c in enumerate(sc) if dd != me) * fmt.nbytes +
+                                                sum(c for dd, c in enumerate(rc) if dd != me) * x.shape[1] * 4)
+        timings.pop("_open", None)
+    return sel, wt

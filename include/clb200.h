@@ -149,6 +149,33 @@ int clb200_ep_pack(clb200_ctx *c, int T, int E, int n_used, int n_ranks, int n_l
                    size_t errlen);
 int clb200_ep_combine(clb200_ctx *c, int T, int E, int n_ranks, const int *slot, const float *back, float *x, float resid_scale,
                       void *stream, char *err, size_t errlen);
+/* The same exchange over peer memory (NVLink / NVSwitch) instead of a library all-to-all, with no host synchronisation:
+ * every rank allocates an exchange buffer of one layout (clb200_ep_xbuf_alloc: zeroed device memory and its CUDA IPC
+ * handle, 64 bytes, for the other processes) and maps every other rank's (clb200_ep_xbuf_open); bufs[r] below is rank r's
+ * buffer as this GPU addresses it (this rank's own at bufs[me]). clb200_ep_push stores the send rows of clb200_ep_pack
+ * (counts[r] rows for rank r, device memory) into region me of each rank's receive area and then signals each with
+ * (seq, rows); clb200_ep_wait (which 0) waits for every sender's signal of step seq and writes the row counts
+ * (counts_out [n_ranks], device memory); region s of the receive area (clb200_ep_xbuf_layout: recv_off, n_ranks x t_max
+ * rows) then holds sender s's rows in [0, counts_out[s]). clb200_ep_push_back returns the partial sums of those rows
+ * (partial: [n_ranks x t_max] rows of E floats in the same regions) to each sender's back area and signals it;
+ * clb200_ep_wait (which 1) waits for every rank's; clb200_ep_combine_regions is clb200_ep_combine over the back area
+ * (back_off; row r * t_max + i is the i-th row sent to rank r). A rank must not push step seq + 1 before its wait for the
+ * partial sums of step seq returned. Every wait is bounded: a rank that does not arrive sets the device error word
+ * (clb200_status), it does not hang. All asynchronous on stream. */
+void clb200_ep_xbuf_layout(int n_ranks, int t_max, int E, int n_used, size_t *bytes, size_t *recv_off, size_t *back_off);
+int clb200_ep_xbuf_alloc(clb200_ctx *c, int n_ranks, int t_max, int E, int n_used, void **buf, void *ipc_handle, char *err,
+                         size_t errlen);
+int clb200_ep_xbuf_open(clb200_ctx *c, const void *ipc_handle, void **peer, char *err, size_t errlen);
+int clb200_ep_xbuf_close(clb200_ctx *c, void *peer, char *err, size_t errlen);
+int clb200_ep_xbuf_free(clb200_ctx *c, void *buf, char *err, size_t errlen);
+int clb200_ep_push(clb200_ctx *c, int me, int n_ranks, int t_max, int E, int n_used, void *const *bufs, const uint8_t *send,
+                   const int *counts, unsigned int seq, void *stream, char *err, size_t errlen);
+int clb200_ep_wait(clb200_ctx *c, const void *own_buf, int n_ranks, int which, unsigned int seq, int *counts_out, void *stream,
+                   char *err, size_t errlen);
+int clb200_ep_push_back(clb200_ctx *c, int me, int n_ranks, int t_max, int E, int n_used, void *const *bufs, const float *partial,
+                        const int *rcounts, unsigned int seq, void *stream, char *err, size_t errlen);
+int clb200_ep_combine_regions(clb200_ctx *c, int T, int E, int n_ranks, int t_max, const int *slot, const int *counts,
+                              const float *back, float *x, float resid_scale, void *stream, char *err, size_t errlen);
 /* Waits for the context's work and reports a device-side error recorded since the last call (0: none). */
 int clb200_status(clb200_ctx *c, char *err, size_t errlen);
 /* Bytes of device memory the context holds for layers and scratch. */

@@ -1,8 +1,9 @@
 """Multi-GPU parity of the expert-parallel layer (run under torchrun, one rank per GPU; driven by test_gpu_ep_multi.py).
 
-Each rank routes its own tokens, exchanges rows with the other ranks over NCCL, and compares the result with the
-single-GPU block it computes itself from the whole layer: top-k identical, x within 1e-5 relative L2. Exits non-zero on
-a mismatch.
+Each rank routes its own tokens, exchanges rows with the other ranks -- over NCCL, and over peer memory (the library's
+store kernels into the other GPUs' exchange buffers, ep.PeerExchange) -- and compares the result with the single-GPU
+block it computes itself from the whole layer: top-k identical, x within 1e-5 relative L2. The peer exchange runs several
+steps in a row with batches of different sizes (its regions and step signals are reused). Exits non-zero on a mismatch.
 """
 import datetime
 import os
@@ -22,6 +23,7 @@ def main() -> int:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     ctx = cb.Context(local)
     worst, ok = 0.0, True
+    xchg = ep.PeerExchange(ctx, 256, 2048, 8)
     for gt in (synth.T_Q4_K, synth.T_Q8_0):
         L = synth.device_layer(E=2048, FF=768, NE=128, K=8, seed=31, gate_type=gt, router_scale=0.05)
         full = ctx.bind(L)
@@ -35,10 +37,12 @@ def main() -> int:
                 pass
             continue
         comp = ep.GpuCompute(ctx, full, ctx.bind(sh), L.E, L.K)
-        for T in (256, 37):
+        # (T >= 2: the single-GPU block the results are checked against takes its batched path, the same arithmetic as the
+        # expert side; one token would take the one-token kernel's exact integer path)
+        for T, via in ((256, None), (37, None), (256, xchg), (37, xchg), (2, xchg), (200, xchg), (256, xchg)):
             x0 = torch.from_numpy(synth.activations(T, L.E, seed=100 * rank + T)).cuda()
             x = x0.clone()
-            sel, _ = ep.moe_layer(x, comp, L.NE // world, L.resid_scale)
+            sel, _ = ep.moe_layer(x, comp, L.NE // world, L.resid_scale, xchg=via)
             xb = x0.clone()
             selb = torch.zeros((T, L.K), dtype=torch.int32, device="cuda")
             ctx.moe_ffn_dev(full, xb, selb)
@@ -47,7 +51,14 @@ def main() -> int:
             worst = max(worst, err)
             if not torch.equal(sel, selb) or not err <= 1e-5:
                 ok = False
-                print(f"rank {rank} T={T}: top-k equal {torch.equal(sel, selb)}, relative L2 {err:.2e}", flush=True)
+                print(f"rank {rank} T={T} ({'peer' if via else 'nccl'}): top-k equal {torch.equal(sel, selb)}, relative L2 {err:.2e}",
+                      flush=True)
+    xchg.close()
+    try:
+        ctx.status()
+    except Exception as e:   # a peer wait that ran out
+        ok = False
+        print(f"rank {rank}: {e}", flush=True)
     flag = torch.tensor([0 if ok else 1], device="cuda")
     dist.all_reduce(flag)
     if rank == 0:
