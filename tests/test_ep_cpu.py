@@ -146,9 +146,16 @@ def _leaving_rank(rank, world, port, outdir):
     comp = StubCompute(NE)
     x = torch.from_numpy(synth.activations(T, E, seed=rank))
     ep.moe_layer(x, comp, NE // world, 1.0)
-    if rank == 1:
-        return   # leaves between steps, with no step of its own in flight
     import time
+    if rank == 1:
+        # leaves between steps, with no step of its own in flight -- once every other rank has its first step's data
+        # (otherwise rows still on their way from this process could be lost with it, and the FIRST step would fail);
+        # the others say so through files, not through another collective
+        t_end = time.monotonic() + 60.0
+        while time.monotonic() < t_end and not all(os.path.exists(os.path.join(outdir, f"step1.{r}")) for r in range(world) if r != 1):
+            time.sleep(0.05)
+        return
+    open(os.path.join(outdir, f"step1.{rank}"), "w").close()
     t0 = time.monotonic()
     try:
         ep.moe_layer(x, comp, NE // world, 1.0)
