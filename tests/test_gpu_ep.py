@@ -93,3 +93,89 @@ def test_device_exchange_equals_the_host_form(ctx, n_ranks):
     gpu.combine(xd, back, plan_d, counts_d, 0.75)
     torch.cuda.synchronize()
     assert torch.equal(xd.view(torch.int32), xh.view(torch.int32))
+
+
+@pytest.mark.parametrize("n_ranks", [2, 3])
+def test_peer_exchange_kernels_emulated(ctx, n_ranks):
+    """The peer-memory exchange's kernels (clb200_ep_push / _wait / _push_back / _combine_regions) with N ranks emulated in
+    one process on one GPU: every rank's exchange buffer is local here, and each wait runs after the pushes it waits for
+    have finished (one stream), so no kernel waits on another that is still running. Two steps with different batches per
+    rank reuse the regions and the step signals; each rank's x must match the single-GPU block on its tokens (top-k
+    identical, 1e-5 relative L2)."""
+    import ctypes as C
+
+    import torch
+
+    import clutor_b200 as cb
+    L = synth.device_layer(E=2048, FF=768, NE=120, K=8, seed=23, router_scale=0.05)
+    full = ctx.bind(L)
+    n, n_local, t_max = n_ranks, L.NE // n_ranks, 256
+    comps = [ep.GpuCompute(ctx, full, ctx.bind(ep.shard_layer(L, r, n)), L.E, L.K) for r in range(n)]
+    lib = cb.lib()
+    lib.clb200_ep_xbuf_layout.restype = None
+    lib.clb200_ep_xbuf_layout.argtypes = [C.c_int] * 4 + [C.POINTER(C.c_size_t)] * 3
+    lib.clb200_ep_xbuf_alloc.argtypes = [C.c_void_p] + [C.c_int] * 4 + [C.POINTER(C.c_void_p), C.c_char_p, C.c_char_p, C.c_size_t]
+    lib.clb200_ep_xbuf_free.argtypes = [C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+    lib.clb200_ep_push.argtypes = [C.c_void_p] + [C.c_int] * 5 + [C.c_void_p] * 3 + [C.c_uint, C.c_void_p, C.c_char_p, C.c_size_t]
+    lib.clb200_ep_push_back.argtypes = lib.clb200_ep_push.argtypes
+    lib.clb200_ep_wait.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_uint, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+    err = C.create_string_buffer(512)
+    size, roff, boff = C.c_size_t(), C.c_size_t(), C.c_size_t()
+    lib.clb200_ep_xbuf_layout(n, t_max, L.E, L.K, C.byref(size), C.byref(roff), C.byref(boff))
+    fmt = ep.RowFormat(L.E, L.K)
+    own, recv, back = [], [], []
+    for r in range(n):
+        p, h = C.c_void_p(), C.create_string_buffer(64)
+        assert lib.clb200_ep_xbuf_alloc(ctx.handle, n, t_max, L.E, L.K, C.byref(p), h, err, 512) == 0, err.value.decode()
+        own.append(p.value)
+        whole = torch.as_tensor(ep._DeviceBytes(p.value, size.value), device="cuda")
+        recv.append(whole[roff.value:roff.value + n * t_max * fmt.nbytes].view(n * t_max, fmt.nbytes))
+        back.append(whole[boff.value:boff.value + n * t_max * L.E * 4].view(torch.float32).view(n * t_max, L.E))
+    bufs = (C.c_void_p * n)(*own)
+    st = C.c_void_p(cb._stream(None))
+    try:
+        for seq, Ts in ((1, (200, 37, 64)), (2, (5, 120, 256))):
+            Ts = Ts[:n]
+            x0 = [torch.from_numpy(synth.activations(T, L.E, seed=10 * seq + r)).cuda() for r, T in enumerate(Ts)]
+            x = [v.clone() for v in x0]
+            plans, sels = [], []
+            for r in range(n):
+                sel, wt, qs, d, bs = comps[r].route(x[r])
+                sels.append(sel)
+                plans.append(comps[r].pack_device(fmt, sel, wt, qs, d, bs, n, n_local))
+            for r in range(n):
+                send, _, counts = plans[r]
+                assert lib.clb200_ep_push(ctx.handle, r, n, t_max, L.E, L.K, bufs, send.data_ptr(), counts.data_ptr(), seq, st,
+                                          err, 512) == 0, err.value.decode()
+            rcounts = [torch.zeros(n, dtype=torch.int32, device="cuda") for _ in range(n)]
+            for r in range(n):
+                assert lib.clb200_ep_wait(ctx.handle, own[r], n, 0, seq, rcounts[r].data_ptr(), st, err, 512) == 0
+            partials = []
+            for r in range(n):
+                rows = fmt.unpack(recv[r])
+                live = (torch.arange(t_max, device="cuda")[None, :] < rcounts[r][:, None].long()).reshape(-1, 1)
+                partials.append(comps[r].experts(rows["qs"], rows["d"], rows["bs"], torch.where(live, rows["sel"], -1), rows["wt"]))
+            for r in range(n):
+                assert lib.clb200_ep_push_back(ctx.handle, r, n, t_max, L.E, L.K, bufs, partials[r].data_ptr(), rcounts[r].data_ptr(),
+                                               seq, st, err, 512) == 0, err.value.decode()
+            for r in range(n):
+                assert lib.clb200_ep_wait(ctx.handle, own[r], n, 1, seq, None, st, err, 512) == 0
+            for r in range(n):
+                _, slot, counts = plans[r]
+                comps[r].combine_regions(x[r], back[r], slot, counts, t_max, L.resid_scale)
+            ctx.status()
+            for r in range(n):
+                # rows from sender q: its tokens with at least one expert on rank r
+                want = torch.tensor([int(((sels[q] // n_local) == r).any(1).sum()) for q in range(n)], dtype=torch.int32)
+                assert torch.equal(rcounts[r].cpu(), want), f"step {seq} rank {r}: rows received {rcounts[r].tolist()}"
+                xb = x0[r].clone()
+                selb = torch.zeros((Ts[r], L.K), dtype=torch.int32, device="cuda")
+                ctx.moe_ffn_dev(full, xb, selb)
+                ctx.status()
+                assert torch.equal(sels[r], selb)
+                e = float(torch.linalg.norm((x[r] - xb).double()) / torch.linalg.norm((xb - x0[r]).double()))
+                assert e <= 1e-5, f"step {seq} rank {r}: relative L2 {e:.2e}"
+    finally:
+        torch.cuda.synchronize()
+        for p in own:
+            lib.clb200_ep_xbuf_free(ctx.handle, p, err, 512)
