@@ -618,7 +618,9 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
                          "NCCL all_to_all_single (counts, rows, partial sums)") if world > 1 else "none (one GPU)",
             "weak": summary(ms_w, T, ph_w, "weak"), "strong": summary(ms_s, T // world, ph_s, "strong"),
             "parity_rank0": parity, "clocks": clk.summary() if clocks else None,
-            "gpu_launches_per_layer": 9, "dtype": "int8 dot (Q8_K x Q4_K) exact router; Q4_K experts on tcgen05 from fp16 hi/lo "
+            # this library's kernels a layer step launches: route 3, pack 2, experts 7, combine 1, and with the peer exchange
+            # its push, wait, push-back and wait
+            "gpu_launches_per_layer": 16 if (world > 1 and exchange == "peer") else 13, "dtype": "int8 dot (Q8_K x Q4_K) exact router; Q4_K experts on tcgen05 from fp16 hi/lo "
             "operands, fp32 accumulate"}
 
 
