@@ -526,7 +526,12 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
         torch.cuda.empty_cache()
 
     # the exchange: stores into the other GPUs' memory from the library's kernels (default), or NCCL all-to-alls
-    xchg = ep.PeerExchange(ctx, T, E, K) if dist and exchange == "peer" else None
+    xchg = None
+    if dist and exchange == "peer":
+        try:
+            xchg = ep.PeerExchange(ctx, T, E, K)
+        except RuntimeError as e:   # every rank gives up together (the constructor agrees on it): NCCL instead
+            exchange = f"nccl ({e})"
 
     def timed_run(Tr: int, seed: int):
         x0 = torch.from_numpy(synth.activations(Tr, E, seed=seed + rank)).cuda()
@@ -615,7 +620,8 @@ def ep_measure(steps: int, warmup: int, rank: int, world: int, local: int, dist=
             "parallelism": f"ep{world}",
             "exchange": ("stores into the other GPUs' memory from the library's kernels (CUDA IPC mappings), arrival signals "
                          "waited on in a kernel; no host synchronisation" if exchange == "peer" else
-                         "NCCL all_to_all_single (counts, rows, partial sums)") if world > 1 else "none (one GPU)",
+                         "NCCL all_to_all_single (counts, rows, partial sums)" + (exchange[4:] if exchange.startswith("nccl (") else ""))
+                        if world > 1 else "none (one GPU)",
             "weak": summary(ms_w, T, ph_w, "weak"), "strong": summary(ms_s, T // world, ph_s, "strong"),
             "parity_rank0": parity, "clocks": clk.summary() if clocks else None,
             # this library's kernels a layer step launches: route 3, pack 2, experts 7, combine 1, and with the peer exchange

@@ -212,28 +212,46 @@ class PeerExchange:
         size, roff, boff = C.c_size_t(), C.c_size_t(), C.c_size_t()
         L.clb200_ep_xbuf_layout(self.n, t_max, E, K, C.byref(size), C.byref(roff), C.byref(boff))
         self.size, self.recv_off, self.back_off = size.value, roff.value, boff.value
-        own, handle = C.c_void_p(), C.create_string_buffer(64)
-        self._check(L.clb200_ep_xbuf_alloc(ctx.handle, self.n, t_max, E, K, C.byref(own), handle, self._err, 512))
-        self.own = own.value
+        own, handle, failure = C.c_void_p(), C.create_string_buffer(64), None
+        if L.clb200_ep_xbuf_alloc(ctx.handle, self.n, t_max, E, K, C.byref(own), handle, self._err, 512):
+            failure = self._err.value.decode()
+        self.own = own.value if not failure else None
         handles = [None] * self.n
-        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        dist.all_gather_object(handles, None if failure else bytes(handle.raw), group=group)
         self.mapped, bases = [], []
         for r in range(self.n):
+            if failure:
+                break
             if r == self.me:
                 bases.append(self.own)
                 continue
+            if handles[r] is None:
+                failure = f"rank {r} could not allocate its exchange buffer"
+                break
             p = C.c_void_p()
-            self._check(L.clb200_ep_xbuf_open(ctx.handle, handles[r], C.byref(p), self._err, 512))
+            if L.clb200_ep_xbuf_open(ctx.handle, handles[r], C.byref(p), self._err, 512):
+                failure = self._err.value.decode()
+                break
             self.mapped.append(p.value)
             bases.append(p.value)
+        # every rank learns whether every rank mapped every buffer (a collective every rank reaches, failed or not), so
+        # that all give up together and a caller can fall back to another exchange on all ranks
+        ok = torch.tensor([0 if failure else 1], dtype=torch.int32, device=f"cuda:{torch.cuda.current_device()}")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            for p in self.mapped:
+                L.clb200_ep_xbuf_close(ctx.handle, p, self._err, 512)
+            if self.own:
+                L.clb200_ep_xbuf_free(ctx.handle, self.own, self._err, 512)
+            self.own, self.mapped = None, []
+            raise RuntimeError(f"peer-memory exchange unavailable: {failure or 'another rank could not map the buffers'}")
         self.bases = (C.c_void_p * self.n)(*bases)
         whole = torch.as_tensor(_DeviceBytes(self.own, self.size), device=f"cuda:{torch.cuda.current_device()}")
         R = self.n * t_max
         self.recv = whole[self.recv_off:self.recv_off + R * self.fmt.nbytes].view(R, self.fmt.nbytes)
         self.back = whole[self.back_off:self.back_off + R * E * 4].view(torch.float32).view(R, E)
         self.rcounts = torch.zeros(self.n, dtype=torch.int32, device=whole.device)
-        self._whole = whole
-        dist.barrier(group=group)   # every rank mapped every buffer before anyone pushes
+        self._whole = whole   # (every rank mapped every buffer before anyone pushes: the all_reduce above)
 
     def _check(self, rc):
         if rc:
