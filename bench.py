@@ -37,7 +37,7 @@ WORKLOADS = {
                       desc="Qwen3-30B-A3B MoE layer, T=64, Q8_0 experts"),
     "ep235b": dict(T=2048, gate="q4_k", down="q4_k", E=4096, FF=1536, NE=128, K=8, layers=2,
                    desc="Qwen3-235B-A22B MoE layer, prefill 2048 tokens per GPU, Q4_K experts, expert-parallel over the GPUs "
-                        "(NCCL all-to-all dispatch and combine)"),
+                        "(rows and partial sums over peer memory from this library's kernels)"),
     "model": dict(T=1, gate="q4_k", down="q6_k", E=2048, FF=768, NE=128, K=8, layers=48,
                   desc="Qwen3-30B-A3B whole model, greedy decode at batch 1 from a 1-token prompt: 48 layers, GQA 32/4 heads "
                        "x 128, QK-norm, NEOX rotary (base 1e6), fp16 key/value cache, Q4_K_M mix (Q4_K embedding, attn_q/k/o and "
@@ -665,7 +665,7 @@ def run_ep(a, wl: dict) -> None:
                            "l2": f"inputs larger than L2: {r['layers_per_step']} layers, "
                                  f"{wl['NE'] * wl['E'] * wl['FF'] * 3 * 144 / 256 / 1e9 * r['layers_per_step'] / world:.2f} GB of experts per GPU"},
                 "roofline": w["roofline"], "ep": r, "cpu_baseline": None, "e2e": None,
-                "gpu_launches": r["layers_per_step"] * a.steps * 9, "clocks": r["clocks"]}
+                "gpu_launches": r["layers_per_step"] * a.steps * r["gpu_launches_per_layer"], "clocks": r["clocks"]}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
